@@ -1,0 +1,99 @@
+// common.cuh — shared device helpers and host error plumbing of libocrcuda.so (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "ocr_cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libocrcuda is written for sm_100a (B200) only"
+#endif
+
+namespace ocr {
+
+// ---- host: the per-thread last error (ocr_last_error) -----------------------------------------------------------
+void set_error(const std::string& msg);
+ocr_status fail(ocr_status code, const std::string& msg);
+ocr_status cuda_fail(cudaError_t e, const char* what);
+
+#define OCR_CUDA(call)                                                                                                 \
+    do {                                                                                                               \
+        cudaError_t e_ = (call);                                                                                       \
+        if (e_ != cudaSuccess) return ::ocr::cuda_fail(e_, #call);                                                     \
+    } while (0)
+#define OCR_TRY(call)                                                                                                  \
+    do {                                                                                                               \
+        ocr_status s_ = (call);                                                                                        \
+        if (s_ != OCR_OK) return s_;                                                                                   \
+    } while (0)
+
+// ---- device -----------------------------------------------------------------------------------------------------
+constexpr unsigned FULL = 0xffffffffu;
+constexpr uint32_t NO_INDEX = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+
+// the argmax order of the sampler: a larger value wins, equal values → the lower index (ocr-decode's argmax keeps the
+// first maximum); NaN never wins (every comparison with it is false)
+__device__ __forceinline__ bool better(float v, uint32_t i, float w, uint32_t j) {
+    return v > w || (v == w && i < j);
+}
+
+__device__ __forceinline__ void warp_argmax(float& v, uint32_t& i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float w = __shfl_xor_sync(FULL, v, o);
+        uint32_t j = __shfl_xor_sync(FULL, i, o);
+        if (better(w, j, v, i)) {
+            v = w;
+            i = j;
+        }
+    }
+}
+
+// 16-byte streaming load of read-once data (weights): no L1 allocation
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// four signed bytes of a word → four exact floats: the biased byte (q + 128) is placed in the mantissa of 2^23
+// (0x4B0000bb = 8388608 + byte) by one byte permute, then 2^23 + 128 is subtracted (exact: all values are integers
+// below 2^24)
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* out) {
+    const uint32_t u = w ^ 0x80808080u;
+    out[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7440)) - 8388736.0f;
+    out[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7441)) - 8388736.0f;
+    out[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7442)) - 8388736.0f;
+    out[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7443)) - 8388736.0f;
+}
+
+// programmatic dependent launch: wait for the grids this one depends on (their memory visible); let dependents start
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// device-side error flag (ocr_ctx_sync reports it): the first code wins
+enum DevErr : int { DEV_OK = 0, DEV_BAD_INDEX = 1, DEV_BAD_POS = 2 };
+
+__device__ __forceinline__ void dev_error(int* flag, int code) {
+    if (flag) atomicCAS(flag, 0, code);
+}
+
+}  // namespace ocr

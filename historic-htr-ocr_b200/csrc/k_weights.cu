@@ -1,0 +1,141 @@
+// k_weights.cu — q8_0 device layout: repack from GGUF blocks, the seeded synthetic generator, unpack for export.
+//
+// The synthetic generator's arithmetic is integer-only up to one f32 multiply, an IEEE division and the f16 RNE
+// store, each written with the _rn intrinsics so no contraction changes a rounding: the host test generator of the
+// same seed gives the same bits.
+#include "kernels.cuh"
+
+namespace ocr {
+
+// ---- the GGUF q8_0 block (ocr-gguf/src/lib.rs:129-135): f16 d (little endian) + 32 x int8 ---------------------------
+__global__ void k_repack_q8_0(const uint8_t* __restrict__ blocks, int rows, int cols, int8_t* __restrict__ q,
+                              __half* __restrict__ d, int row_mul, int row_add) {
+    const int nbr = cols / 32;
+    const long nblk = (long)rows * nbr;
+    for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(b / nbr), c = (int)(b % nbr);
+        const uint8_t* src = blocks + b * 34;
+        // 34-byte blocks start on 2-byte boundaries: read 17 half-words
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+        uint32_t w[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) w[k] = (uint32_t)s16[1 + 2 * k] | ((uint32_t)s16[2 + 2 * k] << 16);
+        const long dr = (long)r * row_mul + row_add;
+        uint4* dst = reinterpret_cast<uint4*>(q + dr * cols + c * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        d[dr * nbr + c] = __ushort_as_half(s16[0]);
+    }
+}
+
+__global__ void k_unpack_q8_0(const int8_t* __restrict__ q, const __half* __restrict__ d, int rows, int cols,
+                              int row_mul, int row_add, uint8_t* __restrict__ blocks) {
+    const int nbr = cols / 32;
+    const long nblk = (long)rows * nbr;
+    for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(b / nbr), c = (int)(b % nbr);
+        const long sr = (long)r * row_mul + row_add;
+        uint8_t* dst = blocks + b * 34;
+        const uint16_t h = __half_as_ushort(d[sr * nbr + c]);
+        dst[0] = (uint8_t)(h & 0xff);
+        dst[1] = (uint8_t)(h >> 8);
+        const int8_t* src = q + sr * cols + c * 32;
+        for (int k = 0; k < 32; k++) dst[2 + k] = (uint8_t)src[k];
+    }
+}
+
+// ---- SplitMix64 addressed by output index (ocr-decode sampling.rs:24-35's generator) ---------------------------------
+__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t i) {
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ int u16sum4(uint64_t z) {
+    return (int)(z & 0xffff) + (int)((z >> 16) & 0xffff) + (int)((z >> 32) & 0xffff) + (int)(z >> 48);
+}
+
+// N(0,1) stand-in: Irwin–Hall sum of 12 uniform u16, centred, scaled by 2^-16 (exact)
+__device__ __forceinline__ float gauss(uint64_t seed, uint64_t i) {
+    const int s = u16sum4(splitmix64_at(seed, 3 * i)) + u16sum4(splitmix64_at(seed, 3 * i + 1)) +
+                  u16sum4(splitmix64_at(seed, 3 * i + 2)) - 6 * 65535;
+    return __fmul_rn((float)s, 1.0f / 65536.0f);
+}
+
+__device__ __forceinline__ int8_t sat_i8(float v) {
+    if (v != v) return 0;
+    if (v >= 127.0f) return 127;
+    if (v <= -128.0f) return -128;
+    return (int8_t)v;
+}
+
+// one q8_0 block of generated values, quantized as ggml's quantize_row_q8_0_ref (text.rs:676-691)
+__global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, int8_t* __restrict__ q,
+                             __half* __restrict__ d, int row_mul, int row_add) {
+    const int nbr = cols / 32;
+    const long nblk = (long)rows * nbr;
+    for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
+        float x[32];
+        float amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            x[j] = __fmul_rn(sigma, gauss(seed, (uint64_t)b * 32 + j));
+            const float a = fabsf(x[j]);
+            if (a > amax) amax = a;
+        }
+        const float dv = __fdiv_rn(amax, 127.0f);
+        const float id = dv != 0.0f ? __fdiv_rn(1.0f, dv) : 0.0f;
+        const int r = (int)(b / nbr), c = (int)(b % nbr);
+        const long dr = (long)r * row_mul + row_add;
+        uint32_t w[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int m = 0; m < 4; m++) v |= ((uint32_t)(uint8_t)sat_i8(roundf(__fmul_rn(x[4 * k + m], id)))) << (8 * m);
+            w[k] = v;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(q + dr * cols + c * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        d[dr * nbr + c] = __float2half_rn(dv);
+    }
+}
+
+// 1 + 0.01 u, u = the top 24 bits of output i mapped to [-1, 1) (the tests' norm weights, text.rs:1304)
+__global__ void k_synth_norm(uint64_t seed, int n, float* __restrict__ out) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float u = (float)(splitmix64_at(seed, (uint64_t)i) >> 40) * (1.0f / 16777216.0f) * 2.0f - 1.0f;
+        out[i] = __fadd_rn(1.0f, __fmul_rn(0.01f, u));
+    }
+}
+
+static int grid_for(long n, int threads) {
+    long g = (n + threads - 1) / threads;
+    return (int)(g < 1 ? 1 : (g > 65535 * 8 ? 65535 * 8 : g));
+}
+
+void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, int8_t* q, __half* d, int row_mul,
+                        int row_add) {
+    const long n = (long)rows * (cols / 32);
+    k_repack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(blocks, rows, cols, q, d, row_mul, row_add);
+}
+
+void launch_unpack_q8_0(cudaStream_t st, const int8_t* q, const __half* d, int rows, int cols, int row_mul,
+                        int row_add, uint8_t* blocks) {
+    const long n = (long)rows * (cols / 32);
+    k_unpack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(q, d, rows, cols, row_mul, row_add, blocks);
+}
+
+void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, int8_t* q, __half* d,
+                       int row_mul, int row_add) {
+    const long n = (long)rows * (cols / 32);
+    k_synth_q8_0<<<grid_for(n, 128), 128, 0, st>>>(seed, sigma, rows, cols, q, d, row_mul, row_add);
+}
+
+void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out) {
+    k_synth_norm<<<grid_for(n, 256), 256, 0, st>>>(seed, n, out);
+}
+
+}  // namespace ocr

@@ -1,0 +1,127 @@
+// kernels.cuh — parameter blocks and launchers of the device kernels (one translation unit each, sm_100a).
+//
+// Device layout of a q8_0 matrix [rows][cols] (cols % 32 == 0), repacked at load from GGUF's 34-byte blocks:
+//   quants  int8 [rows][cols]      row-major, rows 16-B aligned (cols % 16 == 0): a warp's 16-B lane loads of one
+//                                  512-column chunk are one contiguous, fully coalesced 512-B transaction
+//   scales  f16  [rows][cols / 32] the block scale d of columns [32 b, 32 b + 32)
+// value(r, c) = quants[r][c] * f32(scales[r][c / 32]) — the same q and d bits as the GGUF block.
+#pragma once
+
+#include "common.cuh"
+
+namespace ocr {
+
+struct QMat {
+    const int8_t* q = nullptr;
+    const __half* d = nullptr;
+    int rows = 0, cols = 0;
+};
+
+// ---- weights: repack / synthetic generation (k_weights.cu) ---------------------------------------------------------
+// GGUF blocks [rows][cols/32] x 34 B → quants/scales at destination row r * row_mul + row_add
+void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, int8_t* q, __half* d, int row_mul,
+                        int row_add);
+// the synthetic generator (bit-identical to the oracle's orc_synth_q8_0 / orc_fill_norm)
+void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, int8_t* q, __half* d,
+                       int row_mul, int row_add);
+void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out);
+// back to GGUF blocks (ocr_model_tensor_gguf): source rows r * row_mul + row_add
+void launch_unpack_q8_0(cudaStream_t st, const int8_t* q, const __half* d, int rows, int cols, int row_mul,
+                        int row_add, uint8_t* blocks);
+
+// ---- matvec family (k_matvec.cu) -----------------------------------------------------------------------------------
+enum MvMode : int { MV_STORE = 0, MV_ADD = 1, MV_SWIGLU = 2 };
+
+struct MvArgs {
+    QMat w;
+    const float* x = nullptr;  // [B][x_stride] input rows
+    int x_stride = 0;
+    const float* nw = nullptr;  // RMSNorm weights (null = no norm)
+    float eps = 1e-6f;
+    // layer-0 embedding: x = token_embd[tok[b]] (dequantized), written to x_out by the grid's first column of CTAs
+    const int32_t* tok = nullptr;
+    QMat emb;
+    float* x_out = nullptr;
+    float* y = nullptr;  // [B][y_stride]
+    int y_stride = 0;
+    int mode = MV_STORE;
+    int nb = 1;  // slots
+    const int32_t* active = nullptr;  // [B] (null = all); an idle slot's rows are not written
+};
+void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl);
+
+// the LM head + greedy choice (dmv_norm → choose_pen → choose_max → choose_pick, fused)
+struct LmArgs {
+    QMat w;  // tied token_embd [n_vocab][dim]
+    const float* x = nullptr;
+    int x_stride = 0;
+    const float* nw = nullptr;
+    float eps = 1e-6f;
+    int nb = 1;
+    float* logits = nullptr;  // [B][n_vocab] raw logits (null = not stored)
+    // the choice (sample = 0: logits only)
+    int sample = 0;
+    float rp = 1.0f;
+    int window = 1;
+    int use_fp = 0;
+    float fp = 0.0f;
+    int32_t* hist = nullptr;  // [B][hist_cap]
+    int hist_cap = 0;
+    int32_t* len = nullptr;   // [B]
+    int32_t* tok = nullptr;   // [B]
+    int32_t* pos = nullptr;   // [B] advanced by one per choice when advance_pos
+    int advance_pos = 0;
+    uint32_t* counts = nullptr;  // [B][n_vocab] (use_fp)
+    float* fpen = nullptr;       // [B][n_vocab]
+    const int32_t* active = nullptr;
+    float* part = nullptr;       // scratch: [B][grid][2] + nan flags
+    uint32_t* done = nullptr;    // scratch counter (self-resetting)
+    int* err = nullptr;
+};
+void launch_lm_head(cudaStream_t st, const LmArgs& a, int num_sms, bool pdl);
+int lm_head_grid(int num_sms);
+
+// the choice alone over logits on the device (choice 0 from the prompt's logits; ocr_sample_logits)
+// slots [slot_base, slot_base + n_slots) of logits [B][logits_stride]; a.nb = B (the partials' layout)
+void launch_sample(cudaStream_t st, const float* logits, int logits_stride, int n_vocab, const LmArgs& a,
+                   int num_sms, int slot_base, int n_slots);
+int sample_grid(int num_sms);
+
+// ---- attention (k_attn.cu) -------------------------------------------------------------------------------------------
+struct AttnArgs {
+    float* qkv = nullptr;  // [B][(n_head + 2 n_kv) * 128] raw projections
+    int qkv_stride = 0;
+    const float* q_norm = nullptr;
+    const float* k_norm = nullptr;
+    const float* rope = nullptr;  // [n_ctx][64][2]
+    __half* kc = nullptr;         // [B][n_kv][n_ctx][128]
+    __half* vc = nullptr;
+    const int32_t* pos = nullptr;  // [B] the token's position (device)
+    const int32_t* active = nullptr;
+    int n_head = 16, n_kv = 8, n_ctx = 0, splits = 1;
+    float eps = 1e-6f, scale = 0.0f;
+    float* part = nullptr;      // [B][n_head][splits][130]
+    uint32_t* done = nullptr;   // [B][n_kv] self-resetting
+    float* out = nullptr;       // [B][out_stride]
+    int out_stride = 0;
+    int nb = 1;
+    int* err = nullptr;
+};
+void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);
+int attention_splits(int num_sms, int nb, int n_kv, int n_ctx);
+size_t attention_smem(const AttnArgs& a);
+
+// ---- prefill (k_prefill.cu) -------------------------------------------------------------------------------------------
+void launch_embed_rows(cudaStream_t st, const int32_t* ids, int n, QMat emb, float* x);
+void launch_rmsnorm_rows(cudaStream_t st, const float* x, const float* w, float* y, int rows, int dim, float eps);
+// Y[L][N] (+)= X[L][K] . W^T; swiglu: W rows interleaved (gate, up) → Y[L][N/2] = silu(gate) * up
+void launch_gemm_q8_0(cudaStream_t st, const float* x, int L, QMat w, float* y, int accumulate, int swiglu);
+// per-row q/k head norm + RoPE (q in place), K/V rows pos0 + r stored f16
+void launch_qk_norm_rope_store(cudaStream_t st, float* qkv, int L, int n_head, int n_kv, const float* q_norm,
+                               const float* k_norm, const float* rope, int pos0, float eps, __half* kc, __half* vc,
+                               int n_ctx);
+// causal attention of L queries (positions pos0…) over the f16 cache rows 0…pos0+r → out [L][n_head*128]
+void launch_attention_prefill(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
+                              const __half* vc, int n_ctx, int pos0, float scale, float* out);
+
+}  // namespace ocr

@@ -1,0 +1,1335 @@
+// runtime.cu — the host runtime behind ocr_cuda.h: context (device, stream, byte ledger), model (GGUF streaming
+// upload + device repack, or the seeded synthetic generator), session (KV cache, decode scratch, device-side sampler
+// state), prefill, step, and the run-ahead decode loop replaying one captured CUDA graph per token.
+//
+// Reference map (b-straub/historic-htr-ocr): Gpu (app/crates/ocr-wgpu/src/gpu.rs:972-1324), TextModel::load /
+// session / prefill / step / decode_gpu (text.rs:332-625), Choice (text.rs:167-232), TextConfig::from_gguf
+// (text.rs:51-82), rope_table (text.rs:132-142).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+#include "gguf.h"
+#include "kernels.cuh"
+
+namespace ocr {
+
+thread_local std::string g_err;
+void set_error(const std::string& m) { g_err = m; }
+ocr_status fail(ocr_status c, const std::string& m) {
+    g_err = m;
+    return c;
+}
+ocr_status cuda_fail(cudaError_t e, const char* what) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return OCR_ERR_CUDA;
+}
+
+}  // namespace ocr
+
+using namespace ocr;
+
+// ---------------------------------------------------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------------------------------------------------
+struct ocr_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    bool pdl = true;
+    int* d_err = nullptr;
+    uint64_t mem_weights = 0, mem_kv = 0, mem_work = 0;
+    // scratch of the low-level ops (grown on demand, freed with the context)
+    void* op_scratch = nullptr;
+    size_t op_scratch_bytes = 0;
+    // pinned staging for uploads
+    void* h_stage = nullptr;
+    void* d_stage = nullptr;
+    size_t stage_bytes = 0;
+};
+
+namespace {
+
+constexpr size_t STAGE_BYTES = 64u << 20;
+
+cudaError_t dalloc(void** p, size_t n, uint64_t* ctr) {
+    cudaError_t e = cudaMalloc(p, n ? n : 16);
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(*p, 0, n ? n : 16);
+    if (ctr) *ctr += n;
+    return e;
+}
+
+void dfree(void* p, size_t n, uint64_t* ctr) {
+    if (p) cudaFree(p);
+    if (ctr) *ctr -= n;
+}
+
+ocr_status ensure_op_scratch(ocr_ctx* ctx, size_t n) {
+    if (ctx->op_scratch_bytes >= n) return OCR_OK;
+    if (ctx->op_scratch) {
+        OCR_CUDA(cudaStreamSynchronize(ctx->stream));
+        dfree(ctx->op_scratch, ctx->op_scratch_bytes, &ctx->mem_work);
+        ctx->op_scratch = nullptr;
+        ctx->op_scratch_bytes = 0;
+    }
+    OCR_CUDA(dalloc(&ctx->op_scratch, n, &ctx->mem_work));
+    ctx->op_scratch_bytes = n;
+    return OCR_OK;
+}
+
+ocr_status check_device_error(ocr_ctx* ctx) {
+    int err = 0;
+    OCR_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err != DEV_OK) {
+        OCR_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        return fail(OCR_ERR_DEVICE, err == DEV_BAD_POS ? "a kernel saw a position outside the KV cache"
+                                                       : "a kernel saw an index outside its buffer");
+    }
+    return OCR_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------------------------------------------------
+struct LayerW {
+    QMat qkv, o, gu, down;  // qkv rows [q | k | v]; gu rows interleaved (gate 0, up 0, gate 1, …)
+    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct ocr_model {
+    ocr_ctx* ctx = nullptr;
+    ocr_text_cfg cfg{};
+    void* mem = nullptr;
+    size_t mem_bytes = 0;
+    std::vector<LayerW> layers;
+    QMat tok;
+    float* out_norm = nullptr;
+};
+
+namespace {
+
+struct Planner {
+    size_t off = 0;
+    size_t take(size_t n) {
+        const size_t o = off;
+        off = (off + n + 255) / 256 * 256;
+        return o;
+    }
+};
+
+// offsets of every tensor in the model's one allocation
+struct Layout {
+    struct MatOff {
+        size_t q, d;
+        int rows, cols;
+    };
+    struct LayerOff {
+        MatOff qkv, o, gu, down;
+        size_t attn_norm, q_norm, k_norm, ffn_norm;
+    };
+    std::vector<LayerOff> layers;
+    MatOff tok;
+    size_t out_norm, total;
+};
+
+Layout plan(const ocr_text_cfg& c) {
+    Planner p;
+    Layout L;
+    const int qd = c.n_head * c.d_head, kvd = c.n_kv * c.d_head;
+    auto mat = [&](int rows, int cols) {
+        Layout::MatOff m;
+        m.rows = rows;
+        m.cols = cols;
+        m.q = p.take((size_t)rows * cols);
+        m.d = p.take((size_t)rows * (cols / 32) * 2);
+        return m;
+    };
+    for (int l = 0; l < c.n_layer; l++) {
+        Layout::LayerOff lo;
+        lo.qkv = mat(qd + 2 * kvd, c.dim);
+        lo.o = mat(c.dim, qd);
+        lo.gu = mat(2 * c.n_ff, c.dim);
+        lo.down = mat(c.dim, c.n_ff);
+        lo.attn_norm = p.take((size_t)c.dim * 4);
+        lo.q_norm = p.take((size_t)c.d_head * 4);
+        lo.k_norm = p.take((size_t)c.d_head * 4);
+        lo.ffn_norm = p.take((size_t)c.dim * 4);
+        L.layers.push_back(lo);
+    }
+    L.tok = mat(c.n_vocab, c.dim);
+    L.out_norm = p.take((size_t)c.dim * 4);
+    L.total = p.off;
+    return L;
+}
+
+QMat qmat(void* base, const Layout::MatOff& m) {
+    QMat q;
+    q.q = (const int8_t*)((char*)base + m.q);
+    q.d = (const __half*)((char*)base + m.d);
+    q.rows = m.rows;
+    q.cols = m.cols;
+    return q;
+}
+
+ocr_status check_cfg(const ocr_text_cfg& c) {
+    if (c.n_layer < 1 || c.dim < 32 || c.n_head < 1 || c.n_kv < 1 || c.n_ff < 32 || c.n_vocab < 1)
+        return fail(OCR_ERR_ARG, "text config: every dimension must be positive");
+    if (c.d_head != 128) return fail(OCR_ERR_FORMAT, "head dim " + std::to_string(c.d_head) + ": the attention kernels are written for 128");
+    if (c.n_head % c.n_kv != 0) return fail(OCR_ERR_FORMAT, std::to_string(c.n_head) + " q heads on " + std::to_string(c.n_kv) + " kv heads");
+    const int g = c.n_head / c.n_kv;
+    if (g != 1 && g != 2 && g != 4 && g != 8) return fail(OCR_ERR_FORMAT, "GQA groups of 1, 2, 4 or 8 query heads only");
+    if (c.dim % 32 || c.n_ff % 32) return fail(OCR_ERR_FORMAT, "dims " + std::to_string(c.dim) + " / " + std::to_string(c.n_ff) + ": q8_0 rows must be whole blocks");
+    if (c.n_ctx_train < 1) return fail(OCR_ERR_ARG, "n_ctx_train must be positive");
+    return OCR_OK;
+}
+
+ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
+    OCR_TRY(check_cfg(c));
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    Layout L = plan(c);
+    auto* m = new ocr_model;
+    m->ctx = ctx;
+    m->cfg = c;
+    cudaError_t e = dalloc(&m->mem, L.total, &ctx->mem_weights);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "cudaMalloc(weights)");
+    }
+    m->mem_bytes = L.total;
+    for (const auto& lo : L.layers) {
+        LayerW w;
+        w.qkv = qmat(m->mem, lo.qkv);
+        w.o = qmat(m->mem, lo.o);
+        w.gu = qmat(m->mem, lo.gu);
+        w.down = qmat(m->mem, lo.down);
+        w.attn_norm = (float*)((char*)m->mem + lo.attn_norm);
+        w.q_norm = (float*)((char*)m->mem + lo.q_norm);
+        w.k_norm = (float*)((char*)m->mem + lo.k_norm);
+        w.ffn_norm = (float*)((char*)m->mem + lo.ffn_norm);
+        m->layers.push_back(w);
+    }
+    m->tok = qmat(m->mem, L.tok);
+    m->out_norm = (float*)((char*)m->mem + L.out_norm);
+    *out = m;
+    return OCR_OK;
+}
+
+// where a GGUF-level tensor (layer, kind) lives: matrix + its row mapping, or a norm vector
+struct Where {
+    bool is_norm = false;
+    QMat mat;
+    int rows = 0, row_mul = 1, row_add = 0;
+    float* norm = nullptr;
+    int n = 0;
+};
+
+bool where(const ocr_model* m, int layer, int kind, Where& w) {
+    const auto& c = m->cfg;
+    const int qd = c.n_head * c.d_head, kvd = c.n_kv * c.d_head;
+    if (layer < 0) {
+        if (kind == 0) {
+            w.mat = m->tok;
+            w.rows = c.n_vocab;
+            return true;
+        }
+        if (kind == 1) {
+            w.is_norm = true;
+            w.norm = m->out_norm;
+            w.n = c.dim;
+            return true;
+        }
+        return false;
+    }
+    if (layer >= c.n_layer) return false;
+    const LayerW& L = m->layers[layer];
+    switch (kind) {
+    case 0: w.is_norm = true; w.norm = L.attn_norm; w.n = c.dim; return true;
+    case 1: w.mat = L.qkv; w.rows = qd; return true;
+    case 2: w.mat = L.qkv; w.rows = kvd; w.row_add = qd; return true;
+    case 3: w.mat = L.qkv; w.rows = kvd; w.row_add = qd + kvd; return true;
+    case 4: w.mat = L.o; w.rows = c.dim; return true;
+    case 5: w.is_norm = true; w.norm = L.q_norm; w.n = c.d_head; return true;
+    case 6: w.is_norm = true; w.norm = L.k_norm; w.n = c.d_head; return true;
+    case 7: w.is_norm = true; w.norm = L.ffn_norm; w.n = c.dim; return true;
+    case 8: w.mat = L.gu; w.rows = c.n_ff; w.row_mul = 2; return true;
+    case 9: w.mat = L.gu; w.rows = c.n_ff; w.row_mul = 2; w.row_add = 1; return true;
+    case 10: w.mat = L.down; w.rows = c.dim; return true;
+    default: return false;
+    }
+}
+
+ocr_status ensure_stage(ocr_ctx* ctx) {
+    if (ctx->h_stage) return OCR_OK;
+    OCR_CUDA(cudaMallocHost(&ctx->h_stage, STAGE_BYTES));
+    OCR_CUDA(cudaMalloc(&ctx->d_stage, STAGE_BYTES));
+    ctx->stage_bytes = STAGE_BYTES;
+    return OCR_OK;
+}
+
+// stream one GGUF tensor file → pinned staging → device staging → its place (repacked)
+ocr_status upload_tensor(ocr_model* m, const Gguf& g, const GTensor& t, const Where& w) {
+    ocr_ctx* ctx = m->ctx;
+    OCR_TRY(ensure_stage(ctx));
+    std::string msg;
+    if (w.is_norm) {
+        const size_t n = (size_t)w.n * 4;
+        if (!g.src->read_at(t.file_offset, ctx->h_stage, n, msg)) return fail(OCR_ERR_IO, msg);
+        OCR_CUDA(cudaMemcpyAsync(w.norm, ctx->h_stage, n, cudaMemcpyHostToDevice, ctx->stream));
+        OCR_CUDA(cudaStreamSynchronize(ctx->stream));
+        return OCR_OK;
+    }
+    const int cols = w.mat.cols;
+    const size_t row_bytes = (size_t)cols / 32 * 34;
+    const int rows_per = (int)std::max<size_t>(1, ctx->stage_bytes / row_bytes);
+    for (int r0 = 0; r0 < w.rows; r0 += rows_per) {
+        const int nr = std::min(rows_per, w.rows - r0);
+        const size_t n = (size_t)nr * row_bytes;
+        if (!g.src->read_at(t.file_offset + (uint64_t)r0 * row_bytes, ctx->h_stage, n, msg)) return fail(OCR_ERR_IO, msg);
+        OCR_CUDA(cudaMemcpyAsync(ctx->d_stage, ctx->h_stage, n, cudaMemcpyHostToDevice, ctx->stream));
+        launch_repack_q8_0(ctx->stream, (const uint8_t*)ctx->d_stage, nr, cols, const_cast<int8_t*>(w.mat.q),
+                           const_cast<__half*>(w.mat.d), w.row_mul, r0 * w.row_mul + w.row_add);
+        OCR_CUDA(cudaGetLastError());
+        OCR_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return OCR_OK;
+}
+
+// TextConfig::from_gguf (text.rs:51-82)
+ocr_status cfg_from_gguf(const Gguf& g, ocr_text_cfg& c) {
+    std::string msg, arch;
+    if (!g.get_str("general.architecture", arch, msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (arch != "qwen3") return fail(OCR_ERR_FORMAT, "architecture \"" + arch + "\": this engine runs qwen3 only");
+    uint32_t v[8];
+    const char* keys[] = {"qwen3.attention.key_length", "qwen3.attention.value_length", "qwen3.attention.head_count",
+                          "qwen3.attention.head_count_kv", "qwen3.block_count", "qwen3.embedding_length",
+                          "qwen3.feed_forward_length", "qwen3.context_length"};
+    for (int i = 0; i < 8; i++)
+        if (!g.get_u32(keys[i], v[i], msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (v[0] != 128 || v[1] != 128)
+        return fail(OCR_ERR_FORMAT, "head dim " + std::to_string(v[0]) + ": the attention kernels are written for 128");
+    if (v[3] == 0 || v[2] % v[3] != 0)
+        return fail(OCR_ERR_FORMAT, std::to_string(v[2]) + " q heads on " + std::to_string(v[3]) + " kv heads");
+    if (g.has_key("qwen3.rope.scaling.type") || g.has_key("qwen3.rope.dimension_count"))
+        return fail(OCR_ERR_FORMAT, "rope scaling / partial rope in the GGUF: not part of this engine's graph");
+    const GTensor* tok = g.info("token_embd.weight");
+    if (!tok) return fail(OCR_ERR_FORMAT, "GGUF has no tensor token_embd.weight");
+    c.d_head = (int)v[0];
+    c.n_head = (int)v[2];
+    c.n_kv = (int)v[3];
+    c.n_layer = (int)v[4];
+    c.dim = (int)v[5];
+    c.n_ff = (int)v[6];
+    c.n_ctx_train = (int)v[7];
+    if (!g.get_f32("qwen3.attention.layer_norm_rms_epsilon", c.eps, msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (!g.get_f32("qwen3.rope.freq_base", c.rope_base, msg)) return fail(OCR_ERR_FORMAT, msg);
+    c.n_vocab = (int)tok->shape.back();
+    return OCR_OK;
+}
+
+// TextModel::load (text.rs:332-375) from a parsed GGUF
+ocr_status load_gguf(ocr_ctx* ctx, Gguf& g, ocr_model** out) {
+    ocr_text_cfg c{};
+    OCR_TRY(cfg_from_gguf(g, c));
+    const int qd = c.n_head * c.d_head;
+    if (c.dim % 32 != 0 || c.n_ff % 32 != 0 || qd % 32 != 0)
+        return fail(OCR_ERR_FORMAT, "dims " + std::to_string(c.dim) + " / " + std::to_string(c.n_ff) + " / " +
+                                        std::to_string(qd) + ": q8_0 rows must be whole blocks");
+    // the graph's tensors: refuse what the engine does not run (text.rs:341-366)
+    for (int i = 0; i < c.n_layer; i++) {
+        for (const char* absent : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"}) {
+            const std::string b = "blk." + std::to_string(i) + "." + absent + ".bias";
+            if (g.has(b)) return fail(OCR_ERR_FORMAT, b + " is in the GGUF but not part of this engine's graph");
+        }
+        if (g.has("blk." + std::to_string(i) + ".attn_qkv.weight"))
+            return fail(OCR_ERR_FORMAT, "blk." + std::to_string(i) + ": a fused attn_qkv — this engine reads separate q / k / v");
+    }
+    if (g.has("output.weight")) return fail(OCR_ERR_FORMAT, "output.weight is in the GGUF: this engine ties the output to token_embd");
+    ocr_model* m = nullptr;
+    OCR_TRY(model_alloc(ctx, c, &m));
+    static const char* names[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm",
+                                  "attn_k_norm", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+    auto load_one = [&](int layer, int kind, const std::string& name) -> ocr_status {
+        Where w;
+        where(m, layer, kind, w);
+        const GTensor* t = g.info(name);
+        if (!t) return fail(OCR_ERR_FORMAT, "GGUF has no tensor " + name);
+        if (w.is_norm) {
+            if (t->type != GType::F32 || t->shape.size() != 1 || t->shape[0] != (uint64_t)w.n)
+                return fail(OCR_ERR_FORMAT, name + ": expected F32 [" + std::to_string(w.n) + "]");
+        } else {
+            if (t->shape.size() != 2 || t->shape[0] != (uint64_t)w.mat.cols || t->shape[1] != (uint64_t)w.rows)
+                return fail(OCR_ERR_FORMAT, name + ": shape, expected [" + std::to_string(w.mat.cols) + ", " + std::to_string(w.rows) + "]");
+            if (t->type != GType::Q8_0) return fail(OCR_ERR_FORMAT, name + ": the text decoder's kernels read q8_0 weights");
+        }
+        return upload_tensor(m, g, *t, w);
+    };
+    ocr_status st = OCR_OK;
+    for (int l = 0; l < c.n_layer && st == OCR_OK; l++)
+        for (int k = 0; k < 11 && st == OCR_OK; k++)
+            st = load_one(l, k, "blk." + std::to_string(l) + "." + names[k] + ".weight");
+    if (st == OCR_OK) st = load_one(-1, 0, "token_embd.weight");
+    if (st == OCR_OK) st = load_one(-1, 1, "output_norm.weight");
+    if (st != OCR_OK) {
+        std::string keep = g_err;
+        ocr_model_destroy(m);
+        g_err = keep;
+        return st;
+    }
+    *out = m;
+    return OCR_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------------
+// session
+// ---------------------------------------------------------------------------------------------------------------------
+struct ocr_session {
+    ocr_model* m = nullptr;
+    ocr_ctx* ctx = nullptr;
+    int n_ctx = 0, B = 0, qkv_w = 0, qd = 0, splits = 1;
+    __half *kc = nullptr, *vc = nullptr;
+    size_t kv_bytes = 0;
+    void* work = nullptr;
+    size_t work_bytes = 0;
+    float *rope = nullptr, *x = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
+    float *lm_part = nullptr, *at_part = nullptr;
+    uint32_t *lm_done = nullptr, *at_done = nullptr;
+    int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
+    int32_t* hist = nullptr;
+    int hist_cap = 0;
+    uint32_t* counts = nullptr;
+    float* fpen = nullptr;
+    std::vector<int> n_past, has_logits;
+    // prefill scratch
+    void* pf = nullptr;
+    size_t pf_bytes = 0;
+    // the decode step's graph and what it was captured with
+    cudaGraphExec_t gexec = nullptr;
+    float g_rp = 0, g_fp = 0;
+    int g_window = -1, g_use_fp = -1;
+    int32_t* g_hist = nullptr;
+    int32_t* h_ids = nullptr;  // pinned readback
+    size_t h_ids_n = 0;
+    std::vector<cudaEvent_t> step_ev;  // run-ahead: one event per queued step (ring)
+
+    __half* kcl(int l) const { return kc + (size_t)l * B * m->cfg.n_kv * n_ctx * 128; }
+    __half* vcl(int l) const { return vc + (size_t)l * B * m->cfg.n_kv * n_ctx * 128; }
+};
+
+namespace {
+
+// one decode step of every active slot: 5 kernels per layer + the LM head (with the choice when sample)
+void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp) {
+    const ocr_model* m = s->m;
+    const auto& c = m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    const bool pdl = ctx->pdl;
+    for (int l = 0; l < c.n_layer; l++) {
+        const LayerW& L = m->layers[l];
+        MvArgs q;
+        q.w = L.qkv;
+        q.nw = L.attn_norm;
+        q.eps = c.eps;
+        q.y = s->qkv;
+        q.y_stride = s->qkv_w;
+        q.nb = s->B;
+        q.active = s->active;
+        q.mode = MV_STORE;
+        q.x_stride = c.dim;
+        if (l == 0) {
+            q.tok = s->tok;
+            q.emb = m->tok;
+            q.x_out = s->x;
+        } else {
+            q.x = s->x;
+        }
+        launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
+
+        AttnArgs a;
+        a.qkv = s->qkv;
+        a.qkv_stride = s->qkv_w;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.rope = s->rope;
+        a.kc = s->kcl(l);
+        a.vc = s->vcl(l);
+        a.pos = s->pos;
+        a.active = s->active;
+        a.n_head = c.n_head;
+        a.n_kv = c.n_kv;
+        a.n_ctx = s->n_ctx;
+        a.splits = s->splits;
+        a.eps = c.eps;
+        a.scale = 1.0f / sqrtf((float)c.d_head);
+        a.part = s->at_part;
+        a.done = s->at_done;
+        a.out = s->attn;
+        a.out_stride = s->qd;
+        a.nb = s->B;
+        a.err = ctx->d_err;
+        launch_attention_decode(st, a, pdl);
+
+        MvArgs o;
+        o.w = L.o;
+        o.x = s->attn;
+        o.x_stride = s->qd;
+        o.y = s->x;
+        o.y_stride = c.dim;
+        o.mode = MV_ADD;
+        o.nb = s->B;
+        o.active = s->active;
+        launch_matvec(st, o, ctx->num_sms, pdl);
+
+        MvArgs f;
+        f.w = L.gu;
+        f.x = s->x;
+        f.x_stride = c.dim;
+        f.nw = L.ffn_norm;
+        f.eps = c.eps;
+        f.y = s->g;
+        f.y_stride = c.n_ff;
+        f.mode = MV_SWIGLU;
+        f.nb = s->B;
+        f.active = s->active;
+        launch_matvec(st, f, ctx->num_sms, pdl);
+
+        MvArgs dn;
+        dn.w = L.down;
+        dn.x = s->g;
+        dn.x_stride = c.n_ff;
+        dn.y = s->x;
+        dn.y_stride = c.dim;
+        dn.mode = MV_ADD;
+        dn.nb = s->B;
+        dn.active = s->active;
+        launch_matvec(st, dn, ctx->num_sms, pdl);
+    }
+    LmArgs lm;
+    lm.w = m->tok;
+    lm.x = s->x;
+    lm.x_stride = c.dim;
+    lm.nw = m->out_norm;
+    lm.eps = c.eps;
+    lm.nb = s->B;
+    lm.logits = s->logits;
+    lm.sample = sample ? 1 : 0;
+    lm.rp = rp;
+    lm.window = window;
+    lm.use_fp = use_fp;
+    lm.fp = fp;
+    lm.hist = s->hist;
+    lm.hist_cap = s->hist_cap;
+    lm.len = s->len;
+    lm.tok = s->tok;
+    lm.pos = s->pos;
+    lm.advance_pos = sample ? 1 : 0;
+    lm.counts = s->counts;
+    lm.fpen = s->fpen;
+    lm.active = s->active;
+    lm.part = s->lm_part;
+    lm.done = s->lm_done;
+    lm.err = ctx->d_err;
+    launch_lm_head(st, lm, ctx->num_sms, pdl);
+}
+
+// rope_table (text.rs:132-142): theta = (f32)pos * base^(-2i/d) in f32, (cos, sin) by the host libm
+std::vector<float> rope_table(float base, int d, int n_pos) {
+    std::vector<float> out((size_t)n_pos * d);
+    const int half = d / 2;
+    for (int p = 0; p < n_pos; p++)
+        for (int i = 0; i < half; i++) {
+            const float theta = (float)p * powf(base, -(float)(2 * i) / (float)d);
+            out[((size_t)p * half + i) * 2] = cosf(theta);
+            out[((size_t)p * half + i) * 2 + 1] = sinf(theta);
+        }
+    return out;
+}
+
+ocr_status ensure_hist(ocr_session* s, int need) {
+    if (s->hist_cap >= need) return OCR_OK;
+    int cap = std::max(need, std::max(4096, s->hist_cap * 2));
+    OCR_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    if (s->hist) dfree(s->hist, (size_t)s->B * s->hist_cap * 4, &s->ctx->mem_work);
+    OCR_CUDA(dalloc((void**)&s->hist, (size_t)s->B * cap * 4, &s->ctx->mem_work));
+    s->hist_cap = cap;
+    if (s->h_ids) cudaFreeHost(s->h_ids);
+    OCR_CUDA(cudaMallocHost((void**)&s->h_ids, (size_t)s->B * cap * 4));
+    s->h_ids_n = (size_t)s->B * cap;
+    return OCR_OK;
+}
+
+ocr_status ensure_counts(ocr_session* s) {
+    if (s->counts) return OCR_OK;
+    const size_t n = (size_t)s->B * s->m->cfg.n_vocab;
+    OCR_CUDA(dalloc((void**)&s->counts, n * 4, &s->ctx->mem_work));
+    OCR_CUDA(dalloc((void**)&s->fpen, n * 4, &s->ctx->mem_work));
+    return OCR_OK;
+}
+
+// gpu_choice_capable (text.rs:154-163) + Preset::validate's ranges (presets.rs:37-57)
+ocr_status check_sampler(const ocr_sampler_cfg* cfg) {
+    if (!cfg) return fail(OCR_ERR_ARG, "no sampler config");
+    if (cfg->rp != 1.0f && !(std::isnormal(cfg->rp) && cfg->rp > 0.0f))
+        return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
+    if (cfg->window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
+    if (!(cfg->fp >= 0.0f)) return fail(OCR_ERR_ARG, "frequency penalty must be >= 0");
+    if (cfg->max_new < 1) return fail(OCR_ERR_ARG, "max_new must be >= 1");
+    return OCR_OK;
+}
+
+LmArgs sampler_args(ocr_session* s, const ocr_sampler_cfg* cfg) {
+    LmArgs a;
+    a.nb = s->B;
+    a.sample = 1;
+    a.rp = cfg->rp;
+    a.window = cfg->window;
+    a.use_fp = cfg->fp > 0.0f ? 1 : 0;
+    a.fp = cfg->fp;
+    a.hist = s->hist;
+    a.hist_cap = s->hist_cap;
+    a.len = s->len;
+    a.tok = s->tok;
+    a.pos = s->pos;
+    a.counts = s->counts;
+    a.fpen = s->fpen;
+    a.active = s->active;
+    a.part = s->lm_part;
+    a.done = s->lm_done;
+    a.err = s->ctx->d_err;
+    return a;
+}
+
+ocr_status capture_graph(ocr_session* s, const ocr_sampler_cfg* cfg) {
+    const int use_fp = cfg->fp > 0.0f ? 1 : 0;
+    if (s->gexec && s->g_rp == cfg->rp && s->g_window == cfg->window && s->g_use_fp == use_fp && s->g_fp == cfg->fp &&
+        s->g_hist == s->hist)
+        return OCR_OK;
+    if (s->gexec) {
+        cudaGraphExecDestroy(s->gexec);
+        s->gexec = nullptr;
+    }
+    cudaStream_t st = s->ctx->stream;
+    cudaGraph_t graph;
+    OCR_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    record_step(s, true, cfg->rp, cfg->window, use_fp, cfg->fp);
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture(decode step)");
+    e = cudaGraphInstantiate(&s->gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate(decode step)");
+    s->g_rp = cfg->rp;
+    s->g_window = cfg->window;
+    s->g_use_fp = use_fp;
+    s->g_fp = cfg->fp;
+    s->g_hist = s->hist;
+    return OCR_OK;
+}
+
+// the shared decode loop: slots [s0, s0 + ns) active, history [ns][n_hist], up to max_new choices each
+ocr_status decode_slots(ocr_session* s, int s0, int ns, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
+                        ocr_token_cb cb, void* user, int32_t* ids_out, int* n_out) {
+    OCR_TRY(check_sampler(cfg));
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    const int max_new = cfg->max_new;
+    if (n_hist < 0 || (n_hist > 0 && !history)) return fail(OCR_ERR_ARG, "history: bad length or null");
+    const int seed = std::min(n_hist, cfg->window);
+    for (int k = 0; k < ns; k++) {
+        const int b = s0 + k;
+        if (!s->has_logits[b]) return fail(OCR_ERR_STATE, "slot " + std::to_string(b) + ": no logits yet (prefill first)");
+        if (s->n_past[b] + max_new - 1 > s->n_ctx)
+            return fail(OCR_ERR_STATE, std::to_string(max_new) + " choices: slot " + std::to_string(b) + " at " +
+                                           std::to_string(s->n_past[b]) + " overflows the session's " + std::to_string(s->n_ctx));
+        for (int i = n_hist - seed; i < n_hist; i++) {
+            const int32_t t = history[(size_t)k * n_hist + i];
+            if (t < 0 || t >= c.n_vocab) return fail(OCR_ERR_ARG, "history token " + std::to_string(t) + " is outside the vocabulary");
+        }
+    }
+    OCR_TRY(ensure_hist(s, seed + max_new));
+    if (cfg->fp > 0.0f) OCR_TRY(ensure_counts(s));
+    // device-side state: window seeds, lengths, positions, the active mask
+    std::vector<int32_t> hseed((size_t)ns * s->hist_cap, 0), len(s->B, 0), pos(s->B, 0), act(s->B, 0);
+    for (int b = 0; b < s->B; b++) pos[b] = s->n_past[b];
+    for (int k = 0; k < ns; k++) {
+        const int b = s0 + k;
+        for (int i = 0; i < seed; i++) hseed[(size_t)k * s->hist_cap + i] = history[(size_t)k * n_hist + n_hist - seed + i];
+        len[b] = seed;
+        act[b] = 1;
+    }
+    OCR_CUDA(cudaMemcpyAsync(s->hist + (size_t)s0 * s->hist_cap, hseed.data(), hseed.size() * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->len, len.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    if (cfg->fp > 0.0f) {
+        const size_t n = (size_t)ns * c.n_vocab;
+        OCR_CUDA(cudaMemsetAsync(s->counts + (size_t)s0 * c.n_vocab, 0, n * 4, st));
+        OCR_CUDA(cudaMemsetAsync(s->fpen + (size_t)s0 * c.n_vocab, 0, n * 4, st));
+    }
+    // choice 0 from the current logits
+    LmArgs sa = sampler_args(s, cfg);
+    launch_sample(st, s->logits, c.n_vocab, c.n_vocab, sa, ctx->num_sms, s0, ns);
+    OCR_CUDA(cudaGetLastError());
+    int steps = 0;
+    int delivered = 0;
+    bool stopped = false;
+    const int chunk = 8;
+    const int ring = 4 * chunk;
+    if (cb && ns == 1 && s->step_ev.empty()) {
+        s->step_ev.resize(ring);
+        for (auto& e : s->step_ev) OCR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    // choices [delivered, upto) of slot s0 to the callback, once the step that made choice upto - 1 is done
+    auto deliver = [&](int upto) -> ocr_status {
+        if (upto <= delivered) return OCR_OK;
+        if (upto - 1 >= 1) OCR_CUDA(cudaEventSynchronize(s->step_ev[(upto - 1) % ring]));
+        else OCR_CUDA(cudaStreamSynchronize(st));
+        OCR_CUDA(cudaMemcpy(s->h_ids, s->hist + (size_t)s0 * s->hist_cap + seed + delivered,
+                            (size_t)(upto - delivered) * 4, cudaMemcpyDeviceToHost));
+        for (int i = delivered; i < upto; i++) {
+            ids_out[i] = s->h_ids[i - delivered];
+            if (!cb(user, ids_out[i])) {
+                stopped = true;
+                delivered = i + 1;
+                return OCR_OK;
+            }
+        }
+        delivered = upto;
+        return OCR_OK;
+    };
+    auto mark = [&](int step) -> ocr_status {
+        if (cb && ns == 1) OCR_CUDA(cudaEventRecord(s->step_ev[step % ring], st));
+        return OCR_OK;
+    };
+    if (max_new > 1) {
+        // step 1 runs eagerly (it also settles every launcher's one-time setup), then the captured graph
+        record_step(s, true, cfg->rp, cfg->window, cfg->fp > 0.0f ? 1 : 0, cfg->fp);
+        OCR_CUDA(cudaGetLastError());
+        steps = 1;
+        OCR_TRY(mark(steps));
+        if (max_new > 2) OCR_TRY(capture_graph(s, cfg));
+        while (steps < max_new - 1 && !stopped) {
+            OCR_CUDA(cudaGraphLaunch(s->gexec, st));
+            steps++;
+            OCR_TRY(mark(steps));
+            // keep 2 chunks queued ahead of the callback (the reference's run-ahead: chunk x depth 2)
+            if (cb && ns == 1 && (steps + 1) - delivered >= 3 * chunk) OCR_TRY(deliver(steps + 1 - 2 * chunk));
+        }
+    }
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    if (cb && ns == 1) {
+        if (!stopped) OCR_TRY(deliver(max_new));
+        if (n_out) *n_out = delivered;
+    } else {
+        for (int k = 0; k < ns; k++)
+            OCR_CUDA(cudaMemcpy(ids_out + (size_t)k * max_new, s->hist + (size_t)(s0 + k) * s->hist_cap + seed,
+                                (size_t)max_new * 4, cudaMemcpyDeviceToHost));
+        if (n_out) *n_out = max_new;
+    }
+    for (int k = 0; k < ns; k++) s->n_past[s0 + k] += steps;
+    return OCR_OK;
+}
+
+ocr_status ensure_prefill(ocr_session* s, int n) {
+    const auto& c = s->m->cfg;
+    const size_t per_row = (size_t)c.dim * 2 + s->qkv_w + s->qd + c.n_ff + 1;
+    const size_t need = per_row * n * 4 + 4096;
+    if (s->pf_bytes >= need) return OCR_OK;
+    OCR_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    if (s->pf) dfree(s->pf, s->pf_bytes, &s->ctx->mem_work);
+    s->pf = nullptr;
+    s->pf_bytes = 0;
+    OCR_CUDA(dalloc(&s->pf, need, &s->ctx->mem_work));
+    s->pf_bytes = need;
+    return OCR_OK;
+}
+
+}  // namespace
+
+// =====================================================================================================================
+// the C ABI
+// =====================================================================================================================
+extern "C" {
+
+const char* ocr_last_error(void) { return g_err.c_str(); }
+const char* ocr_version(void) { return "libocrcuda 0.1 (sm_100a)"; }
+
+ocr_status ocr_ctx_create(int device, ocr_ctx** out) {
+    if (!out) return fail(OCR_ERR_ARG, "out is null");
+    int n = 0;
+    OCR_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(OCR_ERR_ARG, "device " + std::to_string(device) + " of " + std::to_string(n));
+    OCR_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    OCR_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return fail(OCR_ERR_CUDA, std::string("device ") + prop.name + ": sm_100a (B200) required");
+    auto* c = new ocr_ctx;
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    const char* pdl = getenv("OCR_PDL");
+    c->pdl = !(pdl && pdl[0] == '0');
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = dalloc((void**)&c->d_err, sizeof(int), nullptr);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "ocr_ctx_create");
+    }
+    *out = c;
+    return OCR_OK;
+}
+
+ocr_status ocr_ctx_destroy(ocr_ctx* c) {
+    if (!c) return OCR_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->op_scratch) cudaFree(c->op_scratch);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->d_stage) cudaFree(c->d_stage);
+    if (c->d_err) cudaFree(c->d_err);
+    cudaStreamDestroy(c->stream);
+    delete c;
+    return OCR_OK;
+}
+
+ocr_status ocr_ctx_sync(ocr_ctx* c) {
+    if (!c) return fail(OCR_ERR_ARG, "ctx is null");
+    OCR_CUDA(cudaStreamSynchronize(c->stream));
+    OCR_CUDA(cudaGetLastError());
+    return check_device_error(c);
+}
+
+ocr_status ocr_ctx_stream(ocr_ctx* c, void** stream) {
+    if (!c || !stream) return fail(OCR_ERR_ARG, "null argument");
+    *stream = (void*)c->stream;
+    return OCR_OK;
+}
+
+ocr_status ocr_ctx_memory(ocr_ctx* c, uint64_t* w, uint64_t* kv, uint64_t* work) {
+    if (!c) return fail(OCR_ERR_ARG, "ctx is null");
+    if (w) *w = c->mem_weights;
+    if (kv) *kv = c->mem_kv;
+    if (work) *work = c->mem_work;
+    return OCR_OK;
+}
+
+ocr_status ocr_model_load_gguf(ocr_ctx* ctx, const char* path, ocr_model** out) {
+    if (!ctx || !path || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg;
+    auto src = file_source(path, msg);
+    if (!src) return fail(OCR_ERR_IO, msg);
+    Gguf g;
+    if (!g.parse(std::move(src), msg)) return fail(OCR_ERR_FORMAT, std::string(path) + " is not a readable GGUF: " + msg);
+    return load_gguf(ctx, g, out);
+}
+
+ocr_status ocr_model_load_gguf_memory(ocr_ctx* ctx, const void* bytes, size_t n, ocr_model** out) {
+    if (!ctx || !bytes || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg;
+    Gguf g;
+    if (!g.parse(memory_source(bytes, n), msg)) return fail(OCR_ERR_FORMAT, "not a readable GGUF: " + msg);
+    return load_gguf(ctx, g, out);
+}
+
+ocr_status ocr_model_synthetic(ocr_ctx* ctx, const ocr_text_cfg* cfg, uint64_t seed, float sigma_w, float sigma_e,
+                               ocr_model** out) {
+    if (!ctx || !cfg || !out) return fail(OCR_ERR_ARG, "null argument");
+    ocr_model* m = nullptr;
+    OCR_TRY(model_alloc(ctx, *cfg, &m));
+    // sub-stream k of the model seed per tensor (the CPU generator's numbering: layer * 16 + kind, token_embd 100000,
+    // output_norm 100001); the sub-stream seed is output k of SplitMix64 seeded with seed ^ "ocr-b200"
+    auto sub = [&](uint64_t k) {
+        uint64_t z = (seed ^ 0x6F63722D62323030ull) + (k + 1) * 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    cudaStream_t st = ctx->stream;
+    for (int l = 0; l < cfg->n_layer; l++)
+        for (int k = 0; k < 11; k++) {
+            Where w;
+            where(m, l, k, w);
+            const uint64_t ss = sub((uint64_t)l * 16 + k);
+            if (w.is_norm) launch_synth_norm(st, ss, w.n, w.norm);
+            else
+                launch_synth_q8_0(st, ss, sigma_w, w.rows, w.mat.cols, const_cast<int8_t*>(w.mat.q),
+                                  const_cast<__half*>(w.mat.d), w.row_mul, w.row_add);
+        }
+    launch_synth_q8_0(st, sub(100000), sigma_e, cfg->n_vocab, cfg->dim, const_cast<int8_t*>(m->tok.q),
+                      const_cast<__half*>(m->tok.d), 1, 0);
+    launch_synth_norm(st, sub(100001), cfg->dim, m->out_norm);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        ocr_model_destroy(m);
+        return cuda_fail(e, "ocr_model_synthetic");
+    }
+    *out = m;
+    return OCR_OK;
+}
+
+ocr_status ocr_model_config(const ocr_model* m, ocr_text_cfg* out) {
+    if (!m || !out) return fail(OCR_ERR_ARG, "null argument");
+    *out = m->cfg;
+    return OCR_OK;
+}
+
+ocr_status ocr_model_tensor_gguf(const ocr_model* m, int layer, int kind, void* out, size_t* n_bytes) {
+    if (!m || !n_bytes) return fail(OCR_ERR_ARG, "null argument");
+    Where w;
+    if (!where(m, layer, kind, w)) return fail(OCR_ERR_ARG, "no tensor (layer " + std::to_string(layer) + ", kind " + std::to_string(kind) + ")");
+    const size_t need = w.is_norm ? (size_t)w.n * 4 : (size_t)w.rows * (w.mat.cols / 32) * 34;
+    if (!out) {
+        *n_bytes = need;
+        return OCR_OK;
+    }
+    if (*n_bytes < need) return fail(OCR_ERR_ARG, "output buffer too small");
+    ocr_ctx* ctx = m->ctx;
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    if (w.is_norm) {
+        OCR_CUDA(cudaMemcpy(out, w.norm, need, cudaMemcpyDeviceToHost));
+    } else {
+        void* d = nullptr;
+        OCR_CUDA(cudaMalloc(&d, need));
+        launch_unpack_q8_0(ctx->stream, w.mat.q, w.mat.d, w.rows, w.mat.cols, w.row_mul, w.row_add, (uint8_t*)d);
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpy(out, d, need, cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        if (e != cudaSuccess) return cuda_fail(e, "ocr_model_tensor_gguf");
+    }
+    *n_bytes = need;
+    return OCR_OK;
+}
+
+ocr_status ocr_model_checksum(const ocr_model* m, uint64_t* out) {
+    if (!m || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::vector<uint8_t> h(m->mem_bytes);
+    OCR_CUDA(cudaSetDevice(m->ctx->device));
+    OCR_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    OCR_CUDA(cudaMemcpy(h.data(), m->mem, m->mem_bytes, cudaMemcpyDeviceToHost));
+    uint64_t x = 0xcbf29ce484222325ull;
+    for (uint8_t b : h) x = (x ^ b) * 0x100000001b3ull;
+    *out = x;
+    return OCR_OK;
+}
+
+ocr_status ocr_model_destroy(ocr_model* m) {
+    if (!m) return OCR_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    dfree(m->mem, m->mem_bytes, &m->ctx->mem_weights);
+    delete m;
+    return OCR_OK;
+}
+
+ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** out) {
+    if (!m || !out) return fail(OCR_ERR_ARG, "null argument");
+    const auto& c = m->cfg;
+    if (n_ctx < 1 || batch < 1) return fail(OCR_ERR_ARG, "n_ctx and batch must be >= 1");
+    if (n_ctx > c.n_ctx_train) return fail(OCR_ERR_ARG, std::to_string(n_ctx) + " positions asked, the model was trained on " + std::to_string(c.n_ctx_train));
+    ocr_ctx* ctx = m->ctx;
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    auto* s = new ocr_session;
+    s->m = m;
+    s->ctx = ctx;
+    s->n_ctx = n_ctx;
+    s->B = batch;
+    s->qd = c.n_head * c.d_head;
+    s->qkv_w = (c.n_head + 2 * c.n_kv) * c.d_head;
+    s->splits = attention_splits(ctx->num_sms, batch, c.n_kv, n_ctx);
+    s->n_past.assign(batch, 0);
+    s->has_logits.assign(batch, 0);
+    s->kv_bytes = (size_t)c.n_layer * batch * c.n_kv * n_ctx * 128 * 2;
+    cudaError_t e = dalloc((void**)&s->kc, s->kv_bytes, &ctx->mem_kv);
+    if (e == cudaSuccess) e = dalloc((void**)&s->vc, s->kv_bytes, &ctx->mem_kv);
+    // work: rope, x, qkv, attn, g, logits, partials, counters, state
+    const int lm_grid = std::max(lm_head_grid(ctx->num_sms), sample_grid(ctx->num_sms));
+    Planner p;
+    const size_t o_rope = p.take((size_t)n_ctx * c.d_head * 4);
+    const size_t o_x = p.take((size_t)batch * c.dim * 4);
+    const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
+    const size_t o_attn = p.take((size_t)batch * s->qd * 4);
+    const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
+    const size_t o_logits = p.take((size_t)batch * c.n_vocab * 4);
+    const size_t o_lmp = p.take(((size_t)batch * lm_grid * 2 + batch) * 4);
+    const size_t o_atp = p.take((size_t)batch * c.n_head * s->splits * 130 * 4);
+    const size_t o_lmd = p.take((size_t)(batch + 64) * 4);
+    const size_t o_atd = p.take((size_t)batch * c.n_kv * 4);
+    const size_t o_state = p.take((size_t)batch * 4 * 4);
+    if (e == cudaSuccess) e = dalloc(&s->work, p.off, &ctx->mem_work);
+    if (e != cudaSuccess) {
+        ocr_session_destroy(s);
+        return cuda_fail(e, "ocr_session_create (device memory)");
+    }
+    s->work_bytes = p.off;
+    char* w = (char*)s->work;
+    s->rope = (float*)(w + o_rope);
+    s->x = (float*)(w + o_x);
+    s->qkv = (float*)(w + o_qkv);
+    s->attn = (float*)(w + o_attn);
+    s->g = (float*)(w + o_g);
+    s->logits = (float*)(w + o_logits);
+    s->lm_part = (float*)(w + o_lmp);
+    s->at_part = (float*)(w + o_atp);
+    s->lm_done = (uint32_t*)(w + o_lmd);
+    s->at_done = (uint32_t*)(w + o_atd);
+    s->pos = (int32_t*)(w + o_state);
+    s->len = s->pos + batch;
+    s->tok = s->len + batch;
+    s->active = s->tok + batch;
+    const std::vector<float> cs = rope_table(c.rope_base, c.d_head, n_ctx);
+    e = cudaMemcpy(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        ocr_status st = ensure_hist(s, 4096);
+        if (st != OCR_OK) {
+            ocr_session_destroy(s);
+            return st;
+        }
+    }
+    if (e != cudaSuccess) {
+        ocr_session_destroy(s);
+        return cuda_fail(e, "ocr_session_create (rope table)");
+    }
+    *out = s;
+    return OCR_OK;
+}
+
+ocr_status ocr_session_destroy(ocr_session* s) {
+    if (!s) return OCR_OK;
+    ocr_ctx* ctx = s->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (s->gexec) cudaGraphExecDestroy(s->gexec);
+    if (s->kc) dfree(s->kc, s->kv_bytes, &ctx->mem_kv);
+    if (s->vc) dfree(s->vc, s->kv_bytes, &ctx->mem_kv);
+    if (s->work) dfree(s->work, s->work_bytes, &ctx->mem_work);
+    if (s->hist) dfree(s->hist, (size_t)s->B * s->hist_cap * 4, &ctx->mem_work);
+    if (s->counts) dfree(s->counts, (size_t)s->B * s->m->cfg.n_vocab * 4, &ctx->mem_work);
+    if (s->fpen) dfree(s->fpen, (size_t)s->B * s->m->cfg.n_vocab * 4, &ctx->mem_work);
+    if (s->pf) dfree(s->pf, s->pf_bytes, &ctx->mem_work);
+    if (s->h_ids) cudaFreeHost(s->h_ids);
+    for (cudaEvent_t e : s->step_ev) cudaEventDestroy(e);
+    delete s;
+    return OCR_OK;
+}
+
+ocr_status ocr_session_n_past(const ocr_session* s, int slot, int* out) {
+    if (!s || !out) return fail(OCR_ERR_ARG, "null argument");
+    if (slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "slot out of range");
+    *out = s->n_past[slot];
+    return OCR_OK;
+}
+
+ocr_status ocr_session_rewind(ocr_session* s, int slot, int n_past) {
+    if (!s) return fail(OCR_ERR_ARG, "null argument");
+    if (slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "slot out of range");
+    if (n_past < 0 || n_past > s->n_past[slot]) return fail(OCR_ERR_ARG, "rewind beyond the slot's positions");
+    s->n_past[slot] = n_past;
+    s->has_logits[slot] = 0;
+    return OCR_OK;
+}
+
+ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float* embd, int n, float* logits_out) {
+    if (!s) return fail(OCR_ERR_ARG, "null session");
+    if (slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "slot out of range");
+    if (n <= 0) return fail(OCR_ERR_ARG, "empty prompt");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    if (s->n_past[slot] + n > s->n_ctx)
+        return fail(OCR_ERR_STATE, std::to_string(s->n_past[slot]) + " + " + std::to_string(n) + " positions overflow the session's " + std::to_string(s->n_ctx));
+    bool any_embd = false;
+    for (int i = 0; i < n; i++) {
+        if (ids && ids[i] >= c.n_vocab) return fail(OCR_ERR_ARG, "token " + std::to_string(ids[i]) + " is outside the vocabulary");
+        if (!ids || ids[i] < 0) any_embd = true;
+    }
+    if (any_embd && !embd) return fail(OCR_ERR_ARG, "embedding rows asked but embd is null");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    OCR_TRY(ensure_prefill(s, n));
+    cudaStream_t st = ctx->stream;
+    float* x = (float*)s->pf;
+    float* h = x + (size_t)n * c.dim;
+    float* qkv = h + (size_t)n * c.dim;
+    float* a = qkv + (size_t)n * s->qkv_w;
+    float* g = a + (size_t)n * s->qd;
+    int32_t* d_ids = (int32_t*)(g + (size_t)n * c.n_ff);
+    std::vector<int32_t> hid(n);
+    for (int i = 0; i < n; i++) hid[i] = ids ? ids[i] : -1;
+    if (any_embd) OCR_CUDA(cudaMemcpyAsync(x, embd, (size_t)n * c.dim * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(d_ids, hid.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    launch_embed_rows(st, d_ids, n, s->m->tok, x);
+    const int pos0 = s->n_past[slot];
+    const float scale = 1.0f / sqrtf((float)c.d_head);
+    for (int l = 0; l < c.n_layer; l++) {
+        const LayerW& L = s->m->layers[l];
+        __half* kc = s->kcl(l) + (size_t)slot * c.n_kv * s->n_ctx * 128;
+        __half* vc = s->vcl(l) + (size_t)slot * c.n_kv * s->n_ctx * 128;
+        launch_rmsnorm_rows(st, x, L.attn_norm, h, n, c.dim, c.eps);
+        launch_gemm_q8_0(st, h, n, L.qkv, qkv, 0, 0);
+        launch_qk_norm_rope_store(st, qkv, n, c.n_head, c.n_kv, L.q_norm, L.k_norm, s->rope, pos0, c.eps, kc, vc, s->n_ctx);
+        launch_attention_prefill(st, qkv, n, c.n_head, c.n_kv, kc, vc, s->n_ctx, pos0, scale, a);
+        launch_gemm_q8_0(st, a, n, L.o, x, 1, 0);
+        launch_rmsnorm_rows(st, x, L.ffn_norm, h, n, c.dim, c.eps);
+        launch_gemm_q8_0(st, h, n, L.gu, g, 0, 1);
+        launch_gemm_q8_0(st, g, n, L.down, x, 1, 0);
+    }
+    LmArgs lm;
+    lm.w = s->m->tok;
+    lm.x = x + (size_t)(n - 1) * c.dim;
+    lm.x_stride = c.dim;
+    lm.nw = s->m->out_norm;
+    lm.eps = c.eps;
+    lm.nb = 1;
+    lm.logits = s->logits + (size_t)slot * c.n_vocab;
+    lm.part = s->lm_part;
+    lm.done = s->lm_done;
+    launch_lm_head(st, lm, ctx->num_sms, false);
+    OCR_CUDA(cudaGetLastError());
+    if (logits_out)
+        OCR_CUDA(cudaMemcpyAsync(logits_out, s->logits + (size_t)slot * c.n_vocab, (size_t)c.n_vocab * 4, cudaMemcpyDeviceToHost, st));
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    s->n_past[slot] += n;
+    s->has_logits[slot] = 1;
+    return OCR_OK;
+}
+
+ocr_status ocr_step(ocr_session* s, const int32_t* tok, float* logits_out) {
+    if (!s || !tok) return fail(OCR_ERR_ARG, "null argument");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    std::vector<int32_t> act(s->B), pos(s->B);
+    for (int b = 0; b < s->B; b++) {
+        if (tok[b] >= c.n_vocab) return fail(OCR_ERR_ARG, "token " + std::to_string(tok[b]) + " is outside the vocabulary");
+        act[b] = tok[b] >= 0;
+        pos[b] = s->n_past[b];
+        if (act[b] && s->n_past[b] + 1 > s->n_ctx) return fail(OCR_ERR_STATE, "slot " + std::to_string(b) + ": the session is full");
+    }
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    OCR_CUDA(cudaMemcpyAsync(s->tok, tok, s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    record_step(s, false, 1.0f, 1, 0, 0.0f);
+    OCR_CUDA(cudaGetLastError());
+    if (logits_out)
+        OCR_CUDA(cudaMemcpyAsync(logits_out, s->logits, (size_t)s->B * c.n_vocab * 4, cudaMemcpyDeviceToHost, st));
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    for (int b = 0; b < s->B; b++)
+        if (act[b]) {
+            s->n_past[b] += 1;
+            s->has_logits[b] = 1;
+        }
+    return OCR_OK;
+}
+
+ocr_status ocr_decode(ocr_session* s, int slot, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
+                      ocr_token_cb on_token, void* user, int32_t* ids_out, int* n_out) {
+    if (!s || !ids_out) return fail(OCR_ERR_ARG, "null argument");
+    if (slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "slot out of range");
+    OCR_CUDA(cudaSetDevice(s->ctx->device));
+    int n = 0;
+    OCR_TRY(decode_slots(s, slot, 1, cfg, history, n_hist, on_token, user, ids_out, &n));
+    if (n_out) *n_out = n;
+    return OCR_OK;
+}
+
+ocr_status ocr_decode_batch(ocr_session* s, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
+                            int32_t* ids_out) {
+    if (!s || !ids_out) return fail(OCR_ERR_ARG, "null argument");
+    OCR_CUDA(cudaSetDevice(s->ctx->device));
+    return decode_slots(s, 0, s->B, cfg, history, n_hist, nullptr, nullptr, ids_out, nullptr);
+}
+
+ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, const ocr_sampler_cfg* cfg,
+                             const int32_t* history, int n_hist, const int32_t* count_tok, const uint32_t* count_n,
+                             int n_counts, int32_t* tok) {
+    if (!ctx || !d_logits || !cfg || !tok) return fail(OCR_ERR_ARG, "null argument");
+    if (cfg->rp != 1.0f && !(std::isnormal(cfg->rp) && cfg->rp > 0.0f))
+        return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
+    if (cfg->window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
+    if (n_vocab < 1 || n_hist < 0 || n_counts < 0) return fail(OCR_ERR_ARG, "bad sizes");
+    for (int i = 0; i < n_hist; i++)
+        if (history[i] < 0 || history[i] >= n_vocab) return fail(OCR_ERR_ARG, "history token " + std::to_string(history[i]) + " is outside the vocabulary");
+    const bool use_fp = cfg->fp > 0.0f && n_counts > 0;
+    for (int i = 0; use_fp && i < n_counts; i++)
+        if (count_tok[i] < 0 || count_tok[i] >= n_vocab) return fail(OCR_ERR_ARG, "count token outside the vocabulary");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    const int grid = sample_grid(ctx->num_sms);
+    const size_t o_part = 0, o_done = ((size_t)grid * 2 + 1) * 4 + 256, o_state = o_done + 256,
+                 o_hist = o_state + 256, o_counts = o_hist + ((size_t)n_hist + 1) * 4 + 256,
+                 o_fpen = o_counts + (use_fp ? (size_t)n_vocab * 4 + 256 : 0),
+                 total = o_fpen + (use_fp ? (size_t)n_vocab * 4 : 0) + 256;
+    OCR_TRY(ensure_op_scratch(ctx, total));
+    char* w = (char*)ctx->op_scratch;
+    cudaStream_t st = ctx->stream;
+    int32_t state[2] = {n_hist, 0};
+    OCR_CUDA(cudaMemcpyAsync(w + o_state, state, 8, cudaMemcpyHostToDevice, st));
+    if (n_hist) OCR_CUDA(cudaMemcpyAsync(w + o_hist, history, (size_t)n_hist * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemsetAsync(w + o_done, 0, 4, st));
+    std::vector<uint32_t> hc;
+    std::vector<float> hf;
+    if (use_fp) {
+        hc.assign(n_vocab, 0);
+        hf.assign(n_vocab, 0.0f);
+        for (int i = 0; i < n_counts; i++) {
+            hc[count_tok[i]] = count_n[i];
+            hf[count_tok[i]] = cfg->fp * (float)count_n[i];
+        }
+        OCR_CUDA(cudaMemcpyAsync(w + o_counts, hc.data(), (size_t)n_vocab * 4, cudaMemcpyHostToDevice, st));
+        OCR_CUDA(cudaMemcpyAsync(w + o_fpen, hf.data(), (size_t)n_vocab * 4, cudaMemcpyHostToDevice, st));
+    }
+    LmArgs a;
+    a.nb = 1;
+    a.sample = 1;
+    a.rp = cfg->rp;
+    a.window = cfg->window;
+    a.use_fp = use_fp ? 1 : 0;
+    a.fp = cfg->fp;
+    a.hist = (int32_t*)(w + o_hist);
+    a.hist_cap = n_hist + 1;
+    a.len = (int32_t*)(w + o_state);
+    a.tok = (int32_t*)(w + o_state) + 1;
+    a.counts = use_fp ? (uint32_t*)(w + o_counts) : nullptr;
+    a.fpen = use_fp ? (float*)(w + o_fpen) : nullptr;
+    a.part = (float*)(w + o_part);
+    a.done = (uint32_t*)(w + o_done);
+    a.err = ctx->d_err;
+    launch_sample(st, d_logits, n_vocab, n_vocab, a, ctx->num_sms, 0, 1);
+    OCR_CUDA(cudaGetLastError());
+    OCR_CUDA(cudaMemcpyAsync(state, w + o_state, 8, cudaMemcpyDeviceToHost, st));
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    *tok = state[1];
+    return OCR_OK;
+}
+
+ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, int8_t* d_quants,
+                              uint16_t* d_scales) {
+    if (!ctx || !d_blocks || !d_quants || !d_scales) return fail(OCR_ERR_ARG, "null argument");
+    if (rows < 1 || cols < 32 || cols % 32) return fail(OCR_ERR_ARG, "rows >= 1, cols a positive multiple of 32");
+    if (((uintptr_t)d_blocks & 1) || ((uintptr_t)d_quants & 15) || ((uintptr_t)d_scales & 1))
+        return fail(OCR_ERR_ARG, "alignment: blocks 2 B, quants 16 B, scales 2 B");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    launch_repack_q8_0(ctx->stream, (const uint8_t*)d_blocks, rows, cols, d_quants, (__half*)d_scales, 1, 0);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
+ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int rows, int cols,
+                              const float* d_x, const float* d_norm_w, float eps, int nb, float* d_y, int accumulate) {
+    if (!ctx || !d_quants || !d_scales || !d_x || !d_y) return fail(OCR_ERR_ARG, "null argument");
+    if (rows < 1 || cols < 32 || cols % 32 || nb < 1) return fail(OCR_ERR_ARG, "bad shape");
+    if ((uintptr_t)d_quants & 15) return fail(OCR_ERR_ARG, "quants must be 16-B aligned");
+    if ((size_t)nb * cols * 4 > 96 * 1024 * 8) return fail(OCR_ERR_ARG, "nb x cols too large for the staged activations");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    MvArgs a;
+    a.w.q = d_quants;
+    a.w.d = (const __half*)d_scales;
+    a.w.rows = rows;
+    a.w.cols = cols;
+    a.x = d_x;
+    a.x_stride = cols;
+    a.nw = d_norm_w;
+    a.eps = eps;
+    a.y = d_y;
+    a.y_stride = rows;
+    a.mode = accumulate ? MV_ADD : MV_STORE;
+    a.nb = nb;
+    launch_matvec(ctx->stream, a, ctx->num_sms, false);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
+ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int n_vocab, int dim,
+                                 const float* d_x, const float* d_norm_w, float eps, float rp, int window,
+                                 int32_t* d_hist, int32_t* d_len, int32_t* d_tok, float* d_logits) {
+    if (!ctx || !d_quants || !d_scales || !d_x || !d_hist || !d_len || !d_tok) return fail(OCR_ERR_ARG, "null argument");
+    if (n_vocab < 1 || dim < 32 || dim % 32) return fail(OCR_ERR_ARG, "bad shape");
+    if (rp != 1.0f && !(std::isnormal(rp) && rp > 0.0f)) return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
+    if (window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    const int grid = lm_head_grid(ctx->num_sms);
+    const size_t o_done = ((size_t)grid * 2 + 1) * 4 + 256;
+    OCR_TRY(ensure_op_scratch(ctx, o_done + 256));
+    char* w = (char*)ctx->op_scratch;
+    LmArgs a;
+    a.w.q = d_quants;
+    a.w.d = (const __half*)d_scales;
+    a.w.rows = n_vocab;
+    a.w.cols = dim;
+    a.x = d_x;
+    a.x_stride = dim;
+    a.nw = d_norm_w;
+    a.eps = eps;
+    a.nb = 1;
+    a.logits = d_logits;
+    a.sample = 1;
+    a.rp = rp;
+    a.window = window;
+    a.hist = d_hist;
+    a.hist_cap = 1 << 30;
+    a.len = d_len;
+    a.tok = d_tok;
+    a.part = (float*)w;
+    a.done = (uint32_t*)(w + o_done);
+    a.err = ctx->d_err;
+    OCR_CUDA(cudaMemsetAsync(a.done, 0, 4, ctx->stream));
+    launch_lm_head(ctx->stream, a, ctx->num_sms, false);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
+ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_norm, const float* d_k_norm,
+                                   const float* d_rope, uint16_t* d_k_cache, uint16_t* d_v_cache, int n_head, int n_kv,
+                                   int n_ctx, int pos, float eps, float* d_out) {
+    if (!ctx || !d_qkv || !d_q_norm || !d_k_norm || !d_rope || !d_k_cache || !d_v_cache || !d_out)
+        return fail(OCR_ERR_ARG, "null argument");
+    if (n_kv < 1 || n_head % n_kv) return fail(OCR_ERR_ARG, "n_head must be a multiple of n_kv");
+    const int g = n_head / n_kv;
+    if (g != 1 && g != 2 && g != 4 && g != 8) return fail(OCR_ERR_ARG, "GQA groups of 1, 2, 4 or 8 only");
+    if (pos < 0 || pos >= n_ctx) return fail(OCR_ERR_ARG, "pos outside the cache");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    AttnArgs a;
+    a.splits = attention_splits(ctx->num_sms, 1, n_kv, n_ctx);
+    const size_t o_part = 256, o_done = o_part + (size_t)n_head * a.splits * 130 * 4 + 256;
+    OCR_TRY(ensure_op_scratch(ctx, o_done + (size_t)n_kv * 4 + 256));
+    char* w = (char*)ctx->op_scratch;
+    cudaStream_t st = ctx->stream;
+    OCR_CUDA(cudaMemcpyAsync(w, &pos, 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemsetAsync(w + o_done, 0, (size_t)n_kv * 4, st));
+    a.qkv = d_qkv;
+    a.qkv_stride = (n_head + 2 * n_kv) * 128;
+    a.q_norm = d_q_norm;
+    a.k_norm = d_k_norm;
+    a.rope = d_rope;
+    a.kc = (__half*)d_k_cache;
+    a.vc = (__half*)d_v_cache;
+    a.pos = (const int32_t*)w;
+    a.n_head = n_head;
+    a.n_kv = n_kv;
+    a.n_ctx = n_ctx;
+    a.eps = eps;
+    a.scale = 1.0f / sqrtf(128.0f);
+    a.part = (float*)(w + o_part);
+    a.done = (uint32_t*)(w + o_done);
+    a.out = d_out;
+    a.out_stride = n_head * 128;
+    a.nb = 1;
+    a.err = ctx->d_err;
+    launch_attention_decode(st, a, false);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,411 @@
+"""ocr_b200 — Python host binding of libocrcuda.so (the C ABI in include/ocr_cuda.h).
+
+It mirrors the reference engine's text-decode API (b-straub/historic-htr-ocr, app/crates/ocr-wgpu/src/text.rs):
+    TextModel.load(ctx, path)            ≡ TextModel::load (text.rs:332-375)
+    model.session(n_ctx, batch)          ≡ TextModel::session / session_for (text.rs:378-434)
+    session.prefill(slot, ids, embd)     ≡ TextModel::prefill (text.rs:437-521), Input::Tokens / Input::Embeddings
+    session.step(tokens)                 ≡ TextModel::step (text.rs:524-537)
+    session.decode_gpu(slot, preset, history, on_token)  ≡ Choice::new + TextModel::decode_gpu (text.rs:185, 587-625)
+    choose_gpu(ctx, d_logits, …)         ≡ ocr_decode::sampling::choose, greedy (sampling.rs:38-62)
+Errors raise OcrError with the library's message (anyhow's text in the reference). The library must be built
+(historic-htr-ocr_b200/build.py); importing this module without it raises — there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libocrcuda.so"
+
+# ---------------------------------------------------------------------------------------------------------------------
+# the library
+# ---------------------------------------------------------------------------------------------------------------------
+
+
+class OcrError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class TextCfg(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("n_layer", "dim", "n_head", "n_kv", "d_head", "n_ff", "n_vocab",
+                                          "n_ctx_train")] + [("eps", C.c_float), ("rope_base", C.c_float)]
+
+
+class SamplerCfg(C.Structure):
+    _fields_ = [("rp", C.c_float), ("window", C.c_int32), ("fp", C.c_float), ("max_new", C.c_int32)]
+
+
+TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32)
+
+_P = C.c_void_p
+_SIGS = {
+    "ocr_last_error": (C.c_char_p, []),
+    "ocr_version": (C.c_char_p, []),
+    "ocr_ctx_create": (C.c_int, [C.c_int, C.POINTER(_P)]),
+    "ocr_ctx_destroy": (C.c_int, [_P]),
+    "ocr_ctx_sync": (C.c_int, [_P]),
+    "ocr_ctx_stream": (C.c_int, [_P, C.POINTER(_P)]),
+    "ocr_ctx_memory": (C.c_int, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "ocr_model_load_gguf": (C.c_int, [_P, C.c_char_p, C.POINTER(_P)]),
+    "ocr_model_load_gguf_memory": (C.c_int, [_P, _P, C.c_size_t, C.POINTER(_P)]),
+    "ocr_model_synthetic": (C.c_int, [_P, C.POINTER(TextCfg), C.c_uint64, C.c_float, C.c_float, C.POINTER(_P)]),
+    "ocr_model_config": (C.c_int, [_P, C.POINTER(TextCfg)]),
+    "ocr_model_tensor_gguf": (C.c_int, [_P, C.c_int, C.c_int, _P, C.POINTER(C.c_size_t)]),
+    "ocr_model_checksum": (C.c_int, [_P, C.POINTER(C.c_uint64)]),
+    "ocr_model_destroy": (C.c_int, [_P]),
+    "ocr_session_create": (C.c_int, [_P, C.c_int, C.c_int, C.POINTER(_P)]),
+    "ocr_session_destroy": (C.c_int, [_P]),
+    "ocr_session_n_past": (C.c_int, [_P, C.c_int, C.POINTER(C.c_int)]),
+    "ocr_session_rewind": (C.c_int, [_P, C.c_int, C.c_int]),
+    "ocr_prefill": (C.c_int, [_P, C.c_int, _P, _P, C.c_int, _P]),
+    "ocr_step": (C.c_int, [_P, _P, _P]),
+    "ocr_decode": (C.c_int, [_P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, TOKEN_CB, _P, _P,
+                             C.POINTER(C.c_int)]),
+    "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
+    "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
+    "ocr_op_repack_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
+    "ocr_op_matvec_q8_0": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_int, _P, C.c_int]),
+    "ocr_op_lm_head_sample": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P, _P,
+                                        _P, _P]),
+    "ocr_op_attention_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                          _P]),
+}
+
+# every symbol include/ocr_cuda.h declares (tests check the library exports each)
+EXPORTS = tuple(_SIGS)
+
+_lib: Optional[C.CDLL] = None
+
+
+def lib() -> C.CDLL:
+    """The loaded libocrcuda.so; raises if it is not built (no fallback of any kind)."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("OCR_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise OcrError(-1, f"{path} is not built: run historic-htr-ocr_b200/build.py")
+        L = C.CDLL(str(path))
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise OcrError(rc, lib().ocr_last_error().decode(errors="replace"))
+
+
+def _ptr(a) -> Optional[int]:
+    """host numpy array → address (None stays NULL); torch tensors → their data_ptr()"""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# presets (app/crates/ocr-decode/src/presets.rs:18-57) — greedy only on the device (text.rs:151-163)
+# ---------------------------------------------------------------------------------------------------------------------
+@dataclass
+class Preset:
+    name: str = "greedy_rp1.1"
+    temperature: float = 0.0
+    top_p: float = 1.0
+    repetition_penalty: float = 1.1
+    repetition_window: int = 20
+    frequency_penalty: float = 0.0
+    max_new_tokens: int = 7024
+
+    def greedy(self) -> bool:
+        return self.temperature == 0.0
+
+    def sampler(self, max_new: Optional[int] = None) -> SamplerCfg:
+        if not self.greedy():
+            raise OcrError(1, f"preset '{self.name}': sampled (temperature > 0): the token is drawn on the CPU")
+        return SamplerCfg(float(self.repetition_penalty), int(self.repetition_window), float(self.frequency_penalty),
+                          int(max_new if max_new is not None else self.max_new_tokens))
+
+
+# the shipped presets (app/presets.json)
+PRESETS = {
+    "greedy_rp1.1": Preset("greedy_rp1.1", 0.0, 1.0, 1.1, 20, 0.0, 7024),
+    "greedy_rp1.1_fp0.1": Preset("greedy_rp1.1_fp0.1", 0.0, 1.0, 1.1, 20, 0.1, 7024),
+}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# context / model / session
+# ---------------------------------------------------------------------------------------------------------------------
+class Context:
+    """One device, one stream (Gpu::create's role)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().ocr_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.h:
+            lib().ocr_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def sync(self) -> None:
+        _check(lib().ocr_ctx_sync(self.h))
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        _check(lib().ocr_ctx_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def memory(self) -> dict:
+        w, kv, wk = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(lib().ocr_ctx_memory(self.h, C.byref(w), C.byref(kv), C.byref(wk)))
+        return {"weights": w.value, "kv_cache": kv.value, "work": wk.value}
+
+
+@dataclass
+class TextConfig:
+    n_layer: int = 28
+    dim: int = 1024
+    n_head: int = 16
+    n_kv: int = 8
+    d_head: int = 128
+    n_ff: int = 3072
+    n_vocab: int = 151936
+    n_ctx_train: int = 40960
+    eps: float = 1e-6
+    rope_base: float = 1e6
+
+    def c(self) -> TextCfg:
+        return TextCfg(self.n_layer, self.dim, self.n_head, self.n_kv, self.d_head, self.n_ff, self.n_vocab,
+                       self.n_ctx_train, self.eps, self.rope_base)
+
+    @staticmethod
+    def from_c(c: TextCfg) -> "TextConfig":
+        return TextConfig(c.n_layer, c.dim, c.n_head, c.n_kv, c.d_head, c.n_ff, c.n_vocab, c.n_ctx_train, c.eps,
+                          c.rope_base)
+
+
+# tensor kinds of a layer (ocr_model_tensor_gguf numbering), with their GGUF names
+KINDS = ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm", "attn_k_norm", "ffn_norm",
+         "ffn_gate", "ffn_up", "ffn_down")
+
+
+class TextModel:
+    def __init__(self, ctx: Context, h: C.c_void_p):
+        self.ctx, self.h = ctx, h
+        c = TextCfg()
+        _check(lib().ocr_model_config(h, C.byref(c)))
+        self.cfg = TextConfig.from_c(c)
+
+    @classmethod
+    def load(cls, ctx: Context, path: str) -> "TextModel":
+        h = C.c_void_p()
+        _check(lib().ocr_model_load_gguf(ctx.h, str(path).encode(), C.byref(h)))
+        return cls(ctx, h)
+
+    @classmethod
+    def from_bytes(cls, ctx: Context, data: bytes) -> "TextModel":
+        buf = C.create_string_buffer(data, len(data))
+        h = C.c_void_p()
+        _check(lib().ocr_model_load_gguf_memory(ctx.h, buf, len(data), C.byref(h)))
+        return cls(ctx, h)
+
+    @classmethod
+    def synthetic(cls, ctx: Context, cfg: TextConfig, seed: int, sigma_w: float = 0.02,
+                  sigma_e: float = 0.02) -> "TextModel":
+        h = C.c_void_p()
+        c = cfg.c()
+        _check(lib().ocr_model_synthetic(ctx.h, C.byref(c), C.c_uint64(seed), sigma_w, sigma_e, C.byref(h)))
+        return cls(ctx, h)
+
+    def close(self) -> None:
+        if self.h:
+            lib().ocr_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tensor_gguf(self, layer: int, kind: int) -> bytes:
+        n = C.c_size_t(0)
+        _check(lib().ocr_model_tensor_gguf(self.h, layer, kind, None, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        _check(lib().ocr_model_tensor_gguf(self.h, layer, kind, buf, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def checksum(self) -> int:
+        x = C.c_uint64()
+        _check(lib().ocr_model_checksum(self.h, C.byref(x)))
+        return x.value
+
+    def session(self, n_ctx: int, batch: int = 1) -> "Session":
+        h = C.c_void_p()
+        _check(lib().ocr_session_create(self.h, n_ctx, batch, C.byref(h)))
+        return Session(self, h, n_ctx, batch)
+
+
+class Session:
+    def __init__(self, model: TextModel, h: C.c_void_p, n_ctx: int, batch: int):
+        self.model, self.h, self.n_ctx, self.batch = model, h, n_ctx, batch
+
+    def close(self) -> None:
+        if self.h:
+            lib().ocr_session_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def n_past(self, slot: int = 0) -> int:
+        n = C.c_int()
+        _check(lib().ocr_session_n_past(self.h, slot, C.byref(n)))
+        return n.value
+
+    def rewind(self, slot: int, n_past: int) -> None:
+        _check(lib().ocr_session_rewind(self.h, slot, n_past))
+
+    def prefill(self, slot: int = 0, ids: Optional[Sequence[int]] = None, embd: Optional[np.ndarray] = None,
+                logits: bool = True) -> Optional[np.ndarray]:
+        """rows: ids[i] >= 0 → token, else embedding row i of embd ([n][dim] f32)"""
+        dim, V = self.model.cfg.dim, self.model.cfg.n_vocab
+        ida = None if ids is None else np.ascontiguousarray(ids, dtype=np.int32)
+        ea = None if embd is None else np.ascontiguousarray(embd, dtype=np.float32).reshape(-1, dim)
+        n = len(ida) if ida is not None else (0 if ea is None else ea.shape[0])
+        out = np.empty(V, np.float32) if logits else None
+        _check(lib().ocr_prefill(self.h, slot, _ptr(ida), _ptr(ea), n, _ptr(out)))
+        return out
+
+    def step(self, tokens: Sequence[int], logits: bool = True) -> Optional[np.ndarray]:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        assert t.shape == (self.batch,)
+        out = np.empty((self.batch, self.model.cfg.n_vocab), np.float32) if logits else None
+        _check(lib().ocr_step(self.h, _ptr(t), _ptr(out)))
+        return out
+
+    def decode_gpu(self, slot: int, preset: Preset, history: Sequence[int], max_new: Optional[int] = None,
+                   on_token: Optional[Callable[[int], bool]] = None) -> list[int]:
+        sc = preset.sampler(max_new)
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        out = np.empty(sc.max_new, np.int32)
+        n = C.c_int(0)
+        cb = TOKEN_CB(0) if on_token is None else TOKEN_CB(lambda _u, t: 1 if on_token(int(t)) else 0)
+        _check(lib().ocr_decode(self.h, slot, C.byref(sc), _ptr(h) if len(h) else None, len(h), cb, None,
+                                _ptr(out), C.byref(n)))
+        return out[: n.value].tolist()
+
+    def decode_batch(self, preset: Preset, histories: np.ndarray, max_new: Optional[int] = None) -> np.ndarray:
+        sc = preset.sampler(max_new)
+        h = np.ascontiguousarray(histories, dtype=np.int32).reshape(self.batch, -1)
+        out = np.empty((self.batch, sc.max_new), np.int32)
+        _check(lib().ocr_decode_batch(self.h, C.byref(sc), _ptr(h) if h.size else None, h.shape[1], _ptr(out)))
+        return out
+
+
+def choose_gpu(ctx: Context, d_logits: int, n_vocab: int, preset: Preset, history: Sequence[int],
+               counts: Optional[dict] = None) -> int:
+    """ocr_decode::sampling::choose (greedy) on device logits (left unchanged)."""
+    sc = preset.sampler(1)
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    ct = np.ascontiguousarray(list((counts or {}).keys()), dtype=np.int32)
+    cn = np.ascontiguousarray(list((counts or {}).values()), dtype=np.uint32)
+    tok = np.zeros(1, np.int32)
+    _check(lib().ocr_sample_logits(ctx.h, d_logits, n_vocab, C.byref(sc), _ptr(h) if len(h) else None, len(h),
+                                   _ptr(ct) if len(ct) else None, _ptr(cn) if len(cn) else None, len(ct), _ptr(tok)))
+    return int(tok[0])
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# low-level ops on device pointers (ints)
+# ---------------------------------------------------------------------------------------------------------------------
+def op_repack_q8_0(ctx: Context, d_blocks: int, rows: int, cols: int, d_quants: int, d_scales: int) -> None:
+    _check(lib().ocr_op_repack_q8_0(ctx.h, d_blocks, rows, cols, d_quants, d_scales))
+
+
+def op_matvec_q8_0(ctx: Context, d_quants: int, d_scales: int, rows: int, cols: int, d_x: int, d_norm_w: Optional[int],
+                   eps: float, nb: int, d_y: int, accumulate: bool) -> None:
+    _check(lib().ocr_op_matvec_q8_0(ctx.h, d_quants, d_scales, rows, cols, d_x, d_norm_w, eps, nb, d_y,
+                                    1 if accumulate else 0))
+
+
+def op_lm_head_sample(ctx: Context, d_quants: int, d_scales: int, n_vocab: int, dim: int, d_x: int, d_norm_w: int,
+                      eps: float, rp: float, window: int, d_hist: int, d_len: int, d_tok: int,
+                      d_logits: Optional[int]) -> None:
+    _check(lib().ocr_op_lm_head_sample(ctx.h, d_quants, d_scales, n_vocab, dim, d_x, d_norm_w, eps, rp, window,
+                                       d_hist, d_len, d_tok, d_logits))
+
+
+def op_attention_decode(ctx: Context, d_qkv: int, d_q_norm: int, d_k_norm: int, d_rope: int, d_k: int, d_v: int,
+                        n_head: int, n_kv: int, n_ctx: int, pos: int, eps: float, d_out: int) -> None:
+    _check(lib().ocr_op_attention_decode(ctx.h, d_qkv, d_q_norm, d_k_norm, d_rope, d_k, d_v, n_head, n_kv, n_ctx,
+                                         pos, eps, d_out))
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# the seeded synthetic data spec (shared with the CPU test generator; numpy, vectorised)
+# ---------------------------------------------------------------------------------------------------------------------
+_G = np.uint64(0x9E3779B97F4A7C15)
+_M1 = np.uint64(0xBF58476D1CE4E5B9)
+_M2 = np.uint64(0x94D049BB133111EB)
+SEED_BASE = 0x4F43522D42323030  # "OCR-B200"
+
+
+def splitmix64_at(seed: int, idx: np.ndarray) -> np.ndarray:
+    """output idx (0-based) of SplitMix64 seeded with `seed` (ocr-decode sampling.rs:24-35)"""
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + (idx.astype(np.uint64) + np.uint64(1)) * _G
+        z = (z ^ (z >> np.uint64(30))) * _M1
+        z = (z ^ (z >> np.uint64(27))) * _M2
+        return z ^ (z >> np.uint64(31))
+
+
+def substream(seed: int, k: int) -> int:
+    return int(splitmix64_at(seed ^ 0x6F63722D62323030, np.array([k]))[0])
+
+
+def gauss(seed: int, n: int, sigma: float = 1.0, start: int = 0) -> np.ndarray:
+    """sigma * N(0,1) stand-in: Irwin–Hall sum of 12 uniform u16 (3 outputs per value), centred, / 2^16"""
+    i = np.arange(start, start + n, dtype=np.uint64)
+    s = np.zeros(n, np.int64)
+    for k in range(3):
+        z = splitmix64_at(seed, np.uint64(3) * i + np.uint64(k))
+        for sh in (0, 16, 32, 48):
+            s += ((z >> np.uint64(sh)) & np.uint64(0xFFFF)).astype(np.int64)
+    g = (s - 6 * 65535).astype(np.float32) * np.float32(1.0 / 65536.0)
+    return (np.float32(sigma) * g).astype(np.float32)
+
+
+def fill_ids(seed: int, n: int, n_vocab: int) -> np.ndarray:
+    z = splitmix64_at(seed, np.arange(n, dtype=np.uint64))
+    return (((z >> np.uint64(32)) * np.uint64(n_vocab)) >> np.uint64(32)).astype(np.int32)
+
+
+def version() -> str:
+    return lib().ocr_version().decode()

@@ -1,0 +1,154 @@
+/*
+ * ocr_cuda.h — the C ABI of libocrcuda.so, a B200 (sm_100a) q8_0 text-decode engine for the LightOnOCR-style VLM.
+ *
+ * It replaces, behind the same shapes of call, the wgpu text decoder of b-straub/historic-htr-ocr (paths relative to
+ * that project). Each entry point names the reference interface it stands in for. All calls return an ocr_status
+ * (0 = OCR_OK); on failure ocr_last_error() holds a message (per host thread). Handles are single-thread-affine, like
+ * the reference's Gpu (RefCell inside, not Sync): one host thread drives one ocr_ctx. The caller owns every host
+ * buffer; the library owns all device memory it allocates. Device pointers in the low-level ops (ocr_op_*) are plain
+ * CUDA device addresses on the context's device; those ops run on the context's stream and return when queued unless
+ * stated otherwise (ocr_ctx_sync waits).
+ */
+#ifndef OCR_CUDA_H
+#define OCR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int ocr_status;
+enum {
+    OCR_OK = 0,
+    OCR_ERR_ARG = 1,      /* an argument is out of range (a token outside the vocabulary, a size, a null pointer) */
+    OCR_ERR_CUDA = 2,     /* a CUDA call failed; the message has cudaGetErrorString */
+    OCR_ERR_FORMAT = 3,   /* the GGUF file is malformed or holds what this engine does not run */
+    OCR_ERR_IO = 4,       /* the file could not be read */
+    OCR_ERR_STATE = 5,    /* the call does not fit the session's state (positions overflow, no logits yet) */
+    OCR_ERR_DEVICE = 6,   /* a kernel reported a device-side error (a bounded wait gave up, a bad index) */
+};
+
+typedef struct ocr_ctx ocr_ctx;
+typedef struct ocr_model ocr_model;
+typedef struct ocr_session ocr_session;
+
+/* TextConfig (app/crates/ocr-wgpu/src/text.rs:37-82) */
+typedef struct {
+    int32_t n_layer, dim, n_head, n_kv, d_head, n_ff, n_vocab, n_ctx_train;
+    float eps, rope_base;
+} ocr_text_cfg;
+
+/* the greedy preset's knobs (app/crates/ocr-decode/src/presets.rs:18-35; Preset::greedy, temperature 0):
+ * rp = repetitionPenalty (1 = off; a positive normal f32 otherwise, text.rs:154-163), window = repetitionWindow (>= 1),
+ * fp = frequencyPenalty (0 = off), max_new = maxNewTokens */
+typedef struct {
+    float rp;
+    int32_t window;
+    float fp;
+    int32_t max_new;
+} ocr_sampler_cfg;
+
+/* ---- errors ---------------------------------------------------------------------------------------------------- */
+/* the message of the last failed call on this host thread ("" if none) — anyhow's error text in the reference */
+const char* ocr_last_error(void);
+/* the library's version string and the device code it carries ("sm_100a") */
+const char* ocr_version(void);
+
+/* ---- context: one device, one stream, the device arena (replaces Gpu::create, gpu.rs:1172-1324) ---------------- */
+ocr_status ocr_ctx_create(int device, ocr_ctx** out);
+ocr_status ocr_ctx_destroy(ocr_ctx* ctx);
+/* wait for everything queued on the context's stream; returns OCR_ERR_DEVICE if a kernel flagged an error */
+ocr_status ocr_ctx_sync(ocr_ctx* ctx);
+/* the context's cudaStream_t (as void*), for callers that order their own work against it */
+ocr_status ocr_ctx_stream(ocr_ctx* ctx, void** stream);
+/* bytes of device memory the library holds, by kind (GpuBytes, sampling.rs:137-146): weights, kv_cache, work */
+ocr_status ocr_ctx_memory(ocr_ctx* ctx, uint64_t* weights, uint64_t* kv_cache, uint64_t* work);
+
+/* ---- model (TextModel::load, text.rs:332-375; Gguf::from_source, ocr-gguf/src/lib.rs:300-338) -------------------- */
+/* a qwen3 text GGUF: q8_0 matrices, f32 norms, tied token_embd — streamed to the device and repacked there */
+ocr_status ocr_model_load_gguf(ocr_ctx* ctx, const char* path, ocr_model** out);
+/* the same from bytes in memory (TensorSource for Vec<u8>, ocr-gguf/src/lib.rs:71-84) */
+ocr_status ocr_model_load_gguf_memory(ocr_ctx* ctx, const void* bytes, size_t n_bytes, ocr_model** out);
+/* a seeded synthetic model of the given shape, generated and quantized on the device (no file): matrices
+ * sigma_w * g, token_embd sigma_e * g (g the generator's N(0,1) stand-in), norms 1 + 0.01 u — the same values, bit for
+ * bit, as the CPU test generator of the same seed */
+ocr_status ocr_model_synthetic(ocr_ctx* ctx, const ocr_text_cfg* cfg, uint64_t seed, float sigma_w, float sigma_e,
+                               ocr_model** out);
+ocr_status ocr_model_config(const ocr_model* m, ocr_text_cfg* out);
+/* copy one tensor back in GGUF form (q8_0 34-byte blocks, or f32 for norms): layer -1 with kind 0 = token_embd, kind
+ * 1 = output_norm; kinds of a layer: 0 attn_norm 1 q 2 k 3 v 4 o 5 q_norm 6 k_norm 7 ffn_norm 8 gate 9 up 10 down.
+ * `out` NULL → *n_bytes = the size needed */
+ocr_status ocr_model_tensor_gguf(const ocr_model* m, int layer, int kind, void* out, size_t* n_bytes);
+/* a 64-bit FNV-1a checksum of all repacked weight bytes (identity checks across loads / generators) */
+ocr_status ocr_model_checksum(const ocr_model* m, uint64_t* out);
+ocr_status ocr_model_destroy(ocr_model* m);
+
+/* ---- session: KV cache + decode scratch for `batch` independent sequences (Session, text.rs:242-434) ----------- */
+/* n_ctx = positions per sequence (prompt + new tokens), <= n_ctx_train; the KV cache is allocated once, whole */
+ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** out);
+ocr_status ocr_session_destroy(ocr_session* s);
+ocr_status ocr_session_n_past(const ocr_session* s, int slot, int* out);
+/* rewind a slot to n_past positions (<= its current n_past): later steps overwrite the rows beyond */
+ocr_status ocr_session_rewind(ocr_session* s, int slot, int n_past);
+
+/* TextModel::prefill (text.rs:437-521) for one slot: n_rows rows at positions n_past…; row i is token ids[i] when
+ * ids != NULL and ids[i] >= 0, else embedding row i of embd ([n_rows][dim] f32, Input::Embeddings). Host buffers.
+ * logits_out (nullable, [n_vocab]) = the last row's logits; they also stay on the device for the first choice. */
+ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float* embd, int n_rows, float* logits_out);
+
+/* TextModel::step (text.rs:524-537): one token per slot (tok[slot] < 0 = slot idle) at each slot's n_past → logits
+ * ([batch][n_vocab], nullable). The CPU token choice path: logits come back every step. */
+ocr_status ocr_step(ocr_session* s, const int32_t* tok, float* logits_out);
+
+/* TextModel::decode_gpu + Choice (text.rs:185-231, 587-625) for one slot: greedy choices with the windowed
+ * repetition penalty (and frequency penalty), the token chosen on the device and fed back without a host round trip.
+ * history = the window's start (prompt tail) as ocr-decode's generate gets it; choice 0 comes from the slot's current
+ * logits (the prefill's or the last step's). on_token (nullable) sees each id in order; returning 0 ends the read
+ * (steps already queued past it finish unseen). ids_out [max_new] gets the ids, *n_out their count. */
+typedef int (*ocr_token_cb)(void* user, int32_t token);
+ocr_status ocr_decode(ocr_session* s, int slot, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
+                      ocr_token_cb on_token, void* user, int32_t* ids_out, int* n_out);
+
+/* the same for every slot at once (batched decode; each slot its own history): history [batch][n_hist] (a shared
+ * length), ids_out [batch][max_new]. All slots run max_new choices. */
+ocr_status ocr_decode_batch(ocr_session* s, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
+                            int32_t* ids_out);
+
+/* ocr_decode::sampling::choose, greedy branch (sampling.rs:38-62) ≡ choose_pen → choose_max → choose_pick
+ * (shaders/choose_*.wgsl) on logits already on the device (d_logits [n_vocab] f32, left unchanged): the windowed
+ * penalty over the DISTINCT tokens of history[n_hist - window, n_hist), the frequency penalty over (count_tok,
+ * count_n) pairs (host arrays, n_counts entries), the first maximum. Returns the token in *tok (host). Synchronous. */
+ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, const ocr_sampler_cfg* cfg,
+                             const int32_t* history, int n_hist, const int32_t* count_tok, const uint32_t* count_n,
+                             int n_counts, int32_t* tok);
+
+/* ---- low-level ops on device buffers (the kernels behind the calls above; tests and the LM-head benchmark) ------ */
+/* GGUF q8_0 blocks (34 B each, rows x cols/32 blocks, any alignment) → the device layout: quants [rows][cols] int8
+ * (16-B aligned rows) + scales [rows][cols/32] f16. Same values. (Gpu::upload_tensor's q8_0 case, gpu.rs:1595-1647) */
+ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, int8_t* d_quants,
+                              uint16_t* d_scales);
+/* y[b][r] (+)= sum_c W[r][c] * xn[b][c] for b < nb: xn = x, or RMSNorm(x) * norm_w when norm_w != NULL
+ * (dmv.wgsl / dmv_norm / matvec_q8_0.wgsl). accumulate = 1 adds onto y. x [nb][cols], y [nb][rows]. */
+ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int rows, int cols,
+                              const float* d_x, const float* d_norm_w, float eps, int nb, float* d_y, int accumulate);
+/* the LM head fused with the sampler (dmv_norm → choose_pen → choose_max → choose_pick): logits = W . RMSNorm(x) *
+ * norm_w over n_vocab rows, the windowed penalty on the distinct tokens of d_hist[len - window, len) (device, len =
+ * *d_len), argmax (first maximum) → *d_tok, d_hist[len] = token, *d_len += 1. d_logits (nullable) receives the raw
+ * logits. One slot. */
+ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int n_vocab,
+                                 int dim, const float* d_x, const float* d_norm_w, float eps, float rp, int window,
+                                 int32_t* d_hist, int32_t* d_len, int32_t* d_tok, float* d_logits);
+/* decode attention of one token (qkv_post.wgsl + attn_decode.wgsl + attn_merge.wgsl): raw qkv [n_head + 2 n_kv][128]
+ * f32 → per-head RMSNorm (q_norm / k_norm), RoPE NEOX at `pos` from the table rope [n_ctx][64][2], K/V rows `pos`
+ * stored f16 into k_cache / v_cache ([n_kv][n_ctx][128] f16), then softmax(q k / sqrt(128)) v over keys 0…pos → out
+ * [n_head][128] f32. */
+ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_norm, const float* d_k_norm,
+                                   const float* d_rope, uint16_t* d_k_cache, uint16_t* d_v_cache, int n_head, int n_kv,
+                                   int n_ctx, int pos, float eps, float* d_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
