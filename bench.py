@@ -1,0 +1,358 @@
+"""bench.py — decode throughput of the B200 q8_0 text-decode engine (libocrcuda.so) on BASELINE config 2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|1|3]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+
+Workload (config 2): a Qwen3-0.6B-shaped decoder (28 layers, dim 1024, 16/8 heads of 128,
+ffn 3072, vocab 151936, tied head) with seeded synthetic q8_0 weights (sigma 0.02) generated on the device; the f16
+KV cache prefilled (untimed) from 2048 seeded N(0,1) embedding rows; one step = a full greedy decode of 512 tokens
+with the windowed repetition penalty (rp 1.15, window 64, seeded with 64 x <|image_pad|>) through the C ABI
+(ocr_decode), preceded by re-feeding the prefix's last row (one prefill row, so every step starts from the same
+logits). Pages are independent: at N GPUs every rank decodes its own replica (weak scaling, no data-path
+collective); ranks only meet for the timing barrier and the max-over-ranks (gloo, host memory).
+The weights streamed per token (633 MB) exceed the 126 MB L2, so no flush is needed between steps.
+
+--config 1: the LM head + windowed penalty + greedy argmax alone (ocr_op_lm_head_sample),
+x N(0,1) [1024], W [151936 x 1024] N(0, 0.02) q8_0, history 512 uniform ids, penalty 1.15 over the last 64.
+--config 3: batched decode, 32 sequences per GPU (3072-row prefixes), 1024 tokens each.
+
+--impl reference: the reference's own path cannot run here (Rust + WGSL on wgpu: no Rust toolchain, no graphics
+adapter), so the reference arm times the CPU restatement of it (oracle/, OpenMP on all host cores) on a bounded
+sample of the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "historic-htr-ocr_b200"))
+
+CONFIG2 = dict(n_layer=28, dim=1024, n_head=16, n_kv=8, d_head=128, n_ff=3072, n_vocab=151936, eps=1e-6,
+               rope_base=1e6)
+IMAGE_PAD = 151655
+PREFIX, NEW = 2048, 512
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, max, throttle reasons)"""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# the LM head + sampler kernel timed alone (config 1, and the roofline of the dominant kernel)
+# ---------------------------------------------------------------------------------------------------------------------
+def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
+    """(mean µs per launch, algorithmic bytes per launch): W 151936 x 1024 q8_0 (165,306,368 B) + x (4 KB) + norm
+    (4 KB) + logits written (607,744 B) + the 64-token window; L2 flushed between launches (256 MB write)"""
+    V, D = 151936, 1024
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randint(-127, 128, (V, D), dtype=torch.int8, device="cuda", generator=g)
+    d = (torch.rand(V, D // 32, device="cuda", generator=g) * 0.0003 + 0.0001).half()
+    x = torch.randn(D, device="cuda", generator=g)
+    nw = torch.ones(D, device="cuda")
+    hist = torch.randint(0, V, (512 + reps + 8,), dtype=torch.int32, device="cuda", generator=g)
+    ln = torch.tensor([512], dtype=torch.int32, device="cuda")
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    logits = torch.empty(V, device="cuda")
+    flush = torch.empty(flush_bytes // 4, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    torch.cuda.synchronize()
+    times = []
+    for i in range(reps + 3):
+        flush.fill_(float(i))
+        torch.cuda.synchronize()
+        ln.fill_(512)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ocr.op_lm_head_sample(ctx, q.data_ptr(), d.data_ptr(), V, D, x.data_ptr(), nw.data_ptr(), 1e-6, 1.15, 64,
+                              hist.data_ptr(), ln.data_ptr(), tok.data_ptr(), logits.data_ptr())
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            times.append(a.elapsed_time(b) * 1e3)
+    ctx.sync()
+    algo = V * D + V * (D // 32) * 2 + 2 * D * 4 + V * 4 + 64 * 4
+    return sum(times) / len(times), algo
+
+
+def kernel_roofline(ocr, ctx, torch):
+    us, algo = lm_head_kernel(ocr, ctx, torch, 10)
+    peak, which = peaks()
+    gbs = algo / (us * 1e-6) / 1e9
+    return {"kernel": "k_lm_head<1> (LM head + windowed penalty + argmax, 151936 x 1024 q8_0)", "bound": "hbm",
+            "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+            "peak_source": f"{which} hbm_gbs", "traffic": None, "us_per_launch": round(us, 2),
+            "algorithmic_bytes": algo}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    import ocr_b200 as ocr
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        pg = dist
+    ctx = ocr.Context(local)
+    cfg = ocr.TextConfig(**{k: v for k, v in CONFIG2.items()})
+    seed = ocr.SEED_BASE + 2
+    if args.config == 1:
+        return run_config1(args, ocr, ctx, torch, pg, rank, world)
+    model = ocr.TextModel.synthetic(ctx, cfg, seed, 0.02, 0.02)
+    B = 32 if args.config == 3 else 1
+    prefix_len, new = (3072, 1024) if args.config == 3 else (PREFIX, NEW)
+    sess = model.session(prefix_len + new, batch=B)
+    for b in range(B):
+        embd = ocr.gauss(ocr.substream(seed + b, 200000), prefix_len * 1024, 1.0).reshape(prefix_len, 1024)
+        sess.prefill(b, embd=embd, logits=False)
+    last_rows = [ocr.gauss(ocr.substream(seed + b, 200000), 1024, 1.0, start=(prefix_len - 1) * 1024)
+                 for b in range(B)]
+    preset = ocr.Preset("bench", 0.0, 1.0, 1.15, 64, 0.0, new)
+    hist = np.full((B, 64), IMAGE_PAD, np.int32)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    def step():
+        for b in range(B):
+            sess.rewind(b, prefix_len - 1)
+            sess.prefill(b, embd=last_rows[b], logits=False)
+        if B == 1:
+            return sess.decode_gpu(0, preset, hist[0])
+        return sess.decode_batch(preset, hist)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+        wall = time.perf_counter() - t0
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    times = np.array([dev_s, wall], np.float64)
+    if pg:
+        import torch.distributed as dist
+
+        t = torch.from_numpy(times)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times = t.numpy()
+    dev_s, wall = float(times[0]), float(times[1])
+    tokens = world * B * new * args.steps
+    # per step: the one-row prefill per slot (embed + 8 per layer + LM head), choice 0, then new - 1 decode steps
+    # of 5 kernels per layer + the fused LM head / choice
+    launches_per_token = CONFIG2["n_layer"] * 5 + 1
+    launches = args.steps * ((CONFIG2["n_layer"] * 8 + 2) * B + 1 + (new - 1) * launches_per_token)
+    out = None
+    if rank == 0:
+        roof = kernel_roofline(ocr, ctx, torch)
+        out = {
+            "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
+            "value": round(tokens / dev_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_s / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV",
+            "data": "synthetic (seeded q8_0 weights sigma 0.02, N(0,1) prefix embeddings; no checkpoint)",
+            "config": {"workload": f"BASELINE config {args.config}: greedy decode of {new} tokens per sequence, "
+                                   f"{B} sequence(s) per GPU, {prefix_len}-row prefilled f16 KV cache, rp 1.15 "
+                                   "window 64", "model": "Qwen3-0.6B-shaped text decoder (28 x 1024, 16/8 heads, "
+                                   "ffn 3072, vocab 151936, tied head)", "global_batch": B * world,
+                       "seq_len": prefix_len + new, "parallelism": f"replicas x{world} (pages partitioned, no "
+                                                                   "collectives)",
+                       "l2": "inputs larger than L2 (633 MB of weights streamed per token)"},
+            "e2e": {"value": round(tokens / wall, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": B * (64 * 4 + 1024 * 4), "d2h_bytes_per_step": B * new * 4},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline_sample(tokens_sample=16)
+        print(json.dumps(out), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    sess.close()
+    model.close()
+    ctx.close()
+    return out
+
+
+def run_config1(args, ocr, ctx, torch, pg, rank, world):
+    us_list = []
+    with Clocks(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        us, algo = lm_head_kernel(ocr, ctx, torch, args.steps)
+    peak, which = peaks()
+    if rank == 0:
+        gbs = algo / (us * 1e-6) / 1e9
+        print(json.dumps({
+            "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
+            "value": round(world * 1e6 / us, 1), "unit": "choices/s", "n_gpus": world, "steps": args.steps,
+            "warmup": 3, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 x f32", "data": "synthetic",
+            "config": {"workload": "BASELINE config 1: LM head 151936 x 1024 q8_0 + windowed penalty + argmax",
+                       "l2": "flushed between launches (256 MB write)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": which, "traffic": None},
+            "clocks": clk.summary()}), flush=True)
+    del us_list
+    return None
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# the CPU baseline (the oracle: the reference's path restated, OpenMP on all host cores)
+# ---------------------------------------------------------------------------------------------------------------------
+def cpu_baseline_sample(tokens_sample: int = 16):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    import ocr_b200 as ocr
+
+    m = O.Model(CONFIG2, seed=ocr.SEED_BASE + 2, sigma_w=0.02, sigma_e=0.02)
+    s = m.session(PREFIX + NEW)
+    s.n_past = PREFIX  # a 2048-row cache: the per-token work is the same whatever the rows hold
+    s.step(IMAGE_PAD)  # warm-up
+    s.n_past = PREFIX
+    t0 = time.perf_counter()
+    for i in range(tokens_sample):
+        s.step((IMAGE_PAD + 7 * i) % CONFIG2["n_vocab"])
+    dt = time.perf_counter() - t0
+    return {"value": round(tokens_sample / dt, 2), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{tokens_sample} config-2 decode steps at positions {PREFIX}..{PREFIX + tokens_sample - 1} "
+                      f"over a {PREFIX}-row f16 KV cache, oracle/oracle.c (OpenMP)"}
+
+
+def run_reference(args):
+    rank, local, world = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    import ocr_b200 as ocr
+
+    m = O.Model(CONFIG2, seed=ocr.SEED_BASE + 2, sigma_w=0.02, sigma_e=0.02)
+    s = m.session(PREFIX + NEW)
+    per_step = 4  # tokens per step: a bounded sample of the 512-token decode
+
+    def step():
+        s.n_past = PREFIX
+        for i in range(per_step):
+            s.step((IMAGE_PAD + 7 * i) % CONFIG2["n_vocab"])
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    v = round(per_step * args.steps / dt, 3)
+    sample = (f"{per_step} config-2 decode steps per step at positions {PREFIX}..{PREFIX + per_step - 1} over a "
+              f"{PREFIX}-row f16 KV cache (the reference's Rust/WGSL path cannot run here: no Rust toolchain, no "
+              "graphics adapter; timed is its CPU restatement oracle/oracle.c, OpenMP)")
+    print(json.dumps({
+        "impl": "reference", "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
+        "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2 (bounded CPU sample)", "global_batch": 1,
+                   "seq_len": PREFIX + NEW, "parallelism": "host cores"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": O.num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3], default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -537,6 +537,20 @@ __global__ void __launch_bounds__(MV_THREADS) k_sample(const float* __restrict__
 
 int sample_grid(int num_sms) { return num_sms; }
 
+// the penalty alone, in place (choose_pen.wgsl's job): the same prefilter + pen_apply the fused choice uses
+__global__ void __launch_bounds__(MV_THREADS) k_penalize(float* __restrict__ logits, int n_vocab, LmArgs a, int per_cta) {
+    __shared__ PenList pl;
+    const int lo = blockIdx.x * per_cta, hi = min(n_vocab, lo + per_cta);
+    pen_prefilter(pl, 1, 0, a, lo, hi);
+    for (int t = lo + threadIdx.x; t < hi; t += blockDim.x) logits[t] = pen_apply(pl, 0, 0, t, logits[t], a, n_vocab);
+}
+
+void launch_penalize(cudaStream_t st, float* logits, int n_vocab, const LmArgs& a, int num_sms) {
+    const int grid = sample_grid(num_sms);
+    const int per = (n_vocab + grid - 1) / grid;
+    k_penalize<<<grid, MV_THREADS, 0, st>>>(logits, n_vocab, a, per);
+}
+
 void launch_sample(cudaStream_t st, const float* logits, int logits_stride, int n_vocab, const LmArgs& a,
                    int num_sms, int slot_base, int n_slots) {
     const int grid = sample_grid(num_sms);

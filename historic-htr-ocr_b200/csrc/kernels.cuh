@@ -86,6 +86,8 @@ int lm_head_grid(int num_sms);
 void launch_sample(cudaStream_t st, const float* logits, int logits_stride, int n_vocab, const LmArgs& a,
                    int num_sms, int slot_base, int n_slots);
 int sample_grid(int num_sms);
+// the windowed penalty alone, in place (a.sample = 1, a.len → n_hist, a.hist, a.rp, a.window)
+void launch_penalize(cudaStream_t st, float* logits, int n_vocab, const LmArgs& a, int num_sms);
 
 // ---- attention (k_attn.cu) -------------------------------------------------------------------------------------------
 struct AttnArgs {

@@ -334,15 +334,46 @@ ocr_status cfg_from_gguf(const Gguf& g, ocr_text_cfg& c) {
     return OCR_OK;
 }
 
-// TextModel::load (text.rs:332-375) from a parsed GGUF
-ocr_status load_gguf(ocr_ctx* ctx, Gguf& g, ocr_model** out) {
-    ocr_text_cfg c{};
+// the GGUF tensor names of a layer's kinds (ocr_model_tensor_gguf numbering)
+const char* const KIND_NAMES[11] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm",
+                                    "attn_k_norm", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+
+// a kind's expected GGUF form: a matrix [cols, rows] q8_0 or an f32 vector [n]
+void kind_shape(const ocr_text_cfg& c, int kind, bool& is_norm, int& rows, int& cols) {
+    const int qd = c.n_head * c.d_head, kvd = c.n_kv * c.d_head;
+    is_norm = false;
+    switch (kind) {
+    case 0: case 7: is_norm = true; rows = 1; cols = c.dim; break;
+    case 5: case 6: is_norm = true; rows = 1; cols = c.d_head; break;
+    case 1: rows = qd; cols = c.dim; break;
+    case 2: case 3: rows = kvd; cols = c.dim; break;
+    case 4: rows = c.dim; cols = qd; break;
+    case 8: case 9: rows = c.n_ff; cols = c.dim; break;
+    default: rows = c.dim; cols = c.n_ff; break;
+    }
+}
+
+ocr_status check_tensor(const Gguf& g, const std::string& name, bool is_norm, int rows, int cols) {
+    const GTensor* t = g.info(name);
+    if (!t) return fail(OCR_ERR_FORMAT, "GGUF has no tensor " + name);
+    if (is_norm) {
+        if (t->type != GType::F32 || t->shape.size() != 1 || t->shape[0] != (uint64_t)cols)
+            return fail(OCR_ERR_FORMAT, name + ": expected F32 [" + std::to_string(cols) + "]");
+        return OCR_OK;
+    }
+    if (t->shape.size() != 2 || t->shape[0] != (uint64_t)cols || t->shape[1] != (uint64_t)rows)
+        return fail(OCR_ERR_FORMAT, name + ": shape, expected [" + std::to_string(cols) + ", " + std::to_string(rows) + "]");
+    if (t->type != GType::Q8_0) return fail(OCR_ERR_FORMAT, name + ": the text decoder's kernels read q8_0 weights");
+    return OCR_OK;
+}
+
+// TextConfig::from_gguf + every check TextModel::load makes before it uploads (text.rs:51-82, 111-128, 332-375)
+ocr_status validate_gguf(const Gguf& g, ocr_text_cfg& c) {
     OCR_TRY(cfg_from_gguf(g, c));
     const int qd = c.n_head * c.d_head;
     if (c.dim % 32 != 0 || c.n_ff % 32 != 0 || qd % 32 != 0)
         return fail(OCR_ERR_FORMAT, "dims " + std::to_string(c.dim) + " / " + std::to_string(c.n_ff) + " / " +
                                         std::to_string(qd) + ": q8_0 rows must be whole blocks");
-    // the graph's tensors: refuse what the engine does not run (text.rs:341-366)
     for (int i = 0; i < c.n_layer; i++) {
         for (const char* absent : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"}) {
             const std::string b = "blk." + std::to_string(i) + "." + absent + ".bias";
@@ -350,31 +381,34 @@ ocr_status load_gguf(ocr_ctx* ctx, Gguf& g, ocr_model** out) {
         }
         if (g.has("blk." + std::to_string(i) + ".attn_qkv.weight"))
             return fail(OCR_ERR_FORMAT, "blk." + std::to_string(i) + ": a fused attn_qkv — this engine reads separate q / k / v");
+        for (int k = 0; k < 11; k++) {
+            bool is_norm;
+            int rows, cols;
+            kind_shape(c, k, is_norm, rows, cols);
+            OCR_TRY(check_tensor(g, "blk." + std::to_string(i) + "." + KIND_NAMES[k] + ".weight", is_norm, rows, cols));
+        }
     }
     if (g.has("output.weight")) return fail(OCR_ERR_FORMAT, "output.weight is in the GGUF: this engine ties the output to token_embd");
+    OCR_TRY(check_tensor(g, "token_embd.weight", false, c.n_vocab, c.dim));
+    OCR_TRY(check_tensor(g, "output_norm.weight", true, 1, c.dim));
+    return check_cfg(c);
+}
+
+// TextModel::load (text.rs:332-375) from a parsed GGUF
+ocr_status load_gguf(ocr_ctx* ctx, Gguf& g, ocr_model** out) {
+    ocr_text_cfg c{};
+    OCR_TRY(validate_gguf(g, c));
     ocr_model* m = nullptr;
     OCR_TRY(model_alloc(ctx, c, &m));
-    static const char* names[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm",
-                                  "attn_k_norm", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
     auto load_one = [&](int layer, int kind, const std::string& name) -> ocr_status {
         Where w;
         where(m, layer, kind, w);
-        const GTensor* t = g.info(name);
-        if (!t) return fail(OCR_ERR_FORMAT, "GGUF has no tensor " + name);
-        if (w.is_norm) {
-            if (t->type != GType::F32 || t->shape.size() != 1 || t->shape[0] != (uint64_t)w.n)
-                return fail(OCR_ERR_FORMAT, name + ": expected F32 [" + std::to_string(w.n) + "]");
-        } else {
-            if (t->shape.size() != 2 || t->shape[0] != (uint64_t)w.mat.cols || t->shape[1] != (uint64_t)w.rows)
-                return fail(OCR_ERR_FORMAT, name + ": shape, expected [" + std::to_string(w.mat.cols) + ", " + std::to_string(w.rows) + "]");
-            if (t->type != GType::Q8_0) return fail(OCR_ERR_FORMAT, name + ": the text decoder's kernels read q8_0 weights");
-        }
-        return upload_tensor(m, g, *t, w);
+        return upload_tensor(m, g, *g.info(name), w);
     };
     ocr_status st = OCR_OK;
     for (int l = 0; l < c.n_layer && st == OCR_OK; l++)
         for (int k = 0; k < 11 && st == OCR_OK; k++)
-            st = load_one(l, k, "blk." + std::to_string(l) + "." + names[k] + ".weight");
+            st = load_one(l, k, "blk." + std::to_string(l) + "." + KIND_NAMES[k] + ".weight");
     if (st == OCR_OK) st = load_one(-1, 0, "token_embd.weight");
     if (st == OCR_OK) st = load_one(-1, 1, "output_norm.weight");
     if (st != OCR_OK) {
@@ -1328,6 +1362,170 @@ ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_
     a.nb = 1;
     a.err = ctx->d_err;
     launch_attention_decode(st, a, false);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
+
+// ---- GGUF reader, host only ---------------------------------------------------------------------------------------
+struct ocr_gguf {
+    Gguf g;
+};
+
+ocr_status ocr_gguf_open(const char* path, ocr_gguf** out) {
+    if (!path || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg;
+    auto src = file_source(path, msg);
+    if (!src) return fail(OCR_ERR_IO, msg);
+    auto* h = new ocr_gguf;
+    if (!h->g.parse(std::move(src), msg)) {
+        delete h;
+        return fail(OCR_ERR_FORMAT, std::string(path) + " is not a readable GGUF: " + msg);
+    }
+    *out = h;
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_open_memory(const void* bytes, size_t n, ocr_gguf** out) {
+    if ((!bytes && n) || !out) return fail(OCR_ERR_ARG, "null argument");
+    static const uint8_t empty = 0;
+    std::string msg;
+    auto* h = new ocr_gguf;
+    if (!h->g.parse(memory_source(bytes ? bytes : &empty, n), msg)) {
+        delete h;
+        return fail(OCR_ERR_FORMAT, "not a readable GGUF: " + msg);
+    }
+    *out = h;
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_close(ocr_gguf* g) {
+    delete g;
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_header(const ocr_gguf* h, uint32_t* version, uint64_t* n_tensors, uint64_t* alignment,
+                           uint64_t* data_offset) {
+    if (!h) return fail(OCR_ERR_ARG, "null argument");
+    if (version) *version = h->g.version;
+    if (n_tensors) *n_tensors = h->g.tensors.size();
+    if (alignment) *alignment = h->g.alignment;
+    if (data_offset) *data_offset = h->g.data_offset;
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_get_u32(const ocr_gguf* h, const char* key, uint32_t* out) {
+    if (!h || !key || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg;
+    if (!h->g.get_u32(key, *out, msg)) return fail(OCR_ERR_FORMAT, msg);
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_get_f32(const ocr_gguf* h, const char* key, float* out) {
+    if (!h || !key || !out) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg;
+    if (!h->g.get_f32(key, *out, msg)) return fail(OCR_ERR_FORMAT, msg);
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_get_str(const ocr_gguf* h, const char* key, char* out, size_t cap) {
+    if (!h || !key || !out || !cap) return fail(OCR_ERR_ARG, "null argument");
+    std::string msg, v;
+    if (!h->g.get_str(key, v, msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (v.size() + 1 > cap) return fail(OCR_ERR_ARG, key + std::string(": string longer than the buffer"));
+    memcpy(out, v.c_str(), v.size() + 1);
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_f32_array(const ocr_gguf* h, const char* key, float* out, size_t cap, size_t* n) {
+    if (!h || !key || !n) return fail(OCR_ERR_ARG, "null argument");
+    auto it = h->g.meta.find(key);
+    if (it == h->g.meta.end()) return fail(OCR_ERR_FORMAT, std::string("GGUF has no metadata key ") + key);
+    if (it->second.type != 9) return fail(OCR_ERR_FORMAT, std::string(key) + " is not an array");
+    const auto& a = it->second.arr;
+    for (const auto& v : a)
+        if (v.type != 6) return fail(OCR_ERR_FORMAT, std::string(key) + " holds a non-f32 value");
+    *n = a.size();
+    if (out) {
+        if (cap < a.size()) return fail(OCR_ERR_ARG, "output buffer too small");
+        for (size_t i = 0; i < a.size(); i++) out[i] = (float)a[i].f;
+    }
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_tensor(const ocr_gguf* h, const char* name, int* ggml_type, uint64_t shape[4], int* n_dims,
+                           uint64_t* file_offset) {
+    if (!h || !name) return fail(OCR_ERR_ARG, "null argument");
+    const GTensor* t = h->g.info(name);
+    if (!t) return fail(OCR_ERR_FORMAT, std::string("GGUF has no tensor ") + name);
+    if (ggml_type) *ggml_type = t->type == GType::F32 ? 0 : t->type == GType::F16 ? 1 : t->type == GType::Q8_0 ? 8 : 30;
+    if (shape)
+        for (int i = 0; i < 4; i++) shape[i] = i < (int)t->shape.size() ? t->shape[i] : 1;
+    if (n_dims) *n_dims = (int)t->shape.size();
+    if (file_offset) *file_offset = t->file_offset;
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_to_f32(const ocr_gguf* h, const char* name, float* out, size_t cap, size_t* n) {
+    if (!h || !name || !n) return fail(OCR_ERR_ARG, "null argument");
+    const GTensor* t = h->g.info(name);
+    if (!t) return fail(OCR_ERR_FORMAT, std::string("GGUF has no tensor ") + name);
+    if (t->n_bytes() > (1u << 20))
+        return fail(OCR_ERR_ARG, std::string(name) + ": " + std::to_string(t->n_bytes()) + " bytes is not small");
+    *n = (size_t)t->n_elements();
+    if (!out) return OCR_OK;
+    if (cap < *n) return fail(OCR_ERR_ARG, "output buffer too small");
+    std::vector<uint8_t> d((size_t)t->n_bytes());
+    std::string msg;
+    if (!h->g.src->read_at(t->file_offset, d.data(), d.size(), msg)) return fail(OCR_ERR_IO, msg);
+    auto h2f = [](uint16_t x) { return __half2float(__ushort_as_half(x)); };
+    switch (t->type) {
+    case GType::F32: memcpy(out, d.data(), *n * 4); break;
+    case GType::F16:
+        for (size_t i = 0; i < *n; i++) out[i] = h2f((uint16_t)(d[2 * i] | (d[2 * i + 1] << 8)));
+        break;
+    case GType::BF16:
+        for (size_t i = 0; i < *n; i++) {
+            const uint32_t b = (uint32_t)(d[2 * i] | (d[2 * i + 1] << 8)) << 16;
+            memcpy(&out[i], &b, 4);
+        }
+        break;
+    case GType::Q8_0:
+        for (size_t b = 0; b < *n / 32; b++) {
+            const uint8_t* blk = d.data() + b * 34;
+            const float s = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int j = 0; j < 32; j++) out[b * 32 + j] = (float)(int8_t)blk[2 + j] * s;
+        }
+        break;
+    }
+    return OCR_OK;
+}
+
+ocr_status ocr_gguf_text_config(const ocr_gguf* h, ocr_text_cfg* out) {
+    if (!h || !out) return fail(OCR_ERR_ARG, "null argument");
+    ocr_text_cfg c{};
+    OCR_TRY(validate_gguf(h->g, c));
+    *out = c;
+    return OCR_OK;
+}
+
+ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp, int window, const int32_t* d_hist,
+                           int n_hist) {
+    if (!ctx || !d_logits || (!d_hist && n_hist)) return fail(OCR_ERR_ARG, "null argument");
+    if (rp != 1.0f && !(std::isnormal(rp) && rp > 0.0f)) return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
+    if (window < 1 || n_vocab < 1 || n_hist < 0) return fail(OCR_ERR_ARG, "bad sizes");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    OCR_TRY(ensure_op_scratch(ctx, 256));
+    OCR_CUDA(cudaMemcpyAsync(ctx->op_scratch, &n_hist, 4, cudaMemcpyHostToDevice, ctx->stream));
+    LmArgs a;
+    a.nb = 1;
+    a.sample = 1;
+    a.rp = rp;
+    a.window = window;
+    a.hist = const_cast<int32_t*>(d_hist);
+    a.hist_cap = n_hist;
+    a.len = (int32_t*)ctx->op_scratch;
+    launch_penalize(ctx->stream, d_logits, n_vocab, a, ctx->num_sms);
     OCR_CUDA(cudaGetLastError());
     return OCR_OK;
 }

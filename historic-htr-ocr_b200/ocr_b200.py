@@ -71,6 +71,20 @@ _SIGS = {
                              C.POINTER(C.c_int)]),
     "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
+    "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
+    "ocr_gguf_open_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
+    "ocr_gguf_close": (C.c_int, [_P]),
+    "ocr_gguf_header": (C.c_int, [_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                                  C.POINTER(C.c_uint64)]),
+    "ocr_gguf_get_u32": (C.c_int, [_P, C.c_char_p, C.POINTER(C.c_uint32)]),
+    "ocr_gguf_get_f32": (C.c_int, [_P, C.c_char_p, C.POINTER(C.c_float)]),
+    "ocr_gguf_get_str": (C.c_int, [_P, C.c_char_p, C.c_char_p, C.c_size_t]),
+    "ocr_gguf_f32_array": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "ocr_gguf_tensor": (C.c_int, [_P, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_uint64 * 4),
+                                  C.POINTER(C.c_int), C.POINTER(C.c_uint64)]),
+    "ocr_gguf_to_f32": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "ocr_gguf_text_config": (C.c_int, [_P, C.POINTER(TextCfg)]),
+    "ocr_op_penalize": (C.c_int, [_P, _P, C.c_int, C.c_float, C.c_int, _P, C.c_int]),
     "ocr_op_repack_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
     "ocr_op_matvec_q8_0": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_int, _P, C.c_int]),
     "ocr_op_lm_head_sample": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P, _P,
@@ -345,6 +359,79 @@ def choose_gpu(ctx: Context, d_logits: int, n_vocab: int, preset: Preset, histor
 # ---------------------------------------------------------------------------------------------------------------------
 # low-level ops on device pointers (ints)
 # ---------------------------------------------------------------------------------------------------------------------
+class Gguf:
+    """ocr_gguf::Gguf (host only): header, metadata, tensor infos, small tensors as f32, the text config."""
+
+    def __init__(self, path: Optional[str] = None, data: Optional[bytes] = None):
+        h = C.c_void_p()
+        if path is not None:
+            _check(lib().ocr_gguf_open(str(path).encode(), C.byref(h)))
+        else:
+            self._buf = C.create_string_buffer(data, len(data)) if data else None
+            _check(lib().ocr_gguf_open_memory(self._buf, len(data or b""), C.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            lib().ocr_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def header(self) -> dict:
+        v, n, a, d = C.c_uint32(), C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(lib().ocr_gguf_header(self.h, C.byref(v), C.byref(n), C.byref(a), C.byref(d)))
+        return dict(version=v.value, n_tensors=n.value, alignment=a.value, data_offset=d.value)
+
+    def u32(self, key: str) -> int:
+        v = C.c_uint32()
+        _check(lib().ocr_gguf_get_u32(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def f32(self, key: str) -> float:
+        v = C.c_float()
+        _check(lib().ocr_gguf_get_f32(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def str(self, key: str) -> str:
+        buf = C.create_string_buffer(4096)
+        _check(lib().ocr_gguf_get_str(self.h, key.encode(), buf, 4096))
+        return buf.value.decode()
+
+    def f32_array(self, key: str) -> list[float]:
+        n = C.c_size_t()
+        _check(lib().ocr_gguf_f32_array(self.h, key.encode(), None, 0, C.byref(n)))
+        out = np.empty(n.value, np.float32)
+        _check(lib().ocr_gguf_f32_array(self.h, key.encode(), _ptr(out), n.value, C.byref(n)))
+        return out.tolist()
+
+    def info(self, name: str) -> dict:
+        ty, nd, off = C.c_int(), C.c_int(), C.c_uint64()
+        shape = (C.c_uint64 * 4)()
+        _check(lib().ocr_gguf_tensor(self.h, name.encode(), C.byref(ty), C.byref(shape), C.byref(nd), C.byref(off)))
+        return dict(type=ty.value, shape=list(shape)[: nd.value], file_offset=off.value)
+
+    def to_f32(self, name: str) -> np.ndarray:
+        n = C.c_size_t()
+        _check(lib().ocr_gguf_to_f32(self.h, name.encode(), None, 0, C.byref(n)))
+        out = np.empty(n.value, np.float32)
+        _check(lib().ocr_gguf_to_f32(self.h, name.encode(), _ptr(out), n.value, C.byref(n)))
+        return out
+
+    def text_config(self) -> TextConfig:
+        c = TextCfg()
+        _check(lib().ocr_gguf_text_config(self.h, C.byref(c)))
+        return TextConfig.from_c(c)
+
+
+def op_penalize(ctx: Context, d_logits: int, n_vocab: int, rp: float, window: int, d_hist: int, n_hist: int) -> None:
+    _check(lib().ocr_op_penalize(ctx.h, d_logits, n_vocab, rp, window, d_hist, n_hist))
+
+
 def op_repack_q8_0(ctx: Context, d_blocks: int, rows: int, cols: int, d_quants: int, d_scales: int) -> None:
     _check(lib().ocr_op_repack_q8_0(ctx.h, d_blocks, rows, cols, d_quants, d_scales))
 

@@ -124,7 +124,32 @@ ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, c
                              const int32_t* history, int n_hist, const int32_t* count_tok, const uint32_t* count_n,
                              int n_counts, int32_t* tok);
 
+/* ---- GGUF reader, host only (ocr_gguf::Gguf, app/crates/ocr-gguf/src/lib.rs:213-509) ------------------------------ */
+typedef struct ocr_gguf ocr_gguf;
+/* Gguf::open / Gguf::from_source (lib.rs:291-338): the header from a growing prefix, every tensor inside the file */
+ocr_status ocr_gguf_open(const char* path, ocr_gguf** out);
+ocr_status ocr_gguf_open_memory(const void* bytes, size_t n_bytes, ocr_gguf** out);
+ocr_status ocr_gguf_close(ocr_gguf* g);
+ocr_status ocr_gguf_header(const ocr_gguf* g, uint32_t* version, uint64_t* n_tensors, uint64_t* alignment,
+                           uint64_t* data_offset);
+/* Gguf::u32 / f32 / str / f32_array (lib.rs:415-460); a string is copied NUL-terminated into out[cap] */
+ocr_status ocr_gguf_get_u32(const ocr_gguf* g, const char* key, uint32_t* out);
+ocr_status ocr_gguf_get_f32(const ocr_gguf* g, const char* key, float* out);
+ocr_status ocr_gguf_get_str(const ocr_gguf* g, const char* key, char* out, size_t cap);
+ocr_status ocr_gguf_f32_array(const ocr_gguf* g, const char* key, float* out, size_t cap, size_t* n);
+/* Gguf::info (lib.rs:462-465): ggml type (0 f32, 1 f16, 8 q8_0, 30 bf16), shape (ggml order), absolute offset */
+ocr_status ocr_gguf_tensor(const ocr_gguf* g, const char* name, int* ggml_type, uint64_t shape[4], int* n_dims,
+                           uint64_t* file_offset);
+/* Gguf::to_f32 (lib.rs:494-509) of a small tensor (<= 1 MiB) */
+ocr_status ocr_gguf_to_f32(const ocr_gguf* g, const char* name, float* out, size_t cap, size_t* n);
+/* TextConfig::from_gguf + TextModel::load's tensor checks (text.rs:51-82, 111-128, 332-375), no device */
+ocr_status ocr_gguf_text_config(const ocr_gguf* g, ocr_text_cfg* out);
+
 /* ---- low-level ops on device buffers (the kernels behind the calls above; tests and the LM-head benchmark) ------ */
+/* choose_pen.wgsl: the windowed repetition penalty in place on d_logits [n_vocab] over the distinct tokens of
+ * d_hist[n_hist - window, n_hist) (device ids) — the device function the fused sampler applies */
+ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp, int window, const int32_t* d_hist,
+                           int n_hist);
 /* GGUF q8_0 blocks (34 B each, rows x cols/32 blocks, any alignment) → the device layout: quants [rows][cols] int8
  * (16-B aligned rows) + scales [rows][cols/32] f16. Same values. (Gpu::upload_tensor's q8_0 case, gpu.rs:1595-1647) */
 ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, int8_t* d_quants,

@@ -1,0 +1,187 @@
+"""The whole decode path on a B200 through the C ABI, against the CPU oracle.
+
+- the seeded synthetic generator on the device gives the oracle's weights bit for bit; a GGUF written from the
+  oracle's tensors loads (stream + repack) to the same device bytes (ocr_model_checksum)
+- prefill, the CPU-choice step loop and the device-choice run-ahead decode of a small qwen3-shaped model match the
+  oracle: logits within 2e-3 of max |logit| (the acceptance bound) and 1e-4 relative L2; greedy ids identical
+  (kv_growth_matches_presized_cache's checks, app/crates/ocr-wgpu/src/text.rs:1329-1379, on this engine's
+  preallocated cache)
+- batched decode equals one slot at a time; a callback that stops ends the read where it says
+- BASELINE config 2 at full size: the 512 greedy ids equal the oracle's (tests/golden/config2_greedy.json)
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import gguf_writer as W
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+# the reference's tiny_text_model shape (text.rs:1297-1323): 5 layers, dim 256, 2 q heads on 1 kv head, ffn 512
+TINY = dict(n_layer=5, dim=256, n_head=2, n_kv=1, d_head=128, n_ff=512, n_vocab=1000, eps=1e-6, rope_base=1e6)
+
+
+def text_config(ocr, c, n_ctx_train=40960):
+    return ocr.TextConfig(c["n_layer"], c["dim"], c["n_head"], c["n_kv"], c["d_head"], c["n_ff"], c["n_vocab"],
+                          n_ctx_train, c.get("eps", 1e-6), c.get("rope_base", 1e6))
+
+
+def close_logits(got, want):
+    m = np.abs(want).max()
+    assert np.abs(got - want).max() <= 2e-3 * m, np.abs(got - want).max() / m
+    rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert rel < 1e-4, rel
+
+
+@pytest.fixture(scope="module")
+def tiny(ocr, orc, ctx):
+    om = orc.Model(TINY, seed=31, sigma_w=0.2, sigma_e=1.0)
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, TINY), 31, 0.2, 1.0)
+    return om, gm
+
+
+def test_synthetic_weights_are_the_oracles(ocr, orc, tiny):
+    om, gm = tiny
+    for layer in range(TINY["n_layer"]):
+        for kind in range(11):
+            assert gm.tensor_gguf(layer, kind) == om.tensor(layer, kind).tobytes(), (layer, kind)
+    assert gm.tensor_gguf(-1, 0) == om.tensor(-1, 0).tobytes()
+    assert gm.tensor_gguf(-1, 1) == om.tensor(-1, 1).tobytes()
+
+
+def test_gguf_load_equals_synthetic(ocr, orc, ctx, tiny, tmp_path):
+    om, gm = tiny
+    data = W.text_model(om)
+    p = tmp_path / "tiny.gguf"
+    p.write_bytes(data)
+    a = ocr.TextModel.load(ctx, str(p))
+    b = ocr.TextModel.from_bytes(ctx, W.text_model(om, alignment=64))
+    assert a.checksum() == gm.checksum() == b.checksum()
+    assert a.cfg.n_vocab == 1000 and a.cfg.n_layer == 5
+
+
+def test_prefill_step_decode_match_oracle(ocr, orc, ctx, tiny):
+    om, gm = tiny
+    prompt = [int(t) for t in orc.fill_ids(5, 20, TINY["n_vocab"])]
+    n_new, n_steps = 150, 40
+    n_ctx = len(prompt) + n_new
+    # the CPU-choice path: prefill, then steps of the greedy token, logits every step
+    gs = gm.session(n_ctx)
+    osn = om.session(n_ctx)
+    lg = gs.prefill(0, ids=prompt)
+    lo = osn.prefill(prompt, None, len(prompt))
+    close_logits(lg, lo)
+    for _ in range(n_steps):
+        t = int(np.argmax(lo))
+        lg = gs.step([t])[0]
+        lo = osn.step(t)
+        close_logits(lg, lo)
+    assert gs.n_past(0) == len(prompt) + n_steps
+    # the device choice, run ahead, from the prompt's logits
+    gs2 = gm.session(n_ctx)
+    gs2.prefill(0, ids=prompt, logits=False)
+    preset = ocr.Preset("greedy_rp1.1", 0.0, 1.0, 1.1, 20, 0.0, n_new)
+    got = gs2.decode_gpu(0, preset, prompt)
+    assert len(got) == n_new
+    assert gs2.n_past(0) == n_ctx - 1  # the last choice needs no row
+    os2 = om.session(n_ctx)
+    first = os2.prefill(prompt, None, len(prompt))
+    want, margins = os2.decode(first, 1.1, 20, 0.0, prompt, n_new)
+    k = next((i for i in range(n_new) if got[i] != want[i]), None)
+    assert k is None, f"first divergence at choice {k}: device {got[k]} vs oracle {want[k]} (oracle top-2 margin {margins[k]})"
+
+
+def test_frequency_penalty_decode_matches_oracle(ocr, orc, ctx, tiny):
+    om, gm = tiny
+    prompt = [int(t) for t in orc.fill_ids(6, 12, TINY["n_vocab"])]
+    n_new = 60
+    gs = gm.session(len(prompt) + n_new)
+    gs.prefill(0, ids=prompt, logits=False)
+    got = gs.decode_gpu(0, ocr.Preset("greedy_rp1.1_fp0.1", 0.0, 1.0, 1.1, 20, 0.1, n_new), prompt)
+    os_ = om.session(len(prompt) + n_new)
+    first = os_.prefill(prompt, None, len(prompt))
+    want, margins = os_.decode(first, 1.1, 20, 0.1, prompt, n_new)
+    assert got == want.tolist()
+
+
+def test_embedding_rows_and_batch_equal_single(ocr, orc, ctx, tiny):
+    """Input::Embeddings rows mixed with tokens; decode_batch == each slot decoded alone (same session shape)"""
+    om, gm = tiny
+    B, n_new = 3, 24
+    rows = [int(t) for t in orc.fill_ids(8, 10, TINY["n_vocab"])]
+    prompts = []
+    for b in range(B):
+        ids = np.array(rows[: 4 + b] + [-1] * 6 + rows[4 + b:], np.int32)
+        embd = np.zeros((ids.size, TINY["dim"]), np.float32)
+        embd[ids < 0] = ocr.gauss(100 + b, int((ids < 0).sum()) * TINY["dim"]).reshape(-1, TINY["dim"])
+        prompts.append((ids, embd))
+    preset = ocr.Preset("t", 0.0, 1.0, 1.15, 8, 0.0, n_new)
+    hist = np.full((B, 8), 151655 % TINY["n_vocab"], np.int32)
+    sa = gm.session(64, batch=B)
+    sb = gm.session(64, batch=B)
+    for b, (ids, embd) in enumerate(prompts):
+        la = sa.prefill(b, ids=ids, embd=embd)
+        sb.prefill(b, ids=ids, embd=embd, logits=False)
+        os_ = om.session(64)
+        lo = os_.prefill(ids, embd, ids.size)
+        close_logits(la, lo)
+    batch = sa.decode_batch(preset, hist)
+    for b in range(B):
+        single = sb.decode_gpu(b, preset, hist[b])
+        assert single == batch[b].tolist(), b
+
+
+def test_callback_stops_the_read(ocr, orc, ctx, tiny):
+    om, gm = tiny
+    prompt = [int(t) for t in orc.fill_ids(9, 16, TINY["n_vocab"])]
+    preset = ocr.Preset("t", 0.0, 1.0, 1.1, 20, 0.0, 80)
+    s1 = gm.session(120)
+    s1.prefill(0, ids=prompt, logits=False)
+    full = s1.decode_gpu(0, preset, prompt)
+    seen = []
+    s2 = gm.session(120)
+    s2.prefill(0, ids=prompt, logits=False)
+    got = s2.decode_gpu(0, preset, prompt, on_token=lambda t: (seen.append(t), len(seen) < 37)[1])
+    assert got == full[:37] and seen == full[:37]
+
+
+def test_session_errors(ocr, ctx, tiny):
+    om, gm = tiny
+    s = gm.session(30)
+    with pytest.raises(ocr.OcrError, match="no logits"):
+        s.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1.1, 20, 0.0, 5), [1])
+    with pytest.raises(ocr.OcrError, match="outside the vocabulary"):
+        s.prefill(0, ids=[5, 1000])
+    with pytest.raises(ocr.OcrError, match="overflow"):
+        s.prefill(0, ids=list(range(31)))
+    s.prefill(0, ids=list(range(25)), logits=False)
+    with pytest.raises(ocr.OcrError, match="overflows"):
+        s.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1.1, 20, 0.0, 10), [1])
+    with pytest.raises(ocr.OcrError, match="positive normal"):
+        s.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1e-40, 20, 0.0, 2), [1])
+    with pytest.raises(ocr.OcrError, match="trained on"):
+        gm.session(50000)
+
+
+def test_config2_greedy_ids_match_oracle(ocr, ctx):
+    """BASELINE config 2 at full size: 28 layers, 2048-row prefix, 512 greedy ids with rp 1.15 / window 64"""
+    fx = json.loads((GOLDEN / "config2_greedy.json").read_text())
+    from tests.golden.make_golden import config2_inputs
+
+    seed, prefix, history = config2_inputs()
+    assert seed == fx["seed"]
+    m = ocr.TextModel.synthetic(ctx, text_config(ocr, fx["config"]), seed, fx["sigma_w"], fx["sigma_e"])
+    s = m.session(2048 + 512)
+    first = s.prefill(0, embd=prefix)
+    top = np.argsort(-first, kind="stable")[:8]
+    assert abs(float(np.abs(first).max()) - fx["first_max_abs"]) <= 2e-3 * fx["first_max_abs"]
+    assert top[0] == fx["first_top8"][0]
+    got = s.decode_gpu(0, ocr.Preset("c2", 0.0, 1.0, fx["rp"], fx["window"], 0.0, fx["max_new"]), history)
+    want = fx["ids"]
+    k = next((i for i in range(len(want)) if got[i] != want[i]), None)
+    assert k is None, f"first divergence at choice {k}: device {got[k]} vs oracle {want[k]} (margin {fx['margins'][k]})"
