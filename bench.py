@@ -107,8 +107,11 @@ def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
     (4 KB) + logits written (607,744 B) + the 64-token window; L2 flushed between launches (256 MB write)"""
     V, D = 151936, 1024
     g = torch.Generator(device="cuda").manual_seed(1)
-    q = torch.randint(-127, 128, (V, D), dtype=torch.int8, device="cuda", generator=g)
-    d = (torch.rand(V, D // 32, device="cuda", generator=g) * 0.0003 + 0.0001).half()
+    stride = ocr.q8_row_bytes(D)
+    w = torch.zeros(V, stride, dtype=torch.uint8, device="cuda")
+    w[:, :D] = torch.randint(-127, 128, (V, D), dtype=torch.int8, device="cuda", generator=g).view(torch.uint8)
+    w[:, D:D + D // 16] = (torch.rand(V, D // 32, device="cuda", generator=g) * 0.0003 + 0.0001).half() \
+        .view(torch.uint8)
     x = torch.randn(D, device="cuda", generator=g)
     nw = torch.ones(D, device="cuda")
     hist = torch.randint(0, V, (512 + reps + 8,), dtype=torch.int32, device="cuda", generator=g)
@@ -126,8 +129,8 @@ def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        ocr.op_lm_head_sample(ctx, q.data_ptr(), d.data_ptr(), V, D, x.data_ptr(), nw.data_ptr(), 1e-6, 1.15, 64,
-                              hist.data_ptr(), ln.data_ptr(), tok.data_ptr(), logits.data_ptr())
+        ocr.op_lm_head_sample(ctx, w.data_ptr(), V, D, x.data_ptr(), nw.data_ptr(), 1e-6, 1.15, 64, hist.data_ptr(),
+                              ln.data_ptr(), tok.data_ptr(), logits.data_ptr())
         b.record(stream)
         b.synchronize()
         if i >= 3:

@@ -90,10 +90,61 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // device-side error flag (ocr_ctx_sync reports it): the first code wins
-enum DevErr : int { DEV_OK = 0, DEV_BAD_INDEX = 1, DEV_BAD_POS = 2 };
+enum DevErr : int { DEV_OK = 0, DEV_BAD_INDEX = 1, DEV_BAD_POS = 2, DEV_TIMEOUT = 3 };
 
 __device__ __forceinline__ void dev_error(int* flag, int code) {
     if (flag) atomicCAS(flag, 0, code);
+}
+
+// ---- bulk-async copies (the copy engine, no tensor map: contiguous 16-B multiples) and mbarriers ----------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// make the initialised barriers visible to the copy engine (async proxy)
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// one poll that suspends the thread until the phase completes or `hint_ns` nanoseconds pass
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 100000) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// a bounded wait: gives up after MBAR_TRIES polls of at most 100 µs each (≈ 2 s), flags DEV_TIMEOUT, returns false
+constexpr uint32_t MBAR_TRIES = 20000;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    dev_error(err, DEV_TIMEOUT);
+    return false;
+}
+
+// global → shared, `bytes` (multiple of 16, both addresses 16-B aligned), completion counted on `bar`
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// a barrier among the first `threads` threads of the CTA (named barrier 1; the producer warp stays out)
+__device__ __forceinline__ void bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace ocr

@@ -1,250 +1,47 @@
-// k_matvec.cu — q8_0 dequant-matvec for decode (the reference's dmv / dmv_norm / dmv_qkv / dmv_ffn / matvec_q8_0
-// kernels, shaders/*.wgsl) and the LM head fused with the greedy token choice (choose_pen / choose_max / choose_pick).
+// k_matvec.cu — q8_0 dequant-matvec for decode (the reference's dmv / dmv_norm / dmv_qkv / dmv_ffn / matvec_q8_0,
+// shaders/*.wgsl) and the LM head fused with the greedy token choice (choose_pen / choose_max / choose_pick).
 //
-// Mapping (256 threads = 8 warps): a warp owns R rows at a time; lane l reads, per 512-column chunk i, the 16 quants at
-// columns 512 i + 16 l (one 16-B streaming load per row: the warp's 32 loads are one contiguous 512 B) and the f16
-// scale of their block. The activations x (NB slots, RMSNorm and the norm weight folded in when asked) sit in shared
-// memory "lane-blocked" — float4 index ((s * nch + i) * 4 + j4) * 32 + l holds x[s][512 i + 16 l + 4 j4 … +4] — so the
-// 4 float4 reads a lane makes per chunk are bank-conflict free. int8 → f32 by byte-permute into 2^23's mantissa.
-// Per row: lane partial = sum over its half-blocks of scale * dot16; warp butterfly sum; the epilogue stores, adds the
-// residual, or pairs interleaved gate/up rows into silu(gate) * up.
+// One kernel, streamed through the copy engine. A CTA owns a contiguous range of rows — one contiguous byte range in
+// the row layout (kernels.cuh) — cut into stages of SR = W x R rows. Warp W (the producer; one lane) moves stage after
+// stage with cp.async.bulk into a ring of NS shared-memory slots, each slot's arrival counted by an mbarrier
+// (complete_tx); the first NS stages are issued BEFORE griddepcontrol.wait, since weights never depend on the previous
+// kernel: their DRAM latency overlaps the previous kernel's tail. Warps 0..W-1 (consumers) wait for the previous
+// kernel, stage the activations (NB slots; RMSNorm x norm weight folded in; layer 0 gathers the token's embedding row)
+// in shared memory "lane-blocked" — float4 ((s * nch + i) * 4 + j4) * 32 + l holds x[s][512 i + 16 l + 4 j4 … +4] —
+// then, per stage, each warp takes R rows: lane l reads the 16 quants at columns 512 i + 16 l (one conflict-free
+// 16-B shared load), their block scale, dequantizes by byte-permute into 2^23's mantissa (exact), and accumulates
+// scale * dot16 per slot. A consumed slot is released with an mbarrier arrive (count W). Warp butterfly sums, then the
+// epilogue: store, residual add, silu(gate) * up over interleaved gate/up rows, or the LM head's choice.
+// Every wait is bounded (mbar_wait → DEV_TIMEOUT); no spin on another CTA.
 #include "kernels.cuh"
 
 namespace ocr {
 
-constexpr int MV_WARPS = 8;
-constexpr int MV_THREADS = MV_WARPS * 32;
-
-// dot of 16 dequantized quants (one 16-B load) with the lane's 16 activations of chunk i (4 float4 in smem)
-__device__ __forceinline__ float dot16(const float* wf, const float4* xs4, int base, int lane) {
-    const float4 a = xs4[base + 0 * 32 + lane];
-    const float4 b = xs4[base + 1 * 32 + lane];
-    const float4 c = xs4[base + 2 * 32 + lane];
-    const float4 e = xs4[base + 3 * 32 + lane];
-    float s0 = wf[0] * a.x, s1 = wf[1] * a.y, s2 = wf[2] * a.z, s3 = wf[3] * a.w;
-    s0 = fmaf(wf[4], b.x, s0);
-    s1 = fmaf(wf[5], b.y, s1);
-    s2 = fmaf(wf[6], b.z, s2);
-    s3 = fmaf(wf[7], b.w, s3);
-    s0 = fmaf(wf[8], c.x, s0);
-    s1 = fmaf(wf[9], c.y, s1);
-    s2 = fmaf(wf[10], c.z, s2);
-    s3 = fmaf(wf[11], c.w, s3);
-    s0 = fmaf(wf[12], e.x, s0);
-    s1 = fmaf(wf[13], e.y, s1);
-    s2 = fmaf(wf[14], e.z, s2);
-    s3 = fmaf(wf[15], e.w, s3);
-    return (s0 + s1) + (s2 + s3);
-}
-
-__device__ __forceinline__ void unpack16(const uint4 w, float* wf) {
-    i8x4_to_f32(w.x, wf + 0);
-    i8x4_to_f32(w.y, wf + 4);
-    i8x4_to_f32(w.z, wf + 8);
-    i8x4_to_f32(w.w, wf + 12);
-}
-
-// the smem float index of x[s][c] in the lane-blocked layout
-__device__ __forceinline__ int xs_index(int s, int nch, int c) {
-    const int i = c >> 9, w = c & 511, l = w >> 4, j = w & 15;
-    return ((((s * nch + i) * 4 + (j >> 2)) * 32 + l) << 2) + (j & 3);
-}
-
-__device__ __forceinline__ float block_sum(float v, float* red) {
-    v = warp_sum(v);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-#pragma unroll
-    for (int k = 0; k < MV_WARPS; k++) t += red[k];
-    return t;
-}
-
-// x rows → smem (optionally from the embedding table, optionally RMS-normalised and scaled by nw)
-template <int NB>
-__device__ __forceinline__ void stage_x(float* xsf, int nch, int K, int nb, int slot0, const float* x, int x_stride,
-                                        const float* nw, float eps, const int32_t* tok, const QMat& emb, float* x_out,
-                                        bool write_x, float* red) {
-    for (int s = 0; s < nb; s++) {
-        const int b = slot0 + s;
-        float ss = 0.0f;
-        int t = -1;
-        if (tok) {
-            t = tok[b];
-            if (t < 0 || t >= emb.rows) t = -1;
-        }
-        for (int c = threadIdx.x; c < K; c += MV_THREADS) {
-            float v;
-            if (tok) v = t < 0 ? 0.0f : (float)emb.q[(long)t * K + c] * __half2float(emb.d[(long)t * (K / 32) + c / 32]);
-            else v = x[(long)b * x_stride + c];
-            if (write_x) x_out[(long)b * x_stride + c] = v;  // idle slots get zeros (scratch only)
-            ss = fmaf(v, v, ss);
-            xsf[xs_index(s, nch, c)] = v;
-        }
-        if (nw) {
-            const float tot = block_sum(ss, red);
-            const float scale = 1.0f / sqrtf(tot / (float)K + eps);
-            for (int c = threadIdx.x; c < K; c += MV_THREADS) {
-                const int k = xs_index(s, nch, c);
-                xsf[k] = xsf[k] * scale * nw[c];
-            }
-        }
-    }
-}
-
-template <int NB, int R, int CH>
-__global__ void __launch_bounds__(MV_THREADS) k_matvec(MvArgs a) {
-    extern __shared__ float4 xs4[];
-    __shared__ float red[MV_WARPS];
-    float* xsf = reinterpret_cast<float*>(xs4);
-    const int K = a.w.cols, N = a.w.rows;
-    const int nch = (K + 511) >> 9;
-    const int slot0 = blockIdx.y * NB;
-    const int nb = min(NB, a.nb - slot0);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-    pdl_wait();
-    stage_x<NB>(xsf, nch, K, nb, slot0, a.x, a.x_stride, a.nw, a.eps, a.tok, a.emb, a.x_out,
-                a.x_out != nullptr && blockIdx.x == 0, red);
-    __syncthreads();
-
-    const long groups = (N + R - 1) / R;
-    const int kb = K >> 5;
-    for (long g = (long)blockIdx.x * MV_WARPS + warp; g < groups; g += (long)gridDim.x * MV_WARPS) {
-        const int row0 = (int)(g * R);
-        float acc[NB][R];
-#pragma unroll
-        for (int s = 0; s < NB; s++)
-#pragma unroll
-            for (int r = 0; r < R; r++) acc[s][r] = 0.0f;
-        for (int i0 = 0; i0 < nch; i0 += CH) {
-            uint4 wq[CH][R];
-            float wd[CH][R];
-#pragma unroll
-            for (int ci = 0; ci < CH; ci++) {
-                const int col = (i0 + ci) * 512 + lane * 16;
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    const int row = row0 + r;
-                    if (i0 + ci < nch && row < N && col < K) {
-                        wq[ci][r] = ld_stream(a.w.q + (long)row * K + col);
-                        wd[ci][r] = __half2float(a.w.d[(long)row * kb + (col >> 5)]);
-                    } else {
-                        wq[ci][r] = make_uint4(0, 0, 0, 0);
-                        wd[ci][r] = 0.0f;
-                    }
-                }
-            }
-#pragma unroll
-            for (int ci = 0; ci < CH; ci++) {
-                if (i0 + ci >= nch) break;
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    float wf[16];
-                    unpack16(wq[ci][r], wf);
-#pragma unroll
-                    for (int s = 0; s < NB; s++)
-                        if (s < nb) acc[s][r] = fmaf(dot16(wf, xs4, (s * nch + i0 + ci) * 128, lane), wd[ci][r], acc[s][r]);
-                }
-            }
-        }
-#pragma unroll
-        for (int s = 0; s < NB; s++)
-#pragma unroll
-            for (int r = 0; r < R; r++) acc[s][r] = warp_sum(acc[s][r]);
-        if (lane == 0) {
-#pragma unroll
-            for (int s = 0; s < NB; s++) {
-                if (s >= nb) break;
-                const int b = slot0 + s;
-                if (a.active && !a.active[b]) continue;
-                float* y = a.y + (long)b * a.y_stride;
-                if (a.mode == MV_SWIGLU) {
-#pragma unroll
-                    for (int r = 0; r + 1 < R; r += 2) {
-                        if (row0 + r + 1 < N) {
-                            const float gv = acc[s][r], uv = acc[s][r + 1];
-                            y[(row0 + r) >> 1] = gv / (1.0f + expf(-gv)) * uv;
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        if (row0 + r < N) {
-                            if (a.mode == MV_ADD) y[row0 + r] += acc[s][r];
-                            else y[row0 + r] = acc[s][r];
-                        }
-                    }
-                }
-            }
-        }
-    }
-    pdl_trigger();
-}
-
-template <int NB, int R, int CH>
-static void launch_mv_t(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
-    const int nch = (a.w.cols + 511) / 512;
-    const size_t smem = (size_t)NB * nch * 512 * sizeof(float);
-    auto kern = k_matvec<NB, R, CH>;
-    static int configured = 0;
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        configured = 1;
-    }
-    int occ = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, MV_THREADS, smem);
-    if (occ < 1) occ = 1;
-    const long groups = (a.w.rows + R - 1) / R;
-    long blocks = (groups + MV_WARPS - 1) / MV_WARPS;
-    const long cap = (long)num_sms * occ;
-    if (blocks > cap) blocks = cap;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)blocks, (unsigned)((a.nb + NB - 1) / NB), 1);
-    cfg.blockDim = dim3(MV_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, kern, a);
-}
-
-void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
-    // slots per pass: 1, 2, 4 or 8 (more slots → more passes over the weights, one per blockIdx.y)
-    const int nb = a.nb;
-    if (nb <= 1) launch_mv_t<1, 2, 4>(st, a, num_sms, pdl);
-    else if (nb <= 2) launch_mv_t<2, 2, 2>(st, a, num_sms, pdl);
-    else if (nb <= 4) launch_mv_t<4, 2, 2>(st, a, num_sms, pdl);
-    else launch_mv_t<8, 2, 1>(st, a, num_sms, pdl);
-}
-
-// =====================================================================================================================
+// ---------------------------------------------------------------------------------------------------------------------
 // the token choice: windowed repetition penalty (distinct tokens of the window), frequency penalty, first maximum
-// =====================================================================================================================
-
+// ---------------------------------------------------------------------------------------------------------------------
 constexpr int PEN_CAP = 64;  // window tokens kept per CTA and slot (more → the CTA scans the window per row)
+constexpr int MAX_NB = 8;
 
 struct PenList {
-    int n[8];
-    int t[8][PEN_CAP];
+    int n[MAX_NB];
+    int t[MAX_NB][PEN_CAP];
 };
 
-// the window tokens of slot s that fall in [lo, hi): hist[len - min(len, window), len)
-__device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, int lo, int hi) {
-    if (threadIdx.x < 8) pl.n[threadIdx.x] = 0;
-    __syncthreads();
+// the window tokens of slot s that fall in [lo, hi): hist[len - min(len, window), len); `nthr` threads take part
+// (barrier 1)
+__device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, int lo, int hi, int nthr) {
+    const int tid = threadIdx.x;
+    if (tid < MAX_NB) pl.n[tid] = 0;
+    bar_sync(1, nthr);
     if (a.sample && a.rp != 1.0f) {
         for (int s = 0; s < nb; s++) {
             const int b = slot0 + s;
+            if (a.active && !a.active[b]) continue;
             const int len = a.len[b];
             const int start = len - min(len, a.window);
             const int32_t* h = a.hist + (long)b * a.hist_cap;
-            for (int j = start + threadIdx.x; j < len; j += blockDim.x) {
+            for (int j = start + tid; j < len; j += nthr) {
                 const int t = h[j];
                 if (t >= lo && t < hi) {
                     const int k = atomicAdd(&pl.n[s], 1);
@@ -253,7 +50,7 @@ __device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, i
             }
         }
     }
-    __syncthreads();
+    bar_sync(1, nthr);
 }
 
 // the choice's value of logit v of token t in slot s (choose(): rp on window members, then − fp * count)
@@ -278,7 +75,8 @@ __device__ __forceinline__ float pen_apply(const PenList& pl, int s, int b, int 
     return v;
 }
 
-// the CTA's best per slot → part; the last CTA of the grid row reduces all parts and records the choice
+// The CTA's best per slot → part; the last CTA of the grid row (threadfence + ticket, no waiting) reduces all parts
+// and records the choice. Called by every thread of the CTA.
 __device__ void choice_finish(const float* bv_sm, const uint32_t* bi_sm, int nb, int slot0, const LmArgs& a,
                               int n_vocab) {
     const int grid = gridDim.x;
@@ -332,28 +130,194 @@ __device__ void choice_finish(const float* bv_sm, const uint32_t* bi_sm, int nb,
     if (threadIdx.x == 0) a.done[blockIdx.y] = 0u;
 }
 
-// LM head: contiguous row ranges per CTA (so the window prefilter is per CTA), R = 2 rows per warp
-template <int NB>
-__global__ void __launch_bounds__(MV_THREADS) k_lm_head(LmArgs a, int rows_per_cta) {
-    extern __shared__ float4 xs4[];
-    __shared__ float red[MV_WARPS];
+// ---------------------------------------------------------------------------------------------------------------------
+// the streamed matvec
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int MAX_NS = 16;
+constexpr int SM_HEAD = 256;  // mbarriers full[MAX_NS], empty[MAX_NS]
+
+// ---- packed f32x2 arithmetic (sm_100): two lanes of f32 per instruction ------------------------------------------
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 16 int8 quants (one 16-B load) · 16 activations (8 f32 pairs): each byte, biased to q + 128, is placed in the
+// mantissa of 2^23 by one byte permute and 2^23 + 128 is subtracted pairwise (exact: integers below 2^24); the pairs
+// then multiply-accumulate packed, two accumulators deep. Returns the f32 dot.
+__device__ __forceinline__ float dot16x2(const uint4 w, const uint64_t* xp) {
+    const uint64_t bias = pk2(-8388736.0f, -8388736.0f);
+    const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+    uint64_t a0 = 0, a1 = 0;  // +0.0f pairs
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const uint32_t u = wv[k];
+        const uint64_t p01 = add2(pk2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7441))), bias);
+        const uint64_t p23 = add2(pk2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7443))), bias);
+        a0 = fma2(p01, xp[2 * k], a0);
+        a1 = fma2(p23, xp[2 * k + 1], a1);
+    }
+    const float2 s = upk2(add2(a0, a1));
+    return s.x + s.y;
+}
+
+// the smem float index of x[s][c] in the lane-blocked layout
+__device__ __forceinline__ int xs_index(int s, int nch, int c) {
+    const int i = c >> 9, w = c & 511, l = w >> 4, j = w & 15;
+    return ((((s * nch + i) * 4 + (j >> 2)) * 32 + l) << 2) + (j & 3);
+}
+
+// sum over the `nthr` consumer threads (barrier 1)
+__device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    bar_sync(1, nthr);
+    if (lane == 0) red[warp] = v;
+    bar_sync(1, nthr);
+    float t = 0.0f;
+    for (int k = 0; k < nthr / 32; k++) t += red[k];
+    return t;
+}
+
+// x rows → smem (from the embedding table when a.tok; RMS-normalised and scaled by nw when a.nw). Every global
+// load of a pass is issued before any is used (float4, up to XU per thread in flight): the staging costs one
+// round trip, not one per element.
+constexpr int XU = 8;
+__device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr) {
+    const int K = a.w.cols, K4 = K >> 2;
+    const bool write_x = a.x_out != nullptr && blockIdx.x == 0;
+    float4* xs4 = reinterpret_cast<float4*>(xsf);
+    const int tid = threadIdx.x;
+    for (int s = 0; s < nb; s++) {
+        const int b = slot0 + s;
+        const uint8_t* er = nullptr;
+        if (a.tok) {
+            const int t = a.tok[b];
+            if (t >= 0 && t < a.emb.rows) er = a.emb.w + (long)t * a.emb.stride;
+        }
+        const float4* xg = reinterpret_cast<const float4*>(a.x + (long)b * a.x_stride);
+        const float4* nw4 = reinterpret_cast<const float4*>(a.nw);
+        const bool fits = K4 <= XU * nthr;  // one pass: values stay in registers across the norm's reduction
+        float ss = 0.0f;
+        for (int base = 0; base < K4; base += XU * nthr) {
+            float4 v[XU], wn[XU];
+            if (a.nw && fits) {
+#pragma unroll
+                for (int u = 0; u < XU; u++) {
+                    const int i4 = base + u * nthr + tid;
+                    if (i4 < K4) wn[u] = nw4[i4];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < XU; u++) {
+                const int i4 = base + u * nthr + tid;
+                if (i4 < K4) {
+                    if (a.tok) {
+                        if (er) {
+                            const uint32_t q = *reinterpret_cast<const uint32_t*>(er + 4 * i4);
+                            const float d = __half2float(reinterpret_cast<const __half*>(er + K)[i4 >> 3]);
+                            v[u] = make_float4((float)(int8_t)(q & 0xff) * d, (float)(int8_t)((q >> 8) & 0xff) * d,
+                                               (float)(int8_t)((q >> 16) & 0xff) * d, (float)(int8_t)(q >> 24) * d);
+                        } else {
+                            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    } else {
+                        v[u] = xg[i4];
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < XU; u++) {
+                const int i4 = base + u * nthr + tid;
+                if (i4 < K4) {
+                    if (write_x) reinterpret_cast<float4*>(a.x_out + (long)b * a.x_stride)[i4] = v[u];
+                    ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+                }
+            }
+            if (a.nw && fits) {
+                // scale known after the reduction; the values wait in registers
+                const float tot = consumer_sum(ss, red, nthr);
+                const float scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+#pragma unroll
+                for (int u = 0; u < XU; u++) {
+                    const int i4 = base + u * nthr + tid;
+                    if (i4 < K4) {
+                        const float4 w = wn[u];
+                        v[u] = make_float4(v[u].x * scale * w.x, v[u].y * scale * w.y, v[u].z * scale * w.z,
+                                           v[u].w * scale * w.w);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < XU; u++) {
+                const int i4 = base + u * nthr + tid;
+                if (i4 < K4) xs4[xs_index(s, nch, 4 * i4) >> 2] = v[u];
+            }
+        }
+        // the last chunk's columns past K: lanes there see zero quants, the staged values must be finite
+        for (int c = K + 4 * tid; c < nch * 512; c += 4 * nthr) xs4[xs_index(s, nch, c) >> 2] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.nw && !fits) {
+            const float tot = consumer_sum(ss, red, nthr);
+            const float scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+            for (int c = tid; c < K; c += nthr) {
+                const int k = xs_index(s, nch, c);
+                xsf[k] = xsf[k] * scale * a.nw[c];
+            }
+        }
+    }
+}
+
+template <int NB, int W, int R>
+__global__ void __launch_bounds__((W + 1) * 32) k_mv(MvArgs a, int rpc, int ns) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* empty = full + MAX_NS;
+    constexpr int SR = W * R;
+    constexpr int NC = W * 32;  // consumer threads
+    __shared__ float red[W];
     __shared__ PenList pl;
-    __shared__ float bv_w[MV_WARPS][NB];
-    __shared__ uint32_t bi_w[MV_WARPS][NB];
+    __shared__ float bv_w[W][NB];
+    __shared__ uint32_t bi_w[W][NB];
     __shared__ float bv_sm[NB];
     __shared__ uint32_t bi_sm[NB];
-    constexpr int R = 2, CH = 2;
-    float* xsf = reinterpret_cast<float*>(xs4);
-    const int K = a.w.cols, N = a.w.rows;
-    const int nch = (K + 511) >> 9;
-    const int slot0 = blockIdx.y * NB;
-    const int nb = min(NB, a.nb - slot0);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int lo = blockIdx.x * rows_per_cta, hi = min(N, lo + rows_per_cta);
 
-    pdl_wait();
-    stage_x<NB>(xsf, nch, K, nb, slot0, a.x, a.x_stride, a.nw, a.eps, nullptr, a.w, nullptr, false, red);
-    pen_prefilter(pl, nb, slot0, a, lo, hi);  // (its barriers also publish the staged x)
+    const int K = a.w.cols, N = a.w.rows, stride = a.w.stride;
+    const int nch = (K + 511) >> 9;
+    float* xsf = reinterpret_cast<float*>(sm + SM_HEAD);
+    uint8_t* ring = sm + SM_HEAD + (size_t)NB * nch * 512 * sizeof(float);
+    const size_t stage_bytes = (size_t)SR * stride;
+    const int lo = blockIdx.x * rpc, hi = min(N, lo + rpc);
+    const int n_stage = (hi - lo + SR - 1) / SR;
+    const int slot0 = blockIdx.y * NB, nb = min(NB, a.nb - slot0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool lmhead = a.mode == MV_LMHEAD;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ns; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], W);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
 
     float bv[NB];
     uint32_t bi[NB];
@@ -362,88 +326,181 @@ __global__ void __launch_bounds__(MV_THREADS) k_lm_head(LmArgs a, int rows_per_c
         bv[s] = -INFINITY;
         bi[s] = NO_INDEX;
     }
-    const int kb = K >> 5;
-    for (int row0 = lo + warp * R; row0 < hi; row0 += MV_WARPS * R) {
-        float acc[NB][R];
+
+    if (warp == W) {
+        // ---- producer: weights never depend on the previous kernel, so no griddepcontrol.wait here ----
+        if (lane == 0) {
+            for (int t = 0; t < n_stage; t++) {
+                const int slot = t % ns;
+                if (t >= ns && !mbar_wait(&empty[slot], ((t / ns) - 1) & 1, a.err)) break;
+                const int r0 = lo + t * SR;
+                const uint32_t bytes = (uint32_t)(min(SR, hi - r0) * stride);
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_g2s(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot]);
+                if (t == min(ns, n_stage) - 1) pdl_trigger();
+            }
+        }
+    } else {
+        // ---- consumers ----
+        pdl_wait();
+        // per-slot activity, read once; for the residual add, the first stages' old values of this warp's rows are
+        // fetched now so the epilogue's read-modify-write does not wait on memory
+        bool act[NB];
 #pragma unroll
-        for (int s = 0; s < NB; s++)
+        for (int s = 0; s < NB; s++) act[s] = s < nb && (!a.active || a.active[slot0 + s] != 0);
+        constexpr int PF = 2;
+        float yold[PF][NB][R];
+        if (a.mode == MV_ADD && lane == 0) {
 #pragma unroll
-            for (int r = 0; r < R; r++) acc[s][r] = 0.0f;
-        for (int i0 = 0; i0 < nch; i0 += CH) {
-            uint4 wq[CH][R];
-            float wd[CH][R];
+            for (int t = 0; t < PF; t++)
 #pragma unroll
-            for (int ci = 0; ci < CH; ci++) {
-                const int col = (i0 + ci) * 512 + lane * 16;
+                for (int s = 0; s < NB; s++)
 #pragma unroll
-                for (int r = 0; r < R; r++) {
-                    const int row = row0 + r;
-                    if (i0 + ci < nch && row < hi && col < K) {
-                        wq[ci][r] = ld_stream(a.w.q + (long)row * K + col);
-                        wd[ci][r] = __half2float(a.w.d[(long)row * kb + (col >> 5)]);
-                    } else {
-                        wq[ci][r] = make_uint4(0, 0, 0, 0);
-                        wd[ci][r] = 0.0f;
+                    for (int r = 0; r < R; r++) {
+                        const int row = lo + t * SR + warp * R + r;
+                        // (no dependence on act: all these loads go out together)
+                        yold[t][s][r] = (t < n_stage && s < nb && row < hi) ? a.y[(long)(slot0 + s) * a.y_stride + row]
+                                                                          : 0.0f;
+                    }
+        }
+        stage_x(xsf, nch, nb, slot0, a, red, NC);
+        if (lmhead) pen_prefilter(pl, nb, slot0, a.lm, lo, hi, NC);
+        bar_sync(1, NC);
+        const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
+        for (int t = 0; t < n_stage; t++) {
+            const int slot = t % ns;
+            if (!mbar_wait(&full[slot], (t / ns) & 1, a.err)) break;
+            const uint8_t* st = ring + slot * stage_bytes;
+            const int r0 = lo + t * SR, nr = min(SR, hi - r0);
+            float acc[NB][R];
+#pragma unroll
+            for (int s = 0; s < NB; s++)
+#pragma unroll
+                for (int r = 0; r < R; r++) acc[s][r] = 0.0f;
+            if (warp * R < nr) {
+                for (int i = 0; i < nch; i++) {
+                    const int col = i * 512 + lane * 16;
+                    uint4 wq[R];
+                    float sc[R];
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        const int rr = warp * R + r;
+                        if (col < K && rr < nr) {
+                            const uint8_t* row = st + (size_t)rr * stride;
+                            wq[r] = *reinterpret_cast<const uint4*>(row + col);
+                            sc[r] = __half2float(reinterpret_cast<const __half*>(row + K)[col >> 5]);
+                        } else {
+                            wq[r] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // q = 0
+                            sc[r] = 0.0f;
+                        }
+                    }
+#pragma unroll
+                    for (int s = 0; s < NB; s++) {
+                        if (s < nb) {
+                            uint64_t xp[8];
+                            const int base = ((s * nch + i) * 128 + lane) * 2;  // in f32 pairs
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                xp[2 * j] = xsp[base + j * 64];
+                                xp[2 * j + 1] = xsp[base + j * 64 + 1];
+                            }
+#pragma unroll
+                            for (int r = 0; r < R; r++) acc[s][r] = fmaf(dot16x2(wq[r], xp), sc[r], acc[s][r]);
+                        }
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (warp * R >= nr) continue;
 #pragma unroll
-            for (int ci = 0; ci < CH; ci++) {
-                if (i0 + ci >= nch) break;
+            for (int s = 0; s < NB; s++)
 #pragma unroll
-                for (int r = 0; r < R; r++) {
-                    float wf[16];
-                    unpack16(wq[ci][r], wf);
+                for (int r = 0; r < R; r++) acc[s][r] = warp_sum(acc[s][r]);
+            const int row0 = r0 + warp * R;
+            if (!lmhead) {
+                if (lane == 0) {
 #pragma unroll
-                    for (int s = 0; s < NB; s++)
-                        if (s < nb) acc[s][r] = fmaf(dot16(wf, xs4, (s * nch + i0 + ci) * 128, lane), wd[ci][r], acc[s][r]);
+                    for (int s = 0; s < NB; s++) {
+                        if (s >= nb) break;
+                        const int b = slot0 + s;
+                        if (!act[s]) continue;
+                        float* y = a.y + (long)b * a.y_stride;
+                        if (a.mode == MV_SWIGLU) {
+#pragma unroll
+                            for (int r = 0; r + 1 < R; r += 2)
+                                if (row0 + r + 1 < hi) {
+                                    const float gv = acc[s][r], uv = acc[s][r + 1];
+                                    y[(row0 + r) >> 1] = gv / (1.0f + expf(-gv)) * uv;
+                                }
+                        } else {
+#pragma unroll
+                            for (int r = 0; r < R; r++)
+                                if (row0 + r < hi) {
+                                    if (a.mode == MV_ADD) {
+                                        float old;
+                                        if (t < PF) {
+#pragma unroll
+                                            for (int tt = 0; tt < PF; tt++)
+                                                if (tt == t) old = yold[tt][s][r];
+                                        } else {
+                                            old = y[row0 + r];
+                                        }
+                                        y[row0 + r] = old + acc[s][r];
+                                    } else {
+                                        y[row0 + r] = acc[s][r];
+                                    }
+                                }
+                        }
+                    }
                 }
-            }
-        }
+            } else {
+                // lane s * R + r takes logit (slot s, row row0 + r)
 #pragma unroll
-        for (int s = 0; s < NB; s++)
+                for (int s = 0; s < NB; s++) {
 #pragma unroll
-            for (int r = 0; r < R; r++) acc[s][r] = warp_sum(acc[s][r]);
-        // lane (s * R + r) takes logit (s, row0 + r)
-#pragma unroll
-        for (int s = 0; s < NB; s++) {
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int row = row0 + r;
-                if (lane == s * R + r && s < nb && row < hi) {
-                    const int b = slot0 + s;
-                    float v = acc[s][r];
-                    if (a.logits && (!a.active || a.active[b])) a.logits[(long)b * N + row] = v;
-                    if (a.sample) {
-                        v = pen_apply(pl, s, b, row, v, a, N);
-                        if (row == 0) reinterpret_cast<int*>(a.part + (long)a.nb * gridDim.x * 2)[b] = (v != v);
-                        if (better(v, (uint32_t)row, bv[s], bi[s])) {
-                            bv[s] = v;
-                            bi[s] = (uint32_t)row;
+                    for (int r = 0; r < R; r++) {
+                        const int row = row0 + r;
+                        if (lane == s * R + r && s < nb && row < hi) {
+                            const int b = slot0 + s;
+                            float v = acc[s][r];
+                            if (a.y && act[s]) a.y[(long)b * N + row] = v;
+                            if (a.lm.sample) {
+                                v = pen_apply(pl, s, b, row, v, a.lm, N);
+                                if (row == 0)
+                                    reinterpret_cast<int*>(a.lm.part + (long)a.lm.nb * gridDim.x * 2)[b] = (v != v);
+                                if (better(v, (uint32_t)row, bv[s], bi[s])) {
+                                    bv[s] = v;
+                                    bi[s] = (uint32_t)row;
+                                }
+                            }
                         }
                     }
                 }
             }
         }
     }
-    pdl_trigger();
-    if (!a.sample) return;
-    // CTA reduce per slot: lanes holding slot s are s*R .. s*R+R-1; a warp argmax over all lanes per slot
+    if (!lmhead || !a.lm.sample) return;  // (uniform over the grid)
+    // ---- the LM head's choice: CTA reduce per slot, then the last CTA picks ----
+    __syncthreads();
+    if (warp < W) {
 #pragma unroll
-    for (int s = 0; s < NB; s++) {
-        float v = (lane >= s * R && lane < s * R + R) ? bv[s] : -INFINITY;
-        uint32_t i = (lane >= s * R && lane < s * R + R) ? bi[s] : NO_INDEX;
-        warp_argmax(v, i);
-        if (lane == 0) {
-            bv_w[warp][s] = v;
-            bi_w[warp][s] = i;
+        for (int s = 0; s < NB; s++) {
+            const bool mine = lane >= s * R && lane < s * R + R;
+            float v = mine ? bv[s] : -INFINITY;
+            uint32_t i = mine ? bi[s] : NO_INDEX;
+            warp_argmax(v, i);
+            if (lane == 0) {
+                bv_w[warp][s] = v;
+                bi_w[warp][s] = i;
+            }
         }
     }
     __syncthreads();
     if (threadIdx.x < NB) {
         float v = -INFINITY;
         uint32_t i = NO_INDEX;
-        for (int w = 0; w < MV_WARPS; w++)
+        for (int w = 0; w < W; w++)
             if (better(bv_w[w][threadIdx.x], bi_w[w][threadIdx.x], v, i)) {
                 v = bv_w[w][threadIdx.x];
                 i = bi_w[w][threadIdx.x];
@@ -452,56 +509,112 @@ __global__ void __launch_bounds__(MV_THREADS) k_lm_head(LmArgs a, int rows_per_c
         bi_sm[threadIdx.x] = i;
     }
     __syncthreads();
-    choice_finish(bv_sm, bi_sm, nb, slot0, a, N);
+    choice_finish(bv_sm, bi_sm, nb, slot0, a.lm, N);
 }
 
-int lm_head_grid(int num_sms) { return num_sms * 4; }
+// ---- launch geometry --------------------------------------------------------------------------------------------------
+struct Geo {
+    int W, R, rpc, grid, ns;
+    size_t smem;
+};
 
-template <int NB>
-static void launch_lm_t(cudaStream_t st, const LmArgs& a, int num_sms, bool pdl) {
-    const int nch = (a.w.cols + 511) / 512;
-    const size_t smem = (size_t)NB * nch * 512 * sizeof(float);
-    auto kern = k_lm_head<NB>;
-    static int configured = 0;
-    if (!configured) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        configured = 1;
+constexpr size_t SMEM_MAX = 220 * 1024;
+
+// streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 2 rows, a deep ring. Small matrices: about
+// two CTAs per SM, 8 consumer warps (x 2 rows for SwiGLU pairs, else 1), one or two stages each.
+static Geo geometry(const MvArgs& a, int nb_pass, int num_sms) {
+    const int N = a.w.rows, K = a.w.cols, stride = a.w.stride;
+    const int nch = (K + 511) / 512;
+    const size_t xs = (size_t)nb_pass * nch * 512 * 4;
+    Geo g;
+    const bool big = (size_t)N * stride > (size_t)48 << 20;
+    const int target = big ? num_sms : 2 * num_sms;
+    if (big) {
+        g.W = 16;
+        g.R = 2;
+    } else if (a.mode == MV_SWIGLU) {
+        g.W = 8;
+        g.R = 2;
+    } else {
+        g.W = 8;
+        g.R = 1;
     }
-    const int grid = lm_head_grid(num_sms);
-    int rpc = (a.w.rows + grid - 1) / grid;
-    rpc = (rpc + 2 * MV_WARPS - 1) / (2 * MV_WARPS) * (2 * MV_WARPS);
+    const int SR = g.W * g.R;
+    g.rpc = (N + target - 1) / target;
+    g.rpc = (g.rpc + 1) / 2 * 2;  // even: interleaved gate/up pairs never straddle CTAs
+    g.grid = (N + g.rpc - 1) / g.rpc;
+    const int n_stage = (g.rpc + SR - 1) / SR;
+    const size_t stage = (size_t)SR * stride;
+    const size_t budget = (big ? SMEM_MAX : SMEM_MAX / 2) - SM_HEAD - xs;
+    g.ns = (int)std::min<size_t>(std::min<size_t>((size_t)n_stage, MAX_NS), std::max<size_t>(1, budget / stage));
+    g.smem = SM_HEAD + xs + (size_t)g.ns * stage;
+    return g;
+}
+
+int lm_head_grid(int num_sms, int n_vocab, int dim) {
+    MvArgs a;
+    a.mode = MV_LMHEAD;
+    a.w.rows = n_vocab;
+    a.w.cols = dim;
+    a.w.stride = q8_stride(dim);
+    return geometry(a, 1, num_sms).grid;
+}
+
+template <int NB, int W, int R>
+static void launch_t(cudaStream_t st, const MvArgs& a, const Geo& g, bool pdl) {
+    auto kern = k_mv<NB, W, R>;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncAttributes fa;
+        cudaFuncGetAttributes(&fa, kern);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
+        configured = true;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid, (unsigned)((a.nb + NB - 1) / NB), 1);
-    cfg.blockDim = dim3(MV_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.gridDim = dim3((unsigned)g.grid, (unsigned)((a.nb + NB - 1) / NB), 1);
+    cfg.blockDim = dim3((W + 1) * 32, 1, 1);
+    cfg.dynamicSmemBytes = g.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, kern, a, rpc);
+    cudaLaunchKernelEx(&cfg, kern, a, g.rpc, g.ns);
 }
 
-void launch_lm_head(cudaStream_t st, const LmArgs& a, int num_sms, bool pdl) {
-    if (a.nb <= 1) launch_lm_t<1>(st, a, num_sms, pdl);
-    else if (a.nb <= 2) launch_lm_t<2>(st, a, num_sms, pdl);
-    else if (a.nb <= 4) launch_lm_t<4>(st, a, num_sms, pdl);
-    else launch_lm_t<8>(st, a, num_sms, pdl);
+template <int NB>
+static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
+    const Geo g = geometry(a, NB, num_sms);
+    if (g.W == 16) launch_t<NB, 16, 2>(st, a, g, pdl);
+    else if (g.R == 2) launch_t<NB, 8, 2>(st, a, g, pdl);
+    else launch_t<NB, 8, 1>(st, a, g, pdl);
 }
 
-// ---- the choice alone, over logits in memory ------------------------------------------------------------------------
-__global__ void __launch_bounds__(MV_THREADS) k_sample(const float* __restrict__ logits, int stride, int n_vocab,
-                                                         LmArgs a, int per_cta, int slot_base) {
+void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
+    // slots per pass: 1, 2, 4 or 8 (more slots → one pass over the weights per blockIdx.y)
+    if (a.nb <= 1) launch_nb<1>(st, a, num_sms, pdl);
+    else if (a.nb <= 2) launch_nb<2>(st, a, num_sms, pdl);
+    else if (a.nb <= 4) launch_nb<4>(st, a, num_sms, pdl);
+    else launch_nb<8>(st, a, num_sms, pdl);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// the choice alone, over logits in memory; the penalty alone
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int SAMPLE_THREADS = 256;
+
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float* __restrict__ logits, int stride, int n_vocab,
+                                                             LmArgs a, int per_cta, int slot_base) {
     __shared__ PenList pl;
-    __shared__ float bv_w[MV_WARPS];
-    __shared__ uint32_t bi_w[MV_WARPS];
+    __shared__ float bv_w[SAMPLE_THREADS / 32];
+    __shared__ uint32_t bi_w[SAMPLE_THREADS / 32];
     __shared__ float bv_sm[1];
     __shared__ uint32_t bi_sm[1];
     const int b = slot_base + blockIdx.y;  // one slot per grid row
     const int lo = blockIdx.x * per_cta, hi = min(n_vocab, lo + per_cta);
     pdl_wait();
-    pen_prefilter(pl, 1, b, a, lo, hi);
+    pen_prefilter(pl, 1, b, a, lo, hi, SAMPLE_THREADS);
     float bv = -INFINITY;
     uint32_t bi = NO_INDEX;
     const float* l = logits + (long)b * stride;
@@ -523,7 +636,7 @@ __global__ void __launch_bounds__(MV_THREADS) k_sample(const float* __restrict__
     if (threadIdx.x == 0) {
         float v = -INFINITY;
         uint32_t i = NO_INDEX;
-        for (int w = 0; w < MV_WARPS; w++)
+        for (int w = 0; w < SAMPLE_THREADS / 32; w++)
             if (better(bv_w[w], bi_w[w], v, i)) {
                 v = bv_w[w];
                 i = bi_w[w];
@@ -537,25 +650,25 @@ __global__ void __launch_bounds__(MV_THREADS) k_sample(const float* __restrict__
 
 int sample_grid(int num_sms) { return num_sms; }
 
-// the penalty alone, in place (choose_pen.wgsl's job): the same prefilter + pen_apply the fused choice uses
-__global__ void __launch_bounds__(MV_THREADS) k_penalize(float* __restrict__ logits, int n_vocab, LmArgs a, int per_cta) {
+void launch_sample(cudaStream_t st, const float* logits, int logits_stride, int n_vocab, const LmArgs& a,
+                   int num_sms, int slot_base, int n_slots) {
+    const int grid = sample_grid(num_sms);
+    const int per = (n_vocab + grid - 1) / grid;
+    k_sample<<<dim3(grid, n_slots, 1), SAMPLE_THREADS, 0, st>>>(logits, logits_stride, n_vocab, a, per, slot_base);
+}
+
+__global__ void __launch_bounds__(SAMPLE_THREADS) k_penalize(float* __restrict__ logits, int n_vocab, LmArgs a,
+                                                               int per_cta) {
     __shared__ PenList pl;
     const int lo = blockIdx.x * per_cta, hi = min(n_vocab, lo + per_cta);
-    pen_prefilter(pl, 1, 0, a, lo, hi);
+    pen_prefilter(pl, 1, 0, a, lo, hi, SAMPLE_THREADS);
     for (int t = lo + threadIdx.x; t < hi; t += blockDim.x) logits[t] = pen_apply(pl, 0, 0, t, logits[t], a, n_vocab);
 }
 
 void launch_penalize(cudaStream_t st, float* logits, int n_vocab, const LmArgs& a, int num_sms) {
     const int grid = sample_grid(num_sms);
     const int per = (n_vocab + grid - 1) / grid;
-    k_penalize<<<grid, MV_THREADS, 0, st>>>(logits, n_vocab, a, per);
-}
-
-void launch_sample(cudaStream_t st, const float* logits, int logits_stride, int n_vocab, const LmArgs& a,
-                   int num_sms, int slot_base, int n_slots) {
-    const int grid = sample_grid(num_sms);
-    const int per = (n_vocab + grid - 1) / grid;
-    k_sample<<<dim3(grid, n_slots, 1), MV_THREADS, 0, st>>>(logits, logits_stride, n_vocab, a, per, slot_base);
+    k_penalize<<<grid, SAMPLE_THREADS, 0, st>>>(logits, n_vocab, a, per);
 }
 
 }  // namespace ocr

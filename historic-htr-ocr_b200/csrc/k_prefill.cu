@@ -14,8 +14,10 @@ __global__ void k_embed_rows(const int32_t* __restrict__ ids, int n, QMat emb, f
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int r = (int)(i / dim), c = (int)(i % dim);
         const int t = ids[r];
-        if (t >= 0 && t < emb.rows)
-            x[i] = (float)emb.q[(long)t * dim + c] * __half2float(emb.d[(long)t * (dim / 32) + c / 32]);
+        if (t >= 0 && t < emb.rows) {
+            const uint8_t* row = emb.w + (long)t * emb.stride;
+            x[i] = (float)(int8_t)row[c] * __half2float(reinterpret_cast<const __half*>(row + dim)[c / 32]);
+        }
     }
 }
 
@@ -61,7 +63,6 @@ __global__ void __launch_bounds__(256) k_gemm_q8_0(const float* __restrict__ X, 
     for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-    const int kb = K / 32;
     for (int k0 = 0; k0 < K; k0 += GK) {
         // X tile: 128 rows x 32 floats = 1024 float4, 4 per thread
 #pragma unroll
@@ -80,8 +81,9 @@ __global__ void __launch_bounds__(256) k_gemm_q8_0(const float* __restrict__ X, 
             const int r = tid >> 1, h = tid & 1;
             float wf[16];
             if (n0 + r < N) {
-                const uint4 q = *reinterpret_cast<const uint4*>(W.q + (long)(n0 + r) * K + k0 + h * 16);
-                const float d = __half2float(W.d[(long)(n0 + r) * kb + k0 / 32]);
+                const uint8_t* row = W.w + (long)(n0 + r) * W.stride;
+                const uint4 q = *reinterpret_cast<const uint4*>(row + k0 + h * 16);
+                const float d = __half2float(reinterpret_cast<const __half*>(row + K)[k0 / 32]);
                 i8x4_to_f32(q.x, wf + 0);
                 i8x4_to_f32(q.y, wf + 4);
                 i8x4_to_f32(q.z, wf + 8);

@@ -1,5 +1,6 @@
 // k_weights.cu — q8_0 device layout: repack from GGUF blocks, the seeded synthetic generator, unpack for export.
 //
+// Row layout (kernels.cuh): int8 quants [cols] | f16 scales [cols/32] | pad, stride q8_stride(cols).
 // The synthetic generator's arithmetic is integer-only up to one f32 multiply, an IEEE division and the f16 RNE
 // store, each written with the _rn intrinsics so no contraction changes a rounding: the host test generator of the
 // same seed gives the same bits.
@@ -8,39 +9,38 @@
 namespace ocr {
 
 // ---- the GGUF q8_0 block (ocr-gguf/src/lib.rs:129-135): f16 d (little endian) + 32 x int8 ---------------------------
-__global__ void k_repack_q8_0(const uint8_t* __restrict__ blocks, int rows, int cols, int8_t* __restrict__ q,
-                              __half* __restrict__ d, int row_mul, int row_add) {
-    const int nbr = cols / 32;
+__global__ void k_repack_q8_0(const uint8_t* __restrict__ blocks, int rows, int cols, uint8_t* __restrict__ w,
+                              int row_mul, int row_add) {
+    const int nbr = cols / 32, stride = q8_stride(cols);
     const long nblk = (long)rows * nbr;
     for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
         const int r = (int)(b / nbr), c = (int)(b % nbr);
         const uint8_t* src = blocks + b * 34;
         // 34-byte blocks start on 2-byte boundaries: read 17 half-words
         const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
-        uint32_t w[8];
+        uint32_t v[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) w[k] = (uint32_t)s16[1 + 2 * k] | ((uint32_t)s16[2 + 2 * k] << 16);
-        const long dr = (long)r * row_mul + row_add;
-        uint4* dst = reinterpret_cast<uint4*>(q + dr * cols + c * 32);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        d[dr * nbr + c] = __ushort_as_half(s16[0]);
+        for (int k = 0; k < 8; k++) v[k] = (uint32_t)s16[1 + 2 * k] | ((uint32_t)s16[2 + 2 * k] << 16);
+        uint8_t* row = w + ((long)r * row_mul + row_add) * stride;
+        uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
+        dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_uint4(v[4], v[5], v[6], v[7]);
+        reinterpret_cast<uint16_t*>(row + cols)[c] = s16[0];
     }
 }
 
-__global__ void k_unpack_q8_0(const int8_t* __restrict__ q, const __half* __restrict__ d, int rows, int cols,
-                              int row_mul, int row_add, uint8_t* __restrict__ blocks) {
-    const int nbr = cols / 32;
+__global__ void k_unpack_q8_0(const uint8_t* __restrict__ w, int rows, int cols, int row_mul, int row_add,
+                              uint8_t* __restrict__ blocks) {
+    const int nbr = cols / 32, stride = q8_stride(cols);
     const long nblk = (long)rows * nbr;
     for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
         const int r = (int)(b / nbr), c = (int)(b % nbr);
-        const long sr = (long)r * row_mul + row_add;
+        const uint8_t* row = w + ((long)r * row_mul + row_add) * stride;
         uint8_t* dst = blocks + b * 34;
-        const uint16_t h = __half_as_ushort(d[sr * nbr + c]);
+        const uint16_t h = reinterpret_cast<const uint16_t*>(row + cols)[c];
         dst[0] = (uint8_t)(h & 0xff);
         dst[1] = (uint8_t)(h >> 8);
-        const int8_t* src = q + sr * cols + c * 32;
-        for (int k = 0; k < 32; k++) dst[2 + k] = (uint8_t)src[k];
+        for (int k = 0; k < 32; k++) dst[2 + k] = row[c * 32 + k];
     }
 }
 
@@ -71,9 +71,9 @@ __device__ __forceinline__ int8_t sat_i8(float v) {
 }
 
 // one q8_0 block of generated values, quantized as ggml's quantize_row_q8_0_ref (text.rs:676-691)
-__global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, int8_t* __restrict__ q,
-                             __half* __restrict__ d, int row_mul, int row_add) {
-    const int nbr = cols / 32;
+__global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, uint8_t* __restrict__ w, int row_mul,
+                             int row_add) {
+    const int nbr = cols / 32, stride = q8_stride(cols);
     const long nblk = (long)rows * nbr;
     for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
         float x[32];
@@ -87,19 +87,19 @@ __global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, int
         const float dv = __fdiv_rn(amax, 127.0f);
         const float id = dv != 0.0f ? __fdiv_rn(1.0f, dv) : 0.0f;
         const int r = (int)(b / nbr), c = (int)(b % nbr);
-        const long dr = (long)r * row_mul + row_add;
-        uint32_t w[8];
+        uint8_t* row = w + ((long)r * row_mul + row_add) * stride;
+        uint32_t v[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            uint32_t v = 0;
+            uint32_t u = 0;
 #pragma unroll
-            for (int m = 0; m < 4; m++) v |= ((uint32_t)(uint8_t)sat_i8(roundf(__fmul_rn(x[4 * k + m], id)))) << (8 * m);
-            w[k] = v;
+            for (int m = 0; m < 4; m++) u |= ((uint32_t)(uint8_t)sat_i8(roundf(__fmul_rn(x[4 * k + m], id)))) << (8 * m);
+            v[k] = u;
         }
-        uint4* dst = reinterpret_cast<uint4*>(q + dr * cols + c * 32);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        d[dr * nbr + c] = __float2half_rn(dv);
+        uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
+        dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_uint4(v[4], v[5], v[6], v[7]);
+        reinterpret_cast<__half*>(row + cols)[c] = __float2half_rn(dv);
     }
 }
 
@@ -116,22 +116,22 @@ static int grid_for(long n, int threads) {
     return (int)(g < 1 ? 1 : (g > 65535 * 8 ? 65535 * 8 : g));
 }
 
-void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, int8_t* q, __half* d, int row_mul,
+void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, uint8_t* w, int row_mul,
                         int row_add) {
     const long n = (long)rows * (cols / 32);
-    k_repack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(blocks, rows, cols, q, d, row_mul, row_add);
+    k_repack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(blocks, rows, cols, w, row_mul, row_add);
 }
 
-void launch_unpack_q8_0(cudaStream_t st, const int8_t* q, const __half* d, int rows, int cols, int row_mul,
-                        int row_add, uint8_t* blocks) {
+void launch_unpack_q8_0(cudaStream_t st, const uint8_t* w, int rows, int cols, int row_mul, int row_add,
+                        uint8_t* blocks) {
     const long n = (long)rows * (cols / 32);
-    k_unpack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(q, d, rows, cols, row_mul, row_add, blocks);
+    k_unpack_q8_0<<<grid_for(n, 256), 256, 0, st>>>(w, rows, cols, row_mul, row_add, blocks);
 }
 
-void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, int8_t* q, __half* d,
-                       int row_mul, int row_add) {
+void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, uint8_t* w, int row_mul,
+                       int row_add) {
     const long n = (long)rows * (cols / 32);
-    k_synth_q8_0<<<grid_for(n, 128), 128, 0, st>>>(seed, sigma, rows, cols, q, d, row_mul, row_add);
+    k_synth_q8_0<<<grid_for(n, 128), 128, 0, st>>>(seed, sigma, rows, cols, w, row_mul, row_add);
 }
 
 void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out) {

@@ -1,66 +1,38 @@
-// kernels.cuh — parameter blocks and launchers of the device kernels (one translation unit each, sm_100a).
+// kernels.cuh — parameter blocks and launchers of the device kernels (sm_100a).
 //
 // Device layout of a q8_0 matrix [rows][cols] (cols % 32 == 0), repacked at load from GGUF's 34-byte blocks:
-//   quants  int8 [rows][cols]      row-major, rows 16-B aligned (cols % 16 == 0): a warp's 16-B lane loads of one
-//                                  512-column chunk are one contiguous, fully coalesced 512-B transaction
-//   scales  f16  [rows][cols / 32] the block scale d of columns [32 b, 32 b + 32)
-// value(r, c) = quants[r][c] * f32(scales[r][c / 32]) — the same q and d bits as the GGUF block.
+//   row r at w + r * stride:  int8 quants [cols] | f16 scales [cols / 32] | zero pad to a 16-B multiple
+//   stride = round_up(cols + cols / 16, 16)
+// value(r, c) = quants[c] * f32(scales[c / 32]) — the same q and d bits as the GGUF blocks. Any run of rows is one
+// contiguous, 16-B aligned, 16-B multiple byte range: one bulk-async copy (cp.async.bulk) moves a stage of rows.
 #pragma once
 
 #include "common.cuh"
 
 namespace ocr {
 
+__host__ __device__ constexpr int q8_stride(int cols) { return (cols + cols / 16 + 15) / 16 * 16; }
+
 struct QMat {
-    const int8_t* q = nullptr;
-    const __half* d = nullptr;
-    int rows = 0, cols = 0;
+    const uint8_t* w = nullptr;
+    int rows = 0, cols = 0, stride = 0;
 };
 
 // ---- weights: repack / synthetic generation (k_weights.cu) ---------------------------------------------------------
-// GGUF blocks [rows][cols/32] x 34 B → quants/scales at destination row r * row_mul + row_add
-void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, int8_t* q, __half* d, int row_mul,
+// GGUF blocks [rows][cols/32] x 34 B → the row layout at destination row r * row_mul + row_add
+void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, uint8_t* w, int row_mul,
                         int row_add);
 // the synthetic generator (bit-identical to the oracle's orc_synth_q8_0 / orc_fill_norm)
-void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, int8_t* q, __half* d,
-                       int row_mul, int row_add);
+void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, uint8_t* w, int row_mul,
+                       int row_add);
 void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out);
 // back to GGUF blocks (ocr_model_tensor_gguf): source rows r * row_mul + row_add
-void launch_unpack_q8_0(cudaStream_t st, const int8_t* q, const __half* d, int rows, int cols, int row_mul,
-                        int row_add, uint8_t* blocks);
+void launch_unpack_q8_0(cudaStream_t st, const uint8_t* w, int rows, int cols, int row_mul, int row_add,
+                        uint8_t* blocks);
 
-// ---- matvec family (k_matvec.cu) -----------------------------------------------------------------------------------
-enum MvMode : int { MV_STORE = 0, MV_ADD = 1, MV_SWIGLU = 2 };
-
-struct MvArgs {
-    QMat w;
-    const float* x = nullptr;  // [B][x_stride] input rows
-    int x_stride = 0;
-    const float* nw = nullptr;  // RMSNorm weights (null = no norm)
-    float eps = 1e-6f;
-    // layer-0 embedding: x = token_embd[tok[b]] (dequantized), written to x_out by the grid's first column of CTAs
-    const int32_t* tok = nullptr;
-    QMat emb;
-    float* x_out = nullptr;
-    float* y = nullptr;  // [B][y_stride]
-    int y_stride = 0;
-    int mode = MV_STORE;
-    int nb = 1;  // slots
-    const int32_t* active = nullptr;  // [B] (null = all); an idle slot's rows are not written
-};
-void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl);
-
-// the LM head + greedy choice (dmv_norm → choose_pen → choose_max → choose_pick, fused)
+// ---- the token choice's arguments (shared by the LM head, the standalone choice and the penalty) ------------------
 struct LmArgs {
-    QMat w;  // tied token_embd [n_vocab][dim]
-    const float* x = nullptr;
-    int x_stride = 0;
-    const float* nw = nullptr;
-    float eps = 1e-6f;
-    int nb = 1;
-    float* logits = nullptr;  // [B][n_vocab] raw logits (null = not stored)
-    // the choice (sample = 0: logits only)
-    int sample = 0;
+    int sample = 0;  // 0: logits only
     float rp = 1.0f;
     int window = 1;
     int use_fp = 0;
@@ -74,12 +46,36 @@ struct LmArgs {
     uint32_t* counts = nullptr;  // [B][n_vocab] (use_fp)
     float* fpen = nullptr;       // [B][n_vocab]
     const int32_t* active = nullptr;
-    float* part = nullptr;       // scratch: [B][grid][2] + nan flags
-    uint32_t* done = nullptr;    // scratch counter (self-resetting)
+    float* part = nullptr;       // scratch: [B][grid][2] + [B] NaN-at-token-0 flags
+    uint32_t* done = nullptr;    // scratch counters (self-resetting)
+    int nb = 1;                  // slots in the partials' layout
     int* err = nullptr;
 };
-void launch_lm_head(cudaStream_t st, const LmArgs& a, int num_sms, bool pdl);
-int lm_head_grid(int num_sms);
+
+// ---- the streamed matvec family (k_matvec.cu) -----------------------------------------------------------------------
+enum MvMode : int { MV_STORE = 0, MV_ADD = 1, MV_SWIGLU = 2, MV_LMHEAD = 3 };
+
+struct MvArgs {
+    QMat w;
+    const float* x = nullptr;  // [B][x_stride] input rows
+    int x_stride = 0;
+    const float* nw = nullptr;  // RMSNorm weights (null = no norm)
+    float eps = 1e-6f;
+    // layer-0 embedding: x = token_embd[tok[b]] (dequantized), written to x_out by the grid's first CTA
+    const int32_t* tok = nullptr;
+    QMat emb;
+    float* x_out = nullptr;
+    float* y = nullptr;  // [B][y_stride] (LM head: raw logits [B][n_vocab], may be null)
+    int y_stride = 0;
+    int mode = MV_STORE;
+    int nb = 1;  // slots
+    const int32_t* active = nullptr;  // [B] (null = all); an idle slot's rows are not written
+    LmArgs lm;   // MV_LMHEAD: the choice
+    int* err = nullptr;
+};
+void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl);
+// grid of the LM head (the partials' layout) for n_vocab rows
+int lm_head_grid(int num_sms, int n_vocab, int dim);
 
 // the choice alone over logits on the device (choice 0 from the prompt's logits; ocr_sample_logits)
 // slots [slot_base, slot_base + n_slots) of logits [B][logits_stride]; a.nb = B (the partials' layout)
@@ -111,7 +107,6 @@ struct AttnArgs {
 };
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx);
-size_t attention_smem(const AttnArgs& a);
 
 // ---- prefill (k_prefill.cu) -------------------------------------------------------------------------------------------
 void launch_embed_rows(cudaStream_t st, const int32_t* ids, int n, QMat emb, float* x);

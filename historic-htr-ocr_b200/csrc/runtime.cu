@@ -128,7 +128,7 @@ struct Planner {
 // offsets of every tensor in the model's one allocation
 struct Layout {
     struct MatOff {
-        size_t q, d;
+        size_t off;
         int rows, cols;
     };
     struct LayerOff {
@@ -148,8 +148,7 @@ Layout plan(const ocr_text_cfg& c) {
         Layout::MatOff m;
         m.rows = rows;
         m.cols = cols;
-        m.q = p.take((size_t)rows * cols);
-        m.d = p.take((size_t)rows * (cols / 32) * 2);
+        m.off = p.take((size_t)rows * q8_stride(cols));
         return m;
     };
     for (int l = 0; l < c.n_layer; l++) {
@@ -172,10 +171,10 @@ Layout plan(const ocr_text_cfg& c) {
 
 QMat qmat(void* base, const Layout::MatOff& m) {
     QMat q;
-    q.q = (const int8_t*)((char*)base + m.q);
-    q.d = (const __half*)((char*)base + m.d);
+    q.w = (const uint8_t*)base + m.off;
     q.rows = m.rows;
     q.cols = m.cols;
+    q.stride = q8_stride(m.cols);
     return q;
 }
 
@@ -294,8 +293,8 @@ ocr_status upload_tensor(ocr_model* m, const Gguf& g, const GTensor& t, const Wh
         const size_t n = (size_t)nr * row_bytes;
         if (!g.src->read_at(t.file_offset + (uint64_t)r0 * row_bytes, ctx->h_stage, n, msg)) return fail(OCR_ERR_IO, msg);
         OCR_CUDA(cudaMemcpyAsync(ctx->d_stage, ctx->h_stage, n, cudaMemcpyHostToDevice, ctx->stream));
-        launch_repack_q8_0(ctx->stream, (const uint8_t*)ctx->d_stage, nr, cols, const_cast<int8_t*>(w.mat.q),
-                           const_cast<__half*>(w.mat.d), w.row_mul, r0 * w.row_mul + w.row_add);
+        launch_repack_q8_0(ctx->stream, (const uint8_t*)ctx->d_stage, nr, cols, const_cast<uint8_t*>(w.mat.w),
+                           w.row_mul, r0 * w.row_mul + w.row_add);
         OCR_CUDA(cudaGetLastError());
         OCR_CUDA(cudaStreamSynchronize(ctx->stream));
     }
@@ -548,32 +547,36 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         dn.active = s->active;
         launch_matvec(st, dn, ctx->num_sms, pdl);
     }
-    LmArgs lm;
+    MvArgs lm;
     lm.w = m->tok;
     lm.x = s->x;
     lm.x_stride = c.dim;
     lm.nw = m->out_norm;
     lm.eps = c.eps;
     lm.nb = s->B;
-    lm.logits = s->logits;
-    lm.sample = sample ? 1 : 0;
-    lm.rp = rp;
-    lm.window = window;
-    lm.use_fp = use_fp;
-    lm.fp = fp;
-    lm.hist = s->hist;
-    lm.hist_cap = s->hist_cap;
-    lm.len = s->len;
-    lm.tok = s->tok;
-    lm.pos = s->pos;
-    lm.advance_pos = sample ? 1 : 0;
-    lm.counts = s->counts;
-    lm.fpen = s->fpen;
+    lm.mode = MV_LMHEAD;
+    lm.y = s->logits;
     lm.active = s->active;
-    lm.part = s->lm_part;
-    lm.done = s->lm_done;
     lm.err = ctx->d_err;
-    launch_lm_head(st, lm, ctx->num_sms, pdl);
+    lm.lm.sample = sample ? 1 : 0;
+    lm.lm.rp = rp;
+    lm.lm.window = window;
+    lm.lm.use_fp = use_fp;
+    lm.lm.fp = fp;
+    lm.lm.hist = s->hist;
+    lm.lm.hist_cap = s->hist_cap;
+    lm.lm.len = s->len;
+    lm.lm.tok = s->tok;
+    lm.lm.pos = s->pos;
+    lm.lm.advance_pos = sample ? 1 : 0;
+    lm.lm.counts = s->counts;
+    lm.lm.fpen = s->fpen;
+    lm.lm.active = s->active;
+    lm.lm.part = s->lm_part;
+    lm.lm.done = s->lm_done;
+    lm.lm.nb = s->B;
+    lm.lm.err = ctx->d_err;
+    launch_matvec(st, lm, ctx->num_sms, pdl);
 }
 
 // rope_table (text.rs:132-142): theta = (f32)pos * base^(-2i/d) in f32, (cos, sin) by the host libm
@@ -896,11 +899,10 @@ ocr_status ocr_model_synthetic(ocr_ctx* ctx, const ocr_text_cfg* cfg, uint64_t s
             const uint64_t ss = sub((uint64_t)l * 16 + k);
             if (w.is_norm) launch_synth_norm(st, ss, w.n, w.norm);
             else
-                launch_synth_q8_0(st, ss, sigma_w, w.rows, w.mat.cols, const_cast<int8_t*>(w.mat.q),
-                                  const_cast<__half*>(w.mat.d), w.row_mul, w.row_add);
+                launch_synth_q8_0(st, ss, sigma_w, w.rows, w.mat.cols, const_cast<uint8_t*>(w.mat.w), w.row_mul,
+                                  w.row_add);
         }
-    launch_synth_q8_0(st, sub(100000), sigma_e, cfg->n_vocab, cfg->dim, const_cast<int8_t*>(m->tok.q),
-                      const_cast<__half*>(m->tok.d), 1, 0);
+    launch_synth_q8_0(st, sub(100000), sigma_e, cfg->n_vocab, cfg->dim, const_cast<uint8_t*>(m->tok.w), 1, 0);
     launch_synth_norm(st, sub(100001), cfg->dim, m->out_norm);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
@@ -935,7 +937,7 @@ ocr_status ocr_model_tensor_gguf(const ocr_model* m, int layer, int kind, void* 
     } else {
         void* d = nullptr;
         OCR_CUDA(cudaMalloc(&d, need));
-        launch_unpack_q8_0(ctx->stream, w.mat.q, w.mat.d, w.rows, w.mat.cols, w.row_mul, w.row_add, (uint8_t*)d);
+        launch_unpack_q8_0(ctx->stream, w.mat.w, w.rows, w.mat.cols, w.row_mul, w.row_add, (uint8_t*)d);
         cudaError_t e = cudaStreamSynchronize(ctx->stream);
         if (e == cudaSuccess) e = cudaMemcpy(out, d, need, cudaMemcpyDeviceToHost);
         cudaFree(d);
@@ -971,6 +973,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const auto& c = m->cfg;
     if (n_ctx < 1 || batch < 1) return fail(OCR_ERR_ARG, "n_ctx and batch must be >= 1");
     if (n_ctx > c.n_ctx_train) return fail(OCR_ERR_ARG, std::to_string(n_ctx) + " positions asked, the model was trained on " + std::to_string(c.n_ctx_train));
+    if (n_ctx > 256 * 192) return fail(OCR_ERR_ARG, "n_ctx above 49152: the decode attention splits a context into at most 256 ranges of 192 keys");
     ocr_ctx* ctx = m->ctx;
     OCR_CUDA(cudaSetDevice(ctx->device));
     auto* s = new ocr_session;
@@ -987,7 +990,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     cudaError_t e = dalloc((void**)&s->kc, s->kv_bytes, &ctx->mem_kv);
     if (e == cudaSuccess) e = dalloc((void**)&s->vc, s->kv_bytes, &ctx->mem_kv);
     // work: rope, x, qkv, attn, g, logits, partials, counters, state
-    const int lm_grid = std::max(lm_head_grid(ctx->num_sms), sample_grid(ctx->num_sms));
+    const int lm_grid = std::max(lm_head_grid(ctx->num_sms, c.n_vocab, c.dim), sample_grid(ctx->num_sms));
     Planner p;
     const size_t o_rope = p.take((size_t)n_ctx * c.d_head * 4);
     const size_t o_x = p.take((size_t)batch * c.dim * 4);
@@ -1116,17 +1119,17 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
         launch_gemm_q8_0(st, h, n, L.gu, g, 0, 1);
         launch_gemm_q8_0(st, g, n, L.down, x, 1, 0);
     }
-    LmArgs lm;
+    MvArgs lm;
     lm.w = s->m->tok;
     lm.x = x + (size_t)(n - 1) * c.dim;
     lm.x_stride = c.dim;
     lm.nw = s->m->out_norm;
     lm.eps = c.eps;
     lm.nb = 1;
-    lm.logits = s->logits + (size_t)slot * c.n_vocab;
-    lm.part = s->lm_part;
-    lm.done = s->lm_done;
-    launch_lm_head(st, lm, ctx->num_sms, false);
+    lm.mode = MV_LMHEAD;
+    lm.y = s->logits + (size_t)slot * c.n_vocab;
+    lm.err = ctx->d_err;
+    launch_matvec(st, lm, ctx->num_sms, false);
     OCR_CUDA(cudaGetLastError());
     if (logits_out)
         OCR_CUDA(cudaMemcpyAsync(logits_out, s->logits + (size_t)slot * c.n_vocab, (size_t)c.n_vocab * 4, cudaMemcpyDeviceToHost, st));
@@ -1248,30 +1251,32 @@ ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, c
     return OCR_OK;
 }
 
-ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, int8_t* d_quants,
-                              uint16_t* d_scales) {
-    if (!ctx || !d_blocks || !d_quants || !d_scales) return fail(OCR_ERR_ARG, "null argument");
+int ocr_q8_row_bytes(int cols) { return cols > 0 && cols % 32 == 0 ? q8_stride(cols) : 0; }
+
+ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, uint8_t* d_rows) {
+    if (!ctx || !d_blocks || !d_rows) return fail(OCR_ERR_ARG, "null argument");
     if (rows < 1 || cols < 32 || cols % 32) return fail(OCR_ERR_ARG, "rows >= 1, cols a positive multiple of 32");
-    if (((uintptr_t)d_blocks & 1) || ((uintptr_t)d_quants & 15) || ((uintptr_t)d_scales & 1))
-        return fail(OCR_ERR_ARG, "alignment: blocks 2 B, quants 16 B, scales 2 B");
+    if (((uintptr_t)d_blocks & 1) || ((uintptr_t)d_rows & 15))
+        return fail(OCR_ERR_ARG, "alignment: blocks 2 B, rows 16 B");
     OCR_CUDA(cudaSetDevice(ctx->device));
-    launch_repack_q8_0(ctx->stream, (const uint8_t*)d_blocks, rows, cols, d_quants, (__half*)d_scales, 1, 0);
+    launch_repack_q8_0(ctx->stream, (const uint8_t*)d_blocks, rows, cols, d_rows, 1, 0);
     OCR_CUDA(cudaGetLastError());
     return OCR_OK;
 }
 
-ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int rows, int cols,
-                              const float* d_x, const float* d_norm_w, float eps, int nb, float* d_y, int accumulate) {
-    if (!ctx || !d_quants || !d_scales || !d_x || !d_y) return fail(OCR_ERR_ARG, "null argument");
+ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int cols, const float* d_x,
+                              const float* d_norm_w, float eps, int nb, float* d_y, int accumulate) {
+    if (!ctx || !d_w || !d_x || !d_y) return fail(OCR_ERR_ARG, "null argument");
     if (rows < 1 || cols < 32 || cols % 32 || nb < 1) return fail(OCR_ERR_ARG, "bad shape");
-    if ((uintptr_t)d_quants & 15) return fail(OCR_ERR_ARG, "quants must be 16-B aligned");
-    if ((size_t)nb * cols * 4 > 96 * 1024 * 8) return fail(OCR_ERR_ARG, "nb x cols too large for the staged activations");
+    if ((uintptr_t)d_w & 15) return fail(OCR_ERR_ARG, "the rows must start 16-B aligned");
+    if ((size_t)((cols + 511) / 512) * 512 * 4 * std::min(nb, 8) > 96 * 1024)
+        return fail(OCR_ERR_ARG, "nb x cols too large for the staged activations");
     OCR_CUDA(cudaSetDevice(ctx->device));
     MvArgs a;
-    a.w.q = d_quants;
-    a.w.d = (const __half*)d_scales;
+    a.w.w = d_w;
     a.w.rows = rows;
     a.w.cols = cols;
+    a.w.stride = q8_stride(cols);
     a.x = d_x;
     a.x_stride = cols;
     a.nw = d_norm_w;
@@ -1280,46 +1285,51 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const int8_t* d_quants, const uint16
     a.y_stride = rows;
     a.mode = accumulate ? MV_ADD : MV_STORE;
     a.nb = nb;
+    a.err = ctx->d_err;
     launch_matvec(ctx->stream, a, ctx->num_sms, false);
     OCR_CUDA(cudaGetLastError());
     return OCR_OK;
 }
 
-ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int n_vocab, int dim,
-                                 const float* d_x, const float* d_norm_w, float eps, float rp, int window,
-                                 int32_t* d_hist, int32_t* d_len, int32_t* d_tok, float* d_logits) {
-    if (!ctx || !d_quants || !d_scales || !d_x || !d_hist || !d_len || !d_tok) return fail(OCR_ERR_ARG, "null argument");
+ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const uint8_t* d_w, int n_vocab, int dim, const float* d_x,
+                                 const float* d_norm_w, float eps, float rp, int window, int32_t* d_hist,
+                                 int32_t* d_len, int32_t* d_tok, float* d_logits) {
+    if (!ctx || !d_w || !d_x || !d_hist || !d_len || !d_tok) return fail(OCR_ERR_ARG, "null argument");
     if (n_vocab < 1 || dim < 32 || dim % 32) return fail(OCR_ERR_ARG, "bad shape");
+    if ((uintptr_t)d_w & 15) return fail(OCR_ERR_ARG, "the rows must start 16-B aligned");
     if (rp != 1.0f && !(std::isnormal(rp) && rp > 0.0f)) return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
     if (window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
     OCR_CUDA(cudaSetDevice(ctx->device));
-    const int grid = lm_head_grid(ctx->num_sms);
+    const int grid = lm_head_grid(ctx->num_sms, n_vocab, dim);
     const size_t o_done = ((size_t)grid * 2 + 1) * 4 + 256;
     OCR_TRY(ensure_op_scratch(ctx, o_done + 256));
     char* w = (char*)ctx->op_scratch;
-    LmArgs a;
-    a.w.q = d_quants;
-    a.w.d = (const __half*)d_scales;
+    MvArgs a;
+    a.w.w = d_w;
     a.w.rows = n_vocab;
     a.w.cols = dim;
+    a.w.stride = q8_stride(dim);
     a.x = d_x;
     a.x_stride = dim;
     a.nw = d_norm_w;
     a.eps = eps;
     a.nb = 1;
-    a.logits = d_logits;
-    a.sample = 1;
-    a.rp = rp;
-    a.window = window;
-    a.hist = d_hist;
-    a.hist_cap = 1 << 30;
-    a.len = d_len;
-    a.tok = d_tok;
-    a.part = (float*)w;
-    a.done = (uint32_t*)(w + o_done);
+    a.mode = MV_LMHEAD;
+    a.y = d_logits;
     a.err = ctx->d_err;
-    OCR_CUDA(cudaMemsetAsync(a.done, 0, 4, ctx->stream));
-    launch_lm_head(ctx->stream, a, ctx->num_sms, false);
+    a.lm.sample = 1;
+    a.lm.rp = rp;
+    a.lm.window = window;
+    a.lm.hist = d_hist;
+    a.lm.hist_cap = 1 << 30;
+    a.lm.len = d_len;
+    a.lm.tok = d_tok;
+    a.lm.part = (float*)w;
+    a.lm.done = (uint32_t*)(w + o_done);
+    a.lm.nb = 1;
+    a.lm.err = ctx->d_err;
+    OCR_CUDA(cudaMemsetAsync(a.lm.done, 0, 4, ctx->stream));
+    launch_matvec(ctx->stream, a, ctx->num_sms, false);
     OCR_CUDA(cudaGetLastError());
     return OCR_OK;
 }

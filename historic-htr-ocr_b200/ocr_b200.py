@@ -85,10 +85,11 @@ _SIGS = {
     "ocr_gguf_to_f32": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
     "ocr_gguf_text_config": (C.c_int, [_P, C.POINTER(TextCfg)]),
     "ocr_op_penalize": (C.c_int, [_P, _P, C.c_int, C.c_float, C.c_int, _P, C.c_int]),
-    "ocr_op_repack_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P]),
-    "ocr_op_matvec_q8_0": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_int, _P, C.c_int]),
-    "ocr_op_lm_head_sample": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P, _P,
-                                        _P, _P]),
+    "ocr_q8_row_bytes": (C.c_int, [C.c_int]),
+    "ocr_op_repack_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P]),
+    "ocr_op_matvec_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_int, _P, C.c_int]),
+    "ocr_op_lm_head_sample": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P, _P, _P,
+                                        _P]),
     "ocr_op_attention_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                           _P]),
 }
@@ -432,21 +433,34 @@ def op_penalize(ctx: Context, d_logits: int, n_vocab: int, rp: float, window: in
     _check(lib().ocr_op_penalize(ctx.h, d_logits, n_vocab, rp, window, d_hist, n_hist))
 
 
-def op_repack_q8_0(ctx: Context, d_blocks: int, rows: int, cols: int, d_quants: int, d_scales: int) -> None:
-    _check(lib().ocr_op_repack_q8_0(ctx.h, d_blocks, rows, cols, d_quants, d_scales))
+def q8_row_bytes(cols: int) -> int:
+    """the row stride of the device q8_0 layout: int8 quants [cols] | f16 scales [cols/32] | pad to 16 B"""
+    return int(lib().ocr_q8_row_bytes(cols))
 
 
-def op_matvec_q8_0(ctx: Context, d_quants: int, d_scales: int, rows: int, cols: int, d_x: int, d_norm_w: Optional[int],
-                   eps: float, nb: int, d_y: int, accumulate: bool) -> None:
-    _check(lib().ocr_op_matvec_q8_0(ctx.h, d_quants, d_scales, rows, cols, d_x, d_norm_w, eps, nb, d_y,
-                                    1 if accumulate else 0))
+def q8_rows_from_blocks(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """GGUF q8_0 blocks → the device row layout, on the host (uint8 [rows][q8_row_bytes(cols)])"""
+    stride = (cols + cols // 16 + 15) // 16 * 16
+    b = np.asarray(blocks, np.uint8).reshape(rows, cols // 32, 34)
+    out = np.zeros((rows, stride), np.uint8)
+    out[:, :cols] = b[:, :, 2:].reshape(rows, cols)
+    out[:, cols:cols + cols // 16] = b[:, :, :2].reshape(rows, cols // 16)
+    return out
 
 
-def op_lm_head_sample(ctx: Context, d_quants: int, d_scales: int, n_vocab: int, dim: int, d_x: int, d_norm_w: int,
-                      eps: float, rp: float, window: int, d_hist: int, d_len: int, d_tok: int,
-                      d_logits: Optional[int]) -> None:
-    _check(lib().ocr_op_lm_head_sample(ctx.h, d_quants, d_scales, n_vocab, dim, d_x, d_norm_w, eps, rp, window,
-                                       d_hist, d_len, d_tok, d_logits))
+def op_repack_q8_0(ctx: Context, d_blocks: int, rows: int, cols: int, d_rows: int) -> None:
+    _check(lib().ocr_op_repack_q8_0(ctx.h, d_blocks, rows, cols, d_rows))
+
+
+def op_matvec_q8_0(ctx: Context, d_w: int, rows: int, cols: int, d_x: int, d_norm_w: Optional[int], eps: float,
+                   nb: int, d_y: int, accumulate: bool) -> None:
+    _check(lib().ocr_op_matvec_q8_0(ctx.h, d_w, rows, cols, d_x, d_norm_w, eps, nb, d_y, 1 if accumulate else 0))
+
+
+def op_lm_head_sample(ctx: Context, d_w: int, n_vocab: int, dim: int, d_x: int, d_norm_w: int, eps: float, rp: float,
+                      window: int, d_hist: int, d_len: int, d_tok: int, d_logits: Optional[int]) -> None:
+    _check(lib().ocr_op_lm_head_sample(ctx.h, d_w, n_vocab, dim, d_x, d_norm_w, eps, rp, window, d_hist, d_len, d_tok,
+                                       d_logits))
 
 
 def op_attention_decode(ctx: Context, d_qkv: int, d_q_norm: int, d_k_norm: int, d_rope: int, d_k: int, d_v: int,

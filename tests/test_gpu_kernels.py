@@ -29,15 +29,10 @@ def host(torch, t):
     return t.cpu().numpy()
 
 
-def split_blocks(blocks, rows, cols):
-    b = blocks.reshape(rows * cols // 32, 34)
-    return b[:, 2:].reshape(rows, cols).view(np.int8).copy(), b[:, :2].copy().view(np.uint16).reshape(rows, cols // 32)
-
-
-def device_matrix(torch, orc, rows, cols, seed, sigma):
+def device_matrix(torch, ocr, orc, rows, cols, seed, sigma):
+    """(GGUF blocks, the device row layout built on the host)"""
     w = orc.synth_q8_0(rows * cols, seed, sigma)
-    q, d = split_blocks(w, rows, cols)
-    return w, dev(torch, q), dev(torch, d.view(np.int16))
+    return w, dev(torch, ocr.q8_rows_from_blocks(w, rows, cols))
 
 
 def test_repack_holds_the_same_values(ocr, orc, ctx, torch_cuda):
@@ -46,14 +41,16 @@ def test_repack_holds_the_same_values(ocr, orc, ctx, torch_cuda):
         w = orc.synth_q8_0(rows * cols, 1234 + rows, 0.3)
         buf = torch.zeros(w.size + 2, dtype=torch.uint8, device="cuda")
         buf[2:] = torch.from_numpy(w).cuda()  # blocks at a 2-byte (not 4-byte) boundary
-        q = torch.zeros(rows * cols, dtype=torch.int8, device="cuda")
-        d = torch.zeros(rows * cols // 32, dtype=torch.int16, device="cuda")
+        stride = ocr.q8_row_bytes(cols)
+        out = torch.full((rows * stride,), 0xAB, dtype=torch.uint8, device="cuda")
         torch.cuda.synchronize()
-        ocr.op_repack_q8_0(ctx, buf.data_ptr() + 2, rows, cols, q.data_ptr(), d.data_ptr())
+        ocr.op_repack_q8_0(ctx, buf.data_ptr() + 2, rows, cols, out.data_ptr())
         ctx.sync()
-        eq, ed = split_blocks(w, rows, cols)
-        assert np.array_equal(host(torch, q).reshape(rows, cols), eq)
-        assert np.array_equal(host(torch, d).view(np.uint16).reshape(rows, cols // 32), ed)
+        got = host(torch, out).reshape(rows, stride)
+        want = ocr.q8_rows_from_blocks(w, rows, cols)
+        assert np.array_equal(got[:, :cols + cols // 16], want[:, :cols + cols // 16])
+        b = w.reshape(rows, cols // 32, 34)
+        assert np.array_equal(got[:, :cols].view(np.int8), b[:, :, 2:].reshape(rows, cols).view(np.int8))
 
 
 def _norm_rows(orc, x, nw, eps):
@@ -63,16 +60,17 @@ def _norm_rows(orc, x, nw, eps):
 @pytest.mark.parametrize("rows,cols,nb,norm,acc", [
     (37, 96, 1, False, False), (37, 96, 1, True, True), (4096, 1024, 1, True, False), (1024, 3072, 1, False, True),
     (1024, 2048, 2, False, True), (6144, 1024, 4, True, False), (1000, 256, 8, True, False), (512, 1024, 32, False, True),
+    (3, 3072, 3, True, False), (20011, 1024, 1, True, False), (151936, 1024, 1, False, False),
 ])
 def test_matvec_matches_oracle(ocr, orc, ctx, torch_cuda, rows, cols, nb, norm, acc):
     torch = torch_cuda
-    w, q, d = device_matrix(torch, orc, rows, cols, 77 + rows + cols, 0.02)
+    w, wd = device_matrix(torch, ocr, orc, rows, cols, 77 + rows + cols, 0.02)
     x = ocr.gauss(5 + nb, nb * cols, 1.0).reshape(nb, cols)
     nw = (1.0 + 0.1 * ocr.gauss(6, cols)).astype(np.float32)
     base = ocr.gauss(7, nb * rows, 1.0).reshape(nb, rows)
     xd, nwd, yd = dev(torch, x), dev(torch, nw), dev(torch, base.copy())
-    ocr.op_matvec_q8_0(ctx, q.data_ptr(), d.data_ptr(), rows, cols, xd.data_ptr(), nwd.data_ptr() if norm else None,
-                       1e-6, nb, yd.data_ptr(), acc)
+    ocr.op_matvec_q8_0(ctx, wd.data_ptr(), rows, cols, xd.data_ptr(), nwd.data_ptr() if norm else None, 1e-6, nb,
+                       yd.data_ptr(), acc)
     ctx.sync()
     got = host(torch, yd)
     xn = _norm_rows(orc, x, nw, 1e-6) if norm else x
@@ -198,7 +196,7 @@ def test_lm_head_sample_matches_oracle(ocr, orc, ctx, torch_cuda, vocab, window,
     """dmv_norm + choose: logits within 2e-3 max|logit| (and 1e-5 sum|w x|); the token is choose() of those logits"""
     torch = torch_cuda
     dim = 1024
-    w, q, d = device_matrix(torch, orc, vocab, dim, 4242 + vocab, 0.02)
+    w, wd = device_matrix(torch, ocr, orc, vocab, dim, 4242 + vocab, 0.02)
     x = ocr.gauss(17, dim, 1.0)
     nw = orc.fill_norm(18, dim)
     hist = ocr.fill_ids(19, 70, vocab)
@@ -212,8 +210,8 @@ def test_lm_head_sample_matches_oracle(ocr, orc, ctx, torch_cuda, vocab, window,
     for rep in range(2):  # twice: the self-resetting counters
         lend.fill_(hist.size)
         torch.cuda.synchronize()
-        ocr.op_lm_head_sample(ctx, q.data_ptr(), d.data_ptr(), vocab, dim, xd.data_ptr(), nwd.data_ptr(), 1e-6, rp,
-                              window, hd.data_ptr(), lend.data_ptr(), tokd.data_ptr(), logits.data_ptr())
+        ocr.op_lm_head_sample(ctx, wd.data_ptr(), vocab, dim, xd.data_ptr(), nwd.data_ptr(), 1e-6, rp, window,
+                              hd.data_ptr(), lend.data_ptr(), tokd.data_ptr(), logits.data_ptr())
         ctx.sync()
         got = host(torch, logits)
         assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
