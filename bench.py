@@ -140,14 +140,42 @@ def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
     return sum(times) / len(times), algo
 
 
-def kernel_roofline(ocr, ctx, torch):
-    us, algo = lm_head_kernel(ocr, ctx, torch, 10)
+def kernel_classes(sess, B, prefix_len, last_rows, steps=4):
+    """in-situ per-kernel times of the decode step (ocr_profile_step: an event after every launch, the same kernels
+    the timed graph replays), grouped by kernel class: launches, mean µs, algorithmic bytes per launch, share"""
+    for b in range(B):
+        sess.rewind(b, prefix_len - 1)
+        sess.prefill(b, embd=last_rows[b], logits=False)
+    agg = {}
+    for i in range(steps):
+        for k in sess.profile_step([IMAGE_PAD] * B):
+            a = agg.setdefault(k["name"], [0, 0.0, 0.0])
+            a[0] += 1
+            a[1] += k["us"]
+            a[2] += k["bytes"]
+    tot = sum(a[1] for a in agg.values())
+    peak, _ = peaks()
+    out = []
+    for name, (n, us, by) in sorted(agg.items(), key=lambda x: -x[1][1]):
+        gbs = by / (us * 1e-6) / 1e9
+        out.append({"kernel": name, "launches": n, "us_per_launch": round(us / n, 2),
+                    "bytes_per_launch": round(by / n), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                    "share": round(us / tot, 4)})
+    return out
+
+
+def kernel_roofline(classes):
+    """the roofline object for the dominant class (largest share of the step's device time)"""
     peak, which = peaks()
-    gbs = algo / (us * 1e-6) / 1e9
-    return {"kernel": "k_lm_head<1> (LM head + windowed penalty + argmax, 151936 x 1024 q8_0)", "bound": "hbm",
-            "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
-            "peak_source": f"{which} hbm_gbs", "traffic": None, "us_per_launch": round(us, 2),
-            "algorithmic_bytes": algo}
+    top = classes[0]
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(top["kernel"])
+    return {"kernel": top["kernel"], "bound": "hbm", "achieved": top["achieved_gbs"], "peak": peak, "unit": "GB/s",
+            "frac": top["frac"], "peak_source": f"{which} hbm_gbs (of {which})", "traffic": traffic,
+            "us_per_launch": top["us_per_launch"], "algorithmic_bytes_per_launch": top["bytes_per_launch"],
+            "share_of_step": top["share"]}
 
 
 # ---------------------------------------------------------------------------------------------------------------------
@@ -225,7 +253,9 @@ def run_ours(args):
     launches = args.steps * ((CONFIG2["n_layer"] * 8 + 2) * B + 1 + (new - 1) * launches_per_token)
     out = None
     if rank == 0:
-        roof = kernel_roofline(ocr, ctx, torch)
+        classes = kernel_classes(sess, B, prefix_len, last_rows)
+        roof = kernel_roofline(classes)
+        lm_us, lm_bytes = lm_head_kernel(ocr, ctx, torch, 10)
         out = {
             "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
             "value": round(tokens / dev_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -243,6 +273,9 @@ def run_ours(args):
                     "h2d_bytes_per_step": B * (64 * 4 + 1024 * 4), "d2h_bytes_per_step": B * new * 4},
             "gpu_launches": int(launches),
             "roofline": roof,
+            "kernels": classes,
+            "lm_head_alone": {"us_per_launch": round(lm_us, 2), "achieved_gbs": round(lm_bytes / lm_us / 1e3, 1),
+                              "note": "the LM head + penalty + argmax kernel timed alone after a 256 MB L2 flush"},
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

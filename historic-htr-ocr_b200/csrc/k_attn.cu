@@ -1,63 +1,53 @@
 // k_attn.cu — decode attention of one token per slot over the f16 KV cache, GQA, split over the keys ("flash
-// decoding"): the reference's qkv_post.wgsl (q/k RMSNorm → RoPE NEOX → K/V store), attn_decode.wgsl (per-chunk softmax
+// decoding"): the reference's qkv_post.wgsl (q/k RMSNorm → RoPE NEOX → K/V store), attn_decode.wgsl (per-range softmax
 // partials m, l, o[128]) and attn_merge.wgsl (M = max m, L = Σ l e^(m−M), O = Σ o e^(m−M) / L) in one kernel.
 //
-// Grid (splits, n_kv, slots), 128 threads. A CTA owns one kv head (its G = n_head / n_kv query heads) and a
-// contiguous key range [k0, k1) (≤ KEYS_MAX keys) of the slot's pos + 1 keys; k0, k1 come from the device-side
-// position, so one captured graph serves every step. KV layout [slot][kv head][n_ctx][128] f16: the range is one
-// contiguous run of K and one of V, each moved into shared memory by one bulk-async copy issued before the kernel
-// waits on its predecessor (no earlier kernel still writes those rows; the row at pos is computed here and written to
-// both the cache and shared memory). Scores: 8 lanes per key (16 dims each), 4 keys per warp per pass; P·V: a warp per
-// key stripe, lane = 4 dims; all from shared memory. The last CTA of a (slot, kv head) to finish merges the partials
-// (threadfence + ticket, counter reset by that CTA; no waiting on other CTAs). The one mbarrier wait is bounded.
+// Grid (CL, n_kv, slots) in thread-block clusters of CL CTAs: one cluster per (slot, kv head), CTA rank r owning a
+// contiguous key range [k0, k1) of the slot's pos + 1 keys (from the device-side position: one captured graph serves
+// every step). KV layout [slot][kv head][n_ctx][128] f16: a range is one contiguous run of K and one of V, moved into
+// shared memory in tiles of TILE keys by bulk-async copies on a ring of up to MAX_BUF tiles (96 KB: two CTAs per SM,
+// so every 16-CTA cluster of a one-token step is resident at once). The first ring's copies are issued before the
+// kernel waits on its predecessor — no kernel of this step writes rows below pos; the row at pos is computed here
+// (one warp per head: RMSNorm by a warp reduction, RoPE in registers), stored to the cache and to an extra shared row
+// read in place of its tile row. The keys are taken in rounds of the resident tiles; each of the 8 warps owns a
+// contiguous eighth of a round: scores by 8 lanes per key (16 dims each), one online-softmax update per round
+// (running max, sum, output rescale) and P·V with lane = 4 dims. The block meets only when the ring wraps. The warps'
+// states merge in shared memory into the CTA's (m, l, o); the cluster's CL
+// partials merge through distributed shared memory — each CTA folds a slice of the outputs by reading the other CTAs'
+// partials — between two cluster barriers: no global round trip, no atomic. mbarrier waits are bounded; a warp whose
+// wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets every barrier.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
 #include "kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace ocr {
 
-constexpr int AT_THREADS = 128;
-constexpr int HD = 128;          // head dim (TextConfig::from_gguf requires 128, text.rs:57-60)
-constexpr int KEYS_MAX = 192;    // keys per CTA: K + V tiles 96 KB of shared memory
-constexpr int MAX_SPLITS = 256;  // key ranges per (slot, kv head): the merge keeps one weight per range in smem
+constexpr int AT_THREADS = 256;
+constexpr int NW = AT_THREADS / 32;  // warps per CTA
+constexpr int HD = 128;              // head dim (TextConfig::from_gguf requires 128, text.rs:57-60)
+constexpr int TILE = 64;             // keys per tile (K + V: 32 KB)
+constexpr int MAX_BUF = 3;           // ring depth: at most 96 KB, so two CTAs share an SM
+constexpr int KPW = (MAX_BUF * TILE + NW - 1) / NW;  // keys per warp per round (one per lane)
 
-__device__ __forceinline__ float block_sum128(float v, float* red) {
-    v = warp_sum(v);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    return red[0] + red[1] + red[2] + red[3];
-}
-
-__device__ __forceinline__ float block_max128(float v, float* red) {
-    v = warp_max(v);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-}
-
-template <int G>
-__global__ void __launch_bounds__(AT_THREADS) k_attn_decode(AttnArgs a, int per_max) {
+template <int G, int CL>
+__global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf) {
     extern __shared__ __align__(128) uint8_t sm[];
-    __half* Ks = reinterpret_cast<__half*>(sm);             // [per_max][128]
-    __half* Vs = Ks + (size_t)per_max * HD;                  // [per_max][128]
-    float* sc = reinterpret_cast<float*>(Vs + (size_t)per_max * HD);  // [G][per_max]
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ float qs[G][HD];
-    __shared__ float tmp2[G + 1][HD];
-    __shared__ float red[4];
-    __shared__ float red2[4][G + 1];
-    __shared__ float mw[G][MAX_SPLITS];
-    __shared__ float lw[G][MAX_SPLITS];
-    __shared__ float osum[4][G][HD];
-    __shared__ uint32_t ticket;
+    __shared__ __align__(8) uint64_t full[MAX_BUF];
+    __shared__ __align__(16) float qs[G][HD];
+    __shared__ float scw[NW][G][KPW];  // per warp: the round's scores, then probabilities
+    __shared__ float wm[NW][G], wl[NW][G];
+    __shared__ __align__(16) float wo[NW][G][HD];
+    __shared__ float part[G][HD + 2];  // this CTA's (m, l, o[128]) per head, read by the cluster
+    cg::cluster_group cluster = cg::this_cluster();
     const int b = blockIdx.z, j = blockIdx.y, sp = blockIdx.x, t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
-    const int S = gridDim.x;
-    const int n_head = a.n_head;
 
-    // the slot's position was written by the previous step (its last kernel completed before this step began)
+    // the slot's position was written by the previous step (its last kernel completed before this step began); the
+    // conditions below are the same for every CTA of the cluster (same slot), so a cluster leaves together
     if (a.active && !a.active[b]) return;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.n_ctx) {
@@ -65,279 +55,357 @@ __global__ void __launch_bounds__(AT_THREADS) k_attn_decode(AttnArgs a, int per_
         return;
     }
     const int n_keys = pos + 1;
-    const int per = (n_keys + S - 1) / S;
+    const int per = (n_keys + CL - 1) / CL;
     const int k0 = min(n_keys, sp * per), k1 = min(n_keys, k0 + per);
-    if (k1 - k0 > per_max) {  // the launch sized per_max for this n_ctx; anything else is a bad position
-        if (t == 0) dev_error(a.err, DEV_BAD_POS);
-        return;
-    }
+    const int n_tiles = (k1 - k0 + TILE - 1) / TILE;
     const long head_base = ((long)b * a.n_kv + j) * a.n_ctx;
     __half* kb = a.kc + head_base * HD;
     __half* vb = a.vc + head_base * HD;
-    const int kend = min(k1, pos);  // rows [k0, kend) are in the cache already; the row at pos is written below
-    const bool copy = kend > k0;
-    if (t == 0) {
-        mbar_init(&bar, 1);
-        mbar_fence_init();
-        if (copy) {
-            const uint32_t bytes = (uint32_t)(kend - k0) * HD * 2;
-            mbar_expect_tx(&bar, 2 * bytes);
-            bulk_g2s(Ks, kb + (long)k0 * HD, bytes, &bar);
-            bulk_g2s(Vs, vb + (long)k0 * HD, bytes, &bar);
+    // shared layout: K rows [ring + 1][HD], then V rows [ring + 1][HD]; tile tl occupies rows (tl % n_buf) * TILE …,
+    // row `ring` holds the new token's K (V), written here rather than copied
+    const int ring = n_buf * TILE;
+    __half* Ks = reinterpret_cast<__half*>(sm);
+    __half* Vs = Ks + (size_t)(ring + 1) * HD;
+
+    // rows [ts, min(te, pos)) of tile tl (the row at pos is not in the cache yet)
+    auto issue = [&](int tl) {
+        const int slot = tl % n_buf, ts = k0 + tl * TILE, ce = min(min(k1, ts + TILE), pos);
+        if (ce > ts) {
+            const uint32_t bytes = (uint32_t)(ce - ts) * HD * 2;
+            mbar_expect_tx(&full[slot], 2 * bytes);
+            const uint64_t pol = l2_evict_first();
+            bulk_g2s_stream(Ks + (size_t)slot * TILE * HD, kb + (long)ts * HD, bytes, &full[slot], pol);
+            bulk_g2s_stream(Vs + (size_t)slot * TILE * HD, vb + (long)ts * HD, bytes, &full[slot], pol);
+        } else {
+            mbar_arrive(&full[slot]);  // nothing to copy: complete the phase
         }
+    };
+    if (t == 0) {
+        for (int i = 0; i < n_buf; i++) mbar_init(&full[i], 1);
+        mbar_fence_init();
+        for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl);
         pdl_trigger();
+    }
+    // warp h prepares q head h (h < G) or the new k / v head (h = G), warps taking heads h, h + NW; lane holds dims
+    // d0, d0 + 1 and their RoPE partners 64 + d0, 64 + d0 + 1. Not written by this step, so loaded before the dependency wait: the norm
+    // weights and the RoPE row of pos ([64][2] cos, sin).
+    constexpr int HPW = (G + 1 + NW - 1) / NW;  // heads per warp (2 for the k / v head when G = 8)
+    const int d0 = lane * 2;
+    float2 w_lo[HPW], w_hi[HPW];
+    float4 cs = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (warp <= G) cs = *reinterpret_cast<const float4*>(a.rope + (long)pos * HD + 2 * d0);
+#pragma unroll
+    for (int u = 0; u < HPW; u++) {
+        const int h = warp + u * NW;
+        if (h <= G) {
+            const float* wv = h < G ? a.q_norm : a.k_norm;
+            w_lo[u] = *reinterpret_cast<const float2*>(wv + d0);
+            w_hi[u] = *reinterpret_cast<const float2*>(wv + 64 + d0);
+        }
     }
     pdl_wait();
 
-    // q heads (and, in the CTA whose range holds pos, the new k head): RMSNorm x weight, then RoPE NEOX — all heads'
-    // loads issued together, one reduction round, one rotation exchange
-    const float* qkv = a.qkv + (long)b * a.qkv_stride;
-    const float* cs = a.rope + (long)pos * HD;  // [64][2]
+    // RMSNorm x weight (one warp reduction), RoPE NEOX in registers
     const bool own = pos >= k0 && pos < k1;
-    constexpr int NH = G + 1;
-    float raw[NH];
+    const float* qkv = a.qkv + (long)b * a.qkv_stride;
 #pragma unroll
-    for (int g = 0; g < G; g++) raw[g] = qkv[(j * G + g) * HD + t];
-    raw[G] = own ? qkv[(a.n_head + j) * HD + t] : 0.0f;
-    const float vraw = own ? qkv[(a.n_head + a.n_kv + j) * HD + t] : 0.0f;
-    const float wq = a.q_norm[t], wk = a.k_norm[t];
-    const float cr = cs[2 * (t & 63)], sr = cs[2 * (t & 63) + 1];
-#pragma unroll
-    for (int g = 0; g < NH; g++) {
-        const float s2 = warp_sum(raw[g] * raw[g]);
-        if (lane == 0) red2[warp][g] = s2;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < NH; g++) {
-        const float tot = red2[0][g] + red2[1][g] + red2[2][g] + red2[3][g];
-        tmp2[g][t] = raw[g] * (1.0f / sqrtf(tot / (float)HD + a.eps)) * (g < G ? wq : wk);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < NH; g++) {
-        const float r = t < 64 ? tmp2[g][t] * cr - tmp2[g][t + 64] * sr : tmp2[g][t - 64] * sr + tmp2[g][t] * cr;
-        if (g < G) qs[g][t] = r * a.scale;
-        else if (own) {
-            // the new token's K / V row: to the cache and to the shared tiles
-            const __half kh = __float2half_rn(r), vh = __float2half_rn(vraw);
-            kb[(long)pos * HD + t] = kh;
-            vb[(long)pos * HD + t] = vh;
-            Ks[(pos - k0) * HD + t] = kh;
-            Vs[(pos - k0) * HD + t] = vh;
+    for (int u = 0; u < HPW; u++) {
+        const int h = warp + u * NW;
+        if (h > G || (h == G && !own)) continue;
+        const float* xr = qkv + (long)(h < G ? j * G + h : a.n_head + j) * HD;
+        const float2 xa = *reinterpret_cast<const float2*>(xr + d0), xb = *reinterpret_cast<const float2*>(xr + 64 + d0);
+        float2 va = make_float2(0.f, 0.f), vc = va;
+        if (h == G) {
+            const float* vr = qkv + (long)(a.n_head + a.n_kv + j) * HD;
+            va = *reinterpret_cast<const float2*>(vr + d0);
+            vc = *reinterpret_cast<const float2*>(vr + 64 + d0);
+        }
+        const float ss = warp_sum(xa.x * xa.x + xa.y * xa.y + xb.x * xb.x + xb.y * xb.y);
+        const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+        const float n0 = xa.x * inv * w_lo[u].x, n1 = xa.y * inv * w_lo[u].y;
+        const float n2 = xb.x * inv * w_hi[u].x, n3 = xb.y * inv * w_hi[u].y;
+        const float r0 = n0 * cs.x - n2 * cs.y, r1 = n1 * cs.z - n3 * cs.w;  // dims d0, d0 + 1
+        const float r2 = n0 * cs.y + n2 * cs.x, r3 = n1 * cs.w + n3 * cs.z;  // dims 64 + d0, 64 + d0 + 1
+        if (h < G) {
+            *reinterpret_cast<float2*>(&qs[h][d0]) = make_float2(r0 * a.scale, r1 * a.scale);
+            *reinterpret_cast<float2*>(&qs[h][64 + d0]) = make_float2(r2 * a.scale, r3 * a.scale);
+        } else {
+            // the new token's K / V row: to the cache, and to the extra shared row
+            const __half2 k01 = __floats2half2_rn(r0, r1), k23 = __floats2half2_rn(r2, r3);
+            const __half2 v01 = __floats2half2_rn(va.x, va.y), v23 = __floats2half2_rn(vc.x, vc.y);
+            *reinterpret_cast<__half2*>(kb + (long)pos * HD + d0) = k01;
+            *reinterpret_cast<__half2*>(kb + (long)pos * HD + 64 + d0) = k23;
+            *reinterpret_cast<__half2*>(vb + (long)pos * HD + d0) = v01;
+            *reinterpret_cast<__half2*>(vb + (long)pos * HD + 64 + d0) = v23;
+            *reinterpret_cast<__half2*>(Ks + (size_t)ring * HD + d0) = k01;
+            *reinterpret_cast<__half2*>(Ks + (size_t)ring * HD + 64 + d0) = k23;
+            *reinterpret_cast<__half2*>(Vs + (size_t)ring * HD + d0) = v01;
+            *reinterpret_cast<__half2*>(Vs + (size_t)ring * HD + 64 + d0) = v23;
         }
     }
     __syncthreads();
-    // every thread waits for the tiles; the CTA leaves together if any wait gave up
-    const int ok = copy ? (int)mbar_wait(&bar, 0, a.err) : 1;
-    if (!__syncthreads_and(ok)) return;
 
-    // scores: lane group (lane >> 3) takes one key, lane & 7 its 16 dims
-    const int n = k1 - k0;
-    const int sub = lane >> 3, part = lane & 7;
+    // ---- the key range in rounds of up to n_buf resident tiles: each warp a contiguous eighth of the round, scores,
+    // one online-softmax update and P·V per round; the block meets only when the ring wraps ----
+    // scores: 8 lanes per key, lane prt takes dims prt*8 … +7 and 64 + prt*8 … +7 (a quarter-warp's 16-byte reads
+    // cover 128 consecutive bytes: no bank conflict)
+    const int sub = lane >> 3, prt = lane & 7;
     float qr[G][16];
 #pragma unroll
-    for (int g = 0; g < G; g++)
+    for (int g = 0; g < G; g++) {
+        const float4* q4 = reinterpret_cast<const float4*>(&qs[g][0]);
+        const float4 qa = q4[prt * 2], qb = q4[prt * 2 + 1], qc = q4[16 + prt * 2], qd = q4[16 + prt * 2 + 1];
+        qr[g][0] = qa.x; qr[g][1] = qa.y; qr[g][2] = qa.z; qr[g][3] = qa.w;
+        qr[g][4] = qb.x; qr[g][5] = qb.y; qr[g][6] = qb.z; qr[g][7] = qb.w;
+        qr[g][8] = qc.x; qr[g][9] = qc.y; qr[g][10] = qc.z; qr[g][11] = qc.w;
+        qr[g][12] = qd.x; qr[g][13] = qd.y; qr[g][14] = qd.z; qr[g][15] = qd.w;
+    }
+    float mw[G], lw[G], ow[G][4];
 #pragma unroll
-        for (int i = 0; i < 16; i++) qr[g][i] = qs[g][part * 16 + i];
-    for (int base = 0; base < n; base += 16) {
-        const int key = base + warp * 4 + sub;
-        const bool valid = key < n;
-        float d[G];
+    for (int g = 0; g < G; g++) {
+        mw[g] = -INFINITY;
+        lw[g] = 0.0f;
 #pragma unroll
-        for (int g = 0; g < G; g++) d[g] = 0.0f;
-        if (valid) {
-            const uint4* kp = reinterpret_cast<const uint4*>(Ks + key * HD + part * 16);
-            const uint4 u0 = kp[0], u1 = kp[1];
-            const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
-            const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
+        for (int i = 0; i < 4; i++) ow[g][i] = 0.0f;
+    }
+    bool alive = true;
+    for (int t0 = 0; t0 < n_tiles; t0 += n_buf) {
+        const int t1 = min(n_tiles, t0 + n_buf);  // tiles t0 … t1-1 sit in slots 0 … t1-t0-1
+        for (int tl = t0; tl < t1 && alive; tl++)
+            alive = __all_sync(FULL, mbar_wait(&full[tl - t0], (tl / n_buf) & 1, a.err));
+        const int r0 = k0 + t0 * TILE, nk = min(k1, k0 + t1 * TILE) - r0;  // the round's keys [r0, r0 + nk)
+        const int prel = pos - r0;  // the new row's index in the round (outside [0, nk) elsewhere)
+        const int kw = (nk + NW - 1) / NW;
+        const int w0 = min(nk, warp * kw), nw = alive ? min(nk, w0 + kw) - w0 : 0;  // this warp's keys
+#pragma unroll 2
+        for (int ps = 0; ps < (nw + 3) >> 2; ps++) {
+            const int kk = ps * 4 + sub;
+            float d[G], e[G];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float2 f0 = __half22float2(h0[i]), f1 = __half22float2(h1[i]);
+            for (int g = 0; g < G; g++) d[g] = e[g] = 0.0f;
+            if (kk < nw) {
+                const int i = w0 + kk;
+                const __half* kr = Ks + (size_t)(i == prel ? ring : i) * HD;
+                const uint4 u0 = *reinterpret_cast<const uint4*>(kr + prt * 8);
+                const uint4 u1 = *reinterpret_cast<const uint4*>(kr + 64 + prt * 8);
+                const __half2* h0 = reinterpret_cast<const __half2*>(&u0);
+                const __half2* h1 = reinterpret_cast<const __half2*>(&u1);
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    d[g] = fmaf(qr[g][2 * i], f0.x, d[g]);
-                    d[g] = fmaf(qr[g][2 * i + 1], f0.y, d[g]);
-                    d[g] = fmaf(qr[g][8 + 2 * i], f1.x, d[g]);
-                    d[g] = fmaf(qr[g][8 + 2 * i + 1], f1.y, d[g]);
+                for (int c = 0; c < 4; c++) {
+                    const float2 f0 = __half22float2(h0[c]), f1 = __half22float2(h1[c]);
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        d[g] = fmaf(qr[g][2 * c], f0.x, d[g]);
+                        d[g] = fmaf(qr[g][2 * c + 1], f0.y, d[g]);
+                        e[g] = fmaf(qr[g][8 + 2 * c], f1.x, e[g]);
+                        e[g] = fmaf(qr[g][8 + 2 * c + 1], f1.y, e[g]);
+                    }
                 }
             }
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            d[g] += __shfl_xor_sync(FULL, d[g], 4);
-            d[g] += __shfl_xor_sync(FULL, d[g], 2);
-            d[g] += __shfl_xor_sync(FULL, d[g], 1);
-        }
-        if (valid && part == 0)
-#pragma unroll
-            for (int g = 0; g < G; g++) sc[g * per_max + key] = d[g];
-    }
-    __syncthreads();
-    // softmax of every head at once: one max round, one sum round
-    float m[G], l[G];
-    {
-        float mx[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) mx[g] = -INFINITY;
-        for (int i = t; i < n; i += AT_THREADS)
-#pragma unroll
-            for (int g = 0; g < G; g++) mx[g] = fmaxf(mx[g], sc[g * per_max + i]);
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            mx[g] = warp_max(mx[g]);
-            if (lane == 0) red2[warp][g] = mx[g];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int g = 0; g < G; g++) m[g] = fmaxf(fmaxf(red2[0][g], red2[1][g]), fmaxf(red2[2][g], red2[3][g]));
-        __syncthreads();
-        float sm_[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) sm_[g] = 0.0f;
-        for (int i = t; i < n; i += AT_THREADS)
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                const float p = expf(sc[g * per_max + i] - m[g]);
-                sc[g * per_max + i] = p;
-                sm_[g] += p;
+                float v = d[g] + e[g];
+                v += __shfl_xor_sync(FULL, v, 4);
+                v += __shfl_xor_sync(FULL, v, 2);
+                v += __shfl_xor_sync(FULL, v, 1);
+                if (prt == 0 && kk < nw) scw[warp][g][kk] = v;
             }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            sm_[g] = warp_sum(sm_[g]);
-            if (lane == 0) red2[warp][g] = sm_[g];
         }
-        __syncthreads();
+        __syncwarp();
+        // lane = key of this warp's share: the round's max, probabilities, sum
+        if (nw > 0) {
 #pragma unroll
-        for (int g = 0; g < G; g++) l[g] = (red2[0][g] + red2[1][g]) + (red2[2][g] + red2[3][g]);
-    }
-    __syncthreads();
-    // P·V: warp w takes keys w, w + 4, …; lane owns dims 4 lane … 4 lane + 3
-    float o[G][4];
+            for (int g = 0; g < G; g++) {
+                const float sc = lane < nw ? scw[warp][g][lane] : -INFINITY;
+                const float mn = fmaxf(mw[g], warp_max(sc));
+                const float corr = expf(mw[g] - mn);  // exp(-inf) = 0 on the first round
+                const float p = lane < nw ? expf(sc - mn) : 0.0f;
+                if (lane < nw) scw[warp][g][lane] = p;
+                lw[g] = fmaf(lw[g], corr, warp_sum(p));
 #pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) o[g][i] = 0.0f;
+                for (int c = 0; c < 4; c++) ow[g][c] *= corr;
+                mw[g] = mn;
+            }
+        }
+        __syncwarp();
+        // P·V; lane owns dims 4 lane … 4 lane + 3
 #pragma unroll 4
-    for (int key = warp; key < n; key += 4) {
-        const uint2 u = *reinterpret_cast<const uint2*>(Vs + key * HD + lane * 4);
-        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        for (int kk = 0; kk < nw; kk++) {
+            const int i = w0 + kk;
+            const uint2 u = *reinterpret_cast<const uint2*>(Vs + (size_t)(i == prel ? ring : i) * HD + lane * 4);
+            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                const float p = scw[warp][g][kk];
+                ow[g][0] = fmaf(p, v0.x, ow[g][0]);
+                ow[g][1] = fmaf(p, v0.y, ow[g][1]);
+                ow[g][2] = fmaf(p, v1.x, ow[g][2]);
+                ow[g][3] = fmaf(p, v1.y, ow[g][3]);
+            }
+        }
+        if (t1 < n_tiles) {
+            // the ring wraps: every warp is done with the round's rows before they are refilled
+            __syncthreads();
+            if (t == 0) {
+                fence_proxy_async();
+                for (int tl = t1; tl < min(n_tiles, t1 + n_buf); tl++) issue(tl);
+            }
+        }
+    }
+    // ---- the CTA's partial: merge the warps ----
+    if (lane == 0)
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            const float p = sc[g * per_max + key];
-            o[g][0] = fmaf(p, v0.x, o[g][0]);
-            o[g][1] = fmaf(p, v0.y, o[g][1]);
-            o[g][2] = fmaf(p, v1.x, o[g][2]);
-            o[g][3] = fmaf(p, v1.y, o[g][3]);
+            wm[warp][g] = mw[g];
+            wl[warp][g] = lw[g];
         }
-    }
 #pragma unroll
     for (int g = 0; g < G; g++)
+        *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(ow[g][0], ow[g][1], ow[g][2], ow[g][3]);
+    const bool ok = __syncthreads_and(alive);  // a warp whose copy wait ran out voids the CTA's partial
+    for (int q = t; q < G * HD; q += AT_THREADS) {
+        const int g = q / HD, d = q % HD;
+        float M = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 4; i++) osum[warp][g][lane * 4 + i] = o[g][i];
-    __syncthreads();
+        for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
+        float L = 0.0f, O = 0.0f;
+        if (M != -INFINITY && ok)
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        const int h = j * G + g;
-        float* pp = a.part + (((long)b * n_head + h) * S + sp) * (HD + 2);
-        const float ov = osum[0][g][t] + osum[1][g][t] + osum[2][g][t] + osum[3][g][t];
-        pp[2 + t] = n > 0 ? ov : 0.0f;
-        if (t == 0) {
-            pp[0] = n > 0 ? m[g] : -INFINITY;
-            pp[1] = n > 0 ? l[g] : 0.0f;
+            for (int w = 0; w < NW; w++) {
+                const float e = expf(wm[w][g] - M);
+                L = fmaf(wl[w][g], e, L);
+                O = fmaf(wo[w][g][d], e, O);
+            }
+        part[g][2 + d] = O;
+        if (d == 0) {
+            part[g][0] = (ok && L > 0.0f) ? M : -INFINITY;
+            part[g][1] = ok ? L : 0.0f;
         }
     }
-    __threadfence();
-    __syncthreads();
-    if (t == 0) ticket = atomicAdd(&a.done[(long)b * a.n_kv + j], 1u);
-    __syncthreads();
-    if (ticket != (uint32_t)S - 1) return;
-    __threadfence();
-    // the merge: every split's (m, l) and this thread's o values loaded in one go; then each thread folds the splits
-    // itself (S is small: no reductions, no further round trips unless S > OC)
-    constexpr int OC = 64 / G;
-    for (int q = t; q < S * G; q += AT_THREADS) {
-        const int g = q / S, s2 = q - g * S;
-        const float* pp = a.part + (((long)b * n_head + j * G + g) * S + s2) * (HD + 2);
-        mw[g][s2] = __ldcg(pp);
-        lw[g][s2] = __ldcg(pp + 1);
-    }
-    float ov[G][OC];
+    // ---- the cluster's merge through distributed shared memory ----
+    cluster.sync();
+    constexpr int PER = G * HD / CL;  // outputs this CTA folds
+    for (int q0 = t; q0 < PER; q0 += AT_THREADS) {
+        const int q = sp * PER + q0, g = q / HD, d = q % HD;
+        float ms[CL], ls[CL], os[CL];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float* pb = a.part + ((long)b * n_head + j * G + g) * S * (HD + 2) + 2 + t;
-#pragma unroll
-        for (int u = 0; u < OC; u++) ov[g][u] = u < S ? __ldcg(pb + (long)u * (HD + 2)) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < G; g++) {
+        for (int r = 0; r < CL; r++) {
+            const float* rp = cluster.map_shared_rank(&part[g][0], r);
+            ms[r] = rp[0];
+            ls[r] = rp[1];
+            os[r] = rp[2 + d];
+        }
         float M = -INFINITY;
-        for (int s2 = 0; s2 < S; s2++) M = fmaxf(M, mw[g][s2]);
+#pragma unroll
+        for (int r = 0; r < CL; r++) M = fmaxf(M, ms[r]);
         float L = 0.0f, O = 0.0f;
 #pragma unroll
-        for (int u = 0; u < OC; u++)
-            if (u < S) {
-                const float w = expf(mw[g][u] - M);
-                L = fmaf(lw[g][u], w, L);
-                O = fmaf(ov[g][u], w, O);
-            }
-        const float* pb = a.part + ((long)b * n_head + j * G + g) * S * (HD + 2) + 2 + t;
-        for (int s2 = OC; s2 < S; s2++) {
-            const float w = expf(mw[g][s2] - M);
-            L = fmaf(lw[g][s2], w, L);
-            O = fmaf(__ldcg(pb + (long)s2 * (HD + 2)), w, O);
+        for (int r = 0; r < CL; r++) {
+            const float e = ms[r] == -INFINITY ? 0.0f : expf(ms[r] - M);
+            L = fmaf(ls[r], e, L);
+            O = fmaf(os[r], e, O);
         }
-        a.out[(long)b * a.out_stride + (j * G + g) * HD + t] = O / L;
+        a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
     }
-    if (t == 0) a.done[(long)b * a.n_kv + j] = 0u;
+    cluster.sync();  // no CTA leaves while another still reads its partial
 }
 
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx) {
-    // one wave of CTAs at least; at most KEYS_MAX keys per CTA at the session's longest context
+    // the cluster size: 16 CTAs per (slot, kv head) while the clusters fit one wave at two CTAs per SM (a 16-cluster
+    // takes 8 SMs of one GPC; a B200 holds 14 such clusters), fewer for batches
+    (void)n_ctx;
     const int heads = nb * n_kv;
-    int s = (num_sms + heads - 1) / heads;
-    const int min_s = (n_ctx + KEYS_MAX - 1) / KEYS_MAX;
-    if (s < min_s) s = min_s;
-    if (s > n_ctx) s = n_ctx;
-    if (s > MAX_SPLITS) s = MAX_SPLITS;  // (n_ctx <= MAX_SPLITS * KEYS_MAX, checked at session creation)
-    if (s < 1) s = 1;
-    return s;
+    if (heads * 16 <= num_sms) return 16;
+    if (heads * 9 <= 2 * num_sms) return 8;
+    return 4;
 }
 
-template <int G>
-static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
-    const int per_max = (a.n_ctx + a.splits - 1) / a.splits;
-    const size_t smem = (size_t)per_max * HD * 2 * 2 + (size_t)G * per_max * sizeof(float);
-    auto kern = k_attn_decode<G>;
+// the ring depth: the tiles of the longest range, at most MAX_BUF, and no more than keeps a CTA within half an SM's
+// shared memory (two CTAs per SM: a cluster of 16 then needs 8 SMs of a GPC)
+static int ring_depth(int n_ctx, int cl, int static_bytes) {
+    const int tiles = ((n_ctx + cl - 1) / cl + TILE - 1) / TILE;
+    const int fit = (113 * 1024 - static_bytes - 2 * HD * 2) / (2 * TILE * HD * 2);
+    return std::max(1, std::min(std::min(tiles, MAX_BUF), fit));
+}
+
+template <int G, int CL>
+static int static_smem() {
+    static int bytes = -1;
+    if (bytes < 0) {
+        cudaFuncAttributes fa;
+        bytes = cudaFuncGetAttributes(&fa, k_attn_decode<G, CL>) == cudaSuccess ? (int)fa.sharedSizeBytes : 0;
+    }
+    return bytes;
+}
+
+template <int G, int CL>
+static cudaLaunchConfig_t config_t(cudaStream_t st, const AttnArgs& a, cudaLaunchAttribute* attr, int* n_buf) {
+    *n_buf = ring_depth(a.n_ctx, CL, static_smem<G, CL>());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)CL, (unsigned)a.n_kv, (unsigned)a.nb);
+    cfg.blockDim = dim3(AT_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)2 * (*n_buf * TILE + 1) * HD * 2;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+// true when a cluster of CL CTAs of this kernel can be resident (16 needs 16 SMs of one GPC with the shared memory)
+template <int G, int CL>
+static bool usable_t(cudaStream_t st, const AttnArgs& a) {
+    auto kern = k_attn_decode<G, CL>;
     static bool configured = false;
     if (!configured) {
         // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
-        cudaFuncAttributes fa;
-        cudaFuncGetAttributes(&fa, kern);
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+        if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         configured = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)a.splits, (unsigned)a.n_kv, (unsigned)a.nb);
-    cfg.blockDim = dim3(AT_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, kern, a, per_max);
+    if (CL <= 8) return true;
+    static int usable[MAX_BUF] = {-1, -1, -1};  // per ring depth, asked once
+    cudaLaunchAttribute attr[2];
+    int n_buf = 1, n = 0;
+    cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
+    if (usable[n_buf - 1] < 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        usable[n_buf - 1] = n >= 1;
+    }
+    return usable[n_buf - 1] == 1;
+}
+
+template <int G, int CL>
+static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
+    cudaLaunchAttribute attr[2];
+    int n_buf = 1;
+    cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
+    cfg.numAttrs = pdl ? 2 : 1;
+    cudaLaunchKernelEx(&cfg, k_attn_decode<G, CL>, a, n_buf);
+}
+
+template <int G>
+static void launch_g(cudaStream_t st, const AttnArgs& a, bool pdl) {
+    if (a.splits == 16 && usable_t<G, 16>(st, a)) launch_t<G, 16>(st, a, pdl);
+    else if (a.splits >= 8 && usable_t<G, 8>(st, a)) launch_t<G, 8>(st, a, pdl);
+    else if (usable_t<G, 4>(st, a)) launch_t<G, 4>(st, a, pdl);
 }
 
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl) {
     const int G = a.n_head / a.n_kv;
-    if (G == 1) launch_t<1>(st, a, pdl);
-    else if (G == 2) launch_t<2>(st, a, pdl);
-    else if (G == 4) launch_t<4>(st, a, pdl);
-    else launch_t<8>(st, a, pdl);
+    if (G == 1) launch_g<1>(st, a, pdl);
+    else if (G == 2) launch_g<2>(st, a, pdl);
+    else if (G == 4) launch_g<4>(st, a, pdl);
+    else launch_g<8>(st, a, pdl);
 }
 
 }  // namespace ocr

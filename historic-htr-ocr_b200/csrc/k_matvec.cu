@@ -201,7 +201,9 @@ __device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
 // load of a pass is issued before any is used (float4, up to XU per thread in flight): the staging costs one
 // round trip, not one per element.
 constexpr int XU = 8;
-__device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr) {
+// `wn` holds this thread's norm-weight float4s, loaded by the caller (before its dependency wait) when K fits one pass
+__device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr,
+                        const float4* wn) {
     const int K = a.w.cols, K4 = K >> 2;
     const bool write_x = a.x_out != nullptr && blockIdx.x == 0;
     float4* xs4 = reinterpret_cast<float4*>(xsf);
@@ -214,18 +216,10 @@ __device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a,
             if (t >= 0 && t < a.emb.rows) er = a.emb.w + (long)t * a.emb.stride;
         }
         const float4* xg = reinterpret_cast<const float4*>(a.x + (long)b * a.x_stride);
-        const float4* nw4 = reinterpret_cast<const float4*>(a.nw);
         const bool fits = K4 <= XU * nthr;  // one pass: values stay in registers across the norm's reduction
         float ss = 0.0f;
         for (int base = 0; base < K4; base += XU * nthr) {
-            float4 v[XU], wn[XU];
-            if (a.nw && fits) {
-#pragma unroll
-                for (int u = 0; u < XU; u++) {
-                    const int i4 = base + u * nthr + tid;
-                    if (i4 < K4) wn[u] = nw4[i4];
-                }
-            }
+            float4 v[XU];
 #pragma unroll
             for (int u = 0; u < XU; u++) {
                 const int i4 = base + u * nthr + tid;
@@ -330,24 +324,39 @@ __global__ void __launch_bounds__((W + 1) * 32) k_mv(MvArgs a, int rpc, int ns) 
     if (warp == W) {
         // ---- producer: weights never depend on the previous kernel, so no griddepcontrol.wait here ----
         if (lane == 0) {
+            const uint64_t pol = l2_evict_first();
             for (int t = 0; t < n_stage; t++) {
                 const int slot = t % ns;
                 if (t >= ns && !mbar_wait(&empty[slot], ((t / ns) - 1) & 1, a.err)) break;
                 const int r0 = lo + t * SR;
                 const uint32_t bytes = (uint32_t)(min(SR, hi - r0) * stride);
                 mbar_expect_tx(&full[slot], bytes);
-                bulk_g2s(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot]);
+                bulk_g2s_stream(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot], pol);
                 if (t == min(ns, n_stage) - 1) pdl_trigger();
             }
         }
     } else {
         // ---- consumers ----
-        pdl_wait();
-        // per-slot activity, read once; for the residual add, the first stages' old values of this warp's rows are
-        // fetched now so the epilogue's read-modify-write does not wait on memory
+        // Before the dependency wait: what no kernel of this step writes — the norm weights, the per-slot
+        // activity, and for the LM head the window's tokens (history and length were written by the previous
+        // step's choice, complete before this step's first kernel started; every later kernel launched after it).
         bool act[NB];
 #pragma unroll
         for (int s = 0; s < NB; s++) act[s] = s < nb && (!a.active || a.active[slot0 + s] != 0);
+        float4 wn[XU];
+        const int K4 = K >> 2;
+        if (a.nw && K4 <= XU * NC) {
+            const float4* nw4 = reinterpret_cast<const float4*>(a.nw);
+#pragma unroll
+            for (int u = 0; u < XU; u++) {
+                const int i4 = u * NC + threadIdx.x;
+                if (i4 < K4) wn[u] = nw4[i4];
+            }
+        }
+        if (lmhead) pen_prefilter(pl, nb, slot0, a.lm, lo, hi, NC);
+        pdl_wait();
+        // for the residual add, the first stages' old values of this warp's rows are fetched now so the epilogue's
+        // read-modify-write does not wait on memory
         constexpr int PF = 2;
         float yold[PF][NB][R];
         if (a.mode == MV_ADD && lane == 0) {
@@ -363,8 +372,7 @@ __global__ void __launch_bounds__((W + 1) * 32) k_mv(MvArgs a, int rpc, int ns) 
                                                                           : 0.0f;
                     }
         }
-        stage_x(xsf, nch, nb, slot0, a, red, NC);
-        if (lmhead) pen_prefilter(pl, nb, slot0, a.lm, lo, hi, NC);
+        stage_x(xsf, nch, nb, slot0, a, red, NC, wn);
         bar_sync(1, NC);
         const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
         for (int t = 0; t < n_stage; t++) {

@@ -96,10 +96,8 @@ struct AttnArgs {
     __half* vc = nullptr;
     const int32_t* pos = nullptr;  // [B] the token's position (device)
     const int32_t* active = nullptr;
-    int n_head = 16, n_kv = 8, n_ctx = 0, splits = 1;
+    int n_head = 16, n_kv = 8, n_ctx = 0, splits = 16;  // splits: CTAs per cluster (4, 8 or 16)
     float eps = 1e-6f, scale = 0.0f;
-    float* part = nullptr;      // [B][n_head][splits][130]
-    uint32_t* done = nullptr;   // [B][n_kv] self-resetting
     float* out = nullptr;       // [B][out_stride]
     int out_stride = 0;
     int nb = 1;

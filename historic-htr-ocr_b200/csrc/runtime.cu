@@ -10,6 +10,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <string>
 #include <vector>
@@ -38,6 +39,7 @@ using namespace ocr;
 // context
 // ---------------------------------------------------------------------------------------------------------------------
 struct ocr_ctx {
+    int refs = 1;  // the caller's handle + one per live model: freed when the last is released
     int device = 0;
     cudaStream_t stream = nullptr;
     int num_sms = 148;
@@ -105,6 +107,7 @@ struct LayerW {
 };
 
 struct ocr_model {
+    int refs = 1;  // the caller's handle + one per live session
     ocr_ctx* ctx = nullptr;
     ocr_text_cfg cfg{};
     void* mem = nullptr;
@@ -202,6 +205,7 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
         delete m;
         return cuda_fail(e, "cudaMalloc(weights)");
     }
+    ctx->refs++;
     m->mem_bytes = L.total;
     for (const auto& lo : L.layers) {
         LayerW w;
@@ -434,8 +438,8 @@ struct ocr_session {
     void* work = nullptr;
     size_t work_bytes = 0;
     float *rope = nullptr, *x = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
-    float *lm_part = nullptr, *at_part = nullptr;
-    uint32_t *lm_done = nullptr, *at_done = nullptr;
+    float* lm_part = nullptr;
+    uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
     int32_t* hist = nullptr;
     int hist_cap = 0;
@@ -460,13 +464,36 @@ struct ocr_session {
 
 namespace {
 
+// the per-dispatch profiler: an event after every launch, with the kernel's name, layer and algorithmic bytes
+struct Prof {
+    cudaStream_t st = nullptr;
+    std::vector<cudaEvent_t> ev;
+    std::vector<ocr_kernel_time> rec;
+    std::vector<int> pos;  // host positions of the active slots (the attention's key counts)
+    void mark(const char* name, int layer, double bytes) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, st);
+        ev.push_back(e);
+        ocr_kernel_time k{};
+        snprintf(k.name, sizeof(k.name), "%s", name);
+        k.layer = layer;
+        k.bytes = bytes;
+        rec.push_back(k);
+    }
+};
+
+double mat_bytes(const QMat& w) { return (double)w.rows * w.stride; }
+
 // one decode step of every active slot: 5 kernels per layer + the LM head (with the choice when sample)
-void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp) {
+void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof = nullptr) {
     const ocr_model* m = s->m;
     const auto& c = m->cfg;
     ocr_ctx* ctx = s->ctx;
     cudaStream_t st = ctx->stream;
-    const bool pdl = ctx->pdl;
+    // programmatic dependent launch chains each kernel to the one before it in the stream; the profiler's events
+    // between launches would break that chain, so a profiled step launches without it
+    const bool pdl = ctx->pdl && !prof;
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
         MvArgs q;
@@ -487,6 +514,8 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
             q.x = s->x;
         }
         launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
+        const double nact = prof ? (double)prof->pos.size() : 0.0;
+        if (prof) prof->mark("qkv (norm + q|k|v)", l, mat_bytes(L.qkv) + nact * (c.dim * 8.0 + s->qkv_w * 4.0));
 
         AttnArgs a;
         a.qkv = s->qkv;
@@ -504,13 +533,16 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         a.splits = s->splits;
         a.eps = c.eps;
         a.scale = 1.0f / sqrtf((float)c.d_head);
-        a.part = s->at_part;
-        a.done = s->at_done;
         a.out = s->attn;
         a.out_stride = s->qd;
         a.nb = s->B;
         a.err = ctx->d_err;
         launch_attention_decode(st, a, pdl);
+        if (prof) {
+            double kv = 0;
+            for (int p : prof->pos) kv += (double)(p + 1) * c.n_kv * 128 * 2 * 2;
+            prof->mark("attention (split-KV)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
+        }
 
         MvArgs o;
         o.w = L.o;
@@ -522,6 +554,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         o.nb = s->B;
         o.active = s->active;
         launch_matvec(st, o, ctx->num_sms, pdl);
+        if (prof) prof->mark("o (+ residual)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
 
         MvArgs f;
         f.w = L.gu;
@@ -535,6 +568,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         f.nb = s->B;
         f.active = s->active;
         launch_matvec(st, f, ctx->num_sms, pdl);
+        if (prof) prof->mark("gate|up + swiglu", l, mat_bytes(L.gu) + nact * (c.dim * 8.0 + c.n_ff * 4.0));
 
         MvArgs dn;
         dn.w = L.down;
@@ -546,6 +580,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         dn.nb = s->B;
         dn.active = s->active;
         launch_matvec(st, dn, ctx->num_sms, pdl);
+        if (prof) prof->mark("down (+ residual)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
     }
     MvArgs lm;
     lm.w = m->tok;
@@ -577,6 +612,8 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     lm.lm.nb = s->B;
     lm.lm.err = ctx->d_err;
     launch_matvec(st, lm, ctx->num_sms, pdl);
+    if (prof)
+        prof->mark("lm head (+ choice)", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));
 }
 
 // rope_table (text.rs:132-142): theta = (f32)pos * base^(-2i/d) in f32, (cos, sin) by the host libm
@@ -826,8 +863,10 @@ ocr_status ocr_ctx_create(int device, ocr_ctx** out) {
     return OCR_OK;
 }
 
-ocr_status ocr_ctx_destroy(ocr_ctx* c) {
-    if (!c) return OCR_OK;
+// Handles may be released in any order (a garbage collector's, say): a context lives while a model made in it does,
+// a model while a session of it does; each destroy call releases the caller's reference.
+static void ctx_release(ocr_ctx* c) {
+    if (--c->refs > 0) return;
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     if (c->op_scratch) cudaFree(c->op_scratch);
@@ -836,6 +875,10 @@ ocr_status ocr_ctx_destroy(ocr_ctx* c) {
     if (c->d_err) cudaFree(c->d_err);
     cudaStreamDestroy(c->stream);
     delete c;
+}
+
+ocr_status ocr_ctx_destroy(ocr_ctx* c) {
+    if (c) ctx_release(c);
     return OCR_OK;
 }
 
@@ -959,12 +1002,18 @@ ocr_status ocr_model_checksum(const ocr_model* m, uint64_t* out) {
     return OCR_OK;
 }
 
-ocr_status ocr_model_destroy(ocr_model* m) {
-    if (!m) return OCR_OK;
-    cudaSetDevice(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
-    dfree(m->mem, m->mem_bytes, &m->ctx->mem_weights);
+static void model_release(ocr_model* m) {
+    if (--m->refs > 0) return;
+    ocr_ctx* ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    dfree(m->mem, m->mem_bytes, &ctx->mem_weights);
     delete m;
+    ctx_release(ctx);
+}
+
+ocr_status ocr_model_destroy(ocr_model* m) {
+    if (m) model_release(m);
     return OCR_OK;
 }
 
@@ -973,11 +1022,11 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const auto& c = m->cfg;
     if (n_ctx < 1 || batch < 1) return fail(OCR_ERR_ARG, "n_ctx and batch must be >= 1");
     if (n_ctx > c.n_ctx_train) return fail(OCR_ERR_ARG, std::to_string(n_ctx) + " positions asked, the model was trained on " + std::to_string(c.n_ctx_train));
-    if (n_ctx > 256 * 192) return fail(OCR_ERR_ARG, "n_ctx above 49152: the decode attention splits a context into at most 256 ranges of 192 keys");
     ocr_ctx* ctx = m->ctx;
     OCR_CUDA(cudaSetDevice(ctx->device));
     auto* s = new ocr_session;
     s->m = m;
+    m->refs++;
     s->ctx = ctx;
     s->n_ctx = n_ctx;
     s->B = batch;
@@ -999,9 +1048,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
     const size_t o_logits = p.take((size_t)batch * c.n_vocab * 4);
     const size_t o_lmp = p.take(((size_t)batch * lm_grid * 2 + batch) * 4);
-    const size_t o_atp = p.take((size_t)batch * c.n_head * s->splits * 130 * 4);
     const size_t o_lmd = p.take((size_t)(batch + 64) * 4);
-    const size_t o_atd = p.take((size_t)batch * c.n_kv * 4);
     const size_t o_state = p.take((size_t)batch * 4 * 4);
     if (e == cudaSuccess) e = dalloc(&s->work, p.off, &ctx->mem_work);
     if (e != cudaSuccess) {
@@ -1017,9 +1064,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     s->g = (float*)(w + o_g);
     s->logits = (float*)(w + o_logits);
     s->lm_part = (float*)(w + o_lmp);
-    s->at_part = (float*)(w + o_atp);
     s->lm_done = (uint32_t*)(w + o_lmd);
-    s->at_done = (uint32_t*)(w + o_atd);
     s->pos = (int32_t*)(w + o_state);
     s->len = s->pos + batch;
     s->tok = s->len + batch;
@@ -1056,7 +1101,9 @@ ocr_status ocr_session_destroy(ocr_session* s) {
     if (s->pf) dfree(s->pf, s->pf_bytes, &ctx->mem_work);
     if (s->h_ids) cudaFreeHost(s->h_ids);
     for (cudaEvent_t e : s->step_ev) cudaEventDestroy(e);
+    ocr_model* m = s->m;
     delete s;
+    model_release(m);
     return OCR_OK;
 }
 
@@ -1167,6 +1214,53 @@ ocr_status ocr_step(ocr_session* s, const int32_t* tok, float* logits_out) {
             s->n_past[b] += 1;
             s->has_logits[b] = 1;
         }
+    return OCR_OK;
+}
+
+ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time* out, int cap, int* n) {
+    if (!s || !tok || !out || !n) return fail(OCR_ERR_ARG, "null argument");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    std::vector<int32_t> act(s->B), pos(s->B);
+    Prof prof;
+    for (int b = 0; b < s->B; b++) {
+        if (tok[b] >= c.n_vocab) return fail(OCR_ERR_ARG, "token " + std::to_string(tok[b]) + " is outside the vocabulary");
+        act[b] = tok[b] >= 0;
+        pos[b] = s->n_past[b];
+        if (act[b] && s->n_past[b] + 1 > s->n_ctx) return fail(OCR_ERR_STATE, "slot " + std::to_string(b) + ": the session is full");
+        if (act[b]) prof.pos.push_back(s->n_past[b]);
+    }
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    OCR_CUDA(cudaMemcpyAsync(s->tok, tok, s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    prof.st = st;
+    cudaEvent_t e0;
+    OCR_CUDA(cudaEventCreate(&e0));
+    OCR_CUDA(cudaEventRecord(e0, st));
+    record_step(s, false, 1.0f, 1, 0, 0.0f, &prof);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaEvent_t prev = e0;
+    const int k = std::min<int>(cap, (int)prof.rec.size());
+    for (int i = 0; i < (int)prof.rec.size(); i++) {
+        float ms = 0.0f;
+        if (e == cudaSuccess) cudaEventElapsedTime(&ms, prev, prof.ev[i]);
+        prof.rec[i].us = ms * 1000.0f;
+        if (i < k) out[i] = prof.rec[i];
+        prev = prof.ev[i];
+    }
+    for (cudaEvent_t ev : prof.ev) cudaEventDestroy(ev);
+    cudaEventDestroy(e0);
+    if (e != cudaSuccess) return cuda_fail(e, "ocr_profile_step");
+    OCR_TRY(check_device_error(ctx));
+    for (int b = 0; b < s->B; b++)
+        if (act[b]) {
+            s->n_past[b] += 1;
+            s->has_logits[b] = 1;
+        }
+    *n = k;
     return OCR_OK;
 }
 
@@ -1346,12 +1440,10 @@ ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_
     OCR_CUDA(cudaSetDevice(ctx->device));
     AttnArgs a;
     a.splits = attention_splits(ctx->num_sms, 1, n_kv, n_ctx);
-    const size_t o_part = 256, o_done = o_part + (size_t)n_head * a.splits * 130 * 4 + 256;
-    OCR_TRY(ensure_op_scratch(ctx, o_done + (size_t)n_kv * 4 + 256));
+    OCR_TRY(ensure_op_scratch(ctx, 256));
     char* w = (char*)ctx->op_scratch;
     cudaStream_t st = ctx->stream;
     OCR_CUDA(cudaMemcpyAsync(w, &pos, 4, cudaMemcpyHostToDevice, st));
-    OCR_CUDA(cudaMemsetAsync(w + o_done, 0, (size_t)n_kv * 4, st));
     a.qkv = d_qkv;
     a.qkv_stride = (n_head + 2 * n_kv) * 128;
     a.q_norm = d_q_norm;
@@ -1365,8 +1457,6 @@ ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_
     a.n_ctx = n_ctx;
     a.eps = eps;
     a.scale = 1.0f / sqrtf(128.0f);
-    a.part = (float*)(w + o_part);
-    a.done = (uint32_t*)(w + o_done);
     a.out = d_out;
     a.out_stride = n_head * 128;
     a.nb = 1;

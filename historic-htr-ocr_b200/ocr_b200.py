@@ -43,6 +43,10 @@ class SamplerCfg(C.Structure):
     _fields_ = [("rp", C.c_float), ("window", C.c_int32), ("fp", C.c_float), ("max_new", C.c_int32)]
 
 
+class KernelTime(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("layer", C.c_int32), ("us", C.c_float), ("bytes", C.c_double)]
+
+
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32)
 
 _P = C.c_void_p
@@ -70,6 +74,7 @@ _SIGS = {
     "ocr_decode": (C.c_int, [_P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, TOKEN_CB, _P, _P,
                              C.POINTER(C.c_int)]),
     "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
+    "ocr_profile_step": (C.c_int, [_P, _P, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
     "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
     "ocr_gguf_open_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
@@ -335,6 +340,15 @@ class Session:
         _check(lib().ocr_decode(self.h, slot, C.byref(sc), _ptr(h) if len(h) else None, len(h), cb, None,
                                 _ptr(out), C.byref(n)))
         return out[: n.value].tolist()
+
+    def profile_step(self, tokens: Sequence[int]) -> list[dict]:
+        """one eager decode step with an event after every kernel: [{name, layer, us, bytes}] (OCR_WGPU_PROFILE)"""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = (KernelTime * 1024)()
+        n = C.c_int(0)
+        _check(lib().ocr_profile_step(self.h, _ptr(t), out, 1024, C.byref(n)))
+        return [dict(name=out[i].name.decode(), layer=out[i].layer, us=out[i].us, bytes=out[i].bytes)
+                for i in range(n.value)]
 
     def decode_batch(self, preset: Preset, histories: np.ndarray, max_new: Optional[int] = None) -> np.ndarray:
         sc = preset.sampler(max_new)

@@ -58,6 +58,8 @@ const char* ocr_version(void);
 
 /* ---- context: one device, one stream, the device arena (replaces Gpu::create, gpu.rs:1172-1324) ---------------- */
 ocr_status ocr_ctx_create(int device, ocr_ctx** out);
+/* releases the caller's handle. Destroy calls may come in any order: a context stays alive while a model made in it
+ * does, a model while one of its sessions does; the last release frees. No handle is used after its own destroy. */
 ocr_status ocr_ctx_destroy(ocr_ctx* ctx);
 /* wait for everything queued on the context's stream; returns OCR_ERR_DEVICE if a kernel flagged an error */
 ocr_status ocr_ctx_sync(ocr_ctx* ctx);
@@ -110,6 +112,19 @@ ocr_status ocr_step(ocr_session* s, const int32_t* tok, float* logits_out);
 typedef int (*ocr_token_cb)(void* user, int32_t token);
 ocr_status ocr_decode(ocr_session* s, int slot, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
                       ocr_token_cb on_token, void* user, int32_t* ids_out, int* n_out);
+
+/* the per-dispatch profiler (OCR_WGPU_PROFILE's role, gpu.rs:1006-1016, 1416-1436): one decode step of every slot
+ * with tok[slot] >= 0 (at its n_past, like ocr_step, logits kept on the device), run eagerly with a CUDA event after
+ * each kernel. out[i] = that kernel's name, layer (-1 for the LM head), device microseconds from the previous event,
+ * and the algorithmic bytes it must move (weights read once, KV rows read, activations). The slots' positions
+ * advance as with ocr_step. cap entries at most; *n = the count. */
+typedef struct {
+    char name[32];
+    int32_t layer;
+    float us;
+    double bytes;
+} ocr_kernel_time;
+ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time* out, int cap, int* n);
 
 /* the same for every slot at once (batched decode; each slot its own history): history [batch][n_hist] (a shared
  * length), ids_out [batch][max_new]. All slots run max_new choices. */

@@ -152,6 +152,40 @@ def test_callback_stops_the_read(ocr, orc, ctx, tiny):
     assert got == full[:37] and seen == full[:37]
 
 
+def test_profile_step_matches_step(ocr, orc, ctx, tiny):
+    """the per-dispatch profiler runs the same step: 5 kernels per layer + the LM head, positive times, the slot
+    advances, and the logits it leaves equal a plain step's"""
+    om, gm = tiny
+    prompt = [int(t) for t in orc.fill_ids(12, 10, TINY["n_vocab"])]
+    a, b = gm.session(32), gm.session(32)
+    a.prefill(0, ids=prompt, logits=False)
+    b.prefill(0, ids=prompt, logits=False)
+    rec = a.profile_step([7])
+    assert len(rec) == 5 * TINY["n_layer"] + 1
+    assert [r["name"] for r in rec[:5]] == ["qkv (norm + q|k|v)", "attention (split-KV)", "o (+ residual)",
+                                            "gate|up + swiglu", "down (+ residual)"]
+    assert rec[-1]["layer"] == -1 and all(r["us"] > 0 and r["bytes"] > 0 for r in rec)
+    assert a.n_past(0) == b.n_past(0) + 1
+    lb = b.step([7])[0]
+    la = a.step([9])  # a's next step runs from the profiled step's state
+    lb2 = b.step([9])[0]
+    assert np.array_equal(la[0], lb2) and np.isfinite(lb).all()
+
+
+def test_handles_release_in_any_order(ocr, orc):
+    """a context outlives its handle while a model or session made in it lives (a garbage collector may release
+    them in any order): the session still steps after the context and model handles are gone"""
+    c = ocr.Context(0)
+    m = ocr.TextModel.synthetic(c, text_config(ocr, TINY), 31, 0.2, 1.0)
+    s = m.session(16)
+    s.prefill(0, ids=[1, 2, 3], logits=False)
+    c.close()
+    m.close()
+    lg = s.step([4])
+    assert np.isfinite(lg).all() and s.n_past(0) == 4
+    s.close()
+
+
 def test_session_errors(ocr, ctx, tiny):
     om, gm = tiny
     s = gm.session(30)
