@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1631,3 +1632,88 @@ ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------------------------------
+// the LM head + choice with no allocation
+// ---------------------------------------------------------------------------------------------------------------------
+// Some callers cannot let a library allocate device memory mid-run: a serving loop that plans every byte of HBM up
+// front and runs under a fixed budget, a caller whose allocator owns the device and forbids hidden cudaMalloc calls,
+// or a latency-critical path where cudaMalloc/cudaFree would synchronise the device. ocr_op_lm_head_sample grows a
+// per-context scratch buffer on its first call; this variant instead keeps its scratch (the CTAs' partial maxima and
+// the completion ticket) in a file-scope device array that exists from module load on, so the call allocates
+// nothing. The array is one per device: two calls that can run at the same time on one device (different contexts
+// or streams) race on it; calls queued on one context's stream are ordered and safe.
+namespace {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = 16384;  // partials of up to 2000 CTAs + the ticket
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[NOALLOC_MAX_DEVICES] = {};
+
+// the array's device address on `device`, looked up once per device with that device current (the first call on a
+// device does this setup — make it before any stream capture)
+ocr_status noalloc_scratch(int device, void** out) {
+    if (device < 0 || device >= NOALLOC_MAX_DEVICES) return fail(OCR_ERR_ARG, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return OCR_OK;
+}
+
+}  // namespace
+
+ocr_status ocr_op_lm_head_sample_noalloc(ocr_ctx* ctx, const uint8_t* d_w, int n_vocab, int dim, const float* d_x,
+                                         const float* d_norm_w, float eps, float rp, int window, int32_t* d_hist,
+                                         int32_t* d_len, int32_t* d_tok, float* d_logits) {
+    if (!ctx || !d_w || !d_x || !d_hist || !d_len || !d_tok) return fail(OCR_ERR_ARG, "null argument");
+    if (n_vocab < 1 || dim < 32 || dim % 32) return fail(OCR_ERR_ARG, "bad shape");
+    if ((uintptr_t)d_w & 15) return fail(OCR_ERR_ARG, "the rows must start 16-B aligned");
+    if (rp != 1.0f && !(std::isnormal(rp) && rp > 0.0f)) return fail(OCR_ERR_ARG, "the repetition penalty is no positive normal f32");
+    if (window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
+    const int grid = lm_head_grid(ctx->num_sms, n_vocab, dim);
+    const size_t o_done = ((size_t)grid * 2 + 1) * 4 + 256;  // partials, then the ticket on its own 256 B
+    if (o_done + 4 > NOALLOC_SCRATCH_BYTES)
+        return fail(OCR_ERR_ARG, "the LM head would run " + std::to_string(grid) + " CTAs; the static scratch holds the partials of at most " +
+                                     std::to_string((NOALLOC_SCRATCH_BYTES - 264) / 8));
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    void* scratch = nullptr;
+    OCR_TRY(noalloc_scratch(ctx->device, &scratch));
+    char* w = (char*)scratch;
+    MvArgs a;
+    a.w.w = d_w;
+    a.w.rows = n_vocab;
+    a.w.cols = dim;
+    a.w.stride = q8_stride(dim);
+    a.x = d_x;
+    a.x_stride = dim;
+    a.nw = d_norm_w;
+    a.eps = eps;
+    a.nb = 1;
+    a.mode = MV_LMHEAD;
+    a.y = d_logits;
+    a.err = ctx->d_err;
+    a.lm.sample = 1;
+    a.lm.rp = rp;
+    a.lm.window = window;
+    a.lm.hist = d_hist;
+    a.lm.hist_cap = 1 << 30;
+    a.lm.len = d_len;
+    a.lm.tok = d_tok;
+    a.lm.part = (float*)w;
+    a.lm.done = (uint32_t*)(w + o_done);
+    a.lm.nb = 1;
+    a.lm.err = ctx->d_err;
+    // the completion ticket must start at zero (the kernel's last CTA resets it, but an earlier call that failed
+    // part way may not have); the partials need no clearing, every CTA writes its own before the ticket
+    OCR_CUDA(cudaMemsetAsync(a.lm.done, 0, 4, ctx->stream));
+    launch_matvec(ctx->stream, a, ctx->num_sms, false);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}

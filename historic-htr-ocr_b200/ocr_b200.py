@@ -95,6 +95,8 @@ _SIGS = {
     "ocr_op_matvec_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_int, _P, C.c_int]),
     "ocr_op_lm_head_sample": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P, _P, _P,
                                         _P]),
+    "ocr_op_lm_head_sample_noalloc": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P,
+                                                _P, _P, _P]),
     "ocr_op_attention_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                           _P]),
 }
@@ -475,6 +477,14 @@ def op_lm_head_sample(ctx: Context, d_w: int, n_vocab: int, dim: int, d_x: int, 
                       window: int, d_hist: int, d_len: int, d_tok: int, d_logits: Optional[int]) -> None:
     _check(lib().ocr_op_lm_head_sample(ctx.h, d_w, n_vocab, dim, d_x, d_norm_w, eps, rp, window, d_hist, d_len, d_tok,
                                        d_logits))
+
+
+def op_lm_head_sample_noalloc(ctx: Context, d_w: int, n_vocab: int, dim: int, d_x: int, d_norm_w: int, eps: float,
+                              rp: float, window: int, d_hist: int, d_len: int, d_tok: int,
+                              d_logits: Optional[int]) -> None:
+    """op_lm_head_sample with its scratch in a static device array: the call allocates no device memory"""
+    _check(lib().ocr_op_lm_head_sample_noalloc(ctx.h, d_w, n_vocab, dim, d_x, d_norm_w, eps, rp, window, d_hist, d_len,
+                                               d_tok, d_logits))
 
 
 def op_attention_decode(ctx: Context, d_qkv: int, d_q_norm: int, d_k_norm: int, d_rope: int, d_k: int, d_v: int,

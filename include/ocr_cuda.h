@@ -184,6 +184,14 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int co
 ocr_status ocr_op_lm_head_sample(ocr_ctx* ctx, const uint8_t* d_w, int n_vocab, int dim, const float* d_x,
                                  const float* d_norm_w, float eps, float rp, int window, int32_t* d_hist,
                                  int32_t* d_len, int32_t* d_tok, float* d_logits);
+/* ocr_op_lm_head_sample without any device allocation (no counterpart in the reference, which allocates through
+ * wgpu). The CTAs' partials and the completion ticket live in a 16 KB static device array, one per device, instead of
+ * the context's scratch: an LM head of more CTAs than it holds is refused with OCR_ERR_ARG. The first call on a device
+ * looks the array up (cudaGetSymbolAddress) — make it before any stream capture. Two calls that may overlap in time
+ * on one device (different contexts or streams) race on the array; calls on one context's stream are ordered. */
+ocr_status ocr_op_lm_head_sample_noalloc(ocr_ctx* ctx, const uint8_t* d_w, int n_vocab, int dim, const float* d_x,
+                                         const float* d_norm_w, float eps, float rp, int window, int32_t* d_hist,
+                                         int32_t* d_len, int32_t* d_tok, float* d_logits);
 /* decode attention of one token (qkv_post.wgsl + attn_decode.wgsl + attn_merge.wgsl): raw qkv [n_head + 2 n_kv][128]
  * f32 → per-head RMSNorm (q_norm / k_norm), RoPE NEOX at `pos` from the table rope [n_ctx][64][2], K/V rows `pos`
  * stored f16 into k_cache / v_cache ([n_kv][n_ctx][128] f16), then softmax(q k / sqrt(128)) v over keys 0…pos → out
