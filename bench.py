@@ -104,7 +104,7 @@ def peaks():
 # ---------------------------------------------------------------------------------------------------------------------
 def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
     """(mean µs per launch, algorithmic bytes per launch): W 151936 x 1024 q8_0 (165,306,368 B) + x (4 KB) + norm
-    (4 KB) + logits written (607,744 B) + the 64-token window; L2 flushed between launches (256 MB write)"""
+    (4 KB) + logits written (607,744 B) + the 64-token window; L2 flushed between launches (a 256 MB read)"""
     V, D = 151936, 1024
     g = torch.Generator(device="cuda").manual_seed(1)
     stride = ocr.q8_row_bytes(D)
@@ -118,13 +118,12 @@ def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
     ln = torch.tensor([512], dtype=torch.int32, device="cuda")
     tok = torch.zeros(1, dtype=torch.int32, device="cuda")
     logits = torch.empty(V, device="cuda")
-    flush = torch.empty(flush_bytes // 4, device="cuda")
+    flush = torch.zeros(flush_bytes // 4, device="cuda")
     stream = torch.cuda.ExternalStream(ctx.stream())
     torch.cuda.synchronize()
     times = []
     for i in range(reps + 3):
-        flush.fill_(float(i))
-        torch.cuda.synchronize()
+        float(flush.sum())  # a read larger than L2 (a write would leave dirty lines to drain during the launch)
         ln.fill_(512)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -204,6 +203,8 @@ def run_ours(args):
     model = ocr.TextModel.synthetic(ctx, cfg, seed, 0.02, 0.02)
     B = 32 if args.config == 3 else 1
     prefix_len, new = (3072, 1024) if args.config == 3 else (PREFIX, NEW)
+    if args.tokens:
+        new = args.tokens
     sess = model.session(prefix_len + new, batch=B)
     for b in range(B):
         embd = ocr.gauss(ocr.substream(seed + b, 200000), prefix_len * 1024, 1.0).reshape(prefix_len, 1024)
@@ -247,10 +248,10 @@ def run_ours(args):
         times = t.numpy()
     dev_s, wall = float(times[0]), float(times[1])
     tokens = world * B * new * args.steps
-    # per step: the one-row prefill per slot (embed + 8 per layer + LM head), choice 0, then new - 1 decode steps
-    # of 5 kernels per layer + the fused LM head / choice
+    # per step: the one-row prefill per slot (a decode step of that slot: 5 kernels per layer + the LM head),
+    # choice 0, then new - 1 decode steps of 5 kernels per layer + the fused LM head / choice
     launches_per_token = CONFIG2["n_layer"] * 5 + 1
-    launches = args.steps * ((CONFIG2["n_layer"] * 8 + 2) * B + 1 + (new - 1) * launches_per_token)
+    launches = args.steps * (launches_per_token * B + 1 + (new - 1) * launches_per_token)
     out = None
     if rank == 0:
         classes = kernel_classes(sess, B, prefix_len, last_rows)
@@ -381,6 +382,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=[1, 2, 3], default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="decode this many tokens per step instead of the config's (short runs for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

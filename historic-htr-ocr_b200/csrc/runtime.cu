@@ -486,8 +486,10 @@ struct Prof {
 
 double mat_bytes(const QMat& w) { return (double)w.rows * w.stride; }
 
-// one decode step of every active slot: 5 kernels per layer + the LM head (with the choice when sample)
-void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof = nullptr) {
+// one decode step of every active slot: 5 kernels per layer + the LM head (with the choice when sample). The first
+// layer embeds the slots' tokens, or with x_given takes the rows already in s->x (Input::Embeddings rows).
+void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof = nullptr,
+                 bool x_given = false) {
     const ocr_model* m = s->m;
     const auto& c = m->cfg;
     ocr_ctx* ctx = s->ctx;
@@ -507,7 +509,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         q.active = s->active;
         q.mode = MV_STORE;
         q.x_stride = c.dim;
-        if (l == 0) {
+        if (l == 0 && !x_given) {
             q.tok = s->tok;
             q.emb = m->tok;
             q.x_out = s->x;
@@ -1124,6 +1126,40 @@ ocr_status ocr_session_rewind(ocr_session* s, int slot, int n_past) {
     return OCR_OK;
 }
 
+// A few rows (a prompt's tail, the bench's re-run of the last prefix row) are cheaper as decode steps of this slot
+// alone — 5 matvec / attention kernels per layer per row — than through the prefill GEMMs, whose tiles are sized for
+// hundreds of rows.
+constexpr int SHORT_PREFILL = 4;
+
+ocr_status prefill_short(ocr_session* s, int slot, const int32_t* ids, const float* embd, int n, float* logits_out) {
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    std::vector<int32_t> act(s->B, 0), pos(s->B, 0), tok(s->B, -1);
+    act[slot] = 1;
+    OCR_CUDA(cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    for (int i = 0; i < n; i++) {
+        const bool given = !ids || ids[i] < 0;
+        pos[slot] = s->n_past[slot] + i;
+        tok[slot] = given ? -1 : ids[i];
+        if (given)
+            OCR_CUDA(cudaMemcpyAsync(s->x + (size_t)slot * c.dim, embd + (size_t)i * c.dim, (size_t)c.dim * 4,
+                                     cudaMemcpyHostToDevice, st));
+        OCR_CUDA(cudaMemcpyAsync(s->tok, tok.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+        OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+        record_step(s, false, 1.0f, 1, 0, 0.0f, nullptr, given);
+        OCR_CUDA(cudaGetLastError());
+    }
+    if (logits_out)
+        OCR_CUDA(cudaMemcpyAsync(logits_out, s->logits + (size_t)slot * c.n_vocab, (size_t)c.n_vocab * 4,
+                                 cudaMemcpyDeviceToHost, st));
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    s->n_past[slot] += n;
+    s->has_logits[slot] = 1;
+    return OCR_OK;
+}
+
 ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float* embd, int n, float* logits_out) {
     if (!s) return fail(OCR_ERR_ARG, "null session");
     if (slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "slot out of range");
@@ -1139,6 +1175,7 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
     }
     if (any_embd && !embd) return fail(OCR_ERR_ARG, "embedding rows asked but embd is null");
     OCR_CUDA(cudaSetDevice(ctx->device));
+    if (n <= SHORT_PREFILL) return prefill_short(s, slot, ids, embd, n, logits_out);
     OCR_TRY(ensure_prefill(s, n));
     cudaStream_t st = ctx->stream;
     float* x = (float*)s->pf;

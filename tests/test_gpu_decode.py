@@ -138,6 +138,25 @@ def test_embedding_rows_and_batch_equal_single(ocr, orc, ctx, tiny):
         assert single == batch[b].tolist(), b
 
 
+def test_short_prefill_matches_oracle(ocr, orc, ctx, tiny):
+    """prompts of up to 4 rows run as decode steps of their slot: token and embedding rows after a long prefill, and
+    one row alone after a rewind (the benchmark's step) — logits as the oracle's prefill of the whole prompt"""
+    om, gm = tiny
+    dim = TINY["dim"]
+    rows = [int(t) for t in orc.fill_ids(14, 12, TINY["n_vocab"])]
+    ids = np.array(rows[:9] + [-1, rows[9], -1], np.int32)
+    embd = np.zeros((ids.size, dim), np.float32)
+    embd[ids < 0] = ocr.gauss(140, 2 * dim).reshape(-1, dim)
+    lo = om.session(32).prefill(ids, embd, ids.size)
+    gs = gm.session(32, batch=2)
+    gs.prefill(1, ids=ids[:9], embd=embd[:9], logits=False)  # slot 1: the other slot must stay untouched
+    lg = gs.prefill(1, ids=ids[9:], embd=embd[9:])
+    close_logits(lg, lo)
+    assert gs.n_past(1) == ids.size and gs.n_past(0) == 0
+    gs.rewind(1, ids.size - 1)
+    close_logits(gs.prefill(1, ids=ids[-1:], embd=embd[-1:]), lo)
+
+
 def test_callback_stops_the_read(ocr, orc, ctx, tiny):
     om, gm = tiny
     prompt = [int(t) for t in orc.fill_ids(9, 16, TINY["n_vocab"])]
