@@ -280,7 +280,9 @@ __device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a,
 }
 
 template <int NB, int W, int R>
-__global__ void __launch_bounds__((W + 1) * 32) k_mv(MvArgs a, int rpc, int ns) {
+// two CTAs per SM for the small matrices of one or two slots (the grid is sized for it; at most 112 registers);
+// wider slot batches keep their accumulators in registers at one CTA per SM
+__global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_mv(MvArgs a, int rpc, int ns) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + MAX_NS;
@@ -528,15 +530,17 @@ struct Geo {
 
 constexpr size_t SMEM_MAX = 220 * 1024;
 
-// streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 2 rows, a deep ring. Small matrices: about
-// two CTAs per SM, 8 consumer warps (x 2 rows for SwiGLU pairs, else 1), one or two stages each.
-static Geo geometry(const MvArgs& a, int nb_pass, int num_sms) {
+// streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 2 rows, a deep ring. Small matrices:
+// `per_sm` CTAs per SM (two when registers and shared memory allow), 8 consumer warps (x 2 rows for SwiGLU pairs,
+// else 1), one or two stages each. The grid is one wave: a CTA that cannot be resident with the others would stream
+// its rows after them.
+static Geo geometry(const MvArgs& a, int nb_pass, int num_sms, int per_sm = 2) {
     const int N = a.w.rows, K = a.w.cols, stride = a.w.stride;
     const int nch = (K + 511) / 512;
     const size_t xs = (size_t)nb_pass * nch * 512 * 4;
     Geo g;
     const bool big = (size_t)N * stride > (size_t)48 << 20;
-    const int target = big ? num_sms : 2 * num_sms;
+    const int target = big ? num_sms : per_sm * num_sms;
     if (big) {
         g.W = 16;
         g.R = 2;
@@ -569,15 +573,38 @@ int lm_head_grid(int num_sms, int n_vocab, int dim) {
 }
 
 template <int NB, int W, int R>
-static void launch_t(cudaStream_t st, const MvArgs& a, const Geo& g, bool pdl) {
-    auto kern = k_mv<NB, W, R>;
+static void configure_t() {
     static bool configured = false;
     if (!configured) {
+        auto kern = k_mv<NB, W, R>;
         cudaFuncAttributes fa;
         cudaFuncGetAttributes(&fa, kern);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
         configured = true;
     }
+}
+
+// CTAs of this instantiation resident per SM with a small matrix's shared memory (registers decide: the build's
+// count for the template), asked once
+template <int NB, int W, int R>
+static int per_sm_t() {
+    static int n = -1;
+    if (n < 0) {
+        configure_t<NB, W, R>();
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_mv<NB, W, R>, (W + 1) * 32, SMEM_MAX / 2) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            n = 1;
+        }
+        n = std::max(1, std::min(2, n));
+    }
+    return n;
+}
+
+template <int NB, int W, int R>
+static void launch_t(cudaStream_t st, const MvArgs& a, const Geo& g, bool pdl) {
+    auto kern = k_mv<NB, W, R>;
+    configure_t<NB, W, R>();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)g.grid, (unsigned)((a.nb + NB - 1) / NB), 1);
     cfg.blockDim = dim3((W + 1) * 32, 1, 1);
@@ -593,10 +620,16 @@ static void launch_t(cudaStream_t st, const MvArgs& a, const Geo& g, bool pdl) {
 
 template <int NB>
 static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
-    const Geo g = geometry(a, NB, num_sms);
-    if (g.W == 16) launch_t<NB, 16, 2>(st, a, g, pdl);
-    else if (g.R == 2) launch_t<NB, 8, 2>(st, a, g, pdl);
-    else launch_t<NB, 8, 1>(st, a, g, pdl);
+    Geo g = geometry(a, NB, num_sms);
+    if (g.W == 16) {
+        launch_t<NB, 16, 2>(st, a, g, pdl);
+    } else if (g.R == 2) {
+        if (per_sm_t<NB, 8, 2>() < 2) g = geometry(a, NB, num_sms, 1);
+        launch_t<NB, 8, 2>(st, a, g, pdl);
+    } else {
+        if (per_sm_t<NB, 8, 1>() < 2) g = geometry(a, NB, num_sms, 1);
+        launch_t<NB, 8, 1>(st, a, g, pdl);
+    }
 }
 
 void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {

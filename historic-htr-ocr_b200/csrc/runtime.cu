@@ -508,6 +508,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         q.nb = s->B;
         q.active = s->active;
         q.mode = MV_STORE;
+        q.err = ctx->d_err;
         q.x_stride = c.dim;
         if (l == 0 && !x_given) {
             q.tok = s->tok;
@@ -556,6 +557,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         o.mode = MV_ADD;
         o.nb = s->B;
         o.active = s->active;
+        o.err = ctx->d_err;
         launch_matvec(st, o, ctx->num_sms, pdl);
         if (prof) prof->mark("o (+ residual)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
 
@@ -570,6 +572,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         f.mode = MV_SWIGLU;
         f.nb = s->B;
         f.active = s->active;
+        f.err = ctx->d_err;
         launch_matvec(st, f, ctx->num_sms, pdl);
         if (prof) prof->mark("gate|up + swiglu", l, mat_bytes(L.gu) + nact * (c.dim * 8.0 + c.n_ff * 4.0));
 
@@ -582,6 +585,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         dn.mode = MV_ADD;
         dn.nb = s->B;
         dn.active = s->active;
+        dn.err = ctx->d_err;
         launch_matvec(st, dn, ctx->num_sms, pdl);
         if (prof) prof->mark("down (+ residual)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
     }
