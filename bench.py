@@ -248,13 +248,13 @@ def run_ours(args):
         times = t.numpy()
     dev_s, wall = float(times[0]), float(times[1])
     tokens = world * B * new * args.steps
-    # per step: the one-row prefill per slot (a decode step of that slot: 5 kernels per layer + the LM head),
-    # choice 0, then new - 1 decode steps of 5 kernels per layer + the fused LM head / choice
-    launches_per_token = CONFIG2["n_layer"] * 5 + 1
-    launches = args.steps * (launches_per_token * B + 1 + (new - 1) * launches_per_token)
     out = None
     if rank == 0:
         classes = kernel_classes(sess, B, prefix_len, last_rows)
+        # per step: the one-row prefill per slot (a decode step of that slot), choice 0, then new - 1 decode steps;
+        # a decode step's launches as the profiler counted them (kernels per layer + the fused LM head / choice)
+        launches_per_token = sum(k["launches"] for k in classes) // 4
+        launches = args.steps * (launches_per_token * B + 1 + (new - 1) * launches_per_token)
         roof = kernel_roofline(classes)
         lm_us, lm_bytes = lm_head_kernel(ocr, ctx, torch, 10)
         out = {

@@ -145,6 +145,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// pulls [src, src + bytes) into L2: no shared memory, no completion to wait for (16-B aligned, multiple of 16)
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // An L2 policy under which the lines a copy brings in are the first to go. Weights and KV rows are read once per
 // step and together exceed L2 many times over; streamed under this policy they leave the activations, norms, tables
 // and kernel code that every step touches resident.

@@ -5,22 +5,28 @@
 // Grid (CL, n_kv, slots) in thread-block clusters of CL CTAs: one cluster per (slot, kv head), CTA rank r owning a
 // contiguous key range [k0, k1) of the slot's pos + 1 keys (from the device-side position: one captured graph serves
 // every step). KV layout [slot][kv head][n_ctx][128] f16: a range is one contiguous run of K and one of V, moved into
-// shared memory in tiles of TILE keys by bulk-async copies on a ring of up to MAX_BUF tiles (96 KB: two CTAs per SM,
-// so every 16-CTA cluster of a one-token step is resident at once). The first ring's copies are issued before the
-// kernel waits on its predecessor — no kernel of this step writes rows below pos; the row at pos is computed here
-// (one warp per head: RMSNorm by a warp reduction, RoPE in registers), stored to the cache and to an extra shared row
-// read in place of its tile row. The keys are taken in rounds of the resident tiles; each of the 8 warps owns a
-// contiguous eighth of a round: scores by 8 lanes per key (16 dims each), one online-softmax update per round
-// (running max, sum, output rescale) and P·V with lane = 4 dims. The block meets only when the ring wraps. The warps'
-// states merge in shared memory into the CTA's (m, l, o); the cluster's CL
-// partials merge through distributed shared memory — each CTA folds a slice of the outputs by reading the other CTAs'
-// partials — between two cluster barriers: no global round trip, no atomic. mbarrier waits are bounded; a warp whose
-// wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets every barrier.
+// shared memory in tiles of TILE keys by bulk-async copies on a ring of up to MAX_BUF tiles (two CTAs per SM, so
+// every 16-CTA cluster of a one-token step is resident at once). The first ring's copies are issued before the kernel
+// waits on its predecessor — no kernel of this step writes rows below pos; the row at pos is computed here (one warp
+// per head: RMSNorm by a warp reduction, RoPE in registers), stored to the cache and to an extra shared row read in
+// place of its tile row. The keys are taken in rounds of the resident tiles; each of the 8 warps owns a contiguous
+// eighth of a round: scores by 8 lanes per key (16 dims each), one online-softmax update per round (running max, sum,
+// output rescale) and P·V with lane = 4 dims. The block meets only when the ring wraps. The warps' states merge in
+// shared memory into the CTA's (o, m, l); the cluster's CL partials merge through distributed shared memory, with no
+// global round trip and no atomic.
+//
+// Two endings. Unfused (the op entry point): each CTA merges a 1/CL slice of the output and stores it. Fused (the
+// decode step): a reduce-scatter (each CTA merges its slice from float4 copies of the ranks' partials) and an
+// all-gather (every CTA reads every slice) leave the group's whole output in every CTA, which multiplies it by its
+// dim/CL rows of W_o's slice for this kv head (fetched before the dependency wait) into opart[b][j] — the o-projection
+// as n_kv per-head partial products, summed in a fixed order by the next kernel. mbarrier waits are bounded; a warp
+// whose wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets every barrier.
 #include <cooperative_groups.h>
 
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "qdot.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -29,19 +35,21 @@ namespace ocr {
 constexpr int AT_THREADS = 256;
 constexpr int NW = AT_THREADS / 32;  // warps per CTA
 constexpr int HD = 128;              // head dim (TextConfig::from_gguf requires 128, text.rs:57-60)
-constexpr int TILE = 64;             // keys per tile (K + V: 32 KB)
-constexpr int MAX_BUF = 3;           // ring depth: at most 96 KB, so two CTAs share an SM
+constexpr int TILE = 80;             // keys per tile (K + V: 40 KB; two cover a 16-way split of 2560 keys)
+constexpr int MAX_BUF = 2;           // ring depth: at most 80 KB, so two CTAs share an SM
 constexpr int KPW = (MAX_BUF * TILE + NW - 1) / NW;  // keys per warp per round (one per lane)
+constexpr int PW = HD + 4;  // a head's partial: o[128], m, l, two floats of pad (whole float4s)
 
 template <int G, int CL>
-__global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf) {
+__global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf, int smem) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ __align__(8) uint64_t full[MAX_BUF];
+    __shared__ __align__(8) uint64_t obar;  // W_o slice chunks (fused o-projection)
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float scw[NW][G][KPW];  // per warp: the round's scores, then probabilities
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wo[NW][G][HD];
-    __shared__ float part[G][HD + 2];  // this CTA's (m, l, o[128]) per head, read by the cluster
+    __shared__ __align__(16) float part[G][PW];  // this CTA's (o[128], m, l, pad) per head, read by the cluster
     cg::cluster_group cluster = cg::this_cluster();
     const int b = blockIdx.z, j = blockIdx.y, sp = blockIdx.x, t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
@@ -67,6 +75,18 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     __half* Ks = reinterpret_cast<__half*>(sm);
     __half* Vs = Ks + (size_t)(ring + 1) * HD;
 
+    // the fused o-projection's W_o rows [row0, row0 + rpc) of slice j, in chunks of `ro` rows in the region after the
+    // KV ring (`smem` bytes of dynamic shared memory in all)
+    const int NCOL = G * HD, ostride = q8_stride(NCOL);
+    const int rpc = a.wo ? a.dim / CL : 0, row0 = sp * rpc;
+    const int kv_bytes = 2 * (ring + 1) * HD * 2;
+    uint8_t* wsm = sm + kv_bytes;
+    const int ro = rpc ? max(1, min(rpc, (smem - kv_bytes) / ostride)) : 1;
+    auto issue_o = [&](int c0) {
+        const uint32_t bytes = (uint32_t)(min(ro, rpc - c0) * ostride);
+        mbar_expect_tx(&obar, bytes);
+        bulk_g2s(wsm, a.wo + ((size_t)j * a.dim + row0 + c0) * ostride, bytes, &obar);
+    };
     // rows [ts, min(te, pos)) of tile tl (the row at pos is not in the cache yet)
     auto issue = [&](int tl) {
         const int slot = tl % n_buf, ts = k0 + tl * TILE, ce = min(min(k1, ts + TILE), pos);
@@ -82,9 +102,12 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     };
     if (t == 0) {
         for (int i = 0; i < n_buf; i++) mbar_init(&full[i], 1);
+        mbar_init(&obar, 1);
         mbar_fence_init();
         for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl);
+        if (rpc > 0) issue_o(0);  // constant weights: fetched before the wait
         pdl_trigger();
+        l2_next(a.next, (b * gridDim.y + j) * CL + sp, CL * gridDim.y * gridDim.z);
     }
     // warp h prepares q head h (h < G) or the new k / v head (h = G), warps taking heads h, h + NW; lane holds dims
     // d0, d0 + 1 and their RoPE partners 64 + d0, 64 + d0 + 1. Not written by this step, so loaded before the dependency wait: the norm
@@ -277,38 +300,126 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
                 L = fmaf(wl[w][g], e, L);
                 O = fmaf(wo[w][g][d], e, O);
             }
-        part[g][2 + d] = O;
+        part[g][d] = O;
         if (d == 0) {
-            part[g][0] = (ok && L > 0.0f) ? M : -INFINITY;
-            part[g][1] = ok ? L : 0.0f;
+            part[g][HD] = (ok && L > 0.0f) ? M : -INFINITY;
+            part[g][HD + 1] = ok ? L : 0.0f;
         }
     }
     // ---- the cluster's merge through distributed shared memory ----
     cluster.sync();
-    constexpr int PER = G * HD / CL;  // outputs this CTA folds
-    for (int q0 = t; q0 < PER; q0 += AT_THREADS) {
-        const int q = sp * PER + q0, g = q / HD, d = q % HD;
-        float ms[CL], ls[CL], os[CL];
+    constexpr int PER = G * HD / CL;  // the slice of the group's outputs this CTA merges
+    const int q0 = sp * PER;
+    if (rpc == 0) {
+        // the attention output: this CTA's slice, from the CL partials
+        for (int i = t; i < PER; i += AT_THREADS) {
+            const int q = q0 + i, g = q / HD, d = q % HD;
+            float ms[CL], ls[CL], os[CL];
 #pragma unroll
-        for (int r = 0; r < CL; r++) {
-            const float* rp = cluster.map_shared_rank(&part[g][0], r);
-            ms[r] = rp[0];
-            ls[r] = rp[1];
-            os[r] = rp[2 + d];
+            for (int r = 0; r < CL; r++) {
+                const float* rp = cluster.map_shared_rank(&part[g][0], r);
+                os[r] = rp[d];
+                ms[r] = rp[HD];
+                ls[r] = rp[HD + 1];
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < CL; r++) M = fmaxf(M, ms[r]);
+            float L = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int r = 0; r < CL; r++) {
+                const float e = ms[r] == -INFINITY ? 0.0f : expf(ms[r] - M);
+                L = fmaf(ls[r], e, L);
+                O = fmaf(os[r], e, O);
+            }
+            a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
         }
+        cluster.sync();  // no CTA leaves while another still reads its partial
+        return;
+    }
+    // fused: reduce-scatter (this CTA merges its slice from the ranks' partials, copied in float4s), then all-gather
+    // (every CTA reads every slice) — the group's whole output in every CTA, the o-projection's input. Scratch in the
+    // idle KV ring: the ranks' slice values [CL][PER], their (m, l) [CL][G][2], this CTA's merged slice [PER].
+    float* rsl = reinterpret_cast<float*>(sm);
+    float* rml = rsl + CL * PER;
+    float* mine = rml + CL * G * 2;
+    for (int i = t; i < CL * (PER / 4); i += AT_THREADS) {
+        const int r = i / (PER / 4), q = q0 + 4 * (i % (PER / 4));
+        const float* rp = cluster.map_shared_rank(&part[0][0], r);
+        reinterpret_cast<float4*>(rsl)[i] = *reinterpret_cast<const float4*>(rp + (q / HD) * PW + q % HD);
+    }
+    for (int i = t; i < CL * G; i += AT_THREADS) {
+        const float* rp = cluster.map_shared_rank(&part[0][0], i / G);
+        reinterpret_cast<float2*>(rml)[i] = *reinterpret_cast<const float2*>(rp + (i % G) * PW + HD);
+    }
+    __syncthreads();
+    for (int i = t; i < PER; i += AT_THREADS) {
+        const int g = (q0 + i) / HD;
         float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < CL; r++) M = fmaxf(M, ms[r]);
+        for (int r = 0; r < CL; r++) M = fmaxf(M, rml[(r * G + g) * 2]);
         float L = 0.0f, O = 0.0f;
 #pragma unroll
         for (int r = 0; r < CL; r++) {
-            const float e = ms[r] == -INFINITY ? 0.0f : expf(ms[r] - M);
-            L = fmaf(ls[r], e, L);
-            O = fmaf(os[r], e, O);
+            const float m = rml[(r * G + g) * 2];
+            const float e = m == -INFINITY ? 0.0f : expf(m - M);
+            L = fmaf(rml[(r * G + g) * 2 + 1], e, L);
+            O = fmaf(rsl[r * PER + i], e, O);
         }
-        a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
+        mine[i] = O / L;
     }
-    cluster.sync();  // no CTA leaves while another still reads its partial
+    cluster.sync();  // every slice merged; no rank reads `part` any more
+    float* att = &wo[0][0][0];  // the warps' partial outputs are folded into part: reuse
+    const int nch = (NCOL + 511) / 512;
+    for (int i = t; i < NCOL / 4; i += AT_THREADS) {
+        const int q = 4 * i;
+        const float* rp = cluster.map_shared_rank(mine, q / PER);
+        *reinterpret_cast<float4*>(&att[xs_index(0, nch, q)]) = *reinterpret_cast<const float4*>(rp + q % PER);
+    }
+    // no remote reads of this CTA's shared memory follow: arrive now, wait before leaving
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    __syncthreads();
+    // 8 lanes per row (16-column pieces lane&7, +8, …: a row's 128 B per quarter-warp), 4 rows per warp
+    const uint64_t* ap = reinterpret_cast<const uint64_t*>(att);
+    float* op = a.opart + ((long)b * a.n_kv + j) * a.dim + row0;
+    const int l8 = lane & 7;
+    for (int c0 = 0, k = 0; c0 < rpc; c0 += ro, k++) {
+        const int nr = min(ro, rpc - c0);
+        const bool got = __all_sync(FULL, mbar_wait(&obar, k & 1, a.err));
+        if (got) {
+            for (int base = warp * 4; base < nr; base += NW * 4) {
+                const int rr = base + (lane >> 3);
+                float acc = 0.0f;
+                if (rr < nr) {
+                    const uint8_t* row = wsm + (size_t)rr * ostride;
+                    for (int pc = l8; pc < NCOL / 16; pc += 8) {
+                        const uint4 wq = *reinterpret_cast<const uint4*>(row + pc * 16);
+                        const float dsc = __half2float(reinterpret_cast<const __half*>(row + NCOL)[pc >> 1]);
+                        uint64_t xp[8];
+                        const int xb = ((pc >> 5) * 128 + (pc & 31)) * 2;  // in f32 pairs
+#pragma unroll
+                        for (int jj = 0; jj < 4; jj++) {
+                            xp[2 * jj] = ap[xb + jj * 64];
+                            xp[2 * jj + 1] = ap[xb + jj * 64 + 1];
+                        }
+                        acc = fmaf(dot16x2(wq, xp), dsc, acc);
+                    }
+                }
+                acc += __shfl_xor_sync(FULL, acc, 4);
+                acc += __shfl_xor_sync(FULL, acc, 2);
+                acc += __shfl_xor_sync(FULL, acc, 1);
+                if (l8 == 0 && rr < nr) op[c0 + rr] = acc;
+            }
+        }
+        if (c0 + ro < rpc) {
+            __syncthreads();  // every warp is done with the chunk
+            if (t == 0) {
+                fence_proxy_async();  // the chunk's generic reads before the copy engine's writes
+                issue_o(c0 + ro);
+            }
+        }
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx) {
@@ -324,6 +435,7 @@ int attention_splits(int num_sms, int nb, int n_kv, int n_ctx) {
 // the ring depth: the tiles of the longest range, at most MAX_BUF, and no more than keeps a CTA within half an SM's
 // shared memory (two CTAs per SM: a cluster of 16 then needs 8 SMs of a GPC)
 static int ring_depth(int n_ctx, int cl, int static_bytes) {
+    // static_bytes: the kernel's static shared memory plus any dynamic region besides the ring
     const int tiles = ((n_ctx + cl - 1) / cl + TILE - 1) / TILE;
     const int fit = (113 * 1024 - static_bytes - 2 * HD * 2) / (2 * TILE * HD * 2);
     return std::max(1, std::min(std::min(tiles, MAX_BUF), fit));
@@ -341,11 +453,13 @@ static int static_smem() {
 
 template <int G, int CL>
 static cudaLaunchConfig_t config_t(cudaStream_t st, const AttnArgs& a, cudaLaunchAttribute* attr, int* n_buf) {
-    *n_buf = ring_depth(a.n_ctx, CL, static_smem<G, CL>());
+    // the fused o-projection's W_o region after the ring: up to 64 rows of the CTA's slice rows
+    const size_t wo_bytes = a.wo ? (size_t)std::min(a.dim / CL, 64) * q8_stride(G * HD) : 0;
+    *n_buf = ring_depth(a.n_ctx, CL, static_smem<G, CL>() + (int)wo_bytes);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)CL, (unsigned)a.n_kv, (unsigned)a.nb);
     cfg.blockDim = dim3(AT_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = (size_t)2 * (*n_buf * TILE + 1) * HD * 2;
+    cfg.dynamicSmemBytes = (size_t)2 * (*n_buf * TILE + 1) * HD * 2 + wo_bytes;
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = CL;
@@ -370,18 +484,24 @@ static bool usable_t(cudaStream_t st, const AttnArgs& a) {
         configured = true;
     }
     if (CL <= 8) return true;
-    static int usable[MAX_BUF] = {-1, -1, -1};  // per ring depth, asked once
+    // asked once per dynamic shared memory size
+    static size_t keys[8];
+    static bool vals[8];
+    static int n_keys = 0;
     cudaLaunchAttribute attr[2];
     int n_buf = 1, n = 0;
     cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
-    if (usable[n_buf - 1] < 0) {
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
-            cudaGetLastError();
-            n = 0;
-        }
-        usable[n_buf - 1] = n >= 1;
+    for (int i = 0; i < n_keys; i++)
+        if (keys[i] == cfg.dynamicSmemBytes) return vals[i];
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
     }
-    return usable[n_buf - 1] == 1;
+    if (n_keys < 8) {
+        keys[n_keys] = cfg.dynamicSmemBytes;
+        vals[n_keys++] = n >= 1;
+    }
+    return n >= 1;
 }
 
 template <int G, int CL>
@@ -390,7 +510,7 @@ static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
     int n_buf = 1;
     cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
     cfg.numAttrs = pdl ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, k_attn_decode<G, CL>, a, n_buf);
+    cudaLaunchKernelEx(&cfg, k_attn_decode<G, CL>, a, n_buf, (int)cfg.dynamicSmemBytes);
 }
 
 template <int G>

@@ -14,6 +14,7 @@
 // epilogue: store, residual add, silu(gate) * up over interleaved gate/up rows, or the LM head's choice.
 // Every wait is bounded (mbar_wait → DEV_TIMEOUT); no spin on another CTA.
 #include "kernels.cuh"
+#include "qdot.cuh"
 
 namespace ocr {
 
@@ -136,55 +137,6 @@ __device__ void choice_finish(const float* bv_sm, const uint32_t* bi_sm, int nb,
 constexpr int MAX_NS = 16;
 constexpr int SM_HEAD = 256;  // mbarriers full[MAX_NS], empty[MAX_NS]
 
-// ---- packed f32x2 arithmetic (sm_100): two lanes of f32 per instruction ------------------------------------------
-__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ float2 upk2(uint64_t v) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-    return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
-// 16 int8 quants (one 16-B load) · 16 activations (8 f32 pairs): each byte, biased to q + 128, is placed in the
-// mantissa of 2^23 by one byte permute and 2^23 + 128 is subtracted pairwise (exact: integers below 2^24); the pairs
-// then multiply-accumulate packed, two accumulators deep. Returns the f32 dot.
-__device__ __forceinline__ float dot16x2(const uint4 w, const uint64_t* xp) {
-    const uint64_t bias = pk2(-8388736.0f, -8388736.0f);
-    const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
-    uint64_t a0 = 0, a1 = 0;  // +0.0f pairs
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const uint32_t u = wv[k];
-        const uint64_t p01 = add2(pk2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
-                                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7441))), bias);
-        const uint64_t p23 = add2(pk2(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
-                                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7443))), bias);
-        a0 = fma2(p01, xp[2 * k], a0);
-        a1 = fma2(p23, xp[2 * k + 1], a1);
-    }
-    const float2 s = upk2(add2(a0, a1));
-    return s.x + s.y;
-}
-
-// the smem float index of x[s][c] in the lane-blocked layout
-__device__ __forceinline__ int xs_index(int s, int nch, int c) {
-    const int i = c >> 9, w = c & 511, l = w >> 4, j = w & 15;
-    return ((((s * nch + i) * 4 + (j >> 2)) * 32 + l) << 2) + (j & 3);
-}
-
 // sum over the `nthr` consumer threads (barrier 1)
 __device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
     v = warp_sum(v);
@@ -197,13 +149,13 @@ __device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
     return t;
 }
 
-// x rows → smem (from the embedding table when a.tok; RMS-normalised and scaled by nw when a.nw). Every global
-// load of a pass is issued before any is used (float4, up to XU per thread in flight): the staging costs one
-// round trip, not one per element.
+// x rows → smem in the lane-blocked layout: from the embedding table when a.tok, plus the partial products when
+// a.xadd, RMS-normalised and scaled by the norm weights when a.nw. Two shapes. One float4 per thread (K <= 4 x the
+// threads: every normed input here, its norm weights `wn0` loaded by the caller before its dependency wait): the
+// row's loads all in flight at once, the values held in registers across the norm's reduction. Wider rows in
+// passes of XU float4s per thread, every load of a pass issued before any is used.
 constexpr int XU = 8;
-// `wn` holds this thread's norm-weight float4s, loaded by the caller (before its dependency wait) when K fits one pass
-__device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr,
-                        const float4* wn) {
+__device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr, float4 wn0) {
     const int K = a.w.cols, K4 = K >> 2;
     const bool write_x = a.x_out != nullptr && blockIdx.x == 0;
     float4* xs4 = reinterpret_cast<float4*>(xsf);
@@ -215,67 +167,76 @@ __device__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a,
             const int t = a.tok[b];
             if (t >= 0 && t < a.emb.rows) er = a.emb.w + (long)t * a.emb.stride;
         }
-        const float4* xg = reinterpret_cast<const float4*>(a.x + (long)b * a.x_stride);
-        const bool fits = K4 <= XU * nthr;  // one pass: values stay in registers across the norm's reduction
-        float ss = 0.0f;
-        for (int base = 0; base < K4; base += XU * nthr) {
-            float4 v[XU];
-#pragma unroll
-            for (int u = 0; u < XU; u++) {
-                const int i4 = base + u * nthr + tid;
-                if (i4 < K4) {
-                    if (a.tok) {
-                        if (er) {
-                            const uint32_t q = *reinterpret_cast<const uint32_t*>(er + 4 * i4);
-                            const float d = __half2float(reinterpret_cast<const __half*>(er + K)[i4 >> 3]);
-                            v[u] = make_float4((float)(int8_t)(q & 0xff) * d, (float)(int8_t)((q >> 8) & 0xff) * d,
-                                               (float)(int8_t)((q >> 16) & 0xff) * d, (float)(int8_t)(q >> 24) * d);
-                        } else {
-                            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-                    } else {
-                        v[u] = xg[i4];
-                    }
-                }
+        // element group i4 (4 columns) of the input row
+        auto load = [&](int i4) -> float4 {
+            if (a.tok) {
+                if (!er) return make_float4(0.f, 0.f, 0.f, 0.f);
+                const uint32_t q = *reinterpret_cast<const uint32_t*>(er + 4 * i4);
+                const float d = __half2float(reinterpret_cast<const __half*>(er + K)[i4 >> 3]);
+                return make_float4((float)(int8_t)(q & 0xff) * d, (float)(int8_t)((q >> 8) & 0xff) * d,
+                                   (float)(int8_t)((q >> 16) & 0xff) * d, (float)(int8_t)(q >> 24) * d);
             }
+            return reinterpret_cast<const float4*>(a.x + (long)b * a.x_stride)[i4];
+        };
+        float4* xo = write_x ? reinterpret_cast<float4*>(a.x_out + (long)b * a.x_stride) : nullptr;
+        if (K4 <= nthr) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (tid < K4) {
+                if (a.xadd) {
+                    // x + (p_0 + … + p_{n-1}): every load in flight, the partials summed in order
+                    const float4* pa = reinterpret_cast<const float4*>(a.xadd) + (long)b * a.n_add * K4 + tid;
+                    float4 pv[MAX_ADD];
+                    v = load(tid);
 #pragma unroll
-            for (int u = 0; u < XU; u++) {
-                const int i4 = base + u * nthr + tid;
-                if (i4 < K4) {
-                    if (write_x) reinterpret_cast<float4*>(a.x_out + (long)b * a.x_stride)[i4] = v[u];
-                    ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+                    for (int k = 0; k < MAX_ADD; k++)
+                        if (k < a.n_add) pv[k] = pa[(long)k * K4];
+                    float4 o = pv[0];
+#pragma unroll
+                    for (int k = 1; k < MAX_ADD; k++)
+                        if (k < a.n_add) o = make_float4(o.x + pv[k].x, o.y + pv[k].y, o.z + pv[k].z, o.w + pv[k].w);
+                    v = make_float4(v.x + o.x, v.y + o.y, v.z + o.z, v.w + o.w);
+                } else {
+                    v = load(tid);
                 }
+                if (xo) xo[tid] = v;
             }
-            if (a.nw && fits) {
-                // scale known after the reduction; the values wait in registers
+            if (a.nw) {
+                const float ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, v.w * v.w)));
                 const float tot = consumer_sum(ss, red, nthr);
                 const float scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+                v = make_float4(v.x * scale * wn0.x, v.y * scale * wn0.y, v.z * scale * wn0.z, v.w * scale * wn0.w);
+            }
+            if (tid < K4) xs4[xs_index(s, nch, 4 * tid) >> 2] = v;
+        } else {
+            float ss = 0.0f;
+            for (int base = 0; base < K4; base += XU * nthr) {
+                float4 v[XU];
+#pragma unroll
+                for (int u = 0; u < XU; u++) {
+                    const int i4 = base + u * nthr + tid;
+                    if (i4 < K4) v[u] = load(i4);
+                }
 #pragma unroll
                 for (int u = 0; u < XU; u++) {
                     const int i4 = base + u * nthr + tid;
                     if (i4 < K4) {
-                        const float4 w = wn[u];
-                        v[u] = make_float4(v[u].x * scale * w.x, v[u].y * scale * w.y, v[u].z * scale * w.z,
-                                           v[u].w * scale * w.w);
+                        if (xo) xo[i4] = v[u];
+                        ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+                        xs4[xs_index(s, nch, 4 * i4) >> 2] = v[u];
                     }
                 }
             }
-#pragma unroll
-            for (int u = 0; u < XU; u++) {
-                const int i4 = base + u * nthr + tid;
-                if (i4 < K4) xs4[xs_index(s, nch, 4 * i4) >> 2] = v[u];
+            if (a.nw) {
+                const float tot = consumer_sum(ss, red, nthr);
+                const float scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+                for (int c = tid; c < K; c += nthr) {
+                    const int k = xs_index(s, nch, c);
+                    xsf[k] = xsf[k] * scale * a.nw[c];
+                }
             }
         }
         // the last chunk's columns past K: lanes there see zero quants, the staged values must be finite
         for (int c = K + 4 * tid; c < nch * 512; c += 4 * nthr) xs4[xs_index(s, nch, c) >> 2] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (a.nw && !fits) {
-            const float tot = consumer_sum(ss, red, nthr);
-            const float scale = 1.0f / sqrtf(tot / (float)K + a.eps);
-            for (int c = tid; c < K; c += nthr) {
-                const int k = xs_index(s, nch, c);
-                xsf[k] = xsf[k] * scale * a.nw[c];
-            }
-        }
     }
 }
 
@@ -334,7 +295,10 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                 const uint32_t bytes = (uint32_t)(min(SR, hi - r0) * stride);
                 mbar_expect_tx(&full[slot], bytes);
                 bulk_g2s_stream(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot], pol);
-                if (t == min(ns, n_stage) - 1) pdl_trigger();
+                if (t == min(ns, n_stage) - 1) {
+                    pdl_trigger();
+                    l2_next(a.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+                }
             }
         }
     } else {
@@ -345,16 +309,8 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
         bool act[NB];
 #pragma unroll
         for (int s = 0; s < NB; s++) act[s] = s < nb && (!a.active || a.active[slot0 + s] != 0);
-        float4 wn[XU];
-        const int K4 = K >> 2;
-        if (a.nw && K4 <= XU * NC) {
-            const float4* nw4 = reinterpret_cast<const float4*>(a.nw);
-#pragma unroll
-            for (int u = 0; u < XU; u++) {
-                const int i4 = u * NC + threadIdx.x;
-                if (i4 < K4) wn[u] = nw4[i4];
-            }
-        }
+        float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.nw && K <= 4 * NC && (int)threadIdx.x < (K >> 2)) wn0 = reinterpret_cast<const float4*>(a.nw)[threadIdx.x];
         if (lmhead) pen_prefilter(pl, nb, slot0, a.lm, lo, hi, NC);
         pdl_wait();
         // for the residual add, the first stages' old values of this warp's rows are fetched now so the epilogue's
@@ -374,7 +330,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                                                                           : 0.0f;
                     }
         }
-        stage_x(xsf, nch, nb, slot0, a, red, NC, wn);
+        stage_x(xsf, nch, nb, slot0, a, red, NC, wn0);
         bar_sync(1, NC);
         const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
         for (int t = 0; t < n_stage; t++) {

@@ -111,6 +111,19 @@ __global__ void k_synth_norm(uint64_t seed, int n, float* __restrict__ out) {
     }
 }
 
+// one CTA per (row, slice): quants as 32-bit words, then the slice's scales, then zeros to the stride
+__global__ void k_slice_o(const uint8_t* __restrict__ w, int cols, int parts, uint8_t* __restrict__ out) {
+    const int r = blockIdx.x, j = blockIdx.y, rows = gridDim.x;
+    const int sc = cols / parts, ss = q8_stride(sc);
+    const uint8_t* src = w + (size_t)r * q8_stride(cols);
+    uint8_t* dst = out + ((size_t)j * rows + r) * ss;
+    for (int i = threadIdx.x; i < sc / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src + (size_t)j * sc)[i];
+    const uint16_t* scales = reinterpret_cast<const uint16_t*>(src + cols) + (size_t)j * (sc / 32);
+    for (int i = threadIdx.x; i < sc / 32; i += blockDim.x) reinterpret_cast<uint16_t*>(dst + sc)[i] = scales[i];
+    for (int i = sc + sc / 16 + threadIdx.x; i < ss; i += blockDim.x) dst[i] = 0;
+}
+
 static int grid_for(long n, int threads) {
     long g = (n + threads - 1) / threads;
     return (int)(g < 1 ? 1 : (g > 65535 * 8 ? 65535 * 8 : g));
@@ -136,6 +149,10 @@ void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, in
 
 void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out) {
     k_synth_norm<<<grid_for(n, 256), 256, 0, st>>>(seed, n, out);
+}
+
+void launch_slice_o(cudaStream_t st, const uint8_t* w, int rows, int cols, int parts, uint8_t* out) {
+    k_slice_o<<<dim3((unsigned)rows, (unsigned)parts), 128, 0, st>>>(w, cols, parts, out);
 }
 
 }  // namespace ocr

@@ -29,6 +29,10 @@ void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out);
 // back to GGUF blocks (ocr_model_tensor_gguf): source rows r * row_mul + row_add
 void launch_unpack_q8_0(cudaStream_t st, const uint8_t* w, int rows, int cols, int row_mul, int row_add,
                         uint8_t* blocks);
+// W_o (rows x cols, row layout) cut into `parts` column slices of cols/parts: slice j, row r = the row's quants of
+// those columns | their f16 scales | zero pad to q8_stride(cols / parts) (the decode attention's fused o-projection
+// reads the slice of its kv head's q heads as one contiguous run)
+void launch_slice_o(cudaStream_t st, const uint8_t* w, int rows, int cols, int parts, uint8_t* out);
 
 // ---- the token choice's arguments (shared by the LM head, the standalone choice and the penalty) ------------------
 struct LmArgs {
@@ -55,6 +59,46 @@ struct LmArgs {
 // ---- the streamed matvec family (k_matvec.cu) -----------------------------------------------------------------------
 enum MvMode : int { MV_STORE = 0, MV_ADD = 1, MV_SWIGLU = 2, MV_LMHEAD = 3 };
 
+// What the next kernel of the step will read, pulled into L2 by this kernel's CTAs as they start (each CTA its share):
+// a weight matrix, and/or a layer's KV rows [0, pos[b]) of every active (slot, kv head). Those bytes then stream
+// from HBM while this kernel and the dependency chain run, and the next kernel's copies hit L2.
+struct L2Next {
+    const uint8_t* w = nullptr;  // 16-B aligned
+    size_t w_bytes = 0;          // multiple of 16
+    const __half* kc = nullptr;  // [B][n_kv][n_ctx][128]
+    const __half* vc = nullptr;
+    const int32_t* pos = nullptr;
+    const int32_t* active = nullptr;
+    int n_kv = 0, n_ctx = 0, nb = 0;
+};
+// issues CTA `part`'s share of `p` (one thread calls it): 1/parts of the matrix, and 1/parts of each KV run (whole
+// 256-B rows), in prefetches of at most 64 KB
+__device__ __forceinline__ void l2_next(const L2Next& p, int part, int parts) {
+    constexpr uint32_t CH = 64u << 10;
+    if (p.w && p.w_bytes) {
+        const size_t share = ((p.w_bytes + parts - 1) / parts + 15) / 16 * 16;
+        const size_t lo = (size_t)part * share, hi = min(p.w_bytes, lo + share);
+        for (size_t o = lo; o < hi; o += CH) prefetch_l2(p.w + o, (uint32_t)min((size_t)CH, hi - o));
+    }
+    if (p.kc) {
+        for (int b = 0; b < p.nb; b++) {
+            if (p.active && !p.active[b]) continue;
+            const int rows = min(max(p.pos[b], 0), p.n_ctx);
+            const int r0 = (int)((long)rows * part / parts), r1 = (int)((long)rows * (part + 1) / parts);
+            if (r1 <= r0) continue;
+            for (int j = 0; j < p.n_kv; j++) {
+                const long base = (((long)b * p.n_kv + j) * p.n_ctx + r0) * 128;
+                const uint32_t bytes = (uint32_t)(r1 - r0) * 256;
+                for (uint32_t o = 0; o < bytes; o += CH) {
+                    const uint32_t n = min(CH, bytes - o);
+                    prefetch_l2(reinterpret_cast<const uint8_t*>(p.kc + base) + o, n);
+                    prefetch_l2(reinterpret_cast<const uint8_t*>(p.vc + base) + o, n);
+                }
+            }
+        }
+    }
+}
+
 struct MvArgs {
     QMat w;
     const float* x = nullptr;  // [B][x_stride] input rows
@@ -65,14 +109,20 @@ struct MvArgs {
     const int32_t* tok = nullptr;
     QMat emb;
     float* x_out = nullptr;
+    // x = x + (xadd[b][0] + … + xadd[b][n_add - 1]) ([B][n_add][cols] partial products, n_add <= MAX_ADD,
+    // cols <= 4 x the consumer threads), also written to x_out by the grid's first CTA
+    const float* xadd = nullptr;
+    int n_add = 0;
     float* y = nullptr;  // [B][y_stride] (LM head: raw logits [B][n_vocab], may be null)
     int y_stride = 0;
     int mode = MV_STORE;
     int nb = 1;  // slots
     const int32_t* active = nullptr;  // [B] (null = all); an idle slot's rows are not written
     LmArgs lm;   // MV_LMHEAD: the choice
+    L2Next next;
     int* err = nullptr;
 };
+constexpr int MAX_ADD = 8;
 void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl);
 // grid of the LM head (the partials' layout) for n_vocab rows
 int lm_head_grid(int num_sms, int n_vocab, int dim);
@@ -98,9 +148,16 @@ struct AttnArgs {
     const int32_t* active = nullptr;
     int n_head = 16, n_kv = 8, n_ctx = 0, splits = 16;  // splits: CTAs per cluster (4, 8 or 16)
     float eps = 1e-6f, scale = 0.0f;
-    float* out = nullptr;       // [B][out_stride]
+    float* out = nullptr;       // [B][out_stride] the attention output (when wo is null)
     int out_stride = 0;
+    // the fused o-projection (when wo is set): the cluster of kv head j multiplies its q heads' merged output by
+    // W_o's slice j (launch_slice_o: [n_kv][dim rows] of q8_stride(G * 128) bytes) → opart[b][j][dim], the
+    // per-head partial products that the next kernel sums in a fixed order
+    const uint8_t* wo = nullptr;
+    int dim = 0;
+    float* opart = nullptr;
     int nb = 1;
+    L2Next next;
     int* err = nullptr;
 };
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);

@@ -105,6 +105,7 @@ ocr_status check_device_error(ocr_ctx* ctx) {
 struct LayerW {
     QMat qkv, o, gu, down;  // qkv rows [q | k | v]; gu rows interleaved (gate 0, up 0, gate 1, …)
     float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+    uint8_t* o_s = nullptr;  // W_o cut per kv head (launch_slice_o), derived on the device after the load
 };
 
 struct ocr_model {
@@ -137,7 +138,7 @@ struct Layout {
     };
     struct LayerOff {
         MatOff qkv, o, gu, down;
-        size_t attn_norm, q_norm, k_norm, ffn_norm;
+        size_t attn_norm, q_norm, k_norm, ffn_norm, o_s;
     };
     std::vector<LayerOff> layers;
     MatOff tok;
@@ -165,6 +166,7 @@ Layout plan(const ocr_text_cfg& c) {
         lo.q_norm = p.take((size_t)c.d_head * 4);
         lo.k_norm = p.take((size_t)c.d_head * 4);
         lo.ffn_norm = p.take((size_t)c.dim * 4);
+        lo.o_s = p.take((size_t)c.n_kv * c.dim * q8_stride(qd / c.n_kv));
         L.layers.push_back(lo);
     }
     L.tok = mat(c.n_vocab, c.dim);
@@ -194,6 +196,12 @@ ocr_status check_cfg(const ocr_text_cfg& c) {
     return OCR_OK;
 }
 
+// the layouts derived from the loaded weights (W_o's per-kv-head slices)
+void derive_weights(ocr_model* m, cudaStream_t st) {
+    const auto& c = m->cfg;
+    for (auto& L : m->layers) launch_slice_o(st, L.o.w, L.o.rows, L.o.cols, c.n_kv, L.o_s);
+}
+
 ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
     OCR_TRY(check_cfg(c));
     OCR_CUDA(cudaSetDevice(ctx->device));
@@ -218,6 +226,7 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
         w.q_norm = (float*)((char*)m->mem + lo.q_norm);
         w.k_norm = (float*)((char*)m->mem + lo.k_norm);
         w.ffn_norm = (float*)((char*)m->mem + lo.ffn_norm);
+        w.o_s = (uint8_t*)m->mem + lo.o_s;
         m->layers.push_back(w);
     }
     m->tok = qmat(m->mem, L.tok);
@@ -415,6 +424,12 @@ ocr_status load_gguf(ocr_ctx* ctx, Gguf& g, ocr_model** out) {
             st = load_one(l, k, "blk." + std::to_string(l) + "." + KIND_NAMES[k] + ".weight");
     if (st == OCR_OK) st = load_one(-1, 0, "token_embd.weight");
     if (st == OCR_OK) st = load_one(-1, 1, "output_norm.weight");
+    if (st == OCR_OK) {
+        derive_weights(m, ctx->stream);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) st = cuda_fail(e, "derive_weights");
+    }
     if (st != OCR_OK) {
         std::string keep = g_err;
         ocr_model_destroy(m);
@@ -439,6 +454,8 @@ struct ocr_session {
     void* work = nullptr;
     size_t work_bytes = 0;
     float *rope = nullptr, *x = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
+    float* x2 = nullptr;     // the second residual buffer of the fused layer
+    float* opart = nullptr;  // [B][n_kv][dim] the attention clusters' o-projection partials (null: unfused layer)
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -497,8 +514,33 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     // programmatic dependent launch chains each kernel to the one before it in the stream; the profiler's events
     // between launches would break that chain, so a profiled step launches without it
     const bool pdl = ctx->pdl && !prof;
+    // each kernel pulls what a later kernel of the step reads into L2 (the attention's KV two kernels ahead, a
+    // matrix two kernels ahead, past the attention which reads none)
+    auto kv_of = [&](int l) {
+        L2Next n;
+        n.kc = s->kcl(l);
+        n.vc = s->vcl(l);
+        n.pos = s->pos;
+        n.active = s->active;
+        n.n_kv = c.n_kv;
+        n.n_ctx = s->n_ctx;
+        n.nb = s->B;
+        return n;
+    };
+    auto with_w = [](L2Next n, const QMat& w) {
+        n.w = w.w;
+        n.w_bytes = (size_t)w.rows * w.stride;
+        return n;
+    };
+    // Fused (the decode shapes this engine targets): the attention cluster of each kv head also multiplies its heads'
+    // output by its slice of W_o, and the gate/up kernel sums those n_kv partial products onto the residual, which
+    // it writes to the other of two residual buffers (its other CTAs are still reading the first) — 4 kernels per
+    // layer. Otherwise the o-projection is its own kernel, adding in place.
+    const bool fused = s->opart != nullptr;
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
+        float* xin = fused && (l & 1) ? s->x2 : s->x;   // this layer's input residual
+        float* xout = fused ? ((l & 1) ? s->x : s->x2) : s->x;  // and its output
         MvArgs q;
         q.w = L.qkv;
         q.nw = L.attn_norm;
@@ -509,13 +551,20 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         q.active = s->active;
         q.mode = MV_STORE;
         q.err = ctx->d_err;
+        q.next = l == 0 ? kv_of(0) : L2Next();
+        if (fused) {
+            q.next.w = L.o_s;
+            q.next.w_bytes = (size_t)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv);
+        } else {
+            q.next = with_w(q.next, L.o);
+        }
         q.x_stride = c.dim;
         if (l == 0 && !x_given) {
             q.tok = s->tok;
             q.emb = m->tok;
-            q.x_out = s->x;
+            q.x_out = xin;
         } else {
-            q.x = s->x;
+            q.x = xin;
         }
         launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
         const double nact = prof ? (double)prof->pos.size() : 0.0;
@@ -541,13 +590,24 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         a.out_stride = s->qd;
         a.nb = s->B;
         a.err = ctx->d_err;
+        a.next = with_w(L2Next(), L.gu);
+        if (fused) {
+            a.wo = L.o_s;
+            a.dim = c.dim;
+            a.opart = s->opart;
+        }
         launch_attention_decode(st, a, pdl);
         if (prof) {
             double kv = 0;
             for (int p : prof->pos) kv += (double)(p + 1) * c.n_kv * 128 * 2 * 2;
-            prof->mark("attention (split-KV)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
+            if (fused)
+                prof->mark("attention + o-proj", l,
+                           kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
+                               nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
+            else
+                prof->mark("attention (split-KV)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
         }
-
+        if (!fused) {
         MvArgs o;
         o.w = L.o;
         o.x = s->attn;
@@ -558,12 +618,19 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         o.nb = s->B;
         o.active = s->active;
         o.err = ctx->d_err;
+        o.next = with_w(L2Next(), L.down);
         launch_matvec(st, o, ctx->num_sms, pdl);
         if (prof) prof->mark("o (+ residual)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
+        }
 
         MvArgs f;
         f.w = L.gu;
-        f.x = s->x;
+        f.x = xin;
+        if (fused) {
+            f.xadd = s->opart;
+            f.n_add = c.n_kv;
+            f.x_out = xout;
+        }
         f.x_stride = c.dim;
         f.nw = L.ffn_norm;
         f.eps = c.eps;
@@ -573,25 +640,29 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         f.nb = s->B;
         f.active = s->active;
         f.err = ctx->d_err;
+        if (l + 1 < c.n_layer) f.next = with_w(L2Next(), m->layers[l + 1].qkv);
         launch_matvec(st, f, ctx->num_sms, pdl);
-        if (prof) prof->mark("gate|up + swiglu", l, mat_bytes(L.gu) + nact * (c.dim * 8.0 + c.n_ff * 4.0));
+        if (prof)
+            prof->mark(fused ? "sum + gate|up + swiglu" : "gate|up + swiglu", l,
+                       mat_bytes(L.gu) + nact * (c.dim * (fused ? 8.0 + 4.0 * c.n_kv : 8.0) + c.n_ff * 4.0));
 
         MvArgs dn;
         dn.w = L.down;
         dn.x = s->g;
         dn.x_stride = c.n_ff;
-        dn.y = s->x;
+        dn.y = xout;
         dn.y_stride = c.dim;
         dn.mode = MV_ADD;
         dn.nb = s->B;
         dn.active = s->active;
         dn.err = ctx->d_err;
+        if (l + 1 < c.n_layer) dn.next = kv_of(l + 1);
         launch_matvec(st, dn, ctx->num_sms, pdl);
         if (prof) prof->mark("down (+ residual)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
     }
     MvArgs lm;
     lm.w = m->tok;
-    lm.x = s->x;
+    lm.x = fused && (c.n_layer & 1) ? s->x2 : s->x;
     lm.x_stride = c.dim;
     lm.nw = m->out_norm;
     lm.eps = c.eps;
@@ -618,6 +689,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     lm.lm.done = s->lm_done;
     lm.lm.nb = s->B;
     lm.lm.err = ctx->d_err;
+    lm.next = with_w(kv_of(0), m->layers[0].qkv);  // the next step's first kernels
     launch_matvec(st, lm, ctx->num_sms, pdl);
     if (prof)
         prof->mark("lm head (+ choice)", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));
@@ -954,6 +1026,7 @@ ocr_status ocr_model_synthetic(ocr_ctx* ctx, const ocr_text_cfg* cfg, uint64_t s
         }
     launch_synth_q8_0(st, sub(100000), sigma_e, cfg->n_vocab, cfg->dim, const_cast<uint8_t*>(m->tok.w), 1, 0);
     launch_synth_norm(st, sub(100001), cfg->dim, m->out_norm);
+    derive_weights(m, st);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) {
@@ -1050,6 +1123,10 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     Planner p;
     const size_t o_rope = p.take((size_t)n_ctx * c.d_head * 4);
     const size_t o_x = p.take((size_t)batch * c.dim * 4);
+    // the fused layer: the gate/up kernel sums at most MAX_ADD partials, one float4 of the row per consumer thread
+    const bool fuse = c.n_kv <= MAX_ADD && c.dim <= 1024;
+    const size_t o_x2 = fuse ? p.take((size_t)batch * c.dim * 4) : 0;
+    const size_t o_opart = fuse ? p.take((size_t)batch * c.n_kv * c.dim * 4) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
@@ -1066,6 +1143,10 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     char* w = (char*)s->work;
     s->rope = (float*)(w + o_rope);
     s->x = (float*)(w + o_x);
+    if (fuse) {
+        s->x2 = (float*)(w + o_x2);
+        s->opart = (float*)(w + o_opart);
+    }
     s->qkv = (float*)(w + o_qkv);
     s->attn = (float*)(w + o_attn);
     s->g = (float*)(w + o_g);
