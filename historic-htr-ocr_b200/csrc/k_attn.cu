@@ -200,8 +200,11 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         const int prel = pos - r0;  // the new row's index in the round (outside [0, nk) elsewhere)
         const int kw = (nk + NW - 1) / NW;
         const int w0 = min(nk, warp * kw), nw = alive ? min(nk, w0 + kw) - w0 : 0;  // this warp's keys
-#pragma unroll 2
-        for (int ps = 0; ps < (nw + 3) >> 2; ps++) {
+        // every pass's dot first (independent), then the passes' 8-lane reductions interleaved
+        constexpr int NP = KPW / 4;  // passes of 4 keys
+        float dk[NP][G];
+#pragma unroll
+        for (int ps = 0; ps < NP; ps++) {
             const int kk = ps * 4 + sub;
             float d[G], e[G];
 #pragma unroll
@@ -226,14 +229,20 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
                 }
             }
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                float v = d[g] + e[g];
-                v += __shfl_xor_sync(FULL, v, 4);
-                v += __shfl_xor_sync(FULL, v, 2);
-                v += __shfl_xor_sync(FULL, v, 1);
-                if (prt == 0 && kk < nw) scw[warp][g][kk] = v;
-            }
+            for (int g = 0; g < G; g++) dk[ps][g] = d[g] + e[g];
         }
+#pragma unroll
+        for (int m = 4; m >= 1; m >>= 1)
+#pragma unroll
+            for (int ps = 0; ps < NP; ps++)
+#pragma unroll
+                for (int g = 0; g < G; g++) dk[ps][g] += __shfl_xor_sync(FULL, dk[ps][g], m);
+        if (prt == 0)
+#pragma unroll
+            for (int ps = 0; ps < NP; ps++)
+                if (ps * 4 + sub < nw)
+#pragma unroll
+                    for (int g = 0; g < G; g++) scw[warp][g][ps * 4 + sub] = dk[ps][g];
         __syncwarp();
         // lane = key of this warp's share: the round's max, probabilities, sum
         if (nw > 0) {
@@ -389,22 +398,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         if (got) {
             for (int base = warp * 4; base < nr; base += NW * 4) {
                 const int rr = base + (lane >> 3);
-                float acc = 0.0f;
-                if (rr < nr) {
-                    const uint8_t* row = wsm + (size_t)rr * ostride;
-                    for (int pc = l8; pc < NCOL / 16; pc += 8) {
-                        const uint4 wq = *reinterpret_cast<const uint4*>(row + pc * 16);
-                        const float dsc = __half2float(reinterpret_cast<const __half*>(row + NCOL)[pc >> 1]);
-                        uint64_t xp[8];
-                        const int xb = ((pc >> 5) * 128 + (pc & 31)) * 2;  // in f32 pairs
-#pragma unroll
-                        for (int jj = 0; jj < 4; jj++) {
-                            xp[2 * jj] = ap[xb + jj * 64];
-                            xp[2 * jj + 1] = ap[xb + jj * 64 + 1];
-                        }
-                        acc = fmaf(dot16x2(wq, xp), dsc, acc);
-                    }
-                }
+                float acc = rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
                 acc += __shfl_xor_sync(FULL, acc, 4);
                 acc += __shfl_xor_sync(FULL, acc, 2);
                 acc += __shfl_xor_sync(FULL, acc, 1);

@@ -1,0 +1,194 @@
+// k_ffn.cu — the decode step's feed-forward block for one slot in one kernel: the reference's dmv_ffn.wgsl
+// (ffn_norm, gate|up, SwiGLU) and dmv.wgsl (down + residual), text.rs:4-10's layer order.
+//
+// Grid (FFN_CL, FFN_NCLU) in clusters of FFN_CL CTAs. Cluster c owns the slice h[c·HC, (c+1)·HC) of the n_ff hidden
+// values (HC = n_ff / FFN_NCLU), CTA r of it HR = HC / FFN_CL of them: 2·HR consecutive rows of the interleaved
+// gate|up matrix, and rows [r·dim/FFN_CL, …) of W_down's column slice c. Both are constant, so both bulk copies are
+// issued before the dependency wait. After it: the residual x plus the attention's per-head o-projection partials
+// (summed in order; the grid's first CTA writes the sum back as the new residual), RMS-normalised — the shared
+// staging of stage.cuh — then one warp per gate/up row pair, SwiGLU, the HR values to shared memory; the cluster
+// all-gathers its HC values through distributed shared memory and each CTA multiplies them by its W_down rows into
+// the cluster's partial product of the down projection, dpart[c]. The next kernel adds x + dpart[0] + … in order.
+// mbarrier waits are bounded (error flag, work skipped, every barrier still met).
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "stage.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ocr {
+
+constexpr int FFN_THREADS = 256;
+constexpr int FFN_NW = FFN_THREADS / 32;
+
+// shared layout (bytes): gate|up rows, W_down rows, x (lane-blocked), this CTA's h, the cluster's h (lane-blocked)
+struct FfnSmem {
+    int gu, wd, xs, hs, hall, total;
+};
+__host__ __device__ inline FfnSmem ffn_layout(int dim, int n_ff) {
+    const int HC = n_ff / FFN_NCLU, HR = HC / FFN_CL;
+    FfnSmem m;
+    m.gu = 0;
+    m.wd = m.gu + 2 * HR * q8_stride(dim);
+    m.xs = m.wd + (dim / FFN_CL) * q8_stride(HC);
+    m.hs = m.xs + ((dim + 511) / 512) * 512 * 4;
+    m.hall = m.hs + (HR * 4 + 15) / 16 * 16;
+    m.total = m.hall + ((HC + 511) / 512) * 512 * 4;
+    return m;
+}
+
+__global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ __align__(8) uint64_t bar_gu, bar_wd;
+    __shared__ float red[FFN_NW];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int r = blockIdx.x, c = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int dim = a.in.w.cols, HC = a.n_ff / FFN_NCLU, HR = HC / FFN_CL, drows = dim / FFN_CL;
+    const int gstride = q8_stride(dim), dstride = q8_stride(HC);
+    const FfnSmem L = ffn_layout(dim, a.n_ff);
+    uint8_t* gsm = sm + L.gu;
+    uint8_t* dsm = sm + L.wd;
+    float* xs = reinterpret_cast<float*>(sm + L.xs);
+    float* hs = reinterpret_cast<float*>(sm + L.hs);
+    float* hall = reinterpret_cast<float*>(sm + L.hall);
+    if (t == 0) {
+        mbar_init(&bar_gu, 1);
+        mbar_init(&bar_wd, 1);
+        mbar_fence_init();
+        const uint64_t pol = l2_evict_first();
+        const uint32_t gbytes = (uint32_t)(2 * HR * gstride), dbytes = (uint32_t)(drows * dstride);
+        mbar_expect_tx(&bar_gu, gbytes);
+        bulk_g2s_stream(gsm, a.gu.w + (size_t)2 * (c * HC + r * HR) * gstride, gbytes, &bar_gu, pol);
+        mbar_expect_tx(&bar_wd, dbytes);
+        bulk_g2s_stream(dsm, a.wd + ((size_t)c * dim + r * drows) * dstride, dbytes, &bar_wd, pol);
+        pdl_trigger();
+        l2_next(a.next, c * FFN_CL + r, FFN_NCLU * FFN_CL);
+    }
+    float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.in.nw && dim <= 4 * FFN_THREADS && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
+    pdl_wait();
+
+    const int nch = (dim + 511) / 512;
+    stage_x(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
+    __syncthreads();
+
+    // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
+    const bool got_gu = __all_sync(FULL, mbar_wait(&bar_gu, 0, a.err));
+    const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xs);
+    for (int p = warp; p < HR; p += FFN_NW) {
+        float g = 0.0f, u = 0.0f;
+        if (got_gu) {
+            const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
+            const uint8_t* ru = rg + gstride;
+            for (int i = 0; i < nch; i++) {
+                const int col = i * 512 + lane * 16;
+                if (col >= dim) continue;
+                uint64_t xp[8];
+                const int base = (i * 128 + lane) * 2;
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    xp[2 * jj] = xsp[base + jj * 64];
+                    xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+                }
+                const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
+                const float du = __half2float(reinterpret_cast<const __half*>(ru + dim)[col >> 5]);
+                g = fmaf(dot16x2(*reinterpret_cast<const uint4*>(rg + col), xp), dg, g);
+                u = fmaf(dot16x2(*reinterpret_cast<const uint4*>(ru + col), xp), du, u);
+            }
+        }
+        g = warp_sum(g);
+        u = warp_sum(u);
+        if (lane == 0) hs[p] = g / (1.0f + expf(-g)) * u;
+    }
+    // the cluster's h slice, in every CTA of it (lane-blocked for the down rows' dot)
+    cluster.sync();
+    const int nchh = (HC + 511) / 512;
+    for (int i = t; i < HC / 4; i += FFN_THREADS) {
+        const int q = 4 * i;
+        const float* rp = cluster.map_shared_rank(hs, q / HR);
+        *reinterpret_cast<float4*>(&hall[xs_index(0, nchh, q)]) = *reinterpret_cast<const float4*>(rp + q % HR);
+    }
+    for (int q = HC + 4 * t; q < nchh * 512; q += 4 * FFN_THREADS)
+        *reinterpret_cast<float4*>(&hall[xs_index(0, nchh, q)]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    // no remote reads of this CTA's h follow: arrive now, wait before leaving
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    __syncthreads();
+
+    // down: this CTA's rows of the slice, 8 lanes per row, 4 rows per warp
+    const bool got_wd = __all_sync(FULL, mbar_wait(&bar_wd, 0, a.err));
+    const uint64_t* hp = reinterpret_cast<const uint64_t*>(hall);
+    float* op = a.dpart + (size_t)c * dim + r * drows;
+    const int l8 = lane & 7;
+    for (int base = warp * 4; base < drows; base += FFN_NW * 4) {
+        const int rr = base + (lane >> 3);
+        float acc = (got_wd && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
+        acc += __shfl_xor_sync(FULL, acc, 4);
+        acc += __shfl_xor_sync(FULL, acc, 2);
+        acc += __shfl_xor_sync(FULL, acc, 1);
+        if (l8 == 0 && rr < drows) op[rr] = acc;
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+int ffn_smem(int dim, int n_ff) {
+    if (n_ff % (FFN_NCLU * FFN_CL * 4) || dim % (FFN_CL * 4) || dim % 32 || (n_ff / FFN_NCLU) % 32) return 0;
+    const int total = ffn_layout(dim, n_ff).total;
+    return total <= 100 * 1024 ? total : 0;  // two CTAs per SM
+}
+
+static void ffn_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaStream_t st, int smem) {
+    cfg = {};
+    cfg.gridDim = dim3(FFN_CL, FFN_NCLU, 1);
+    cfg.blockDim = dim3(FFN_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = FFN_CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+}
+
+bool ffn_usable(int dim, int n_ff) {
+    const int smem = ffn_smem(dim, n_ff);
+    if (!smem) return false;
+    static int keys[8], vals[8], n_keys = 0;
+    for (int i = 0; i < n_keys; i++)
+        if (keys[i] == smem) return vals[i] != 0;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncAttributes fa;
+        cudaFuncGetAttributes(&fa, k_ffn);
+        cudaFuncSetAttribute(k_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
+        cudaFuncSetAttribute(k_ffn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    ffn_config(cfg, attr, nullptr, smem);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_ffn, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    if (n_keys < 8) {
+        keys[n_keys] = smem;
+        vals[n_keys++] = n >= FFN_NCLU;  // every cluster resident at once
+    }
+    return n >= FFN_NCLU;
+}
+
+void launch_ffn(cudaStream_t st, const FfnArgs& a, bool pdl) {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    ffn_config(cfg, attr, st, ffn_smem(a.in.w.cols, a.n_ff));
+    cfg.numAttrs = pdl ? 2 : 1;
+    cudaLaunchKernelEx(&cfg, k_ffn, a);
+}
+
+}  // namespace ocr

@@ -65,6 +65,8 @@ enum MvMode : int { MV_STORE = 0, MV_ADD = 1, MV_SWIGLU = 2, MV_LMHEAD = 3 };
 struct L2Next {
     const uint8_t* w = nullptr;  // 16-B aligned
     size_t w_bytes = 0;          // multiple of 16
+    const uint8_t* w2 = nullptr;  // a second matrix (the fused FFN reads two)
+    size_t w2_bytes = 0;
     const __half* kc = nullptr;  // [B][n_kv][n_ctx][128]
     const __half* vc = nullptr;
     const int32_t* pos = nullptr;
@@ -75,11 +77,14 @@ struct L2Next {
 // 256-B rows), in prefetches of at most 64 KB
 __device__ __forceinline__ void l2_next(const L2Next& p, int part, int parts) {
     constexpr uint32_t CH = 64u << 10;
-    if (p.w && p.w_bytes) {
-        const size_t share = ((p.w_bytes + parts - 1) / parts + 15) / 16 * 16;
-        const size_t lo = (size_t)part * share, hi = min(p.w_bytes, lo + share);
-        for (size_t o = lo; o < hi; o += CH) prefetch_l2(p.w + o, (uint32_t)min((size_t)CH, hi - o));
-    }
+    auto mat = [&](const uint8_t* w, size_t bytes) {
+        if (!w || !bytes) return;
+        const size_t share = ((bytes + parts - 1) / parts + 15) / 16 * 16;
+        const size_t lo = (size_t)part * share, hi = min(bytes, lo + share);
+        for (size_t o = lo; o < hi; o += CH) prefetch_l2(w + o, (uint32_t)min((size_t)CH, hi - o));
+    };
+    mat(p.w, p.w_bytes);
+    mat(p.w2, p.w2_bytes);
     if (p.kc) {
         for (int b = 0; b < p.nb; b++) {
             if (p.active && !p.active[b]) continue;
@@ -161,6 +166,29 @@ struct AttnArgs {
     int* err = nullptr;
 };
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);
+
+// ---- the fused FFN (k_ffn.cu) ----------------------------------------------------------------------------------------
+// One slot: x + (o-partials) → residual, RMSNorm → gate|up → SwiGLU → down, in FFN_NCLU thread-block clusters of
+// FFN_CL CTAs. Cluster c owns h[c·n_ff/FFN_NCLU …) — its gate|up rows are one contiguous run of the interleaved
+// matrix — and multiplies it by its column slice of W_down (launch_slice_o with FFN_NCLU parts), leaving FFN_NCLU
+// partial products of the down projection that the next kernel's staging sums in a fixed order.
+constexpr int FFN_CL = 16;
+constexpr int FFN_NCLU = 8;
+struct FfnArgs {
+    MvArgs in;  // the staging: in.x, in.xadd / n_add (o-partials), in.x_out (the new residual), in.nw, in.eps;
+                // in.w.cols = dim
+    QMat gu;    // gate|up, rows interleaved [2 n_ff][dim]
+    const uint8_t* wd = nullptr;  // W_down cut by h slice: [FFN_NCLU][dim][q8_stride(n_ff / FFN_NCLU)]
+    int n_ff = 0;
+    float* dpart = nullptr;  // [FFN_NCLU][dim]
+    L2Next next;
+    int* err = nullptr;
+};
+// the dynamic shared memory the fused FFN needs for this shape, or 0 when the shape does not fit it
+int ffn_smem(int dim, int n_ff);
+// true when the fused FFN's clusters can be resident on this device (asks the occupancy API once per shape)
+bool ffn_usable(int dim, int n_ff);
+void launch_ffn(cudaStream_t st, const FfnArgs& a, bool pdl);
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx);
 
 // ---- prefill (k_prefill.cu) -------------------------------------------------------------------------------------------

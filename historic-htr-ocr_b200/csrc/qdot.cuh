@@ -56,4 +56,24 @@ __device__ __forceinline__ int xs_index(int s, int nch, int c) {
     return ((((s * nch + i) * 4 + (j >> 2)) * 32 + l) << 2) + (j & 3);
 }
 
+// this lane's share of row · x over the row's 16-column pieces l8, l8 + 8, … (8 lanes per row, so a quarter-warp
+// reads 128 contiguous bytes of one row): `row` in the row layout (ncol quants, then the f16 block scales), x staged
+// lane-blocked as f32 pairs (`ap`)
+__device__ __forceinline__ float row_dot8(const uint8_t* row, int ncol, const uint64_t* ap, int l8) {
+    float acc = 0.0f;
+    for (int pc = l8; pc < ncol / 16; pc += 8) {
+        const uint4 wq = *reinterpret_cast<const uint4*>(row + pc * 16);
+        const float dsc = __half2float(reinterpret_cast<const __half*>(row + ncol)[pc >> 1]);
+        uint64_t xp[8];
+        const int xb = ((pc >> 5) * 128 + (pc & 31)) * 2;  // in f32 pairs
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            xp[2 * jj] = ap[xb + jj * 64];
+            xp[2 * jj + 1] = ap[xb + jj * 64 + 1];
+        }
+        acc = fmaf(dot16x2(wq, xp), dsc, acc);
+    }
+    return acc;
+}
+
 }  // namespace ocr

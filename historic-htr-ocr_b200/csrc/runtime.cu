@@ -106,6 +106,7 @@ struct LayerW {
     QMat qkv, o, gu, down;  // qkv rows [q | k | v]; gu rows interleaved (gate 0, up 0, gate 1, …)
     float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
     uint8_t* o_s = nullptr;  // W_o cut per kv head (launch_slice_o), derived on the device after the load
+    uint8_t* d_s = nullptr;  // W_down cut into FFN_NCLU h slices (the fused FFN), when the shape fits it
 };
 
 struct ocr_model {
@@ -138,7 +139,7 @@ struct Layout {
     };
     struct LayerOff {
         MatOff qkv, o, gu, down;
-        size_t attn_norm, q_norm, k_norm, ffn_norm, o_s;
+        size_t attn_norm, q_norm, k_norm, ffn_norm, o_s, d_s;
     };
     std::vector<LayerOff> layers;
     MatOff tok;
@@ -167,6 +168,7 @@ Layout plan(const ocr_text_cfg& c) {
         lo.k_norm = p.take((size_t)c.d_head * 4);
         lo.ffn_norm = p.take((size_t)c.dim * 4);
         lo.o_s = p.take((size_t)c.n_kv * c.dim * q8_stride(qd / c.n_kv));
+        lo.d_s = ffn_smem(c.dim, c.n_ff) ? p.take((size_t)FFN_NCLU * c.dim * q8_stride(c.n_ff / FFN_NCLU)) : 0;
         L.layers.push_back(lo);
     }
     L.tok = mat(c.n_vocab, c.dim);
@@ -199,7 +201,10 @@ ocr_status check_cfg(const ocr_text_cfg& c) {
 // the layouts derived from the loaded weights (W_o's per-kv-head slices)
 void derive_weights(ocr_model* m, cudaStream_t st) {
     const auto& c = m->cfg;
-    for (auto& L : m->layers) launch_slice_o(st, L.o.w, L.o.rows, L.o.cols, c.n_kv, L.o_s);
+    for (auto& L : m->layers) {
+        launch_slice_o(st, L.o.w, L.o.rows, L.o.cols, c.n_kv, L.o_s);
+        if (L.d_s) launch_slice_o(st, L.down.w, L.down.rows, L.down.cols, FFN_NCLU, L.d_s);
+    }
 }
 
 ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
@@ -227,6 +232,7 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
         w.k_norm = (float*)((char*)m->mem + lo.k_norm);
         w.ffn_norm = (float*)((char*)m->mem + lo.ffn_norm);
         w.o_s = (uint8_t*)m->mem + lo.o_s;
+        w.d_s = lo.d_s ? (uint8_t*)m->mem + lo.d_s : nullptr;
         m->layers.push_back(w);
     }
     m->tok = qmat(m->mem, L.tok);
@@ -456,6 +462,7 @@ struct ocr_session {
     float *rope = nullptr, *x = nullptr, *qkv = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
     float* x2 = nullptr;     // the second residual buffer of the fused layer
     float* opart = nullptr;  // [B][n_kv][dim] the attention clusters' o-projection partials (null: unfused layer)
+    float* dpart = nullptr;  // [FFN_NCLU][dim] the fused FFN's down partials (one slot)
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -536,11 +543,15 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     // output by its slice of W_o, and the gate/up kernel sums those n_kv partial products onto the residual, which
     // it writes to the other of two residual buffers (its other CTAs are still reading the first) — 4 kernels per
     // layer. Otherwise the o-projection is its own kernel, adding in place.
+    // One slot with a fitting shape goes further: the FFN is one kernel of FFN_NCLU clusters whose down-projection
+    // partials the next layer's qkv kernel (or the LM head) sums onto the residual — 3 kernels per layer. Residual
+    // buffers then: the qkv kernel writes x (layer input + FFN partials), the FFN kernel x2 (x + o-partials).
     const bool fused = s->opart != nullptr;
+    const bool ffn = s->dpart != nullptr && ffn_usable(c.dim, c.n_ff);
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
-        float* xin = fused && (l & 1) ? s->x2 : s->x;   // this layer's input residual
-        float* xout = fused ? ((l & 1) ? s->x : s->x2) : s->x;  // and its output
+        float* xin = fused && !ffn && (l & 1) ? s->x2 : s->x;   // this layer's input residual
+        float* xout = fused ? ((l & 1) && !ffn ? s->x : s->x2) : s->x;  // and its output
         MvArgs q;
         q.w = L.qkv;
         q.nw = L.attn_norm;
@@ -563,6 +574,11 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
             q.tok = s->tok;
             q.emb = m->tok;
             q.x_out = xin;
+        } else if (l > 0 && ffn) {
+            q.x = s->x2;
+            q.xadd = s->dpart;
+            q.n_add = FFN_NCLU;
+            q.x_out = s->x;
         } else {
             q.x = xin;
         }
@@ -591,6 +607,10 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         a.nb = s->B;
         a.err = ctx->d_err;
         a.next = with_w(L2Next(), L.gu);
+        if (ffn) {
+            a.next.w2 = L.d_s;
+            a.next.w2_bytes = (size_t)FFN_NCLU * c.dim * q8_stride(c.n_ff / FFN_NCLU);
+        }
         if (fused) {
             a.wo = L.o_s;
             a.dim = c.dim;
@@ -623,6 +643,29 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         if (prof) prof->mark("o (+ residual)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
         }
 
+        if (ffn) {
+            FfnArgs f;
+            f.in.w.cols = c.dim;
+            f.in.x = s->x;
+            f.in.x_stride = c.dim;
+            f.in.xadd = s->opart;
+            f.in.n_add = c.n_kv;
+            f.in.x_out = s->x2;
+            f.in.nw = L.ffn_norm;
+            f.in.eps = c.eps;
+            f.gu = L.gu;
+            f.wd = L.d_s;
+            f.n_ff = c.n_ff;
+            f.dpart = s->dpart;
+            f.err = ctx->d_err;
+            if (l + 1 < c.n_layer) f.next = with_w(kv_of(l + 1), m->layers[l + 1].qkv);
+            launch_ffn(st, f, pdl);
+            if (prof)
+                prof->mark("ffn (gate|up, swiglu, down)", l,
+                           mat_bytes(L.gu) + (double)FFN_NCLU * c.dim * q8_stride(c.n_ff / FFN_NCLU) +
+                               c.dim * 4.0 * (2 + c.n_kv + FFN_NCLU));
+            continue;
+        }
         MvArgs f;
         f.w = L.gu;
         f.x = xin;
@@ -662,7 +705,12 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     }
     MvArgs lm;
     lm.w = m->tok;
-    lm.x = fused && (c.n_layer & 1) ? s->x2 : s->x;
+    lm.x = fused && !ffn && (c.n_layer & 1) ? s->x2 : s->x;
+    if (ffn) {
+        lm.x = s->x2;
+        lm.xadd = s->dpart;
+        lm.n_add = FFN_NCLU;
+    }
     lm.x_stride = c.dim;
     lm.nw = m->out_norm;
     lm.eps = c.eps;
@@ -1127,6 +1175,8 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const bool fuse = c.n_kv <= MAX_ADD && c.dim <= 1024;
     const size_t o_x2 = fuse ? p.take((size_t)batch * c.dim * 4) : 0;
     const size_t o_opart = fuse ? p.take((size_t)batch * c.n_kv * c.dim * 4) : 0;
+    const bool fuse_ffn = fuse && batch == 1 && m->layers[0].d_s != nullptr;
+    const size_t o_dpart = fuse_ffn ? p.take((size_t)FFN_NCLU * c.dim * 4) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
@@ -1147,6 +1197,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         s->x2 = (float*)(w + o_x2);
         s->opart = (float*)(w + o_opart);
     }
+    if (fuse_ffn) s->dpart = (float*)(w + o_dpart);
     s->qkv = (float*)(w + o_qkv);
     s->attn = (float*)(w + o_attn);
     s->g = (float*)(w + o_g);
