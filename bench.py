@@ -48,6 +48,32 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
 
 
+def max_over_ranks(values, dist=None):
+    """each value's maximum over the ranks (a gloo all-reduce of a host tensor; no data-path collective: the replicas
+    only meet here and at the timing barrier) — the values themselves for one process"""
+    import torch
+
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64)
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def workload_config(config, B, new, prefix_len, world):
+    """the `config` object of both arms' JSON lines"""
+    return {"workload": f"BASELINE config {config}: greedy decode of {new} tokens per sequence, {B} sequence(s) per "
+                        f"GPU, {prefix_len}-row prefilled f16 KV cache, rp 1.15 window 64",
+            "model": "Qwen3-0.6B-shaped text decoder (28 x 1024, 16/8 heads, ffn 3072, vocab 151936, tied head)",
+            "global_batch": B * world, "seq_len": prefix_len + new,
+            "parallelism": f"replicas x{world} (pages partitioned, no collectives)",
+            "l2": "inputs larger than L2 (633 MB of weights streamed per token)"}
+
+
+def whole_job_rate(world, units_per_rank, seconds):
+    """units of all replicas (weak scaling: each rank decodes its own sequences) over the slowest rank's time"""
+    return world * units_per_rank / seconds
+
+
 class Clocks:
     """nvidia-smi samples during the timed region (SM clock, max, throttle reasons)"""
 
@@ -238,15 +264,7 @@ def run_ours(args):
         ev1.record(stream)
         ev1.synchronize()
         wall = time.perf_counter() - t0
-    dev_s = ev0.elapsed_time(ev1) / 1e3
-    times = np.array([dev_s, wall], np.float64)
-    if pg:
-        import torch.distributed as dist
-
-        t = torch.from_numpy(times)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times = t.numpy()
-    dev_s, wall = float(times[0]), float(times[1])
+    dev_s, wall = max_over_ranks([ev0.elapsed_time(ev1) / 1e3, wall], pg)
     tokens = world * B * new * args.steps
     out = None
     if rank == 0:
@@ -259,17 +277,12 @@ def run_ours(args):
         lm_us, lm_bytes = lm_head_kernel(ocr, ctx, torch, 10)
         out = {
             "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
-            "value": round(tokens / dev_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "value": round(whole_job_rate(world, B * new * args.steps, dev_s), 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_s / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV",
             "data": "synthetic (seeded q8_0 weights sigma 0.02, N(0,1) prefix embeddings; no checkpoint)",
-            "config": {"workload": f"BASELINE config {args.config}: greedy decode of {new} tokens per sequence, "
-                                   f"{B} sequence(s) per GPU, {prefix_len}-row prefilled f16 KV cache, rp 1.15 "
-                                   "window 64", "model": "Qwen3-0.6B-shaped text decoder (28 x 1024, 16/8 heads, "
-                                   "ffn 3072, vocab 151936, tied head)", "global_batch": B * world,
-                       "seq_len": prefix_len + new, "parallelism": f"replicas x{world} (pages partitioned, no "
-                                                                   "collectives)",
-                       "l2": "inputs larger than L2 (633 MB of weights streamed per token)"},
+            "config": workload_config(args.config, B, new, prefix_len, world),
             "e2e": {"value": round(tokens / wall, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": B * (64 * 4 + 1024 * 4), "d2h_bytes_per_step": B * new * 4},
             "gpu_launches": int(launches),
@@ -368,8 +381,7 @@ def run_reference(args):
         "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2 (bounded CPU sample)", "global_batch": 1,
-                   "seq_len": PREFIX + NEW, "parallelism": "host cores"},
+        "config": workload_config(2, 1, NEW, PREFIX, world),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": O.num_threads(), "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 

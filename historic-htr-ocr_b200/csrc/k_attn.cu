@@ -396,13 +396,23 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         const int nr = min(ro, rpc - c0);
         const bool got = __all_sync(FULL, mbar_wait(&obar, k & 1, a.err));
         if (got) {
-            for (int base = warp * 4; base < nr; base += NW * 4) {
-                const int rr = base + (lane >> 3);
-                float acc = rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
-                acc += __shfl_xor_sync(FULL, acc, 4);
-                acc += __shfl_xor_sync(FULL, acc, 2);
-                acc += __shfl_xor_sync(FULL, acc, 1);
-                if (l8 == 0 && rr < nr) op[c0 + rr] = acc;
+            // two row groups per warp at once: both dots, then both reductions
+            for (int base = warp * 4; base < nr; base += NW * 8) {
+                float acc[2];
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const int rr = base + k * NW * 4 + (lane >> 3);
+                    acc[k] = rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
+                }
+#pragma unroll
+                for (int m = 4; m >= 1; m >>= 1)
+#pragma unroll
+                    for (int k = 0; k < 2; k++) acc[k] += __shfl_xor_sync(FULL, acc[k], m);
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const int rr = base + k * NW * 4 + (lane >> 3);
+                    if (l8 == 0 && rr < nr) op[c0 + rr] = acc[k];
+                }
             }
         }
         if (c0 + ro < rpc) {

@@ -77,30 +77,45 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
     const bool got_gu = __all_sync(FULL, mbar_wait(&bar_gu, 0, a.err));
     const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xs);
-    for (int p = warp; p < HR; p += FFN_NW) {
-        float g = 0.0f, u = 0.0f;
-        if (got_gu) {
-            const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
-            const uint8_t* ru = rg + gstride;
-            for (int i = 0; i < nch; i++) {
-                const int col = i * 512 + lane * 16;
-                if (col >= dim) continue;
-                uint64_t xp[8];
-                const int base = (i * 128 + lane) * 2;
+    // up to PB pairs per warp at once: every dot first, then the reductions interleaved
+    constexpr int PB = 4;
+    for (int p0 = warp; p0 < HR; p0 += FFN_NW * PB) {
+        float g[PB], u[PB];
 #pragma unroll
-                for (int jj = 0; jj < 4; jj++) {
-                    xp[2 * jj] = xsp[base + jj * 64];
-                    xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+        for (int k = 0; k < PB; k++) {
+            g[k] = u[k] = 0.0f;
+            const int p = p0 + k * FFN_NW;
+            if (got_gu && p < HR) {
+                const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
+                const uint8_t* ru = rg + gstride;
+                for (int i = 0; i < nch; i++) {
+                    const int col = i * 512 + lane * 16;
+                    if (col >= dim) continue;
+                    uint64_t xp[8];
+                    const int base = (i * 128 + lane) * 2;
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) {
+                        xp[2 * jj] = xsp[base + jj * 64];
+                        xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+                    }
+                    const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
+                    const float du = __half2float(reinterpret_cast<const __half*>(ru + dim)[col >> 5]);
+                    g[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(rg + col), xp), dg, g[k]);
+                    u[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(ru + col), xp), du, u[k]);
                 }
-                const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
-                const float du = __half2float(reinterpret_cast<const __half*>(ru + dim)[col >> 5]);
-                g = fmaf(dot16x2(*reinterpret_cast<const uint4*>(rg + col), xp), dg, g);
-                u = fmaf(dot16x2(*reinterpret_cast<const uint4*>(ru + col), xp), du, u);
             }
         }
-        g = warp_sum(g);
-        u = warp_sum(u);
-        if (lane == 0) hs[p] = g / (1.0f + expf(-g)) * u;
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+            for (int k = 0; k < PB; k++) {
+                g[k] += __shfl_xor_sync(FULL, g[k], m);
+                u[k] += __shfl_xor_sync(FULL, u[k], m);
+            }
+        if (lane == 0)
+#pragma unroll
+            for (int k = 0; k < PB; k++)
+                if (p0 + k * FFN_NW < HR) hs[p0 + k * FFN_NW] = g[k] / (1.0f + expf(-g[k])) * u[k];
     }
     // the cluster's h slice, in every CTA of it (lane-blocked for the down rows' dot)
     cluster.sync();
@@ -121,13 +136,23 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     const uint64_t* hp = reinterpret_cast<const uint64_t*>(hall);
     float* op = a.dpart + (size_t)c * dim + r * drows;
     const int l8 = lane & 7;
-    for (int base = warp * 4; base < drows; base += FFN_NW * 4) {
-        const int rr = base + (lane >> 3);
-        float acc = (got_wd && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
-        acc += __shfl_xor_sync(FULL, acc, 4);
-        acc += __shfl_xor_sync(FULL, acc, 2);
-        acc += __shfl_xor_sync(FULL, acc, 1);
-        if (l8 == 0 && rr < drows) op[rr] = acc;
+    // two row groups per warp at once (rows base + lane/8 and base + 32 + lane/8)
+    for (int base = warp * 4; base < drows; base += FFN_NW * 8) {
+        float acc[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int rr = base + k * FFN_NW * 4 + (lane >> 3);
+            acc[k] = (got_wd && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
+        }
+#pragma unroll
+        for (int m = 4; m >= 1; m >>= 1)
+#pragma unroll
+            for (int k = 0; k < 2; k++) acc[k] += __shfl_xor_sync(FULL, acc[k], m);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int rr = base + k * FFN_NW * 4 + (lane >> 3);
+            if (l8 == 0 && rr < drows) op[rr] = acc[k];
+        }
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
