@@ -22,19 +22,26 @@ namespace ocr {
 // ---------------------------------------------------------------------------------------------------------------------
 // the token choice: windowed repetition penalty (distinct tokens of the window), frequency penalty, first maximum
 // ---------------------------------------------------------------------------------------------------------------------
-constexpr int PEN_CAP = 64;  // window tokens kept per CTA and slot (more → the CTA scans the window per row)
+constexpr int PEN_CAP = 64;     // window tokens listed per CTA and slot (more → the CTA scans the window per row)
+constexpr int PEN_BITS = 2048;  // rows of a CTA's range covered by the membership bitmask (wider → the list)
 constexpr int MAX_NB = 8;
 
+// the window's tokens that fall in a CTA's row range [lo, hi): a bitmask over the range (one shared load per row,
+// however many times a token repeats in the window) and, for ranges wider than the mask, a list
 struct PenList {
     int n[MAX_NB];
     int t[MAX_NB][PEN_CAP];
+    uint32_t bits[MAX_NB][PEN_BITS / 32];
 };
 
 // the window tokens of slot s that fall in [lo, hi): hist[len - min(len, window), len); `nthr` threads take part
 // (barrier 1)
 __device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, int lo, int hi, int nthr) {
     const int tid = threadIdx.x;
+    const bool masked = hi - lo <= PEN_BITS;
     if (tid < MAX_NB) pl.n[tid] = 0;
+    if (masked)
+        for (int i = tid; i < nb * (PEN_BITS / 32); i += nthr) pl.bits[i / (PEN_BITS / 32)][i % (PEN_BITS / 32)] = 0u;
     bar_sync(1, nthr);
     if (a.sample && a.rp != 1.0f) {
         for (int s = 0; s < nb; s++) {
@@ -46,8 +53,12 @@ __device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, i
             for (int j = start + tid; j < len; j += nthr) {
                 const int t = h[j];
                 if (t >= lo && t < hi) {
-                    const int k = atomicAdd(&pl.n[s], 1);
-                    if (k < PEN_CAP) pl.t[s][k] = t;
+                    if (masked) {
+                        atomicOr(&pl.bits[s][(t - lo) >> 5], 1u << ((t - lo) & 31));
+                    } else {
+                        const int k = atomicAdd(&pl.n[s], 1);
+                        if (k < PEN_CAP) pl.t[s][k] = t;
+                    }
                 }
             }
         }
@@ -55,13 +66,16 @@ __device__ void pen_prefilter(PenList& pl, int nb, int slot0, const LmArgs& a, i
     bar_sync(1, nthr);
 }
 
-// the choice's value of logit v of token t in slot s (choose(): rp on window members, then − fp * count)
+// the choice's value of logit v of token t (in the CTA's range [lo, hi)) in slot s (choose(): rp on window members,
+// then − fp * count)
 __device__ __forceinline__ float pen_apply(const PenList& pl, int s, int b, int t, float v, const LmArgs& a,
-                                           int n_vocab) {
+                                           int n_vocab, int lo, int hi) {
     if (a.rp != 1.0f) {
         const int n = pl.n[s];
         bool member = false;
-        if (n <= PEN_CAP) {
+        if (hi - lo <= PEN_BITS) {
+            member = (pl.bits[s][(t - lo) >> 5] >> ((t - lo) & 31)) & 1u;
+        } else if (n <= PEN_CAP) {
             for (int k = 0; k < n; k++) member |= (pl.t[s][k] == t);
         } else {
             const int len = a.len[b];
@@ -174,13 +188,8 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
     }
     __syncthreads();
 
-    float bv[NB];
-    uint32_t bi[NB];
-#pragma unroll
-    for (int s = 0; s < NB; s++) {
-        bv[s] = -INFINITY;
-        bi[s] = NO_INDEX;
-    }
+    float bvl = -INFINITY;  // this lane's best (LM head: the lane's slot lane / R)
+    uint32_t bil = NO_INDEX;
 
     if (warp == W) {
         // ---- producer: weights never depend on the previous kernel, so no griddepcontrol.wait here ----
@@ -319,25 +328,27 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                     }
                 }
             } else {
-                // lane s * R + r takes logit (slot s, row row0 + r)
+                // lane s * R + r takes logit (slot s, row row0 + r): one pass of the epilogue for all of them
+                const int ls = lane / R, lr = lane % R, row = row0 + lr;
+                float v = 0.0f;
+                bool la = false;
 #pragma unroll
-                for (int s = 0; s < NB; s++) {
+                for (int s = 0; s < NB; s++)
 #pragma unroll
-                    for (int r = 0; r < R; r++) {
-                        const int row = row0 + r;
-                        if (lane == s * R + r && s < nb && row < hi) {
-                            const int b = slot0 + s;
-                            float v = acc[s][r];
-                            if (a.y && act[s]) a.y[(long)b * N + row] = v;
-                            if (a.lm.sample) {
-                                v = pen_apply(pl, s, b, row, v, a.lm, N);
-                                if (row == 0)
-                                    reinterpret_cast<int*>(a.lm.part + (long)a.lm.nb * gridDim.x * 2)[b] = (v != v);
-                                if (better(v, (uint32_t)row, bv[s], bi[s])) {
-                                    bv[s] = v;
-                                    bi[s] = (uint32_t)row;
-                                }
-                            }
+                    for (int r = 0; r < R; r++)
+                        if (lane == s * R + r) {
+                            v = acc[s][r];
+                            la = act[s];
+                        }
+                if (lane < NB * R && ls < nb && row < hi) {
+                    const int b = slot0 + ls;
+                    if (a.y && la) a.y[(long)b * N + row] = v;
+                    if (a.lm.sample) {
+                        v = pen_apply(pl, ls, b, row, v, a.lm, N, lo, hi);
+                        if (row == 0) reinterpret_cast<int*>(a.lm.part + (long)a.lm.nb * gridDim.x * 2)[b] = (v != v);
+                        if (better(v, (uint32_t)row, bvl, bil)) {
+                            bvl = v;
+                            bil = (uint32_t)row;
                         }
                     }
                 }
@@ -351,8 +362,8 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
 #pragma unroll
         for (int s = 0; s < NB; s++) {
             const bool mine = lane >= s * R && lane < s * R + R;
-            float v = mine ? bv[s] : -INFINITY;
-            uint32_t i = mine ? bi[s] : NO_INDEX;
+            float v = mine ? bvl : -INFINITY;
+            uint32_t i = mine ? bil : NO_INDEX;
             warp_argmax(v, i);
             if (lane == 0) {
                 bv_w[warp][s] = v;
@@ -382,7 +393,8 @@ struct Geo {
     size_t smem;
 };
 
-constexpr size_t SMEM_MAX = 220 * 1024;
+constexpr size_t SMEM_MAX = 220 * 1024;   // the streamed LM head's ring (one CTA per SM)
+constexpr size_t SMEM_SMALL = 96 * 1024;  // a small matrix's ring: two CTAs (with their static memory) per SM
 
 // streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 2 rows, a deep ring. Small matrices:
 // `per_sm` CTAs per SM (two when registers and shared memory allow), 8 consumer warps (x 2 rows for SwiGLU pairs,
@@ -411,7 +423,7 @@ static Geo geometry(const MvArgs& a, int nb_pass, int num_sms, int per_sm = 2) {
     g.grid = (N + g.rpc - 1) / g.rpc;
     const int n_stage = (g.rpc + SR - 1) / SR;
     const size_t stage = (size_t)SR * stride;
-    const size_t budget = (big ? SMEM_MAX : SMEM_MAX / 2) - SM_HEAD - xs;
+    const size_t budget = (big ? SMEM_MAX : SMEM_SMALL) - SM_HEAD - xs;
     g.ns = (int)std::min<size_t>(std::min<size_t>((size_t)n_stage, MAX_NS), std::max<size_t>(1, budget / stage));
     g.smem = SM_HEAD + xs + (size_t)g.ns * stage;
     return g;
@@ -445,7 +457,7 @@ static int per_sm_t() {
     static int n = -1;
     if (n < 0) {
         configure_t<NB, W, R>();
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_mv<NB, W, R>, (W + 1) * 32, SMEM_MAX / 2) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_mv<NB, W, R>, (W + 1) * 32, SMEM_SMALL) !=
             cudaSuccess) {
             cudaGetLastError();
             n = 1;
@@ -514,7 +526,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const float* __restri
     uint32_t bi = NO_INDEX;
     const float* l = logits + (long)b * stride;
     for (int t = lo + threadIdx.x; t < hi; t += blockDim.x) {
-        const float v = pen_apply(pl, 0, b, t, l[t], a, n_vocab);
+        const float v = pen_apply(pl, 0, b, t, l[t], a, n_vocab, lo, hi);
         if (t == 0) reinterpret_cast<int*>(a.part + (long)a.nb * gridDim.x * 2)[b] = (v != v);
         if (better(v, (uint32_t)t, bv, bi)) {
             bv = v;
@@ -557,7 +569,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_penalize(float* __restrict__
     __shared__ PenList pl;
     const int lo = blockIdx.x * per_cta, hi = min(n_vocab, lo + per_cta);
     pen_prefilter(pl, 1, 0, a, lo, hi, SAMPLE_THREADS);
-    for (int t = lo + threadIdx.x; t < hi; t += blockDim.x) logits[t] = pen_apply(pl, 0, 0, t, logits[t], a, n_vocab);
+    for (int t = lo + threadIdx.x; t < hi; t += blockDim.x)
+        logits[t] = pen_apply(pl, 0, 0, t, logits[t], a, n_vocab, lo, hi);
 }
 
 void launch_penalize(cudaStream_t st, float* logits, int n_vocab, const LmArgs& a, int num_sms) {

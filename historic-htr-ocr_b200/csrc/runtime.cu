@@ -740,7 +740,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     lm.next = with_w(kv_of(0), m->layers[0].qkv);  // the next step's first kernels
     launch_matvec(st, lm, ctx->num_sms, pdl);
     if (prof)
-        prof->mark("lm head (+ choice)", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));
+        prof->mark(sample ? "lm head + choice" : "lm head", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));
 }
 
 // rope_table (text.rs:132-142): theta = (f32)pos * base^(-2i/d) in f32, (cos, sin) by the host libm
