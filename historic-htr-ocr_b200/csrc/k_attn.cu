@@ -26,7 +26,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
-#include "qdot.cuh"
+#include "stage.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -43,8 +43,11 @@ constexpr int PW = HD + 4;  // a head's partial: o[128], m, l, two floats of pad
 template <int G, int CL>
 __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf, int smem) {
     extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ __align__(8) uint64_t full[MAX_BUF];
+    __shared__ __align__(8) uint64_t fk[MAX_BUF], fv[MAX_BUF];  // a ring slot's K rows, its V rows
     __shared__ __align__(8) uint64_t obar;  // W_o slice chunks (fused o-projection)
+    __shared__ __align__(8) uint64_t qbar;  // the W_qkv rows (fused qkv projection)
+    __shared__ float red[NW];
+    __shared__ __align__(16) float qv[64];  // this CTA's qkv rows (fused qkv projection), read by the cluster
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float scw[NW][G][KPW];  // per warp: the round's scores, then probabilities
     __shared__ float wm[NW][G], wl[NW][G];
@@ -69,9 +72,13 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     const long head_base = ((long)b * a.n_kv + j) * a.n_ctx;
     __half* kb = a.kc + head_base * HD;
     __half* vb = a.vc + head_base * HD;
-    // shared layout: K rows [ring + 1][HD], then V rows [ring + 1][HD]; tile tl occupies rows (tl % n_buf) * TILE …,
-    // row `ring` holds the new token's K (V), written here rather than copied
+    // shared layout: K rows [ring + 1][HD], then the V region — V rows [ring + 1][HD], holding first the W_qkv rows
+    // when the qkv projection is fused (it is at least as large as those) — then the W_o region; tile tl occupies
+    // rows (tl % n_buf) * TILE …, row `ring` holds the new token's K (V), written here rather than copied
     const int ring = n_buf * TILE;
+    const bool fq = a.wqkv.w != nullptr;
+    const int RQ = (G + 2) * HD / CL;  // the fused qkv projection: this CTA's rows of the group's [q | k | v] rows
+    const int vreg = max((ring + 1) * HD * 2, fq ? RQ * a.wqkv.stride : 0);
     __half* Ks = reinterpret_cast<__half*>(sm);
     __half* Vs = Ks + (size_t)(ring + 1) * HD;
 
@@ -79,7 +86,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     // KV ring (`smem` bytes of dynamic shared memory in all)
     const int NCOL = G * HD, ostride = q8_stride(NCOL);
     const int rpc = a.wo ? a.dim / CL : 0, row0 = sp * rpc;
-    const int kv_bytes = 2 * (ring + 1) * HD * 2;
+    const int kv_bytes = (ring + 1) * HD * 2 + vreg;
     uint8_t* wsm = sm + kv_bytes;
     const int ro = rpc ? max(1, min(rpc, (smem - kv_bytes) / ostride)) : 1;
     auto issue_o = [&](int c0) {
@@ -87,25 +94,49 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         mbar_expect_tx(&obar, bytes);
         bulk_g2s(wsm, a.wo + ((size_t)j * a.dim + row0 + c0) * ostride, bytes, &obar);
     };
-    // rows [ts, min(te, pos)) of tile tl (the row at pos is not in the cache yet)
-    auto issue = [&](int tl) {
+    // rows [ts, min(te, pos)) of tile tl (the row at pos is not in the cache yet): its K rows and/or its V rows
+    auto issue = [&](int tl, bool k, bool v) {
         const int slot = tl % n_buf, ts = k0 + tl * TILE, ce = min(min(k1, ts + TILE), pos);
-        if (ce > ts) {
-            const uint32_t bytes = (uint32_t)(ce - ts) * HD * 2;
-            mbar_expect_tx(&full[slot], 2 * bytes);
-            const uint64_t pol = l2_evict_first();
-            bulk_g2s_stream(Ks + (size_t)slot * TILE * HD, kb + (long)ts * HD, bytes, &full[slot], pol);
-            bulk_g2s_stream(Vs + (size_t)slot * TILE * HD, vb + (long)ts * HD, bytes, &full[slot], pol);
-        } else {
-            mbar_arrive(&full[slot]);  // nothing to copy: complete the phase
+        const uint64_t pol = l2_evict_first();
+        const uint32_t bytes = ce > ts ? (uint32_t)(ce - ts) * HD * 2 : 0;
+        if (k) {
+            if (bytes) {
+                mbar_expect_tx(&fk[slot], bytes);
+                bulk_g2s_stream(Ks + (size_t)slot * TILE * HD, kb + (long)ts * HD, bytes, &fk[slot], pol);
+            } else {
+                mbar_arrive(&fk[slot]);  // nothing to copy: complete the phase
+            }
+        }
+        if (v) {
+            if (bytes) {
+                mbar_expect_tx(&fv[slot], bytes);
+                bulk_g2s_stream(Vs + (size_t)slot * TILE * HD, vb + (long)ts * HD, bytes, &fv[slot], pol);
+            } else {
+                mbar_arrive(&fv[slot]);
+            }
         }
     };
     if (t == 0) {
-        for (int i = 0; i < n_buf; i++) mbar_init(&full[i], 1);
+        for (int i = 0; i < n_buf; i++) {
+            mbar_init(&fk[i], 1);
+            mbar_init(&fv[i], 1);
+        }
         mbar_init(&obar, 1);
+        mbar_init(&qbar, 1);
         mbar_fence_init();
-        for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl);
-        if (rpc > 0) issue_o(0);  // constant weights: fetched before the wait
+        // constant weights and the cache's rows below pos: fetched before the wait (the V rows after the fused
+        // projection, whose weights borrow their region)
+        for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl, true, !fq);
+        if (fq) {
+            const int ci0 = sp * RQ;  // this CTA's first row of the group's [q heads | k | v]
+            const int grow = ci0 < G * HD ? j * G * HD + ci0
+                             : ci0 < (G + 1) * HD ? a.n_head * HD + j * HD + (ci0 - G * HD)
+                                                  : (a.n_head + a.n_kv) * HD + j * HD + (ci0 - (G + 1) * HD);
+            const uint32_t bytes = (uint32_t)(RQ * a.wqkv.stride);
+            mbar_expect_tx(&qbar, bytes);
+            bulk_g2s_stream(Vs, a.wqkv.w + (size_t)grow * a.wqkv.stride, bytes, &qbar, l2_evict_first());
+        }
+        if (rpc > 0) issue_o(0);
         pdl_trigger();
         l2_next(a.next, (b * gridDim.y + j) * CL + sp, CL * gridDim.y * gridDim.z);
     }
@@ -126,7 +157,65 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             w_hi[u] = *reinterpret_cast<const float2*>(wv + 64 + d0);
         }
     }
+    const int dim = a.in.w.cols;
+    float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (fq && a.in.nw && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
+
+    // the fused qkv projection: the slot's residual staged (plus the FFN's partials, RMS-normalised), this CTA's RQ
+    // rows (RQ / NW per warp, their dots together), then the group's (G + 2)·128 values all-gathered from the cluster
+    float* qkvs = &wo[0][0][0];  // the staged row, then the gathered q | k | v (the warps' partials come later)
+    if (fq) {
+        const int nch = (dim + 511) / 512;
+        stage_x(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
+        __syncthreads();
+        constexpr int RPW = 8;  // at most 64 rows per CTA
+        const int rpw = RQ / NW;
+        const bool got = __all_sync(FULL, mbar_wait(&qbar, 0, a.err));
+        const uint64_t* xsp = reinterpret_cast<const uint64_t*>(qkvs);
+        const uint8_t* wq = reinterpret_cast<const uint8_t*>(Vs);
+        float acc[RPW];
+#pragma unroll
+        for (int k = 0; k < RPW; k++) acc[k] = 0.0f;
+        if (got)
+            for (int i = 0; i < nch; i++) {
+                const int col = i * 512 + lane * 16;
+                if (col >= dim) continue;
+                uint64_t xp[8];
+                const int base = (i * 128 + lane) * 2;
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    xp[2 * jj] = xsp[base + jj * 64];
+                    xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+                }
+#pragma unroll
+                for (int k = 0; k < RPW; k++)
+                    if (k < rpw) {
+                        const uint8_t* row = wq + (size_t)(warp * rpw + k) * a.wqkv.stride;
+                        const float d = __half2float(reinterpret_cast<const __half*>(row + dim)[col >> 5]);
+                        acc[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(row + col), xp), d, acc[k]);
+                    }
+            }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+            for (int k = 0; k < RPW; k++) acc[k] += __shfl_xor_sync(FULL, acc[k], m);
+        if (lane == 0)
+#pragma unroll
+            for (int k = 0; k < RPW; k++)
+                if (k < rpw) qv[warp * rpw + k] = acc[k];
+        cluster.sync();  // every rank's rows computed; the W_qkv region is free
+        if (t == 0) {
+            fence_proxy_async();  // the weights' generic reads before the copy engine's writes
+            for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl, false, true);
+        }
+        for (int i = t; i < (G + 2) * HD / 4; i += AT_THREADS) {
+            const int q = 4 * i;
+            const float* rp = cluster.map_shared_rank(qv, q / RQ);
+            *reinterpret_cast<float4*>(qkvs + q) = *reinterpret_cast<const float4*>(rp + q % RQ);
+        }
+        __syncthreads();
+    }
 
     // RMSNorm x weight (one warp reduction), RoPE NEOX in registers
     const bool own = pos >= k0 && pos < k1;
@@ -135,11 +224,11 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     for (int u = 0; u < HPW; u++) {
         const int h = warp + u * NW;
         if (h > G || (h == G && !own)) continue;
-        const float* xr = qkv + (long)(h < G ? j * G + h : a.n_head + j) * HD;
+        const float* xr = fq ? qkvs + (size_t)h * HD : qkv + (long)(h < G ? j * G + h : a.n_head + j) * HD;
         const float2 xa = *reinterpret_cast<const float2*>(xr + d0), xb = *reinterpret_cast<const float2*>(xr + 64 + d0);
         float2 va = make_float2(0.f, 0.f), vc = va;
         if (h == G) {
-            const float* vr = qkv + (long)(a.n_head + a.n_kv + j) * HD;
+            const float* vr = fq ? qkvs + (size_t)(G + 1) * HD : qkv + (long)(a.n_head + a.n_kv + j) * HD;
             va = *reinterpret_cast<const float2*>(vr + d0);
             vc = *reinterpret_cast<const float2*>(vr + 64 + d0);
         }
@@ -195,11 +284,12 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     for (int t0 = 0; t0 < n_tiles; t0 += n_buf) {
         const int t1 = min(n_tiles, t0 + n_buf);  // tiles t0 … t1-1 sit in slots 0 … t1-t0-1
         for (int tl = t0; tl < t1 && alive; tl++)
-            alive = __all_sync(FULL, mbar_wait(&full[tl - t0], (tl / n_buf) & 1, a.err));
+            alive = __all_sync(FULL, mbar_wait(&fk[tl - t0], (tl / n_buf) & 1, a.err));
         const int r0 = k0 + t0 * TILE, nk = min(k1, k0 + t1 * TILE) - r0;  // the round's keys [r0, r0 + nk)
         const int prel = pos - r0;  // the new row's index in the round (outside [0, nk) elsewhere)
         const int kw = (nk + NW - 1) / NW;
-        const int w0 = min(nk, warp * kw), nw = alive ? min(nk, w0 + kw) - w0 : 0;  // this warp's keys
+        const int w0 = min(nk, warp * kw);
+        int nw = alive ? min(nk, w0 + kw) - w0 : 0;  // this warp's keys
         // every pass's dot first (independent), then the passes' 8-lane reductions interleaved
         constexpr int NP = KPW / 4;  // passes of 4 keys
         float dk[NP][G];
@@ -260,6 +350,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             }
         }
         __syncwarp();
+        for (int tl = t0; tl < t1 && alive; tl++)
+            alive = __all_sync(FULL, mbar_wait(&fv[tl - t0], (tl / n_buf) & 1, a.err));
+        if (!alive) nw = 0;
         // P·V; lane owns dims 4 lane … 4 lane + 3
 #pragma unroll 4
         for (int kk = 0; kk < nw; kk++) {
@@ -281,7 +374,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             __syncthreads();
             if (t == 0) {
                 fence_proxy_async();
-                for (int tl = t1; tl < min(n_tiles, t1 + n_buf); tl++) issue(tl);
+                for (int tl = t1; tl < min(n_tiles, t1 + n_buf); tl++) issue(tl, true, true);
             }
         }
     }
@@ -457,13 +550,18 @@ static int static_smem() {
 
 template <int G, int CL>
 static cudaLaunchConfig_t config_t(cudaStream_t st, const AttnArgs& a, cudaLaunchAttribute* attr, int* n_buf) {
-    // the fused o-projection's W_o region after the ring: up to 64 rows of the CTA's slice rows
+    // the fused o-projection's W_o region after the ring: up to 64 rows of the CTA's slice rows; the fused qkv
+    // projection's W_qkv rows borrow the V region, which grows to hold them when the ring is short
     const size_t wo_bytes = a.wo ? (size_t)std::min(a.dim / CL, 64) * q8_stride(G * HD) : 0;
-    *n_buf = ring_depth(a.n_ctx, CL, static_smem<G, CL>() + (int)wo_bytes);
+    const int wq_bytes = a.wqkv.w ? (G + 2) * HD / CL * a.wqkv.stride : 0;
+    const int st_bytes = static_smem<G, CL>() + (int)wo_bytes;
+    *n_buf = ring_depth(a.n_ctx, CL, st_bytes);
+    if (wq_bytes > (*n_buf * TILE + 1) * HD * 2) *n_buf = ring_depth(a.n_ctx, CL, st_bytes + wq_bytes);
+    const size_t kreg = (size_t)(*n_buf * TILE + 1) * HD * 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)CL, (unsigned)a.n_kv, (unsigned)a.nb);
     cfg.blockDim = dim3(AT_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = (size_t)2 * (*n_buf * TILE + 1) * HD * 2 + wo_bytes;
+    cfg.dynamicSmemBytes = kreg + std::max(kreg, (size_t)wq_bytes) + wo_bytes;
     cfg.stream = st;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = CL;
@@ -518,10 +616,29 @@ static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
 }
 
 template <int G>
+static int cluster_g(const AttnArgs& a) {
+    if (a.splits == 16 && usable_t<G, 16>(nullptr, a)) return 16;
+    if (a.splits >= 8 && usable_t<G, 8>(nullptr, a)) return 8;
+    return 4;
+}
+
+int attention_cluster(const AttnArgs& a) {
+    const int G = a.n_head / a.n_kv;
+    return G == 1 ? cluster_g<1>(a) : G == 2 ? cluster_g<2>(a) : G == 4 ? cluster_g<4>(a) : cluster_g<8>(a);
+}
+
+bool attention_fuses_qkv(int g, int cl, int dim) {
+    const int rq = (g + 2) * HD / cl;  // rows per CTA: whole, within one of q / k / v, RQ / NW per warp (≤ 8)
+    return (g + 2) * HD % cl == 0 && HD % rq == 0 && rq % NW == 0 && rq / NW <= 8 && rq % 4 == 0 && dim % 32 == 0 &&
+           dim <= 1024 && (dim + 511) / 512 * 512 <= NW * g * HD;
+}
+
+template <int G>
 static void launch_g(cudaStream_t st, const AttnArgs& a, bool pdl) {
-    if (a.splits == 16 && usable_t<G, 16>(st, a)) launch_t<G, 16>(st, a, pdl);
-    else if (a.splits >= 8 && usable_t<G, 8>(st, a)) launch_t<G, 8>(st, a, pdl);
-    else if (usable_t<G, 4>(st, a)) launch_t<G, 4>(st, a, pdl);
+    const int cl = cluster_g<G>(a);
+    if (cl == 16) launch_t<G, 16>(st, a, pdl);
+    else if (cl == 8) launch_t<G, 8>(st, a, pdl);
+    else launch_t<G, 4>(st, a, pdl);
 }
 
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl) {

@@ -161,11 +161,20 @@ struct AttnArgs {
     const uint8_t* wo = nullptr;
     int dim = 0;
     float* opart = nullptr;
+    // the fused qkv projection (when wqkv.w is set; qkv is then unused): the slot's residual row is staged from `in`
+    // (as the qkv matvec would) and the cluster of kv head j computes its q heads' and its k / v rows of wqkv, each
+    // CTA (G + 2)·128 / CL consecutive ones
+    MvArgs in;
+    QMat wqkv;
     int nb = 1;
     L2Next next;
     int* err = nullptr;
 };
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);
+// the cluster size the launch of `a` will use (its `splits`, or fewer when those clusters cannot be resident)
+int attention_cluster(const AttnArgs& a);
+// true when the qkv projection can be fused for a group of g q heads in clusters of cl CTAs at this model width
+bool attention_fuses_qkv(int g, int cl, int dim);
 
 // ---- the fused FFN (k_ffn.cu) ----------------------------------------------------------------------------------------
 // One slot: x + (o-partials) → residual, RMSNorm → gate|up → SwiGLU → down, in FFN_NCLU thread-block clusters of

@@ -548,6 +548,9 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     // buffers then: the qkv kernel writes x (layer input + FFN partials), the FFN kernel x2 (x + o-partials).
     const bool fused = s->opart != nullptr;
     const bool ffn = s->dpart != nullptr && ffn_usable(c.dim, c.n_ff);
+    // the qkv projection fused into the attention (decided per layer by the clusters' shape): with the o-projection
+    // fused as well, a layer is two kernels
+    const bool fqkv = fused;
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
         float* xin = fused && !ffn && (l & 1) ? s->x2 : s->x;   // this layer's input residual
@@ -582,10 +585,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         } else {
             q.x = xin;
         }
-        launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
         const double nact = prof ? (double)prof->pos.size() : 0.0;
-        if (prof) prof->mark("qkv (norm + q|k|v)", l, mat_bytes(L.qkv) + nact * (c.dim * 8.0 + s->qkv_w * 4.0));
-
         AttnArgs a;
         a.qkv = s->qkv;
         a.qkv_stride = s->qkv_w;
@@ -616,11 +616,25 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
             a.dim = c.dim;
             a.opart = s->opart;
         }
-        launch_attention_decode(st, a, pdl);
+        // the qkv projection inside the attention clusters when their shape allows: the attention kernel stages the
+        // residual row itself (the qkv matvec's arguments) and, as that matvec would, starts the step at layer 0
+        a.in = q;
+        a.wqkv = L.qkv;
+        const bool fq = fqkv && attention_fuses_qkv(c.n_head / c.n_kv, attention_cluster(a), c.dim);
+        if (!fq) {
+            a.wqkv = QMat();
+            launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
+            if (prof) prof->mark("qkv (norm + q|k|v)", l, mat_bytes(L.qkv) + nact * (c.dim * 8.0 + s->qkv_w * 4.0));
+        }
+        launch_attention_decode(st, a, pdl && (l > 0 || !fq));
         if (prof) {
             double kv = 0;
             for (int p : prof->pos) kv += (double)(p + 1) * c.n_kv * 128 * 2 * 2;
-            if (fused)
+            if (fq)
+                prof->mark("qkv + attention + o-proj", l,
+                           mat_bytes(L.qkv) + kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
+                               nact * (c.dim * 8.0 + c.n_kv * c.dim * 4.0));
+            else if (fused)
                 prof->mark("attention + o-proj", l,
                            kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
                                nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
@@ -658,7 +672,11 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
             f.n_ff = c.n_ff;
             f.dpart = s->dpart;
             f.err = ctx->d_err;
-            if (l + 1 < c.n_layer) f.next = with_w(kv_of(l + 1), m->layers[l + 1].qkv);
+            if (l + 1 < c.n_layer) {
+                f.next = with_w(kv_of(l + 1), m->layers[l + 1].qkv);
+                f.next.w2 = m->layers[l + 1].o_s;  // read by the next attention (its o-projection)
+                f.next.w2_bytes = (size_t)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv);
+            }
             launch_ffn(st, f, pdl);
             if (prof)
                 prof->mark("ffn (gate|up, swiglu, down)", l,
@@ -738,6 +756,10 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     lm.lm.nb = s->B;
     lm.lm.err = ctx->d_err;
     lm.next = with_w(kv_of(0), m->layers[0].qkv);  // the next step's first kernels
+    if (fused) {
+        lm.next.w2 = m->layers[0].o_s;
+        lm.next.w2_bytes = (size_t)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv);
+    }
     launch_matvec(st, lm, ctx->num_sms, pdl);
     if (prof)
         prof->mark(sample ? "lm head + choice" : "lm head", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));

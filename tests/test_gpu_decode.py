@@ -198,7 +198,7 @@ def test_callback_stops_the_read(ocr, orc, ctx, tiny):
 
 
 def test_profile_step_matches_step(ocr, orc, ctx, tiny):
-    """the per-dispatch profiler runs the same step: 3 kernels per layer (the o-projection fused into the
+    """the per-dispatch profiler runs the same step: 2 kernels per layer (the qkv and o projections fused into the
     attention, the FFN one kernel) + the LM head, positive times, the slot advances, and the logits it leaves equal a
     plain step's"""
     om, gm = tiny
@@ -207,9 +207,8 @@ def test_profile_step_matches_step(ocr, orc, ctx, tiny):
     a.prefill(0, ids=prompt, logits=False)
     b.prefill(0, ids=prompt, logits=False)
     rec = a.profile_step([7])
-    assert len(rec) == 3 * TINY["n_layer"] + 1
-    assert [r["name"] for r in rec[:3]] == ["qkv (norm + q|k|v)", "attention + o-proj",
-                                            "ffn (gate|up, swiglu, down)"]
+    assert len(rec) == 2 * TINY["n_layer"] + 1
+    assert [r["name"] for r in rec[:2]] == ["qkv + attention + o-proj", "ffn (gate|up, swiglu, down)"]
     assert rec[-1]["layer"] == -1 and all(r["us"] > 0 and r["bytes"] > 0 for r in rec)
     assert a.n_past(0) == b.n_past(0) + 1
     lb = b.step([7])[0]
