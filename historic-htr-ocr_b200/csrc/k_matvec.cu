@@ -396,7 +396,9 @@ struct Geo {
 constexpr size_t SMEM_MAX = 220 * 1024;   // the streamed LM head's ring (one CTA per SM)
 constexpr size_t SMEM_SMALL = 96 * 1024;  // a small matrix's ring: two CTAs (with their static memory) per SM
 
-// streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 2 rows, a deep ring. Small matrices:
+// streamed (> 48 MB: the LM head): one CTA per SM, 16 consumer warps x 4 rows for one slot (the activation loads
+// and the per-stage waits shared by more rows; 2 for slot batches, whose accumulators need the registers), a ring
+// as deep as fits. Small matrices:
 // `per_sm` CTAs per SM (two when registers and shared memory allow), 8 consumer warps (x 2 rows for SwiGLU pairs,
 // else 1), one or two stages each. The grid is one wave: a CTA that cannot be resident with the others would stream
 // its rows after them.
@@ -409,7 +411,7 @@ static Geo geometry(const MvArgs& a, int nb_pass, int num_sms, int per_sm = 2) {
     const int target = big ? num_sms : per_sm * num_sms;
     if (big) {
         g.W = 16;
-        g.R = 2;
+        g.R = nb_pass == 1 ? 4 : 2;
     } else if (a.mode == MV_SWIGLU) {
         g.W = 8;
         g.R = 2;
@@ -488,7 +490,7 @@ template <int NB>
 static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
     Geo g = geometry(a, NB, num_sms);
     if (g.W == 16) {
-        launch_t<NB, 16, 2>(st, a, g, pdl);
+        launch_t<NB, 16, NB == 1 ? 4 : 2>(st, a, g, pdl);
     } else if (g.R == 2) {
         if (per_sm_t<NB, 8, 2>() < 2) g = geometry(a, NB, num_sms, 1);
         launch_t<NB, 8, 2>(st, a, g, pdl);
