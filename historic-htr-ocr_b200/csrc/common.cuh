@@ -168,6 +168,17 @@ __device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint
         : "memory");
 }
 
+// one bulk copy as pieces of at most 4 KB, issued by the `n` lanes of the calling warp (lane i: pieces i, i + n, …):
+// the copy engine then works on several at once rather than one long copy. Every lane calls it; the barrier's
+// expected bytes (the whole copy) were raised by one lane before a __syncwarp.
+__device__ __forceinline__ void bulk_g2s_lanes(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy, int lane, int n) {
+    constexpr uint32_t PIECE = 4096;
+    for (uint32_t o = (uint32_t)lane * PIECE; o < bytes; o += (uint32_t)n * PIECE)
+        bulk_g2s_stream(static_cast<uint8_t*>(dst) + o, static_cast<const uint8_t*>(src) + o, min(PIECE, bytes - o), bar,
+                        policy);
+}
+
 // a barrier among the first `threads` threads of the CTA (named barrier 1; the producer warp stays out)
 __device__ __forceinline__ void bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -192,20 +192,20 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
     uint32_t bil = NO_INDEX;
 
     if (warp == W) {
-        // ---- producer: weights never depend on the previous kernel, so no griddepcontrol.wait here ----
-        if (lane == 0) {
-            const uint64_t pol = l2_evict_first();
-            for (int t = 0; t < n_stage; t++) {
-                const int slot = t % ns;
-                if (t >= ns && !mbar_wait(&empty[slot], ((t / ns) - 1) & 1, a.err)) break;
-                const int r0 = lo + t * SR;
-                const uint32_t bytes = (uint32_t)(min(SR, hi - r0) * stride);
-                mbar_expect_tx(&full[slot], bytes);
-                bulk_g2s_stream(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot], pol);
-                if (t == min(ns, n_stage) - 1) {
-                    pdl_trigger();
-                    l2_next(a.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
-                }
+        // ---- producer: weights never depend on the previous kernel, so no griddepcontrol.wait here. The warp
+        // waits for a free slot, lane 0 arms its barrier, every lane issues its 4 KB pieces of the stage. ----
+        const uint64_t pol = l2_evict_first();
+        for (int t = 0; t < n_stage; t++) {
+            const int slot = t % ns;
+            if (t >= ns && !__all_sync(FULL, mbar_wait(&empty[slot], ((t / ns) - 1) & 1, a.err))) break;
+            const int r0 = lo + t * SR;
+            const uint32_t bytes = (uint32_t)(min(SR, hi - r0) * stride);
+            if (lane == 0) mbar_expect_tx(&full[slot], bytes);
+            __syncwarp();
+            bulk_g2s_lanes(ring + slot * stage_bytes, a.w.w + (size_t)r0 * stride, bytes, &full[slot], pol, lane, 32);
+            if (t == min(ns, n_stage) - 1 && lane == 0) {
+                pdl_trigger();
+                l2_next(a.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
             }
         }
     } else {
