@@ -77,34 +77,37 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
     const bool got_gu = __all_sync(FULL, mbar_wait(&bar_gu, 0, a.err));
     const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xs);
-    // up to PB pairs per warp at once: every dot first, then the reductions interleaved
+    // up to PB pairs per warp at once (each chunk's x loaded once for all of them): every dot first, then the
+    // reductions interleaved
     constexpr int PB = 4;
     for (int p0 = warp; p0 < HR; p0 += FFN_NW * PB) {
         float g[PB], u[PB];
 #pragma unroll
-        for (int k = 0; k < PB; k++) {
-            g[k] = u[k] = 0.0f;
-            const int p = p0 + k * FFN_NW;
-            if (got_gu && p < HR) {
-                const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
-                const uint8_t* ru = rg + gstride;
-                for (int i = 0; i < nch; i++) {
-                    const int col = i * 512 + lane * 16;
-                    if (col >= dim) continue;
-                    uint64_t xp[8];
-                    const int base = (i * 128 + lane) * 2;
+        for (int k = 0; k < PB; k++) g[k] = u[k] = 0.0f;
+        if (got_gu)
+            for (int i = 0; i < nch; i++) {
+                const int col = i * 512 + lane * 16;
+                if (col >= dim) continue;
+                uint64_t xp[8];
+                const int base = (i * 128 + lane) * 2;
 #pragma unroll
-                    for (int jj = 0; jj < 4; jj++) {
-                        xp[2 * jj] = xsp[base + jj * 64];
-                        xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+                for (int jj = 0; jj < 4; jj++) {
+                    xp[2 * jj] = xsp[base + jj * 64];
+                    xp[2 * jj + 1] = xsp[base + jj * 64 + 1];
+                }
+#pragma unroll
+                for (int k = 0; k < PB; k++) {
+                    const int p = p0 + k * FFN_NW;
+                    if (p < HR) {
+                        const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
+                        const uint8_t* ru = rg + gstride;
+                        const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
+                        const float du = __half2float(reinterpret_cast<const __half*>(ru + dim)[col >> 5]);
+                        g[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(rg + col), xp), dg, g[k]);
+                        u[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(ru + col), xp), du, u[k]);
                     }
-                    const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
-                    const float du = __half2float(reinterpret_cast<const __half*>(ru + dim)[col >> 5]);
-                    g[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(rg + col), xp), dg, g[k]);
-                    u[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(ru + col), xp), du, u[k]);
                 }
             }
-        }
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
