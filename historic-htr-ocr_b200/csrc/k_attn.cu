@@ -19,8 +19,15 @@
 // decode step): a reduce-scatter (each CTA merges its slice from float4 copies of the ranks' partials) and an
 // all-gather (every CTA reads every slice) leave the group's whole output in every CTA, which multiplies it by its
 // dim/CL rows of W_o's slice for this kv head (fetched before the dependency wait) into opart[b][j] — the o-projection
-// as n_kv per-head partial products, summed in a fixed order by the next kernel. mbarrier waits are bounded; a warp
-// whose wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets every barrier.
+// as n_kv per-head partial products, summed in a fixed order by the next kernel.
+//
+// Fused qkv (a.wqkv set; the reference's dmv_qkv.wgsl): the cluster also computes its group's (G + 2)·128 rows of
+// the [q | k | v] projection. CTA r stages the slot's residual (plus the FFN's partials, RMS-normalised by attn_norm:
+// stage.cuh, as the qkv matvec would), multiplies it by its RQ = (G + 2)·128 / CL rows of W_qkv — fetched before the
+// dependency wait into the V region, whose V tiles are copied once the projection is done — and the cluster
+// all-gathers the group's values through distributed shared memory before the q/k preparation. mbarrier waits are
+// bounded; a warp whose wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets
+// every barrier.
 #include <cooperative_groups.h>
 
 #include <algorithm>

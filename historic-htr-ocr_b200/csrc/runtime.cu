@@ -541,15 +541,15 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     };
     // Fused (the decode shapes this engine targets): the attention cluster of each kv head also multiplies its heads'
     // output by its slice of W_o, and the gate/up kernel sums those n_kv partial products onto the residual, which
-    // it writes to the other of two residual buffers (its other CTAs are still reading the first) — 4 kernels per
-    // layer. Otherwise the o-projection is its own kernel, adding in place.
+    // it writes to the other of two residual buffers (its other CTAs are still reading the first). Otherwise the
+    // o-projection is its own kernel, adding in place.
     // One slot with a fitting shape goes further: the FFN is one kernel of FFN_NCLU clusters whose down-projection
-    // partials the next layer's qkv kernel (or the LM head) sums onto the residual — 3 kernels per layer. Residual
-    // buffers then: the qkv kernel writes x (layer input + FFN partials), the FFN kernel x2 (x + o-partials).
+    // partials the next layer's first kernel (or the LM head) sums onto the residual. Residual buffers then: the
+    // layer's first kernel writes x (layer input + FFN partials), the FFN kernel x2 (x + o-partials).
+    // With the o-projection fused, the qkv projection moves into the attention clusters too when their shape allows
+    // (decided per layer): the attention kernel stages the residual itself. One slot: 2 kernels per layer.
     const bool fused = s->opart != nullptr;
     const bool ffn = s->dpart != nullptr && ffn_usable(c.dim, c.n_ff);
-    // the qkv projection fused into the attention (decided per layer by the clusters' shape): with the o-projection
-    // fused as well, a layer is two kernels
     const bool fqkv = fused;
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
