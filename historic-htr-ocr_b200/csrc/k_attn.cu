@@ -448,34 +448,46 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     }
     // fused: reduce-scatter (this CTA merges its slice from the ranks' partials, copied in float4s), then all-gather
     // (every CTA reads every slice) — the group's whole output in every CTA, the o-projection's input. Scratch in the
-    // idle KV ring: the ranks' slice values [CL][PER], their (m, l) [CL][G][2], this CTA's merged slice [PER].
+    // idle KV ring: the ranks' slice values [CL][PER], their (m, l) for the slice's head [CL][2], the weights
+    // e^(m_r − M) [CL] and their sum L, this CTA's merged slice [PER] (16-B aligned for the all-gather's float4s).
+    const int gs = q0 / HD;  // the slice lies within one head
     float* rsl = reinterpret_cast<float*>(sm);
     float* rml = rsl + CL * PER;
-    float* mine = rml + CL * G * 2;
-    for (int i = t; i < CL * (PER / 4); i += AT_THREADS) {
-        const int r = i / (PER / 4), q = q0 + 4 * (i % (PER / 4));
-        const float* rp = cluster.map_shared_rank(&part[0][0], r);
-        reinterpret_cast<float4*>(rsl)[i] = *reinterpret_cast<const float4*>(rp + (q / HD) * PW + q % HD);
-    }
-    for (int i = t; i < CL * G; i += AT_THREADS) {
-        const float* rp = cluster.map_shared_rank(&part[0][0], i / G);
-        reinterpret_cast<float2*>(rml)[i] = *reinterpret_cast<const float2*>(rp + (i % G) * PW + HD);
+    float* ew = rml + CL * 2;
+    float* mine = ew + CL + 4;
+    constexpr int NSL = CL * (PER / 4);
+    for (int i = t; i < NSL + CL; i += AT_THREADS) {
+        if (i < NSL) {
+            const int r = i / (PER / 4), q = q0 + 4 * (i % (PER / 4));
+            const float* rp = cluster.map_shared_rank(&part[0][0], r);
+            reinterpret_cast<float4*>(rsl)[i] = *reinterpret_cast<const float4*>(rp + (q / HD) * PW + q % HD);
+        } else {
+            const float* rp = cluster.map_shared_rank(&part[0][0], i - NSL);
+            reinterpret_cast<float2*>(rml)[i - NSL] = *reinterpret_cast<const float2*>(rp + gs * PW + HD);
+        }
     }
     __syncthreads();
-    for (int i = t; i < PER; i += AT_THREADS) {
-        const int g = (q0 + i) / HD;
+    // the slice's weights once (lane r of warp 0), L summed over the ranks in order, then one output per thread —
+    // the same operations in the same order as merging each output on its own
+    if (warp == 0) {
         float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < CL; r++) M = fmaxf(M, rml[(r * G + g) * 2]);
-        float L = 0.0f, O = 0.0f;
+        for (int r = 0; r < CL; r++) M = fmaxf(M, rml[2 * r]);
+        const float m = lane < CL ? rml[2 * lane] : -INFINITY;
+        const float e = m == -INFINITY ? 0.0f : expf(m - M);
+        float L = 0.0f;
 #pragma unroll
-        for (int r = 0; r < CL; r++) {
-            const float m = rml[(r * G + g) * 2];
-            const float e = m == -INFINITY ? 0.0f : expf(m - M);
-            L = fmaf(rml[(r * G + g) * 2 + 1], e, L);
-            O = fmaf(rsl[r * PER + i], e, O);
-        }
-        mine[i] = O / L;
+        for (int r = 0; r < CL; r++) L = fmaf(rml[2 * r + 1], __shfl_sync(FULL, e, r), L);
+        if (lane < CL) ew[lane] = e;
+        if (lane == 0) ew[CL] = L;
+    }
+    if (PER <= 32) __syncwarp();  // the outputs are warp 0's own
+    else __syncthreads();
+    for (int i = t; i < PER; i += AT_THREADS) {
+        float O = 0.0f;
+#pragma unroll
+        for (int r = 0; r < CL; r++) O = fmaf(rsl[r * PER + i], ew[r], O);
+        mine[i] = O / ew[CL];
     }
     cluster.sync();  // every slice merged; no rank reads `part` any more
     float* att = &wo[0][0][0];  // the warps' partial outputs are folded into part: reuse

@@ -115,10 +115,15 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
                 g[k] += __shfl_xor_sync(FULL, g[k], m);
                 u[k] += __shfl_xor_sync(FULL, u[k], m);
             }
-        if (lane == 0)
+        // every lane holds the sums: lane k finishes pair k (the SwiGLUs side by side)
+        float gk = g[0], uk = u[0];
 #pragma unroll
-            for (int k = 0; k < PB; k++)
-                if (p0 + k * FFN_NW < HR) hs[p0 + k * FFN_NW] = g[k] / (1.0f + expf(-g[k])) * u[k];
+        for (int k = 1; k < PB; k++)
+            if (lane == k) {
+                gk = g[k];
+                uk = u[k];
+            }
+        if (lane < PB && p0 + lane * FFN_NW < HR) hs[p0 + lane * FFN_NW] = gk / (1.0f + expf(-gk)) * uk;
     }
     // the cluster's h slice, in every CTA of it (lane-blocked for the down rows' dot)
     cluster.sync();
