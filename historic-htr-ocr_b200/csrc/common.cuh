@@ -137,6 +137,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// bounded wait on bars[0 … n) (n ≤ N) for the same phase, their polls issued side by side
+template <int N>
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bars, int n, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++) {
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < N; k++)
+            if (k < n) ok &= mbar_try_wait(&bars[k], parity);
+        if (ok) return true;
+    }
+    dev_error(err, DEV_TIMEOUT);
+    return false;
+}
+
 // global → shared, `bytes` (multiple of 16, both addresses 16-B aligned), completion counted on `bar`
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(

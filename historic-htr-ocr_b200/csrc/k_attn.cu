@@ -269,29 +269,29 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     // scores: 8 lanes per key, lane prt takes dims prt*8 … +7 and 64 + prt*8 … +7 (a quarter-warp's 16-byte reads
     // cover 128 consecutive bytes: no bank conflict)
     const int sub = lane >> 3, prt = lane & 7;
-    float qr[G][16];
+    // q as f32 pairs: [0, 4) dims prt*8 …, [4, 8) dims 64 + prt*8 …
+    uint64_t qp[G][8];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         const float4* q4 = reinterpret_cast<const float4*>(&qs[g][0]);
         const float4 qa = q4[prt * 2], qb = q4[prt * 2 + 1], qc = q4[16 + prt * 2], qd = q4[16 + prt * 2 + 1];
-        qr[g][0] = qa.x; qr[g][1] = qa.y; qr[g][2] = qa.z; qr[g][3] = qa.w;
-        qr[g][4] = qb.x; qr[g][5] = qb.y; qr[g][6] = qb.z; qr[g][7] = qb.w;
-        qr[g][8] = qc.x; qr[g][9] = qc.y; qr[g][10] = qc.z; qr[g][11] = qc.w;
-        qr[g][12] = qd.x; qr[g][13] = qd.y; qr[g][14] = qd.z; qr[g][15] = qd.w;
+        qp[g][0] = pk2(qa.x, qa.y); qp[g][1] = pk2(qa.z, qa.w); qp[g][2] = pk2(qb.x, qb.y); qp[g][3] = pk2(qb.z, qb.w);
+        qp[g][4] = pk2(qc.x, qc.y); qp[g][5] = pk2(qc.z, qc.w); qp[g][6] = pk2(qd.x, qd.y); qp[g][7] = pk2(qd.z, qd.w);
     }
-    float mw[G], lw[G], ow[G][4];
+    // per head the running max, sum and this lane's 4 output dims as two f32 pairs
+    float mw[G], lw[G];
+    uint64_t o2[G][2];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         mw[g] = -INFINITY;
         lw[g] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; i++) ow[g][i] = 0.0f;
+        o2[g][0] = o2[g][1] = 0;
     }
     bool alive = true;
     for (int t0 = 0; t0 < n_tiles; t0 += n_buf) {
         const int t1 = min(n_tiles, t0 + n_buf);  // tiles t0 … t1-1 sit in slots 0 … t1-t0-1
-        for (int tl = t0; tl < t1 && alive; tl++)
-            alive = __all_sync(FULL, mbar_wait(&fk[tl - t0], (tl / n_buf) & 1, a.err));
+        // (the round's slots share its phase)
+        alive = alive && __all_sync(FULL, mbar_wait_n<MAX_BUF>(fk, t1 - t0, (t0 / n_buf) & 1, a.err));
         const int r0 = k0 + t0 * TILE, nk = min(k1, k0 + t1 * TILE) - r0;  // the round's keys [r0, r0 + nk)
         const int prel = pos - r0;  // the new row's index in the round (outside [0, nk) elsewhere)
         const int kw = (nk + NW - 1) / NW;
@@ -303,9 +303,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
         for (int ps = 0; ps < NP; ps++) {
             const int kk = ps * 4 + sub;
-            float d[G], e[G];
+            uint64_t d[G], e[G];
 #pragma unroll
-            for (int g = 0; g < G; g++) d[g] = e[g] = 0.0f;
+            for (int g = 0; g < G; g++) d[g] = e[g] = 0;
             if (kk < nw) {
                 const int i = w0 + kk;
                 const __half* kr = Ks + (size_t)(i == prel ? ring : i) * HD;
@@ -316,17 +316,19 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
                     const float2 f0 = __half22float2(h0[c]), f1 = __half22float2(h1[c]);
+                    const uint64_t k0p = pk2(f0.x, f0.y), k1p = pk2(f1.x, f1.y);
 #pragma unroll
                     for (int g = 0; g < G; g++) {
-                        d[g] = fmaf(qr[g][2 * c], f0.x, d[g]);
-                        d[g] = fmaf(qr[g][2 * c + 1], f0.y, d[g]);
-                        e[g] = fmaf(qr[g][8 + 2 * c], f1.x, e[g]);
-                        e[g] = fmaf(qr[g][8 + 2 * c + 1], f1.y, e[g]);
+                        d[g] = fma2(qp[g][c], k0p, d[g]);
+                        e[g] = fma2(qp[g][4 + c], k1p, e[g]);
                     }
                 }
             }
 #pragma unroll
-            for (int g = 0; g < G; g++) dk[ps][g] = d[g] + e[g];
+            for (int g = 0; g < G; g++) {
+                const float2 s2 = upk2(add2(d[g], e[g]));
+                dk[ps][g] = s2.x + s2.y;
+            }
         }
 #pragma unroll
         for (int m = 4; m >= 1; m >>= 1)
@@ -351,14 +353,14 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
                 const float p = lane < nw ? expf(sc - mn) : 0.0f;
                 if (lane < nw) scw[warp][g][lane] = p;
                 lw[g] = fmaf(lw[g], corr, warp_sum(p));
-#pragma unroll
-                for (int c = 0; c < 4; c++) ow[g][c] *= corr;
+                const uint64_t c2 = pk2(corr, corr);
+                o2[g][0] = mul2(o2[g][0], c2);
+                o2[g][1] = mul2(o2[g][1], c2);
                 mw[g] = mn;
             }
         }
         __syncwarp();
-        for (int tl = t0; tl < t1 && alive; tl++)
-            alive = __all_sync(FULL, mbar_wait(&fv[tl - t0], (tl / n_buf) & 1, a.err));
+        alive = alive && __all_sync(FULL, mbar_wait_n<MAX_BUF>(fv, t1 - t0, (t0 / n_buf) & 1, a.err));
         if (!alive) nw = 0;
         // P·V; lane owns dims 4 lane … 4 lane + 3
 #pragma unroll 4
@@ -367,13 +369,13 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             const uint2 u = *reinterpret_cast<const uint2*>(Vs + (size_t)(i == prel ? ring : i) * HD + lane * 4);
             const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
             const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            const uint64_t v01 = pk2(v0.x, v0.y), v23 = pk2(v1.x, v1.y);
 #pragma unroll
             for (int g = 0; g < G; g++) {
                 const float p = scw[warp][g][kk];
-                ow[g][0] = fmaf(p, v0.x, ow[g][0]);
-                ow[g][1] = fmaf(p, v0.y, ow[g][1]);
-                ow[g][2] = fmaf(p, v1.x, ow[g][2]);
-                ow[g][3] = fmaf(p, v1.y, ow[g][3]);
+                const uint64_t pp = pk2(p, p);
+                o2[g][0] = fma2(pp, v01, o2[g][0]);
+                o2[g][1] = fma2(pp, v23, o2[g][1]);
             }
         }
         if (t1 < n_tiles) {
@@ -393,8 +395,10 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             wl[warp][g] = lw[g];
         }
 #pragma unroll
-    for (int g = 0; g < G; g++)
-        *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(ow[g][0], ow[g][1], ow[g][2], ow[g][3]);
+    for (int g = 0; g < G; g++) {
+        const float2 o01 = upk2(o2[g][0]), o23 = upk2(o2[g][1]);
+        *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o01.x, o01.y, o23.x, o23.y);
+    }
     const bool ok = __syncthreads_and(alive);  // a warp whose copy wait ran out voids the CTA's partial
     for (int q = t; q < G * HD; q += AT_THREADS) {
         const int g = q / HD, d = q % HD;

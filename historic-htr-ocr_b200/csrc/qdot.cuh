@@ -28,6 +28,11 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 
 // 16 int8 quants (one 16-B load) · 16 activations (8 f32 pairs): each byte, biased to q + 128, is placed in the
 // mantissa of 2^23 by one byte permute and 2^23 + 128 is subtracted pairwise (exact: integers below 2^24); the pairs
