@@ -137,6 +137,45 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// ---- pushes into another CTA's shared memory (thread-block clusters) ----
+// the cluster address of this CTA's shared variable `p` in the CTA of cluster rank `rank`
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// stores into a cluster peer's shared memory (addresses from cluster_addr), each counting its bytes as complete-tx on
+// the peer's mbarrier `rbar`: the peer waits on its own barrier for everything pushed to it
+__device__ __forceinline__ void st_async(uint32_t raddr, float v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+                 "r"(__float_as_uint(v)), "r"(rbar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async(uint32_t raddr, float4 v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+                 "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+                 "r"(__float_as_uint(v.w)), "r"(rbar)
+                 : "memory");
+}
+// the split cluster barrier (every thread of every CTA, in the same order): arrive, later wait
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// a bounded wait for a phase whose bytes other CTAs of the cluster pushed (acquire at cluster scope)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+            : "memory");
+        if (ok) return true;
+    }
+    dev_error(err, DEV_TIMEOUT);
+    return false;
+}
+
 // bounded wait on bars[0 … n) (n ≤ N) for the same phase, their polls issued side by side
 template <int N>
 __device__ __forceinline__ bool mbar_wait_n(uint64_t* bars, int n, uint32_t parity, int* err) {

@@ -53,8 +53,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     __shared__ __align__(8) uint64_t fk[MAX_BUF], fv[MAX_BUF];  // a ring slot's K rows, its V rows
     __shared__ __align__(8) uint64_t obar;  // W_o slice chunks (fused o-projection)
     __shared__ __align__(8) uint64_t qbar;  // the W_qkv rows (fused qkv projection)
+    __shared__ __align__(8) uint64_t gbar;  // the group's projected values, pushed by the cluster (fused qkv)
     __shared__ float red[NW];
-    __shared__ __align__(16) float qv[64];  // this CTA's qkv rows (fused qkv projection), read by the cluster
+    __shared__ __align__(16) float gq[G <= 4 ? (G + 2) * HD : 4];  // the group's [q heads | k | v] (fused qkv, G ≤ 4)
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float scw[NW][G][KPW];  // per warp: the round's scores, then probabilities
     __shared__ float wm[NW][G], wl[NW][G];
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     // when the qkv projection is fused (it is at least as large as those) — then the W_o region; tile tl occupies
     // rows (tl % n_buf) * TILE …, row `ring` holds the new token's K (V), written here rather than copied
     const int ring = n_buf * TILE;
-    const bool fq = a.wqkv.w != nullptr;
+    const bool fq = G <= 4 && a.wqkv.w != nullptr;
     const int RQ = (G + 2) * HD / CL;  // the fused qkv projection: this CTA's rows of the group's [q | k | v] rows
     const int vreg = max((ring + 1) * HD * 2, fq ? RQ * a.wqkv.stride : 0);
     __half* Ks = reinterpret_cast<__half*>(sm);
@@ -130,7 +131,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         }
         mbar_init(&obar, 1);
         mbar_init(&qbar, 1);
+        mbar_init(&gbar, 1);
         mbar_fence_init();
+        if (fq) mbar_expect_tx(&gbar, (uint32_t)(G + 2) * HD * 4);
         // constant weights and the cache's rows below pos: fetched before the wait (the V rows after the fused
         // projection, whose weights borrow their region)
         for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl, true, !fq);
@@ -164,14 +167,17 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             w_hi[u] = *reinterpret_cast<const float2*>(wv + 64 + d0);
         }
     }
+    if (fq) cluster_arrive_relaxed();  // every barrier initialised before a peer pushes (waited below)
     const int dim = a.in.w.cols;
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (fq && a.in.nw && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
 
     // the fused qkv projection: the slot's residual staged (plus the FFN's partials, RMS-normalised), this CTA's RQ
-    // rows (RQ / NW per warp, their dots together), then the group's (G + 2)·128 values all-gathered from the cluster
-    float* qkvs = &wo[0][0][0];  // the staged row, then the gathered q | k | v (the warps' partials come later)
+    // rows (RQ / NW per warp, their dots together), each value pushed into every CTA of the cluster (st.async into
+    // gq, counted on the peers' gbar), so every CTA holds the group's (G + 2)·128 values once its gbar completes
+    float* qkvs = &wo[0][0][0];  // the staged row (the warps' partials come later)
+    bool got_g = true;
     if (fq) {
         const int nch = (dim + 511) / 512;
         stage_x(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
@@ -207,21 +213,22 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
             for (int k = 0; k < RPW; k++) acc[k] += __shfl_xor_sync(FULL, acc[k], m);
-        if (lane == 0)
+        // every lane holds the warp's rpw values: (value k, rank rr) pairs spread over the lanes
+        cluster_wait();
+        for (int idx = lane; idx < rpw * CL; idx += 32) {
+            const int k = idx / CL, rr = idx % CL;
+            float v = acc[0];
 #pragma unroll
-            for (int k = 0; k < RPW; k++)
-                if (k < rpw) qv[warp * rpw + k] = acc[k];
-        cluster.sync();  // every rank's rows computed; the W_qkv region is free
+            for (int kk = 1; kk < RPW; kk++)
+                if (k == kk) v = acc[kk];
+            st_async(cluster_addr(&gq[sp * RQ + warp * rpw + k], rr), v, cluster_addr(&gbar, rr));
+        }
+        __syncthreads();  // every warp done with the W_qkv rows: their region takes the V tiles
         if (t == 0) {
             fence_proxy_async();  // the weights' generic reads before the copy engine's writes
             for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl, false, true);
         }
-        for (int i = t; i < (G + 2) * HD / 4; i += AT_THREADS) {
-            const int q = 4 * i;
-            const float* rp = cluster.map_shared_rank(qv, q / RQ);
-            *reinterpret_cast<float4*>(qkvs + q) = *reinterpret_cast<const float4*>(rp + q % RQ);
-        }
-        __syncthreads();
+        got_g = __all_sync(FULL, mbar_wait_cluster(&gbar, 0, a.err));  // (if not, the CTA's partial is void)
     }
 
     // RMSNorm x weight (one warp reduction), RoPE NEOX in registers
@@ -231,11 +238,15 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     for (int u = 0; u < HPW; u++) {
         const int h = warp + u * NW;
         if (h > G || (h == G && !own)) continue;
-        const float* xr = fq ? qkvs + (size_t)h * HD : qkv + (long)(h < G ? j * G + h : a.n_head + j) * HD;
+        const float* xr = qkv + (long)(h < G ? j * G + h : a.n_head + j) * HD;
+        if constexpr (G <= 4)
+            if (fq) xr = gq + (size_t)h * HD;
         const float2 xa = *reinterpret_cast<const float2*>(xr + d0), xb = *reinterpret_cast<const float2*>(xr + 64 + d0);
         float2 va = make_float2(0.f, 0.f), vc = va;
         if (h == G) {
-            const float* vr = fq ? qkvs + (size_t)(G + 1) * HD : qkv + (long)(a.n_head + a.n_kv + j) * HD;
+            const float* vr = qkv + (long)(a.n_head + a.n_kv + j) * HD;
+            if constexpr (G <= 4)
+                if (fq) vr = gq + (size_t)(G + 1) * HD;
             va = *reinterpret_cast<const float2*>(vr + d0);
             vc = *reinterpret_cast<const float2*>(vr + 64 + d0);
         }
@@ -287,7 +298,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         lw[g] = 0.0f;
         o2[g][0] = o2[g][1] = 0;
     }
-    bool alive = true;
+    bool alive = got_g;
     for (int t0 = 0; t0 < n_tiles; t0 += n_buf) {
         const int t1 = min(n_tiles, t0 + n_buf);  // tiles t0 … t1-1 sit in slots 0 … t1-t0-1
         // (the round's slots share its phase)
@@ -652,7 +663,7 @@ int attention_cluster(const AttnArgs& a) {
 
 bool attention_fuses_qkv(int g, int cl, int dim) {
     const int rq = (g + 2) * HD / cl;  // rows per CTA: whole, within one of q / k / v, RQ / NW per warp (≤ 8)
-    return (g + 2) * HD % cl == 0 && HD % rq == 0 && rq % NW == 0 && rq / NW <= 8 && rq % 4 == 0 && dim % 32 == 0 &&
+    return g <= 4 && (g + 2) * HD % cl == 0 && HD % rq == 0 && rq % NW == 0 && rq / NW <= 8 && rq % 4 == 0 && dim % 32 == 0 &&
            dim <= 1024 && (dim + 511) / 512 * 512 <= NW * g * HD;
 }
 

@@ -6,10 +6,12 @@
 // gate|up matrix, and rows [r·dim/FFN_CL, …) of W_down's column slice c. Both are constant, so both bulk copies are
 // issued before the dependency wait. After it: the residual x plus the attention's per-head o-projection partials
 // (summed in order; the grid's first CTA writes the sum back as the new residual), RMS-normalised — the shared
-// staging of stage.cuh — then one warp per gate/up row pair, SwiGLU, the HR values to shared memory; the cluster
-// all-gathers its HC values through distributed shared memory and each CTA multiplies them by its W_down rows into
-// the cluster's partial product of the down projection, dpart[c]. The next kernel adds x + dpart[0] + … in order.
-// mbarrier waits are bounded (error flag, work skipped, every barrier still met).
+// staging of stage.cuh — then one warp per gate/up row pair and SwiGLU; each of the HR values is pushed straight
+// from registers into every CTA of the cluster (st.async into the peers' shared memory, counted on their mbarrier),
+// so each CTA holds the cluster's HC values once its barrier completes — no cluster barrier on that path — and
+// multiplies them by its W_down rows into the cluster's partial product of the down projection, dpart[c]. The next
+// kernel adds x + dpart[0] + … in order. mbarrier waits are bounded (error flag, work skipped, every barrier still
+// met).
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -23,9 +25,9 @@ namespace ocr {
 constexpr int FFN_THREADS = 256;
 constexpr int FFN_NW = FFN_THREADS / 32;
 
-// shared layout (bytes): gate|up rows, W_down rows, x (lane-blocked), this CTA's h, the cluster's h (lane-blocked)
+// shared layout (bytes): gate|up rows, W_down rows, x (lane-blocked), the cluster's h (lane-blocked)
 struct FfnSmem {
-    int gu, wd, xs, hs, hall, total;
+    int gu, wd, xs, hall, total;
 };
 __host__ __device__ inline FfnSmem ffn_layout(int dim, int n_ff) {
     const int HC = n_ff / FFN_NCLU, HR = HC / FFN_CL;
@@ -33,17 +35,15 @@ __host__ __device__ inline FfnSmem ffn_layout(int dim, int n_ff) {
     m.gu = 0;
     m.wd = m.gu + 2 * HR * q8_stride(dim);
     m.xs = m.wd + (dim / FFN_CL) * q8_stride(HC);
-    m.hs = m.xs + ((dim + 511) / 512) * 512 * 4;
-    m.hall = m.hs + (HR * 4 + 15) / 16 * 16;
+    m.hall = m.xs + ((dim + 511) / 512) * 512 * 4;
     m.total = m.hall + ((HC + 511) / 512) * 512 * 4;
     return m;
 }
 
 __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ __align__(8) uint64_t bar_gu, bar_wd;
+    __shared__ __align__(8) uint64_t bar_gu, bar_wd, bar_h;
     __shared__ float red[FFN_NW];
-    cg::cluster_group cluster = cg::this_cluster();
     const int r = blockIdx.x, c = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int dim = a.in.w.cols, HC = a.n_ff / FFN_NCLU, HR = HC / FFN_CL, drows = dim / FFN_CL;
     const int gstride = q8_stride(dim), dstride = q8_stride(HC);
@@ -51,12 +51,14 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     uint8_t* gsm = sm + L.gu;
     uint8_t* dsm = sm + L.wd;
     float* xs = reinterpret_cast<float*>(sm + L.xs);
-    float* hs = reinterpret_cast<float*>(sm + L.hs);
     float* hall = reinterpret_cast<float*>(sm + L.hall);
+    const int nchh = (HC + 511) / 512;
     if (t == 0) {
         mbar_init(&bar_gu, 1);
         mbar_init(&bar_wd, 1);
+        mbar_init(&bar_h, 1);
         mbar_fence_init();
+        mbar_expect_tx(&bar_h, (uint32_t)HC * 4);  // the cluster's h values, pushed by the CTAs that own them
         const uint64_t pol = l2_evict_first();
         const uint32_t gbytes = (uint32_t)(2 * HR * gstride), dbytes = (uint32_t)(drows * dstride);
         mbar_expect_tx(&bar_gu, gbytes);
@@ -66,6 +68,10 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
         pdl_trigger();
         l2_next(a.next, c * FFN_CL + r, FFN_NCLU * FFN_CL);
     }
+    // hall's pad columns past HC are this CTA's own zeros; every barrier initialised before any CTA pushes
+    for (int q = HC + 4 * t; q < nchh * 512; q += 4 * FFN_THREADS)
+        *reinterpret_cast<float4*>(&hall[xs_index(0, nchh, q)]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    cluster_arrive_relaxed();
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (a.in.nw && dim <= 4 * FFN_THREADS && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
@@ -76,6 +82,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
 
     // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
     const bool got_gu = __all_sync(FULL, mbar_wait(&bar_gu, 0, a.err));
+    cluster_wait();  // (the peers' barriers are ready)
     const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xs);
     // up to PB pairs per warp at once (each chunk's x loaded once for all of them): every dot first, then the
     // reductions interleaved
@@ -115,7 +122,8 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
                 g[k] += __shfl_xor_sync(FULL, g[k], m);
                 u[k] += __shfl_xor_sync(FULL, u[k], m);
             }
-        // every lane holds the sums: lane k finishes pair k (the SwiGLUs side by side)
+        // every lane holds the sums: lane k finishes pair k (the SwiGLUs side by side), then pushes go out 8 lanes
+        // per value: value k = lane / 8 to ranks lane % 8, lane % 8 + 8 (its place in every CTA's lane-blocked h)
         float gk = g[0], uk = u[0];
 #pragma unroll
         for (int k = 1; k < PB; k++)
@@ -123,21 +131,17 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
                 gk = g[k];
                 uk = u[k];
             }
-        if (lane < PB && p0 + lane * FFN_NW < HR) hs[p0 + lane * FFN_NW] = gk / (1.0f + expf(-gk)) * uk;
+        const float h = gk / (1.0f + expf(-gk)) * uk;
+        const int k = lane >> 3, p = p0 + k * FFN_NW;
+        const float hv = __shfl_sync(FULL, h, k);
+        if (k < PB && p < HR) {
+            float* dst = &hall[xs_index(0, nchh, r * HR + p)];
+            for (int rr = lane & 7; rr < FFN_CL; rr += 8) st_async(cluster_addr(dst, rr), hv, cluster_addr(&bar_h, rr));
+        }
     }
-    // the cluster's h slice, in every CTA of it (lane-blocked for the down rows' dot)
-    cluster.sync();
-    const int nchh = (HC + 511) / 512;
-    for (int i = t; i < HC / 4; i += FFN_THREADS) {
-        const int q = 4 * i;
-        const float* rp = cluster.map_shared_rank(hs, q / HR);
-        *reinterpret_cast<float4*>(&hall[xs_index(0, nchh, q)]) = *reinterpret_cast<const float4*>(rp + q % HR);
-    }
-    for (int q = HC + 4 * t; q < nchh * 512; q += 4 * FFN_THREADS)
-        *reinterpret_cast<float4*>(&hall[xs_index(0, nchh, q)]) = make_float4(0.f, 0.f, 0.f, 0.f);
-    // no remote reads of this CTA's h follow: arrive now, wait before leaving
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    __syncthreads();
+    cluster_arrive();  // (the final wait keeps every CTA until its peers are done with it)
+    // the cluster's h slice, pushed into every CTA (lane-blocked for the down rows' dot)
+    const bool got_h = __all_sync(FULL, mbar_wait_cluster(&bar_h, 0, a.err));
 
     // down: this CTA's rows of the slice, 8 lanes per row, 4 rows per warp
     const bool got_wd = __all_sync(FULL, mbar_wait(&bar_wd, 0, a.err));
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
 #pragma unroll
         for (int k = 0; k < 2; k++) {
             const int rr = base + k * FFN_NW * 4 + (lane >> 3);
-            acc[k] = (got_wd && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
+            acc[k] = (got_wd && got_h && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
         }
 #pragma unroll
         for (int m = 4; m >= 1; m >>= 1)
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
             if (l8 == 0 && rr < drows) op[rr] = acc[k];
         }
     }
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    cluster_wait();
 }
 
 int ffn_smem(int dim, int n_ff) {
