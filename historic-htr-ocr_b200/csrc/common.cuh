@@ -151,6 +151,11 @@ __device__ __forceinline__ void st_async(uint32_t raddr, float v, uint32_t rbar)
                  "r"(__float_as_uint(v)), "r"(rbar)
                  : "memory");
 }
+__device__ __forceinline__ void st_async(uint32_t raddr, float2 v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(raddr),
+                 "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(rbar)
+                 : "memory");
+}
 __device__ __forceinline__ void st_async(uint32_t raddr, float4 v, uint32_t rbar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
                  "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),

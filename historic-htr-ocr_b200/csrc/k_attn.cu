@@ -54,13 +54,18 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     __shared__ __align__(8) uint64_t obar;  // W_o slice chunks (fused o-projection)
     __shared__ __align__(8) uint64_t qbar;  // the W_qkv rows (fused qkv projection)
     __shared__ __align__(8) uint64_t gbar;  // the group's projected values, pushed by the cluster (fused qkv)
+    __shared__ __align__(8) uint64_t mbar, abar;  // fused ending by pushes: the slice's partials, the merged outputs
     __shared__ float red[NW];
     __shared__ __align__(16) float gq[G <= 4 ? (G + 2) * HD : 4];  // the group's [q heads | k | v] (fused qkv, G ≤ 4)
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float scw[NW][G][KPW];  // per warp: the round's scores, then probabilities
     __shared__ float wm[NW][G], wl[NW][G];
     __shared__ __align__(16) float wo[NW][G][HD];
-    __shared__ __align__(16) float part[G][PW];  // this CTA's (o[128], m, l, pad) per head, read by the cluster
+    // this CTA's (o[128], m, l, pad) per head, read by the cluster; in the fused ending by pushes (G ≤ 4) the same
+    // storage receives the ranks' values for this CTA's slice [CL][PER], then their (m, l) [CL][2]
+    constexpr int PART_F = G * PW > G * HD + 2 * CL ? G * PW : G * HD + 2 * CL;
+    __shared__ __align__(16) float partbuf[PART_F];
+    float(*part)[PW] = reinterpret_cast<float(*)[PW]>(partbuf);
     cg::cluster_group cluster = cg::this_cluster();
     const int b = blockIdx.z, j = blockIdx.y, sp = blockIdx.x, t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
@@ -94,6 +99,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     // KV ring (`smem` bytes of dynamic shared memory in all)
     const int NCOL = G * HD, ostride = q8_stride(NCOL);
     const int rpc = a.wo ? a.dim / CL : 0, row0 = sp * rpc;
+    const bool pushm = G <= 4 && rpc > 0;  // the fused ending's exchanges as pushes
     const int kv_bytes = (ring + 1) * HD * 2 + vreg;
     uint8_t* wsm = sm + kv_bytes;
     const int ro = rpc ? max(1, min(rpc, (smem - kv_bytes) / ostride)) : 1;
@@ -132,8 +138,14 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         mbar_init(&obar, 1);
         mbar_init(&qbar, 1);
         mbar_init(&gbar, 1);
+        mbar_init(&mbar, 1);
+        mbar_init(&abar, 1);
         mbar_fence_init();
         if (fq) mbar_expect_tx(&gbar, (uint32_t)(G + 2) * HD * 4);
+        if (pushm) {
+            mbar_expect_tx(&mbar, (uint32_t)(G * HD + 2 * CL) * 4);
+            mbar_expect_tx(&abar, (uint32_t)NCOL * 4);
+        }
         // constant weights and the cache's rows below pos: fetched before the wait (the V rows after the fused
         // projection, whose weights borrow their region)
         for (int tl = 0; tl < min(n_buf, n_tiles); tl++) issue(tl, true, !fq);
@@ -167,7 +179,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             w_hi[u] = *reinterpret_cast<const float2*>(wv + 64 + d0);
         }
     }
-    if (fq) cluster_arrive_relaxed();  // every barrier initialised before a peer pushes (waited below)
+    if (fq || pushm) cluster_arrive_relaxed();  // every barrier initialised before a peer pushes (waited below)
     const int dim = a.in.w.cols;
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (fq && a.in.nw && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
@@ -411,110 +423,189 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         *reinterpret_cast<float4*>(&wo[warp][g][lane * 4]) = make_float4(o01.x, o01.y, o23.x, o23.y);
     }
     const bool ok = __syncthreads_and(alive);  // a warp whose copy wait ran out voids the CTA's partial
-    for (int q = t; q < G * HD; q += AT_THREADS) {
-        const int g = q / HD, d = q % HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
-        float L = 0.0f, O = 0.0f;
-        if (M != -INFINITY && ok)
-#pragma unroll
-            for (int w = 0; w < NW; w++) {
-                const float e = expf(wm[w][g] - M);
-                L = fmaf(wl[w][g], e, L);
-                O = fmaf(wo[w][g][d], e, O);
-            }
-        part[g][d] = O;
-        if (d == 0) {
-            part[g][HD] = (ok && L > 0.0f) ? M : -INFINITY;
-            part[g][HD + 1] = ok ? L : 0.0f;
-        }
-    }
-    // ---- the cluster's merge through distributed shared memory ----
-    cluster.sync();
     constexpr int PER = G * HD / CL;  // the slice of the group's outputs this CTA merges
     const int q0 = sp * PER;
-    if (rpc == 0) {
-        // the attention output: this CTA's slice, from the CL partials
-        for (int i = t; i < PER; i += AT_THREADS) {
-            const int q = q0 + i, g = q / HD, d = q % HD;
-            float ms[CL], ls[CL], os[CL];
-#pragma unroll
-            for (int r = 0; r < CL; r++) {
-                const float* rp = cluster.map_shared_rank(&part[g][0], r);
-                os[r] = rp[d];
-                ms[r] = rp[HD];
-                ls[r] = rp[HD + 1];
-            }
+    float* att = &wo[0][0][0];  // the o-projection's input: the warps' partial outputs are folded by then
+    const int nch = (NCOL + 511) / 512;
+    bool got_in = true;
+    if (!pushm) {
+        for (int q = t; q < G * HD; q += AT_THREADS) {
+            const int g = q / HD, d = q % HD;
             float M = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < CL; r++) M = fmaxf(M, ms[r]);
+            for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
             float L = 0.0f, O = 0.0f;
+            if (M != -INFINITY && ok)
 #pragma unroll
-            for (int r = 0; r < CL; r++) {
-                const float e = ms[r] == -INFINITY ? 0.0f : expf(ms[r] - M);
-                L = fmaf(ls[r], e, L);
-                O = fmaf(os[r], e, O);
+                for (int w = 0; w < NW; w++) {
+                    const float e = expf(wm[w][g] - M);
+                    L = fmaf(wl[w][g], e, L);
+                    O = fmaf(wo[w][g][d], e, O);
+                }
+            part[g][d] = O;
+            if (d == 0) {
+                part[g][HD] = (ok && L > 0.0f) ? M : -INFINITY;
+                part[g][HD + 1] = ok ? L : 0.0f;
             }
-            a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
         }
-        cluster.sync();  // no CTA leaves while another still reads its partial
-        return;
-    }
-    // fused: reduce-scatter (this CTA merges its slice from the ranks' partials, copied in float4s), then all-gather
-    // (every CTA reads every slice) — the group's whole output in every CTA, the o-projection's input. Scratch in the
-    // idle KV ring: the ranks' slice values [CL][PER], their (m, l) for the slice's head [CL][2], the weights
-    // e^(m_r − M) [CL] and their sum L, this CTA's merged slice [PER] (16-B aligned for the all-gather's float4s).
-    const int gs = q0 / HD;  // the slice lies within one head
-    float* rsl = reinterpret_cast<float*>(sm);
-    float* rml = rsl + CL * PER;
-    float* ew = rml + CL * 2;
-    float* mine = ew + CL + 4;
-    constexpr int NSL = CL * (PER / 4);
-    for (int i = t; i < NSL + CL; i += AT_THREADS) {
-        if (i < NSL) {
-            const int r = i / (PER / 4), q = q0 + 4 * (i % (PER / 4));
-            const float* rp = cluster.map_shared_rank(&part[0][0], r);
-            reinterpret_cast<float4*>(rsl)[i] = *reinterpret_cast<const float4*>(rp + (q / HD) * PW + q % HD);
-        } else {
-            const float* rp = cluster.map_shared_rank(&part[0][0], i - NSL);
-            reinterpret_cast<float2*>(rml)[i - NSL] = *reinterpret_cast<const float2*>(rp + gs * PW + HD);
+        // ---- the cluster's merge through distributed shared memory ----
+        cluster.sync();
+        if (rpc == 0) {
+            // the attention output: this CTA's slice, from the CL partials
+            for (int i = t; i < PER; i += AT_THREADS) {
+                const int q = q0 + i, g = q / HD, d = q % HD;
+                float ms[CL], ls[CL], os[CL];
+#pragma unroll
+                for (int r = 0; r < CL; r++) {
+                    const float* rp = cluster.map_shared_rank(&part[g][0], r);
+                    os[r] = rp[d];
+                    ms[r] = rp[HD];
+                    ls[r] = rp[HD + 1];
+                }
+                float M = -INFINITY;
+#pragma unroll
+                for (int r = 0; r < CL; r++) M = fmaxf(M, ms[r]);
+                float L = 0.0f, O = 0.0f;
+#pragma unroll
+                for (int r = 0; r < CL; r++) {
+                    const float e = ms[r] == -INFINITY ? 0.0f : expf(ms[r] - M);
+                    L = fmaf(ls[r], e, L);
+                    O = fmaf(os[r], e, O);
+                }
+                a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
+            }
+            cluster.sync();  // no CTA leaves while another still reads its partial
+            return;
         }
-    }
-    __syncthreads();
-    // the slice's weights once (lane r of warp 0), L summed over the ranks in order, then one output per thread —
-    // the same operations in the same order as merging each output on its own
-    if (warp == 0) {
-        float M = -INFINITY;
+        // fused: reduce-scatter (this CTA merges its slice from the ranks' partials, copied in float4s), then all-gather
+        // (every CTA reads every slice) — the group's whole output in every CTA, the o-projection's input. Scratch in the
+        // idle KV ring: the ranks' slice values [CL][PER], their (m, l) for the slice's head [CL][2], the weights
+        // e^(m_r − M) [CL] and their sum L, this CTA's merged slice [PER] (16-B aligned for the all-gather's float4s).
+        const int gs = q0 / HD;  // the slice lies within one head
+        float* rsl = reinterpret_cast<float*>(sm);
+        float* rml = rsl + CL * PER;
+        float* ew = rml + CL * 2;
+        float* mine = ew + CL + 4;
+        constexpr int NSL = CL * (PER / 4);
+        for (int i = t; i < NSL + CL; i += AT_THREADS) {
+            if (i < NSL) {
+                const int r = i / (PER / 4), q = q0 + 4 * (i % (PER / 4));
+                const float* rp = cluster.map_shared_rank(&part[0][0], r);
+                reinterpret_cast<float4*>(rsl)[i] = *reinterpret_cast<const float4*>(rp + (q / HD) * PW + q % HD);
+            } else {
+                const float* rp = cluster.map_shared_rank(&part[0][0], i - NSL);
+                reinterpret_cast<float2*>(rml)[i - NSL] = *reinterpret_cast<const float2*>(rp + gs * PW + HD);
+            }
+        }
+        __syncthreads();
+        // the slice's weights once (lane r of warp 0), L summed over the ranks in order, then one output per thread —
+        // the same operations in the same order as merging each output on its own
+        if (warp == 0) {
+            float M = -INFINITY;
 #pragma unroll
-        for (int r = 0; r < CL; r++) M = fmaxf(M, rml[2 * r]);
-        const float m = lane < CL ? rml[2 * lane] : -INFINITY;
-        const float e = m == -INFINITY ? 0.0f : expf(m - M);
-        float L = 0.0f;
+            for (int r = 0; r < CL; r++) M = fmaxf(M, rml[2 * r]);
+            const float m = lane < CL ? rml[2 * lane] : -INFINITY;
+            const float e = m == -INFINITY ? 0.0f : expf(m - M);
+            float L = 0.0f;
 #pragma unroll
-        for (int r = 0; r < CL; r++) L = fmaf(rml[2 * r + 1], __shfl_sync(FULL, e, r), L);
-        if (lane < CL) ew[lane] = e;
-        if (lane == 0) ew[CL] = L;
-    }
-    if (PER <= 32) __syncwarp();  // the outputs are warp 0's own
-    else __syncthreads();
-    for (int i = t; i < PER; i += AT_THREADS) {
-        float O = 0.0f;
+            for (int r = 0; r < CL; r++) L = fmaf(rml[2 * r + 1], __shfl_sync(FULL, e, r), L);
+            if (lane < CL) ew[lane] = e;
+            if (lane == 0) ew[CL] = L;
+        }
+        if (PER <= 32) __syncwarp();  // the outputs are warp 0's own
+        else __syncthreads();
+        for (int i = t; i < PER; i += AT_THREADS) {
+            float O = 0.0f;
 #pragma unroll
-        for (int r = 0; r < CL; r++) O = fmaf(rsl[r * PER + i], ew[r], O);
-        mine[i] = O / ew[CL];
+            for (int r = 0; r < CL; r++) O = fmaf(rsl[r * PER + i], ew[r], O);
+            mine[i] = O / ew[CL];
+        }
+        cluster.sync();  // every slice merged; no rank reads `part` any more
+        for (int i = t; i < NCOL / 4; i += AT_THREADS) {
+            const int q = 4 * i;
+            const float* rp = cluster.map_shared_rank(mine, q / PER);
+            *reinterpret_cast<float4*>(&att[xs_index(0, nch, q)]) = *reinterpret_cast<const float4*>(rp + q % PER);
+        }
+        // no remote reads of this CTA's shared memory follow: arrive now, wait before leaving
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        __syncthreads();
+    } else {
+        // fused ending by pushes: every output's CTA-merged value goes to the owner of its slice, every head's (m, l)
+        // to the owners of that head's slices (into their partbuf); values first, then one barrier — wo is read
+        // until then, and it receives the merged outputs after — then the pushes
+        constexpr int QPT = (G * HD + AT_THREADS - 1) / AT_THREADS;
+        float ov[QPT], mv[QPT], lv[QPT];
+#pragma unroll
+        for (int u = 0; u < QPT; u++) {
+            const int q = t + u * AT_THREADS;
+            ov[u] = 0.0f;
+            mv[u] = -INFINITY;
+            lv[u] = 0.0f;
+            if (q < G * HD) {
+                const int g = q / HD, d = q % HD;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][g]);
+                float L = 0.0f, O = 0.0f;
+                if (M != -INFINITY && ok)
+#pragma unroll
+                    for (int w = 0; w < NW; w++) {
+                        const float e = expf(wm[w][g] - M);
+                        L = fmaf(wl[w][g], e, L);
+                        O = fmaf(wo[w][g][d], e, O);
+                    }
+                ov[u] = O;
+                mv[u] = (ok && L > 0.0f) ? M : -INFINITY;
+                lv[u] = ok ? L : 0.0f;
+            }
+        }
+        __syncthreads();
+        if (!fq) cluster_wait();  // (the prologue's arrive: the peers' barriers are ready)
+        float* mrs = partbuf;            // [CL][PER]
+        float* mrml = partbuf + G * HD;  // [CL][2]
+#pragma unroll
+        for (int u = 0; u < QPT; u++) {
+            const int q = t + u * AT_THREADS;
+            if (q < G * HD) {
+                const int s = q / PER, d = q % HD;
+                st_async(cluster_addr(&mrs[sp * PER + q % PER], s), ov[u], cluster_addr(&mbar, s));
+                if (d < HD / PER) {
+                    const int s2 = (q / HD) * (HD / PER) + d;
+                    st_async(cluster_addr(&mrml[2 * sp], s2), make_float2(mv[u], lv[u]), cluster_addr(&mbar, s2));
+                }
+            }
+        }
+        // the merged outputs' pad columns past NCOL are this CTA's zeros
+        for (int q = NCOL + 4 * t; q < nch * 512; q += 4 * AT_THREADS)
+            *reinterpret_cast<float4*>(&att[xs_index(0, nch, q)]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        const bool got_m = __all_sync(FULL, mbar_wait_cluster(&mbar, 0, a.err));
+        // this CTA's slice: the ranks' weights once (lane r of warp 0), L summed over the ranks in order, then each
+        // (output, rank) pair merged by one thread — the same operations in the same order as merging each output
+        // on its own — and pushed into that rank's o-projection input
+        float* ew = &scw[0][0][0];  // [CL] weights, then L (the scores' scratch is idle)
+        if (warp == 0) {
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < CL; r++) M = fmaxf(M, mrml[2 * r]);
+            const float m = lane < CL ? mrml[2 * lane] : -INFINITY;
+            const float e = m == -INFINITY ? 0.0f : expf(m - M);
+            float L = 0.0f;
+#pragma unroll
+            for (int r = 0; r < CL; r++) L = fmaf(mrml[2 * r + 1], __shfl_sync(FULL, e, r), L);
+            if (lane < CL) ew[lane] = e;
+            if (lane == 0) ew[CL] = L;
+        }
+        __syncthreads();
+        for (int idx = t; idx < PER * CL; idx += AT_THREADS) {
+            const int i = idx % PER, s = idx / PER;
+            float O = 0.0f;
+#pragma unroll
+            for (int r = 0; r < CL; r++) O = fmaf(mrs[r * PER + i], ew[r], O);
+            st_async(cluster_addr(&att[xs_index(0, nch, q0 + i)], s), O / ew[CL], cluster_addr(&abar, s));
+        }
+        cluster_arrive();  // (the final wait keeps every CTA until its peers are done with it)
+        got_in = got_m && __all_sync(FULL, mbar_wait_cluster(&abar, 0, a.err));
     }
-    cluster.sync();  // every slice merged; no rank reads `part` any more
-    float* att = &wo[0][0][0];  // the warps' partial outputs are folded into part: reuse
-    const int nch = (NCOL + 511) / 512;
-    for (int i = t; i < NCOL / 4; i += AT_THREADS) {
-        const int q = 4 * i;
-        const float* rp = cluster.map_shared_rank(mine, q / PER);
-        *reinterpret_cast<float4*>(&att[xs_index(0, nch, q)]) = *reinterpret_cast<const float4*>(rp + q % PER);
-    }
-    // no remote reads of this CTA's shared memory follow: arrive now, wait before leaving
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    __syncthreads();
     // 8 lanes per row (16-column pieces lane&7, +8, …: a row's 128 B per quarter-warp), 4 rows per warp
     const uint64_t* ap = reinterpret_cast<const uint64_t*>(att);
     float* op = a.opart + ((long)b * a.n_kv + j) * a.dim + row0;
@@ -522,7 +613,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     for (int c0 = 0, k = 0; c0 < rpc; c0 += ro, k++) {
         const int nr = min(ro, rpc - c0);
         const bool got = __all_sync(FULL, mbar_wait(&obar, k & 1, a.err));
-        if (got) {
+        if (got && got_in) {
             // two row groups per warp at once: both dots, then both reductions
             for (int base = warp * 4; base < nr; base += NW * 8) {
                 float acc[2];
