@@ -40,14 +40,18 @@ __host__ __device__ inline FfnSmem ffn_layout(int dim, int n_ff) {
     return m;
 }
 
+// DIM_T / NFF_T: the model's dim and n_ff fixed at compile time (0: read from the arguments) — with the shape known
+// the loops over chunks, row pairs and W_down pieces are straight-line code
+template <int DIM_T, int NFF_T>
 __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ __align__(8) uint64_t bar_gu, bar_wd, bar_h;
     __shared__ float red[FFN_NW];
     const int r = blockIdx.x, c = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int dim = a.in.w.cols, HC = a.n_ff / FFN_NCLU, HR = HC / FFN_CL, drows = dim / FFN_CL;
+    const int dim = DIM_T ? DIM_T : a.in.w.cols, n_ff = NFF_T ? NFF_T : a.n_ff;
+    const int HC = n_ff / FFN_NCLU, HR = HC / FFN_CL, drows = dim / FFN_CL;
     const int gstride = q8_stride(dim), dstride = q8_stride(HC);
-    const FfnSmem L = ffn_layout(dim, a.n_ff);
+    const FfnSmem L = ffn_layout(dim, n_ff);
     uint8_t* gsm = sm + L.gu;
     uint8_t* dsm = sm + L.wd;
     float* xs = reinterpret_cast<float*>(sm + L.xs);
@@ -77,7 +81,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     pdl_wait();
 
     const int nch = (dim + 511) / 512;
-    stage_x(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
+    stage_x<DIM_T>(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
     __syncthreads();
 
     // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
@@ -86,7 +90,10 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xs);
     // up to PB pairs per warp at once (each chunk's x loaded once for all of them): every dot first, then the
     // reductions interleaved
-    constexpr int PB = 4;
+    // (a compiled shape whose HR is a multiple of the warps: exactly PB pairs per warp, no bounds to test)
+    constexpr int HR_T = NFF_T / FFN_NCLU / FFN_CL;
+    constexpr bool EXACT = NFF_T != 0 && HR_T % FFN_NW == 0 && HR_T / FFN_NW <= 4;
+    constexpr int PB = EXACT ? HR_T / FFN_NW : 4;
     for (int p0 = warp; p0 < HR; p0 += FFN_NW * PB) {
         float g[PB], u[PB];
 #pragma unroll
@@ -105,7 +112,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
 #pragma unroll
                 for (int k = 0; k < PB; k++) {
                     const int p = p0 + k * FFN_NW;
-                    if (p < HR) {
+                    if (EXACT || p < HR) {
                         const uint8_t* rg = gsm + (size_t)(2 * p) * gstride;
                         const uint8_t* ru = rg + gstride;
                         const float dg = __half2float(reinterpret_cast<const __half*>(rg + dim)[col >> 5]);
@@ -191,25 +198,34 @@ static void ffn_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaS
     cfg.numAttrs = 1;
 }
 
+// the instance for a shape: Qwen3-0.6B's (1024, 3072) compiled for it, any other shape generic
+using FfnKernel = void (*)(FfnArgs);
+static FfnKernel ffn_kernel(int dim, int n_ff) {
+    static bool configured = false;
+    if (!configured) {
+        for (FfnKernel k : {k_ffn<1024, 3072>, k_ffn<0, 0>}) {
+            cudaFuncAttributes fa;
+            cudaFuncGetAttributes(&fa, k);
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
+            cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        }
+        configured = true;
+    }
+    return dim == 1024 && n_ff == 3072 ? k_ffn<1024, 3072> : k_ffn<0, 0>;
+}
+
 bool ffn_usable(int dim, int n_ff) {
     const int smem = ffn_smem(dim, n_ff);
     if (!smem) return false;
     static int keys[8], vals[8], n_keys = 0;
     for (int i = 0; i < n_keys; i++)
         if (keys[i] == smem) return vals[i] != 0;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncAttributes fa;
-        cudaFuncGetAttributes(&fa, k_ffn);
-        cudaFuncSetAttribute(k_ffn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
-        cudaFuncSetAttribute(k_ffn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        configured = true;
-    }
+    const FfnKernel kern = ffn_kernel(dim, n_ff);
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
     ffn_config(cfg, attr, nullptr, smem);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, k_ffn, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
     }
@@ -225,7 +241,7 @@ void launch_ffn(cudaStream_t st, const FfnArgs& a, bool pdl) {
     cudaLaunchAttribute attr[2];
     ffn_config(cfg, attr, st, ffn_smem(a.in.w.cols, a.n_ff));
     cfg.numAttrs = pdl ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, k_ffn, a);
+    cudaLaunchKernelEx(&cfg, ffn_kernel(a.in.w.cols, a.n_ff), a);
 }
 
 }  // namespace ocr

@@ -25,10 +25,12 @@ __device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
 // threads: every normed input here, its norm weights `wn0` loaded by the caller before its dependency wait): the
 // row's loads all in flight at once, the values held in registers across the norm's reduction. Wider rows in
 // passes of XU float4s per thread, every load of a pass issued before any is used.
+// KT: the row length fixed at compile time (0: a.w.cols).
 constexpr int XU = 8;
+template <int KT = 0>
 __device__ __forceinline__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr,
                                     float4 wn0, bool writer) {
-    const int K = a.w.cols, K4 = K >> 2;
+    const int K = KT ? KT : a.w.cols, K4 = K >> 2;
     const bool write_x = a.x_out != nullptr && writer;
     float4* xs4 = reinterpret_cast<float4*>(xsf);
     const int tid = threadIdx.x;
