@@ -47,7 +47,9 @@ constexpr int MAX_BUF = 2;           // ring depth: at most 80 KB, so two CTAs s
 constexpr int KPW = (MAX_BUF * TILE + NW - 1) / NW;  // keys per warp per round (one per lane)
 constexpr int PW = HD + 4;  // a head's partial: o[128], m, l, two floats of pad (whole float4s)
 
-template <int G, int CL>
+// DIM_T: the model's dim fixed at compile time (0: read from the arguments) — the staging, the projection's chunk
+// loop and the o-projection's rows become straight-line code
+template <int G, int CL, int DIM_T = 0>
 __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf, int smem) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ __align__(8) uint64_t fk[MAX_BUF], fv[MAX_BUF];  // a ring slot's K rows, its V rows
@@ -91,14 +93,16 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     const int ring = n_buf * TILE;
     const bool fq = G <= 4 && a.wqkv.w != nullptr;
     const int RQ = (G + 2) * HD / CL;  // the fused qkv projection: this CTA's rows of the group's [q | k | v] rows
-    const int vreg = max((ring + 1) * HD * 2, fq ? RQ * a.wqkv.stride : 0);
+    const int qstride = DIM_T ? q8_stride(DIM_T) : a.wqkv.stride;  // W_qkv's row stride
+    const int mdim = DIM_T ? DIM_T : a.dim;                          // the o-projection's rows (the model dim)
+    const int vreg = max((ring + 1) * HD * 2, fq ? RQ * qstride : 0);
     __half* Ks = reinterpret_cast<__half*>(sm);
     __half* Vs = Ks + (size_t)(ring + 1) * HD;
 
     // the fused o-projection's W_o rows [row0, row0 + rpc) of slice j, in chunks of `ro` rows in the region after the
     // KV ring (`smem` bytes of dynamic shared memory in all)
     const int NCOL = G * HD, ostride = q8_stride(NCOL);
-    const int rpc = a.wo ? a.dim / CL : 0, row0 = sp * rpc;
+    const int rpc = a.wo ? mdim / CL : 0, row0 = sp * rpc;
     const bool pushm = G <= 4 && rpc > 0;  // the fused ending's exchanges as pushes
     const int kv_bytes = (ring + 1) * HD * 2 + vreg;
     uint8_t* wsm = sm + kv_bytes;
@@ -106,7 +110,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     auto issue_o = [&](int c0) {
         const uint32_t bytes = (uint32_t)(min(ro, rpc - c0) * ostride);
         mbar_expect_tx(&obar, bytes);
-        bulk_g2s(wsm, a.wo + ((size_t)j * a.dim + row0 + c0) * ostride, bytes, &obar);
+        bulk_g2s(wsm, a.wo + ((size_t)j * mdim + row0 + c0) * ostride, bytes, &obar);
     };
     // rows [ts, min(te, pos)) of tile tl (the row at pos is not in the cache yet): its K rows and/or its V rows
     auto issue = [&](int tl, bool k, bool v) {
@@ -154,9 +158,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             const int grow = ci0 < G * HD ? j * G * HD + ci0
                              : ci0 < (G + 1) * HD ? a.n_head * HD + j * HD + (ci0 - G * HD)
                                                   : (a.n_head + a.n_kv) * HD + j * HD + (ci0 - (G + 1) * HD);
-            const uint32_t bytes = (uint32_t)(RQ * a.wqkv.stride);
+            const uint32_t bytes = (uint32_t)(RQ * qstride);
             mbar_expect_tx(&qbar, bytes);
-            bulk_g2s_stream(Vs, a.wqkv.w + (size_t)grow * a.wqkv.stride, bytes, &qbar, l2_evict_first());
+            bulk_g2s_stream(Vs, a.wqkv.w + (size_t)grow * qstride, bytes, &qbar, l2_evict_first());
         }
         if (rpc > 0) issue_o(0);
         pdl_trigger();
@@ -180,7 +184,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         }
     }
     if (fq || pushm) cluster_arrive_relaxed();  // every barrier initialised before a peer pushes (waited below)
-    const int dim = a.in.w.cols;
+    const int dim = DIM_T ? DIM_T : a.in.w.cols;
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (fq && a.in.nw && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     bool got_g = true;
     if (fq) {
         const int nch = (dim + 511) / 512;
-        stage_x(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
+        stage_x<DIM_T>(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
         __syncthreads();
         constexpr int RPW = 8;  // at most 64 rows per CTA
         const int rpw = RQ / NW;
@@ -216,7 +220,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
                 for (int k = 0; k < RPW; k++)
                     if (k < rpw) {
-                        const uint8_t* row = wq + (size_t)(warp * rpw + k) * a.wqkv.stride;
+                        const uint8_t* row = wq + (size_t)(warp * rpw + k) * qstride;
                         const float d = __half2float(reinterpret_cast<const __half*>(row + dim)[col >> 5]);
                         acc[k] = fmaf(dot16x2(*reinterpret_cast<const uint4*>(row + col), xp), d, acc[k]);
                     }
@@ -608,7 +612,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     }
     // 8 lanes per row (16-column pieces lane&7, +8, …: a row's 128 B per quarter-warp), 4 rows per warp
     const uint64_t* ap = reinterpret_cast<const uint64_t*>(att);
-    float* op = a.opart + ((long)b * a.n_kv + j) * a.dim + row0;
+    float* op = a.opart + ((long)b * a.n_kv + j) * mdim + row0;
     const int l8 = lane & 7;
     for (int c0 = 0, k = 0; c0 < rpc; c0 += ro, k++) {
         const int nr = min(ro, rpc - c0);
@@ -708,6 +712,11 @@ static bool usable_t(cudaStream_t st, const AttnArgs& a) {
         // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
         if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if constexpr (G == 2 && CL == 16) {
+            auto k1024 = k_attn_decode<G, CL, 1024>;  // (the same static shared memory)
+            cudaFuncSetAttribute(k1024, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+            cudaFuncSetAttribute(k1024, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        }
         configured = true;
     }
     if (CL <= 8) return true;
@@ -737,7 +746,11 @@ static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
     int n_buf = 1;
     cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
     cfg.numAttrs = pdl ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, k_attn_decode<G, CL>, a, n_buf, (int)cfg.dynamicSmemBytes);
+    auto kern = k_attn_decode<G, CL>;
+    // Qwen3-0.6B's decode step (fused projections, dim 1024): the instance compiled for that dim
+    if constexpr (G == 2 && CL == 16)
+        if (a.wqkv.w && a.in.w.cols == 1024 && a.wo && a.dim == 1024) kern = k_attn_decode<G, CL, 1024>;
+    cudaLaunchKernelEx(&cfg, kern, a, n_buf, (int)cfg.dynamicSmemBytes);
 }
 
 template <int G>
