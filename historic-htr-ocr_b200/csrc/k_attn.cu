@@ -106,7 +106,9 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     const bool pushm = G <= 4 && rpc > 0;  // the fused ending's exchanges as pushes
     const int kv_bytes = (ring + 1) * HD * 2 + vreg;
     uint8_t* wsm = sm + kv_bytes;
-    const int ro = rpc ? max(1, min(rpc, (smem - kv_bytes) / ostride)) : 1;
+    // (a compiled dim whose rows make exactly 8 per warp: one chunk, every row in range — its W_o region holds them)
+    constexpr bool OEX = DIM_T != 0 && DIM_T / CL == NW * 8;
+    const int ro = OEX ? rpc : rpc ? max(1, min(rpc, (smem - kv_bytes) / ostride)) : 1;
     auto issue_o = [&](int c0) {
         const uint32_t bytes = (uint32_t)(min(ro, rpc - c0) * ostride);
         mbar_expect_tx(&obar, bytes);
@@ -624,7 +626,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
                 for (int k = 0; k < 2; k++) {
                     const int rr = base + k * NW * 4 + (lane >> 3);
-                    acc[k] = rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
+                    acc[k] = OEX || rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
                 }
 #pragma unroll
                 for (int m = 4; m >= 1; m >>= 1)
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
                 for (int k = 0; k < 2; k++) {
                     const int rr = base + k * NW * 4 + (lane >> 3);
-                    if (l8 == 0 && rr < nr) op[c0 + rr] = acc[k];
+                    if (l8 == 0 && (OEX || rr < nr)) op[c0 + rr] = acc[k];
                 }
             }
         }

@@ -156,12 +156,14 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     float* op = a.dpart + (size_t)c * dim + r * drows;
     const int l8 = lane & 7;
     // two row groups per warp at once (rows base + lane/8 and base + 32 + lane/8)
+    // (a compiled shape with exactly 8 W_down rows per warp: every row in range)
+    constexpr bool DEX = NFF_T != 0 && DIM_T / FFN_CL == FFN_NW * 8;
     for (int base = warp * 4; base < drows; base += FFN_NW * 8) {
         float acc[2];
 #pragma unroll
         for (int k = 0; k < 2; k++) {
             const int rr = base + k * FFN_NW * 4 + (lane >> 3);
-            acc[k] = (got_wd && got_h && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
+            acc[k] = (got_wd && got_h && (DEX || rr < drows)) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
         }
 #pragma unroll
         for (int m = 4; m >= 1; m >>= 1)
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
 #pragma unroll
         for (int k = 0; k < 2; k++) {
             const int rr = base + k * FFN_NW * 4 + (lane >> 3);
-            if (l8 == 0 && rr < drows) op[rr] = acc[k];
+            if (l8 == 0 && (DEX || rr < drows)) op[rr] = acc[k];
         }
     }
     cluster_wait();
