@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         const bool got = __all_sync(FULL, mbar_wait(&obar, k & 1, a.err));
         if (got && got_in) {
             // two row groups per warp at once: both dots, then both reductions
-            for (int base = warp * 4; base < nr; base += NW * 8) {
+            for (int base = warp * 4; base < (OEX ? warp * 4 + 1 : nr); base += NW * 8) {  // (OEX: one pass)
                 float acc[2];
 #pragma unroll
                 for (int k = 0; k < 2; k++) {

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     constexpr int HR_T = NFF_T / FFN_NCLU / FFN_CL;
     constexpr bool EXACT = NFF_T != 0 && HR_T % FFN_NW == 0 && HR_T / FFN_NW <= 4;
     constexpr int PB = EXACT ? HR_T / FFN_NW : 4;
-    for (int p0 = warp; p0 < HR; p0 += FFN_NW * PB) {
+    for (int p0 = warp; p0 < (EXACT ? warp + 1 : HR); p0 += FFN_NW * PB) {  // (EXACT: one pass)
         float g[PB], u[PB];
 #pragma unroll
         for (int k = 0; k < PB; k++) g[k] = u[k] = 0.0f;
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     // two row groups per warp at once (rows base + lane/8 and base + 32 + lane/8)
     // (a compiled shape with exactly 8 W_down rows per warp: every row in range)
     constexpr bool DEX = NFF_T != 0 && DIM_T / FFN_CL == FFN_NW * 8;
-    for (int base = warp * 4; base < drows; base += FFN_NW * 8) {
+    for (int base = warp * 4; base < (DEX ? warp * 4 + 1 : drows); base += FFN_NW * 8) {  // (DEX: one pass)
         float acc[2];
 #pragma unroll
         for (int k = 0; k < 2; k++) {

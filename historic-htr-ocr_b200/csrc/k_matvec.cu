@@ -152,9 +152,10 @@ __device__ void choice_finish(const float* bv_sm, const uint32_t* bi_sm, int nb,
 constexpr int MAX_NS = 16;
 constexpr int SM_HEAD = 256;  // mbarriers full[MAX_NS], empty[MAX_NS]
 
-template <int NB, int W, int R>
 // two CTAs per SM for the small matrices of one or two slots (the grid is sized for it; at most 112 registers);
-// wider slot batches keep their accumulators in registers at one CTA per SM
+// wider slot batches keep their accumulators in registers at one CTA per SM. KT: the row length fixed at compile
+// time (0: a.w.cols) — the LM head of a 1024-wide model runs its chunk loop and bounds as straight-line code.
+template <int NB, int W, int R, int KT = 0>
 __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_mv(MvArgs a, int rpc, int ns) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
     __shared__ float bv_sm[NB];
     __shared__ uint32_t bi_sm[NB];
 
-    const int K = a.w.cols, N = a.w.rows, stride = a.w.stride;
+    const int K = KT ? KT : a.w.cols, N = a.w.rows, stride = KT ? q8_stride(KT) : a.w.stride;
     const int nch = (K + 511) >> 9;
     float* xsf = reinterpret_cast<float*>(sm + SM_HEAD);
     uint8_t* ring = sm + SM_HEAD + (size_t)NB * nch * 512 * sizeof(float);
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                                                                           : 0.0f;
                     }
         }
-        stage_x(xsf, nch, nb, slot0, a, red, NC, wn0, blockIdx.x == 0);
+        stage_x<KT>(xsf, nch, nb, slot0, a, red, NC, wn0, blockIdx.x == 0);
         bar_sync(1, NC);
         const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
         for (int t = 0; t < n_stage; t++) {
@@ -440,11 +441,11 @@ int lm_head_grid(int num_sms, int n_vocab, int dim) {
     return geometry(a, 1, num_sms).grid;
 }
 
-template <int NB, int W, int R>
+template <int NB, int W, int R, int KT = 0>
 static void configure_t() {
     static bool configured = false;
     if (!configured) {
-        auto kern = k_mv<NB, W, R>;
+        auto kern = k_mv<NB, W, R, KT>;
         cudaFuncAttributes fa;
         cudaFuncGetAttributes(&fa, kern);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
@@ -469,10 +470,10 @@ static int per_sm_t() {
     return n;
 }
 
-template <int NB, int W, int R>
+template <int NB, int W, int R, int KT = 0>
 static void launch_t(cudaStream_t st, const MvArgs& a, const Geo& g, bool pdl) {
-    auto kern = k_mv<NB, W, R>;
-    configure_t<NB, W, R>();
+    auto kern = k_mv<NB, W, R, KT>;
+    configure_t<NB, W, R, KT>();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)g.grid, (unsigned)((a.nb + NB - 1) / NB), 1);
     cfg.blockDim = dim3((W + 1) * 32, 1, 1);
@@ -490,7 +491,14 @@ template <int NB>
 static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
     Geo g = geometry(a, NB, num_sms);
     if (g.W == 16) {
-        launch_t<NB, 16, NB == 1 ? 4 : 2>(st, a, g, pdl);
+        bool done = false;
+        if constexpr (NB == 1) {
+            if (a.w.cols == 1024) {
+                launch_t<NB, 16, 4, 1024>(st, a, g, pdl);
+                done = true;
+            }
+        }
+        if (!done) launch_t<NB, 16, NB == 1 ? 4 : 2>(st, a, g, pdl);
     } else if (g.R == 2) {
         if (per_sm_t<NB, 8, 2>() < 2) g = geometry(a, NB, num_sms, 1);
         launch_t<NB, 8, 2>(st, a, g, pdl);
