@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     bool got_g = true;
     if (fq) {
         const int nch = (dim + 511) / 512;
-        stage_x<DIM_T>(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
+        // (the partials it adds, when any, are the fused FFN's FFN_NCLU)
+        stage_x<DIM_T, DIM_T ? FFN_NCLU : 0>(qkvs, nch, 1, b, a.in, red, AT_THREADS, wn0, sp == 0 && j == 0);
         __syncthreads();
         constexpr int RPW = 8;  // at most 64 rows per CTA
         const int rpw = RQ / NW;
@@ -335,8 +336,10 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
             uint64_t d[G], e[G];
 #pragma unroll
             for (int g = 0; g < G; g++) d[g] = e[g] = 0;
-            if (kk < nw) {
-                const int i = w0 + kk;
+            {
+                // every pass computes (no branch in the unrolled passes): a key past the warp's share reads a row
+                // of the ring (its score is never stored)
+                const int i = w0 + min(kk, max(nw - 1, 0));
                 const __half* kr = Ks + (size_t)(i == prel ? ring : i) * HD;
                 const uint4 u0 = *reinterpret_cast<const uint4*>(kr + prt * 8);
                 const uint4 u1 = *reinterpret_cast<const uint4*>(kr + 64 + prt * 8);

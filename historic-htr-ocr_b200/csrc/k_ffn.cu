@@ -42,7 +42,7 @@ __host__ __device__ inline FfnSmem ffn_layout(int dim, int n_ff) {
 
 // DIM_T / NFF_T: the model's dim and n_ff fixed at compile time (0: read from the arguments) — with the shape known
 // the loops over chunks, row pairs and W_down pieces are straight-line code
-template <int DIM_T, int NFF_T>
+template <int DIM_T, int NFF_T, int NKV_T>
 __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ __align__(8) uint64_t bar_gu, bar_wd, bar_h;
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     pdl_wait();
 
     const int nch = (dim + 511) / 512;
-    stage_x<DIM_T>(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
+    stage_x<DIM_T, NKV_T>(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
     __syncthreads();
 
     // gate|up: one warp per row pair, 16 columns per lane per 512-column chunk
@@ -200,12 +200,13 @@ static void ffn_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaS
     cfg.numAttrs = 1;
 }
 
-// the instance for a shape: Qwen3-0.6B's (1024, 3072) compiled for it, any other shape generic
+// the instance for a shape: Qwen3-0.6B's (dim 1024, n_ff 3072, 8 kv heads' o-partials) compiled for it, any other
+// shape generic
 using FfnKernel = void (*)(FfnArgs);
-static FfnKernel ffn_kernel(int dim, int n_ff) {
+static FfnKernel ffn_kernel(int dim, int n_ff, int n_add) {
     static bool configured = false;
     if (!configured) {
-        for (FfnKernel k : {k_ffn<1024, 3072>, k_ffn<0, 0>}) {
+        for (FfnKernel k : {k_ffn<1024, 3072, 8>, k_ffn<0, 0, 0>}) {
             cudaFuncAttributes fa;
             cudaFuncGetAttributes(&fa, k);
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
@@ -213,7 +214,7 @@ static FfnKernel ffn_kernel(int dim, int n_ff) {
         }
         configured = true;
     }
-    return dim == 1024 && n_ff == 3072 ? k_ffn<1024, 3072> : k_ffn<0, 0>;
+    return dim == 1024 && n_ff == 3072 && n_add == 8 ? k_ffn<1024, 3072, 8> : k_ffn<0, 0, 0>;
 }
 
 bool ffn_usable(int dim, int n_ff) {
@@ -222,7 +223,7 @@ bool ffn_usable(int dim, int n_ff) {
     static int keys[8], vals[8], n_keys = 0;
     for (int i = 0; i < n_keys; i++)
         if (keys[i] == smem) return vals[i] != 0;
-    const FfnKernel kern = ffn_kernel(dim, n_ff);
+    const FfnKernel kern = ffn_kernel(dim, n_ff, 8);  // (either instance: the same resources)
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
     ffn_config(cfg, attr, nullptr, smem);
@@ -243,7 +244,7 @@ void launch_ffn(cudaStream_t st, const FfnArgs& a, bool pdl) {
     cudaLaunchAttribute attr[2];
     ffn_config(cfg, attr, st, ffn_smem(a.in.w.cols, a.n_ff));
     cfg.numAttrs = pdl ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, ffn_kernel(a.in.w.cols, a.n_ff), a);
+    cudaLaunchKernelEx(&cfg, ffn_kernel(a.in.w.cols, a.n_ff, a.in.n_add), a);
 }
 
 }  // namespace ocr

@@ -25,12 +25,13 @@ __device__ __forceinline__ float consumer_sum(float v, float* red, int nthr) {
 // threads: every normed input here, its norm weights `wn0` loaded by the caller before its dependency wait): the
 // row's loads all in flight at once, the values held in registers across the norm's reduction. Wider rows in
 // passes of XU float4s per thread, every load of a pass issued before any is used.
-// KT: the row length fixed at compile time (0: a.w.cols).
+// KT: the row length fixed at compile time (0: a.w.cols); NADD_T: the count of partial products (0: a.n_add).
 constexpr int XU = 8;
-template <int KT = 0>
+template <int KT = 0, int NADD_T = 0>
 __device__ __forceinline__ void stage_x(float* xsf, int nch, int nb, int slot0, const MvArgs& a, float* red, int nthr,
                                     float4 wn0, bool writer) {
     const int K = KT ? KT : a.w.cols, K4 = K >> 2;
+    const int n_add = NADD_T ? NADD_T : a.n_add;
     const bool write_x = a.x_out != nullptr && writer;
     float4* xs4 = reinterpret_cast<float4*>(xsf);
     const int tid = threadIdx.x;
@@ -58,16 +59,16 @@ __device__ __forceinline__ void stage_x(float* xsf, int nch, int nb, int slot0, 
             if (tid < K4) {
                 if (a.xadd) {
                     // x + (p_0 + … + p_{n-1}): every load in flight, the partials summed in order
-                    const float4* pa = reinterpret_cast<const float4*>(a.xadd) + (long)b * a.n_add * K4 + tid;
+                    const float4* pa = reinterpret_cast<const float4*>(a.xadd) + (long)b * n_add * K4 + tid;
                     float4 pv[MAX_ADD];
                     v = load(tid);
 #pragma unroll
                     for (int k = 0; k < MAX_ADD; k++)
-                        if (k < a.n_add) pv[k] = pa[(long)k * K4];
+                        if (k < n_add) pv[k] = pa[(long)k * K4];
                     float4 o = pv[0];
 #pragma unroll
                     for (int k = 1; k < MAX_ADD; k++)
-                        if (k < a.n_add) o = make_float4(o.x + pv[k].x, o.y + pv[k].y, o.z + pv[k].z, o.w + pv[k].w);
+                        if (k < n_add) o = make_float4(o.x + pv[k].x, o.y + pv[k].y, o.z + pv[k].z, o.w + pv[k].w);
                     v = make_float4(v.x + o.x, v.y + o.y, v.z + o.z, v.w + o.w);
                 } else {
                     v = load(tid);
