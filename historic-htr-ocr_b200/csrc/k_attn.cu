@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
                 const float mn = fmaxf(mw[g], warp_max(sc));
                 const float corr = expf(mw[g] - mn);  // exp(-inf) = 0 on the first round
                 const float p = lane < nw ? expf(sc - mn) : 0.0f;
-                if (lane < nw) scw[warp][g][lane] = p;
+                if (lane < KPW) scw[warp][g][lane] = p;  // (0 past the warp's keys: the P·V slots there)
                 lw[g] = fmaf(lw[g], corr, warp_sum(p));
                 const uint64_t c2 = pk2(corr, corr);
                 o2[g][0] = mul2(o2[g][0], c2);
@@ -394,20 +394,23 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         __syncwarp();
         alive = alive && __all_sync(FULL, mbar_wait_n<MAX_BUF>(fv, t1 - t0, (t0 / n_buf) & 1, a.err));
         if (!alive) nw = 0;
-        // P·V; lane owns dims 4 lane … 4 lane + 3
-#pragma unroll 4
-        for (int kk = 0; kk < nw; kk++) {
-            const int i = w0 + kk;
-            const uint2 u = *reinterpret_cast<const uint2*>(Vs + (size_t)(i == prel ? ring : i) * HD + lane * 4);
-            const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-            const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-            const uint64_t v01 = pk2(v0.x, v0.y), v23 = pk2(v1.x, v1.y);
+        // P·V; lane owns dims 4 lane … 4 lane + 3, over all KPW slots (no trip count): a slot past the warp's
+        // keys weighs 0 on a row of its share
+        if (nw > 0) {
 #pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float p = scw[warp][g][kk];
-                const uint64_t pp = pk2(p, p);
-                o2[g][0] = fma2(pp, v01, o2[g][0]);
-                o2[g][1] = fma2(pp, v23, o2[g][1]);
+            for (int kk = 0; kk < KPW; kk++) {
+                const int i = w0 + min(kk, nw - 1);
+                const uint2 u = *reinterpret_cast<const uint2*>(Vs + (size_t)(i == prel ? ring : i) * HD + lane * 4);
+                const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+                const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+                const uint64_t v01 = pk2(v0.x, v0.y), v23 = pk2(v1.x, v1.y);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float p = scw[warp][g][kk];
+                    const uint64_t pp = pk2(p, p);
+                    o2[g][0] = fma2(pp, v01, o2[g][0]);
+                    o2[g][1] = fma2(pp, v23, o2[g][1]);
+                }
             }
         }
         if (t1 < n_tiles) {

@@ -238,7 +238,8 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                                                                           : 0.0f;
                     }
         }
-        stage_x<KT>(xsf, nch, nb, slot0, a, red, NC, wn0, blockIdx.x == 0);
+        // (the compiled LM head's partials, when any, are the fused FFN's FFN_NCLU)
+        stage_x<KT, KT ? FFN_NCLU : 0>(xsf, nch, nb, slot0, a, red, NC, wn0, blockIdx.x == 0);
         bar_sync(1, NC);
         const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
         for (int t = 0; t < n_stage; t++) {
@@ -493,7 +494,7 @@ static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
     if (g.W == 16) {
         bool done = false;
         if constexpr (NB == 1) {
-            if (a.w.cols == 1024) {
+            if (a.w.cols == 1024 && (!a.xadd || a.n_add == FFN_NCLU)) {
                 launch_t<NB, 16, 4, 1024>(st, a, g, pdl);
                 done = true;
             }
