@@ -16,18 +16,20 @@
 // global round trip and no atomic.
 //
 // Two endings. Unfused (the op entry point): each CTA merges a 1/CL slice of the output and stores it. Fused (the
-// decode step): a reduce-scatter (each CTA merges its slice from float4 copies of the ranks' partials) and an
-// all-gather (every CTA reads every slice) leave the group's whole output in every CTA, which multiplies it by its
-// dim/CL rows of W_o's slice for this kv head (fetched before the dependency wait) into opart[b][j] — the o-projection
-// as n_kv per-head partial products, summed in a fixed order by the next kernel.
+// decode step): every CTA ends with the group's whole output, which it multiplies by its dim/CL rows of W_o's slice
+// for this kv head (fetched before the dependency wait) into opart[b][j] — the o-projection as n_kv per-head partial
+// products, summed in a fixed order by the next kernel. For G ≤ 4 the exchange is by pushes: each CTA stores its
+// merged values into the shared memory of the CTA owning their 1/CL slice (st.async, counted as complete-tx on the
+// owner's mbarrier), the owner merges the slice and pushes it into every CTA; G = 8 reduce-scatters and all-gathers
+// with float4 reads of the ranks' partials between cluster barriers.
 //
 // Fused qkv (a.wqkv set; the reference's dmv_qkv.wgsl): the cluster also computes its group's (G + 2)·128 rows of
 // the [q | k | v] projection. CTA r stages the slot's residual (plus the FFN's partials, RMS-normalised by attn_norm:
 // stage.cuh, as the qkv matvec would), multiplies it by its RQ = (G + 2)·128 / CL rows of W_qkv — fetched before the
-// dependency wait into the V region, whose V tiles are copied once the projection is done — and the cluster
-// all-gathers the group's values through distributed shared memory before the q/k preparation. mbarrier waits are
-// bounded; a warp whose wait ran out skips its work (the CTA's partial is void, the error flag set) but still meets
-// every barrier.
+// dependency wait into the V region, whose V tiles are copied once the projection is done — and pushes each value
+// into every CTA of the cluster before the q/k preparation. DIM_T instances are compiled for one model dim (the
+// loops over chunks and rows straight-line). mbarrier waits are bounded; a warp whose wait ran out skips its work
+// (the CTA's partial is void, the error flag set) but still meets every barrier.
 #include <cooperative_groups.h>
 
 #include <algorithm>
