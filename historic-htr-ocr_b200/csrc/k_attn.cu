@@ -52,7 +52,9 @@ constexpr int PW = HD + 4;  // a head's partial: o[128], m, l, two floats of pad
 // DIM_T: the model's dim fixed at compile time (0: read from the arguments) — the staging, the projection's chunk
 // loop and the o-projection's rows become straight-line code
 template <int G, int CL, int DIM_T = 0>
-__global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf, int smem) {
+__global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(AttnArgs a, int n_buf_arg, int smem) {
+    // (a compiled dim's instance runs with the full ring: its slot and phase arithmetic by constants)
+    const int n_buf = DIM_T ? MAX_BUF : n_buf_arg;
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ __align__(8) uint64_t fk[MAX_BUF], fv[MAX_BUF];  // a ring slot's K rows, its V rows
     __shared__ __align__(8) uint64_t obar;  // W_o slice chunks (fused o-projection)
@@ -759,7 +761,8 @@ static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
     auto kern = k_attn_decode<G, CL>;
     // Qwen3-0.6B's decode step (fused projections, dim 1024): the instance compiled for that dim
     if constexpr (G == 2 && CL == 16)
-        if (a.wqkv.w && a.in.w.cols == 1024 && a.wo && a.dim == 1024) kern = k_attn_decode<G, CL, 1024>;
+        if (a.wqkv.w && a.in.w.cols == 1024 && a.wo && a.dim == 1024 && n_buf == MAX_BUF)
+            kern = k_attn_decode<G, CL, 1024>;
     cudaLaunchKernelEx(&cfg, kern, a, n_buf, (int)cfg.dynamicSmemBytes);
 }
 
