@@ -150,13 +150,16 @@ __device__ void choice_finish(const float* bv_sm, const uint32_t* bi_sm, int nb,
 // the streamed matvec
 // ---------------------------------------------------------------------------------------------------------------------
 constexpr int MAX_NS = 16;
+constexpr int LM_NS = 3;  // the compiled 1024-wide LM head's ring: three 64-row stages (68 KB each)
 constexpr int SM_HEAD = 256;  // mbarriers full[MAX_NS], empty[MAX_NS]
 
 // two CTAs per SM for the small matrices of one or two slots (the grid is sized for it; at most 112 registers);
 // wider slot batches keep their accumulators in registers at one CTA per SM. KT: the row length fixed at compile
 // time (0: a.w.cols) — the LM head of a 1024-wide model runs its chunk loop and bounds as straight-line code.
 template <int NB, int W, int R, int KT = 0>
-__global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_mv(MvArgs a, int rpc, int ns) {
+__global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_mv(MvArgs a, int rpc, int ns_arg) {
+    // (the compiled LM head runs a ring of LM_NS stages: its slot and phase arithmetic by constants)
+    const int ns = KT ? LM_NS : ns_arg;
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + MAX_NS;
@@ -494,7 +497,7 @@ static void launch_nb(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl) {
     if (g.W == 16) {
         bool done = false;
         if constexpr (NB == 1) {
-            if (a.w.cols == 1024 && (!a.xadd || a.n_add == FFN_NCLU)) {
+            if (a.w.cols == 1024 && (!a.xadd || a.n_add == FFN_NCLU) && g.ns == LM_NS) {
                 launch_t<NB, 16, 4, 1024>(st, a, g, pdl);
                 done = true;
             }
