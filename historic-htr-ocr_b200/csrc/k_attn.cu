@@ -636,7 +636,10 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
 #pragma unroll
                 for (int k = 0; k < 2; k++) {
                     const int rr = base + k * NW * 4 + (lane >> 3);
-                    acc[k] = OEX || rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
+                    if constexpr (OEX && NCOL % 128 == 0)
+                        acc[k] = row_dot8c<NCOL / 128>(wsm + (size_t)rr * ostride, ap, l8);
+                    else
+                        acc[k] = rr < nr ? row_dot8(wsm + (size_t)rr * ostride, NCOL, ap, l8) : 0.0f;
                 }
 #pragma unroll
                 for (int m = 4; m >= 1; m >>= 1)

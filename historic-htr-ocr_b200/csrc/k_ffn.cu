@@ -163,7 +163,11 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
 #pragma unroll
         for (int k = 0; k < 2; k++) {
             const int rr = base + k * FFN_NW * 4 + (lane >> 3);
-            acc[k] = (got_wd && got_h && (DEX || rr < drows)) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
+            constexpr int HC_T = NFF_T / FFN_NCLU;
+            if constexpr (DEX && HC_T % 128 == 0)
+                acc[k] = (got_wd && got_h) ? row_dot8c<HC_T / 128>(dsm + (size_t)rr * dstride, hp, l8) : 0.0f;
+            else
+                acc[k] = (got_wd && got_h && rr < drows) ? row_dot8(dsm + (size_t)rr * dstride, HC, hp, l8) : 0.0f;
         }
 #pragma unroll
         for (int m = 4; m >= 1; m >>= 1)

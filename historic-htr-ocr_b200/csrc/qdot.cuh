@@ -81,4 +81,26 @@ __device__ __forceinline__ float row_dot8(const uint8_t* row, int ncol, const ui
     return acc;
 }
 
+// row_dot8 for a row of exactly 128·NPC columns: the lane's NPC pieces unrolled, no trip count
+template <int NPC>
+__device__ __forceinline__ float row_dot8c(const uint8_t* row, const uint64_t* ap, int l8) {
+    constexpr int ncol = NPC * 128;
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NPC; i++) {
+        const int pc = l8 + 8 * i;
+        const uint4 wq = *reinterpret_cast<const uint4*>(row + pc * 16);
+        const float dsc = __half2float(reinterpret_cast<const __half*>(row + ncol)[pc >> 1]);
+        uint64_t xp[8];
+        const int xb = ((pc >> 5) * 128 + (pc & 31)) * 2;  // in f32 pairs
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            xp[2 * jj] = ap[xb + jj * 64];
+            xp[2 * jj + 1] = ap[xb + jj * 64 + 1];
+        }
+        acc = fmaf(dot16x2(wq, xp), dsc, acc);
+    }
+    return acc;
+}
+
 }  // namespace ocr
