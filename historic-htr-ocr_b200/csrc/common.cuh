@@ -156,12 +156,6 @@ __device__ __forceinline__ void st_async(uint32_t raddr, float2 v, uint32_t rbar
                  "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(rbar)
                  : "memory");
 }
-__device__ __forceinline__ void st_async(uint32_t raddr, float4 v, uint32_t rbar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
-                 "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
-                 "r"(__float_as_uint(v.w)), "r"(rbar)
-                 : "memory");
-}
 // the split cluster barrier (every thread of every CTA, in the same order): arrive, later wait
 __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
