@@ -719,21 +719,27 @@ static cudaLaunchConfig_t config_t(cudaStream_t st, const AttnArgs& a, cudaLaunc
 }
 
 // true when a cluster of CL CTAs of this kernel can be resident (16 needs 16 SMs of one GPC with the shared memory)
+// the instances' launch attributes, once (every cluster size: each launches with more than 48 KB of shared memory)
+template <int G, int CL>
+static void configure_t() {
+    static bool configured = false;
+    if (configured) return;
+    auto kern = k_attn_decode<G, CL>;
+    // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+    if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if constexpr (G == 2 && CL == 16) {
+        auto k1024 = k_attn_decode<G, CL, 1024>;  // (the same static shared memory)
+        cudaFuncSetAttribute(k1024, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+        cudaFuncSetAttribute(k1024, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    }
+    configured = true;
+}
+
 template <int G, int CL>
 static bool usable_t(cudaStream_t st, const AttnArgs& a) {
     auto kern = k_attn_decode<G, CL>;
-    static bool configured = false;
-    if (!configured) {
-        // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
-        if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if constexpr (G == 2 && CL == 16) {
-            auto k1024 = k_attn_decode<G, CL, 1024>;  // (the same static shared memory)
-            cudaFuncSetAttribute(k1024, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
-            cudaFuncSetAttribute(k1024, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        }
-        configured = true;
-    }
+    configure_t<G, CL>();
     if (CL <= 8) return true;
     // asked once per dynamic shared memory size
     static size_t keys[8];
@@ -757,6 +763,7 @@ static bool usable_t(cudaStream_t st, const AttnArgs& a) {
 
 template <int G, int CL>
 static void launch_t(cudaStream_t st, const AttnArgs& a, bool pdl) {
+    configure_t<G, CL>();
     cudaLaunchAttribute attr[2];
     int n_buf = 1;
     cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);

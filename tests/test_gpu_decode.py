@@ -138,6 +138,27 @@ def test_embedding_rows_and_batch_equal_single(ocr, orc, ctx, tiny):
         assert single == batch[b].tolist(), b
 
 
+def test_wide_batch_matches_oracle(ocr, orc, ctx):
+    """a batch whose (slot, kv head) pairs outnumber the 16- and 8-CTA cluster splits (5 slots x 8 kv heads: 4-CTA
+    clusters, one wave of 40): its first step and greedy choices as the oracle's per slot"""
+    cfg = dict(n_layer=2, dim=256, n_head=16, n_kv=8, d_head=128, n_ff=512, n_vocab=1000, eps=1e-6, rope_base=1e6)
+    B, n_new = 5, 12
+    om = orc.Model(cfg, seed=43, sigma_w=0.2, sigma_e=1.0)
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 43, 0.2, 1.0)
+    prompts = [[int(t) for t in orc.fill_ids(20 + b, 10, cfg["n_vocab"])] for b in range(B)]
+    sess = gm.session(48, batch=B)
+    wants = []
+    for b, prompt in enumerate(prompts):
+        lg = sess.prefill(b, ids=prompt)
+        os_ = om.session(48)
+        lo = os_.prefill(prompt, None, len(prompt))
+        close_logits(lg, lo)
+        wants.append(os_.decode(lo, 1.1, 8, 0.0, prompt, n_new)[0].tolist())
+    got = sess.decode_batch(ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, n_new), np.array(prompts, np.int32))
+    for b in range(B):
+        assert got[b].tolist() == wants[b], b
+
+
 @pytest.mark.parametrize("shape", [
     dict(n_layer=2, dim=256, n_head=16, n_kv=16, d_head=128, n_ff=512, n_vocab=1000),  # 16 kv heads: unfused o-proj
     dict(n_layer=2, dim=1280, n_head=2, n_kv=1, d_head=128, n_ff=512, n_vocab=1000),   # dim > 1024: wide staging
