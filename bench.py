@@ -317,7 +317,7 @@ def run_config1(args, ocr, ctx, torch, pg, rank, world):
             "warmup": 3, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 x f32", "data": "synthetic",
             "config": {"workload": "BASELINE config 1: LM head 151936 x 1024 q8_0 + windowed penalty + argmax",
-                       "l2": "flushed between launches (256 MB write)"},
+                       "l2": "flushed between launches (a 256 MB read)"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 4), "peak_source": which, "traffic": None},
             "clocks": clk.summary()}), flush=True)

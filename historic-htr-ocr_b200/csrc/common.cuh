@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 
 #include "ocr_cuda.h"
@@ -30,6 +31,37 @@ ocr_status cuda_fail(cudaError_t e, const char* what);
         ocr_status s_ = (call);                                                                                        \
         if (s_ != OCR_OK) return s_;                                                                                   \
     } while (0)
+
+// Kernel attributes (the opt-in shared memory limit, non-portable cluster sizes) belong to the current device's
+// context, and occupancy answers are per device: a process may drive contexts on several GPUs, so every such setup
+// and cache is kept per device. MAX_DEVICES bounds the tables.
+constexpr int MAX_DEVICES = 64;
+inline int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        d = 0;
+    }
+    return d;
+}
+// runs f() once per device (the current one), serialised across host threads
+struct PerDeviceOnce {
+    std::mutex mu;
+    bool done[MAX_DEVICES] = {};
+    template <class F>
+    void operator()(F&& f) {
+        const int d = current_device();
+        std::lock_guard<std::mutex> lock(mu);
+        if (d < 0 || d >= MAX_DEVICES) {
+            f();
+            return;
+        }
+        if (!done[d]) {
+            f();
+            done[d] = true;
+        }
+    }
+};
 
 // ---- device -----------------------------------------------------------------------------------------------------
 constexpr unsigned FULL = 0xffffffffu;

@@ -722,18 +722,18 @@ static cudaLaunchConfig_t config_t(cudaStream_t st, const AttnArgs& a, cudaLaunc
 // the instances' launch attributes, once (every cluster size: each launches with more than 48 KB of shared memory)
 template <int G, int CL>
 static void configure_t() {
-    static bool configured = false;
-    if (configured) return;
-    auto kern = k_attn_decode<G, CL>;
-    // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
-    if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if constexpr (G == 2 && CL == 16) {
-        auto k1024 = k_attn_decode<G, CL, 1024>;  // (the same static shared memory)
-        cudaFuncSetAttribute(k1024, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
-        cudaFuncSetAttribute(k1024, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    }
-    configured = true;
+    static PerDeviceOnce once;  // the attributes live in each device's context
+    once([] {
+        auto kern = k_attn_decode<G, CL>;
+        // the opt-in limit: what the SM offers a CTA minus this kernel's static shared memory
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+        if (CL > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if constexpr (G == 2 && CL == 16) {
+            auto k1024 = k_attn_decode<G, CL, 1024>;  // (the same static shared memory)
+            cudaFuncSetAttribute(k1024, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - static_smem<G, CL>());
+            cudaFuncSetAttribute(k1024, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        }
+    });
 }
 
 template <int G, int CL>
@@ -741,20 +741,25 @@ static bool usable_t(cudaStream_t st, const AttnArgs& a) {
     auto kern = k_attn_decode<G, CL>;
     configure_t<G, CL>();
     if (CL <= 8) return true;
-    // asked once per dynamic shared memory size
-    static size_t keys[8];
-    static bool vals[8];
+    // asked once per (device, dynamic shared memory size), under a lock (contexts may live on several threads)
+    static std::mutex mu;
+    static int dev_k[16];
+    static size_t keys[16];
+    static bool vals[16];
     static int n_keys = 0;
     cudaLaunchAttribute attr[2];
     int n_buf = 1, n = 0;
     cudaLaunchConfig_t cfg = config_t<G, CL>(st, a, attr, &n_buf);
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < n_keys; i++)
-        if (keys[i] == cfg.dynamicSmemBytes) return vals[i];
+        if (dev_k[i] == dev && keys[i] == cfg.dynamicSmemBytes) return vals[i];
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
     }
-    if (n_keys < 8) {
+    if (n_keys < 16) {
+        dev_k[n_keys] = dev;
         keys[n_keys] = cfg.dynamicSmemBytes;
         vals[n_keys++] = n >= 1;
     }

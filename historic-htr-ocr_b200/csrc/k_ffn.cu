@@ -208,25 +208,28 @@ static void ffn_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, cudaS
 // shape generic
 using FfnKernel = void (*)(FfnArgs);
 static FfnKernel ffn_kernel(int dim, int n_ff, int n_add) {
-    static bool configured = false;
-    if (!configured) {
+    static PerDeviceOnce once;  // the attributes live in each device's context
+    once([] {
         for (FfnKernel k : {k_ffn<1024, 3072, 8>, k_ffn<0, 0, 0>}) {
             cudaFuncAttributes fa;
             cudaFuncGetAttributes(&fa, k);
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
             cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         }
-        configured = true;
-    }
+    });
     return dim == 1024 && n_ff == 3072 && n_add == 8 ? k_ffn<1024, 3072, 8> : k_ffn<0, 0, 0>;
 }
 
 bool ffn_usable(int dim, int n_ff) {
     const int smem = ffn_smem(dim, n_ff);
     if (!smem) return false;
-    static int keys[8], vals[8], n_keys = 0;
+    // asked once per (device, shared memory size), under a lock
+    static std::mutex mu;
+    static int dev_k[16], keys[16], vals[16], n_keys = 0;
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < n_keys; i++)
-        if (keys[i] == smem) return vals[i] != 0;
+        if (dev_k[i] == dev && keys[i] == smem) return vals[i] != 0;
     const FfnKernel kern = ffn_kernel(dim, n_ff, 8);  // (either instance: the same resources)
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[2];
@@ -236,7 +239,8 @@ bool ffn_usable(int dim, int n_ff) {
         cudaGetLastError();
         n = 0;
     }
-    if (n_keys < 8) {
+    if (n_keys < 16) {
+        dev_k[n_keys] = dev;
         keys[n_keys] = smem;
         vals[n_keys++] = n >= FFN_NCLU;  // every cluster resident at once
     }

@@ -447,31 +447,34 @@ int lm_head_grid(int num_sms, int n_vocab, int dim) {
 
 template <int NB, int W, int R, int KT = 0>
 static void configure_t() {
-    static bool configured = false;
-    if (!configured) {
+    static PerDeviceOnce once;  // the attribute lives in each device's context
+    once([] {
         auto kern = k_mv<NB, W, R, KT>;
         cudaFuncAttributes fa;
         cudaFuncGetAttributes(&fa, kern);
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - (int)fa.sharedSizeBytes);
-        configured = true;
-    }
+    });
 }
 
 // CTAs of this instantiation resident per SM with a small matrix's shared memory (registers decide: the build's
-// count for the template), asked once
+// count for the template), asked once per device
 template <int NB, int W, int R>
 static int per_sm_t() {
-    static int n = -1;
-    if (n < 0) {
-        configure_t<NB, W, R>();
+    configure_t<NB, W, R>();
+    static PerDeviceOnce once;
+    static int n_dev[MAX_DEVICES];
+    const int d = current_device();
+    int n = 1;
+    once([&] {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_mv<NB, W, R>, (W + 1) * 32, SMEM_SMALL) !=
             cudaSuccess) {
             cudaGetLastError();
             n = 1;
         }
         n = std::max(1, std::min(2, n));
-    }
-    return n;
+        if (d >= 0 && d < MAX_DEVICES) n_dev[d] = n;
+    });
+    return d >= 0 && d < MAX_DEVICES ? n_dev[d] : n;
 }
 
 template <int NB, int W, int R, int KT = 0>

@@ -1840,7 +1840,10 @@ ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp,
 // or streams) race on it; calls queued on one context's stream are ordered and safe.
 namespace {
 
-constexpr size_t NOALLOC_SCRATCH_BYTES = 16384;  // partials of up to 2000 CTAs + the ticket
+constexpr size_t NOALLOC_SCRATCH_BYTES = 16384;
+// the ticket sits on its own 256 B after the partials (8 B per CTA, plus one NaN flag and the 256 B gap): the CTA count
+// the array holds, 2015
+constexpr int NOALLOC_MAX_CTAS = (int)((NOALLOC_SCRATCH_BYTES - 264) / 8);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
 constexpr int NOALLOC_MAX_DEVICES = 64;
@@ -1874,9 +1877,9 @@ ocr_status ocr_op_lm_head_sample_noalloc(ocr_ctx* ctx, const uint8_t* d_w, int n
     if (window < 1) return fail(OCR_ERR_ARG, "repetition window must be >= 1");
     const int grid = lm_head_grid(ctx->num_sms, n_vocab, dim);
     const size_t o_done = ((size_t)grid * 2 + 1) * 4 + 256;  // partials, then the ticket on its own 256 B
-    if (o_done + 4 > NOALLOC_SCRATCH_BYTES)
+    if (grid > NOALLOC_MAX_CTAS || o_done + 4 > NOALLOC_SCRATCH_BYTES)
         return fail(OCR_ERR_ARG, "the LM head would run " + std::to_string(grid) + " CTAs; the static scratch holds the partials of at most " +
-                                     std::to_string((NOALLOC_SCRATCH_BYTES - 264) / 8));
+                                     std::to_string(NOALLOC_MAX_CTAS));
     OCR_CUDA(cudaSetDevice(ctx->device));
     void* scratch = nullptr;
     OCR_TRY(noalloc_scratch(ctx->device, &scratch));

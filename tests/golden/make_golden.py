@@ -1,6 +1,6 @@
 """Generate the committed golden fixtures under tests/golden/ (run here, in the container that mounts the reference).
 
-    python tests/golden/make_golden.py penalty [--reference-root DIR]   → penalty_ref.json
+    python tests/golden/make_golden.py penalty --reference-root DIR     → penalty_ref.json
     python tests/golden/make_golden.py config2                          → config2_greedy.json
 
 penalty: the reference's own windowed repetition penalty — hf/window_rep_penalty.py's WindowRepetitionPenalty.apply
@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 import time
 import types
@@ -144,9 +145,12 @@ def make_config2() -> dict:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["penalty", "config2"])
-    ap.add_argument("--reference-root", default="/root/reference")
+    ap.add_argument("--reference-root", default=os.environ.get("OCR_REFERENCE_ROOT"),
+                    help="the reference checkout (or OCR_REFERENCE_ROOT); needed for `penalty` only")
     a = ap.parse_args()
     if a.what == "penalty":
+        if not a.reference_root:
+            ap.error("penalty needs --reference-root DIR (or OCR_REFERENCE_ROOT): the reference's hf/ directory")
         out = make_penalty(Path(a.reference_root))
         (HERE / "penalty_ref.json").write_text(json.dumps(out, indent=1))
     else:

@@ -287,3 +287,24 @@ def test_config2_greedy_ids_match_oracle(ocr, ctx):
     want = fx["ids"]
     k = next((i for i in range(len(want)) if got[i] != want[i]), None)
     assert k is None, f"first divergence at choice {k}: device {got[k]} vs oracle {want[k]} (margin {fx['margins'][k]})"
+
+
+def test_contexts_on_two_devices(ocr, orc, torch_cuda):
+    """kernel attributes (the opt-in shared memory, 16-CTA clusters) are set per device: a process with a context on
+    each of two GPUs decodes on both, the same ids as the oracle's"""
+    if torch_cuda.cuda.device_count() < 2:
+        pytest.skip("one GPU visible")
+    om = orc.Model(TINY, seed=31, sigma_w=0.2, sigma_e=1.0)
+    prompt = [int(t) for t in orc.fill_ids(5, 20, TINY["n_vocab"])]
+    os_ = om.session(64)
+    want, _ = os_.decode(os_.prefill(prompt, None, len(prompt)), 1.1, 20, 0.0, prompt, 16)
+    for dev in (1, 0):
+        c = ocr.Context(dev)
+        m = ocr.TextModel.synthetic(c, text_config(ocr, TINY), 31, 0.2, 1.0)
+        s = m.session(64)
+        s.prefill(0, ids=prompt, logits=False)
+        got = s.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1.1, 20, 0.0, 16), prompt)
+        assert got == want.tolist(), dev
+        s.close()
+        m.close()
+        c.close()

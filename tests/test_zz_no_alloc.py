@@ -40,14 +40,24 @@ def test_noalloc_lm_head_equals_lm_head(ocr, orc, torch_cuda, vocab, window, rp)
 
     ctx = ocr.Context(0)  # a fresh context: its memory ledger shows what the call allocates
     try:
+        # one call on a throwaway state first: with lazy module loading the first launch loads the kernels' module
+        # (and with it the static array, which the library holds from then on); the checks below are on later calls
+        hw, lw, tw, gw = state()
+        ocr.op_lm_head_sample_noalloc(ctx, wd.data_ptr(), vocab, dim, xd.data_ptr(), nwd.data_ptr(), 1e-6, rp,
+                                      window, hw.data_ptr(), lw.data_ptr(), tw.data_ptr(), gw.data_ptr())
+        ctx.sync()
         ha, la, ta, ga = state()
         hb, lb, tb, gb = state()
         for call in range(2):  # two in a row on the same state: the second decodes one token further
             before = ctx.memory()
+            torch.cuda.synchronize()
+            free_before = torch.cuda.mem_get_info()[0]  # the driver's count: sees any cudaMalloc, tracked or not
             ocr.op_lm_head_sample_noalloc(ctx, wd.data_ptr(), vocab, dim, xd.data_ptr(), nwd.data_ptr(), 1e-6, rp,
                                           window, ha.data_ptr(), la.data_ptr(), ta.data_ptr(), ga.data_ptr())
             ctx.sync()
+            torch.cuda.synchronize()
             assert ctx.memory() == before, "the no-alloc call took device memory"
+            assert torch.cuda.mem_get_info()[0] == free_before, "the no-alloc call changed the device's free memory"
             ocr.op_lm_head_sample(ctx, wd.data_ptr(), vocab, dim, xd.data_ptr(), nwd.data_ptr(), 1e-6, rp, window,
                                   hb.data_ptr(), lb.data_ptr(), tb.data_ptr(), gb.data_ptr())
             ctx.sync()
