@@ -1,0 +1,673 @@
+// k_bgemm.cu — the batched decode contraction on the 5th-generation tensor cores (tcgen05, sm_100a): the reference's
+// q8_0 matvecs (shaders/dmv.wgsl, dmv_qkv.wgsl, dmv_ffn.wgsl, the LM head's dmv_norm) and its tiled GEMM
+// (shaders/matmul128.wgsl, the `matmul` dispatch of app/crates/ocr-wgpu/src/gpu.rs:1967-2016) for a batch of decode
+// slots, Y[slot][row] = sum_k W[row][k] x[slot][k], with the same epilogues as the CUDA-core matvec (store, residual
+// add, SwiGLU over interleaved gate/up rows, the LM head's windowed penalty + first-maximum choice).
+//
+// Numerics. Each weight q * d (int8 times the block's f16 scale) is exact in f32 and splits exactly into two f16
+// values, w_hi = RN_f16(q * d) (one HMUL2) and w_lo = RN_f16(q * d - w_hi) (one HFMA2 — the remainder has at most 8
+// significant bits, so it is exact unless it falls below f16's normal range); each activation splits the same way,
+// x_hi = RN_f16(x), x_lo = RN_f16(x - x_hi). tcgen05.mma kind::f16 multiplies f16 pairs exactly and accumulates in f32,
+// so D = w_hi x_hi + w_hi x_lo + w_lo x_hi carries the f32 matvec's result to within f32 rounding; the dropped w_lo x_lo
+// is below 2^-22 of each product.
+//
+// One CTA per SM, persistent over 128-row tiles of W (tile t, t + grid, …), 320 threads in three roles:
+//  - warp 0 (one lane), the copies: per 128-column chunk of K, one TMA tile of the quants (128 rows x 128 B, 128-B
+//    swizzle, from the row layout through a tensor map) and one bulk copy of the slots' activation chunk (16 KB, already
+//    in the MMA operand order), both counted on the stage's mbarrier; a 128-row tile's block scales once per tile. The
+//    weights of the first stages are issued before griddepcontrol.wait (they never depend on the previous kernel).
+//  - warps 2-9, the dequantisation: per 64-column half chunk, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
+//    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into the A operand buffers in core-matrix order; then, per
+//    tile, the epilogue: tcgen05.ld of their TMEM lanes, hi + lo columns summed, the mode's output.
+//  - warp 1, the tensor cores: TMEM allocation (64 columns: 32 slots' hi products + 32 slots' lo products), and per
+//    16-column step two MMAs (M = 128): A = w_hi with B = [x_hi | x_lo] (N = 64), A = w_lo with B = x_hi (N = 32) into the
+//    first 32 columns; tcgen05.commit releases the operand buffer, the copy stage, and at a tile's end the accumulator
+//    to the epilogue.
+// Every mbarrier wait is bounded; a wait that runs out sets the device error flag and a shared abort flag that every
+// role polls; the copies in flight and the MMAs issued are then waited for (bounded) and the TMEM is freed before the
+// CTA exits.
+#include <cudaTypedefs.h>
+
+#include "choice.cuh"
+#include "kernels.cuh"
+
+namespace ocr {
+
+constexpr int BG_M = 128;       // weight rows per tile: the MMA's M, one TMEM lane each
+constexpr int BG_KC = 128;      // K columns per copy stage
+constexpr int BG_KS = 64;       // K columns per dequantised operand buffer
+constexpr int BG_THREADS = 320;
+constexpr int BG_DQ = 256;      // dequantisation / epilogue threads (warps 2-9)
+constexpr uint32_t BG_WTILE = BG_M * BG_KC;                 // 16 KB of int8 quants
+constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 32 KB
+constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of one half chunk
+constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
+constexpr int BG_NA = 2;        // operand buffers
+constexpr int BG_MAX_NS = 4;    // copy stages
+constexpr uint32_t BG_TMEM_COLS = 64;
+constexpr int BG_SMEM_OPTIN = 227 * 1024;
+
+// ---- tcgen05 / TMA primitives ------------------------------------------------------------------------------------------
+// instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16 (0), both K-major (bits 15, 16 = 0), N >> 3 at
+// bit 17, M >> 4 at bit 24
+__host__ __device__ constexpr uint32_t bg_idesc(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BG_M >> 4) << 24);
+}
+// shared-memory matrix descriptor, K-major without swizzle: start >> 4, `lbo` = bytes to the next 8-column core along
+// K, `sbo` = bytes to the next group of 8 rows, descriptor version 1 (bit 46) of sm_100
+__device__ __forceinline__ uint64_t bg_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+           (1ull << 46);
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// D[tmem] (+)= A[desc a] . B[desc b]^T, both K-major f16, f32 accumulate (accumulate = 0: D is overwritten)
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// the mbarrier gets one arrive when every MMA this thread issued before has completed
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 16 consecutive f32 columns of the warp's 32 TMEM lanes (lane i of the warp reads TMEM lane base + i)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// a 2-D TMA tile load (x = the inner coordinate in elements; a multiple of 16 bytes here), counted on `bar`
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// a bounded wait that also gives up when another role of the CTA has given up (`abort_flag`)
+__device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    dev_error(err, DEV_TIMEOUT);
+    return false;
+}
+
+// 16 int8 quants and their f16 block scale → 8 half2 of w_hi and 8 of w_lo (w_hi + w_lo = q * d exactly)
+__device__ __forceinline__ void dequant16(uint4 q, __half d, uint32_t* hi, uint32_t* lo) {
+    const __half2 d2 = __half2half2(d);
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152 = 1024 + 128
+    const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        // 0x64bb as f16 is 1024 + bb exactly: bytes (q + 128) below the 0x64 exponent byte
+        uint32_t p01 = __byte_perm(w[k], 0x64646464u, 0x5140), p23 = __byte_perm(w[k], 0x64646464u, 0x5342);
+        const __half2 q01 = __hsub2(*reinterpret_cast<__half2*>(&p01), bias);
+        const __half2 q23 = __hsub2(*reinterpret_cast<__half2*>(&p23), bias);
+        const __half2 h01 = __hmul2(q01, d2), h23 = __hmul2(q23, d2);
+        const __half2 l01 = __hfma2(q01, d2, __hneg2(h01)), l23 = __hfma2(q23, d2, __hneg2(h23));
+        hi[2 * k] = *reinterpret_cast<const uint32_t*>(&h01);
+        hi[2 * k + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+        lo[2 * k] = *reinterpret_cast<const uint32_t*>(&l01);
+        lo[2 * k + 1] = *reinterpret_cast<const uint32_t*>(&l23);
+    }
+}
+
+struct BgShared {
+    uint64_t tfull[BG_MAX_NS], tempty[BG_MAX_NS];  // copy stage landed / free again (MMAs done)
+    uint64_t afull[BG_NA], aempty[BG_NA];          // operand buffer written / free again
+    uint64_t sfull[2], sempty[2];                  // a tile's block scales landed / read
+    uint64_t tfin, mdone;                          // a tile's accumulator complete; every MMA done (exit)
+    uint32_t tmem_base;
+    int abort_flag;
+    uint32_t pbits[BG_SLOTS][BG_M / 32];  // LM head: the tile's rows in each slot's penalty window
+    float bvq[8][16];                     // LM head: each epilogue warp's best per slot
+    uint32_t biq[8][16];
+    float bv[BG_SLOTS];
+    uint32_t bi[BG_SLOTS];
+};
+
+__global__ void __launch_bounds__(BG_THREADS, 1)
+    k_bgemm(const __grid_constant__ BgArgs a, const __grid_constant__ CUtensorMap mq,
+            const __grid_constant__ CUtensorMap ms, int ns) {
+    extern __shared__ uint8_t sm_raw[];
+    __shared__ __align__(16) BgShared sh;
+    volatile int* abort_flag = &sh.abort_flag;
+
+    const int K = a.w.cols, N = a.w.rows;
+    const int nkc = K / BG_KC;
+    const int sbytes = BG_M * (K / 16);  // a tile's block scales (TMA box K/16 x 128 rows)
+    const int sstride = (sbytes + 1023) & ~1023;
+    // the dynamic region starts 1024-B aligned (the 128-B swizzle's pattern repeats every 1024 B)
+    uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+    uint8_t* stage0 = smp;
+    uint8_t* abuf0 = smp + (size_t)ns * BG_STAGE;
+    uint8_t* sbuf0 = abuf0 + BG_NA * BG_ABUF;
+    const int n_tiles = (N + BG_M - 1) / BG_M;
+    const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
+    const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool lmhead = a.mode == MV_LMHEAD;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < ns; i++) {
+            mbar_init(&sh.tfull[i], 1);
+            mbar_init(&sh.tempty[i], 1);
+        }
+        for (int i = 0; i < BG_NA; i++) {
+            mbar_init(&sh.afull[i], BG_DQ / 32);
+            mbar_init(&sh.aempty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sh.sfull[i], 1);
+            mbar_init(&sh.sempty[i], BG_DQ / 32);
+        }
+        mbar_init(&sh.tfin, 1);
+        mbar_init(&sh.mdone, 1);
+        sh.abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&sh.tmem_base, BG_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem_base;
+
+    if (warp == 0) {
+        // ---- the copies ----
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first();
+            prefetch_tmap(&mq);
+            prefetch_tmap(&ms);
+            uint32_t g = 0;
+            int li = 0, s_issued = 0;
+            int pre = 0;
+            const int t0 = blockIdx.x;
+            if (t0 < n_tiles) {
+                // before the dependency wait: the first tile's scales and the quants of the first stages
+                mbar_expect_tx(&sh.sfull[0], (uint32_t)sbytes);
+                tma_2d(sbuf0, &ms, 0, t0 * BG_M, &sh.sfull[0], pol);
+                s_issued = 1;
+                pre = min(ns, nkc);
+                for (int s = 0; s < pre; s++) {
+                    mbar_expect_tx(&sh.tfull[s], BG_STAGE);
+                    tma_2d(stage0 + (size_t)s * BG_STAGE, &mq, s * BG_KC, t0 * BG_M, &sh.tfull[s], pol);
+                }
+            }
+            pdl_trigger();
+            pdl_wait();
+            bool ok = true;
+            for (int t = t0; t < n_tiles && ok; t += gridDim.x, li++) {
+                const int sb = li & 1;
+                if (li > 0) {
+                    if (li >= 2 && !bg_wait(&sh.sempty[sb], ((li >> 1) - 1) & 1, abort_flag, a.err)) break;
+                    mbar_expect_tx(&sh.sfull[sb], (uint32_t)sbytes);
+                    tma_2d(sbuf0 + (size_t)sb * sstride, &ms, 0, t * BG_M, &sh.sfull[sb], pol);
+                    s_issued = li + 1;
+                }
+                for (int kc = 0; kc < nkc; kc++, g++) {
+                    const int s = (int)(g % (uint32_t)ns);
+                    uint8_t* st = stage0 + (size_t)s * BG_STAGE;
+                    if (g >= (uint32_t)pre) {  // (the prologue issued the quants of the first `pre` stages)
+                        if (g >= (uint32_t)ns && !bg_wait(&sh.tempty[s], ((g / ns) - 1) & 1, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&sh.tfull[s], BG_STAGE);
+                        tma_2d(st, &mq, kc * BG_KC, t * BG_M, &sh.tfull[s], pol);
+                    }
+                    bulk_g2s(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.tfull[s]);
+                }
+            }
+            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete);
+            // a stage whose activations were never issued (an abort between its quants and them) is not waited for
+            const uint32_t issued = max(g, (uint32_t)pre);
+            for (int s = 0; s < ns && (uint32_t)s < issued; s++) {
+                const uint32_t n = (issued - s + ns - 1) / ns;
+                if (*abort_flag && (uint32_t)s + (n - 1) * ns >= g) continue;
+                mbar_wait(&sh.tfull[s], (n - 1) & 1, a.err);
+            }
+            for (int i = max(0, s_issued - 2); i < s_issued; i++) mbar_wait(&sh.sfull[i & 1], (i >> 1) & 1, a.err);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- the tensor cores ----
+        if (lane == 0) {
+            const uint32_t id1 = bg_idesc(64), id2 = bg_idesc(32);
+            uint32_t g = 0, ai = 0;
+            bool any = false, ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                for (int kc = 0; kc < nkc && ok; kc++, g++) {
+                    const int s = (int)(g % (uint32_t)ns);
+                    if (!bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t xs = smem_u32(stage0 + (size_t)s * BG_STAGE + BG_WTILE);
+                    for (int h = 0; h < 2; h++, ai++) {
+                        const int ab = (int)(ai % BG_NA);
+                        if (!bg_wait(&sh.afull[ab], (ai / BG_NA) & 1, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t ah = smem_u32(abuf0 + (size_t)ab * BG_ABUF), al = ah + BG_AHALF;
+#pragma unroll
+                        for (int ks = 0; ks < BG_KS / 16; ks++) {
+                            const uint64_t dh = bg_desc(ah + ks * 256, 128, 1024);
+                            const uint64_t dl = bg_desc(al + ks * 256, 128, 1024);
+                            const uint64_t db = bg_desc(xs + (h * 4 + ks) * 256, 128, 2048);
+                            mma_f16(tmem, dh, db, id1, (kc | h | ks) != 0);
+                            mma_f16(tmem, dl, db, id2, 1u);
+                        }
+                        mma_commit(&sh.aempty[ab]);
+                        any = true;
+                    }
+                    if (ok) mma_commit(&sh.tempty[s]);
+                }
+                if (ok) mma_commit(&sh.tfin);
+            }
+            if (any) {  // every MMA complete before the accumulator is freed (bounded, abort or not)
+                mma_commit(&sh.mdone);
+                mbar_wait(&sh.mdone, 0, a.err);
+            }
+        }
+        __syncwarp();
+    }
+
+    // ---- dequantisation and epilogue (warps 2-9) ----
+    const int et = (int)threadIdx.x - 64, dw = warp - 2;
+    const int q = warp & 3, half = dw >> 2;  // the TMEM lane quarter this warp may read; its 16 slots
+    float best_v[16];
+    uint32_t best_i[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        best_v[j] = -INFINITY;
+        best_i[j] = NO_INDEX;
+    }
+    if (warp >= 2) {
+        pdl_wait();
+        bool act[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            const int sl = 16 * half + j;
+            act[j] = sl < nb && (!a.active || a.active[slot0 + sl] != 0);
+        }
+        // A warp whose wait gave up (ok = false) still walks every loop, skipping waits and work, so that all eight
+        // warps meet each named barrier of the epilogue the same number of times.
+        uint32_t g = 0, ai = 0;
+        int li = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, li++) {
+            const int sb = li & 1;
+            ok = ok && bg_wait(&sh.sfull[sb], (li >> 1) & 1, abort_flag, a.err);
+            const uint8_t* sc = sbuf0 + (size_t)sb * sstride;
+            for (int kc = 0; kc < nkc; kc++, g++) {
+                const int s = (int)(g % (uint32_t)ns);
+                ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
+                const uint8_t* wt = stage0 + (size_t)s * BG_STAGE;
+                for (int h = 0; h < 2; h++, ai++) {
+                    const int ab = (int)(ai % BG_NA);
+                    ok = ok && (ai < BG_NA || bg_wait(&sh.aempty[ab], ((ai / BG_NA) - 1) & 1, abort_flag, a.err));
+                    if (!ok) continue;
+                    uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        // item i: rows 8 rg + r8, 16 columns c4 of the half chunk; a quarter-warp takes 8 rows of one
+                        // 16-column piece (conflict-free reads through the swizzle, 128 contiguous bytes written)
+                        const int i = et + BG_DQ * j, r8 = i & 7, c4 = (i >> 3) & 3, rg = i >> 5, row = rg * 8 + r8;
+                        const int ch = h * 4 + c4;
+                        const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
+                        const int blk = (kc * BG_KC + h * BG_KS + c4 * 16) >> 5;
+                        const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
+                        uint32_t hi[8], lo[8];
+                        dequant16(qv, d, hi, lo);
+                        const int off = (rg * 8 + c4 * 2) * 128 + r8 * 16;
+                        *reinterpret_cast<uint4*>(ah + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(ah + off + 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        *reinterpret_cast<uint4*>(ah + BG_AHALF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4*>(ah + BG_AHALF + off + 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
+                    fence_proxy_async();  // the generic stores, before the tensor cores read them
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.afull[ab]);
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(&sh.sempty[sb]);
+
+            // ---- the tile's epilogue ----
+            const int r0 = t * BG_M, row = r0 + 32 * q + lane;
+            if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {
+                // the window's tokens that fall in this tile, per slot (the 256 epilogue threads, barrier 2)
+                uint32_t* pb = &sh.pbits[0][0];
+                for (int i = et; i < BG_SLOTS * (BG_M / 32); i += BG_DQ) pb[i] = 0u;
+                bar_sync(2, BG_DQ);
+                const int sl = et >> 3, part = et & 7, b = slot0 + sl;
+                if (sl < nb && (!a.active || a.active[b])) {
+                    const int len = a.lm.len[b];
+                    const int32_t* hst = a.lm.hist + (long)b * a.lm.hist_cap;
+                    for (int jj = len - min(len, a.lm.window) + part; jj < len; jj += 8) {
+                        const int tk = hst[jj];
+                        if (tk >= r0 && tk < r0 + BG_M) atomicOr(&sh.pbits[sl][(tk - r0) >> 5], 1u << ((tk - r0) & 31));
+                    }
+                }
+                bar_sync(2, BG_DQ);
+            }
+            ok = ok && bg_wait(&sh.tfin, li & 1, abort_flag, a.err);
+            if (!ok) continue;
+            tc_fence_after();
+            uint32_t rh[16], rl[16];
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
+            tmem_ld16(ta + 16 * half, rh);
+            tmem_ld16(ta + 32 + 16 * half, rl);
+            tmem_wait_ld();
+            tc_fence_before();  // these reads, before the next tile's MMAs overwrite the accumulator
+            float y[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+            if (a.mode == MV_SWIGLU) {
+                // rows interleaved (gate, up): the even lane of each pair writes silu(gate) * up
+                const int col = row >> 1;
+                uint8_t* y16 = a.y16 ? a.y16 + (size_t)grp * x16_group_bytes(N / 2) : nullptr;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float up = __shfl_xor_sync(FULL, y[j], 1);
+                    const int sl = 16 * half + j;
+                    if ((lane & 1) || !act[j] || row >= N) continue;
+                    const float gv = y[j];
+                    const float hv = gv / (1.0f + expf(-gv)) * up;
+                    if (a.y) a.y[(long)(slot0 + sl) * a.y_stride + col] = hv;
+                    if (y16) {
+                        const __half hh = __float2half_rn(hv);
+                        const __half hl = __float2half_rn(hv - __half2float(hh));
+                        *reinterpret_cast<__half*>(y16 + x16_offset(sl, col)) = hh;
+                        *reinterpret_cast<__half*>(y16 + x16_offset(BG_SLOTS + sl, col)) = hl;
+                    }
+                }
+            } else if (!lmhead) {
+                if (row < N) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (!act[j]) continue;
+                        float* yp = a.y + (long)(slot0 + 16 * half + j) * a.y_stride + row;
+                        *yp = a.mode == MV_ADD ? *yp + y[j] : y[j];
+                    }
+                }
+            } else if (row < N) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (!act[j]) continue;
+                    const int sl = 16 * half + j, b = slot0 + sl;
+                    if (a.y) a.y[(long)b * N + row] = y[j];
+                    if (a.lm.sample) {
+                        const bool member = (sh.pbits[sl][q] >> lane) & 1u;
+                        const float v = pen_value(y[j], member, b, row, a.lm, N);
+                        if (row == 0) reinterpret_cast<int*>(a.lm.part + (long)a.lm.nb * gridDim.x * 2)[b] = (v != v);
+                        if (better(v, (uint32_t)row, best_v[j], best_i[j])) {
+                            best_v[j] = v;
+                            best_i[j] = (uint32_t)row;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BG_TMEM_COLS);
+    }
+    if (!lmhead || !a.lm.sample) return;  // (uniform over the grid)
+    // ---- the LM head's choice: each slot's best over the CTA's tiles, then the last CTA picks ----
+    if (warp >= 2) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            float v = best_v[j];
+            uint32_t i = best_i[j];
+            warp_argmax(v, i);
+            if (lane == 0) {
+                sh.bvq[dw][j] = v;
+                sh.biq[dw][j] = i;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < BG_SLOTS) {
+        const int sl = threadIdx.x, hf = sl >> 4, j = sl & 15;
+        float v = -INFINITY;
+        uint32_t i = NO_INDEX;
+        for (int w = 4 * hf; w < 4 * hf + 4; w++)
+            if (better(sh.bvq[w][j], sh.biq[w][j], v, i)) {
+                v = sh.bvq[w][j];
+                i = sh.biq[w][j];
+            }
+        sh.bv[sl] = v;
+        sh.bi[sl] = i;
+    }
+    __syncthreads();
+    choice_finish(sh.bv, sh.bi, nb, slot0, a.lm, N);
+}
+
+// ---- the activations' operand: per slot, sum, norm, hi / lo split ---------------------------------------------------
+constexpr int XP_THREADS = 256;
+
+__global__ void __launch_bounds__(XP_THREADS) k_xprep(PrepArgs a) {
+    __shared__ float red[XP_THREADS / 32];
+    const int b = blockIdx.x, K = a.K, n = b % BG_SLOTS;
+    uint8_t* xg = a.x16 + (size_t)(b / BG_SLOTS) * x16_group_bytes(K);
+    pdl_trigger();  // the contraction's weight copies may start; its activation copies wait for this grid
+    pdl_wait();
+    const bool live = b < a.nb && (!a.active || a.active[b] != 0);
+    constexpr int IT = 2;  // items of 8 columns per thread: K <= 8 x 2 x 256
+    float v[IT][8];
+    float ss = 0.0f;
+    const uint8_t* er = nullptr;
+    if (live && a.tok) {
+        const int t = a.tok[b];
+        if (t >= 0 && t < a.emb.rows) er = a.emb.w + (long)t * a.emb.stride;
+        else dev_error(a.err, DEV_BAD_INDEX);
+    }
+#pragma unroll
+    for (int it = 0; it < IT; it++) {
+        const int e = threadIdx.x + XP_THREADS * it, k0 = 8 * e;
+#pragma unroll
+        for (int c = 0; c < 8; c++) v[it][c] = 0.0f;
+        if (!live || k0 >= K) continue;
+        if (a.tok) {
+            if (er) {
+                const uint2 qq = *reinterpret_cast<const uint2*>(er + k0);
+                const float d = __half2float(reinterpret_cast<const __half*>(er + K)[k0 >> 5]);
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const uint32_t w = c < 4 ? qq.x : qq.y;
+                    v[it][c] = (float)(int8_t)((w >> (8 * (c & 3))) & 0xff) * d;
+                }
+            }
+        } else {
+            const float4* xr = reinterpret_cast<const float4*>(a.x + (long)b * a.x_stride + k0);
+            const float4 x0 = xr[0], x1 = xr[1];
+            v[it][0] = x0.x, v[it][1] = x0.y, v[it][2] = x0.z, v[it][3] = x0.w;
+            v[it][4] = x1.x, v[it][5] = x1.y, v[it][6] = x1.z, v[it][7] = x1.w;
+        }
+        if (a.xadd) {
+            // x + (p_0 + … + p_{n-1}), the partials summed in order
+            float o[8];
+            const float* pa = a.xadd + (long)b * a.n_add * K + k0;
+#pragma unroll
+            for (int c = 0; c < 8; c++) o[c] = pa[c];
+            for (int p = 1; p < a.n_add; p++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) o[c] += pa[(long)p * K + c];
+#pragma unroll
+            for (int c = 0; c < 8; c++) v[it][c] += o[c];
+        }
+        if (a.x_out) {
+            float4* xo = reinterpret_cast<float4*>(a.x_out + (long)b * a.x_stride + k0);
+            xo[0] = make_float4(v[it][0], v[it][1], v[it][2], v[it][3]);
+            xo[1] = make_float4(v[it][4], v[it][5], v[it][6], v[it][7]);
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) ss = fmaf(v[it][c], v[it][c], ss);
+    }
+    float scale = 1.0f;
+    if (a.nw) {
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float tot = 0.0f;
+        for (int w = 0; w < XP_THREADS / 32; w++) tot += red[w];
+        scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+    }
+#pragma unroll
+    for (int it = 0; it < IT; it++) {
+        const int e = threadIdx.x + XP_THREADS * it, k0 = 8 * e;
+        if (k0 >= K) continue;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int c = 0; c < 8; c += 2) {
+            float y0 = v[it][c], y1 = v[it][c + 1];
+            if (a.nw && live) {
+                y0 = y0 * scale * a.nw[k0 + c];
+                y1 = y1 * scale * a.nw[k0 + c + 1];
+            }
+            const __half h0 = __float2half_rn(y0), h1 = __float2half_rn(y1);
+            const __half l0 = __float2half_rn(y0 - __half2float(h0)), l1 = __float2half_rn(y1 - __half2float(h1));
+            const __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+            hi[c >> 1] = *reinterpret_cast<const uint32_t*>(&hh);
+            lo[c >> 1] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+        *reinterpret_cast<uint4*>(xg + x16_offset(n, k0)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(xg + x16_offset(BG_SLOTS + n, k0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// ---- host ----------------------------------------------------------------------------------------------------------------
+bool bgemm_shape_ok(int rows, int cols) { return rows >= 1 && cols >= 256 && cols % 256 == 0 && cols <= 4096; }
+
+int bgemm_grid(int num_sms, int rows) { return std::max(1, std::min((rows + BG_M - 1) / BG_M, num_sms)); }
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* why) {
+    static std::mutex mu;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
+            if (why) *why = "the driver offers no cuTensorMapEncodeTiled";
+            cudaGetLastError();
+            return nullptr;
+        }
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+bool bgemm_maps(const QMat& w, BgMaps* m, std::string* why) {
+    if (!bgemm_shape_ok(w.rows, w.cols)) {
+        if (why) *why = "shape outside the tensor-core contraction";
+        return false;
+    }
+    auto enc = encode_fn(why);
+    if (!enc) return false;
+    const cuuint64_t strides[1] = {(cuuint64_t)w.stride};
+    const cuuint32_t estr[2] = {1, 1};
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)w.cols, (cuuint64_t)w.rows};
+        const cuuint32_t box[2] = {BG_KC, BG_M};
+        const CUresult r = enc(&m->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w.w), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            if (why) *why = "cuTensorMapEncodeTiled (quants) returned " + std::to_string((int)r);
+            return false;
+        }
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)(w.cols / 16), (cuuint64_t)w.rows};
+        const cuuint32_t box[2] = {(cuuint32_t)(w.cols / 16), BG_M};
+        const CUresult r = enc(&m->s, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w.w + w.cols), dims,
+                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            if (why) *why = "cuTensorMapEncodeTiled (scales) returned " + std::to_string((int)r);
+            return false;
+        }
+    }
+    return true;
+}
+
+static int bg_static_smem() {
+    static int bytes = -1;
+    if (bytes < 0) {
+        cudaFuncAttributes fa;
+        bytes = cudaFuncGetAttributes(&fa, k_bgemm) == cudaSuccess ? (int)fa.sharedSizeBytes : (int)sizeof(BgShared) + 64;
+    }
+    return bytes;
+}
+
+void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms, bool pdl) {
+    static PerDeviceOnce once;
+    once([] {
+        cudaFuncSetAttribute(k_bgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
+    });
+    const int K = a.w.cols;
+    const int sstride = (BG_M * (K / 16) + 1023) & ~1023;
+    const int fixed = BG_NA * (int)BG_ABUF + 2 * sstride + 1024;  // + the 1024-B alignment slack
+    const int ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
+    cfg.blockDim = dim3(BG_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)fixed + (size_t)ns * BG_STAGE;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.q, m.s, ns);
+}
+
+void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS * BG_SLOTS), 1, 1);
+    cfg.blockDim = dim3(XP_THREADS, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, k_xprep, a);
+}
+
+}  // namespace ocr

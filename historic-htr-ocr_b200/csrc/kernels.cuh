@@ -7,6 +7,8 @@
 // contiguous, 16-B aligned, 16-B multiple byte range: one bulk-async copy (cp.async.bulk) moves a stage of rows.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap: the copy engine's descriptors of the weight tiles (no driver library is linked)
+
 #include "common.cuh"
 
 namespace ocr {
@@ -199,6 +201,70 @@ int ffn_smem(int dim, int n_ff);
 bool ffn_usable(int dim, int n_ff);
 void launch_ffn(cudaStream_t st, const FfnArgs& a, bool pdl);
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx);
+
+// ---- the batched decode contraction on the tensor cores (k_bgemm.cu) -----------------------------------------------
+// For batches of slots the matvecs become skinny GEMMs Y[slot][row] = sum_k W[row][k] x[slot][k], run by tcgen05.mma
+// (kind::f16, f32 accumulators in tensor memory) on exact f16 splits of both operands: each weight q * d (exact in
+// f32) is the sum of two f16 values w_hi + w_lo, each activation x = x_hi + x_lo, and the MMAs accumulate
+// w_hi x_hi + w_hi x_lo + w_lo x_hi — the f32 matvec's result to within f32 rounding (the dropped w_lo x_lo term is
+// below 2^-22 of the product).
+//
+// The activation operand ("x16") of a group of BG_SLOTS slots over K columns is K/128 chunks of BG_CHUNK_BYTES:
+// rows n < 32 hold f16(x[slot n]) (hi), rows 32 + n hold f16(x - hi) (lo), for the chunk's 128 columns, in tcgen05's
+// K-major core-matrix order without swizzle — core (n / 8, (k % 128) / 8) is 128 contiguous bytes, 8 rows of 8
+// halves — so one bulk copy of a chunk is an MMA operand as it lands.
+constexpr int BG_SLOTS = 32;
+constexpr uint32_t BG_CHUNK_BYTES = 16384;
+__host__ __device__ constexpr size_t x16_offset(int n, int k) {
+    return (size_t)(k >> 7) * BG_CHUNK_BYTES + (size_t)((((n >> 3) << 4) + ((k & 127) >> 3)) << 7) +
+           (size_t)((n & 7) << 4) + (size_t)((k & 7) << 1);
+}
+__host__ __device__ constexpr size_t x16_group_bytes(int K) { return (size_t)(K / 128) * BG_CHUNK_BYTES; }
+
+// the copy engine's view of a weight matrix in the row layout: its quants as 128 x 128-byte tiles (128-B swizzle)
+// and one 128-row tile's block scales
+struct BgMaps {
+    CUtensorMap q, s;
+};
+struct BgArgs {
+    QMat w;
+    const uint8_t* x16 = nullptr;  // [groups][K/128] chunks (the slots' activations, hi / lo)
+    int mode = MV_STORE;           // MV_STORE, MV_ADD, MV_SWIGLU (rows interleaved gate, up), MV_LMHEAD
+    float* y = nullptr;            // [B][y_stride] (SwiGLU: [B][rows/2]; LM head: raw logits [B][rows], may be null)
+    int y_stride = 0;
+    uint8_t* y16 = nullptr;        // SwiGLU: the result also as the next contraction's operand (x16 over rows/2)
+    int nb = 1;                    // slots (blockIdx.y takes groups of BG_SLOTS)
+    const int32_t* active = nullptr;
+    LmArgs lm;                     // MV_LMHEAD: the choice (lm.nb = nb, partials [nb][grid])
+    int* err = nullptr;
+};
+// true when the tensor-core contraction takes this shape (cols a multiple of 256, at most 4096)
+bool bgemm_shape_ok(int rows, int cols);
+// the two tensor maps of a matrix (false + *why when the driver refuses them)
+bool bgemm_maps(const QMat& w, BgMaps* m, std::string* why);
+// CTAs of a launch: one per 128-row tile, at most one per SM (a persistent CTA takes tiles blockIdx.x + k * grid)
+int bgemm_grid(int num_sms, int rows);
+void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms, bool pdl);
+
+// The activations of a batch as the contraction's operand: per slot x (+ the partial products in order, or the token's
+// embedding row), written back to x_out when set, RMS-normalised by nw when set, split hi / lo into x16. Slots past
+// nb or idle get zeros.
+struct PrepArgs {
+    const float* x = nullptr;  // [B][x_stride]
+    int x_stride = 0;
+    const float* xadd = nullptr;  // [B][n_add][K] (summed in order, then added to x)
+    int n_add = 0;
+    const int32_t* tok = nullptr;  // layer 0: x = token_embd[tok[b]] dequantized
+    QMat emb;
+    float* x_out = nullptr;  // may alias x (each slot's row is read, then written, by one CTA)
+    const float* nw = nullptr;
+    float eps = 1e-6f;
+    int K = 0, nb = 1;
+    const int32_t* active = nullptr;
+    uint8_t* x16 = nullptr;
+    int* err = nullptr;
+};
+void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl);
 
 // ---- prefill (k_prefill.cu) -------------------------------------------------------------------------------------------
 void launch_embed_rows(cudaStream_t st, const int32_t* ids, int n, QMat emb, float* x);

@@ -107,6 +107,7 @@ struct LayerW {
     float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
     uint8_t* o_s = nullptr;  // W_o cut per kv head (launch_slice_o), derived on the device after the load
     uint8_t* d_s = nullptr;  // W_down cut into FFN_NCLU h slices (the fused FFN), when the shape fits it
+    BgMaps bq_qkv, bq_gu, bq_down;  // the tensor-core contraction's views of qkv, gate|up and down (model tc)
 };
 
 struct ocr_model {
@@ -118,6 +119,8 @@ struct ocr_model {
     std::vector<LayerW> layers;
     QMat tok;
     float* out_norm = nullptr;
+    bool tc = false;  // the batched contractions can run on the tensor cores (shapes fit, tensor maps made)
+    BgMaps bq_tok;
 };
 
 namespace {
@@ -237,6 +240,17 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
     }
     m->tok = qmat(m->mem, L.tok);
     m->out_norm = (float*)((char*)m->mem + L.out_norm);
+    // the tensor maps of the batched contractions (they hold the matrices' addresses; the bytes come later)
+    const char* tc_env = getenv("OCR_TC");
+    m->tc = !(tc_env && tc_env[0] == '0') && bgemm_shape_ok(c.n_vocab, c.dim) && bgemm_shape_ok(2 * c.n_ff, c.dim) &&
+            bgemm_shape_ok(c.dim, c.n_ff) && bgemm_shape_ok(c.n_head * c.d_head + 2 * c.n_kv * c.d_head, c.dim);
+    std::string why;
+    for (auto& w : m->layers) {
+        if (!m->tc) break;
+        m->tc = bgemm_maps(w.qkv, &w.bq_qkv, &why) && bgemm_maps(w.gu, &w.bq_gu, &why) &&
+                bgemm_maps(w.down, &w.bq_down, &why);
+    }
+    if (m->tc) m->tc = bgemm_maps(m->tok, &m->bq_tok, &why);
     *out = m;
     return OCR_OK;
 }
@@ -463,6 +477,9 @@ struct ocr_session {
     float* x2 = nullptr;     // the second residual buffer of the fused layer
     float* opart = nullptr;  // [B][n_kv][dim] the attention clusters' o-projection partials (null: unfused layer)
     float* dpart = nullptr;  // [FFN_NCLU][dim] the fused FFN's down partials (one slot)
+    bool tc = false;            // batched contractions on the tensor cores (more than 8 slots)
+    uint8_t* x16a = nullptr;    // [groups] operands of width dim (x16 layout)
+    uint8_t* x16g = nullptr;    // [groups] operands of width n_ff (the SwiGLU output)
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -510,10 +527,124 @@ struct Prof {
 
 double mat_bytes(const QMat& w) { return (double)w.rows * w.stride; }
 
+LmArgs sampler_args(ocr_session* s, const ocr_sampler_cfg* cfg);
+
+// One decode step of a batch of more than 8 slots, its contractions on the tensor cores (k_bgemm.cu). Per layer:
+// the slots' residual rows (layer 0: their tokens' embedding rows) RMS-normalised into the operand (prep), the qkv
+// contraction, the attention with its fused o-projection (per-kv-head partial products), the FFN's operand prep
+// (residual + the partials in order, written back, normalised), the gate|up contraction whose SwiGLU epilogue writes
+// the down contraction's operand, and the down contraction adding onto the residual. Then the LM head's prep and its
+// contraction with the windowed penalty and the choice.
+void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof,
+                    bool x_given) {
+    const ocr_model* m = s->m;
+    const auto& c = m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    const bool pdl = ctx->pdl && !prof;
+    const double nact = prof ? (double)prof->pos.size() : 0.0;
+    auto prep = [&](int layer, const float* nw, const float* xadd, int n_add, bool embed, bool chain) {
+        PrepArgs p;
+        p.x = s->x;
+        p.x_stride = c.dim;
+        p.xadd = xadd;
+        p.n_add = n_add;
+        if (embed) {
+            p.tok = s->tok;
+            p.emb = m->tok;
+        }
+        p.x_out = (embed || xadd) ? s->x : nullptr;
+        p.nw = nw;
+        p.eps = c.eps;
+        p.K = c.dim;
+        p.nb = s->B;
+        p.active = s->active;
+        p.x16 = s->x16a;
+        p.err = ctx->d_err;
+        launch_xprep(st, p, chain);
+        if (prof)
+            prof->mark(embed ? "prep (embed, norm, hi/lo)" : xadd ? "prep (sum, norm, hi/lo)" : "prep (norm, hi/lo)",
+                       layer, nact * c.dim * (8.0 + 4.0 * n_add + (xadd ? 4.0 : 0.0)));
+    };
+    auto gemm = [&](const QMat& w, const BgMaps& bq, const uint8_t* x16, int mode, float* y, int y_stride,
+                    uint8_t* y16) {
+        BgArgs g;
+        g.w = w;
+        g.x16 = x16;
+        g.mode = mode;
+        g.y = y;
+        g.y_stride = y_stride;
+        g.y16 = y16;
+        g.nb = s->B;
+        g.active = s->active;
+        g.err = ctx->d_err;
+        return g;
+    };
+    for (int l = 0; l < c.n_layer; l++) {
+        const LayerW& L = m->layers[l];
+        prep(l, L.attn_norm, nullptr, 0, l == 0 && !x_given, pdl && l > 0);
+        launch_bgemm(st, gemm(L.qkv, L.bq_qkv, s->x16a, MV_STORE, s->qkv, s->qkv_w, nullptr), L.bq_qkv, ctx->num_sms,
+                     pdl);
+        if (prof) prof->mark("qkv (tcgen05)", l, mat_bytes(L.qkv) + nact * (c.dim * 4.0 + s->qkv_w * 4.0));
+        AttnArgs a;
+        a.qkv = s->qkv;
+        a.qkv_stride = s->qkv_w;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.rope = s->rope;
+        a.kc = s->kcl(l);
+        a.vc = s->vcl(l);
+        a.pos = s->pos;
+        a.active = s->active;
+        a.n_head = c.n_head;
+        a.n_kv = c.n_kv;
+        a.n_ctx = s->n_ctx;
+        a.splits = s->splits;
+        a.eps = c.eps;
+        a.scale = 1.0f / sqrtf((float)c.d_head);
+        a.out = s->attn;
+        a.out_stride = s->qd;
+        a.nb = s->B;
+        a.err = ctx->d_err;
+        a.wo = L.o_s;
+        a.dim = c.dim;
+        a.opart = s->opart;
+        launch_attention_decode(st, a, pdl);
+        if (prof) {
+            double kv = 0;
+            for (int p : prof->pos) kv += (double)(p + 1) * c.n_kv * 128 * 2 * 2;
+            prof->mark("attention + o-proj", l,
+                       kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
+                           nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
+        }
+        prep(l, L.ffn_norm, s->opart, c.n_kv, false, pdl);
+        launch_bgemm(st, gemm(L.gu, L.bq_gu, s->x16a, MV_SWIGLU, nullptr, 0, s->x16g), L.bq_gu, ctx->num_sms, pdl);
+        if (prof) prof->mark("gate|up + swiglu (tcgen05)", l, mat_bytes(L.gu) + nact * (c.dim * 4.0 + c.n_ff * 4.0));
+        launch_bgemm(st, gemm(L.down, L.bq_down, s->x16g, MV_ADD, s->x, c.dim, nullptr), L.bq_down, ctx->num_sms, pdl);
+        if (prof) prof->mark("down + residual (tcgen05)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
+    }
+    prep(-1, m->out_norm, nullptr, 0, false, pdl);
+    BgArgs h = gemm(m->tok, m->bq_tok, s->x16a, MV_LMHEAD, s->logits, c.n_vocab, nullptr);
+    ocr_sampler_cfg sc{rp, window, fp, 1};
+    h.lm = sampler_args(s, &sc);
+    h.lm.sample = sample ? 1 : 0;
+    h.lm.use_fp = use_fp;
+    h.lm.advance_pos = sample ? 1 : 0;
+    h.lm.nb = s->B;
+    launch_bgemm(st, h, m->bq_tok, ctx->num_sms, pdl);
+    if (prof)
+        prof->mark(sample ? "lm head + choice (tcgen05)" : "lm head (tcgen05)", -1,
+                   mat_bytes(m->tok) + nact * (c.dim * 4.0 + c.n_vocab * 4.0));
+}
+
 // one decode step of every active slot: 5 kernels per layer + the LM head (with the choice when sample). The first
 // layer embeds the slots' tokens, or with x_given takes the rows already in s->x (Input::Embeddings rows).
 void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof = nullptr,
                  bool x_given = false) {
+    if (s->tc) {
+        record_step_tc(s, sample, rp, window, use_fp, fp, prof, x_given);
+        return;
+    }
     const ocr_model* m = s->m;
     const auto& c = m->cfg;
     ocr_ctx* ctx = s->ctx;
@@ -1189,7 +1320,8 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     cudaError_t e = dalloc((void**)&s->kc, s->kv_bytes, &ctx->mem_kv);
     if (e == cudaSuccess) e = dalloc((void**)&s->vc, s->kv_bytes, &ctx->mem_kv);
     // work: rope, x, qkv, attn, g, logits, partials, counters, state
-    const int lm_grid = std::max(lm_head_grid(ctx->num_sms, c.n_vocab, c.dim), sample_grid(ctx->num_sms));
+    const int lm_grid = std::max(std::max(lm_head_grid(ctx->num_sms, c.n_vocab, c.dim), sample_grid(ctx->num_sms)),
+                                 bgemm_grid(ctx->num_sms, c.n_vocab));
     Planner p;
     const size_t o_rope = p.take((size_t)n_ctx * c.d_head * 4);
     const size_t o_x = p.take((size_t)batch * c.dim * 4);
@@ -1199,6 +1331,12 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_opart = fuse ? p.take((size_t)batch * c.n_kv * c.dim * 4) : 0;
     const bool fuse_ffn = fuse && batch == 1 && m->layers[0].d_s != nullptr;
     const size_t o_dpart = fuse_ffn ? p.take((size_t)FFN_NCLU * c.dim * 4) : 0;
+    // batches of more than 8 slots run their contractions on the tensor cores (with the o-projection fused into the
+    // attention, whose per-head partials the FFN's operand preparation sums)
+    const bool tc = m->tc && fuse && batch > 8;
+    const size_t groups = (size_t)(batch + BG_SLOTS - 1) / BG_SLOTS;
+    const size_t o_x16a = tc ? p.take(groups * x16_group_bytes(c.dim)) : 0;
+    const size_t o_x16g = tc ? p.take(groups * x16_group_bytes(c.n_ff)) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
@@ -1220,6 +1358,11 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         s->opart = (float*)(w + o_opart);
     }
     if (fuse_ffn) s->dpart = (float*)(w + o_dpart);
+    if (tc) {
+        s->tc = true;
+        s->x16a = (uint8_t*)(w + o_x16a);
+        s->x16g = (uint8_t*)(w + o_x16g);
+    }
     s->qkv = (float*)(w + o_qkv);
     s->attn = (float*)(w + o_attn);
     s->g = (float*)(w + o_g);
@@ -1559,9 +1702,43 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int co
     if (!ctx || !d_w || !d_x || !d_y) return fail(OCR_ERR_ARG, "null argument");
     if (rows < 1 || cols < 32 || cols % 32 || nb < 1) return fail(OCR_ERR_ARG, "bad shape");
     if ((uintptr_t)d_w & 15) return fail(OCR_ERR_ARG, "the rows must start 16-B aligned");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    if (nb > 8 && bgemm_shape_ok(rows, cols)) {
+        // a batch: the tensor-core contraction (operand prep, then k_bgemm) — the decode step's batched path
+        QMat w;
+        w.w = d_w;
+        w.rows = rows;
+        w.cols = cols;
+        w.stride = q8_stride(cols);
+        BgMaps maps;
+        std::string why;
+        if (!bgemm_maps(w, &maps, &why)) return fail(OCR_ERR_CUDA, why);
+        const size_t groups = (size_t)(nb + BG_SLOTS - 1) / BG_SLOTS;
+        OCR_TRY(ensure_op_scratch(ctx, groups * x16_group_bytes(cols)));
+        PrepArgs p;
+        p.x = d_x;
+        p.x_stride = cols;
+        p.nw = d_norm_w;
+        p.eps = eps;
+        p.K = cols;
+        p.nb = nb;
+        p.x16 = (uint8_t*)ctx->op_scratch;
+        p.err = ctx->d_err;
+        launch_xprep(ctx->stream, p, false);
+        BgArgs g;
+        g.w = w;
+        g.x16 = (const uint8_t*)ctx->op_scratch;
+        g.mode = accumulate ? MV_ADD : MV_STORE;
+        g.y = d_y;
+        g.y_stride = rows;
+        g.nb = nb;
+        g.err = ctx->d_err;
+        launch_bgemm(ctx->stream, g, maps, ctx->num_sms, false);
+        OCR_CUDA(cudaGetLastError());
+        return OCR_OK;
+    }
     if ((size_t)((cols + 511) / 512) * 512 * 4 * std::min(nb, 8) > 96 * 1024)
         return fail(OCR_ERR_ARG, "nb x cols too large for the staged activations");
-    OCR_CUDA(cudaSetDevice(ctx->device));
     MvArgs a;
     a.w.w = d_w;
     a.w.rows = rows;

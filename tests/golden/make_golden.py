@@ -2,6 +2,7 @@
 
     python tests/golden/make_golden.py penalty --reference-root DIR     → penalty_ref.json
     python tests/golden/make_golden.py config2                          → config2_greedy.json
+    python tests/golden/make_golden.py config3                          → config3_greedy.json
 
 penalty: the reference's own windowed repetition penalty — hf/window_rep_penalty.py's WindowRepetitionPenalty.apply
 (b-straub/historic-htr-ocr, hf/window_rep_penalty.py:65-86) — run on torch CPU float32 logits. vllm is not installed,
@@ -13,6 +14,10 @@ config2: the CPU oracle's greedy decode of BASELINE config 2 (28 layers, dim 102
 151936; q8_0 weights sigma 0.02 from the model seed; a 2048-row N(0,1) embedding prefix; 512 tokens with rp 1.15 over
 a 64-token window seeded with 64 x <|image_pad|> = 151655). The fixture holds the ids and each step's top-2 margin, so
 the GPU test needs no oracle run on the GPU host.
+
+config3: the same oracle decode for slots 0 and 31 of BASELINE config 3 (32 sequences on the config-2 decoder; slot
+b's prefix is 3072 rows of gauss(substream(seed + b, 200000)); 1024 tokens each, rp 1.15, window 64 seeded with 64 x
+<|image_pad|>): the batched GPU path's ids for those slots must equal them.
 """
 from __future__ import annotations
 
@@ -142,9 +147,47 @@ def make_config2() -> dict:
                 oracle_seconds=dict(prefill=round(t1 - t0, 1), decode=round(t2 - t1, 1)), threads=O.num_threads())
 
 
+# 32 sequences on the config-2 decoder, each a 3072-row prefix and 1024 greedy tokens.
+# The oracle decodes a subset of the slots at full length; the GPU test runs the whole batch and compares those.
+CONFIG3_SLOTS = (0, 31)
+CONFIG3_PREFIX, CONFIG3_NEW = 3072, 1024
+
+
+def config3_inputs(slot: int):
+    """(model seed, slot's prefix rows, history): slot b's prefix is gauss(substream(seed + b, 200000)) rows"""
+    seed = P.SEED_BASE + 2
+    prefix = P.gauss(P.substream(seed + slot, 200000), CONFIG3_PREFIX * 1024, 1.0).reshape(CONFIG3_PREFIX, 1024)
+    return seed, prefix, [IMAGE_PAD] * 64
+
+
+def make_config3() -> dict:
+    import oracle as O
+
+    seed = P.SEED_BASE + 2
+    m = O.Model(CONFIG2, seed=seed, sigma_w=0.02, sigma_e=0.02)
+    slots = {}
+    for b in CONFIG3_SLOTS:
+        _, prefix, history = config3_inputs(b)
+        t0 = time.time()
+        s = m.session(CONFIG3_PREFIX + CONFIG3_NEW)
+        first = s.prefill(None, prefix, CONFIG3_PREFIX)
+        t1 = time.time()
+        ids, margins = s.decode(first, 1.15, 64, 0.0, history, CONFIG3_NEW)
+        t2 = time.time()
+        order = np.argsort(-first, kind="stable")[:8]
+        slots[str(b)] = dict(ids=ids.tolist(), margins=[float(x) for x in margins], first_top8=order.tolist(),
+                             first_top8_logits=[float(first[k]) for k in order],
+                             first_max_abs=float(np.abs(first).max()),
+                             oracle_seconds=dict(prefill=round(t1 - t0, 1), decode=round(t2 - t1, 1)))
+        print("slot", b, "done", round(t2 - t0, 1), "s", flush=True)
+    return dict(config=CONFIG2, seed=seed, sigma_w=0.02, sigma_e=0.02, batch=32, prefix_rows=CONFIG3_PREFIX,
+                prefix="slot b: gauss(substream(seed + b, 200000), 3072*1024, 1.0)", history=[IMAGE_PAD] * 64,
+                rp=1.15, window=64, max_new=CONFIG3_NEW, slots=slots, threads=O.num_threads())
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["penalty", "config2"])
+    ap.add_argument("what", choices=["penalty", "config2", "config3"])
     ap.add_argument("--reference-root", default=os.environ.get("OCR_REFERENCE_ROOT"),
                     help="the reference checkout (or OCR_REFERENCE_ROOT); needed for `penalty` only")
     a = ap.parse_args()
@@ -153,7 +196,10 @@ if __name__ == "__main__":
             ap.error("penalty needs --reference-root DIR (or OCR_REFERENCE_ROOT): the reference's hf/ directory")
         out = make_penalty(Path(a.reference_root))
         (HERE / "penalty_ref.json").write_text(json.dumps(out, indent=1))
-    else:
+    elif a.what == "config2":
         out = make_config2()
         (HERE / "config2_greedy.json").write_text(json.dumps(out))
+    else:
+        out = make_config3()
+        (HERE / "config3_greedy.json").write_text(json.dumps(out))
     print("ok", a.what)

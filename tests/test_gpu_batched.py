@@ -1,0 +1,126 @@
+"""The batched decode path on the tensor cores (tcgen05) through the C ABI, against the CPU oracle.
+
+Batches of more than 8 slots run their contractions (qkv, gate|up + SwiGLU, down + residual, the LM head + choice) as
+skinny GEMMs on the tensor cores with f16 hi / lo splits of both operands (k_bgemm.cu). Checked here:
+- ocr_op_matvec_q8_0 with nb > 8 (the same contraction with a plain store or residual add) against the oracle's
+  matvec: within 1e-5 of sum |w x| per output, the CUDA-core matvec's bound (q8_0_matvec_and_matmul_match_cpu_dequant,
+  app/crates/ocr-wgpu/src/text.rs:706-741) — partial 128-row tiles, two slot groups, K from 256 to 4096;
+- whole decode steps of batches of 12 and 33 slots on a small qwen3-shaped model: prefill logits, per-step logits
+  within the acceptance bound (2e-3 of max |logit|, relative L2 1e-3), and greedy ids equal to the oracle's and to the
+  same slots decoded one at a time (the CUDA-core path).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from test_gpu_decode import close_logits, text_config
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, a):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    torch.cuda.synchronize()
+    return t
+
+
+def host(torch, t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("rows,cols,nb,norm,acc", [
+    (512, 1024, 32, False, True), (4096, 1024, 32, True, False), (6144, 1024, 20, True, False),
+    (1024, 3072, 32, False, True), (1000, 2048, 33, True, True), (300, 4096, 9, False, False),
+    (130, 256, 16, True, False), (20011, 1024, 32, True, False),
+])
+def test_tensor_core_matvec_matches_oracle(ocr, orc, ctx, torch_cuda, rows, cols, nb, norm, acc):
+    torch = torch_cuda
+    w = orc.synth_q8_0(rows * cols, 91 + rows + cols, 0.02)
+    wd = dev(torch, ocr.q8_rows_from_blocks(w, rows, cols))
+    x = ocr.gauss(15 + nb, nb * cols, 1.0).reshape(nb, cols)
+    x[:, ::17] *= 40.0  # a spread of magnitudes, so the hi / lo split of the activations matters
+    nw = (1.0 + 0.1 * ocr.gauss(16, cols)).astype(np.float32)
+    base = ocr.gauss(17, nb * rows, 1.0).reshape(nb, rows)
+    xd, nwd, yd = dev(torch, x), dev(torch, nw), dev(torch, base.copy())
+    ocr.op_matvec_q8_0(ctx, wd.data_ptr(), rows, cols, xd.data_ptr(), nwd.data_ptr() if norm else None, 1e-6, nb,
+                       yd.data_ptr(), acc)
+    ctx.sync()
+    got = host(torch, yd)
+    xn = np.stack([r * np.float32(orc.rms_scale(r, 1e-6)) * nw for r in x]).astype(np.float32) if norm else x
+    deq = orc.dequantize_q8_0(w, rows * cols).reshape(rows, cols).astype(np.float64)
+    worst = 0.0
+    for b in range(nb):
+        want = orc.matvec_q8_0(w, rows, cols, xn[b], base[b] if acc else None)
+        absdot = np.abs(deq) @ np.abs(xn[b].astype(np.float64))
+        err = np.abs(got[b].astype(np.float64) - want)
+        bound = 1e-5 * absdot + 1e-6 + (np.abs(base[b]) * 1e-7 if acc else 0)
+        assert (err <= bound).all(), (b, float((err / bound).max()))
+        worst = max(worst, float((err / (absdot + 1e-30)).max()))
+    print(f"worst |err| / sum|w x| = {worst:.2e}")
+
+
+BATCH_CFG = dict(n_layer=3, dim=256, n_head=16, n_kv=8, d_head=128, n_ff=512, n_vocab=1000, eps=1e-6, rope_base=1e6)
+
+
+@pytest.mark.parametrize("B", [12, 33])
+def test_tensor_core_batch_decode_matches_oracle(ocr, orc, ctx, B):
+    """B slots of a 3-layer model (16/8 heads, dim 256, ffn 512): each slot's prompt prefilled, then (a) four CPU-choice
+    steps of the whole batch — every slot's logits against the oracle's — and (b) the device-choice batched decode,
+    whose ids must equal the oracle's greedy ids and those of the slots decoded one at a time"""
+    cfg = BATCH_CFG
+    n_new, n_steps = 20, 4
+    om = orc.Model(cfg, seed=47, sigma_w=0.2, sigma_e=1.0)
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
+    prompts = [[int(t) for t in orc.fill_ids(60 + b, 8 + b % 5, cfg["n_vocab"])] for b in range(B)]
+    n_ctx = 64
+    # (a) the CPU-choice steps
+    sa = gm.session(n_ctx, batch=B)
+    osns, los = [], []
+    for b, prompt in enumerate(prompts):
+        lg = sa.prefill(b, ids=prompt)
+        os_ = om.session(n_ctx)
+        lo = os_.prefill(prompt, None, len(prompt))
+        close_logits(lg, lo)
+        osns.append(os_)
+        los.append(lo)
+    for _ in range(n_steps):
+        toks = [int(np.argmax(lo)) for lo in los]
+        lgs = sa.step(toks)
+        for b in range(B):
+            los[b] = osns[b].step(toks[b])
+            close_logits(lgs[b], los[b])
+    # (b) the device choice for the whole batch from the prompts' logits
+    sb = gm.session(n_ctx, batch=B)
+    wants = []
+    for b, prompt in enumerate(prompts):
+        sb.prefill(b, ids=prompt, logits=False)
+        os_ = om.session(n_ctx)
+        lo = os_.prefill(prompt, None, len(prompt))
+        wants.append(os_.decode(lo, 1.1, 8, 0.0, prompt[-8:], n_new)[0].tolist())
+    hist = np.array([p[-8:] for p in prompts], np.int32)
+    got = sb.decode_batch(ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, n_new), hist)
+    single = gm.session(n_ctx, batch=1)
+    for b in range(B):
+        assert got[b].tolist() == wants[b], (b, got[b].tolist(), wants[b])
+        if b % 8 == 0:
+            single.rewind(0, 0)
+            single.prefill(0, ids=prompts[b], logits=False)
+            assert single.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, n_new), hist[b]) == wants[b], b
+
+
+def test_tensor_core_profile_step(ocr, orc, ctx):
+    """the profiler sees the batched step's kernels: per layer prep, qkv, attention, prep, gate|up, down; then the LM
+    head's prep and contraction"""
+    cfg = BATCH_CFG
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
+    s = gm.session(32, batch=16)
+    for b in range(16):
+        s.prefill(b, ids=[1 + b, 2, 3, 4, 5], logits=False)
+    rec = s.profile_step([7] * 16)
+    names = [r["name"] for r in rec]
+    assert names[:6] == ["prep (embed, norm, hi/lo)", "qkv (tcgen05)", "attention + o-proj", "prep (sum, norm, hi/lo)",
+                         "gate|up + swiglu (tcgen05)", "down + residual (tcgen05)"], names[:6]
+    assert names[-2:] == ["prep (norm, hi/lo)", "lm head (tcgen05)"]
+    assert len(rec) == 6 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
