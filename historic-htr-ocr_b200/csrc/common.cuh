@@ -162,9 +162,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, ui
 
 // a bounded wait: gives up after MBAR_TRIES polls of at most 100 µs each (≈ 2 s), flags DEV_TIMEOUT, returns false
 constexpr uint32_t MBAR_TRIES = 20000;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-    for (uint32_t i = 0; i < MBAR_TRIES; i++)
-        if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, uint32_t tries = MBAR_TRIES,
+                                          uint32_t hint_ns = 100000) {
+    for (uint32_t i = 0; i < tries; i++)
+        if (mbar_try_wait(bar, parity, hint_ns)) return true;
     dev_error(err, DEV_TIMEOUT);
     return false;
 }

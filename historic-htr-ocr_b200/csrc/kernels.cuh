@@ -266,6 +266,10 @@ struct PrepArgs {
 };
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl);
 
+// ---- the bounded-wait test hook (k_probe.cu) ----
+// one mbarrier wait that cannot complete, limited to `tries` polls of ~1 µs: *waited_out = 1 and DEV_TIMEOUT flagged
+void launch_wait_probe(cudaStream_t st, int* err, uint32_t tries, int* waited_out);
+
 // ---- prefill (k_prefill.cu) -------------------------------------------------------------------------------------------
 void launch_embed_rows(cudaStream_t st, const int32_t* ids, int n, QMat emb, float* x);
 void launch_rmsnorm_rows(cudaStream_t st, const float* x, const float* w, float* y, int rows, int dim, float eps);

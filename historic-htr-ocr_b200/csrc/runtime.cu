@@ -91,8 +91,9 @@ ocr_status check_device_error(ocr_ctx* ctx) {
     OCR_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err != DEV_OK) {
         OCR_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
-        return fail(OCR_ERR_DEVICE, err == DEV_BAD_POS ? "a kernel saw a position outside the KV cache"
-                                                       : "a kernel saw an index outside its buffer");
+        return fail(OCR_ERR_DEVICE, err == DEV_BAD_POS     ? "a kernel saw a position outside the KV cache"
+                                    : err == DEV_TIMEOUT ? "a kernel's bounded wait ran out (its work was skipped)"
+                                                         : "a kernel saw an index outside its buffer");
     }
     return OCR_OK;
 }
@@ -1980,6 +1981,20 @@ ocr_status ocr_gguf_text_config(const ocr_gguf* h, ocr_text_cfg* out) {
     OCR_TRY(validate_gguf(h->g, c));
     *out = c;
     return OCR_OK;
+}
+
+ocr_status ocr_op_wait_probe(ocr_ctx* ctx, int tries, int* waited_out) {
+    if (!ctx || !waited_out) return fail(OCR_ERR_ARG, "null argument");
+    if (tries < 1 || tries > 100000) return fail(OCR_ERR_ARG, "tries must be in [1, 100000]");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    OCR_TRY(ensure_op_scratch(ctx, 256));
+    int* d_out = (int*)ctx->op_scratch;
+    OCR_CUDA(cudaMemsetAsync(d_out, 0, 4, ctx->stream));
+    launch_wait_probe(ctx->stream, ctx->d_err, (uint32_t)tries, d_out);
+    OCR_CUDA(cudaGetLastError());
+    OCR_CUDA(cudaMemcpyAsync(waited_out, d_out, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    OCR_CUDA(cudaStreamSynchronize(ctx->stream));
+    return OCR_OK;  // the device error flag stays set: ocr_ctx_sync reports (and clears) it
 }
 
 ocr_status ocr_op_penalize(ocr_ctx* ctx, float* d_logits, int n_vocab, float rp, int window, const int32_t* d_hist,

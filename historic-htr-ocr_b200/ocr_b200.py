@@ -97,6 +97,7 @@ _SIGS = {
                                         _P]),
     "ocr_op_lm_head_sample_noalloc": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P,
                                                 _P, _P, _P]),
+    "ocr_op_wait_probe": (C.c_int, [_P, C.c_int, C.POINTER(C.c_int)]),
     "ocr_op_attention_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                           _P]),
 }
@@ -485,6 +486,14 @@ def op_lm_head_sample_noalloc(ctx: Context, d_w: int, n_vocab: int, dim: int, d_
     """op_lm_head_sample with its scratch in a static device array: the call allocates no device memory"""
     _check(lib().ocr_op_lm_head_sample_noalloc(ctx.h, d_w, n_vocab, dim, d_x, d_norm_w, eps, rp, window, d_hist, d_len,
                                                d_tok, d_logits))
+
+
+def op_wait_probe(ctx: Context, tries: int) -> bool:
+    """runs one device wait that cannot complete, limited to `tries` polls; True when it gave up (the context's error
+    flag is then set: the next ctx.sync() raises OcrError with OCR_ERR_DEVICE)"""
+    out = C.c_int(0)
+    _check(lib().ocr_op_wait_probe(ctx.h, tries, C.byref(out)))
+    return bool(out.value)
 
 
 def op_attention_decode(ctx: Context, d_qkv: int, d_q_norm: int, d_k_norm: int, d_rope: int, d_k: int, d_v: int,

@@ -200,6 +200,13 @@ ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_
                                    const float* d_rope, uint16_t* d_k_cache, uint16_t* d_v_cache, int n_head, int n_kv,
                                    int n_ctx, int pos, float eps, float* d_out);
 
+/* Test hook for the device's bounded waits (the reference's Health rule, app/crates/ocr-wgpu/src/gpu.rs:901-970: a
+ * device failure becomes an error, not a hang). Every kernel waits on mbarriers for at most a fixed number of polls,
+ * then flags an error and skips the work. This runs one such wait that cannot complete, limited to `tries` polls of
+ * about 1 µs: *waited_out = 1 when it gave up. The context's error flag stays set — the next ocr_ctx_sync returns
+ * OCR_ERR_DEVICE and clears it; the context stays usable. Synchronous. */
+ocr_status ocr_op_wait_probe(ocr_ctx* ctx, int tries, int* waited_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -269,3 +269,27 @@ def test_attention_decode_matches_oracle(ocr, orc, ctx, torch_cuda, n_head, n_kv
                                 pos + 1, D, 1.0 / np.sqrt(128.0)) for h in range(n_head)])
     rel = np.linalg.norm(got - want) / np.linalg.norm(want)
     assert rel < 1e-5, rel
+
+
+def test_bounded_wait_runs_out_and_context_recovers(ocr, orc, torch_cuda):
+    """a device wait that cannot complete gives up after its limit (no hang, no fault): the kernel reports it, the host
+    sees OCR_ERR_DEVICE once, and the same context then runs normal work (the reference's Health rule: a device
+    failure is an error, app/crates/ocr-wgpu/src/gpu.rs:901-970)"""
+    torch = torch_cuda
+    c = ocr.Context(0)
+    try:
+        assert ocr.op_wait_probe(c, 50) is True
+        with pytest.raises(ocr.OcrError, match="bounded wait") as e:
+            c.sync()
+        assert e.value.code == 6
+        c.sync()  # the flag was cleared with the report
+        w = orc.synth_q8_0(64 * 256, 3, 0.02)
+        wd = dev(torch, ocr.q8_rows_from_blocks(w, 64, 256))
+        x = ocr.gauss(4, 256, 1.0)
+        xd, yd = dev(torch, x), torch.zeros(64, device="cuda")
+        ocr.op_matvec_q8_0(c, wd.data_ptr(), 64, 256, xd.data_ptr(), None, 1e-6, 1, yd.data_ptr(), False)
+        c.sync()
+        want = orc.matvec_q8_0(w, 64, 256, x, None)
+        assert np.allclose(host(torch, yd), want, rtol=0, atol=1e-4)
+    finally:
+        c.close()
