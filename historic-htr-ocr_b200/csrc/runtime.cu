@@ -1428,6 +1428,27 @@ ocr_status ocr_session_rewind(ocr_session* s, int slot, int n_past) {
     return OCR_OK;
 }
 
+ocr_status ocr_session_kv(const ocr_session* s, int layer, int slot, int row0, int n_rows, uint16_t* k_out,
+                          uint16_t* v_out) {
+    if (!s || !k_out || !v_out) return fail(OCR_ERR_ARG, "null argument");
+    const auto& c = s->m->cfg;
+    if (layer < 0 || layer >= c.n_layer || slot < 0 || slot >= s->B) return fail(OCR_ERR_ARG, "layer or slot out of range");
+    if (row0 < 0 || n_rows < 0 || row0 + n_rows > s->n_ctx) return fail(OCR_ERR_ARG, "rows outside the cache");
+    if (!n_rows) return OCR_OK;
+    OCR_CUDA(cudaSetDevice(s->ctx->device));
+    OCR_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    const size_t row_bytes = (size_t)c.n_kv * 128 * 2;
+    for (int j = 0; j < c.n_kv; j++) {
+        // the device's [slot][kv head][n_ctx][128] rows of head j → columns j*128 … of the host rows
+        const size_t src = (((size_t)slot * c.n_kv + j) * s->n_ctx + row0) * 128;
+        OCR_CUDA(cudaMemcpy2D(k_out + (size_t)j * 128, row_bytes, s->kcl(layer) + src, 256, 256, n_rows,
+                              cudaMemcpyDeviceToHost));
+        OCR_CUDA(cudaMemcpy2D(v_out + (size_t)j * 128, row_bytes, s->vcl(layer) + src, 256, 256, n_rows,
+                              cudaMemcpyDeviceToHost));
+    }
+    return OCR_OK;
+}
+
 // A few rows (a prompt's tail, the bench's re-run of the last prefix row) are cheaper as decode steps of this slot
 // alone — 5 matvec / attention kernels per layer per row — than through the prefill GEMMs, whose tiles are sized for
 // hundreds of rows.

@@ -69,6 +69,7 @@ _SIGS = {
     "ocr_session_destroy": (C.c_int, [_P]),
     "ocr_session_n_past": (C.c_int, [_P, C.c_int, C.POINTER(C.c_int)]),
     "ocr_session_rewind": (C.c_int, [_P, C.c_int, C.c_int]),
+    "ocr_session_kv": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
     "ocr_prefill": (C.c_int, [_P, C.c_int, _P, _P, C.c_int, _P]),
     "ocr_step": (C.c_int, [_P, _P, _P]),
     "ocr_decode": (C.c_int, [_P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, TOKEN_CB, _P, _P,
@@ -314,6 +315,14 @@ class Session:
 
     def rewind(self, slot: int, n_past: int) -> None:
         _check(lib().ocr_session_rewind(self.h, slot, n_past))
+
+    def kv(self, layer: int, slot: int, row0: int, n_rows: int) -> tuple[np.ndarray, np.ndarray]:
+        """KV rows [row0, row0 + n_rows) of a layer and slot: (k, v) f16 bit patterns [n_rows][n_kv * 128]"""
+        w = self.model.cfg.n_kv * 128
+        k = np.empty((n_rows, w), np.uint16)
+        v = np.empty((n_rows, w), np.uint16)
+        _check(lib().ocr_session_kv(self.h, layer, slot, row0, n_rows, _ptr(k), _ptr(v)))
+        return k, v
 
     def prefill(self, slot: int = 0, ids: Optional[Sequence[int]] = None, embd: Optional[np.ndarray] = None,
                 logits: bool = True) -> Optional[np.ndarray]:

@@ -94,6 +94,11 @@ ocr_status ocr_session_destroy(ocr_session* s);
 ocr_status ocr_session_n_past(const ocr_session* s, int slot, int* out);
 /* rewind a slot to n_past positions (<= its current n_past): later steps overwrite the rows beyond */
 ocr_status ocr_session_rewind(ocr_session* s, int slot, int n_past);
+/* copy KV rows [row0, row0 + n_rows) of one layer and slot to the host as the reference's Session holds them per
+ * layer (text.rs:242-328: [n_ctx][n_kv * d_head] f16), k_out and v_out [n_rows][n_kv * 128] f16 bit patterns
+ * (inspection and tests). Synchronous. */
+ocr_status ocr_session_kv(const ocr_session* s, int layer, int slot, int row0, int n_rows, uint16_t* k_out,
+                          uint16_t* v_out);
 
 /* TextModel::prefill (text.rs:437-521) for one slot: n_rows rows at positions n_past…; row i is token ids[i] when
  * ids != NULL and ids[i] >= 0, else embedding row i of embd ([n_rows][dim] f32, Input::Embeddings). Host buffers.

@@ -397,6 +397,17 @@ void orc_session_set_n_past(orc_session* s, int n_past) { s->n_past = n_past; }
 const uint16_t* orc_session_k(const orc_session* s, int layer) { return s->k[layer]; }
 const uint16_t* orc_session_v(const orc_session* s, int layer) { return s->v[layer]; }
 
+/* overwrite KV rows [row0, row0 + n) of a layer with given f16 rows ([n][kvd]): a test takes the device's cache as the
+ * oracle's, so the oracle's decode step checks the device's decode step alone (not its prefill) */
+int orc_session_set_kv(orc_session* s, int layer, int row0, int n, const uint16_t* k, const uint16_t* v) {
+    const orc_cfg* c = &s->m->cfg;
+    const size_t kvd = (size_t)c->n_kv * c->d_head;
+    if (layer < 0 || layer >= c->n_layer || row0 < 0 || n < 0 || row0 + n > s->n_ctx) return 1;
+    memcpy(s->k[layer] + (size_t)row0 * kvd, k, (size_t)n * kvd * 2);
+    memcpy(s->v[layer] + (size_t)row0 * kvd, v, (size_t)n * kvd * 2);
+    return 0;
+}
+
 /* Y[L][N] = X[L][K] . deq(W[N][K])^T (+ Y if acc): prefill projections (the tiled matmul's product, text.rs:485-512) */
 static void gemm_q8_0(const uint8_t* w, int n, int k, const float* x, int l, float* y, int acc) {
     const int TN = 32;

@@ -110,6 +110,8 @@ int orc_decode(orc_session* s, const float* first_logits, float rp, int window, 
 /* KV cache rows of a layer (f16, [n_ctx][n_kv*d_head]) */
 const uint16_t* orc_session_k(const orc_session* s, int layer);
 const uint16_t* orc_session_v(const orc_session* s, int layer);
+/* overwrite KV rows [row0, row0 + n) of a layer ([n][n_kv*d_head] f16 each); 0 = ok */
+int orc_session_set_kv(orc_session* s, int layer, int row0, int n, const uint16_t* k, const uint16_t* v);
 
 int orc_num_threads(void);
 

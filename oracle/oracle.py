@@ -57,6 +57,7 @@ _SIGS = {
     "orc_decode": (C.c_int, [_P, _P, C.c_float, C.c_int, C.c_float, _P, C.c_int, C.c_int, _P, _P]),
     "orc_session_k": (_P, [_P, C.c_int]),
     "orc_session_v": (_P, [_P, C.c_int]),
+    "orc_session_set_kv": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, _P, _P]),
     "orc_num_threads": (C.c_int, []),
 }
 
@@ -266,6 +267,13 @@ class Session:
         k = np.ctypeslib.as_array(C.cast(lib().orc_session_k(self.h, layer), C.POINTER(C.c_uint16)), shape=(n,))
         v = np.ctypeslib.as_array(C.cast(lib().orc_session_v(self.h, layer), C.POINTER(C.c_uint16)), shape=(n,))
         return k.copy(), v.copy()
+
+    def set_kv(self, layer: int, row0: int, k: np.ndarray, v: np.ndarray) -> None:
+        """overwrite KV rows [row0, row0 + len(k)) of a layer (f16 bit patterns, [n][n_kv * d_head])"""
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        if lib().orc_session_set_kv(self.h, layer, row0, k.shape[0], _p(k), _p(v)) != 0:
+            raise RuntimeError("orc_session_set_kv: rows outside the session")
 
 
 def num_threads() -> int:

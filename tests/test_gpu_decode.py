@@ -308,3 +308,37 @@ def test_contexts_on_two_devices(ocr, orc, torch_cuda):
         s.close()
         m.close()
         c.close()
+
+
+@pytest.mark.parametrize("batch,slots", [(1, (0,)), (32, (0, 17))])
+def test_config2_decode_logits_match_oracle_on_the_same_cache(ocr, orc, ctx, batch, slots):
+    """BASELINE config 2's decode kernels at full size (28 x 1024, 16/8 heads, ffn 3072, vocab 151936), logits checked
+    step by step (fused_decode_kernels_match_cpu, app/crates/ocr-wgpu/src/text.rs:863-975): the device's 2048-row
+    prefill cache is copied into the oracle's session, then 4 decode steps on both — logits within 2e-3 of max |logit|
+    and relative L2 1e-3 each step. batch 1 runs the compiled one-slot kernels (fused qkv + attention + o-projection,
+    fused FFN, LM head); batch 32 with two live slots runs the tensor-core contractions and the batched attention."""
+    from tests.golden.make_golden import CONFIG2, IMAGE_PAD, config2_inputs
+
+    seed, prefix, _ = config2_inputs()
+    m = ocr.TextModel.synthetic(ctx, text_config(ocr, CONFIG2), seed, 0.02, 0.02)
+    om = orc.Model(CONFIG2, seed=seed, sigma_w=0.02, sigma_e=0.02)
+    n_ctx, n_pre = 2048 + 8, 2048
+    s = m.session(n_ctx, batch=batch)
+    oss = {}
+    for b in slots:
+        rows = prefix if b == 0 else prefix[::-1].copy()  # two different prefixes
+        s.prefill(b, embd=rows, logits=False)
+        os_ = om.session(n_ctx)
+        for layer in range(CONFIG2["n_layer"]):
+            k, v = s.kv(layer, b, 0, n_pre)
+            os_.set_kv(layer, 0, k, v)
+        os_.n_past = n_pre
+        oss[b] = os_
+    toks = {b: IMAGE_PAD for b in slots}
+    for _ in range(4):
+        feed = [toks.get(b, -1) for b in range(batch)]
+        lg = s.step(feed)
+        for b in slots:
+            lo = oss[b].step(toks[b])
+            close_logits(lg[b], lo)
+            toks[b] = int(np.argmax(lo))
