@@ -124,3 +124,37 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
                          "gate|up + swiglu (tcgen05)", "down + residual (tcgen05)"], names[:6]
     assert names[-2:] == ["prep (norm, hi/lo)", "lm head (tcgen05)"]
     assert len(rec) == 6 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
+
+
+def test_config3_batch_ids_match_oracle_and_single_slot(ocr, ctx):
+    """BASELINE config 3 at full size: 32 slots, each a 3072-row prefix, 1024 greedy tokens with rp 1.15 over a
+    64-token window, decoded as one batch on the tensor-core path. Slots 0 and 31 must give the oracle's ids
+    (tests/golden/config3_greedy.json) and the ids of the same slot decoded alone (the one-slot CUDA-core path)."""
+    import json
+    from pathlib import Path
+
+    from tests.golden.make_golden import CONFIG2, CONFIG3_NEW, CONFIG3_PREFIX, config3_inputs
+
+    fx = json.loads((Path(__file__).resolve().parent / "golden" / "config3_greedy.json").read_text())
+    seed = fx["seed"]
+    m = ocr.TextModel.synthetic(ctx, text_config(ocr, CONFIG2), seed, fx["sigma_w"], fx["sigma_e"])
+    B = fx["batch"]
+    s = m.session(CONFIG3_PREFIX + CONFIG3_NEW, batch=B)
+    for b in range(B):
+        _, prefix, history = config3_inputs(b)
+        s.prefill(b, embd=prefix, logits=False)
+    hist = np.full((B, 64), history[0], np.int32)
+    preset = ocr.Preset("c3", 0.0, 1.0, fx["rp"], fx["window"], 0.0, fx["max_new"])
+    got = s.decode_batch(preset, hist)
+    s.close()
+    one = m.session(CONFIG3_PREFIX + CONFIG3_NEW, batch=1)
+    for key, want in fx["slots"].items():
+        b = int(key)
+        g = got[b].tolist()
+        k = next((i for i in range(len(want["ids"])) if g[i] != want["ids"][i]), None)
+        assert k is None, (f"slot {b}: first divergence from the oracle at choice {k}: device {g[k]} vs oracle "
+                           f"{want['ids'][k]} (oracle top-2 margin {want['margins'][k]})")
+        _, prefix, history = config3_inputs(b)
+        one.rewind(0, 0)
+        one.prefill(0, embd=prefix, logits=False)
+        assert one.decode_gpu(0, preset, history) == g, b
