@@ -206,6 +206,57 @@ def kernel_roofline(classes):
 # ---------------------------------------------------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------------------------------------------------
+# the decode workloads: slots per GPU, prefix rows per slot, tokens decoded per slot (BASELINE configs[1] and [2])
+WORKLOADS = {2: dict(B=1, prefix=PREFIX, new=NEW), 3: dict(B=32, prefix=3072, new=1024)}
+
+
+def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0):
+    """one replica's decode throughput on a config: the model, each slot's prefix prefilled (untimed), then `steps`
+    timed steps of a full greedy decode of every slot through the C ABI (host history in, host ids out). Returns the
+    timing and the session (for the per-kernel profile)."""
+    w = WORKLOADS[config]
+    B, prefix_len, new = w["B"], w["prefix"], tokens or w["new"]
+    seed = ocr.SEED_BASE + 2
+    model = ocr.TextModel.synthetic(ctx, ocr.TextConfig(**CONFIG2), seed, 0.02, 0.02)
+    sess = model.session(prefix_len + new, batch=B)
+    for b in range(B):
+        embd = ocr.gauss(ocr.substream(seed + b, 200000), prefix_len * 1024, 1.0).reshape(prefix_len, 1024)
+        sess.prefill(b, embd=embd, logits=False)
+    last_rows = [ocr.gauss(ocr.substream(seed + b, 200000), 1024, 1.0, start=(prefix_len - 1) * 1024)
+                 for b in range(B)]
+    preset = ocr.Preset("bench", 0.0, 1.0, 1.15, 64, 0.0, new)
+    hist = np.full((B, 64), IMAGE_PAD, np.int32)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    def step():
+        # every slot back to its prefix (the last prefix row re-fed: every step starts from the same logits)
+        for b in range(B):
+            sess.rewind(b, prefix_len - 1)
+            sess.prefill(b, embd=last_rows[b], logits=False)
+        if B == 1:
+            return sess.decode_gpu(0, preset, hist[0])
+        return sess.decode_batch(preset, hist)
+
+    for _ in range(warmup):
+        step()
+    ctx.sync()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+        wall = time.perf_counter() - t0
+    dev_s, wall = max_over_ranks([ev0.elapsed_time(ev1) / 1e3, wall], pg)
+    return dict(B=B, prefix=prefix_len, new=new, dev_s=dev_s, wall=wall, clocks=clk.summary(), sess=sess,
+                model=model, last_rows=last_rows)
+
+
 def run_ours(args):
     import torch
 
@@ -222,59 +273,19 @@ def run_ours(args):
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
         pg = dist
     ctx = ocr.Context(local)
-    cfg = ocr.TextConfig(**{k: v for k, v in CONFIG2.items()})
-    seed = ocr.SEED_BASE + 2
     if args.config == 1:
         return run_config1(args, ocr, ctx, torch, pg, rank, world)
-    model = ocr.TextModel.synthetic(ctx, cfg, seed, 0.02, 0.02)
-    B = 32 if args.config == 3 else 1
-    prefix_len, new = (3072, 1024) if args.config == 3 else (PREFIX, NEW)
-    if args.tokens:
-        new = args.tokens
-    sess = model.session(prefix_len + new, batch=B)
-    for b in range(B):
-        embd = ocr.gauss(ocr.substream(seed + b, 200000), prefix_len * 1024, 1.0).reshape(prefix_len, 1024)
-        sess.prefill(b, embd=embd, logits=False)
-    last_rows = [ocr.gauss(ocr.substream(seed + b, 200000), 1024, 1.0, start=(prefix_len - 1) * 1024)
-                 for b in range(B)]
-    preset = ocr.Preset("bench", 0.0, 1.0, 1.15, 64, 0.0, new)
-    hist = np.full((B, 64), IMAGE_PAD, np.int32)
-    stream = torch.cuda.ExternalStream(ctx.stream())
-
-    def step():
-        for b in range(B):
-            sess.rewind(b, prefix_len - 1)
-            sess.prefill(b, embd=last_rows[b], logits=False)
-        if B == 1:
-            return sess.decode_gpu(0, preset, hist[0])
-        return sess.decode_batch(preset, hist)
-
-    for _ in range(args.warmup):
-        step()
-    ctx.sync()
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
-        t0 = time.perf_counter()
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        ev1.synchronize()
-        wall = time.perf_counter() - t0
-    dev_s, wall = max_over_ranks([ev0.elapsed_time(ev1) / 1e3, wall], pg)
+    r = decode_workload(ocr, ctx, torch, args.config, args.steps, args.warmup, pg, local, args.tokens)
+    B, prefix_len, new, dev_s, wall = r["B"], r["prefix"], r["new"], r["dev_s"], r["wall"]
     tokens = world * B * new * args.steps
     out = None
     if rank == 0:
-        classes = kernel_classes(sess, B, prefix_len, last_rows)
+        classes = kernel_classes(r["sess"], B, prefix_len, r["last_rows"])
         # per step: the one-row prefill per slot (a decode step of that slot), choice 0, then new - 1 decode steps;
-        # a decode step's launches as the profiler counted them (kernels per layer + the fused LM head / choice)
+        # a decode step's launches as the profiler counted them (kernels per layer + the LM head / choice)
         launches_per_token = sum(k["launches"] for k in classes) // 4
         launches = args.steps * (launches_per_token * B + 1 + (new - 1) * launches_per_token)
         roof = kernel_roofline(classes)
-        lm_us, lm_bytes = lm_head_kernel(ocr, ctx, torch, 10)
         out = {
             "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
             "value": round(whole_job_rate(world, B * new * args.steps, dev_s), 1), "unit": "tok/s", "n_gpus": world,
@@ -288,18 +299,30 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "roofline": roof,
             "kernels": classes,
-            "lm_head_alone": {"us_per_launch": round(lm_us, 2), "achieved_gbs": round(lm_bytes / lm_us / 1e3, 1),
-                              "note": "the LM head + penalty + argmax kernel timed alone after a 256 MB L2 flush"},
-            "clocks": clk.summary(),
+            "clocks": r["clocks"],
         }
+    r["sess"].close()
+    r["model"].close()
+    if rank == 0:
+        lm_us, lm_bytes = lm_head_kernel(ocr, ctx, torch, 10)
+        out["lm_head_alone"] = {"us_per_launch": round(lm_us, 2), "achieved_gbs": round(lm_bytes / lm_us / 1e3, 1),
+                                "note": "the LM head + penalty + argmax kernel timed alone after a 256 MB L2 read"}
+        if world == 1 and args.config == 3 and not args.no_secondary:
+            # BASELINE config 2 (one sequence per GPU) measured in the same run, reported beside the headline
+            r2 = decode_workload(ocr, ctx, torch, 2, 3, 3, None, local)
+            c2 = kernel_classes(r2["sess"], 1, r2["prefix"], r2["last_rows"])
+            out["config2"] = {"value": round(r2["new"] * 3 / r2["dev_s"], 1), "unit": "tok/s",
+                              "ms_per_step": round(r2["dev_s"] / 3 * 1e3, 3), "steps": 3, "warmup": 3,
+                              "workload": workload_config(2, 1, r2["new"], r2["prefix"], 1)["workload"],
+                              "roofline": kernel_roofline(c2), "kernels": c2}
+            r2["sess"].close()
+            r2["model"].close()
         if world == 1 and not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline_sample(tokens_sample=16)
+            out["cpu_baseline"] = cpu_baseline_sample(args.config, tokens_sample=16)
         print(json.dumps(out), flush=True)
     if pg:
         pg.barrier()
         pg.destroy_process_group()
-    sess.close()
-    model.close()
     ctx.close()
     return out
 
@@ -328,61 +351,79 @@ def run_config1(args, ocr, ctx, torch, pg, rank, world):
 # ---------------------------------------------------------------------------------------------------------------------
 # the CPU baseline (the oracle: the reference's path restated, OpenMP on all host cores)
 # ---------------------------------------------------------------------------------------------------------------------
-def cpu_baseline_sample(tokens_sample: int = 16):
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle as O
+def cpu_positions(config: int, n: int) -> list[int]:
+    """n decode positions spread evenly over the config's decode (prefix .. prefix + new - 1): the sampled tokens see
+    the same mean key count as the GPU arm's full decode"""
+    w = WORKLOADS[config]
+    return [w["prefix"] + (w["new"] * i) // n for i in range(n)]
 
-    import ocr_b200 as ocr
 
-    m = O.Model(CONFIG2, seed=ocr.SEED_BASE + 2, sigma_w=0.02, sigma_e=0.02)
-    s = m.session(PREFIX + NEW)
-    s.n_past = PREFIX  # a 2048-row cache: the per-token work is the same whatever the rows hold
-    s.step(IMAGE_PAD)  # warm-up
-    s.n_past = PREFIX
-    t0 = time.perf_counter()
-    for i in range(tokens_sample):
-        s.step((IMAGE_PAD + 7 * i) % CONFIG2["n_vocab"])
-    dt = time.perf_counter() - t0
-    return {"value": round(tokens_sample / dt, 2), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{tokens_sample} config-2 decode steps at positions {PREFIX}..{PREFIX + tokens_sample - 1} "
-                      f"over a {PREFIX}-row f16 KV cache, oracle/oracle.c (OpenMP)"}
+class CpuDecode:
+    """the oracle's decode (the reference's path restated, OpenMP on all host cores) on a config's model: timed runs of
+    single-token steps at positions spread over the config's decode, one sequence at a time"""
+
+    def __init__(self, config: int):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+
+        import ocr_b200 as ocr
+
+        self.config, self.O = config, O
+        w = WORKLOADS[config]
+        self.model = O.Model(CONFIG2, seed=ocr.SEED_BASE + 2, sigma_w=0.02, sigma_e=0.02)
+        self.s = self.model.session(w["prefix"] + w["new"])
+        self.s.n_past = w["prefix"]
+        self.s.step(IMAGE_PAD)  # warm-up
+
+    def run(self, n_tokens: int):
+        """(seconds, sample text) for n_tokens steps"""
+        pos = cpu_positions(self.config, n_tokens)
+        t0 = time.perf_counter()
+        for i, p in enumerate(pos):
+            self.s.n_past = p  # the cache rows' values do not change the work of a step
+            self.s.step((IMAGE_PAD + 7 * i) % CONFIG2["n_vocab"])
+        dt = time.perf_counter() - t0
+        sample = (f"{n_tokens} config-{self.config} decode steps at positions {pos[0]}..{pos[-1]} (spread evenly over "
+                  f"the decode, mean {sum(pos) / len(pos) + 1:.0f} keys), one sequence at a time, oracle/oracle.c "
+                  "(OpenMP)")
+        return dt, sample
+
+    def cores(self) -> int:
+        return self.O.num_threads()
+
+
+def cpu_baseline_sample(config: int, tokens_sample: int = 16):
+    cd = CpuDecode(config)
+    dt, sample = cd.run(tokens_sample)
+    return {"value": round(tokens_sample / dt, 2), "unit": "tok/s", "cores": cd.cores(), "kind": "port",
+            "sample": sample}
 
 
 def run_reference(args):
     rank, local, world = dist_env()
     if rank != 0:
         return
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle as O
-
-    import ocr_b200 as ocr
-
-    m = O.Model(CONFIG2, seed=ocr.SEED_BASE + 2, sigma_w=0.02, sigma_e=0.02)
-    s = m.session(PREFIX + NEW)
-    per_step = 4  # tokens per step: a bounded sample of the 512-token decode
-
-    def step():
-        s.n_past = PREFIX
-        for i in range(per_step):
-            s.step((IMAGE_PAD + 7 * i) % CONFIG2["n_vocab"])
-
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = time.perf_counter() - t0
+    config = 2 if args.config == 1 else args.config
+    w = WORKLOADS[config]
+    per_step = 4  # tokens per step: a bounded sample of the decode
+    cd = CpuDecode(config)
+    cores = cd.cores()
+    dt = 0.0
+    for i in range(args.warmup + args.steps):
+        t, sample = cd.run(per_step)
+        if i >= args.warmup:
+            dt += t
     v = round(per_step * args.steps / dt, 3)
-    sample = (f"{per_step} config-2 decode steps per step at positions {PREFIX}..{PREFIX + per_step - 1} over a "
-              f"{PREFIX}-row f16 KV cache (the reference's Rust/WGSL path cannot run here: no Rust toolchain, no "
-              "graphics adapter; timed is its CPU restatement oracle/oracle.c, OpenMP)")
+    sample = (sample.replace(f"{per_step} config", f"{per_step} (per step) config") +
+              " — the reference's Rust/WGSL path cannot run here (no Rust toolchain, no graphics adapter); timed is "
+              "its CPU restatement")
     print(json.dumps({
         "impl": "reference", "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
         "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV", "data": "synthetic",
-        "config": workload_config(2, 1, NEW, PREFIX, world),
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": O.num_threads(), "kind": "port", "sample": sample},
+        "config": workload_config(config, w["B"], w["new"], w["prefix"], world),
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
 
@@ -394,6 +435,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=[1, 2, 3], default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="config 3: skip the config-2 measurement beside it")
     ap.add_argument("--tokens", type=int, default=0,
                     help="decode this many tokens per step instead of the config's (short runs for ncu captures)")
     args = ap.parse_args()
