@@ -266,6 +266,34 @@ struct PrepArgs {
 };
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl);
 
+// ---- decode attention for batches (k_attn_batch.cu) -------------------------------------------------------------------
+// One CTA (or `split` CTAs) per (slot, kv head) streaming its keys; the q/k norm + RoPE + K/V store of the new token
+// as in AttnArgs; the G heads' merged rows written as the o-projection's operand (x16 over n_head x 128 columns)
+// and, when out is set, as f32 rows.
+constexpr int AB_MAX_SPLIT = 16;
+struct AttnBatchArgs {
+    const float* qkv = nullptr;  // [B][qkv_stride] raw projections
+    int qkv_stride = 0;
+    const float* q_norm = nullptr;
+    const float* k_norm = nullptr;
+    const float* rope = nullptr;  // [n_ctx][64][2]
+    __half* kc = nullptr;         // [B][n_kv][n_ctx][128]
+    __half* vc = nullptr;
+    const int32_t* pos = nullptr;
+    const int32_t* active = nullptr;
+    int n_head = 16, n_kv = 8, n_ctx = 0, nb = 1;
+    float eps = 1e-6f, scale = 0.0f;
+    float* out = nullptr;  // [B][out_stride] (nullable)
+    int out_stride = 0;
+    uint8_t* x16 = nullptr;  // [groups] the o-projection's operand (nullable)
+    float* part = nullptr;   // split > 1: [B * n_kv][split][G][132]
+    uint32_t* done = nullptr;  // split > 1: [B * n_kv] tickets (zero between launches)
+    int* err = nullptr;
+};
+// CTAs per (slot, kv head) for a batch: enough to fill two CTAs per SM, at most AB_MAX_SPLIT
+int attn_batch_split(int num_sms, int nb, int n_kv);
+void launch_attention_batch(cudaStream_t st, const AttnBatchArgs& a, int split, bool pdl);
+
 // ---- the bounded-wait test hook (k_probe.cu) ----
 // one mbarrier wait that cannot complete, limited to `tries` polls of ~1 µs: *waited_out = 1 and DEV_TIMEOUT flagged
 void launch_wait_probe(cudaStream_t st, int* err, uint32_t tries, int* waited_out);

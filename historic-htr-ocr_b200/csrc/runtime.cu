@@ -108,7 +108,7 @@ struct LayerW {
     float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
     uint8_t* o_s = nullptr;  // W_o cut per kv head (launch_slice_o), derived on the device after the load
     uint8_t* d_s = nullptr;  // W_down cut into FFN_NCLU h slices (the fused FFN), when the shape fits it
-    BgMaps bq_qkv, bq_gu, bq_down;  // the tensor-core contraction's views of qkv, gate|up and down (model tc)
+    BgMaps bq_qkv, bq_o, bq_gu, bq_down;  // the tensor-core contraction's views of the matrices (model tc)
 };
 
 struct ocr_model {
@@ -244,12 +244,13 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
     // the tensor maps of the batched contractions (they hold the matrices' addresses; the bytes come later)
     const char* tc_env = getenv("OCR_TC");
     m->tc = !(tc_env && tc_env[0] == '0') && bgemm_shape_ok(c.n_vocab, c.dim) && bgemm_shape_ok(2 * c.n_ff, c.dim) &&
-            bgemm_shape_ok(c.dim, c.n_ff) && bgemm_shape_ok(c.n_head * c.d_head + 2 * c.n_kv * c.d_head, c.dim);
+            bgemm_shape_ok(c.dim, c.n_ff) && bgemm_shape_ok(c.n_head * c.d_head + 2 * c.n_kv * c.d_head, c.dim) &&
+            bgemm_shape_ok(c.dim, c.n_head * c.d_head);
     std::string why;
     for (auto& w : m->layers) {
         if (!m->tc) break;
-        m->tc = bgemm_maps(w.qkv, &w.bq_qkv, &why) && bgemm_maps(w.gu, &w.bq_gu, &why) &&
-                bgemm_maps(w.down, &w.bq_down, &why);
+        m->tc = bgemm_maps(w.qkv, &w.bq_qkv, &why) && bgemm_maps(w.o, &w.bq_o, &why) &&
+                bgemm_maps(w.gu, &w.bq_gu, &why) && bgemm_maps(w.down, &w.bq_down, &why);
     }
     if (m->tc) m->tc = bgemm_maps(m->tok, &m->bq_tok, &why);
     *out = m;
@@ -481,6 +482,11 @@ struct ocr_session {
     bool tc = false;            // batched contractions on the tensor cores (more than 8 slots)
     uint8_t* x16a = nullptr;    // [groups] operands of width dim (x16 layout)
     uint8_t* x16g = nullptr;    // [groups] operands of width n_ff (the SwiGLU output)
+    bool battn = false;         // the batched attention (k_attn_batch) and the o-projection on the tensor cores
+    int ab_split = 1;           // its CTAs per (slot, kv head)
+    uint8_t* x16o = nullptr;    // [groups] operands of width n_head x 128 (the attention's output)
+    float* ab_part = nullptr;   // [B * n_kv][split][G][132] partials (split > 1)
+    uint32_t* ab_done = nullptr;  // [B * n_kv] tickets
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -532,10 +538,11 @@ LmArgs sampler_args(ocr_session* s, const ocr_sampler_cfg* cfg);
 
 // One decode step of a batch of more than 8 slots, its contractions on the tensor cores (k_bgemm.cu). Per layer:
 // the slots' residual rows (layer 0: their tokens' embedding rows) RMS-normalised into the operand (prep), the qkv
-// contraction, the attention with its fused o-projection (per-kv-head partial products), the FFN's operand prep
-// (residual + the partials in order, written back, normalised), the gate|up contraction whose SwiGLU epilogue writes
-// the down contraction's operand, and the down contraction adding onto the residual. Then the LM head's prep and its
-// contraction with the windowed penalty and the choice.
+// contraction, the batched attention (k_attn_batch.cu) writing the o-projection's operand, the o-projection adding
+// onto the residual, the FFN's operand prep, the gate|up contraction whose SwiGLU epilogue writes the down
+// contraction's operand, and the down contraction adding onto the residual. Then the LM head's prep and its
+// contraction with the windowed penalty and the choice. (With OCR_BATTN=0 the attention is the cluster kernel with
+// the o-projection fused per kv head, and the FFN's prep sums its partial products.)
 void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_fp, float fp, Prof* prof,
                     bool x_given) {
     const ocr_model* m = s->m;
@@ -587,38 +594,67 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
         launch_bgemm(st, gemm(L.qkv, L.bq_qkv, s->x16a, MV_STORE, s->qkv, s->qkv_w, nullptr), L.bq_qkv, ctx->num_sms,
                      pdl);
         if (prof) prof->mark("qkv (tcgen05)", l, mat_bytes(L.qkv) + nact * (c.dim * 4.0 + s->qkv_w * 4.0));
-        AttnArgs a;
-        a.qkv = s->qkv;
-        a.qkv_stride = s->qkv_w;
-        a.q_norm = L.q_norm;
-        a.k_norm = L.k_norm;
-        a.rope = s->rope;
-        a.kc = s->kcl(l);
-        a.vc = s->vcl(l);
-        a.pos = s->pos;
-        a.active = s->active;
-        a.n_head = c.n_head;
-        a.n_kv = c.n_kv;
-        a.n_ctx = s->n_ctx;
-        a.splits = s->splits;
-        a.eps = c.eps;
-        a.scale = 1.0f / sqrtf((float)c.d_head);
-        a.out = s->attn;
-        a.out_stride = s->qd;
-        a.nb = s->B;
-        a.err = ctx->d_err;
-        a.wo = L.o_s;
-        a.dim = c.dim;
-        a.opart = s->opart;
-        launch_attention_decode(st, a, pdl);
-        if (prof) {
-            double kv = 0;
+        double kv = 0;
+        if (prof)
             for (int p : prof->pos) kv += (double)(p + 1) * c.n_kv * 128 * 2 * 2;
-            prof->mark("attention + o-proj", l,
-                       kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
-                           nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
+        if (s->battn) {
+            // the batched attention writes the o-projection's operand; the o-projection adds onto the residual
+            AttnBatchArgs a;
+            a.qkv = s->qkv;
+            a.qkv_stride = s->qkv_w;
+            a.q_norm = L.q_norm;
+            a.k_norm = L.k_norm;
+            a.rope = s->rope;
+            a.kc = s->kcl(l);
+            a.vc = s->vcl(l);
+            a.pos = s->pos;
+            a.active = s->active;
+            a.n_head = c.n_head;
+            a.n_kv = c.n_kv;
+            a.n_ctx = s->n_ctx;
+            a.nb = s->B;
+            a.eps = c.eps;
+            a.scale = 1.0f / sqrtf((float)c.d_head);
+            a.x16 = s->x16o;
+            a.part = s->ab_part;
+            a.done = s->ab_done;
+            a.err = ctx->d_err;
+            launch_attention_batch(st, a, s->ab_split, pdl);
+            if (prof) prof->mark("attention (batched)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
+            launch_bgemm(st, gemm(L.o, L.bq_o, s->x16o, MV_ADD, s->x, c.dim, nullptr), L.bq_o, ctx->num_sms, pdl);
+            if (prof) prof->mark("o + residual (tcgen05)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
+            prep(l, L.ffn_norm, nullptr, 0, false, pdl);
+        } else {
+            AttnArgs a;
+            a.qkv = s->qkv;
+            a.qkv_stride = s->qkv_w;
+            a.q_norm = L.q_norm;
+            a.k_norm = L.k_norm;
+            a.rope = s->rope;
+            a.kc = s->kcl(l);
+            a.vc = s->vcl(l);
+            a.pos = s->pos;
+            a.active = s->active;
+            a.n_head = c.n_head;
+            a.n_kv = c.n_kv;
+            a.n_ctx = s->n_ctx;
+            a.splits = s->splits;
+            a.eps = c.eps;
+            a.scale = 1.0f / sqrtf((float)c.d_head);
+            a.out = s->attn;
+            a.out_stride = s->qd;
+            a.nb = s->B;
+            a.err = ctx->d_err;
+            a.wo = L.o_s;
+            a.dim = c.dim;
+            a.opart = s->opart;
+            launch_attention_decode(st, a, pdl);
+            if (prof)
+                prof->mark("attention + o-proj", l,
+                           kv + (double)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv) +
+                               nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
+            prep(l, L.ffn_norm, s->opart, c.n_kv, false, pdl);
         }
-        prep(l, L.ffn_norm, s->opart, c.n_kv, false, pdl);
         launch_bgemm(st, gemm(L.gu, L.bq_gu, s->x16a, MV_SWIGLU, nullptr, 0, s->x16g), L.bq_gu, ctx->num_sms, pdl);
         if (prof) prof->mark("gate|up + swiglu (tcgen05)", l, mat_bytes(L.gu) + nact * (c.dim * 4.0 + c.n_ff * 4.0));
         launch_bgemm(st, gemm(L.down, L.bq_down, s->x16g, MV_ADD, s->x, c.dim, nullptr), L.bq_down, ctx->num_sms, pdl);
@@ -1334,10 +1370,18 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_dpart = fuse_ffn ? p.take((size_t)FFN_NCLU * c.dim * 4) : 0;
     // batches of more than 8 slots run their contractions on the tensor cores (with the o-projection fused into the
     // attention, whose per-head partials the FFN's operand preparation sums)
-    const bool tc = m->tc && fuse && batch > 8;
+    const char* ba_env = getenv("OCR_BATTN");
+    const bool ba_on = !(ba_env && ba_env[0] == '0');  // the batched attention (else the cluster kernel, fused o-proj)
+    const bool tc = m->tc && batch > 8 && (ba_on || fuse);
     const size_t groups = (size_t)(batch + BG_SLOTS - 1) / BG_SLOTS;
     const size_t o_x16a = tc ? p.take(groups * x16_group_bytes(c.dim)) : 0;
     const size_t o_x16g = tc ? p.take(groups * x16_group_bytes(c.n_ff)) : 0;
+    const bool battn = tc && ba_on;
+    const int ab_split = battn ? attn_batch_split(ctx->num_sms, batch, c.n_kv) : 1;
+    const size_t o_x16o = battn ? p.take(groups * x16_group_bytes(c.n_head * c.d_head)) : 0;
+    const size_t o_abp = battn && ab_split > 1
+                             ? p.take((size_t)batch * c.n_kv * ab_split * (c.n_head / c.n_kv) * 132 * 4) : 0;
+    const size_t o_abd = battn ? p.take((size_t)batch * c.n_kv * 4) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
@@ -1363,6 +1407,13 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         s->tc = true;
         s->x16a = (uint8_t*)(w + o_x16a);
         s->x16g = (uint8_t*)(w + o_x16g);
+    }
+    if (battn) {
+        s->battn = true;
+        s->ab_split = ab_split;
+        s->x16o = (uint8_t*)(w + o_x16o);
+        s->ab_part = ab_split > 1 ? (float*)(w + o_abp) : nullptr;
+        s->ab_done = (uint32_t*)(w + o_abd);
     }
     s->qkv = (float*)(w + o_qkv);
     s->attn = (float*)(w + o_attn);

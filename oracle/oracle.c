@@ -569,19 +569,27 @@ int orc_step(orc_session* s, int32_t tok, float* logits) {
     return 0;
 }
 
-static float top2_margin(const float* l, int n) {
+/* the gap between the largest and the second largest logit, and the second one's index (the first of equals) */
+static float top2_margin(const float* l, int n, int32_t* second) {
     float b1 = -INFINITY, b2 = -INFINITY;
+    int32_t i1 = -1, i2 = -1;
     for (int i = 0; i < n; i++) {
         float v = l[i];
-        if (v > b1) { b2 = b1; b1 = v; }
-        else if (v > b2) b2 = v;
+        if (v > b1) { b2 = b1; i2 = i1; b1 = v; i1 = i; }
+        else if (v > b2) { b2 = v; i2 = i; }
     }
+    if (second) *second = i2;
     return b1 - b2;
 }
 
 /* text.rs:587-625 + Choice (text.rs:185-231): history seed = the last `window` ids, then every chosen token */
 int orc_decode(orc_session* s, const float* first_logits, float rp, int window, float fp, const int32_t* history,
                int n_hist, int max_new, int32_t* ids_out, float* margins_out) {
+    return orc_decode_top2(s, first_logits, rp, window, fp, history, n_hist, max_new, ids_out, margins_out, NULL);
+}
+
+int orc_decode_top2(orc_session* s, const float* first_logits, float rp, int window, float fp, const int32_t* history,
+                    int n_hist, int max_new, int32_t* ids_out, float* margins_out, int32_t* second_out) {
     const orc_cfg* c = &s->m->cfg;
     int seed = n_hist > window ? window : n_hist;
     int32_t* hist = (int32_t*)malloc(sizeof(int32_t) * (size_t)(seed + max_new));
@@ -606,7 +614,10 @@ int orc_decode(orc_session* s, const float* first_logits, float rp, int window, 
             }
         }
         int32_t t = orc_choose_greedy(l, c->n_vocab, rp, window, fp, hist, seed + i, ctok, cnt, n_distinct);
-        if (margins_out) margins_out[i] = top2_margin(l, c->n_vocab);
+        int32_t second = -1;
+        const float margin = top2_margin(l, c->n_vocab, &second);
+        if (margins_out) margins_out[i] = margin;
+        if (second_out) second_out[i] = second;
         ids_out[i] = t;
         hist[seed + i] = t;
         if (counts) counts[t]++;

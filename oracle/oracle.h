@@ -107,6 +107,9 @@ int orc_step(orc_session* s, int32_t tok, float* logits);
 /* greedy decode with the windowed penalty: the first choice from `logits` (the prompt's), then step+choose */
 int orc_decode(orc_session* s, const float* first_logits, float rp, int window, float fp, const int32_t* history,
                int n_hist, int max_new, int32_t* ids_out, float* margins_out);
+/* orc_decode that also gives, per choice, the runner-up token (the second largest penalised logit) */
+int orc_decode_top2(orc_session* s, const float* first_logits, float rp, int window, float fp, const int32_t* history,
+                    int n_hist, int max_new, int32_t* ids_out, float* margins_out, int32_t* second_out);
 /* KV cache rows of a layer (f16, [n_ctx][n_kv*d_head]) */
 const uint16_t* orc_session_k(const orc_session* s, int layer);
 const uint16_t* orc_session_v(const orc_session* s, int layer);

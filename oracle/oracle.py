@@ -55,6 +55,7 @@ _SIGS = {
     "orc_prefill": (C.c_int, [_P, _P, _P, C.c_int, _P]),
     "orc_step": (C.c_int, [_P, C.c_int32, _P]),
     "orc_decode": (C.c_int, [_P, _P, C.c_float, C.c_int, C.c_float, _P, C.c_int, C.c_int, _P, _P]),
+    "orc_decode_top2": (C.c_int, [_P, _P, C.c_float, C.c_int, C.c_float, _P, C.c_int, C.c_int, _P, _P, _P]),
     "orc_session_k": (_P, [_P, C.c_int]),
     "orc_session_v": (_P, [_P, C.c_int]),
     "orc_session_set_kv": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, _P, _P]),
@@ -260,6 +261,19 @@ class Session:
         if rc != 0:
             raise RuntimeError(f"orc_decode: {rc}")
         return ids, margins
+
+    def decode_top2(self, first_logits: np.ndarray, rp: float, window: int, fp: float, history: Sequence[int],
+                    max_new: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """decode, with each choice's top-2 margin and runner-up token"""
+        ids = np.empty(max_new, np.int32)
+        margins = np.empty(max_new, np.float32)
+        second = np.empty(max_new, np.int32)
+        h = np.ascontiguousarray(history, np.int32)
+        rc = lib().orc_decode_top2(self.h, _p(np.ascontiguousarray(first_logits, np.float32)), rp, window, fp,
+                                   _p(h) if h.size else None, h.size, max_new, _p(ids), _p(margins), _p(second))
+        if rc != 0:
+            raise RuntimeError(f"orc_decode_top2: {rc}")
+        return ids, margins, second
 
     def kv(self, layer: int) -> tuple[np.ndarray, np.ndarray]:
         c = self.model.cfg

@@ -15,9 +15,10 @@ config2: the CPU oracle's greedy decode of BASELINE config 2 (28 layers, dim 102
 a 64-token window seeded with 64 x <|image_pad|> = 151655). The fixture holds the ids and each step's top-2 margin, so
 the GPU test needs no oracle run on the GPU host.
 
-config3: the same oracle decode for slots 0 and 31 of BASELINE config 3 (32 sequences on the config-2 decoder; slot
+config3: the same oracle decode for slots 0, 15 and 31 of BASELINE config 3 (32 sequences on the config-2 decoder; slot
 b's prefix is 3072 rows of gauss(substream(seed + b, 200000)); 1024 tokens each, rp 1.15, window 64 seeded with 64 x
-<|image_pad|>): the batched GPU path's ids for those slots must equal them.
+<|image_pad|>), with each choice's top-2 margin and runner-up token: the batched GPU path's ids for those slots must
+equal them (a swap at a near-tie is told apart from an error by the runner-up).
 """
 from __future__ import annotations
 
@@ -149,7 +150,7 @@ def make_config2() -> dict:
 
 # 32 sequences on the config-2 decoder, each a 3072-row prefix and 1024 greedy tokens.
 # The oracle decodes a subset of the slots at full length; the GPU test runs the whole batch and compares those.
-CONFIG3_SLOTS = (0, 31)
+CONFIG3_SLOTS = (0, 15, 31)
 CONFIG3_PREFIX, CONFIG3_NEW = 3072, 1024
 
 
@@ -172,10 +173,11 @@ def make_config3() -> dict:
         s = m.session(CONFIG3_PREFIX + CONFIG3_NEW)
         first = s.prefill(None, prefix, CONFIG3_PREFIX)
         t1 = time.time()
-        ids, margins = s.decode(first, 1.15, 64, 0.0, history, CONFIG3_NEW)
+        ids, margins, second = s.decode_top2(first, 1.15, 64, 0.0, history, CONFIG3_NEW)
         t2 = time.time()
         order = np.argsort(-first, kind="stable")[:8]
-        slots[str(b)] = dict(ids=ids.tolist(), margins=[float(x) for x in margins], first_top8=order.tolist(),
+        slots[str(b)] = dict(ids=ids.tolist(), margins=[float(x) for x in margins], runner_up=second.tolist(),
+                             first_top8=order.tolist(),
                              first_top8_logits=[float(first[k]) for k in order],
                              first_max_abs=float(np.abs(first).max()),
                              oracle_seconds=dict(prefill=round(t1 - t0, 1), decode=round(t2 - t1, 1)))

@@ -64,12 +64,13 @@ def test_tensor_core_matvec_matches_oracle(ocr, orc, ctx, torch_cuda, rows, cols
 BATCH_CFG = dict(n_layer=3, dim=256, n_head=16, n_kv=8, d_head=128, n_ff=512, n_vocab=1000, eps=1e-6, rope_base=1e6)
 
 
-@pytest.mark.parametrize("B", [12, 33])
-def test_tensor_core_batch_decode_matches_oracle(ocr, orc, ctx, B):
-    """B slots of a 3-layer model (16/8 heads, dim 256, ffn 512): each slot's prompt prefilled, then (a) four CPU-choice
+@pytest.mark.parametrize("B,heads", [(12, (16, 8)), (33, (16, 8)), (9, (8, 8)), (10, (16, 4))])
+def test_tensor_core_batch_decode_matches_oracle(ocr, orc, ctx, B, heads):
+    """B slots of a 3-layer model (dim 256, ffn 512; 16/8, 8/8 or 16/4 heads: 1, 2 or 4 q heads per kv head, one CTA
+    or several per (slot, kv head)): each slot's prompt prefilled, then (a) four CPU-choice
     steps of the whole batch — every slot's logits against the oracle's — and (b) the device-choice batched decode,
     whose ids must equal the oracle's greedy ids and those of the slots decoded one at a time"""
-    cfg = BATCH_CFG
+    cfg = dict(BATCH_CFG, n_head=heads[0], n_kv=heads[1])
     n_new, n_steps = 20, 4
     om = orc.Model(cfg, seed=47, sigma_w=0.2, sigma_e=1.0)
     gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
@@ -111,8 +112,8 @@ def test_tensor_core_batch_decode_matches_oracle(ocr, orc, ctx, B):
 
 
 def test_tensor_core_profile_step(ocr, orc, ctx):
-    """the profiler sees the batched step's kernels: per layer prep, qkv, attention, prep, gate|up, down; then the LM
-    head's prep and contraction"""
+    """the profiler sees the batched step's kernels: per layer prep, qkv, the batched attention, the o-projection,
+    prep, gate|up, down; then the LM head's prep and contraction"""
     cfg = BATCH_CFG
     gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
     s = gm.session(32, batch=16)
@@ -120,16 +121,34 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
         s.prefill(b, ids=[1 + b, 2, 3, 4, 5], logits=False)
     rec = s.profile_step([7] * 16)
     names = [r["name"] for r in rec]
-    assert names[:6] == ["prep (embed, norm, hi/lo)", "qkv (tcgen05)", "attention + o-proj", "prep (sum, norm, hi/lo)",
-                         "gate|up + swiglu (tcgen05)", "down + residual (tcgen05)"], names[:6]
+    assert names[:7] == ["prep (embed, norm, hi/lo)", "qkv (tcgen05)", "attention (batched)", "o + residual (tcgen05)",
+                         "prep (norm, hi/lo)", "gate|up + swiglu (tcgen05)", "down + residual (tcgen05)"], names[:7]
     assert names[-2:] == ["prep (norm, hi/lo)", "lm head (tcgen05)"]
-    assert len(rec) == 6 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
+    assert len(rec) == 7 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
+
+
+# Below this top-2 gap (logit units; about 3e-5 of the largest |logit| here) the order of f32 summation decides the
+# greedy choice: the oracle sums in f64, the device in f32 in another order. A device sequence may leave the oracle's at
+# such a step only by taking the oracle's runner-up there (the comparison ends at that step); anywhere else the ids
+# must be identical (read.rs:324-331 reports a divergence the same way: the step and both margins).
+NEAR_TIE = 1e-4
+
+
+def first_divergence(got, want):
+    """None when identical; else the step where the device took the oracle's runner-up at a near-tie (asserts so)"""
+    k = next((i for i in range(len(want["ids"])) if got[i] != want["ids"][i]), None)
+    if k is not None:
+        assert want["margins"][k] < NEAR_TIE and got[k] == want["runner_up"][k], (
+            f"first divergence at choice {k}: device {got[k]} vs oracle {want['ids'][k]} (runner-up "
+            f"{want['runner_up'][k]}, oracle top-2 margin {want['margins'][k]:.3g})")
+    return k
 
 
 def test_config3_batch_ids_match_oracle_and_single_slot(ocr, ctx):
     """BASELINE config 3 at full size: 32 slots, each a 3072-row prefix, 1024 greedy tokens with rp 1.15 over a
-    64-token window, decoded as one batch on the tensor-core path. Slots 0 and 31 must give the oracle's ids
-    (tests/golden/config3_greedy.json) and the ids of the same slot decoded alone (the one-slot CUDA-core path)."""
+    64-token window, decoded as one batch on the tensor-core path. For the fixture's slots (0, 15, 31) the ids must be
+    the oracle's (tests/golden/config3_greedy.json) — up to a swap at a near-tie — and so must the same slot's ids
+    decoded alone (the one-slot CUDA-core path); at least one slot matches over all 1024 choices."""
     import json
     from pathlib import Path
 
@@ -148,13 +167,15 @@ def test_config3_batch_ids_match_oracle_and_single_slot(ocr, ctx):
     got = s.decode_batch(preset, hist)
     s.close()
     one = m.session(CONFIG3_PREFIX + CONFIG3_NEW, batch=1)
+    full = 0
     for key, want in fx["slots"].items():
         b = int(key)
-        g = got[b].tolist()
-        k = next((i for i in range(len(want["ids"])) if g[i] != want["ids"][i]), None)
-        assert k is None, (f"slot {b}: first divergence from the oracle at choice {k}: device {g[k]} vs oracle "
-                           f"{want['ids'][k]} (oracle top-2 margin {want['margins'][k]})")
+        kb = first_divergence(got[b].tolist(), want)
         _, prefix, history = config3_inputs(b)
         one.rewind(0, 0)
         one.prefill(0, embd=prefix, logits=False)
-        assert one.decode_gpu(0, preset, history) == g, b
+        k1 = first_divergence(one.decode_gpu(0, preset, history), want)
+        print(f"slot {b}: batch {'identical' if kb is None else f'near-tie swap at {kb}'}, one slot "
+              f"{'identical' if k1 is None else f'near-tie swap at {k1}'}")
+        full += kb is None
+    assert full >= 1
