@@ -129,6 +129,11 @@ __device__ inline void choice_finish(const float* bv_sm, const uint32_t* bi_sm, 
             else dev_error(a.err, DEV_BAD_INDEX);
             a.len[b] = len + 1;
             if (a.advance_pos) a.pos[b] += 1;
+            if (a.remaining) {
+                const int32_t r = a.remaining[b] - 1;
+                a.remaining[b] = r;
+                if (r <= 0 && a.active_w) a.active_w[b] = 0;
+            }
             if (a.use_fp) {
                 const long k = (long)b * n_vocab + t;
                 const uint32_t c = a.counts[k] + 1u;

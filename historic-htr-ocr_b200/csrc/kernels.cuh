@@ -55,6 +55,10 @@ struct LmArgs {
     float* part = nullptr;       // scratch: [B][grid][2] + [B] NaN-at-token-0 flags
     uint32_t* done = nullptr;    // scratch counters (self-resetting)
     int nb = 1;                  // slots in the partials' layout
+    // continuous batching (ocr_read_pages): each choice counts down the slot's budget, and the slot goes idle (its
+    // active flag cleared, read by the next step's kernels) when the budget is spent; null = no budgets
+    int32_t* remaining = nullptr;  // [B]
+    int32_t* active_w = nullptr;   // [B] the active flags, writable
     int* err = nullptr;
 };
 

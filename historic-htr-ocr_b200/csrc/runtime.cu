@@ -490,6 +490,8 @@ struct ocr_session {
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
+    int32_t* remaining = nullptr;  // [B] token budgets of the page engine (ocr_read_pages), after `active`
+    bool pages = false;            // steps recorded now count budgets down (the page engine is running)
     int32_t* hist = nullptr;
     int hist_cap = 0;
     uint32_t* counts = nullptr;
@@ -502,6 +504,7 @@ struct ocr_session {
     cudaGraphExec_t gexec = nullptr;
     float g_rp = 0, g_fp = 0;
     int g_window = -1, g_use_fp = -1;
+    bool g_pages = false;
     int32_t* g_hist = nullptr;
     int32_t* h_ids = nullptr;  // pinned readback
     size_t h_ids_n = 0;
@@ -664,6 +667,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
     BgArgs h = gemm(m->tok, m->bq_tok, s->x16a, MV_LMHEAD, s->logits, c.n_vocab, nullptr);
     ocr_sampler_cfg sc{rp, window, fp, 1};
     h.lm = sampler_args(s, &sc);
+    if (!sample) h.lm.remaining = h.lm.active_w = nullptr;
     h.lm.sample = sample ? 1 : 0;
     h.lm.use_fp = use_fp;
     h.lm.advance_pos = sample ? 1 : 0;
@@ -923,6 +927,10 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     lm.lm.done = s->lm_done;
     lm.lm.nb = s->B;
     lm.lm.err = ctx->d_err;
+    if (s->pages && sample) {
+        lm.lm.remaining = s->remaining;
+        lm.lm.active_w = s->active;
+    }
     lm.next = with_w(kv_of(0), m->layers[0].qkv);  // the next step's first kernels
     if (fused) {
         lm.next.w2 = m->layers[0].o_s;
@@ -997,13 +1005,17 @@ LmArgs sampler_args(ocr_session* s, const ocr_sampler_cfg* cfg) {
     a.part = s->lm_part;
     a.done = s->lm_done;
     a.err = s->ctx->d_err;
+    if (s->pages) {
+        a.remaining = s->remaining;
+        a.active_w = s->active;
+    }
     return a;
 }
 
 ocr_status capture_graph(ocr_session* s, const ocr_sampler_cfg* cfg) {
     const int use_fp = cfg->fp > 0.0f ? 1 : 0;
     if (s->gexec && s->g_rp == cfg->rp && s->g_window == cfg->window && s->g_use_fp == use_fp && s->g_fp == cfg->fp &&
-        s->g_hist == s->hist)
+        s->g_hist == s->hist && s->g_pages == s->pages)
         return OCR_OK;
     if (s->gexec) {
         cudaGraphExecDestroy(s->gexec);
@@ -1023,6 +1035,7 @@ ocr_status capture_graph(ocr_session* s, const ocr_sampler_cfg* cfg) {
     s->g_use_fp = use_fp;
     s->g_fp = cfg->fp;
     s->g_hist = s->hist;
+    s->g_pages = s->pages;
     return OCR_OK;
 }
 
@@ -1388,7 +1401,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_logits = p.take((size_t)batch * c.n_vocab * 4);
     const size_t o_lmp = p.take(((size_t)batch * lm_grid * 2 + batch) * 4);
     const size_t o_lmd = p.take((size_t)(batch + 64) * 4);
-    const size_t o_state = p.take((size_t)batch * 4 * 4);
+    const size_t o_state = p.take((size_t)batch * 5 * 4);  // pos, len, tok, active, remaining
     if (e == cudaSuccess) e = dalloc(&s->work, p.off, &ctx->mem_work);
     if (e != cudaSuccess) {
         ocr_session_destroy(s);
@@ -1425,6 +1438,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     s->len = s->pos + batch;
     s->tok = s->len + batch;
     s->active = s->tok + batch;
+    s->remaining = s->active + batch;
     const std::vector<float> cs = rope_table(c.rope_base, c.d_head, n_ctx);
     e = cudaMemcpy(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
@@ -1692,6 +1706,163 @@ ocr_status ocr_decode_batch(ocr_session* s, const ocr_sampler_cfg* cfg, const in
     if (!s || !ids_out) return fail(OCR_ERR_ARG, "null argument");
     OCR_CUDA(cudaSetDevice(s->ctx->device));
     return decode_slots(s, 0, s->B, cfg, history, n_hist, nullptr, nullptr, ids_out, nullptr);
+}
+
+// The page engine: Engine::read_text's per-page loop (app/crates/ocr-wgpu/src/engine.rs:447-524) over many pages at
+// once. The session's slots hold pages at different stages: between chunks of decode steps, every free slot takes the
+// next page (prefill of its rows, the window seeded, choice 0 from the prefill's logits), and each page's token budget
+// counts down on the device, its slot going idle after its last choice — so one captured step serves any mix of pages.
+ocr_status ocr_read_pages(ocr_session* s, const ocr_sampler_cfg* cfg, int chunk, const ocr_page_io* io) {
+    if (!s || !io || !io->next || !io->done) return fail(OCR_ERR_ARG, "null argument");
+    OCR_TRY(check_sampler(cfg));
+    if (chunk < 1 || chunk > 4096) return fail(OCR_ERR_ARG, "chunk must be in [1, 4096]");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    cudaStream_t st = ctx->stream;
+    const int B = s->B;
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    OCR_TRY(ensure_hist(s, cfg->window + cfg->max_new));
+    if (cfg->fp > 0.0f) OCR_TRY(ensure_counts(s));
+    const int cap = s->hist_cap;
+    // host mirrors of the device state block: pos, len, tok, active, remaining (5 x B ints, contiguous)
+    std::vector<int32_t> mir((size_t)5 * B, 0);
+    auto M = [&](int field, int b) -> int32_t& { return mir[(size_t)field * B + b]; };
+    auto upload = [&]() -> ocr_status {
+        OCR_CUDA(cudaMemcpyAsync(s->pos, mir.data(), mir.size() * 4, cudaMemcpyHostToDevice, st));
+        return OCR_OK;
+    };
+    auto readback = [&]() -> ocr_status {
+        OCR_CUDA(cudaMemcpyAsync(mir.data(), s->pos, mir.size() * 4, cudaMemcpyDeviceToHost, st));
+        OCR_CUDA(cudaStreamSynchronize(st));
+        return check_device_error(ctx);
+    };
+    struct Slot {
+        bool busy = false;
+        ocr_page pg{};
+        int seed = 0, made = 0;
+    };
+    std::vector<Slot> sl(B);
+    for (int b = 0; b < B; b++) M(0, b) = s->n_past[b];
+    OCR_TRY(upload());  // every slot idle
+    // a page's ids so far, from the slot's history, to the caller's buffer
+    auto collect = [&](int b) -> ocr_status {
+        Slot& x = sl[b];
+        const int n = M(1, b) - x.seed - x.made;
+        if (n > 0) {
+            OCR_CUDA(cudaMemcpy(x.pg.ids_out + x.made, s->hist + (size_t)b * cap + x.seed + x.made, (size_t)n * 4,
+                                cudaMemcpyDeviceToHost));
+            x.made += n;
+        }
+        return OCR_OK;
+    };
+    bool more = true, stop = false;
+    ocr_status rc = OCR_OK;
+    auto begin = [&](int b, const ocr_page& pg) -> ocr_status {
+        if (pg.n_rows < 1 || pg.max_new < 1 || pg.max_new > cfg->max_new || !pg.ids_out || pg.n_hist < 0 ||
+            (pg.n_hist > 0 && !pg.history))
+            return fail(OCR_ERR_ARG, "page " + std::to_string(pg.id) + ": bad rows, budget, history or output");
+        if (pg.n_rows + pg.max_new - 1 > s->n_ctx)
+            return fail(OCR_ERR_STATE, "page " + std::to_string(pg.id) + ": " + std::to_string(pg.n_rows) + " rows + " +
+                                           std::to_string(pg.max_new) + " tokens overflow the session's " +
+                                           std::to_string(s->n_ctx));
+        const int seed = std::min(pg.n_hist, cfg->window);
+        for (int i = pg.n_hist - seed; i < pg.n_hist; i++)
+            if (pg.history[i] < 0 || pg.history[i] >= c.n_vocab)
+                return fail(OCR_ERR_ARG, "page " + std::to_string(pg.id) + ": history token outside the vocabulary");
+        s->n_past[b] = 0;
+        s->has_logits[b] = 0;
+        OCR_TRY(ocr_prefill(s, b, pg.ids, pg.embd, pg.n_rows, nullptr));
+        // (a prefill of a few rows runs as a step of this slot alone and rewrites every slot's state: restore it)
+        M(0, b) = s->n_past[b];
+        M(1, b) = seed;
+        M(3, b) = 1;
+        M(4, b) = pg.max_new - 1;
+        s->pages = false;  // choice 0 spends no budget
+        OCR_TRY(upload());
+        OCR_CUDA(cudaMemcpyAsync(s->hist + (size_t)b * cap, pg.history + (pg.n_hist - seed), (size_t)seed * 4,
+                                 cudaMemcpyHostToDevice, st));
+        if (cfg->fp > 0.0f) {
+            OCR_CUDA(cudaMemsetAsync(s->counts + (size_t)b * c.n_vocab, 0, (size_t)c.n_vocab * 4, st));
+            OCR_CUDA(cudaMemsetAsync(s->fpen + (size_t)b * c.n_vocab, 0, (size_t)c.n_vocab * 4, st));
+        }
+        LmArgs sa = sampler_args(s, cfg);
+        launch_sample(st, s->logits, c.n_vocab, c.n_vocab, sa, ctx->num_sms, b, 1);
+        OCR_CUDA(cudaGetLastError());
+        s->pages = true;
+        OCR_TRY(readback());
+        Slot& x = sl[b];
+        x.busy = true;
+        x.pg = pg;
+        x.seed = seed;
+        x.made = 0;
+        if (pg.max_new == 1) {  // choice 0 was the page's only token
+            M(3, b) = 0;
+            OCR_TRY(upload());
+        }
+        return OCR_OK;
+    };
+    // a finished page goes back to the caller and frees its slot
+    auto finish = [&](int b) -> ocr_status {
+        Slot& x = sl[b];
+        OCR_TRY(collect(b));
+        x.pg.n_out = x.made;
+        x.busy = false;
+        if (!io->done(io->user, &x.pg)) stop = true;
+        return OCR_OK;
+    };
+    s->pages = true;
+    bool captured = false;
+    while (rc == OCR_OK && !stop) {
+        for (int b = 0; b < B && more && rc == OCR_OK && !stop; b++) {
+            if (sl[b].busy) continue;
+            ocr_page pg{};
+            if (!io->next(io->user, &pg)) {
+                more = false;
+                break;
+            }
+            rc = begin(b, pg);
+            if (rc == OCR_OK && M(3, b) == 0) rc = finish(b);
+        }
+        if (rc != OCR_OK || stop) break;
+        int busy = 0, steps = 0;
+        for (int b = 0; b < B; b++)
+            if (sl[b].busy) {
+                busy++;
+                steps = std::max(steps, M(4, b));
+            }
+        if (!busy) break;
+        steps = std::min(steps, chunk);
+        // the chunk: the captured step, replayed (slots whose budget runs out go idle on the device); the first step
+        // ever runs eagerly, settling every launcher's one-time setup before the capture
+        int i = 0;
+        if (!captured) {
+            record_step(s, true, cfg->rp, cfg->window, cfg->fp > 0.0f ? 1 : 0, cfg->fp);
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) rc = cuda_fail(e, "page step");
+            i = 1;
+            captured = true;
+        }
+        if (rc == OCR_OK && i < steps) rc = capture_graph(s, cfg);
+        for (; i < steps && rc == OCR_OK; i++) {
+            const cudaError_t e = cudaGraphLaunch(s->gexec, st);
+            if (e != cudaSuccess) rc = cuda_fail(e, "cudaGraphLaunch(page step)");
+        }
+        if (rc == OCR_OK) rc = readback();
+        for (int b = 0; b < B && rc == OCR_OK; b++) {
+            if (!sl[b].busy) continue;
+            s->n_past[b] = M(0, b);
+            rc = M(3, b) == 0 ? finish(b) : collect(b);
+        }
+    }
+    s->pages = false;
+    // every slot idle again, positions as the pages left them
+    for (int b = 0; b < B; b++) {
+        M(3, b) = 0;
+        s->has_logits[b] = 0;
+    }
+    if (rc == OCR_OK) rc = upload();
+    if (rc == OCR_OK) OCR_CUDA(cudaStreamSynchronize(st));
+    return rc;
 }
 
 ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, const ocr_sampler_cfg* cfg,

@@ -49,6 +49,19 @@ class KernelTime(C.Structure):
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32)
 
+
+class Page(C.Structure):
+    _fields_ = [("id", C.c_int64), ("ids", C.c_void_p), ("embd", C.c_void_p), ("n_rows", C.c_int32),
+                ("history", C.c_void_p), ("n_hist", C.c_int32), ("max_new", C.c_int32), ("ids_out", C.c_void_p),
+                ("n_out", C.c_int32)]
+
+
+PAGE_CB = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(Page))
+
+
+class PageIO(C.Structure):
+    _fields_ = [("user", C.c_void_p), ("next", PAGE_CB), ("done", PAGE_CB)]
+
 _P = C.c_void_p
 _SIGS = {
     "ocr_last_error": (C.c_char_p, []),
@@ -75,6 +88,7 @@ _SIGS = {
     "ocr_decode": (C.c_int, [_P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, TOKEN_CB, _P, _P,
                              C.POINTER(C.c_int)]),
     "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
+    "ocr_read_pages": (C.c_int, [_P, C.POINTER(SamplerCfg), C.c_int, C.POINTER(PageIO)]),
     "ocr_profile_step": (C.c_int, [_P, _P, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
     "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
@@ -368,6 +382,61 @@ class Session:
         out = np.empty((self.batch, sc.max_new), np.int32)
         _check(lib().ocr_decode_batch(self.h, C.byref(sc), _ptr(h) if h.size else None, h.shape[1], _ptr(out)))
         return out
+
+
+@dataclass
+class PageJob:
+    """a page for Session.read_pages: prompt rows (token ids and/or embedding rows), the window's start, a budget"""
+    id: int
+    embd: Optional[np.ndarray]
+    max_new: int
+    ids: Optional[np.ndarray] = None
+    history: Sequence[int] = ()
+    out: Optional[np.ndarray] = None  # the chosen ids once read
+
+
+def read_pages(sess: "Session", preset: Preset, source: Callable[[], Optional[PageJob]],
+               on_done: Callable[[PageJob], bool], max_new_cap: int, chunk: int = 16) -> None:
+    """ocr_read_pages: pages from `source()` (None = no more) through the session's slots, continuously batched;
+    `on_done(page)` gets each read page (page.out = its ids) and returns False to stop"""
+    sc = preset.sampler(max_new_cap)
+    live: dict[int, tuple] = {}  # page id → (job, the buffers the library reads and writes)
+
+    def _next(_u, pp):
+        try:
+            job = source()
+            if job is None:
+                return 0
+            dim = sess.model.cfg.dim
+            e = None if job.embd is None else np.ascontiguousarray(job.embd, np.float32).reshape(-1, dim)
+            ida = None if job.ids is None else np.ascontiguousarray(job.ids, np.int32)
+            h = np.ascontiguousarray(job.history, np.int32)
+            out = np.zeros(job.max_new, np.int32)
+            n = e.shape[0] if e is not None else ida.size
+            live[job.id] = (job, e, ida, h, out)
+            p = pp.contents
+            p.id, p.ids, p.embd, p.n_rows = job.id, _ptr(ida), _ptr(e), n
+            p.history, p.n_hist, p.max_new, p.ids_out, p.n_out = _ptr(h) if h.size else None, h.size, job.max_new, \
+                _ptr(out), 0
+            return 1
+        except Exception:  # an exception cannot cross the C ABI: no further page
+            import traceback
+            traceback.print_exc()
+            return 0
+
+    def _done(_u, pp):
+        p = pp.contents
+        job, _e, _i, _h, out = live.pop(p.id)
+        job.out = out[: p.n_out].copy()
+        try:
+            return 1 if on_done(job) is not False else 0
+        except Exception:
+            import traceback
+            traceback.print_exc()
+            return 0
+
+    io = PageIO(None, PAGE_CB(_next), PAGE_CB(_done))
+    _check(lib().ocr_read_pages(sess.h, C.byref(sc), chunk, C.byref(io)))
 
 
 def choose_gpu(ctx: Context, d_logits: int, n_vocab: int, preset: Preset, history: Sequence[int],

@@ -136,6 +136,32 @@ ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time*
 ocr_status ocr_decode_batch(ocr_session* s, const ocr_sampler_cfg* cfg, const int32_t* history, int n_hist,
                             int32_t* ids_out);
 
+/* The page engine: Engine::read_text (app/crates/ocr-wgpu/src/engine.rs:447-524) for a stream of pages, one page per
+ * slot of the session at a time (continuous batching). Between chunks of up to `chunk` decode steps, every free slot
+ * takes io->next's page: its rows prefilled (as ocr_prefill), the window seeded from its history (as ocr_decode),
+ * choice 0 from the prefill's logits; then the slot decodes with the others until the page's max_new choices are
+ * made — the budget counts down on the device, so slots end mid-chunk without a host round trip — and io->done gets
+ * the page back with its ids. All pages share cfg's penalties; cfg->max_new bounds every page's max_new. Pages come
+ * and go in the caller's memory: a page's embd / ids / history must stay valid until it is done. Returns when next
+ * has no page and every slot is done, when done returns 0 (pages in other slots are dropped unread), or on error. */
+typedef struct {
+    int64_t id;             /* the caller's page number (echoed back) */
+    const int32_t* ids;     /* prompt rows: token ids (nullable: all rows from embd), as ocr_prefill */
+    const float* embd;      /* [n_rows][dim] embedding rows (Input::Embeddings) */
+    int32_t n_rows;
+    const int32_t* history; /* the window's start, as ocr_decode */
+    int32_t n_hist;
+    int32_t max_new;        /* choices to make (>= 1) */
+    int32_t* ids_out;       /* [max_new] the chosen ids */
+    int32_t n_out;          /* set when done: the ids made */
+} ocr_page;
+typedef struct {
+    void* user;
+    int (*next)(void* user, ocr_page* page); /* fill *page, return 1; or 0 when there is no further page */
+    int (*done)(void* user, ocr_page* page); /* a page is read; return 0 to stop the engine */
+} ocr_page_io;
+ocr_status ocr_read_pages(ocr_session* s, const ocr_sampler_cfg* cfg, int chunk, const ocr_page_io* io);
+
 /* ocr_decode::sampling::choose, greedy branch (sampling.rs:38-62) ≡ choose_pen → choose_max → choose_pick
  * (shaders/choose_*.wgsl) on logits already on the device (d_logits [n_vocab] f32, left unchanged): the windowed
  * penalty over the DISTINCT tokens of history[n_hist - window, n_hist), the frequency penalty over (count_tok,

@@ -179,3 +179,34 @@ def test_config3_batch_ids_match_oracle_and_single_slot(ocr, ctx):
               f"{'identical' if k1 is None else f'near-tie swap at {k1}'}")
         full += kb is None
     assert full >= 1
+
+
+@pytest.mark.parametrize("B", [12, 3])
+def test_page_engine_matches_oracle_per_page(ocr, orc, ctx, B):
+    """ocr_read_pages: 30 pages of different prompt lengths (token rows, some with embedding rows) and budgets
+    through B slots, continuously batched (slots refilled as pages finish, budgets counted down on the device); every
+    page's ids equal the oracle's greedy decode of that page alone"""
+    cfg = BATCH_CFG
+    om = orc.Model(cfg, seed=47, sigma_w=0.2, sigma_e=1.0)
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
+    jobs = []
+    for p in range(30):
+        n = 3 + (p * 7) % 17  # 3 … 19 rows (a few of them short prompts, run as decode steps)
+        ids = np.array([int(t) for t in orc.fill_ids(200 + p, n, cfg["n_vocab"])], np.int32)
+        embd = None
+        if p % 4 == 1:  # rows 1 and 2 as embeddings (Input::Embeddings)
+            ids[1:3] = -1
+            embd = np.zeros((n, cfg["dim"]), np.float32)
+            embd[1:3] = ocr.gauss(300 + p, 2 * cfg["dim"]).reshape(2, -1)
+        jobs.append(ocr.PageJob(p, embd, max_new=1 + (p * 5) % 23, ids=ids, history=[int(t) for t in ids[-8:] if t >= 0]))
+    queue = list(jobs)
+    done = {}
+    sess = gm.session(64, batch=B)
+    ocr.read_pages(sess, ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, 32), lambda: queue.pop(0) if queue else None,
+                   lambda j: done.__setitem__(j.id, j.out.tolist()) or True, max_new_cap=32, chunk=5)
+    assert sorted(done) == list(range(30))
+    for j in jobs:
+        os_ = om.session(64)
+        lo = os_.prefill(j.ids, j.embd, j.ids.size)
+        want = os_.decode(lo, 1.1, 8, 0.0, j.history, j.max_new)[0].tolist()
+        assert done[j.id] == want, (j.id, done[j.id], want)
