@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
                 *reinterpret_cast<__half2*>(vnew + 64 + d0) = v23;
             }
         }
+        // the compute warps only (barrier 1): the copy warp may be waiting for them to free a stage
+        bar_sync(1, AB_WARPS * 32);
     }
-    __syncthreads();
 
     if (warp < AB_WARPS) {
         // ---- the key range, tile by tile ----

@@ -111,6 +111,33 @@ def test_tensor_core_batch_decode_matches_oracle(ocr, orc, ctx, B, heads):
             assert single.decode_gpu(0, ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, n_new), hist[b]) == wants[b], b
 
 
+@pytest.mark.parametrize("B", [12, 32])
+def test_batched_attention_over_many_tiles(ocr, orc, ctx, B):
+    """the batched attention's K/V ring wraps (260-row prefixes: 5 tiles of 64 keys for one CTA per (slot, kv head) at
+    B = 32, several per CTA of a 3-way split at B = 12): four CPU-choice steps, every slot's logits against the
+    oracle's"""
+    cfg = BATCH_CFG
+    om = orc.Model(cfg, seed=53, sigma_w=0.2, sigma_e=1.0)
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 53, 0.2, 1.0)
+    n_pre, n_ctx = 260, 272
+    s = gm.session(n_ctx, batch=B)
+    osns, los = [], []
+    for b in range(B):
+        embd = ocr.gauss(500 + b, n_pre * cfg["dim"]).reshape(n_pre, cfg["dim"])
+        lg = s.prefill(b, embd=embd)
+        os_ = om.session(n_ctx)
+        lo = os_.prefill(None, embd, n_pre)
+        close_logits(lg, lo)
+        osns.append(os_)
+        los.append(lo)
+    for _ in range(4):
+        toks = [int(np.argmax(lo)) for lo in los]
+        lgs = s.step(toks)
+        for b in range(B):
+            los[b] = osns[b].step(toks[b])
+            close_logits(lgs[b], los[b])
+
+
 def test_tensor_core_profile_step(ocr, orc, ctx):
     """the profiler sees the batched step's kernels: per layer prep, qkv, the batched attention, the o-projection,
     prep, gate|up, down; then the LM head's prep and contraction"""
