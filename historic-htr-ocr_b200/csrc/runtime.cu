@@ -60,10 +60,14 @@ namespace {
 
 constexpr size_t STAGE_BYTES = 64u << 20;
 
+// device memory, zeroed before it is returned. cudaMemset on device memory is asynchronous and runs on the legacy
+// stream, which does not order against the contexts' non-blocking streams: without the wait, the zeroing of a buffer
+// grown between two kernels of a context could land after (on top of) the later kernel's writes.
 cudaError_t dalloc(void** p, size_t n, uint64_t* ctr) {
     cudaError_t e = cudaMalloc(p, n ? n : 16);
     if (e != cudaSuccess) return e;
     e = cudaMemset(*p, 0, n ? n : 16);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
     if (ctr) *ctr += n;
     return e;
 }
@@ -90,7 +94,7 @@ ocr_status check_device_error(ocr_ctx* ctx) {
     int err = 0;
     OCR_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err != DEV_OK) {
-        OCR_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        OCR_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(int), ctx->stream));  // (ordered before later kernels)
         return fail(OCR_ERR_DEVICE, err == DEV_BAD_POS     ? "a kernel saw a position outside the KV cache"
                                     : err == DEV_TIMEOUT ? "a kernel's bounded wait ran out (its work was skipped)"
                                                          : "a kernel saw an index outside its buffer");
@@ -1440,7 +1444,8 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     s->active = s->tok + batch;
     s->remaining = s->active + batch;
     const std::vector<float> cs = rope_table(c.rope_base, c.d_head, n_ctx);
-    e = cudaMemcpy(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    e = cudaMemcpyAsync(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e == cudaSuccess) {
         ocr_status st = ensure_hist(s, 4096);
         if (st != OCR_OK) {
@@ -1748,6 +1753,10 @@ ocr_status ocr_read_pages(ocr_session* s, const ocr_sampler_cfg* cfg, int chunk,
     auto collect = [&](int b) -> ocr_status {
         Slot& x = sl[b];
         const int n = M(1, b) - x.seed - x.made;
+        if (n < 0 || x.made + n > x.pg.max_new)
+            return fail(OCR_ERR_DEVICE, "page " + std::to_string(x.pg.id) + ": the slot's history holds " +
+                                            std::to_string(x.made + n) + " choices, its budget is " +
+                                            std::to_string(x.pg.max_new));
         if (n > 0) {
             OCR_CUDA(cudaMemcpy(x.pg.ids_out + x.made, s->hist + (size_t)b * cap + x.seed + x.made, (size_t)n * 4,
                                 cudaMemcpyDeviceToHost));

@@ -280,6 +280,7 @@ struct orc_model {
 struct orc_session {
     const orc_model* m;
     int n_ctx, n_past;
+    int n_layer; /* its own count: a session may be freed after its model */
     uint16_t** k; /* [n_layer] → [n_ctx][kvd] f16 */
     uint16_t** v;
     float* rope; /* [n_ctx][d_head/2][2] */
@@ -368,6 +369,7 @@ orc_session* orc_session_new(const orc_model* m, int n_ctx) {
     orc_session* s = (orc_session*)calloc(1, sizeof(orc_session));
     s->m = m;
     s->n_ctx = n_ctx;
+    s->n_layer = c->n_layer;
     size_t kvd = (size_t)c->n_kv * c->d_head;
     s->k = (uint16_t**)calloc(c->n_layer, sizeof(uint16_t*));
     s->v = (uint16_t**)calloc(c->n_layer, sizeof(uint16_t*));
@@ -382,7 +384,7 @@ orc_session* orc_session_new(const orc_model* m, int n_ctx) {
 
 void orc_session_free(orc_session* s) {
     if (!s) return;
-    for (int l = 0; l < s->m->cfg.n_layer; l++) {
+    for (int l = 0; l < s->n_layer; l++) {
         free(s->k[l]);
         free(s->v[l]);
     }
