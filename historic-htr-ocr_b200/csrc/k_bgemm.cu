@@ -11,17 +11,21 @@
 // so D = w_hi x_hi + w_hi x_lo + w_lo x_hi carries the f32 matvec's result to within f32 rounding; the dropped w_lo x_lo
 // is below 2^-22 of each product.
 //
-// One CTA per SM, persistent over 128-row tiles of W (tile t, t + grid, …), 320 threads in three roles:
+// Work items are 128-row tiles of W — or, for a matrix of few tiles, a tile's share of its 128-column chunks (split-K:
+// every split writes its f32 partial, and the tile's last split to finish, by ticket, sums the partials in split order
+// and runs the epilogue: deterministic, no waiting). One CTA per SM, persistent over items (item w, w + grid, …), 320
+// threads in three roles:
 //  - warp 0 (one lane), the copies: per 128-column chunk of K, one TMA tile of the quants (128 rows x 128 B, 128-B
 //    swizzle, from the row layout through a tensor map) and one bulk copy of the slots' activation chunk (16 KB, already
 //    in the MMA operand order), both counted on the stage's mbarrier; a 128-row tile's block scales once per tile. The
 //    weights of the first stages are issued before griddepcontrol.wait (they never depend on the previous kernel).
-//  - warps 2-9, the dequantisation: per 64-column half chunk, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
-//    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into the A operand buffers in core-matrix order; then, per
-//    tile, the epilogue: tcgen05.ld of their TMEM lanes, hi + lo columns summed, the mode's output.
+//  - warps 2-9, the dequantisation: per 32-column piece, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
+//    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of four A operand buffers in core-matrix order (up
+//    to three pieces ahead of the tensor cores); then, per work item, the epilogue: tcgen05.ld of their TMEM lanes, hi
+//    + lo columns summed, the mode's output.
 //  - warp 1, the tensor cores: TMEM allocation (64 columns: 32 slots' hi products + 32 slots' lo products), and per
 //    16-column step two MMAs (M = 128): A = w_hi with B = [x_hi | x_lo] (N = 64), A = w_lo with B = x_hi (N = 32) into the
-//    first 32 columns; tcgen05.commit releases the operand buffer, the copy stage, and at a tile's end the accumulator
+//    first 32 columns; tcgen05.commit releases the operand buffer, the copy stage, and at an item's end the accumulator
 //    to the epilogue.
 // Every mbarrier wait is bounded; a wait that runs out sets the device error flag and a shared abort flag that every
 // role polls; the copies in flight and the MMAs issued are then waited for (bounded) and the TMEM is freed before the
@@ -35,14 +39,14 @@ namespace ocr {
 
 constexpr int BG_M = 128;       // weight rows per tile: the MMA's M, one TMEM lane each
 constexpr int BG_KC = 128;      // K columns per copy stage
-constexpr int BG_KS = 64;       // K columns per dequantised operand buffer
+constexpr int BG_KS = 32;       // K columns per dequantised operand buffer
 constexpr int BG_THREADS = 320;
 constexpr int BG_DQ = 256;      // dequantisation / epilogue threads (warps 2-9)
 constexpr uint32_t BG_WTILE = BG_M * BG_KC;                 // 16 KB of int8 quants
 constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 32 KB
-constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of one half chunk
+constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 8 KB: the hi (or lo) f16 operand of a 32-column piece
 constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
-constexpr int BG_NA = 2;        // operand buffers
+constexpr int BG_NA = 4;        // operand buffers (the dequantisation runs up to 3 ahead of the tensor cores)
 constexpr int BG_MAX_NS = 4;    // copy stages
 constexpr uint32_t BG_TMEM_COLS = 64;
 constexpr int BG_SMEM_OPTIN = 227 * 1024;
@@ -141,15 +145,30 @@ struct BgShared {
     uint64_t tfull[BG_MAX_NS], tempty[BG_MAX_NS];  // copy stage landed / free again (MMAs done)
     uint64_t afull[BG_NA], aempty[BG_NA];          // operand buffer written / free again
     uint64_t sfull[2], sempty[2];                  // a tile's block scales landed / read
-    uint64_t tfin, mdone;                          // a tile's accumulator complete; every MMA done (exit)
+    uint64_t tfin, mdone;                          // an item's accumulator complete; every MMA done (exit)
     uint32_t tmem_base;
     int abort_flag;
+    uint32_t ticket;                      // split items: this CTA's place among the tile's splits
     uint32_t pbits[BG_SLOTS][BG_M / 32];  // LM head: the tile's rows in each slot's penalty window
     float bvq[8][16];                     // LM head: each epilogue warp's best per slot
     uint32_t biq[8][16];
     float bv[BG_SLOTS];
     uint32_t bi[BG_SLOTS];
 };
+
+// Work items: item w is (tile w / ksplit, split w % ksplit); a split covers chunks [c0, c1) of the K/128 chunks.
+// A CTA takes items blockIdx.x, blockIdx.x + gridDim.x, … (the LM head: every tile, one split).
+struct BgItem {
+    int t, sp, c0, c1;
+};
+__device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
+    BgItem it;
+    it.t = w / ksplit;
+    it.sp = w % ksplit;
+    it.c0 = (int)((long)nkc * it.sp / ksplit);
+    it.c1 = (int)((long)nkc * (it.sp + 1) / ksplit);
+    return it;
+}
 
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const __grid_constant__ CUtensorMap mq,
@@ -159,7 +178,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     volatile int* abort_flag = &sh.abort_flag;
 
     const int K = a.w.cols, N = a.w.rows;
-    const int nkc = K / BG_KC;
+    const int nkc = K / BG_KC, ksplit = a.ksplit;
     const int sbytes = BG_M * (K / 16);  // a tile's block scales (TMA box K/16 x 128 rows)
     const int sstride = (sbytes + 1023) & ~1023;
     // the dynamic region starts 1024-B aligned (the 128-B swizzle's pattern repeats every 1024 B)
@@ -167,7 +186,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     uint8_t* stage0 = smp;
     uint8_t* abuf0 = smp + (size_t)ns * BG_STAGE;
     uint8_t* sbuf0 = abuf0 + BG_NA * BG_ABUF;
-    const int n_tiles = (N + BG_M - 1) / BG_M;
+    const int n_tiles = (N + BG_M - 1) / BG_M, n_items = n_tiles * ksplit;
     const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -207,32 +226,33 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             prefetch_tmap(&mq);
             prefetch_tmap(&ms);
             uint32_t g = 0;
-            int li = 0, s_issued = 0;
-            int pre = 0;
-            const int t0 = blockIdx.x;
-            if (t0 < n_tiles) {
-                // before the dependency wait: the first tile's scales and the quants of the first stages
+            int li = 0, s_issued = 0, pre = 0;
+            const int w0 = blockIdx.x;
+            if (w0 < n_items) {
+                // before the dependency wait: the first item's scales and the quants of its first stages
+                const BgItem it = bg_item(w0, ksplit, nkc);
                 mbar_expect_tx(&sh.sfull[0], (uint32_t)sbytes);
-                tma_2d(sbuf0, &ms, 0, t0 * BG_M, &sh.sfull[0], pol);
+                tma_2d(sbuf0, &ms, 0, it.t * BG_M, &sh.sfull[0], pol);
                 s_issued = 1;
-                pre = min(ns, nkc);
+                pre = min(ns, it.c1 - it.c0);
                 for (int s = 0; s < pre; s++) {
                     mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                    tma_2d(stage0 + (size_t)s * BG_STAGE, &mq, s * BG_KC, t0 * BG_M, &sh.tfull[s], pol);
+                    tma_2d(stage0 + (size_t)s * BG_STAGE, &mq, (it.c0 + s) * BG_KC, it.t * BG_M, &sh.tfull[s], pol);
                 }
             }
             pdl_trigger();
             pdl_wait();
             bool ok = true;
-            for (int t = t0; t < n_tiles && ok; t += gridDim.x, li++) {
+            for (int w = w0; w < n_items && ok; w += gridDim.x, li++) {
+                const BgItem it = bg_item(w, ksplit, nkc);
                 const int sb = li & 1;
                 if (li > 0) {
                     if (li >= 2 && !bg_wait(&sh.sempty[sb], ((li >> 1) - 1) & 1, abort_flag, a.err)) break;
                     mbar_expect_tx(&sh.sfull[sb], (uint32_t)sbytes);
-                    tma_2d(sbuf0 + (size_t)sb * sstride, &ms, 0, t * BG_M, &sh.sfull[sb], pol);
+                    tma_2d(sbuf0 + (size_t)sb * sstride, &ms, 0, it.t * BG_M, &sh.sfull[sb], pol);
                     s_issued = li + 1;
                 }
-                for (int kc = 0; kc < nkc; kc++, g++) {
+                for (int kc = it.c0; kc < it.c1; kc++, g++) {
                     const int s = (int)(g % (uint32_t)ns);
                     uint8_t* st = stage0 + (size_t)s * BG_STAGE;
                     if (g >= (uint32_t)pre) {  // (the prologue issued the quants of the first `pre` stages)
@@ -241,13 +261,12 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                             break;
                         }
                         mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                        tma_2d(st, &mq, kc * BG_KC, t * BG_M, &sh.tfull[s], pol);
+                        tma_2d(st, &mq, kc * BG_KC, it.t * BG_M, &sh.tfull[s], pol);
                     }
                     bulk_g2s(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.tfull[s]);
                 }
             }
-            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete);
-            // a stage whose activations were never issued (an abort between its quants and them) is not waited for
+            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete)
             const uint32_t issued = max(g, (uint32_t)pre);
             for (int s = 0; s < ns && (uint32_t)s < issued; s++) {
                 const uint32_t n = (issued - s + ns - 1) / ns;
@@ -263,15 +282,16 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const uint32_t id1 = bg_idesc(64), id2 = bg_idesc(32);
             uint32_t g = 0, ai = 0;
             bool any = false, ok = true;
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                for (int kc = 0; kc < nkc && ok; kc++, g++) {
+            for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+                const BgItem it = bg_item(w, ksplit, nkc);
+                for (int kc = it.c0; kc < it.c1 && ok; kc++, g++) {
                     const int s = (int)(g % (uint32_t)ns);
                     if (!bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
                     const uint32_t xs = smem_u32(stage0 + (size_t)s * BG_STAGE + BG_WTILE);
-                    for (int h = 0; h < 2; h++, ai++) {
+                    for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                         const int ab = (int)(ai % BG_NA);
                         if (!bg_wait(&sh.afull[ab], (ai / BG_NA) & 1, abort_flag, a.err)) {
                             ok = false;
@@ -281,10 +301,11 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                         const uint32_t ah = smem_u32(abuf0 + (size_t)ab * BG_ABUF), al = ah + BG_AHALF;
 #pragma unroll
                         for (int ks = 0; ks < BG_KS / 16; ks++) {
-                            const uint64_t dh = bg_desc(ah + ks * 256, 128, 1024);
-                            const uint64_t dl = bg_desc(al + ks * 256, 128, 1024);
-                            const uint64_t db = bg_desc(xs + (h * 4 + ks) * 256, 128, 2048);
-                            mma_f16(tmem, dh, db, id1, (kc | h | ks) != 0);
+                            // A: 16 groups of 8 rows, BG_KS / 8 cores each (SBO); B: the chunk's 64 rows
+                            const uint64_t dh = bg_desc(ah + ks * 256, 128, BG_KS * 16);
+                            const uint64_t dl = bg_desc(al + ks * 256, 128, BG_KS * 16);
+                            const uint64_t db = bg_desc(xs + (h * (BG_KS / 16) + ks) * 256, 128, 2048);
+                            mma_f16(tmem, dh, db, id1, (kc != it.c0 || h || ks) ? 1u : 0u);
                             mma_f16(tmem, dl, db, id2, 1u);
                         }
                         mma_commit(&sh.aempty[ab]);
@@ -325,36 +346,35 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         uint32_t g = 0, ai = 0;
         int li = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, li++) {
+        for (int w = blockIdx.x; w < n_items; w += gridDim.x, li++) {
+            const BgItem it = bg_item(w, ksplit, nkc);
             const int sb = li & 1;
             ok = ok && bg_wait(&sh.sfull[sb], (li >> 1) & 1, abort_flag, a.err);
             const uint8_t* sc = sbuf0 + (size_t)sb * sstride;
-            for (int kc = 0; kc < nkc; kc++, g++) {
+            for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
                 ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
                 const uint8_t* wt = stage0 + (size_t)s * BG_STAGE;
-                for (int h = 0; h < 2; h++, ai++) {
+                for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                     const int ab = (int)(ai % BG_NA);
                     ok = ok && (ai < BG_NA || bg_wait(&sh.aempty[ab], ((ai / BG_NA) - 1) & 1, abort_flag, a.err));
                     if (!ok) continue;
                     uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
-#pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        // item i: rows 8 rg + r8, 16 columns c4 of the half chunk; a quarter-warp takes 8 rows of one
-                        // 16-column piece (conflict-free reads through the swizzle, 128 contiguous bytes written)
-                        const int i = et + BG_DQ * j, r8 = i & 7, c4 = (i >> 3) & 3, rg = i >> 5, row = rg * 8 + r8;
-                        const int ch = h * 4 + c4;
-                        const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
-                        const int blk = (kc * BG_KC + h * BG_KS + c4 * 16) >> 5;
-                        const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
-                        uint32_t hi[8], lo[8];
-                        dequant16(qv, d, hi, lo);
-                        const int off = (rg * 8 + c4 * 2) * 128 + r8 * 16;
-                        *reinterpret_cast<uint4*>(ah + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(ah + off + 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                        *reinterpret_cast<uint4*>(ah + BG_AHALF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                        *reinterpret_cast<uint4*>(ah + BG_AHALF + off + 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-                    }
+                    // one item per thread: rows 8 rg + r8, 16 columns c2 of the 32-column piece; a quarter-warp takes
+                    // 8 rows of one 16-column piece (conflict-free reads through the swizzle, 128 contiguous bytes
+                    // written per core)
+                    const int i = et, r8 = i & 7, c2 = (i >> 3) & 1, rg = i >> 4, row = rg * 8 + r8;
+                    const int ch = h * 2 + c2;
+                    const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
+                    const int blk = (kc * BG_KC + h * BG_KS + c2 * 16) >> 5;
+                    const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
+                    uint32_t hi[8], lo[8];
+                    dequant16(qv, d, hi, lo);
+                    const int off = (rg * (BG_KS / 8) + c2 * 2) * 128 + r8 * 16;
+                    *reinterpret_cast<uint4*>(ah + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4*>(ah + off + 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    *reinterpret_cast<uint4*>(ah + BG_AHALF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(ah + BG_AHALF + off + 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                     fence_proxy_async();  // the generic stores, before the tensor cores read them
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sh.afull[ab]);
@@ -363,8 +383,8 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&sh.sempty[sb]);
 
-            // ---- the tile's epilogue ----
-            const int r0 = t * BG_M, row = r0 + 32 * q + lane;
+            // ---- the item's epilogue ----
+            const int r0 = it.t * BG_M, row = r0 + 32 * q + lane;
             if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {
                 // the window's tokens that fall in this tile, per slot (the 256 epilogue threads, barrier 2)
                 uint32_t* pb = &sh.pbits[0][0];
@@ -382,17 +402,42 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 bar_sync(2, BG_DQ);
             }
             ok = ok && bg_wait(&sh.tfin, li & 1, abort_flag, a.err);
-            if (!ok) continue;
-            tc_fence_after();
-            uint32_t rh[16], rl[16];
-            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
-            tmem_ld16(ta + 16 * half, rh);
-            tmem_ld16(ta + 32 + 16 * half, rl);
-            tmem_wait_ld();
-            tc_fence_before();  // these reads, before the next tile's MMAs overwrite the accumulator
             float y[16];
 #pragma unroll
-            for (int j = 0; j < 16; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+            for (int j = 0; j < 16; j++) y[j] = 0.0f;
+            if (ok) {
+                tc_fence_after();
+                uint32_t rh[16], rl[16];
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
+                tmem_ld16(ta + 16 * half, rh);
+                tmem_ld16(ta + 32 + 16 * half, rl);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+            }
+            tc_fence_before();  // these reads, before the next item's MMAs overwrite the accumulator
+            if (ksplit > 1) {
+                // this split's share → the tile's partials [group][tile][split][32 slots][128 rows]; the last split
+                // of the tile to arrive (ticket; no waiting) sums them in split order and runs the epilogue
+                float* pt = a.part + (((size_t)grp * n_tiles + it.t) * ksplit) * (BG_SLOTS * BG_M);
+#pragma unroll
+                for (int j = 0; j < 16; j++) pt[(size_t)it.sp * BG_SLOTS * BG_M + (16 * half + j) * BG_M + 32 * q + lane] = y[j];
+                __threadfence();
+                bar_sync(2, BG_DQ);
+                if (et == 0) sh.ticket = atomicAdd(&a.tickets[grp * n_tiles + it.t], 1u);
+                bar_sync(2, BG_DQ);
+                if (sh.ticket != (uint32_t)ksplit - 1) continue;  // (uniform over the epilogue warps)
+                __threadfence();
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    float v = 0.0f;
+                    for (int r = 0; r < ksplit; r++)
+                        v += __ldcg(pt + (size_t)r * BG_SLOTS * BG_M + (16 * half + j) * BG_M + 32 * q + lane);
+                    y[j] = v;
+                }
+                if (et == 0) a.tickets[grp * n_tiles + it.t] = 0u;  // (self-resetting for the next launch)
+            }
+            if (!ok) continue;
             if (a.mode == MV_SWIGLU) {
                 // rows interleaved (gate, up): the even lane of each pair writes silu(gate) * up
                 const int col = row >> 1;
@@ -572,7 +617,20 @@ __global__ void __launch_bounds__(XP_THREADS) k_xprep(PrepArgs a) {
 // ---- host ----------------------------------------------------------------------------------------------------------------
 bool bgemm_shape_ok(int rows, int cols) { return rows >= 1 && cols >= 256 && cols % 256 == 0 && cols <= 4096; }
 
-int bgemm_grid(int num_sms, int rows) { return std::max(1, std::min((rows + BG_M - 1) / BG_M, num_sms)); }
+int bgemm_grid(int num_sms, int rows, int ksplit) {
+    return std::max(1, std::min((rows + BG_M - 1) / BG_M * ksplit, num_sms));
+}
+
+int bgemm_ksplit(int num_sms, int rows, int cols) {
+    const int tiles = (rows + BG_M - 1) / BG_M, nkc = cols / BG_KC;
+    return std::max(1, std::min(nkc, num_sms / tiles));
+}
+
+size_t bgemm_part_floats(int rows, int ksplit) {
+    return ksplit > 1 ? (size_t)((rows + BG_M - 1) / BG_M) * ksplit * BG_SLOTS * BG_M : 0;
+}
+
+int bgemm_tickets(int rows) { return (rows + BG_M - 1) / BG_M; }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* why) {
     static std::mutex mu;
@@ -645,7 +703,7 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     const int fixed = BG_NA * (int)BG_ABUF + 2 * sstride + 1024;  // + the 1024-B alignment slack
     const int ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
+    cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
     cfg.blockDim = dim3(BG_THREADS, 1, 1);
     cfg.dynamicSmemBytes = (size_t)fixed + (size_t)ns * BG_STAGE;
     cfg.stream = st;

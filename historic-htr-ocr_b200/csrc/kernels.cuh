@@ -240,14 +240,25 @@ struct BgArgs {
     int nb = 1;                    // slots (blockIdx.y takes groups of BG_SLOTS)
     const int32_t* active = nullptr;
     LmArgs lm;                     // MV_LMHEAD: the choice (lm.nb = nb, partials [nb][grid])
+    // split-K: each 128-row tile's K chunks shared by ksplit CTAs, whose f32 partials [groups][tiles][ksplit][32][128]
+    // the tile's last CTA sums in split order (tickets [groups][tiles], zero between launches); 1 = no split
+    int ksplit = 1;
+    float* part = nullptr;
+    uint32_t* tickets = nullptr;
     int* err = nullptr;
 };
 // true when the tensor-core contraction takes this shape (cols a multiple of 256, at most 4096)
 bool bgemm_shape_ok(int rows, int cols);
 // the two tensor maps of a matrix (false + *why when the driver refuses them)
 bool bgemm_maps(const QMat& w, BgMaps* m, std::string* why);
-// CTAs of a launch: one per 128-row tile, at most one per SM (a persistent CTA takes tiles blockIdx.x + k * grid)
-int bgemm_grid(int num_sms, int rows);
+// CTAs of a launch: one per work item (a 128-row tile's split), at most one per SM (a persistent CTA takes items
+// blockIdx.x + k * grid)
+int bgemm_grid(int num_sms, int rows, int ksplit = 1);
+// the K split for a matrix: enough items to give every SM one (at most one per 128-column chunk); 1 for the LM head
+int bgemm_ksplit(int num_sms, int rows, int cols);
+// scratch of a split launch: partial floats and tickets per slot group
+size_t bgemm_part_floats(int rows, int ksplit);
+int bgemm_tickets(int rows);
 void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms, bool pdl);
 
 // The activations of a batch as the contraction's operand: per slot x (+ the partial products in order, or the token's

@@ -491,6 +491,8 @@ struct ocr_session {
     uint8_t* x16o = nullptr;    // [groups] operands of width n_head x 128 (the attention's output)
     float* ab_part = nullptr;   // [B * n_kv][split][G][132] partials (split > 1)
     uint32_t* ab_done = nullptr;  // [B * n_kv] tickets
+    float* bg_part = nullptr;     // the split contractions' partials (sized for the largest)
+    uint32_t* bg_tickets = nullptr;
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -593,6 +595,11 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
         g.nb = s->B;
         g.active = s->active;
         g.err = ctx->d_err;
+        if (mode != MV_LMHEAD) {
+            g.ksplit = bgemm_ksplit(ctx->num_sms, w.rows, w.cols);
+            g.part = s->bg_part;
+            g.tickets = s->bg_tickets;
+        }
         return g;
     };
     for (int l = 0; l < c.n_layer; l++) {
@@ -1399,6 +1406,19 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_abp = battn && ab_split > 1
                              ? p.take((size_t)batch * c.n_kv * ab_split * (c.n_head / c.n_kv) * 132 * 4) : 0;
     const size_t o_abd = battn ? p.take((size_t)batch * c.n_kv * 4) : 0;
+    // the split-K contractions' partials and tickets: the largest of the layer's matrices, per slot group
+    size_t bg_floats = 0;
+    int bg_tk = 0;
+    if (tc) {
+        const int qd = c.n_head * c.d_head, rows[4] = {qd + 2 * c.n_kv * c.d_head, c.dim, 2 * c.n_ff, c.dim},
+                  cols[4] = {c.dim, qd, c.dim, c.n_ff};
+        for (int i = 0; i < 4; i++) {
+            bg_floats = std::max(bg_floats, bgemm_part_floats(rows[i], bgemm_ksplit(ctx->num_sms, rows[i], cols[i])));
+            bg_tk = std::max(bg_tk, bgemm_tickets(rows[i]));
+        }
+    }
+    const size_t o_bgp = tc ? p.take(groups * bg_floats * 4) : 0;
+    const size_t o_bgt = tc ? p.take(groups * (size_t)bg_tk * 4) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
     const size_t o_g = p.take((size_t)batch * c.n_ff * 4);
@@ -1424,6 +1444,10 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         s->tc = true;
         s->x16a = (uint8_t*)(w + o_x16a);
         s->x16g = (uint8_t*)(w + o_x16g);
+    }
+    if (tc) {
+        s->bg_part = (float*)(w + o_bgp);
+        s->bg_tickets = (uint32_t*)(w + o_bgt);
     }
     if (battn) {
         s->battn = true;
@@ -1967,7 +1991,11 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int co
         std::string why;
         if (!bgemm_maps(w, &maps, &why)) return fail(OCR_ERR_CUDA, why);
         const size_t groups = (size_t)(nb + BG_SLOTS - 1) / BG_SLOTS;
-        OCR_TRY(ensure_op_scratch(ctx, groups * x16_group_bytes(cols)));
+        const int ksplit = bgemm_ksplit(ctx->num_sms, rows, cols);
+        const size_t xb = groups * x16_group_bytes(cols), pb = groups * bgemm_part_floats(rows, ksplit) * 4,
+                     tb = groups * (size_t)bgemm_tickets(rows) * 4;
+        OCR_TRY(ensure_op_scratch(ctx, xb + pb + tb));
+        OCR_CUDA(cudaMemsetAsync((char*)ctx->op_scratch + xb + pb, 0, tb, ctx->stream));
         PrepArgs p;
         p.x = d_x;
         p.x_stride = cols;
@@ -1986,6 +2014,9 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int co
         g.y_stride = rows;
         g.nb = nb;
         g.err = ctx->d_err;
+        g.ksplit = ksplit;
+        g.part = (float*)((char*)ctx->op_scratch + xb);
+        g.tickets = (uint32_t*)((char*)ctx->op_scratch + xb + pb);
         launch_bgemm(ctx->stream, g, maps, ctx->num_sms, false);
         OCR_CUDA(cudaGetLastError());
         return OCR_OK;

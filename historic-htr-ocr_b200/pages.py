@@ -13,6 +13,7 @@ methods):
     <ns>rq_n, <ns>rq/<i>  pages given back: a dead rank's unfinished pages
     <ns>rqc/<i>           the claim of requeued entry i (first compare_set wins)
     <ns>reaped/<r>        the survivor that requeued dead rank r's pages (first compare_set wins)
+    <ns>left/<r>          rank r is gone (the store's host waits for the others before it goes)
 
 A rank whose heartbeat is older than `hb_timeout` and that has not declared itself finished is dead: the first
 survivor to notice it requeues the pages it held and did not finish, and every rank keeps claiming until all pages are
@@ -167,6 +168,23 @@ class PageQueue:
 
     def pending_requeued(self) -> bool:
         return self.s.add(self._k("rq_n"), 0) > self.rq_seen
+
+    def leave(self, host_rank: int = 0, poll: float = 0.05, deadline: float = 60.0) -> None:
+        """the end of this rank's part: it marks itself gone; the rank that hosts the store (rank 0 of a
+        torch.distributed rendezvous) waits until every other rank is gone or dead before it returns, so the store
+        outlives their last reads"""
+        self.s.set(self._k("left", self.rank), "1")
+        if self.rank != host_rank:
+            return
+        t_end = time.time() + deadline
+        while time.time() < t_end:
+            pending = [r for r in range(self.world) if r != self.rank and not self._has(self._k("left", r))]
+            now = time.time()
+            alive = [r for r in pending
+                     if self._has(self._k("hb", r)) and now - float(self.s.get(self._k("hb", r))) < self.hb_timeout]
+            if not alive:
+                return
+            time.sleep(poll)
 
 
 def run_worker(read: Callable[[Callable[[], Optional[int]], Callable[[int, int], bool]], None], q: PageQueue,

@@ -68,6 +68,7 @@ def _rank_main(rank, world, port, n_pages, die_rank, die_after, out_path):
     owners = {p: store.get(f"t/done/{p}").decode() for p in range(n_pages)}
     with open(out_path + f".rank{rank}", "w") as f:
         json.dump({"read": read_here, "n_done": q.n_done(), "tokens": q.tokens(), "owners": owners}, f)
+    q.leave()
     os._exit(0)
 
 
