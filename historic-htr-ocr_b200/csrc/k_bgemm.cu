@@ -19,10 +19,10 @@
 //    swizzle, from the row layout through a tensor map) and one bulk copy of the slots' activation chunk (16 KB, already
 //    in the MMA operand order), both counted on the stage's mbarrier; a 128-row tile's block scales once per tile. The
 //    weights of the first stages are issued before griddepcontrol.wait (they never depend on the previous kernel).
-//  - warps 2-9, the dequantisation: per 32-column piece, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
-//    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of four A operand buffers in core-matrix order (up
-//    to three pieces ahead of the tensor cores); then, per work item, the epilogue: tcgen05.ld of their TMEM lanes, hi
-//    + lo columns summed, the mode's output.
+//  - warps 2-9, the dequantisation: per 64-column piece, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
+//    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of 2 to 4 A operand buffers in the 128-byte-swizzle
+//    K-major layout the tensor cores read without bank conflicts; then, per work item, the epilogue: tcgen05.ld of
+//    their TMEM lanes, hi + lo columns summed, the mode's output.
 //  - warp 1, the tensor cores: TMEM allocation (64 columns: 32 slots' hi products + 32 slots' lo products), and per
 //    16-column step two MMAs (M = 128): A = w_hi with B = [x_hi | x_lo] (N = 64), A = w_lo with B = x_hi (N = 32) into the
 //    first 32 columns; tcgen05.commit releases the operand buffer, the copy stage, and at an item's end the accumulator
@@ -39,14 +39,14 @@ namespace ocr {
 
 constexpr int BG_M = 128;       // weight rows per tile: the MMA's M, one TMEM lane each
 constexpr int BG_KC = 128;      // K columns per copy stage
-constexpr int BG_KS = 32;       // K columns per dequantised operand buffer
+constexpr int BG_KS = 64;       // K columns per dequantised operand buffer (one 128-byte swizzle atom wide)
 constexpr int BG_THREADS = 320;
 constexpr int BG_DQ = 256;      // dequantisation / epilogue threads (warps 2-9)
 constexpr uint32_t BG_WTILE = BG_M * BG_KC;                 // 16 KB of int8 quants
 constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 32 KB
-constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 8 KB: the hi (or lo) f16 operand of a 32-column piece
+constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of a 64-column piece
 constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
-constexpr int BG_NA = 4;        // operand buffers (the dequantisation runs up to 3 ahead of the tensor cores)
+constexpr int BG_NA = 4;        // operand buffers at most (2 to 4, as shared memory allows)
 constexpr int BG_MAX_NS = 4;    // copy stages
 constexpr uint32_t BG_TMEM_COLS = 64;
 constexpr int BG_SMEM_OPTIN = 227 * 1024;
@@ -57,11 +57,13 @@ constexpr int BG_SMEM_OPTIN = 227 * 1024;
 __host__ __device__ constexpr uint32_t bg_idesc(int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BG_M >> 4) << 24);
 }
-// shared-memory matrix descriptor, K-major without swizzle: start >> 4, `lbo` = bytes to the next 8-column core along
-// K, `sbo` = bytes to the next group of 8 rows, descriptor version 1 (bit 46) of sm_100
-__device__ __forceinline__ uint64_t bg_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
-           (1ull << 46);
+// shared-memory matrix descriptor, K-major with the 128-byte swizzle: rows 128 bytes apart in atoms of 8 rows (the
+// stride to the next atom, 1024 bytes, at bit 32 in 16-byte units; the leading offset is unused for this layout and
+// set to 1), descriptor version 1 (bit 46) of sm_100, layout type 2 (bits 61-63). The start may sit at 32-byte steps
+// inside a 1024-byte aligned atom: the 16-column K steps of one 64-column atom.
+__device__ __forceinline__ uint64_t bg_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t cols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
@@ -172,7 +174,7 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
 
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const __grid_constant__ CUtensorMap mq,
-            const __grid_constant__ CUtensorMap ms, int ns) {
+            const __grid_constant__ CUtensorMap ms, int ns, int na) {
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(16) BgShared sh;
     volatile int* abort_flag = &sh.abort_flag;
@@ -185,7 +187,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
     uint8_t* stage0 = smp;
     uint8_t* abuf0 = smp + (size_t)ns * BG_STAGE;
-    uint8_t* sbuf0 = abuf0 + BG_NA * BG_ABUF;
+    uint8_t* sbuf0 = abuf0 + (size_t)na * BG_ABUF;
     const int n_tiles = (N + BG_M - 1) / BG_M, n_items = n_tiles * ksplit;
     const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             mbar_init(&sh.tfull[i], 1);
             mbar_init(&sh.tempty[i], 1);
         }
-        for (int i = 0; i < BG_NA; i++) {
+        for (int i = 0; i < na; i++) {
             mbar_init(&sh.afull[i], BG_DQ / 32);
             mbar_init(&sh.aempty[i], 1);
         }
@@ -292,8 +294,8 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     }
                     const uint32_t xs = smem_u32(stage0 + (size_t)s * BG_STAGE + BG_WTILE);
                     for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
-                        const int ab = (int)(ai % BG_NA);
-                        if (!bg_wait(&sh.afull[ab], (ai / BG_NA) & 1, abort_flag, a.err)) {
+                        const int ab = (int)(ai % na);
+                        if (!bg_wait(&sh.afull[ab], (ai / na) & 1, abort_flag, a.err)) {
                             ok = false;
                             break;
                         }
@@ -301,10 +303,10 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                         const uint32_t ah = smem_u32(abuf0 + (size_t)ab * BG_ABUF), al = ah + BG_AHALF;
 #pragma unroll
                         for (int ks = 0; ks < BG_KS / 16; ks++) {
-                            // A: 16 groups of 8 rows, BG_KS / 8 cores each (SBO); B: the chunk's 64 rows
-                            const uint64_t dh = bg_desc(ah + ks * 256, 128, BG_KS * 16);
-                            const uint64_t dl = bg_desc(al + ks * 256, 128, BG_KS * 16);
-                            const uint64_t db = bg_desc(xs + (h * (BG_KS / 16) + ks) * 256, 128, 2048);
+                            // 16 columns = 32 bytes into the swizzle atoms: A's 128 rows, B's 64 rows (half h)
+                            const uint64_t dh = bg_desc(ah + ks * 32);
+                            const uint64_t dl = bg_desc(al + ks * 32);
+                            const uint64_t db = bg_desc(xs + h * 8192 + ks * 32);
                             mma_f16(tmem, dh, db, id1, (kc != it.c0 || h || ks) ? 1u : 0u);
                             mma_f16(tmem, dl, db, id2, 1u);
                         }
@@ -356,25 +358,28 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
                 const uint8_t* wt = stage0 + (size_t)s * BG_STAGE;
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
-                    const int ab = (int)(ai % BG_NA);
-                    ok = ok && (ai < BG_NA || bg_wait(&sh.aempty[ab], ((ai / BG_NA) - 1) & 1, abort_flag, a.err));
+                    const int ab = (int)(ai % na);
+                    ok = ok && (ai < (uint32_t)na || bg_wait(&sh.aempty[ab], ((ai / na) - 1) & 1, abort_flag, a.err));
                     if (!ok) continue;
                     uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
-                    // one item per thread: rows 8 rg + r8, 16 columns c2 of the 32-column piece; a quarter-warp takes
-                    // 8 rows of one 16-column piece (conflict-free reads through the swizzle, 128 contiguous bytes
-                    // written per core)
-                    const int i = et, r8 = i & 7, c2 = (i >> 3) & 1, rg = i >> 4, row = rg * 8 + r8;
-                    const int ch = h * 2 + c2;
-                    const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
-                    const int blk = (kc * BG_KC + h * BG_KS + c2 * 16) >> 5;
-                    const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
-                    uint32_t hi[8], lo[8];
-                    dequant16(qv, d, hi, lo);
-                    const int off = (rg * (BG_KS / 8) + c2 * 2) * 128 + r8 * 16;
-                    *reinterpret_cast<uint4*>(ah + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4*>(ah + off + 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                    *reinterpret_cast<uint4*>(ah + BG_AHALF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                    *reinterpret_cast<uint4*>(ah + BG_AHALF + off + 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        // item i: rows 8 rg + r8, 16 columns c4 of the 64-column piece; a quarter-warp takes 8 rows
+                        // of one 16-column piece: its reads through the copy's swizzle and its writes through the
+                        // operand's (piece 2 c4 and 2 c4 + 1 of a row at (piece ^ row % 8)) are both conflict-free
+                        const int i = et + BG_DQ * j, r8 = i & 7, c4 = (i >> 3) & 3, rg = i >> 5, row = rg * 8 + r8;
+                        const int ch = h * 4 + c4;
+                        const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
+                        const int blk = (kc * BG_KC + h * BG_KS + c4 * 16) >> 5;
+                        const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
+                        uint32_t hi[8], lo[8];
+                        dequant16(qv, d, hi, lo);
+                        const int o0 = row * 128 + (((2 * c4) ^ r8) << 4), o1 = row * 128 + (((2 * c4 + 1) ^ r8) << 4);
+                        *reinterpret_cast<uint4*>(ah + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(ah + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        *reinterpret_cast<uint4*>(ah + BG_AHALF + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4*>(ah + BG_AHALF + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
                     fence_proxy_async();  // the generic stores, before the tensor cores read them
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sh.afull[ab]);
@@ -700,7 +705,11 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     });
     const int K = a.w.cols;
     const int sstride = (BG_M * (K / 16) + 1023) & ~1023;
-    const int fixed = BG_NA * (int)BG_ABUF + 2 * sstride + 1024;  // + the 1024-B alignment slack
+    // shared memory: ns copy stages, na operand buffers, two tiles' scales (+ the 1024-B alignment slack): as many
+    // operand buffers as fit beside 3 stages (2 at K = 3072 and 4096), then as many stages as fit
+    const int room = BG_SMEM_OPTIN - bg_static_smem() - 2 * sstride - 1024;
+    const int na = std::max(2, std::min(BG_NA, (room - 3 * (int)BG_STAGE) / (int)BG_ABUF));
+    const int fixed = na * (int)BG_ABUF + 2 * sstride + 1024;
     const int ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
@@ -712,7 +721,7 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.q, m.s, ns);
+    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.q, m.s, ns, na);
 }
 
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl) {

@@ -214,14 +214,15 @@ int attention_splits(int num_sms, int nb, int n_kv, int n_ctx);
 // below 2^-22 of the product).
 //
 // The activation operand ("x16") of a group of BG_SLOTS slots over K columns is K/128 chunks of BG_CHUNK_BYTES:
-// rows n < 32 hold f16(x[slot n]) (hi), rows 32 + n hold f16(x - hi) (lo), for the chunk's 128 columns, in tcgen05's
-// K-major core-matrix order without swizzle — core (n / 8, (k % 128) / 8) is 128 contiguous bytes, 8 rows of 8
-// halves — so one bulk copy of a chunk is an MMA operand as it lands.
+// rows n < 32 hold f16(x[slot n]) (hi), rows 32 + n hold f16(x - hi) (lo). A chunk is two 8 KB halves of 64 columns,
+// each in tcgen05's K-major 128-byte-swizzle layout: row n's 64 halves are 128 bytes at n * 128, their 16-byte
+// pieces (8 columns each) stored at piece ((k % 64) / 8) ^ (n % 8) — so one bulk copy of a chunk is an MMA operand as
+// it lands, and the tensor cores read it without bank conflicts.
 constexpr int BG_SLOTS = 32;
 constexpr uint32_t BG_CHUNK_BYTES = 16384;
 __host__ __device__ constexpr size_t x16_offset(int n, int k) {
-    return (size_t)(k >> 7) * BG_CHUNK_BYTES + (size_t)((((n >> 3) << 4) + ((k & 127) >> 3)) << 7) +
-           (size_t)((n & 7) << 4) + (size_t)((k & 7) << 1);
+    return (size_t)(k >> 7) * BG_CHUNK_BYTES + (size_t)((k >> 6) & 1) * 8192 + (size_t)n * 128 +
+           (size_t)(((((k & 63) >> 3) ^ (n & 7))) << 4) + (size_t)((k & 7) << 1);
 }
 __host__ __device__ constexpr size_t x16_group_bytes(int K) { return (size_t)(K / 128) * BG_CHUNK_BYTES; }
 
