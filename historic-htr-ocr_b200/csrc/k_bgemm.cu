@@ -13,13 +13,13 @@
 //
 // Work items are 128-row tiles of W — or, for a matrix of few tiles, a tile's share of its 128-column chunks (split-K:
 // every split writes its f32 partial, and the tile's last split to finish, by ticket, sums the partials in split order
-// and runs the epilogue: deterministic, no waiting). One CTA per SM, persistent over items (item w, w + grid, …), 320
+// and runs the epilogue: deterministic, no waiting). One CTA per SM, persistent over items (item w, w + grid, …), 576
 // threads in three roles:
 //  - warp 0 (one lane), the copies: per 128-column chunk of K, one TMA tile of the quants (128 rows x 128 B, 128-B
 //    swizzle, from the row layout through a tensor map) and one bulk copy of the slots' activation chunk (16 KB, already
 //    in the MMA operand order), both counted on the stage's mbarrier; a 128-row tile's block scales once per tile. The
 //    weights of the first stages are issued before griddepcontrol.wait (they never depend on the previous kernel).
-//  - warps 2-9, the dequantisation: per 64-column piece, int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
+//  - warps 2-17, the dequantisation: per 64-column piece (one 16-weight item per thread), int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
 //    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of 2 to 4 A operand buffers in the 128-byte-swizzle
 //    K-major layout the tensor cores read without bank conflicts; then, per work item, the epilogue: tcgen05.ld of
 //    their TMEM lanes, hi + lo columns summed, the mode's output.
@@ -40,8 +40,9 @@ namespace ocr {
 constexpr int BG_M = 128;       // weight rows per tile: the MMA's M, one TMEM lane each
 constexpr int BG_KC = 128;      // K columns per copy stage
 constexpr int BG_KS = 64;       // K columns per dequantised operand buffer (one 128-byte swizzle atom wide)
-constexpr int BG_THREADS = 320;
-constexpr int BG_DQ = 256;      // dequantisation / epilogue threads (warps 2-9)
+constexpr int BG_THREADS = 576;
+constexpr int BG_DQ = 512;      // dequantisation / epilogue threads (warps 2-17)
+constexpr int BG_DW = BG_DQ / 32;  // their warps: 4 per TMEM lane quarter, 8 slots each
 constexpr uint32_t BG_WTILE = BG_M * BG_KC;                 // 16 KB of int8 quants
 constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 32 KB
 constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of a 64-column piece
@@ -99,6 +100,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
         : "r"(taddr)
         : "memory");
 }
+// 8 consecutive f32 columns of the warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // a 2-D TMA tile load (x = the inner coordinate in elements; a multiple of 16 bytes here), counted on `bar`
 __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t pol) {
@@ -152,8 +160,8 @@ struct BgShared {
     int abort_flag;
     uint32_t ticket;                      // split items: this CTA's place among the tile's splits
     uint32_t pbits[BG_SLOTS][BG_M / 32];  // LM head: the tile's rows in each slot's penalty window
-    float bvq[8][16];                     // LM head: each epilogue warp's best per slot
-    uint32_t biq[8][16];
+    float bvq[BG_DW][8];                  // LM head: each epilogue warp's best per slot
+    uint32_t biq[BG_DW][8];
     float bv[BG_SLOTS];
     uint32_t bi[BG_SLOTS];
 };
@@ -325,25 +333,31 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         __syncwarp();
     }
 
-    // ---- dequantisation and epilogue (warps 2-9) ----
+    // ---- dequantisation and epilogue (warps 2-17) ----
     const int et = (int)threadIdx.x - 64, dw = warp - 2;
-    const int q = warp & 3, half = dw >> 2;  // the TMEM lane quarter this warp may read; its 16 slots
-    float best_v[16];
-    uint32_t best_i[16];
+    const int q = warp & 3, part = dw >> 2;  // the TMEM lane quarter this warp may read; its 8 slots 8 part …
+    float best_v[8];
+    uint32_t best_i[8];
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
+    for (int j = 0; j < 8; j++) {
         best_v[j] = -INFINITY;
         best_i[j] = NO_INDEX;
     }
     if (warp >= 2) {
         pdl_wait();
-        bool act[16];
+        bool act[8];
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const int sl = 16 * half + j;
+        for (int j = 0; j < 8; j++) {
+            const int sl = 8 * part + j;
             act[j] = sl < nb && (!a.active || a.active[slot0 + sl] != 0);
         }
-        // A warp whose wait gave up (ok = false) still walks every loop, skipping waits and work, so that all eight
+        // this thread's item of every 64-column piece: row 8 rg + r8, 16 columns c4; a quarter-warp takes 8 rows of one
+        // 16-column piece — its reads through the copy's swizzle and its writes through the operand's (pieces 2 c4 and
+        // 2 c4 + 1 of a row at (piece ^ row % 8)) are both conflict-free
+        const int r8 = et & 7, c4 = (et >> 3) & 3, rg = et >> 5, drow = rg * 8 + r8;
+        const int o0 = drow * 128 + (((2 * c4) ^ r8) << 4), o1 = drow * 128 + (((2 * c4 + 1) ^ r8) << 4);
+        const int srow = drow * (K / 16);
+        // A warp whose wait gave up (ok = false) still walks every loop, skipping waits and work, so that all sixteen
         // warps meet each named barrier of the epilogue the same number of times.
         uint32_t g = 0, ai = 0;
         int li = 0;
@@ -352,34 +366,24 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const BgItem it = bg_item(w, ksplit, nkc);
             const int sb = li & 1;
             ok = ok && bg_wait(&sh.sfull[sb], (li >> 1) & 1, abort_flag, a.err);
-            const uint8_t* sc = sbuf0 + (size_t)sb * sstride;
+            const uint8_t* sc = sbuf0 + (size_t)sb * sstride + srow;
             for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
                 ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
-                const uint8_t* wt = stage0 + (size_t)s * BG_STAGE;
+                const uint8_t* wt = stage0 + (size_t)s * BG_STAGE + drow * 128;
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                     const int ab = (int)(ai % na);
                     ok = ok && (ai < (uint32_t)na || bg_wait(&sh.aempty[ab], ((ai / na) - 1) & 1, abort_flag, a.err));
                     if (!ok) continue;
                     uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
-#pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        // item i: rows 8 rg + r8, 16 columns c4 of the 64-column piece; a quarter-warp takes 8 rows
-                        // of one 16-column piece: its reads through the copy's swizzle and its writes through the
-                        // operand's (piece 2 c4 and 2 c4 + 1 of a row at (piece ^ row % 8)) are both conflict-free
-                        const int i = et + BG_DQ * j, r8 = i & 7, c4 = (i >> 3) & 3, rg = i >> 5, row = rg * 8 + r8;
-                        const int ch = h * 4 + c4;
-                        const uint4 qv = *reinterpret_cast<const uint4*>(wt + row * 128 + ((ch ^ r8) << 4));
-                        const int blk = (kc * BG_KC + h * BG_KS + c4 * 16) >> 5;
-                        const __half d = *reinterpret_cast<const __half*>(sc + row * (K / 16) + blk * 2);
-                        uint32_t hi[8], lo[8];
-                        dequant16(qv, d, hi, lo);
-                        const int o0 = row * 128 + (((2 * c4) ^ r8) << 4), o1 = row * 128 + (((2 * c4 + 1) ^ r8) << 4);
-                        *reinterpret_cast<uint4*>(ah + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(ah + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                        *reinterpret_cast<uint4*>(ah + BG_AHALF + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                        *reinterpret_cast<uint4*>(ah + BG_AHALF + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-                    }
+                    const uint4 qv = *reinterpret_cast<const uint4*>(wt + (((h * 4 + c4) ^ r8) << 4));
+                    const __half d = reinterpret_cast<const __half*>(sc)[(kc * BG_KC + h * BG_KS + c4 * 16) >> 5];
+                    uint32_t hi[8], lo[8];
+                    dequant16(qv, d, hi, lo);
+                    *reinterpret_cast<uint4*>(ah + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4*>(ah + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    *reinterpret_cast<uint4*>(ah + BG_AHALF + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(ah + BG_AHALF + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                     fence_proxy_async();  // the generic stores, before the tensor cores read them
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sh.afull[ab]);
@@ -391,15 +395,15 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             // ---- the item's epilogue ----
             const int r0 = it.t * BG_M, row = r0 + 32 * q + lane;
             if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {
-                // the window's tokens that fall in this tile, per slot (the 256 epilogue threads, barrier 2)
+                // the window's tokens that fall in this tile, per slot (the epilogue threads, barrier 2)
                 uint32_t* pb = &sh.pbits[0][0];
                 for (int i = et; i < BG_SLOTS * (BG_M / 32); i += BG_DQ) pb[i] = 0u;
                 bar_sync(2, BG_DQ);
-                const int sl = et >> 3, part = et & 7, b = slot0 + sl;
+                const int sl = et >> 4, pt = et & 15, b = slot0 + sl;
                 if (sl < nb && (!a.active || a.active[b])) {
                     const int len = a.lm.len[b];
                     const int32_t* hst = a.lm.hist + (long)b * a.lm.hist_cap;
-                    for (int jj = len - min(len, a.lm.window) + part; jj < len; jj += 8) {
+                    for (int jj = len - min(len, a.lm.window) + pt; jj < len; jj += 16) {
                         const int tk = hst[jj];
                         if (tk >= r0 && tk < r0 + BG_M) atomicOr(&sh.pbits[sl][(tk - r0) >> 5], 1u << ((tk - r0) & 31));
                     }
@@ -407,18 +411,18 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 bar_sync(2, BG_DQ);
             }
             ok = ok && bg_wait(&sh.tfin, li & 1, abort_flag, a.err);
-            float y[16];
+            float y[8];
 #pragma unroll
-            for (int j = 0; j < 16; j++) y[j] = 0.0f;
+            for (int j = 0; j < 8; j++) y[j] = 0.0f;
             if (ok) {
                 tc_fence_after();
-                uint32_t rh[16], rl[16];
+                uint32_t rh[8], rl[8];
                 const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
-                tmem_ld16(ta + 16 * half, rh);
-                tmem_ld16(ta + 32 + 16 * half, rl);
+                tmem_ld8(ta + 8 * part, rh);
+                tmem_ld8(ta + 32 + 8 * part, rl);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 16; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+                for (int j = 0; j < 8; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
             }
             tc_fence_before();  // these reads, before the next item's MMAs overwrite the accumulator
             if (ksplit > 1) {
@@ -426,7 +430,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 // of the tile to arrive (ticket; no waiting) sums them in split order and runs the epilogue
                 float* pt = a.part + (((size_t)grp * n_tiles + it.t) * ksplit) * (BG_SLOTS * BG_M);
 #pragma unroll
-                for (int j = 0; j < 16; j++) pt[(size_t)it.sp * BG_SLOTS * BG_M + (16 * half + j) * BG_M + 32 * q + lane] = y[j];
+                for (int j = 0; j < 8; j++) pt[(size_t)it.sp * BG_SLOTS * BG_M + (8 * part + j) * BG_M + 32 * q + lane] = y[j];
                 __threadfence();
                 bar_sync(2, BG_DQ);
                 if (et == 0) sh.ticket = atomicAdd(&a.tickets[grp * n_tiles + it.t], 1u);
@@ -434,10 +438,10 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 if (sh.ticket != (uint32_t)ksplit - 1) continue;  // (uniform over the epilogue warps)
                 __threadfence();
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
+                for (int j = 0; j < 8; j++) {
                     float v = 0.0f;
                     for (int r = 0; r < ksplit; r++)
-                        v += __ldcg(pt + (size_t)r * BG_SLOTS * BG_M + (16 * half + j) * BG_M + 32 * q + lane);
+                        v += __ldcg(pt + (size_t)r * BG_SLOTS * BG_M + (8 * part + j) * BG_M + 32 * q + lane);
                     y[j] = v;
                 }
                 if (et == 0) a.tickets[grp * n_tiles + it.t] = 0u;  // (self-resetting for the next launch)
@@ -448,9 +452,9 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 const int col = row >> 1;
                 uint8_t* y16 = a.y16 ? a.y16 + (size_t)grp * x16_group_bytes(N / 2) : nullptr;
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
+                for (int j = 0; j < 8; j++) {
                     const float up = __shfl_xor_sync(FULL, y[j], 1);
-                    const int sl = 16 * half + j;
+                    const int sl = 8 * part + j;
                     if ((lane & 1) || !act[j] || row >= N) continue;
                     const float gv = y[j];
                     const float hv = gv / (1.0f + expf(-gv)) * up;
@@ -465,17 +469,17 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             } else if (!lmhead) {
                 if (row < N) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
+                    for (int j = 0; j < 8; j++) {
                         if (!act[j]) continue;
-                        float* yp = a.y + (long)(slot0 + 16 * half + j) * a.y_stride + row;
+                        float* yp = a.y + (long)(slot0 + 8 * part + j) * a.y_stride + row;
                         *yp = a.mode == MV_ADD ? *yp + y[j] : y[j];
                     }
                 }
             } else if (row < N) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
+                for (int j = 0; j < 8; j++) {
                     if (!act[j]) continue;
-                    const int sl = 16 * half + j, b = slot0 + sl;
+                    const int sl = 8 * part + j, b = slot0 + sl;
                     if (a.y) a.y[(long)b * N + row] = y[j];
                     if (a.lm.sample) {
                         const bool member = (sh.pbits[sl][q] >> lane) & 1u;
@@ -499,7 +503,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     // ---- the LM head's choice: each slot's best over the CTA's tiles, then the last CTA picks ----
     if (warp >= 2) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
+        for (int j = 0; j < 8; j++) {
             float v = best_v[j];
             uint32_t i = best_i[j];
             warp_argmax(v, i);
@@ -511,10 +515,11 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     }
     __syncthreads();
     if (threadIdx.x < BG_SLOTS) {
-        const int sl = threadIdx.x, hf = sl >> 4, j = sl & 15;
+        // slot sl's 8-slot part is taken by the four warps of that part (one per TMEM lane quarter)
+        const int sl = threadIdx.x, pp = sl >> 3, j = sl & 7;
         float v = -INFINITY;
         uint32_t i = NO_INDEX;
-        for (int w = 4 * hf; w < 4 * hf + 4; w++)
+        for (int w = 4 * pp; w < 4 * pp + 4; w++)
             if (better(sh.bvq[w][j], sh.biq[w][j], v, i)) {
                 v = sh.bvq[w][j];
                 i = sh.biq[w][j];
