@@ -23,10 +23,11 @@
 //    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of 2 to 4 A operand buffers in the 128-byte-swizzle
 //    K-major layout the tensor cores read without bank conflicts; then, per work item, the epilogue: tcgen05.ld of
 //    their TMEM lanes, hi + lo columns summed, the mode's output.
-//  - warp 1, the tensor cores: TMEM allocation (64 columns: 32 slots' hi products + 32 slots' lo products), and per
-//    16-column step two MMAs (M = 128): A = w_hi with B = [x_hi | x_lo] (N = 64), A = w_lo with B = x_hi (N = 32) into the
-//    first 32 columns; tcgen05.commit releases the operand buffer, the copy stage, and at an item's end the accumulator
-//    to the epilogue.
+//  - warp 1, the tensor cores: TMEM allocation (all 512 columns: 4 accumulator sets), and per 16-column step two MMAs
+//    (M = 128) into one set — A = w_hi with B = [x_hi | x_lo] (N = 64) into its columns 0-63, A = w_lo with B = x_hi
+//    (N = 32) into 64-95 — consecutive steps rotating over the sets, so four chains of dependent MMAs run side by side
+//    (one chain of these small-N MMAs is bound by the accumulator's latency); tcgen05.commit releases the operand
+//    buffer, the copy stage, and at an item's end the accumulators to the epilogue, which sums the sets in order.
 // Every mbarrier wait is bounded; a wait that runs out sets the device error flag and a shared abort flag that every
 // role polls; the copies in flight and the MMAs issued are then waited for (bounded) and the TMEM is freed before the
 // CTA exits.
@@ -49,7 +50,9 @@ constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or
 constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
 constexpr int BG_NA = 4;        // operand buffers at most (2 to 4, as shared memory allows)
 constexpr int BG_MAX_NS = 4;    // copy stages
-constexpr uint32_t BG_TMEM_COLS = 64;
+constexpr int BG_NACC = 4;            // accumulator sets the K steps rotate over (independent MMA chains)
+constexpr uint32_t BG_SET_COLS = 128;  // a set: w_hi [x_hi | x_lo] in columns 0-63, w_lo x_hi in 64-95
+constexpr uint32_t BG_TMEM_COLS = BG_NACC * BG_SET_COLS;  // all 512 columns (one CTA per SM)
 constexpr int BG_SMEM_OPTIN = 227 * 1024;
 
 // ---- tcgen05 / TMA primitives ------------------------------------------------------------------------------------------
@@ -301,6 +304,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                         break;
                     }
                     const uint32_t xs = smem_u32(stage0 + (size_t)s * BG_STAGE + BG_WTILE);
+                    const int kstep0 = (kc - it.c0) * (BG_KC / 16);  // the item's K steps so far
                     for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                         const int ab = (int)(ai % na);
                         if (!bg_wait(&sh.afull[ab], (ai / na) & 1, abort_flag, a.err)) {
@@ -315,8 +319,13 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                             const uint64_t dh = bg_desc(ah + ks * 32);
                             const uint64_t dl = bg_desc(al + ks * 32);
                             const uint64_t db = bg_desc(xs + h * 8192 + ks * 32);
-                            mma_f16(tmem, dh, db, id1, (kc != it.c0 || h || ks) ? 1u : 0u);
-                            mma_f16(tmem, dl, db, id2, 1u);
+                            // consecutive K steps go to independent accumulator sets (the MMAs of one set depend
+                            // on each other; of different sets, not); a set's first step overwrites it
+                            const int kstep = kstep0 + h * (BG_KS / 16) + ks;
+                            const uint32_t dset = tmem + (uint32_t)(kstep % BG_NACC) * BG_SET_COLS;
+                            const uint32_t acc = kstep >= BG_NACC ? 1u : 0u;
+                            mma_f16(dset, dh, db, id1, acc);
+                            mma_f16(dset + 64, dl, db, id2, acc);
                         }
                         mma_commit(&sh.aempty[ab]);
                         any = true;
@@ -415,14 +424,20 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 8; j++) y[j] = 0.0f;
             if (ok) {
+                // the sets summed in order, each as w_hi x_hi + w_hi x_lo + w_lo x_hi
                 tc_fence_after();
-                uint32_t rh[8], rl[8];
-                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16);
-                tmem_ld8(ta + 8 * part, rh);
-                tmem_ld8(ta + 32 + 8 * part, rl);
-                tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 8; j++) y[j] = __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+                for (int st = 0; st < BG_NACC; st++) {
+                    uint32_t rh[8], rl[8], rw[8];
+                    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)st * BG_SET_COLS;
+                    tmem_ld8(ta + 8 * part, rh);
+                    tmem_ld8(ta + 32 + 8 * part, rl);
+                    tmem_ld8(ta + 64 + 8 * part, rw);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        y[j] += (__uint_as_float(rh[j]) + __uint_as_float(rw[j])) + __uint_as_float(rl[j]);
+                }
             }
             tc_fence_before();  // these reads, before the next item's MMAs overwrite the accumulator
             if (ksplit > 1) {
