@@ -207,7 +207,8 @@ def kernel_roofline(classes):
 # our arm
 # ---------------------------------------------------------------------------------------------------------------------
 # the decode workloads: slots per GPU, prefix rows per slot, tokens decoded per slot (BASELINE configs[1] and [2])
-WORKLOADS = {2: dict(B=1, prefix=PREFIX, new=NEW), 3: dict(B=32, prefix=3072, new=1024)}
+WORKLOADS = {2: dict(B=1, prefix=PREFIX, new=NEW), 3: dict(B=32, prefix=3072, new=1024),
+             5: dict(B=32, prefix=2286, new=1150)}  # (config 5: its mean page, for the CPU samples' positions)
 
 
 def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0):
@@ -275,6 +276,8 @@ def run_ours(args):
     ctx = ocr.Context(local)
     if args.config == 1:
         return run_config1(args, ocr, ctx, torch, pg, rank, world)
+    if args.config == 5:
+        return run_config5(args, ocr, ctx, torch, pg if pg else None, rank, world, local)
     r = decode_workload(ocr, ctx, torch, args.config, args.steps, args.warmup, pg, local, args.tokens)
     B, prefix_len, new, dev_s, wall = r["B"], r["prefix"], r["new"], r["dev_s"], r["wall"]
     tokens = world * B * new * args.steps
@@ -324,6 +327,83 @@ def run_ours(args):
         pg.barrier()
         pg.destroy_process_group()
     ctx.close()
+    return out
+
+
+def run_config5(args, ocr, ctx, torch, pg, rank, world, local):
+    """the page sweep. 512 seeded pages (prefix rows uniform on [1500, 3072], 800 … 1500 tokens
+    each) claimed by the ranks from a shared queue (the process group's store: no data-path collective), each rank
+    reading its pages through its GPU's page engine (ocr_read_pages: 32 slots, continuous batching; prefill of each
+    page's rows included). Whole-box tokens over the slowest rank's device time; strong scaling (the pages are fixed)."""
+    import pages as P
+
+    seed = ocr.SEED_BASE + 5
+    n_pages = args.pages or P.N_PAGES
+    specs = P.page_specs(seed, n_pages)
+    pool = P.page_pool(seed, CONFIG2["dim"])
+    model = ocr.TextModel.synthetic(ctx, ocr.TextConfig(**CONFIG2), ocr.SEED_BASE + 2, 0.02, 0.02)
+    sess = model.session(P.PREFIX_MAX + P.GEN_MAX, batch=32)
+    preset = ocr.Preset("c5", 0.0, 1.0, 1.15, 64, 0.0, P.GEN_MAX)
+    hist = [IMAGE_PAD] * 64
+    store = pg.distributed_c10d._get_default_store() if pg else P.LocalStore()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    def sweep(ns, page_ids):
+        q = P.PageQueue(store, rank, world, len(page_ids), ns=ns)
+
+        def read(claim, done):
+            def source():
+                i = claim()
+                if i is None:
+                    return None
+                sp = specs[page_ids[i]]
+                return ocr.PageJob(i, pool[sp.row0: sp.row0 + sp.prefix], sp.new, history=hist)
+
+            def on_done(job):
+                return done(job.id, len(job.out))
+
+            ocr.read_pages(sess, preset, source, on_done, max_new_cap=P.GEN_MAX, chunk=16)
+
+        mine = P.run_worker(read, q)
+        return q, mine
+
+    # warm-up: a few pages (one-time setup, graph capture)
+    sweep("warm/", [p % n_pages for p in range(2 * world)])
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        ev0.record(stream)
+        q, mine = sweep("sweep/", list(range(n_pages)))
+        ev1.record(stream)
+        ev1.synchronize()
+        wall = time.perf_counter() - t0
+    dev_s, wall = max_over_ranks([ev0.elapsed_time(ev1) / 1e3, wall], pg)
+    tokens = q.tokens()
+    out = None
+    if rank == 0:
+        out = {
+            "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
+            "value": round(tokens / dev_s, 1), "unit": "tok/s", "n_gpus": world, "steps": 1, "warmup": 1,
+            "ms_per_step": round(dev_s * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "q8_0 weights x f32 activations, f16 KV",
+            "data": "synthetic (seeded q8_0 weights, N(0,1) prefix rows; no checkpoint)",
+            "config": {"workload": f"BASELINE config 5: {n_pages} pages (prefix U[1500,3072] rows, U[800,1500] tokens), "
+                                   "prefill + greedy decode, 32 slots per GPU, continuous batching",
+                       "model": "Qwen3-0.6B-shaped text decoder (28 x 1024, 16/8 heads, ffn 3072, vocab 151936)",
+                       "global_batch": 32 * world, "parallelism": f"replicas x{world}, pages claimed from a shared queue"},
+            "pages": n_pages, "tokens": tokens, "prefix_rows": sum(s.prefix for s in specs),
+            "pages_read_rank0": mine,
+            "e2e": {"value": round(tokens / wall, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": sum(s.prefix for s in specs) * CONFIG2["dim"] * 4 + n_pages * 64 * 4,
+                    "d2h_bytes_per_step": tokens * 4},
+            "clocks": clk.summary()}
+        print(json.dumps(out), flush=True)
+    P.PageQueue(store, rank, world, n_pages, ns="sweep/").leave()
+    sess.close()
+    model.close()
     return out
 
 
@@ -433,7 +513,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3], default=2)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=2)
+    ap.add_argument("--pages", type=int, default=0, help="config 5: pages in the sweep (default 512)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="config 3: skip the config-2 measurement beside it")
     ap.add_argument("--tokens", type=int, default=0,
