@@ -307,11 +307,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* __restrict__ 
 void launch_attention_prefill(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
                               const __half* vc, int n_ctx, int pos0, float scale, float* out) {
     const size_t smem = (size_t)(128 * FQ + 128 * FK + FK * 128 + FK * FQ) * sizeof(float);
-    static int configured = 0;
-    if (!configured) {
-        cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = 1;
-    }
+    static PerDeviceOnce once;  // the attribute lives in each device's context
+    once([&] { cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
     k_attn_prefill<<<dim3((L + FQ - 1) / FQ, n_head, 1), 256, smem, st>>>(qkv, L, n_head, n_kv, kc, vc, n_ctx, pos0,
                                                                           scale, out);
 }

@@ -1156,10 +1156,17 @@ ocr_status decode_slots(ocr_session* s, int s0, int ns, const ocr_sampler_cfg* c
     return OCR_OK;
 }
 
+// the prefill's scratch for n rows: x, h, qkv, attention output, g (f32), the ids; with the tensor-core contractions
+// also the operands of widths dim, n_head x 128 and n_ff for the rows in groups of 32
+size_t prefill_x16_bytes(const ocr_session* s, int n, int K) {
+    return (size_t)((n + BG_SLOTS - 1) / BG_SLOTS) * x16_group_bytes(K);
+}
 ocr_status ensure_prefill(ocr_session* s, int n) {
     const auto& c = s->m->cfg;
     const size_t per_row = (size_t)c.dim * 2 + s->qkv_w + s->qd + c.n_ff + 1;
-    const size_t need = per_row * n * 4 + 4096;
+    size_t need = per_row * n * 4 + 4096;
+    if (s->m->tc)
+        need += prefill_x16_bytes(s, n, c.dim) + prefill_x16_bytes(s, n, s->qd) + prefill_x16_bytes(s, n, c.n_ff) + 1024;
     if (s->pf_bytes >= need) return OCR_OK;
     OCR_CUDA(cudaStreamSynchronize(s->ctx->stream));
     if (s->pf) dfree(s->pf, s->pf_bytes, &s->ctx->mem_work);
@@ -1608,10 +1615,54 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
     launch_embed_rows(st, d_ids, n, s->m->tok, x);
     const int pos0 = s->n_past[slot];
     const float scale = 1.0f / sqrtf((float)c.d_head);
+    // the tensor-core contractions (k_bgemm.cu) take the rows in groups of 32 like decode slots; the operands after
+    // the ids, 256-B aligned
+    const bool tc = s->m->tc;
+    uint8_t* x16a = (uint8_t*)(((uintptr_t)(d_ids + n) + 255) & ~(uintptr_t)255);
+    uint8_t* x16o = x16a + prefill_x16_bytes(s, n, c.dim);
+    uint8_t* x16g = x16o + prefill_x16_bytes(s, n, s->qd);
+    auto prep = [&](const float* src, int K, const float* nw, uint8_t* x16) {
+        PrepArgs p;
+        p.x = src;
+        p.x_stride = K;
+        p.nw = nw;
+        p.eps = c.eps;
+        p.K = K;
+        p.nb = n;
+        p.x16 = x16;
+        p.err = ctx->d_err;
+        launch_xprep(st, p, false);
+    };
+    auto gemm = [&](const QMat& w, const BgMaps& bq, const uint8_t* x16, int mode, float* y, int y_stride,
+                    uint8_t* y16) {
+        BgArgs g;
+        g.w = w;
+        g.x16 = x16;
+        g.mode = mode;
+        g.y = y;
+        g.y_stride = y_stride;
+        g.y16 = y16;
+        g.nb = n;
+        g.err = ctx->d_err;
+        launch_bgemm(st, g, bq, ctx->num_sms, false);
+    };
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = s->m->layers[l];
         __half* kc = s->kcl(l) + (size_t)slot * c.n_kv * s->n_ctx * 128;
         __half* vc = s->vcl(l) + (size_t)slot * c.n_kv * s->n_ctx * 128;
+        if (tc) {
+            prep(x, c.dim, L.attn_norm, x16a);
+            gemm(L.qkv, L.bq_qkv, x16a, MV_STORE, qkv, s->qkv_w, nullptr);
+            launch_qk_norm_rope_store(st, qkv, n, c.n_head, c.n_kv, L.q_norm, L.k_norm, s->rope, pos0, c.eps, kc, vc,
+                                      s->n_ctx);
+            launch_attention_prefill(st, qkv, n, c.n_head, c.n_kv, kc, vc, s->n_ctx, pos0, scale, a);
+            prep(a, s->qd, nullptr, x16o);
+            gemm(L.o, L.bq_o, x16o, MV_ADD, x, c.dim, nullptr);
+            prep(x, c.dim, L.ffn_norm, x16a);
+            gemm(L.gu, L.bq_gu, x16a, MV_SWIGLU, nullptr, 0, x16g);
+            gemm(L.down, L.bq_down, x16g, MV_ADD, x, c.dim, nullptr);
+            continue;
+        }
         launch_rmsnorm_rows(st, x, L.attn_norm, h, n, c.dim, c.eps);
         launch_gemm_q8_0(st, h, n, L.qkv, qkv, 0, 0);
         launch_qk_norm_rope_store(st, qkv, n, c.n_head, c.n_kv, L.q_norm, L.k_norm, s->rope, pos0, c.eps, kc, vc, s->n_ctx);
