@@ -15,10 +15,11 @@
 // every split writes its f32 partial, and the tile's last split to finish, by ticket, sums the partials in split order
 // and runs the epilogue: deterministic, no waiting). One CTA per SM, persistent over items (item w, w + grid, …), 576
 // threads in three roles:
-//  - warp 0 (one lane), the copies: per 128-column chunk of K, one TMA tile of the quants (128 rows x 128 B, 128-B
-//    swizzle, from the row layout through a tensor map) and one bulk copy of the slots' activation chunk (16 KB, already
-//    in the MMA operand order), both counted on the stage's mbarrier; a 128-row tile's block scales once per tile. The
-//    weights of the first stages are issued before griddepcontrol.wait (they never depend on the previous kernel).
+//  - warp 0 (one lane), the copies: per 128-column chunk of K, one bulk copy of the tile's block of the tile-major
+//    weight copy (16 KB of quants, already swizzled, + their 1 KB of block scales: one contiguous run, so the DRAM reads
+//    stream) and one of the slots' activation chunk (16 KB, already in the MMA operand order), both counted on the
+//    stage's mbarrier. The weights of the first stages are issued before griddepcontrol.wait (they never depend on the
+//    previous kernel).
 //  - warps 2-17, the dequantisation: per 64-column piece (one 16-weight item per thread), int8 -> f16 hi / lo (byte permute into 1024 + q + 128's
 //    mantissa, one HSUB2, one HMUL2, one HFMA2 per pair) into one of 2 to 4 A operand buffers in the 128-byte-swizzle
 //    K-major layout the tensor cores read without bank conflicts; then, per work item, the epilogue: tcgen05.ld of
@@ -31,8 +32,6 @@
 // Every mbarrier wait is bounded; a wait that runs out sets the device error flag and a shared abort flag that every
 // role polls; the copies in flight and the MMAs issued are then waited for (bounded) and the TMEM is freed before the
 // CTA exits.
-#include <cudaTypedefs.h>
-
 #include "choice.cuh"
 #include "kernels.cuh"
 
@@ -44,8 +43,8 @@ constexpr int BG_KS = 64;       // K columns per dequantised operand buffer (one
 constexpr int BG_THREADS = 576;
 constexpr int BG_DQ = 512;      // dequantisation / epilogue threads (warps 2-17)
 constexpr int BG_DW = BG_DQ / 32;  // their warps: 4 per TMEM lane quarter, 8 slots each
-constexpr uint32_t BG_WTILE = BG_M * BG_KC;                 // 16 KB of int8 quants
-constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 32 KB
+constexpr uint32_t BG_WTILE = BG_TILE_BYTES;                // a tile-major block: 16 KB of int8 quants + 1 KB of scales
+constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 33 KB (1024-B multiple)
 constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of a 64-column piece
 constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
 constexpr int BG_NA = 4;        // operand buffers at most (2 to 4, as shared memory allows)
@@ -111,18 +110,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
                  : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// a 2-D TMA tile load (x = the inner coordinate in elements; a multiple of 16 bytes here), counted on `bar`
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
-        "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
 // a bounded wait that also gives up when another role of the CTA has given up (`abort_flag`)
 __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
     for (uint32_t i = 0; i < MBAR_TRIES; i++) {
@@ -157,7 +144,6 @@ __device__ __forceinline__ void dequant16(uint4 q, __half d, uint32_t* hi, uint3
 struct BgShared {
     uint64_t tfull[BG_MAX_NS], tempty[BG_MAX_NS];  // copy stage landed / free again (MMAs done)
     uint64_t afull[BG_NA], aempty[BG_NA];          // operand buffer written / free again
-    uint64_t sfull[2], sempty[2];                  // a tile's block scales landed / read
     uint64_t tfin, mdone;                          // an item's accumulator complete; every MMA done (exit)
     uint32_t tmem_base;
     int abort_flag;
@@ -184,21 +170,17 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
 }
 
 __global__ void __launch_bounds__(BG_THREADS, 1)
-    k_bgemm(const __grid_constant__ BgArgs a, const __grid_constant__ CUtensorMap mq,
-            const __grid_constant__ CUtensorMap ms, int ns, int na) {
+    k_bgemm(const __grid_constant__ BgArgs a, const uint8_t* __restrict__ wtiles, int ns, int na) {
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(16) BgShared sh;
     volatile int* abort_flag = &sh.abort_flag;
 
     const int K = a.w.cols, N = a.w.rows;
     const int nkc = K / BG_KC, ksplit = a.ksplit;
-    const int sbytes = BG_M * (K / 16);  // a tile's block scales (TMA box K/16 x 128 rows)
-    const int sstride = (sbytes + 1023) & ~1023;
     // the dynamic region starts 1024-B aligned (the 128-B swizzle's pattern repeats every 1024 B)
     uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
     uint8_t* stage0 = smp;
     uint8_t* abuf0 = smp + (size_t)ns * BG_STAGE;
-    uint8_t* sbuf0 = abuf0 + (size_t)na * BG_ABUF;
     const int n_tiles = (N + BG_M - 1) / BG_M, n_items = n_tiles * ksplit;
     const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
@@ -213,10 +195,6 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         for (int i = 0; i < na; i++) {
             mbar_init(&sh.afull[i], BG_DQ / 32);
             mbar_init(&sh.aempty[i], 1);
-        }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&sh.sfull[i], 1);
-            mbar_init(&sh.sempty[i], BG_DQ / 32);
         }
         mbar_init(&sh.tfin, 1);
         mbar_init(&sh.mdone, 1);
@@ -236,57 +214,46 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         // ---- the copies ----
         if (lane == 0) {
             const uint64_t pol = l2_evict_first();
-            prefetch_tmap(&mq);
-            prefetch_tmap(&ms);
             uint32_t g = 0;
-            int li = 0, s_issued = 0, pre = 0;
+            int pre = 0;
             const int w0 = blockIdx.x;
+            auto wblock = [&](int t, int kc) { return wtiles + ((size_t)t * nkc + kc) * BG_TILE_BYTES; };
             if (w0 < n_items) {
-                // before the dependency wait: the first item's scales and the quants of its first stages
+                // before the dependency wait: the weight blocks of the first item's first stages
                 const BgItem it = bg_item(w0, ksplit, nkc);
-                mbar_expect_tx(&sh.sfull[0], (uint32_t)sbytes);
-                tma_2d(sbuf0, &ms, 0, it.t * BG_M, &sh.sfull[0], pol);
-                s_issued = 1;
                 pre = min(ns, it.c1 - it.c0);
                 for (int s = 0; s < pre; s++) {
                     mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                    tma_2d(stage0 + (size_t)s * BG_STAGE, &mq, (it.c0 + s) * BG_KC, it.t * BG_M, &sh.tfull[s], pol);
+                    bulk_g2s_stream(stage0 + (size_t)s * BG_STAGE, wblock(it.t, it.c0 + s), BG_WTILE, &sh.tfull[s], pol);
                 }
             }
             pdl_trigger();
             pdl_wait();
             bool ok = true;
-            for (int w = w0; w < n_items && ok; w += gridDim.x, li++) {
+            for (int w = w0; w < n_items && ok; w += gridDim.x) {
                 const BgItem it = bg_item(w, ksplit, nkc);
-                const int sb = li & 1;
-                if (li > 0) {
-                    if (li >= 2 && !bg_wait(&sh.sempty[sb], ((li >> 1) - 1) & 1, abort_flag, a.err)) break;
-                    mbar_expect_tx(&sh.sfull[sb], (uint32_t)sbytes);
-                    tma_2d(sbuf0 + (size_t)sb * sstride, &ms, 0, it.t * BG_M, &sh.sfull[sb], pol);
-                    s_issued = li + 1;
-                }
                 for (int kc = it.c0; kc < it.c1; kc++, g++) {
                     const int s = (int)(g % (uint32_t)ns);
                     uint8_t* st = stage0 + (size_t)s * BG_STAGE;
-                    if (g >= (uint32_t)pre) {  // (the prologue issued the quants of the first `pre` stages)
+                    if (g >= (uint32_t)pre) {  // (the prologue issued the weights of the first `pre` stages)
                         if (g >= (uint32_t)ns && !bg_wait(&sh.tempty[s], ((g / ns) - 1) & 1, abort_flag, a.err)) {
                             ok = false;
                             break;
                         }
                         mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                        tma_2d(st, &mq, kc * BG_KC, it.t * BG_M, &sh.tfull[s], pol);
+                        bulk_g2s_stream(st, wblock(it.t, kc), BG_WTILE, &sh.tfull[s], pol);
                     }
                     bulk_g2s(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.tfull[s]);
                 }
             }
-            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete)
+            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete);
+            // a stage whose activations were never issued (an abort between its weights and them) is not waited for
             const uint32_t issued = max(g, (uint32_t)pre);
             for (int s = 0; s < ns && (uint32_t)s < issued; s++) {
                 const uint32_t n = (issued - s + ns - 1) / ns;
                 if (*abort_flag && (uint32_t)s + (n - 1) * ns >= g) continue;
                 mbar_wait(&sh.tfull[s], (n - 1) & 1, a.err);
             }
-            for (int i = max(0, s_issued - 2); i < s_issued; i++) mbar_wait(&sh.sfull[i & 1], (i >> 1) & 1, a.err);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -365,7 +332,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         // 2 c4 + 1 of a row at (piece ^ row % 8)) are both conflict-free
         const int r8 = et & 7, c4 = (et >> 3) & 3, rg = et >> 5, drow = rg * 8 + r8;
         const int o0 = drow * 128 + (((2 * c4) ^ r8) << 4), o1 = drow * 128 + (((2 * c4 + 1) ^ r8) << 4);
-        const int srow = drow * (K / 16);
+
         // A warp whose wait gave up (ok = false) still walks every loop, skipping waits and work, so that all sixteen
         // warps meet each named barrier of the epilogue the same number of times.
         uint32_t g = 0, ai = 0;
@@ -373,20 +340,18 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         bool ok = true;
         for (int w = blockIdx.x; w < n_items; w += gridDim.x, li++) {
             const BgItem it = bg_item(w, ksplit, nkc);
-            const int sb = li & 1;
-            ok = ok && bg_wait(&sh.sfull[sb], (li >> 1) & 1, abort_flag, a.err);
-            const uint8_t* sc = sbuf0 + (size_t)sb * sstride + srow;
             for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
                 ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
                 const uint8_t* wt = stage0 + (size_t)s * BG_STAGE + drow * 128;
+                const __half* sc = reinterpret_cast<const __half*>(stage0 + (size_t)s * BG_STAGE + 16384 + drow * 8);
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                     const int ab = (int)(ai % na);
                     ok = ok && (ai < (uint32_t)na || bg_wait(&sh.aempty[ab], ((ai / na) - 1) & 1, abort_flag, a.err));
                     if (!ok) continue;
                     uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
                     const uint4 qv = *reinterpret_cast<const uint4*>(wt + (((h * 4 + c4) ^ r8) << 4));
-                    const __half d = reinterpret_cast<const __half*>(sc)[(kc * BG_KC + h * BG_KS + c4 * 16) >> 5];
+                    const __half d = sc[(h * BG_KS + c4 * 16) >> 5];
                     uint32_t hi[8], lo[8];
                     dequant16(qv, d, hi, lo);
                     *reinterpret_cast<uint4*>(ah + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -398,8 +363,6 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     if (lane == 0) mbar_arrive(&sh.afull[ab]);
                 }
             }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(&sh.sempty[sb]);
 
             // ---- the item's epilogue ----
             const int r0 = it.t * BG_M, row = r0 + 32 * q + lane;
@@ -657,56 +620,31 @@ size_t bgemm_part_floats(int rows, int ksplit) {
 
 int bgemm_tickets(int rows) { return (rows + BG_M - 1) / BG_M; }
 
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn(std::string* why) {
-    static std::mutex mu;
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
-            if (why) *why = "the driver offers no cuTensorMapEncodeTiled";
-            cudaGetLastError();
-            return nullptr;
-        }
-        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }
-    return fn;
+size_t bgemm_tiled_bytes(int rows, int cols) {
+    return (size_t)((rows + BG_M - 1) / BG_M) * (cols / BG_KC) * BG_TILE_BYTES;
 }
 
-bool bgemm_maps(const QMat& w, BgMaps* m, std::string* why) {
-    if (!bgemm_shape_ok(w.rows, w.cols)) {
-        if (why) *why = "shape outside the tensor-core contraction";
-        return false;
+// the tile-major copy (see BG_TILE_BYTES): one CTA per block, 16-byte pieces of quants swizzled, then the scales
+__global__ void __launch_bounds__(256) k_tile_q8_0(QMat w, uint8_t* __restrict__ out) {
+    const int nkc = w.cols / BG_KC, t = blockIdx.x / nkc, c = blockIdx.x % nkc;
+    uint8_t* o = out + (size_t)blockIdx.x * BG_TILE_BYTES;
+    for (int i = threadIdx.x; i < BG_M * 8; i += blockDim.x) {
+        const int r = i >> 3, pc = i & 7, row = t * BG_M + r;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < w.rows) v = *reinterpret_cast<const uint4*>(w.w + (size_t)row * w.stride + c * BG_KC + pc * 16);
+        *reinterpret_cast<uint4*>(o + r * 128 + ((pc ^ (r & 7)) << 4)) = v;
     }
-    auto enc = encode_fn(why);
-    if (!enc) return false;
-    const cuuint64_t strides[1] = {(cuuint64_t)w.stride};
-    const cuuint32_t estr[2] = {1, 1};
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)w.cols, (cuuint64_t)w.rows};
-        const cuuint32_t box[2] = {BG_KC, BG_M};
-        const CUresult r = enc(&m->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w.w), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) {
-            if (why) *why = "cuTensorMapEncodeTiled (quants) returned " + std::to_string((int)r);
-            return false;
-        }
+    for (int r = threadIdx.x; r < BG_M; r += blockDim.x) {
+        const int row = t * BG_M + r;
+        uint2 v = make_uint2(0u, 0u);  // the 4 f16 scales of the chunk's 4 blocks (8-byte aligned: cols % 256 == 0)
+        if (row < w.rows) v = *reinterpret_cast<const uint2*>(w.w + (size_t)row * w.stride + w.cols + c * 8);
+        *reinterpret_cast<uint2*>(o + BG_M * 128 + r * 8) = v;
     }
-    {
-        const cuuint64_t dims[2] = {(cuuint64_t)(w.cols / 16), (cuuint64_t)w.rows};
-        const cuuint32_t box[2] = {(cuuint32_t)(w.cols / 16), BG_M};
-        const CUresult r = enc(&m->s, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w.w + w.cols), dims,
-                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) {
-            if (why) *why = "cuTensorMapEncodeTiled (scales) returned " + std::to_string((int)r);
-            return false;
-        }
-    }
-    return true;
+}
+
+void launch_tile_q8_0(cudaStream_t st, const QMat& w, uint8_t* out) {
+    const int blocks = (w.rows + BG_M - 1) / BG_M * (w.cols / BG_KC);
+    k_tile_q8_0<<<blocks, 256, 0, st>>>(w, out);
 }
 
 static int bg_static_smem() {
@@ -724,12 +662,11 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
         cudaFuncSetAttribute(k_bgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
     });
     const int K = a.w.cols;
-    const int sstride = (BG_M * (K / 16) + 1023) & ~1023;
-    // shared memory: ns copy stages, na operand buffers, two tiles' scales (+ the 1024-B alignment slack): as many
-    // operand buffers as fit beside 3 stages (2 at K = 3072 and 4096), then as many stages as fit
-    const int room = BG_SMEM_OPTIN - bg_static_smem() - 2 * sstride - 1024;
+    // shared memory: ns copy stages and na operand buffers (+ the 1024-B alignment slack): as many operand buffers as
+    // fit beside 3 stages, then as many stages as fit
+    const int room = BG_SMEM_OPTIN - bg_static_smem() - 1024;
     const int na = std::max(2, std::min(BG_NA, (room - 3 * (int)BG_STAGE) / (int)BG_ABUF));
-    const int fixed = na * (int)BG_ABUF + 2 * sstride + 1024;
+    const int fixed = na * (int)BG_ABUF + 1024;
     const int ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
@@ -741,7 +678,7 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.q, m.s, ns, na);
+    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.tiles, ns, na);
 }
 
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl) {

@@ -7,8 +7,6 @@
 // contiguous, 16-B aligned, 16-B multiple byte range: one bulk-async copy (cp.async.bulk) moves a stage of rows.
 #pragma once
 
-#include <cuda.h>  // CUtensorMap: the copy engine's descriptors of the weight tiles (no driver library is linked)
-
 #include "common.cuh"
 
 namespace ocr {
@@ -226,11 +224,16 @@ __host__ __device__ constexpr size_t x16_offset(int n, int k) {
 }
 __host__ __device__ constexpr size_t x16_group_bytes(int K) { return (size_t)(K / 128) * BG_CHUNK_BYTES; }
 
-// the copy engine's view of a weight matrix in the row layout: its quants as 128 x 128-byte tiles (128-B swizzle)
-// and one 128-row tile's block scales
+// The tile-major copy of a matrix that the contraction streams (derived on the device at load): per 128-row tile t
+// and 128-column chunk c, block t * (cols / 128) + c of BG_TILE_BYTES — the rows' 128 quant bytes (row r at r * 128,
+// its 16-byte piece p at ((p ^ (r % 8)) * 16): the swizzle of the operand reads) and then the rows' 4 block scales
+// (r * 8, f16) — so a stage of the stream is one contiguous 17 KB copy. Rows past the matrix are zero.
+constexpr uint32_t BG_TILE_BYTES = 17408;
 struct BgMaps {
-    CUtensorMap q, s;
+    const uint8_t* tiles = nullptr;
 };
+size_t bgemm_tiled_bytes(int rows, int cols);
+void launch_tile_q8_0(cudaStream_t st, const QMat& w, uint8_t* out);
 struct BgArgs {
     QMat w;
     const uint8_t* x16 = nullptr;  // [groups][K/128] chunks (the slots' activations, hi / lo)
@@ -250,8 +253,6 @@ struct BgArgs {
 };
 // true when the tensor-core contraction takes this shape (cols a multiple of 256, at most 4096)
 bool bgemm_shape_ok(int rows, int cols);
-// the two tensor maps of a matrix (false + *why when the driver refuses them)
-bool bgemm_maps(const QMat& w, BgMaps* m, std::string* why);
 // CTAs of a launch: one per work item (a 128-row tile's split), at most one per SM (a persistent CTA takes items
 // blockIdx.x + k * grid)
 int bgemm_grid(int num_sms, int rows, int ksplit = 1);

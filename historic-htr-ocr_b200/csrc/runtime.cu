@@ -148,11 +148,23 @@ struct Layout {
     struct LayerOff {
         MatOff qkv, o, gu, down;
         size_t attn_norm, q_norm, k_norm, ffn_norm, o_s, d_s;
+        size_t t_qkv = 0, t_o = 0, t_gu = 0, t_down = 0;  // the tile-major copies (tensor-core contractions)
     };
     std::vector<LayerOff> layers;
     MatOff tok;
     size_t out_norm, total;
+    bool tc = false;
+    size_t t_tok = 0;
 };
+
+// the batched contractions can run on the tensor cores: every matrix's shape fits them (OCR_TC=0 turns them off)
+bool tc_shapes(const ocr_text_cfg& c) {
+    const char* env = getenv("OCR_TC");
+    if (env && env[0] == '0') return false;
+    const int qd = c.n_head * c.d_head;
+    return bgemm_shape_ok(c.n_vocab, c.dim) && bgemm_shape_ok(2 * c.n_ff, c.dim) && bgemm_shape_ok(c.dim, c.n_ff) &&
+           bgemm_shape_ok(qd + 2 * c.n_kv * c.d_head, c.dim) && bgemm_shape_ok(c.dim, qd);
+}
 
 Layout plan(const ocr_text_cfg& c) {
     Planner p;
@@ -181,6 +193,16 @@ Layout plan(const ocr_text_cfg& c) {
     }
     L.tok = mat(c.n_vocab, c.dim);
     L.out_norm = p.take((size_t)c.dim * 4);
+    L.tc = tc_shapes(c);
+    if (L.tc) {
+        for (auto& lo : L.layers) {
+            lo.t_qkv = p.take(bgemm_tiled_bytes(lo.qkv.rows, lo.qkv.cols));
+            lo.t_o = p.take(bgemm_tiled_bytes(lo.o.rows, lo.o.cols));
+            lo.t_gu = p.take(bgemm_tiled_bytes(lo.gu.rows, lo.gu.cols));
+            lo.t_down = p.take(bgemm_tiled_bytes(lo.down.rows, lo.down.cols));
+        }
+        L.t_tok = p.take(bgemm_tiled_bytes(L.tok.rows, L.tok.cols));
+    }
     L.total = p.off;
     return L;
 }
@@ -206,13 +228,20 @@ ocr_status check_cfg(const ocr_text_cfg& c) {
     return OCR_OK;
 }
 
-// the layouts derived from the loaded weights (W_o's per-kv-head slices)
+// the layouts derived from the loaded weights (W_o's per-kv-head slices; the tile-major copies)
 void derive_weights(ocr_model* m, cudaStream_t st) {
     const auto& c = m->cfg;
     for (auto& L : m->layers) {
         launch_slice_o(st, L.o.w, L.o.rows, L.o.cols, c.n_kv, L.o_s);
         if (L.d_s) launch_slice_o(st, L.down.w, L.down.rows, L.down.cols, FFN_NCLU, L.d_s);
+        if (m->tc) {
+            launch_tile_q8_0(st, L.qkv, const_cast<uint8_t*>(L.bq_qkv.tiles));
+            launch_tile_q8_0(st, L.o, const_cast<uint8_t*>(L.bq_o.tiles));
+            launch_tile_q8_0(st, L.gu, const_cast<uint8_t*>(L.bq_gu.tiles));
+            launch_tile_q8_0(st, L.down, const_cast<uint8_t*>(L.bq_down.tiles));
+        }
     }
+    if (m->tc) launch_tile_q8_0(st, m->tok, const_cast<uint8_t*>(m->bq_tok.tiles));
 }
 
 ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
@@ -241,22 +270,18 @@ ocr_status model_alloc(ocr_ctx* ctx, const ocr_text_cfg& c, ocr_model** out) {
         w.ffn_norm = (float*)((char*)m->mem + lo.ffn_norm);
         w.o_s = (uint8_t*)m->mem + lo.o_s;
         w.d_s = lo.d_s ? (uint8_t*)m->mem + lo.d_s : nullptr;
+        if (L.tc) {
+            w.bq_qkv.tiles = (const uint8_t*)m->mem + lo.t_qkv;
+            w.bq_o.tiles = (const uint8_t*)m->mem + lo.t_o;
+            w.bq_gu.tiles = (const uint8_t*)m->mem + lo.t_gu;
+            w.bq_down.tiles = (const uint8_t*)m->mem + lo.t_down;
+        }
         m->layers.push_back(w);
     }
     m->tok = qmat(m->mem, L.tok);
     m->out_norm = (float*)((char*)m->mem + L.out_norm);
-    // the tensor maps of the batched contractions (they hold the matrices' addresses; the bytes come later)
-    const char* tc_env = getenv("OCR_TC");
-    m->tc = !(tc_env && tc_env[0] == '0') && bgemm_shape_ok(c.n_vocab, c.dim) && bgemm_shape_ok(2 * c.n_ff, c.dim) &&
-            bgemm_shape_ok(c.dim, c.n_ff) && bgemm_shape_ok(c.n_head * c.d_head + 2 * c.n_kv * c.d_head, c.dim) &&
-            bgemm_shape_ok(c.dim, c.n_head * c.d_head);
-    std::string why;
-    for (auto& w : m->layers) {
-        if (!m->tc) break;
-        m->tc = bgemm_maps(w.qkv, &w.bq_qkv, &why) && bgemm_maps(w.o, &w.bq_o, &why) &&
-                bgemm_maps(w.gu, &w.bq_gu, &why) && bgemm_maps(w.down, &w.bq_down, &why);
-    }
-    if (m->tc) m->tc = bgemm_maps(m->tok, &m->bq_tok, &why);
+    m->tc = L.tc;
+    if (m->tc) m->bq_tok.tiles = (const uint8_t*)m->mem + L.t_tok;
     *out = m;
     return OCR_OK;
 }
@@ -2038,15 +2063,16 @@ ocr_status ocr_op_matvec_q8_0(ocr_ctx* ctx, const uint8_t* d_w, int rows, int co
         w.rows = rows;
         w.cols = cols;
         w.stride = q8_stride(cols);
-        BgMaps maps;
-        std::string why;
-        if (!bgemm_maps(w, &maps, &why)) return fail(OCR_ERR_CUDA, why);
         const size_t groups = (size_t)(nb + BG_SLOTS - 1) / BG_SLOTS;
         const int ksplit = bgemm_ksplit(ctx->num_sms, rows, cols);
         const size_t xb = groups * x16_group_bytes(cols), pb = groups * bgemm_part_floats(rows, ksplit) * 4,
-                     tb = groups * (size_t)bgemm_tickets(rows) * 4;
-        OCR_TRY(ensure_op_scratch(ctx, xb + pb + tb));
+                     tb = (groups * (size_t)bgemm_tickets(rows) * 4 + 255) / 256 * 256, wb = bgemm_tiled_bytes(rows, cols);
+        OCR_TRY(ensure_op_scratch(ctx, xb + pb + tb + wb));
         OCR_CUDA(cudaMemsetAsync((char*)ctx->op_scratch + xb + pb, 0, tb, ctx->stream));
+        // the matrix's tile-major copy, in the scratch
+        BgMaps maps;
+        maps.tiles = (const uint8_t*)ctx->op_scratch + xb + pb + tb;
+        launch_tile_q8_0(ctx->stream, w, const_cast<uint8_t*>(maps.tiles));
         PrepArgs p;
         p.x = d_x;
         p.x_stride = cols;
