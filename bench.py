@@ -1,25 +1,29 @@
-"""bench.py — decode throughput of the B200 q8_0 text-decode engine (libocrcuda.so) on BASELINE config 2.
+"""bench.py — decode throughput of the B200 q8_0 text-decode engine (libocrcuda.so).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|1|3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 3|2|1|5]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N --steps K --warmup W
 
-Workload (config 2): a Qwen3-0.6B-shaped decoder (28 layers, dim 1024, 16/8 heads of 128,
-ffn 3072, vocab 151936, tied head) with seeded synthetic q8_0 weights (sigma 0.02) generated on the device; the f16
-KV cache prefilled (untimed) from 2048 seeded N(0,1) embedding rows; one step = a full greedy decode of 512 tokens
-with the windowed repetition penalty (rp 1.15, window 64, seeded with 64 x <|image_pad|>) through the C ABI
-(ocr_decode), preceded by re-feeding the prefix's last row (one prefill row, so every step starts from the same
-logits). Pages are independent: at N GPUs every rank decodes its own replica (weak scaling, no data-path
-collective); ranks only meet for the timing barrier and the max-over-ranks (gloo, host memory).
-The weights streamed per token (633 MB) exceed the 126 MB L2, so no flush is needed between steps.
+Default workload (config 3, BASELINE.json configs[2] — the largest single-GPU decode config, the per-B200 figure): a
+Qwen3-0.6B-shaped decoder (28 layers, dim 1024, 16/8 heads of 128, ffn 3072, vocab 151936, tied head) with seeded
+synthetic q8_0 weights (sigma 0.02) generated on the device; 32 sequences per GPU, each with its f16 KV cache
+prefilled (untimed) from 3072 seeded N(0,1) embedding rows; one step = a full greedy decode of 1024 tokens for all 32
+sequences with the windowed repetition penalty (rp 1.15, window 64, seeded with 64 x <|image_pad|>) through the C ABI
+(ocr_decode_batch: host history in, host ids out), preceded by re-feeding each prefix's last row (so every step starts
+from the same logits). Pages are independent: at N GPUs every rank decodes its own batch (weak scaling, no data-path
+collective); ranks only meet for the timing barrier and the max-over-ranks (gloo, host memory). The bytes streamed
+per step (633 MB of weights, 13 GB of KV rows) exceed the 126 MB L2, so no flush is needed between steps. At one GPU
+the line also carries config 2 (`config2`: one sequence, 2048-row prefix, 512 tokens) measured in the same run.
 
---config 1 (BASELINE configs[0]): the LM head + windowed penalty + greedy argmax alone (ocr_op_lm_head_sample),
+--config 2: one sequence per GPU, 2048-row prefix, 512 tokens.
+--config 1 (configs[0]): the LM head + windowed penalty + greedy argmax alone (ocr_op_lm_head_sample),
 x N(0,1) [1024], W [151936 x 1024] N(0, 0.02) q8_0, history 512 uniform ids, penalty 1.15 over the last 64.
---config 3: batched decode, 32 sequences per GPU (3072-row prefixes), 1024 tokens each.
+--config 5: the page sweep — 512 seeded pages (prefix U[1500,3072] rows, U[800,1500] tokens) claimed
+from a shared queue by one page engine per GPU (prefill included; strong scaling).
 
 --impl reference: the reference's own path cannot run here (Rust + WGSL on wgpu: no Rust toolchain, no graphics
 adapter), so the reference arm times the CPU restatement of it (oracle/, OpenMP on all host cores) on a bounded
-sample of the same workload, on rank 0 only.
+sample of the same workload (decode steps at positions spread over the decode), on rank 0 only.
 """
 from __future__ import annotations
 
@@ -513,7 +517,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=2)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3)
     ap.add_argument("--pages", type=int, default=0, help="config 5: pages in the sweep (default 512)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="config 3: skip the config-2 measurement beside it")
