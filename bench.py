@@ -170,14 +170,16 @@ def lm_head_kernel(ocr, ctx, torch, reps: int, flush_bytes: int = 256 << 20):
 
 
 def kernel_classes(sess, B, prefix_len, last_rows, steps=4):
-    """in-situ per-kernel times of the decode step (ocr_profile_step: an event after every launch, the same kernels
-    the timed graph replays), grouped by kernel class: launches, mean µs, algorithmic bytes per launch, share"""
+    """in-chain per-kernel times of the decode step (ocr_timeline_step: the step's launches chained as the timed
+    graph chains them, %globaltimer at every CTA's end; a launch's time is its latest CTA end less the previous
+    launch's, the last of 3 chained repetitions), grouped by kernel class: launches, mean µs, algorithmic bytes per
+    launch, share of the step"""
     for b in range(B):
         sess.rewind(b, prefix_len - 1)
         sess.prefill(b, embd=last_rows[b], logits=False)
     agg = {}
     for i in range(steps):
-        for k in sess.profile_step([IMAGE_PAD] * B):
+        for k in sess.timeline_step([IMAGE_PAD] * B, reps=3):
             a = agg.setdefault(k["name"], [0, 0.0, 0.0])
             a[0] += 1
             a[1] += k["us"]
@@ -204,7 +206,7 @@ def kernel_roofline(classes):
     return {"kernel": top["kernel"], "bound": "hbm", "achieved": top["achieved_gbs"], "peak": peak, "unit": "GB/s",
             "frac": top["frac"], "peak_source": f"{which} hbm_gbs (of {which})", "traffic": traffic,
             "us_per_launch": top["us_per_launch"], "algorithmic_bytes_per_launch": top["bytes_per_launch"],
-            "share_of_step": top["share"]}
+            "share_of_step": top["share"], "timing": "in-chain (%globaltimer per CTA, ocr_timeline_step)"}
 
 
 # ---------------------------------------------------------------------------------------------------------------------

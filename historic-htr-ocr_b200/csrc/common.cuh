@@ -121,6 +121,26 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* out) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---- the in-chain timeline ----
+// A launch given a slot records, from thread 0 of each of its CTAs, the latest CTA start, the latest release of its
+// dependency wait (griddepcontrol.wait) and the latest CTA end, in %globaltimer nanoseconds. Slots keep maxima, so a
+// slot written by several replays of one graph holds the last replay's times. A launch's in-chain time is the end of
+// its latest CTA less the end of the launch before it: what it adds to the chained step, overlap included.
+struct TlSlot {
+    unsigned long long start, dep, end, pad;
+};
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void tl_record(TlSlot* s, unsigned long long t_start, unsigned long long t_dep) {
+    if (!s) return;
+    atomicMax(&s->start, t_start);
+    atomicMax(&s->dep, t_dep);
+    atomicMax(&s->end, gtimer());
+}
+
 // device-side error flag (ocr_ctx_sync reports it): the first code wins
 enum DevErr : int { DEV_OK = 0, DEV_BAD_INDEX = 1, DEV_BAD_POS = 2, DEV_TIMEOUT = 3 };
 

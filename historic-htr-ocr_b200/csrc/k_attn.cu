@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     cg::cluster_group cluster = cg::this_cluster();
     const int b = blockIdx.z, j = blockIdx.y, sp = blockIdx.x, t = threadIdx.x;
     const int lane = t & 31, warp = t >> 5;
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
 
     // the slot's position was written by the previous step (its last kernel completed before this step began); the
     // conditions below are the same for every CTA of the cluster (same slot), so a cluster leaves together
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (fq && a.in.nw && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
+    const unsigned long long t_dep = a.tl ? gtimer() : 0ull;
 
     // the fused qkv projection: the slot's residual staged (plus the FFN's partials, RMS-normalised), this CTA's RQ
     // rows (RQ / NW per warp, their dots together), each value pushed into every CTA of the cluster (st.async into
@@ -491,6 +493,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
                 a.out[(long)b * a.out_stride + (j * G + g) * HD + d] = O / L;
             }
             cluster.sync();  // no CTA leaves while another still reads its partial
+            if (t == 0) tl_record(a.tl, t_start, t_dep);
             return;
         }
         // fused: reduce-scatter (this CTA merges its slice from the ranks' partials, copied in float4s), then all-gather
@@ -661,6 +664,7 @@ __global__ void __launch_bounds__(AT_THREADS, G <= 4 ? 2 : 1) k_attn_decode(Attn
         }
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (t == 0) tl_record(a.tl, t_start, t_dep);
 }
 
 int attention_splits(int num_sms, int nb, int n_kv, int n_ctx) {

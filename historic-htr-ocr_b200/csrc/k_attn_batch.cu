@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
     __shared__ uint32_t s_ticket;
     const int sp = blockIdx.x, j = blockIdx.y, b = blockIdx.z, split = gridDim.x;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
+    __shared__ unsigned long long t_dep;
     if (a.active && !a.active[b]) return;  // (uniform over the CTA)
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.n_ctx) {
@@ -112,6 +114,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
         const float4 cs = *reinterpret_cast<const float4*>(a.rope + (long)pos * AB_HD + 4 * lane);
         const int d0 = 2 * lane;  // this lane: dims d0, d0 + 1 and their RoPE partners 64 + d0, 64 + d0 + 1
         pdl_wait();
+        if (t == 0 && a.tl) t_dep = gtimer();
         for (int h = warp; h <= G; h += AB_WARPS) {
             if (h == G && !own) continue;
             const float* wv = h < G ? a.q_norm : a.k_norm;
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
             cta_part(q, cm, cl, co);
             emit(q, cl > 0.0f ? co / cl : 0.0f);
         }
+        if (t == 0) tl_record(a.tl, t_start, t_dep);
         return;
     }
     // the partials of the pair's CTAs: [pair][split][G][AB_PW]; the last CTA to finish merges them in split order
@@ -323,7 +327,10 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
     __syncthreads();
     if (t == 0) s_ticket = atomicAdd(&a.done[pair], 1u);
     __syncthreads();
-    if (s_ticket != (uint32_t)split - 1) return;
+    if (s_ticket != (uint32_t)split - 1) {
+        if (t == 0) tl_record(a.tl, t_start, t_dep);
+        return;
+    }
     __threadfence();
     const float* pp = a.part + pair * split * G * AB_PW;
     for (int q = t; q < G * AB_HD; q += AB_THREADS) {
@@ -340,7 +347,10 @@ __global__ void __launch_bounds__(AB_THREADS, 2) k_attn_batch(AttnBatchArgs a) {
             }
         emit(q, L > 0.0f ? O / L : 0.0f);
     }
-    if (t == 0) a.done[pair] = 0u;  // (self-resetting for the next launch)
+    if (t == 0) {
+        a.done[pair] = 0u;  // (self-resetting for the next launch)
+        tl_record(a.tl, t_start, t_dep);
+    }
 }
 
 int attn_batch_split(int num_sms, int nb, int n_kv) {

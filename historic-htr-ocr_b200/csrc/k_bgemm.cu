@@ -142,7 +142,8 @@ __device__ __forceinline__ void dequant16(uint4 q, __half d, uint32_t* hi, uint3
 }
 
 struct BgShared {
-    uint64_t tfull[BG_MAX_NS], tempty[BG_MAX_NS];  // copy stage landed / free again (MMAs done)
+    uint64_t wfull[BG_MAX_NS], xfull[BG_MAX_NS];  // a copy stage's weights / activations landed
+    uint64_t tempty[BG_MAX_NS];                    // the stage free again (its MMAs done)
     uint64_t afull[BG_NA], aempty[BG_NA];          // operand buffer written / free again
     uint64_t tfin, mdone;                          // an item's accumulator complete; every MMA done (exit)
     uint32_t tmem_base;
@@ -174,6 +175,8 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(16) BgShared sh;
     volatile int* abort_flag = &sh.abort_flag;
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
+    unsigned long long t_dep = 0ull;
 
     const int K = a.w.cols, N = a.w.rows;
     const int nkc = K / BG_KC, ksplit = a.ksplit;
@@ -189,7 +192,8 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < ns; i++) {
-            mbar_init(&sh.tfull[i], 1);
+            mbar_init(&sh.wfull[i], 1);
+            mbar_init(&sh.xfull[i], 1);
             mbar_init(&sh.tempty[i], 1);
         }
         for (int i = 0; i < na; i++) {
@@ -211,48 +215,58 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     const uint32_t tmem = sh.tmem_base;
 
     if (warp == 0) {
-        // ---- the copies ----
-        if (lane == 0) {
-            const uint64_t pol = l2_evict_first();
-            uint32_t g = 0;
-            int pre = 0;
-            const int w0 = blockIdx.x;
-            auto wblock = [&](int t, int kc) { return wtiles + ((size_t)t * nkc + kc) * BG_TILE_BYTES; };
-            if (w0 < n_items) {
-                // before the dependency wait: the weight blocks of the first item's first stages
-                const BgItem it = bg_item(w0, ksplit, nkc);
-                pre = min(ns, it.c1 - it.c0);
-                for (int s = 0; s < pre; s++) {
-                    mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                    bulk_g2s_stream(stage0 + (size_t)s * BG_STAGE, wblock(it.t, it.c0 + s), BG_WTILE, &sh.tfull[s], pol);
-                }
+        // ---- the copies: lane 0 waits and arms, the warp's lanes issue 4 KB pieces (the copy engine works on many at
+        // once; one long copy per stage drains slowly) ----
+        const uint64_t pol = l2_evict_first();
+        uint32_t g = 0;
+        int pre = 0;
+        const int w0 = blockIdx.x;
+        auto wblock = [&](int t, int kc) { return wtiles + ((size_t)t * nkc + kc) * BG_TILE_BYTES; };
+        if (w0 < n_items) {
+            // before the dependency wait: the weight blocks of the first item's first stages
+            const BgItem it = bg_item(w0, ksplit, nkc);
+            pre = min(ns, it.c1 - it.c0);
+            for (int s = 0; s < pre; s++) {
+                if (lane == 0) mbar_expect_tx(&sh.wfull[s], BG_WTILE);
+                __syncwarp();
+                bulk_g2s_lanes(stage0 + (size_t)s * BG_STAGE, wblock(it.t, it.c0 + s), BG_WTILE, &sh.wfull[s], pol,
+                               lane, 32);
             }
-            pdl_trigger();
-            pdl_wait();
-            bool ok = true;
-            for (int w = w0; w < n_items && ok; w += gridDim.x) {
-                const BgItem it = bg_item(w, ksplit, nkc);
-                for (int kc = it.c0; kc < it.c1; kc++, g++) {
-                    const int s = (int)(g % (uint32_t)ns);
-                    uint8_t* st = stage0 + (size_t)s * BG_STAGE;
-                    if (g >= (uint32_t)pre) {  // (the prologue issued the weights of the first `pre` stages)
-                        if (g >= (uint32_t)ns && !bg_wait(&sh.tempty[s], ((g / ns) - 1) & 1, abort_flag, a.err)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_expect_tx(&sh.tfull[s], BG_STAGE);
-                        bulk_g2s_stream(st, wblock(it.t, kc), BG_WTILE, &sh.tfull[s], pol);
+        }
+        if (lane == 0) pdl_trigger();
+        pdl_wait();
+        if (threadIdx.x == 0 && a.tl) t_dep = gtimer();
+        bool ok = true;
+        for (int w = w0; w < n_items && ok; w += gridDim.x) {
+            const BgItem it = bg_item(w, ksplit, nkc);
+            for (int kc = it.c0; kc < it.c1; kc++, g++) {
+                const int s = (int)(g % (uint32_t)ns);
+                uint8_t* st = stage0 + (size_t)s * BG_STAGE;
+                if (g >= (uint32_t)pre) {  // (the prologue issued the weights of the first `pre` stages)
+                    const bool got = g < (uint32_t)ns ||
+                                     (lane == 0 ? bg_wait(&sh.tempty[s], ((g / ns) - 1) & 1, abort_flag, a.err) : true);
+                    if (!__all_sync(FULL, got)) {
+                        ok = false;
+                        break;
                     }
-                    bulk_g2s(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.tfull[s]);
+                    if (lane == 0) mbar_expect_tx(&sh.wfull[s], BG_WTILE);
+                    __syncwarp();
+                    bulk_g2s_lanes(st, wblock(it.t, kc), BG_WTILE, &sh.wfull[s], pol, lane, 32);
                 }
+                if (lane == 0) mbar_expect_tx(&sh.xfull[s], BG_CHUNK_BYTES);
+                __syncwarp();
+                bulk_g2s_lanes(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
+                               lane, 32);
             }
-            // every copy issued lands before the CTA can exit (in a normal run these phases are long complete);
-            // a stage whose activations were never issued (an abort between its weights and them) is not waited for
-            const uint32_t issued = max(g, (uint32_t)pre);
-            for (int s = 0; s < ns && (uint32_t)s < issued; s++) {
-                const uint32_t n = (issued - s + ns - 1) / ns;
-                if (*abort_flag && (uint32_t)s + (n - 1) * ns >= g) continue;
-                mbar_wait(&sh.tfull[s], (n - 1) & 1, a.err);
+        }
+        // every copy issued lands before the CTA can exit (in a normal run these phases are long complete): the
+        // weights of stages [0, max(g, pre)), the activations of [0, g); a stage's last phase is the only one that
+        // can be incomplete (each reuse waited for the one before)
+        if (lane == 0) {
+            const uint32_t wi = max(g, (uint32_t)pre);
+            for (int s = 0; s < ns; s++) {
+                if ((uint32_t)s < wi) mbar_wait(&sh.wfull[s], (((wi - s + ns - 1) / ns) - 1) & 1, a.err);
+                if ((uint32_t)s < g) mbar_wait(&sh.xfull[s], (((g - s + ns - 1) / ns) - 1) & 1, a.err);
             }
         }
         __syncwarp();
@@ -266,7 +280,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 const BgItem it = bg_item(w, ksplit, nkc);
                 for (int kc = it.c0; kc < it.c1 && ok; kc++, g++) {
                     const int s = (int)(g % (uint32_t)ns);
-                    if (!bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err)) {
+                    if (!bg_wait(&sh.xfull[s], (g / ns) & 1, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
@@ -320,13 +334,10 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         best_i[j] = NO_INDEX;
     }
     if (warp >= 2) {
-        pdl_wait();
-        bool act[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int sl = 8 * part + j;
-            act[j] = sl < nb && (!a.active || a.active[slot0 + sl] != 0);
-        }
+        // The weights never depend on the previous kernel: the dequantisation of the first stages runs while it
+        // finishes. Everything the previous kernels write (the slots' states, the outputs this epilogue reads or
+        // adds to) is read after griddepcontrol.wait, at the first item's epilogue.
+        bool act[8] = {};
         // this thread's item of every 64-column piece: row 8 rg + r8, 16 columns c4; a quarter-warp takes 8 rows of one
         // 16-column piece — its reads through the copy's swizzle and its writes through the operand's (pieces 2 c4 and
         // 2 c4 + 1 of a row at (piece ^ row % 8)) are both conflict-free
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const BgItem it = bg_item(w, ksplit, nkc);
             for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
-                ok = ok && bg_wait(&sh.tfull[s], (g / ns) & 1, abort_flag, a.err);
+                ok = ok && bg_wait(&sh.wfull[s], (g / ns) & 1, abort_flag, a.err);
                 const uint8_t* wt = stage0 + (size_t)s * BG_STAGE + drow * 128;
                 const __half* sc = reinterpret_cast<const __half*>(stage0 + (size_t)s * BG_STAGE + 16384 + drow * 8);
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
@@ -365,6 +376,14 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             }
 
             // ---- the item's epilogue ----
+            if (li == 0) {
+                pdl_wait();
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int sl = 8 * part + j;
+                    act[j] = sl < nb && (!a.active || a.active[slot0 + sl] != 0);
+                }
+            }
             const int r0 = it.t * BG_M, row = r0 + 32 * q + lane;
             if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {
                 // the window's tokens that fall in this tile, per slot (the epilogue threads, barrier 2)
@@ -415,12 +434,29 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 bar_sync(2, BG_DQ);
                 if (sh.ticket != (uint32_t)ksplit - 1) continue;  // (uniform over the epilogue warps)
                 __threadfence();
+                // the partials summed in split order, 0 + p_0 + p_1 + …; the loads of four splits (32 values) are in
+                // flight together, so the sum waits for ksplit / 4 round trips to L2 rather than one per load
+                const float* pe = pt + (8 * part) * BG_M + 32 * q + lane;
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    float v = 0.0f;
-                    for (int r = 0; r < ksplit; r++)
-                        v += __ldcg(pt + (size_t)r * BG_SLOTS * BG_M + (8 * part + j) * BG_M + 32 * q + lane);
-                    y[j] = v;
+                for (int j = 0; j < 8; j++) y[j] = 0.0f;
+                int r = 0;
+                for (; r + 4 <= ksplit; r += 4) {
+                    float v[4][8];
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+#pragma unroll
+                        for (int j = 0; j < 8; j++) v[u][j] = __ldcg(pe + (size_t)(r + u) * BG_SLOTS * BG_M + j * BG_M);
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+#pragma unroll
+                        for (int j = 0; j < 8; j++) y[j] += v[u][j];
+                }
+                for (; r < ksplit; r++) {
+                    float v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) v[j] = __ldcg(pe + (size_t)r * BG_SLOTS * BG_M + j * BG_M);
+#pragma unroll
+                    for (int j = 0; j < 8; j++) y[j] += v[j];
                 }
                 if (et == 0) a.tickets[grp * n_tiles + it.t] = 0u;  // (self-resetting for the next launch)
             }
@@ -477,7 +513,10 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, BG_TMEM_COLS);
     }
-    if (!lmhead || !a.lm.sample) return;  // (uniform over the grid)
+    if (!lmhead || !a.lm.sample) {  // (uniform over the grid)
+        if (threadIdx.x == 0) tl_record(a.tl, t_start, t_dep);
+        return;
+    }
     // ---- the LM head's choice: each slot's best over the CTA's tiles, then the last CTA picks ----
     if (warp >= 2) {
 #pragma unroll
@@ -507,6 +546,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     }
     __syncthreads();
     choice_finish(sh.bv, sh.bi, nb, slot0, a.lm, N);
+    if (threadIdx.x == 0) tl_record(a.tl, t_start, t_dep);
 }
 
 // ---- the activations' operand: per slot, sum, norm, hi / lo split ---------------------------------------------------
@@ -516,8 +556,10 @@ __global__ void __launch_bounds__(XP_THREADS) k_xprep(PrepArgs a) {
     __shared__ float red[XP_THREADS / 32];
     const int b = blockIdx.x, K = a.K, n = b % BG_SLOTS;
     uint8_t* xg = a.x16 + (size_t)(b / BG_SLOTS) * x16_group_bytes(K);
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
     pdl_trigger();  // the contraction's weight copies may start; its activation copies wait for this grid
     pdl_wait();
+    const unsigned long long t_dep = a.tl ? gtimer() : 0ull;
     const bool live = b < a.nb && (!a.active || a.active[b] != 0);
     constexpr int IT = 2;  // items of 8 columns per thread: K <= 8 x 2 x 256
     float v[IT][8];
@@ -599,6 +641,10 @@ __global__ void __launch_bounds__(XP_THREADS) k_xprep(PrepArgs a) {
         }
         *reinterpret_cast<uint4*>(xg + x16_offset(n, k0)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         *reinterpret_cast<uint4*>(xg + x16_offset(BG_SLOTS + n, k0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    if (a.tl) {  // (uniform)
+        __syncthreads();
+        if (threadIdx.x == 0) tl_record(a.tl, t_start, t_dep);
     }
 }
 

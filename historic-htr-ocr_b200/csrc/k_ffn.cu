@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     __shared__ __align__(8) uint64_t bar_gu, bar_wd, bar_h;
     __shared__ float red[FFN_NW];
     const int r = blockIdx.x, c = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
     const int dim = DIM_T ? DIM_T : a.in.w.cols, n_ff = NFF_T ? NFF_T : a.n_ff;
     const int HC = n_ff / FFN_NCLU, HR = HC / FFN_CL, drows = dim / FFN_CL;
     const int gstride = q8_stride(dim), dstride = q8_stride(HC);
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
     float4 wn0 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (a.in.nw && dim <= 4 * FFN_THREADS && t < (dim >> 2)) wn0 = reinterpret_cast<const float4*>(a.in.nw)[t];
     pdl_wait();
+    const unsigned long long t_dep = a.tl ? gtimer() : 0ull;
 
     const int nch = (dim + 511) / 512;
     stage_x<DIM_T, NKV_T>(xs, nch, 1, 0, a.in, red, FFN_THREADS, wn0, r == 0 && c == 0);
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(FFN_THREADS, 2) k_ffn(FfnArgs a) {
         }
     }
     cluster_wait();
+    if (t == 0) tl_record(a.tl, t_start, t_dep);
 }
 
 int ffn_smem(int dim, int n_ff) {

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
     // (the compiled LM head runs a ring of LM_NS stages: its slot and phase arithmetic by constants)
     const int ns = KT ? LM_NS : ns_arg;
     extern __shared__ __align__(128) uint8_t sm[];
+    const unsigned long long t_start = a.tl ? gtimer() : 0ull;
+    unsigned long long t_dep = 0ull;
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + MAX_NS;
     constexpr int SR = W * R;
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
         if (a.nw && K <= 4 * NC && (int)threadIdx.x < (K >> 2)) wn0 = reinterpret_cast<const float4*>(a.nw)[threadIdx.x];
         if (lmhead) pen_prefilter(pl, nb, slot0, a.lm, lo, hi, NC);
         pdl_wait();
+        if (threadIdx.x == 0 && a.tl) t_dep = gtimer();
         // for the residual add, the first stages' old values of this warp's rows are fetched now so the epilogue's
         // read-modify-write does not wait on memory
         constexpr int PF = 2;
@@ -234,7 +237,10 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
             }
         }
     }
-    if (!lmhead || !a.lm.sample) return;  // (uniform over the grid)
+    if (!lmhead || !a.lm.sample) {  // (uniform over the grid)
+        if (threadIdx.x == 0) tl_record(a.tl, t_start, t_dep);
+        return;
+    }
     // ---- the LM head's choice: CTA reduce per slot, then the last CTA picks ----
     __syncthreads();
     if (warp < W) {
@@ -264,6 +270,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
     }
     __syncthreads();
     choice_finish(bv_sm, bi_sm, nb, slot0, a.lm, N);
+    if (threadIdx.x == 0) tl_record(a.tl, t_start, t_dep);
 }
 
 // ---- launch geometry --------------------------------------------------------------------------------------------------

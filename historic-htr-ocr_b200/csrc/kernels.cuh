@@ -130,6 +130,7 @@ struct MvArgs {
     LmArgs lm;   // MV_LMHEAD: the choice
     L2Next next;
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 constexpr int MAX_ADD = 8;
 void launch_matvec(cudaStream_t st, const MvArgs& a, int num_sms, bool pdl);
@@ -173,6 +174,7 @@ struct AttnArgs {
     int nb = 1;
     L2Next next;
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 void launch_attention_decode(cudaStream_t st, const AttnArgs& a, bool pdl);
 // the cluster size the launch of `a` will use (its `splits`, or fewer when those clusters cannot be resident)
@@ -196,6 +198,7 @@ struct FfnArgs {
     float* dpart = nullptr;  // [FFN_NCLU][dim]
     L2Next next;
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 // the dynamic shared memory the fused FFN needs for this shape, or 0 when the shape does not fit it
 int ffn_smem(int dim, int n_ff);
@@ -250,6 +253,7 @@ struct BgArgs {
     float* part = nullptr;
     uint32_t* tickets = nullptr;
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 // true when the tensor-core contraction takes this shape (cols a multiple of 256, at most 4096)
 bool bgemm_shape_ok(int rows, int cols);
@@ -280,6 +284,7 @@ struct PrepArgs {
     const int32_t* active = nullptr;
     uint8_t* x16 = nullptr;
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl);
 
@@ -306,6 +311,7 @@ struct AttnBatchArgs {
     float* part = nullptr;   // split > 1: [B * n_kv][split][G][132]
     uint32_t* done = nullptr;  // split > 1: [B * n_kv] tickets (zero between launches)
     int* err = nullptr;
+    TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 // CTAs per (slot, kv head) for a batch: enough to fill two CTAs per SM, at most AB_MAX_SPLIT
 int attn_batch_split(int num_sms, int nb, int n_kv);

@@ -553,11 +553,16 @@ struct Prof {
     std::vector<cudaEvent_t> ev;
     std::vector<ocr_kernel_time> rec;
     std::vector<int> pos;  // host positions of the active slots (the attention's key counts)
+    // the in-chain timeline (ocr_timeline_step): launch i records into tl[i]; no events, the launches chained
+    TlSlot* tl = nullptr;
+    int tl_cap = 0;
     void mark(const char* name, int layer, double bytes) {
-        cudaEvent_t e;
-        cudaEventCreate(&e);
-        cudaEventRecord(e, st);
-        ev.push_back(e);
+        if (!tl) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            cudaEventRecord(e, st);
+            ev.push_back(e);
+        }
         ocr_kernel_time k{};
         snprintf(k.name, sizeof(k.name), "%s", name);
         k.layer = layer;
@@ -567,6 +572,11 @@ struct Prof {
 };
 
 double mat_bytes(const QMat& w) { return (double)w.rows * w.stride; }
+
+// the timeline slot of the next launch (null unless a timeline is being recorded)
+TlSlot* tl_slot(const Prof* p) {
+    return p && p->tl && (int)p->rec.size() < p->tl_cap ? p->tl + p->rec.size() : nullptr;
+}
 
 LmArgs sampler_args(ocr_session* s, const ocr_sampler_cfg* cfg);
 
@@ -583,7 +593,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
     const auto& c = m->cfg;
     ocr_ctx* ctx = s->ctx;
     cudaStream_t st = ctx->stream;
-    const bool pdl = ctx->pdl && !prof;
+    const bool pdl = ctx->pdl && (!prof || prof->tl);
     const double nact = prof ? (double)prof->pos.size() : 0.0;
     auto prep = [&](int layer, const float* nw, const float* xadd, int n_add, bool embed, bool chain) {
         PrepArgs p;
@@ -603,6 +613,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
         p.active = s->active;
         p.x16 = s->x16a;
         p.err = ctx->d_err;
+        p.tl = tl_slot(prof);
         launch_xprep(st, p, chain);
         if (prof)
             prof->mark(embed ? "prep (embed, norm, hi/lo)" : xadd ? "prep (sum, norm, hi/lo)" : "prep (norm, hi/lo)",
@@ -620,6 +631,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
         g.nb = s->B;
         g.active = s->active;
         g.err = ctx->d_err;
+        g.tl = tl_slot(prof);
         if (mode != MV_LMHEAD) {
             g.ksplit = bgemm_ksplit(ctx->num_sms, w.rows, w.cols);
             g.part = s->bg_part;
@@ -658,6 +670,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
             a.part = s->ab_part;
             a.done = s->ab_done;
             a.err = ctx->d_err;
+            a.tl = tl_slot(prof);
             launch_attention_batch(st, a, s->ab_split, pdl);
             if (prof) prof->mark("attention (batched)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
             launch_bgemm(st, gemm(L.o, L.bq_o, s->x16o, MV_ADD, s->x, c.dim, nullptr), L.bq_o, ctx->num_sms, pdl);
@@ -687,6 +700,7 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
             a.wo = L.o_s;
             a.dim = c.dim;
             a.opart = s->opart;
+            a.tl = tl_slot(prof);
             launch_attention_decode(st, a, pdl);
             if (prof)
                 prof->mark("attention + o-proj", l,
@@ -727,8 +741,8 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
     ocr_ctx* ctx = s->ctx;
     cudaStream_t st = ctx->stream;
     // programmatic dependent launch chains each kernel to the one before it in the stream; the profiler's events
-    // between launches would break that chain, so a profiled step launches without it
-    const bool pdl = ctx->pdl && !prof;
+    // between launches would break that chain, so a profiled step launches without it (a timeline keeps it)
+    const bool pdl = ctx->pdl && (!prof || prof->tl);
     // each kernel pulls what a later kernel of the step reads into L2 (the attention's KV two kernels ahead, a
     // matrix two kernels ahead, past the attention which reads none)
     auto kv_of = [&](int l) {
@@ -831,9 +845,11 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         const bool fq = fqkv && attention_fuses_qkv(c.n_head / c.n_kv, attention_cluster(a), c.dim);
         if (!fq) {
             a.wqkv = QMat();
+            q.tl = tl_slot(prof);
             launch_matvec(st, q, ctx->num_sms, pdl && l > 0);
             if (prof) prof->mark("qkv (norm + q|k|v)", l, mat_bytes(L.qkv) + nact * (c.dim * 8.0 + s->qkv_w * 4.0));
         }
+        a.tl = tl_slot(prof);
         launch_attention_decode(st, a, pdl && (l > 0 || !fq));
         if (prof) {
             double kv = 0;
@@ -861,6 +877,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         o.active = s->active;
         o.err = ctx->d_err;
         o.next = with_w(L2Next(), L.down);
+        o.tl = tl_slot(prof);
         launch_matvec(st, o, ctx->num_sms, pdl);
         if (prof) prof->mark("o (+ residual)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
         }
@@ -885,6 +902,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
                 f.next.w2 = m->layers[l + 1].o_s;  // read by the next attention (its o-projection)
                 f.next.w2_bytes = (size_t)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv);
             }
+            f.tl = tl_slot(prof);
             launch_ffn(st, f, pdl);
             if (prof)
                 prof->mark("ffn (gate|up, swiglu, down)", l,
@@ -910,6 +928,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         f.active = s->active;
         f.err = ctx->d_err;
         if (l + 1 < c.n_layer) f.next = with_w(L2Next(), m->layers[l + 1].qkv);
+        f.tl = tl_slot(prof);
         launch_matvec(st, f, ctx->num_sms, pdl);
         if (prof)
             prof->mark(fused ? "sum + gate|up + swiglu" : "gate|up + swiglu", l,
@@ -926,6 +945,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         dn.active = s->active;
         dn.err = ctx->d_err;
         if (l + 1 < c.n_layer) dn.next = kv_of(l + 1);
+        dn.tl = tl_slot(prof);
         launch_matvec(st, dn, ctx->num_sms, pdl);
         if (prof) prof->mark("down (+ residual)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
     }
@@ -972,6 +992,7 @@ void record_step(ocr_session* s, bool sample, float rp, int window, int use_fp, 
         lm.next.w2 = m->layers[0].o_s;
         lm.next.w2_bytes = (size_t)c.n_kv * c.dim * q8_stride(s->qd / c.n_kv);
     }
+    lm.tl = tl_slot(prof);
     launch_matvec(st, lm, ctx->num_sms, pdl);
     if (prof)
         prof->mark(sample ? "lm head + choice" : "lm head", -1, mat_bytes(m->tok) + (prof ? prof->pos.size() : 0) * (c.dim * 8.0 + c.n_vocab * 4.0));
@@ -1786,6 +1807,72 @@ ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time*
     cudaEventDestroy(e0);
     if (e != cudaSuccess) return cuda_fail(e, "ocr_profile_step");
     OCR_TRY(check_device_error(ctx));
+    for (int b = 0; b < s->B; b++)
+        if (act[b]) {
+            s->n_past[b] += 1;
+            s->has_logits[b] = 1;
+        }
+    *n = k;
+    return OCR_OK;
+}
+
+ocr_status ocr_timeline_step(ocr_session* s, const int32_t* tok, int reps, ocr_kernel_time* out, int cap, int* n) {
+    if (!s || !tok || !out || !n) return fail(OCR_ERR_ARG, "null argument");
+    if (reps < 2 || reps > 16 || cap < 1) return fail(OCR_ERR_ARG, "reps must be 2..16 and cap at least 1");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    std::vector<int32_t> act(s->B), pos(s->B);
+    Prof prof;
+    for (int b = 0; b < s->B; b++) {
+        if (tok[b] >= c.n_vocab) return fail(OCR_ERR_ARG, "token " + std::to_string(tok[b]) + " is outside the vocabulary");
+        act[b] = tok[b] >= 0;
+        pos[b] = s->n_past[b];
+        if (act[b] && s->n_past[b] + 1 > s->n_ctx) return fail(OCR_ERR_STATE, "slot " + std::to_string(b) + ": the session is full");
+        if (act[b]) prof.pos.push_back(s->n_past[b]);
+    }
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    const int per_rep = 8 * c.n_layer + 8;  // an upper bound on the launches of one step (slots beyond it: an error)
+    const size_t slots = (size_t)reps * per_rep;
+    TlSlot* d_tl = nullptr;
+    OCR_CUDA(cudaMalloc((void**)&d_tl, slots * sizeof(TlSlot)));
+    cudaError_t e = cudaMemsetAsync(d_tl, 0, slots * sizeof(TlSlot), st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->tok, tok, s->B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st);
+    prof.st = st;
+    prof.tl = d_tl;
+    prof.tl_cap = (int)slots;
+    // the step `reps` times back to back in one graph, chained as the decode's graph chains its launches (each step's
+    // first launch waits for the whole step before it, as between two replays of the decode's graph)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        for (int r = 0; r < reps; r++) record_step(s, false, 1.0f, 1, 0, 0.0f, &prof);
+        e = cudaStreamEndCapture(st, &graph);
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    std::vector<TlSlot> h(prof.rec.size());
+    if (e == cudaSuccess && (int)prof.rec.size() > prof.tl_cap) e = cudaErrorInvalidValue;
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d_tl, h.size() * sizeof(TlSlot), cudaMemcpyDeviceToHost);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    cudaFree(d_tl);
+    if (e != cudaSuccess) return cuda_fail(e, "ocr_timeline_step");
+    OCR_TRY(check_device_error(ctx));
+    // the last repetition: each launch's in-chain time (its latest CTA end less the previous launch's)
+    const int per = (int)prof.rec.size() / reps, first = (reps - 1) * per;
+    const int k = std::min(cap, per);
+    for (int i = 0; i < k; i++) {
+        const int g = first + i;
+        ocr_kernel_time r = prof.rec[g];
+        const unsigned long long prev = h[g - 1].end, end = h[g].end;
+        r.us = (h[g].end && prev && end > prev) ? (float)((double)(end - prev) * 1e-3) : 0.0f;
+        out[i] = r;
+    }
     for (int b = 0; b < s->B; b++)
         if (act[b]) {
             s->n_past[b] += 1;

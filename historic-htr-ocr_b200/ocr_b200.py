@@ -90,6 +90,7 @@ _SIGS = {
     "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
     "ocr_read_pages": (C.c_int, [_P, C.POINTER(SamplerCfg), C.c_int, C.POINTER(PageIO)]),
     "ocr_profile_step": (C.c_int, [_P, _P, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
+    "ocr_timeline_step": (C.c_int, [_P, _P, C.c_int, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
     "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
     "ocr_gguf_open_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
@@ -373,6 +374,16 @@ class Session:
         out = (KernelTime * 1024)()
         n = C.c_int(0)
         _check(lib().ocr_profile_step(self.h, _ptr(t), out, 1024, C.byref(n)))
+        return [dict(name=out[i].name.decode(), layer=out[i].layer, us=out[i].us, bytes=out[i].bytes)
+                for i in range(n.value)]
+
+    def timeline_step(self, tokens: Sequence[int], reps: int = 3) -> list[dict]:
+        """the in-chain times of one decode step: the step chained as the decode's graph runs it, `reps` times in one
+        graph, each launch of the last repetition with the time it adds to the chain ({name, layer, us, bytes})"""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = (KernelTime * 1024)()
+        n = C.c_int(0)
+        _check(lib().ocr_timeline_step(self.h, _ptr(t), reps, out, 1024, C.byref(n)))
         return [dict(name=out[i].name.decode(), layer=out[i].layer, us=out[i].us, bytes=out[i].bytes)
                 for i in range(n.value)]
 

@@ -130,6 +130,13 @@ typedef struct {
     double bytes;
 } ocr_kernel_time;
 ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time* out, int cap, int* n);
+/* The in-chain timeline of one decode step (the same slots and tokens as ocr_profile_step): the step captured `reps`
+   (2..16) times back to back into one graph whose launches are chained as the decode's graph chains them
+   (programmatic dependent launch), each CTA recording %globaltimer at its start, at its dependency wait's release and
+   at its end. Reports the last repetition's launches: `us` = the end of the launch's latest CTA less the end of the
+   launch before it (what the launch adds to the chained step). Positions do not advance between repetitions; after
+   the call each active slot holds one more token, as after ocr_profile_step. Test and inspection entry point. */
+ocr_status ocr_timeline_step(ocr_session* s, const int32_t* tok, int reps, ocr_kernel_time* out, int cap, int* n);
 
 /* the same for every slot at once (batched decode; each slot its own history): history [batch][n_hist] (a shared
  * length), ids_out [batch][max_new]. All slots run max_new choices. */

@@ -154,6 +154,25 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
     assert len(rec) == 7 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
 
 
+def test_tensor_core_timeline_step(ocr, orc, ctx):
+    """the in-chain timeline runs the same launches as the profiler (chained, three times in one graph), every launch
+    of the last repetition ends after the one before it, and the step leaves the state a plain step leaves: the next
+    step's logits equal those of a session that took the step without the timeline"""
+    cfg = BATCH_CFG
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
+    a, b = gm.session(32, batch=16), gm.session(32, batch=16)
+    for s in (a, b):
+        for k in range(16):
+            s.prefill(k, ids=[1 + k, 2, 3, 4, 5], logits=False)
+    rec = a.timeline_step([7] * 16, reps=3)
+    prof = b.profile_step([7] * 16)
+    assert [r["name"] for r in rec] == [r["name"] for r in prof]
+    assert all(r["us"] > 0 for r in rec) and all(r["bytes"] == p["bytes"] for r, p in zip(rec, prof))
+    assert a.n_past(0) == b.n_past(0) == 6
+    la, lb = a.step([9] * 16), b.step([9] * 16)
+    assert np.array_equal(la, lb)
+
+
 # Below this top-2 gap (logit units; about 3e-5 of the largest |logit| here) the order of f32 summation decides the
 # greedy choice: the oracle sums in f64, the device in f32 in another order. A device sequence may leave the oracle's at
 # such a step only by taking the oracle's runner-up there (the comparison ends at that step); anywhere else the ids

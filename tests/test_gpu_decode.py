@@ -238,6 +238,20 @@ def test_profile_step_matches_step(ocr, orc, ctx, tiny):
     assert np.array_equal(la[0], lb2) and np.isfinite(lb).all()
 
 
+def test_timeline_step_matches_step(ocr, orc, ctx, tiny):
+    """the in-chain timeline of the one-slot step: the profiler's kernels, chained; positive in-chain times; the next
+    step's logits equal a plain session's"""
+    om, gm = tiny
+    prompt = [int(t) for t in orc.fill_ids(12, 10, TINY["n_vocab"])]
+    a, b = gm.session(32), gm.session(32)
+    a.prefill(0, ids=prompt, logits=False)
+    b.prefill(0, ids=prompt, logits=False)
+    rec = a.timeline_step([7], reps=2)
+    assert [r["name"] for r in rec] == [r["name"] for r in b.profile_step([7])]
+    assert all(r["us"] > 0 for r in rec) and a.n_past(0) == b.n_past(0)
+    assert np.array_equal(a.step([9])[0], b.step([9])[0])
+
+
 def test_handles_release_in_any_order(ocr, orc):
     """a context outlives its handle while a model or session made in it lives (a garbage collector may release
     them in any order): the session still steps after the context and model handles are gone"""
