@@ -217,12 +217,14 @@ WORKLOADS = {2: dict(B=1, prefix=PREFIX, new=NEW), 3: dict(B=32, prefix=3072, ne
              5: dict(B=32, prefix=2286, new=1150)}  # (config 5: its mean page, for the CPU samples' positions)
 
 
-def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0):
+def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0, prefix=0, profile_range=False):
     """one replica's decode throughput on a config: the model, each slot's prefix prefilled (untimed), then `steps`
     timed steps of a full greedy decode of every slot through the C ABI (host history in, host ids out). Returns the
-    timing and the session (for the per-kernel profile)."""
+    timing and the session (for the per-kernel profile). `tokens` / `prefix` shrink the workload for profiler
+    captures; `profile_range` brackets the first timed step with cudaProfilerStart / Stop (ncu
+    --profile-from-start off captures that step's launches only)."""
     w = WORKLOADS[config]
-    B, prefix_len, new = w["B"], w["prefix"], tokens or w["new"]
+    B, prefix_len, new = w["B"], prefix or w["prefix"], tokens or w["new"]
     seed = ocr.SEED_BASE + 2
     model = ocr.TextModel.synthetic(ctx, ocr.TextConfig(**CONFIG2), seed, 0.02, 0.02)
     sess = model.session(prefix_len + new, batch=B)
@@ -254,8 +256,13 @@ def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0)
     with Clocks(local) as clk:
         t0 = time.perf_counter()
         ev0.record(stream)
-        for _ in range(steps):
+        for i in range(steps):
+            if profile_range and i == 0:
+                torch.cuda.profiler.start()
             step()
+            if profile_range and i == 0:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.stop()
         ev1.record(stream)
         ev1.synchronize()
         wall = time.perf_counter() - t0
@@ -284,7 +291,8 @@ def run_ours(args):
         return run_config1(args, ocr, ctx, torch, pg, rank, world)
     if args.config == 5:
         return run_config5(args, ocr, ctx, torch, pg if pg else None, rank, world, local)
-    r = decode_workload(ocr, ctx, torch, args.config, args.steps, args.warmup, pg, local, args.tokens)
+    r = decode_workload(ocr, ctx, torch, args.config, args.steps, args.warmup, pg, local, args.tokens, args.prefix,
+                        args.profile_range)
     B, prefix_len, new, dev_s, wall = r["B"], r["prefix"], r["new"], r["dev_s"], r["wall"]
     tokens = world * B * new * args.steps
     out = None
@@ -525,6 +533,10 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="config 3: skip the config-2 measurement beside it")
     ap.add_argument("--tokens", type=int, default=0,
                     help="decode this many tokens per step instead of the config's (short runs for ncu captures)")
+    ap.add_argument("--prefix", type=int, default=0,
+                    help="prefix rows per slot instead of the config's (small cases for ncu captures)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the first timed step with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

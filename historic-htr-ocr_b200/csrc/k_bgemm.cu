@@ -154,6 +154,7 @@ struct BgShared {
     uint32_t biq[BG_DW][8];
     float bv[BG_SLOTS];
     uint32_t bi[BG_SLOTS];
+    float ssq[4][BG_SLOTS];  // MV_ADD with ssq_out: the tile's sums of squares per TMEM lane quarter and slot
 };
 
 // Work items: item w is (tile w / ksplit, split w % ksplit); a split covers chunks [c0, c1) of the K/128 chunks.
@@ -170,6 +171,7 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
     return it;
 }
 
+// (18 warps: 5 on two of the SM's four sub-partitions, whose 16K registers each cap a thread at 96)
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const uint8_t* __restrict__ wtiles, int ns, int na) {
     extern __shared__ uint8_t sm_raw[];
@@ -189,11 +191,17 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool lmhead = a.mode == MV_LMHEAD;
+    // the in-kernel operand needs one item per CTA whose chunks fit the stages (the host checks; a launch that breaks
+    // it is refused here, before any barrier or TMEM)
+    if (a.xn && (n_items > (int)gridDim.x || (nkc + ksplit - 1) / ksplit > ns)) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) dev_error(a.err, DEV_BAD_INDEX);
+        return;
+    }
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < ns; i++) {
             mbar_init(&sh.wfull[i], 1);
-            mbar_init(&sh.xfull[i], 1);
+            mbar_init(&sh.xfull[i], a.xn ? BG_DW : 1);  // the copy's bytes, or each operand-building warp
             mbar_init(&sh.tempty[i], 1);
         }
         for (int i = 0; i < na; i++) {
@@ -253,6 +261,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     __syncwarp();
                     bulk_g2s_lanes(st, wblock(it.t, kc), BG_WTILE, &sh.wfull[s], pol, lane, 32);
                 }
+                if (a.xn) continue;  // (the operand is built by warps 2-17)
                 if (lane == 0) mbar_expect_tx(&sh.xfull[s], BG_CHUNK_BYTES);
                 __syncwarp();
                 bulk_g2s_lanes(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
@@ -266,7 +275,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const uint32_t wi = max(g, (uint32_t)pre);
             for (int s = 0; s < ns; s++) {
                 if ((uint32_t)s < wi) mbar_wait(&sh.wfull[s], (((wi - s + ns - 1) / ns) - 1) & 1, a.err);
-                if ((uint32_t)s < g) mbar_wait(&sh.xfull[s], (((g - s + ns - 1) / ns) - 1) & 1, a.err);
+                if ((uint32_t)s < g && !a.xn) mbar_wait(&sh.xfull[s], (((g - s + ns - 1) / ns) - 1) & 1, a.err);
             }
         }
         __syncwarp();
@@ -346,6 +355,48 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
 
         // A warp whose wait gave up (ok = false) still walks every loop, skipping waits and work, so that all sixteen
         // warps meet each named barrier of the epilogue the same number of times.
+        // The normalised operand built here (a.xn; one item per CTA, its chunk c in stage c - c0): after the
+        // dependency wait, each thread takes slot et / 16's 8 columns (et % 16) of every chunk: the residual row
+        // times 1 / sqrt(mean of squares + eps) (the sums of squares over the row's 128-column tiles added in tile
+        // order) times the norm weights, split f16 hi / lo into the stage's operand region, as the operand copy would
+        // have landed it.
+        bool xbuilt = a.xn == nullptr;
+        auto build_x = [&](const BgItem& it) {
+            pdl_wait();
+            const int n = et >> 4, pc = et & 15, b = slot0 + n;
+            const bool live = n < nb && (!a.active || a.active[b] != 0);
+            float scale = 0.0f;
+            if (live) {
+                float tot = 0.0f;
+                for (int t = 0; t < K / BG_KC; t++) tot += a.ssq_in[(size_t)t * a.nb + b];
+                scale = 1.0f / sqrtf(tot / (float)K + a.eps);
+            }
+            for (int kc = it.c0; kc < it.c1; kc++) {
+                const int s = kc - it.c0, k0 = kc * BG_KC + pc * 8;
+                uint8_t* xs = stage0 + (size_t)s * BG_STAGE + BG_WTILE;
+                uint32_t hi[4] = {0u, 0u, 0u, 0u}, lo[4] = {0u, 0u, 0u, 0u};
+                if (live) {
+                    const float2* xr = reinterpret_cast<const float2*>(a.xn + (size_t)b * K + k0);
+                    const float2* wr = reinterpret_cast<const float2*>(a.nw + k0);
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const float2 xv = xr[c], wv = wr[c];
+                        const float v0 = xv.x * scale * wv.x, v1 = xv.y * scale * wv.y;
+                        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+                        const __half l0 = __float2half_rn(v0 - __half2float(h0));
+                        const __half l1 = __float2half_rn(v1 - __half2float(h1));
+                        const __half2 hh = __halves2half2(h0, h1), ll = __halves2half2(l0, l1);
+                        hi[c] = *reinterpret_cast<const uint32_t*>(&hh);
+                        lo[c] = *reinterpret_cast<const uint32_t*>(&ll);
+                    }
+                }
+                *reinterpret_cast<uint4*>(xs + x16_offset(n, pc * 8)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(xs + x16_offset(BG_SLOTS + n, pc * 8)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.xfull[s]);
+            }
+        };
         uint32_t g = 0, ai = 0;
         int li = 0;
         bool ok = true;
@@ -358,6 +409,11 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 const __half* sc = reinterpret_cast<const __half*>(stage0 + (size_t)s * BG_STAGE + 16384 + drow * 8);
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                     const int ab = (int)(ai % na);
+                    // (one call site: before the first piece that waits for the tensor cores, or the item's last)
+                    if (!xbuilt && (ai >= (uint32_t)na || (kc == it.c1 - 1 && h == BG_KC / BG_KS - 1))) {
+                        build_x(it);
+                        xbuilt = true;
+                    }
                     ok = ok && (ai < (uint32_t)na || bg_wait(&sh.aempty[ab], ((ai / na) - 1) & 1, abort_flag, a.err));
                     if (!ok) continue;
                     uint8_t* ah = abuf0 + (size_t)ab * BG_ABUF;
@@ -459,6 +515,26 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     for (int j = 0; j < 8; j++) y[j] += v[j];
                 }
                 if (et == 0) a.tickets[grp * n_tiles + it.t] = 0u;  // (self-resetting for the next launch)
+            }
+            if (a.ssq_out) {
+                // the residual add, then its rows' sums of squares per slot for the next norm: the warp's 32 rows,
+                // the tile's 4 lane quarters added in order (every warp meets the barriers, ok or not)
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    float sq = 0.0f;
+                    if (ok && act[j] && row < N) {
+                        float* yp = a.y + (long)(slot0 + 8 * part + j) * a.y_stride + row;
+                        const float v = a.mode == MV_ADD ? *yp + y[j] : y[j];
+                        *yp = v;
+                        sq = v * v;
+                    }
+                    sq = warp_sum(sq);
+                    if (lane == 0) sh.ssq[q][8 * part + j] = sq;
+                }
+                bar_sync(2, BG_DQ);
+                if (et < nb) a.ssq_out[(size_t)it.t * a.nb + slot0 + et] = ((sh.ssq[0][et] + sh.ssq[1][et]) + sh.ssq[2][et]) + sh.ssq[3][et];
+                bar_sync(2, BG_DQ);
+                continue;
             }
             if (!ok) continue;
             if (a.mode == MV_SWIGLU) {
@@ -702,18 +778,29 @@ static int bg_static_smem() {
     return bytes;
 }
 
+// shared memory: ns copy stages and na operand buffers (+ the 1024-B alignment slack): as many operand buffers as fit
+// beside 3 stages, then as many stages as fit
+static void bg_ring(int& ns, int& na, int& fixed) {
+    const int room = BG_SMEM_OPTIN - bg_static_smem() - 1024;
+    na = std::max(2, std::min(BG_NA, (room - 3 * (int)BG_STAGE) / (int)BG_ABUF));
+    fixed = na * (int)BG_ABUF + 1024;
+    ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
+}
+
+bool bgemm_norm_in_ok(int num_sms, int rows, int cols, int ksplit) {
+    int ns, na, fixed;
+    bg_ring(ns, na, fixed);
+    const int items = (rows + BG_M - 1) / BG_M * ksplit, nkc = cols / BG_KC;
+    return bgemm_shape_ok(rows, cols) && items <= bgemm_grid(num_sms, rows, ksplit) && (nkc + ksplit - 1) / ksplit <= ns;
+}
+
 void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms, bool pdl) {
     static PerDeviceOnce once;
     once([] {
         cudaFuncSetAttribute(k_bgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
     });
-    const int K = a.w.cols;
-    // shared memory: ns copy stages and na operand buffers (+ the 1024-B alignment slack): as many operand buffers as
-    // fit beside 3 stages, then as many stages as fit
-    const int room = BG_SMEM_OPTIN - bg_static_smem() - 1024;
-    const int na = std::max(2, std::min(BG_NA, (room - 3 * (int)BG_STAGE) / (int)BG_ABUF));
-    const int fixed = na * (int)BG_ABUF + 1024;
-    const int ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
+    int ns, na, fixed;
+    bg_ring(ns, na, fixed);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
     cfg.blockDim = dim3(BG_THREADS, 1, 1);

@@ -252,11 +252,24 @@ struct BgArgs {
     int ksplit = 1;
     float* part = nullptr;
     uint32_t* tickets = nullptr;
+    // The RMS-normalised operand built in the kernel (instead of copied from x16): the slots' residual rows xn [B][K],
+    // the norm weights nw [K], and the sums of squares of each row over K/128 column tiles, ssq_in [K/128][B] (written
+    // by the contraction that produced the residual). Then every CTA takes one work item whose K chunks fit its stages
+    // (bgemm_norm_in_ok).
+    const float* xn = nullptr;
+    const float* nw = nullptr;
+    const float* ssq_in = nullptr;
+    float eps = 1e-6f;
+    // MV_ADD: the new residual rows' sums of squares per 128-row tile, ssq_out [rows/128][B] (for the next norm)
+    float* ssq_out = nullptr;
     int* err = nullptr;
     TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
 // true when the tensor-core contraction takes this shape (cols a multiple of 256, at most 4096)
 bool bgemm_shape_ok(int rows, int cols);
+// true when a launch of this shape can build its normalised operand in the kernel (BgArgs::xn): one work item per
+// CTA, each item's K chunks at most the copy stages
+bool bgemm_norm_in_ok(int num_sms, int rows, int cols, int ksplit);
 // CTAs of a launch: one per work item (a 128-row tile's split), at most one per SM (a persistent CTA takes items
 // blockIdx.x + k * grid)
 int bgemm_grid(int num_sms, int rows, int ksplit = 1);

@@ -518,6 +518,9 @@ struct ocr_session {
     uint32_t* ab_done = nullptr;  // [B * n_kv] tickets
     float* bg_part = nullptr;     // the split contractions' partials (sized for the largest)
     uint32_t* bg_tickets = nullptr;
+    // [dim / 128][B] the residual rows' sums of squares per 128-column tile, written by the residual-adding
+    // contractions, read by the next contraction that RMS-normalises its operand itself (null: separate prep kernels)
+    float* ssq = nullptr;
     float* lm_part = nullptr;
     uint32_t* lm_done = nullptr;
     int32_t *pos = nullptr, *len = nullptr, *tok = nullptr, *active = nullptr;
@@ -639,11 +642,27 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
         }
         return g;
     };
+    // the norms inside the contractions: the residual-adding ones write the new rows' sums of squares, the qkv
+    // (layers after the first) and gate|up contractions build their normalised operand from the residual
+    const bool nin = s->ssq != nullptr && s->battn;
+    auto norm_in = [&](BgArgs g, const float* nw) {
+        g.xn = s->x;
+        g.nw = nw;
+        g.ssq_in = s->ssq;
+        g.eps = c.eps;
+        return g;
+    };
+    auto ssq_out = [&](BgArgs g) {
+        if (nin) g.ssq_out = s->ssq;
+        return g;
+    };
     for (int l = 0; l < c.n_layer; l++) {
         const LayerW& L = m->layers[l];
-        prep(l, L.attn_norm, nullptr, 0, l == 0 && !x_given, pdl && l > 0);
-        launch_bgemm(st, gemm(L.qkv, L.bq_qkv, s->x16a, MV_STORE, s->qkv, s->qkv_w, nullptr), L.bq_qkv, ctx->num_sms,
-                     pdl);
+        const bool qkv_in = nin && l > 0;
+        if (!qkv_in) prep(l, L.attn_norm, nullptr, 0, l == 0 && !x_given, pdl && l > 0);
+        BgArgs gq = gemm(L.qkv, L.bq_qkv, s->x16a, MV_STORE, s->qkv, s->qkv_w, nullptr);
+        if (qkv_in) gq = norm_in(gq, L.attn_norm);
+        launch_bgemm(st, gq, L.bq_qkv, ctx->num_sms, pdl);
         if (prof) prof->mark("qkv (tcgen05)", l, mat_bytes(L.qkv) + nact * (c.dim * 4.0 + s->qkv_w * 4.0));
         double kv = 0;
         if (prof)
@@ -673,9 +692,9 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
             a.tl = tl_slot(prof);
             launch_attention_batch(st, a, s->ab_split, pdl);
             if (prof) prof->mark("attention (batched)", l, kv + nact * (s->qkv_w * 4.0 + s->qd * 4.0));
-            launch_bgemm(st, gemm(L.o, L.bq_o, s->x16o, MV_ADD, s->x, c.dim, nullptr), L.bq_o, ctx->num_sms, pdl);
+            launch_bgemm(st, ssq_out(gemm(L.o, L.bq_o, s->x16o, MV_ADD, s->x, c.dim, nullptr)), L.bq_o, ctx->num_sms, pdl);
             if (prof) prof->mark("o + residual (tcgen05)", l, mat_bytes(L.o) + nact * (s->qd * 4.0 + c.dim * 8.0));
-            prep(l, L.ffn_norm, nullptr, 0, false, pdl);
+            if (!nin) prep(l, L.ffn_norm, nullptr, 0, false, pdl);
         } else {
             AttnArgs a;
             a.qkv = s->qkv;
@@ -708,9 +727,12 @@ void record_step_tc(ocr_session* s, bool sample, float rp, int window, int use_f
                                nact * (s->qkv_w * 4.0 + c.n_kv * c.dim * 4.0));
             prep(l, L.ffn_norm, s->opart, c.n_kv, false, pdl);
         }
-        launch_bgemm(st, gemm(L.gu, L.bq_gu, s->x16a, MV_SWIGLU, nullptr, 0, s->x16g), L.bq_gu, ctx->num_sms, pdl);
+        BgArgs gg = gemm(L.gu, L.bq_gu, s->x16a, MV_SWIGLU, nullptr, 0, s->x16g);
+        if (nin) gg = norm_in(gg, L.ffn_norm);
+        launch_bgemm(st, gg, L.bq_gu, ctx->num_sms, pdl);
         if (prof) prof->mark("gate|up + swiglu (tcgen05)", l, mat_bytes(L.gu) + nact * (c.dim * 4.0 + c.n_ff * 4.0));
-        launch_bgemm(st, gemm(L.down, L.bq_down, s->x16g, MV_ADD, s->x, c.dim, nullptr), L.bq_down, ctx->num_sms, pdl);
+        launch_bgemm(st, ssq_out(gemm(L.down, L.bq_down, s->x16g, MV_ADD, s->x, c.dim, nullptr)), L.bq_down,
+                     ctx->num_sms, pdl);
         if (prof) prof->mark("down + residual (tcgen05)", l, mat_bytes(L.down) + nact * (c.n_ff * 4.0 + c.dim * 8.0));
     }
     prep(-1, m->out_norm, nullptr, 0, false, pdl);
@@ -1454,7 +1476,9 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
     const size_t o_x16a = tc ? p.take(groups * x16_group_bytes(c.dim)) : 0;
     const size_t o_x16g = tc ? p.take(groups * x16_group_bytes(c.n_ff)) : 0;
     const bool battn = tc && ba_on;
-    const int ab_split = battn ? attn_batch_split(ctx->num_sms, batch, c.n_kv) : 1;
+    int ab_split = battn ? attn_batch_split(ctx->num_sms, batch, c.n_kv) : 1;
+    const char* abs_env = getenv("OCR_AB_SPLIT");  // the attention's CTAs per (slot, kv head), for comparisons
+    if (battn && abs_env && atoi(abs_env) >= 1) ab_split = std::min(AB_MAX_SPLIT, atoi(abs_env));
     const size_t o_x16o = battn ? p.take(groups * x16_group_bytes(c.n_head * c.d_head)) : 0;
     const size_t o_abp = battn && ab_split > 1
                              ? p.take((size_t)batch * c.n_kv * ab_split * (c.n_head / c.n_kv) * 132 * 4) : 0;
@@ -1471,6 +1495,14 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         }
     }
     const size_t o_bgp = tc ? p.take(groups * bg_floats * 4) : 0;
+    // the norms folded into the qkv and gate|up contractions (their operand built in the kernel) when both shapes
+    // allow it; OCR_NORM_IN=0 keeps the separate prep kernels
+    const char* ni_env = getenv("OCR_NORM_IN");
+    const int qkv_rows = c.n_head * c.d_head + 2 * c.n_kv * c.d_head;
+    const bool norm_in = tc && ba_on && !(ni_env && ni_env[0] == '0') && c.dim % BG_SLOTS == 0 &&
+                         bgemm_norm_in_ok(ctx->num_sms, qkv_rows, c.dim, bgemm_ksplit(ctx->num_sms, qkv_rows, c.dim)) &&
+                         bgemm_norm_in_ok(ctx->num_sms, 2 * c.n_ff, c.dim, bgemm_ksplit(ctx->num_sms, 2 * c.n_ff, c.dim));
+    const size_t o_ssq = norm_in ? p.take((size_t)(c.dim / 128) * batch * 4) : 0;
     const size_t o_bgt = tc ? p.take(groups * (size_t)bg_tk * 4) : 0;
     const size_t o_qkv = p.take((size_t)batch * s->qkv_w * 4);
     const size_t o_attn = p.take((size_t)batch * s->qd * 4);
@@ -1502,6 +1534,7 @@ ocr_status ocr_session_create(ocr_model* m, int n_ctx, int batch, ocr_session** 
         s->bg_part = (float*)(w + o_bgp);
         s->bg_tickets = (uint32_t*)(w + o_bgt);
     }
+    if (norm_in) s->ssq = (float*)(w + o_ssq);
     if (battn) {
         s->battn = true;
         s->ab_split = ab_split;

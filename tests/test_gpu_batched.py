@@ -138,9 +138,15 @@ def test_batched_attention_over_many_tiles(ocr, orc, ctx, B):
             close_logits(lgs[b], los[b])
 
 
+LAYER = ["qkv (tcgen05)", "attention (batched)", "o + residual (tcgen05)", "gate|up + swiglu (tcgen05)",
+         "down + residual (tcgen05)"]
+
+
 def test_tensor_core_profile_step(ocr, orc, ctx):
-    """the profiler sees the batched step's kernels: per layer prep, qkv, the batched attention, the o-projection,
-    prep, gate|up, down; then the LM head's prep and contraction"""
+    """the profiler sees the batched step's kernels: layer 0's operand prep (the tokens' embedding rows, attn_norm),
+    then per layer qkv, the batched attention, the o-projection, gate|up, down — the later norms built inside the
+    qkv and gate|up contractions from the sums of squares the residual-adding ones leave — then the LM head's prep
+    and contraction"""
     cfg = BATCH_CFG
     gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 47, 0.2, 1.0)
     s = gm.session(32, batch=16)
@@ -148,10 +154,32 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
         s.prefill(b, ids=[1 + b, 2, 3, 4, 5], logits=False)
     rec = s.profile_step([7] * 16)
     names = [r["name"] for r in rec]
-    assert names[:7] == ["prep (embed, norm, hi/lo)", "qkv (tcgen05)", "attention (batched)", "o + residual (tcgen05)",
-                         "prep (norm, hi/lo)", "gate|up + swiglu (tcgen05)", "down + residual (tcgen05)"], names[:7]
-    assert names[-2:] == ["prep (norm, hi/lo)", "lm head (tcgen05)"]
-    assert len(rec) == 7 * cfg["n_layer"] + 2 and all(r["us"] > 0 for r in rec)
+    assert names == ["prep (embed, norm, hi/lo)"] + LAYER * cfg["n_layer"] + ["prep (norm, hi/lo)", "lm head (tcgen05)"]
+    assert all(r["us"] > 0 for r in rec)
+
+
+def test_norms_inside_contractions_match_separate_prep(ocr, orc, ctx, monkeypatch):
+    """the norms built inside the contractions (sums of squares per 128-row tile from the residual-adding
+    contraction, added in tile order) against the separate prep kernel (OCR_NORM_IN=0; one CTA's sum per row): the
+    same operand up to the order of the f32 sum of squares — logits within 1e-5 of max |logit| over 3 steps, and the
+    same greedy ids over 24 choices for every slot"""
+    cfg = BATCH_CFG
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 49, 0.2, 1.0)
+    sa = gm.session(64, batch=16)
+    monkeypatch.setenv("OCR_NORM_IN", "0")
+    sb = gm.session(64, batch=16)
+    monkeypatch.delenv("OCR_NORM_IN")
+    assert len(sb.profile_step([-1] * 16)) == 7 * cfg["n_layer"] + 2  # (no slot active: the launches only)
+    for s in (sa, sb):
+        for b in range(16):
+            s.prefill(b, ids=[3 + b, 5, 7, 11, 13, 17], logits=False)
+    for t in range(3):
+        la, lb = sa.step([20 + t] * 16), sb.step([20 + t] * 16)
+        m = np.abs(lb).max()
+        assert np.abs(la - lb).max() <= 1e-5 * m, np.abs(la - lb).max() / m
+    pre = ocr.Preset("t", 0.0, 1.0, 1.1, 8, 0.0, 24)
+    hist = np.full((16, 8), 3, np.int32)
+    assert np.array_equal(sa.decode_batch(pre, hist), sb.decode_batch(pre, hist))
 
 
 def test_tensor_core_timeline_step(ocr, orc, ctx):
