@@ -171,7 +171,11 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
     return it;
 }
 
+// One instance per epilogue mode (MODE = a.mode) and operand source (XN: built from the residual, a.xn; else copied
+// from x16): each launch runs only its own code, which keeps the warps' instruction fetches in cache (a single kernel
+// holding every epilogue stalled its warps on instruction fetch more than on anything else).
 // (18 warps: 5 on two of the SM's four sub-partitions, whose 16K registers each cap a thread at 96)
+template <int MODE, bool XN>
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const uint8_t* __restrict__ wtiles, int ns, int na) {
     extern __shared__ uint8_t sm_raw[];
@@ -190,10 +194,10 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bool lmhead = a.mode == MV_LMHEAD;
+    constexpr bool lmhead = MODE == MV_LMHEAD;
     // the in-kernel operand needs one item per CTA whose chunks fit the stages (the host checks; a launch that breaks
     // it is refused here, before any barrier or TMEM)
-    if (a.xn && (n_items > (int)gridDim.x || (nkc + ksplit - 1) / ksplit > ns)) {
+    if (XN && (n_items > (int)gridDim.x || (nkc + ksplit - 1) / ksplit > ns)) {
         if (threadIdx.x == 0 && blockIdx.x == 0) dev_error(a.err, DEV_BAD_INDEX);
         return;
     }
@@ -201,7 +205,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < ns; i++) {
             mbar_init(&sh.wfull[i], 1);
-            mbar_init(&sh.xfull[i], a.xn ? BG_DW : 1);  // the copy's bytes, or each operand-building warp
+            mbar_init(&sh.xfull[i], XN ? BG_DW : 1);  // the copy's bytes, or each operand-building warp
             mbar_init(&sh.tempty[i], 1);
         }
         for (int i = 0; i < na; i++) {
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     __syncwarp();
                     bulk_g2s_lanes(st, wblock(it.t, kc), BG_WTILE, &sh.wfull[s], pol, lane, 32);
                 }
-                if (a.xn) continue;  // (the operand is built by warps 2-17)
+                if (XN) continue;  // (the operand is built by warps 2-17)
                 if (lane == 0) mbar_expect_tx(&sh.xfull[s], BG_CHUNK_BYTES);
                 __syncwarp();
                 bulk_g2s_lanes(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
@@ -275,7 +279,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const uint32_t wi = max(g, (uint32_t)pre);
             for (int s = 0; s < ns; s++) {
                 if ((uint32_t)s < wi) mbar_wait(&sh.wfull[s], (((wi - s + ns - 1) / ns) - 1) & 1, a.err);
-                if ((uint32_t)s < g && !a.xn) mbar_wait(&sh.xfull[s], (((g - s + ns - 1) / ns) - 1) & 1, a.err);
+                if ((uint32_t)s < g && !XN) mbar_wait(&sh.xfull[s], (((g - s + ns - 1) / ns) - 1) & 1, a.err);
             }
         }
         __syncwarp();
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
         // times 1 / sqrt(mean of squares + eps) (the sums of squares over the row's 128-column tiles added in tile
         // order) times the norm weights, split f16 hi / lo into the stage's operand region, as the operand copy would
         // have landed it.
-        bool xbuilt = a.xn == nullptr;
+        bool xbuilt = !XN;
         auto build_x = [&](const BgItem& it) {
             pdl_wait();
             const int n = et >> 4, pc = et & 15, b = slot0 + n;
@@ -441,7 +445,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 }
             }
             const int r0 = it.t * BG_M, row = r0 + 32 * q + lane;
-            if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {
+            if (lmhead && a.lm.sample && a.lm.rp != 1.0f) {  // (compiled in the LM head's instance only)
                 // the window's tokens that fall in this tile, per slot (the epilogue threads, barrier 2)
                 uint32_t* pb = &sh.pbits[0][0];
                 for (int i = et; i < BG_SLOTS * (BG_M / 32); i += BG_DQ) pb[i] = 0u;
@@ -516,7 +520,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 }
                 if (et == 0) a.tickets[grp * n_tiles + it.t] = 0u;  // (self-resetting for the next launch)
             }
-            if (a.ssq_out) {
+            if (MODE == MV_ADD && a.ssq_out) {
                 // the residual add, then its rows' sums of squares per slot for the next norm: the warp's 32 rows,
                 // the tile's 4 lane quarters added in order (every warp meets the barriers, ok or not)
 #pragma unroll
@@ -524,7 +528,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     float sq = 0.0f;
                     if (ok && act[j] && row < N) {
                         float* yp = a.y + (long)(slot0 + 8 * part + j) * a.y_stride + row;
-                        const float v = a.mode == MV_ADD ? *yp + y[j] : y[j];
+                        const float v = MODE == MV_ADD ? *yp + y[j] : y[j];
                         *yp = v;
                         sq = v * v;
                     }
@@ -537,7 +541,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 continue;
             }
             if (!ok) continue;
-            if (a.mode == MV_SWIGLU) {
+            if (MODE == MV_SWIGLU) {
                 // rows interleaved (gate, up): the even lane of each pair writes silu(gate) * up
                 const int col = row >> 1;
                 uint8_t* y16 = a.y16 ? a.y16 + (size_t)grp * x16_group_bytes(N / 2) : nullptr;
@@ -562,7 +566,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     for (int j = 0; j < 8; j++) {
                         if (!act[j]) continue;
                         float* yp = a.y + (long)(slot0 + 8 * part + j) * a.y_stride + row;
-                        *yp = a.mode == MV_ADD ? *yp + y[j] : y[j];
+                        *yp = MODE == MV_ADD ? *yp + y[j] : y[j];
                     }
                 }
             } else if (row < N) {
@@ -769,11 +773,29 @@ void launch_tile_q8_0(cudaStream_t st, const QMat& w, uint8_t* out) {
     k_tile_q8_0<<<blocks, 256, 0, st>>>(w, out);
 }
 
+// the instances launched: (mode, operand built in the kernel)
+using BgKernel = void (*)(BgArgs, const uint8_t*, int, int);
+static BgKernel bg_kernel(int mode, bool xn) {
+    switch (mode) {
+        case MV_ADD: return xn ? nullptr : k_bgemm<MV_ADD, false>;
+        case MV_SWIGLU: return xn ? k_bgemm<MV_SWIGLU, true> : k_bgemm<MV_SWIGLU, false>;
+        case MV_LMHEAD: return xn ? nullptr : k_bgemm<MV_LMHEAD, false>;
+        default: return xn ? k_bgemm<MV_STORE, true> : k_bgemm<MV_STORE, false>;
+    }
+}
+static const BgKernel BG_ALL[] = {k_bgemm<MV_STORE, false>, k_bgemm<MV_STORE, true>, k_bgemm<MV_ADD, false>,
+                                  k_bgemm<MV_SWIGLU, false>, k_bgemm<MV_SWIGLU, true>, k_bgemm<MV_LMHEAD, false>};
+
+// the largest static shared memory of the instances (the dynamic budget is sized against it)
 static int bg_static_smem() {
     static int bytes = -1;
     if (bytes < 0) {
-        cudaFuncAttributes fa;
-        bytes = cudaFuncGetAttributes(&fa, k_bgemm) == cudaSuccess ? (int)fa.sharedSizeBytes : (int)sizeof(BgShared) + 64;
+        int b = (int)sizeof(BgShared) + 64;
+        for (BgKernel k : BG_ALL) {
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, k) == cudaSuccess) b = std::max(b, (int)fa.sharedSizeBytes);
+        }
+        bytes = b;
     }
     return bytes;
 }
@@ -797,7 +819,8 @@ bool bgemm_norm_in_ok(int num_sms, int rows, int cols, int ksplit) {
 void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms, bool pdl) {
     static PerDeviceOnce once;
     once([] {
-        cudaFuncSetAttribute(k_bgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
+        for (BgKernel k : BG_ALL)
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
     });
     int ns, na, fixed;
     bg_ring(ns, na, fixed);
@@ -811,7 +834,12 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, k_bgemm, a, m.tiles, ns, na);
+    const BgKernel k = bg_kernel(a.mode, a.xn != nullptr);
+    if (!k) {  // (an in-kernel operand for a mode that has no such instance: a caller's error, nothing launched)
+        fprintf(stderr, "launch_bgemm: mode %d has no instance with the operand built in the kernel\n", a.mode);
+        return;
+    }
+    cudaLaunchKernelEx(&cfg, k, a, m.tiles, ns, na);
 }
 
 void launch_xprep(cudaStream_t st, const PrepArgs& a, bool pdl) {
