@@ -122,6 +122,51 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
         stage_x<KT, KT ? FFN_NCLU : 0>(xsf, nch, nb, slot0, a, red, NC, wn0, blockIdx.x == 0);
         bar_sync(1, NC);
         const uint64_t* xsp = reinterpret_cast<const uint64_t*>(xsf);  // x as f32 pairs
+        // The compiled LM head (KT, one slot) takes the staged row as three int8 digits per 32-column block: with s
+        // the power of two at or above max|x| / 126 over the block, x / s = d0 + d1 / 128 + d2 / 128^2 + e with
+        // |d0| <= 126, |d1|, |d2| <= 64 and |e| <= 2^-15 (every step exact: power-of-two scalings and integer
+        // subtractions), so a quant row's dot is three integer dots (dp4a on the raw int8 weights: no conversion)
+        // combined once per 16 columns — about half the instructions of the f32 dot per quant.
+        constexpr bool DIG = KT != 0 && NB == 1;
+        const uint4* xdig = reinterpret_cast<const uint4*>(xsf);  // [nch][3 digits][32 lanes] x 16 int8
+        const float* xsc = xsf + 3 * 4 * 32 * nch;                   // [nch][16 blocks] the block scales s
+        if constexpr (DIG) {
+            const int tid = threadIdx.x, i = tid >> 5, l = tid & 31;
+            float v[16];
+            float m = 0.0f;
+            if (warp < nch) {  // (whole warps: lane pairs l, l ^ 1 hold one 32-column block)
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    const float4 f = reinterpret_cast<const float4*>(xsf)[(i * 4 + jj) * 32 + l];
+                    v[4 * jj] = f.x, v[4 * jj + 1] = f.y, v[4 * jj + 2] = f.z, v[4 * jj + 3] = f.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++) m = fmaxf(m, fabsf(v[j]));
+                m = fmaxf(m, __shfl_xor_sync(FULL, m, 1));
+            }
+            bar_sync(1, NC);  // every staged value read before the region holds the digits
+            if (warp < nch) {
+                int e = 0;
+                if (m > 0.0f) frexpf(m * (1.0f / 126.0f), &e);
+                const float sc_b = m > 0.0f ? ldexpf(1.0f, e) : 1.0f, inv = m > 0.0f ? ldexpf(1.0f, -e) : 1.0f;
+                uint32_t w[3][4] = {};
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float q = v[j] * inv;
+                    const float d0 = rintf(q), r1 = (q - d0) * 128.0f;
+                    const float d1 = rintf(r1), r2 = (r1 - d1) * 128.0f;
+                    const float d2 = rintf(r2);
+                    w[0][j >> 2] |= ((uint32_t)(int)d0 & 0xffu) << (8 * (j & 3));
+                    w[1][j >> 2] |= ((uint32_t)(int)d1 & 0xffu) << (8 * (j & 3));
+                    w[2][j >> 2] |= ((uint32_t)(int)d2 & 0xffu) << (8 * (j & 3));
+                }
+                uint4* xd = reinterpret_cast<uint4*>(xsf);
+#pragma unroll
+                for (int k = 0; k < 3; k++) xd[(i * 3 + k) * 32 + l] = make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]);
+                if (!(l & 1)) xsf[3 * 4 * 32 * nch + i * 16 + (l >> 1)] = sc_b;
+            }
+            bar_sync(1, NC);
+        }
         for (int t = 0; t < n_stage; t++) {
             const int slot = t % ns;
             if (!mbar_wait(&full[slot], (t / ns) & 1, a.err)) break;
@@ -145,10 +190,32 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
                             wq[r] = *reinterpret_cast<const uint4*>(row + col);
                             sc[r] = __half2float(reinterpret_cast<const __half*>(row + K)[col >> 5]);
                         } else {
-                            wq[r] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // q = 0
+                            // q = 0 (the f32 dot reads the quants biased by 128, the integer dot as they are)
+                            wq[r] = DIG ? make_uint4(0u, 0u, 0u, 0u)
+                                        : make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
                             sc[r] = 0.0f;
                         }
                     }
+                    if constexpr (DIG) {
+                        const uint4 e0 = xdig[(i * 3) * 32 + lane], e1 = xdig[(i * 3 + 1) * 32 + lane];
+                        const uint4 e2 = xdig[(i * 3 + 2) * 32 + lane];
+                        const float sb = xsc[i * 16 + (lane >> 1)];
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            const uint4 w = wq[r];
+                            int d0 = __dp4a((int)w.x, (int)e0.x, 0), d1 = __dp4a((int)w.x, (int)e1.x, 0),
+                                d2 = __dp4a((int)w.x, (int)e2.x, 0);
+                            d0 = __dp4a((int)w.y, (int)e0.y, d0), d1 = __dp4a((int)w.y, (int)e1.y, d1);
+                            d2 = __dp4a((int)w.y, (int)e2.y, d2);
+                            d0 = __dp4a((int)w.z, (int)e0.z, d0), d1 = __dp4a((int)w.z, (int)e1.z, d1);
+                            d2 = __dp4a((int)w.z, (int)e2.z, d2);
+                            d0 = __dp4a((int)w.w, (int)e0.w, d0), d1 = __dp4a((int)w.w, (int)e1.w, d1);
+                            d2 = __dp4a((int)w.w, (int)e2.w, d2);
+                            // (|d0| < 2^18: exact in f32; the digits' weights are powers of two)
+                            const float dv = fmaf((float)d2, 1.0f / 16384.0f, fmaf((float)d1, 1.0f / 128.0f, (float)d0));
+                            acc[0][r] = fmaf(dv, sc[r] * sb, acc[0][r]);
+                        }
+                    } else {
 #pragma unroll
                     for (int s = 0; s < NB; s++) {
                         if (s < nb) {
@@ -162,6 +229,7 @@ __global__ void __launch_bounds__((W + 1) * 32, (W == 8 && NB <= 2) ? 2 : 1) k_m
 #pragma unroll
                             for (int r = 0; r < R; r++) acc[s][r] = fmaf(dot16x2(wq[r], xp), sc[r], acc[s][r]);
                         }
+                    }
                     }
                 }
             }
