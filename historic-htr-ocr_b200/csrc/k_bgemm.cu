@@ -44,7 +44,6 @@ constexpr int BG_THREADS = 576;
 constexpr int BG_DQ = 512;      // dequantisation / epilogue threads (warps 2-17)
 constexpr int BG_DW = BG_DQ / 32;  // their warps: 4 per TMEM lane quarter, 8 slots each
 constexpr uint32_t BG_WTILE = BG_TILE_BYTES;                // a tile-major block: 16 KB of int8 quants + 1 KB of scales
-constexpr uint32_t BG_STAGE = BG_WTILE + BG_CHUNK_BYTES;   // + the activations' chunk: 33 KB (1024-B multiple)
 constexpr uint32_t BG_AHALF = BG_M * BG_KS * 2;             // 16 KB: the hi (or lo) f16 operand of a 64-column piece
 constexpr uint32_t BG_ABUF = 2 * BG_AHALF;
 constexpr int BG_NA = 4;        // operand buffers at most (2 to 4, as shared memory allows)
@@ -175,9 +174,15 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
 // from x16): each launch runs only its own code, which keeps the warps' instruction fetches in cache (a single kernel
 // holding every epilogue stalled its warps on instruction fetch more than on anything else).
 // (18 warps: 5 on two of the SM's four sub-partitions, whose 16K registers each cap a thread at 96)
-template <int MODE, bool XN>
+// NG: groups of 32 slots (rows of the activations) per CTA. Two for long prefills: each dequantised weight piece
+// then feeds the MMAs of both groups (2 accumulator sets each), halving the dequantisation per row; one item per CTA
+// pass, no split-K (the host picks it only for unsplit launches over more than one group).
+template <int MODE, bool XN, int NG = 1>
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const uint8_t* __restrict__ wtiles, int ns, int na) {
+    static_assert(NG == 1 || (NG == 2 && !XN && MODE != MV_LMHEAD), "two groups: plain operands, no LM head");
+    constexpr uint32_t STAGE = BG_WTILE + NG * BG_CHUNK_BYTES;  // weights + each group's activation chunk
+    constexpr int NSET = BG_NACC / NG;                             // accumulator sets per group
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(16) BgShared sh;
     volatile int* abort_flag = &sh.abort_flag;
@@ -189,9 +194,11 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     // the dynamic region starts 1024-B aligned (the 128-B swizzle's pattern repeats every 1024 B)
     uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
     uint8_t* stage0 = smp;
-    uint8_t* abuf0 = smp + (size_t)ns * BG_STAGE;
+    uint8_t* abuf0 = smp + (size_t)ns * STAGE;
     const int n_tiles = (N + BG_M - 1) / BG_M, n_items = n_tiles * ksplit;
-    const int grp = blockIdx.y, slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
+    // this CTA's groups grp … grp + ngr - 1 (slot0 / nb: the first group's)
+    const int grp = blockIdx.y * NG, ngr = min(NG, (a.nb + BG_SLOTS - 1) / BG_SLOTS - grp);
+    const int slot0 = grp * BG_SLOTS, nb = min(BG_SLOTS, a.nb - slot0);
     const uint8_t* xg = a.x16 + (size_t)grp * nkc * BG_CHUNK_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool lmhead = MODE == MV_LMHEAD;
@@ -241,7 +248,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             for (int s = 0; s < pre; s++) {
                 if (lane == 0) mbar_expect_tx(&sh.wfull[s], BG_WTILE);
                 __syncwarp();
-                bulk_g2s_lanes(stage0 + (size_t)s * BG_STAGE, wblock(it.t, it.c0 + s), BG_WTILE, &sh.wfull[s], pol,
+                bulk_g2s_lanes(stage0 + (size_t)s * STAGE, wblock(it.t, it.c0 + s), BG_WTILE, &sh.wfull[s], pol,
                                lane, 32);
             }
         }
@@ -253,7 +260,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             const BgItem it = bg_item(w, ksplit, nkc);
             for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
-                uint8_t* st = stage0 + (size_t)s * BG_STAGE;
+                uint8_t* st = stage0 + (size_t)s * STAGE;
                 if (g >= (uint32_t)pre) {  // (the prologue issued the weights of the first `pre` stages)
                     const bool got = g < (uint32_t)ns ||
                                      (lane == 0 ? bg_wait(&sh.tempty[s], ((g / ns) - 1) & 1, abort_flag, a.err) : true);
@@ -266,10 +273,12 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     bulk_g2s_lanes(st, wblock(it.t, kc), BG_WTILE, &sh.wfull[s], pol, lane, 32);
                 }
                 if (XN) continue;  // (the operand is built by warps 2-17)
-                if (lane == 0) mbar_expect_tx(&sh.xfull[s], BG_CHUNK_BYTES);
+                if (lane == 0) mbar_expect_tx(&sh.xfull[s], (uint32_t)ngr * BG_CHUNK_BYTES);
                 __syncwarp();
-                bulk_g2s_lanes(st + BG_WTILE, xg + (size_t)kc * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
-                               lane, 32);
+                for (int gi = 0; gi < ngr; gi++)
+                    bulk_g2s_lanes(st + BG_WTILE + gi * BG_CHUNK_BYTES,
+                                   xg + ((size_t)gi * nkc + kc) * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
+                                   lane, 32);
             }
         }
         // every copy issued lands before the CTA can exit (in a normal run these phases are long complete): the
@@ -297,7 +306,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t xs = smem_u32(stage0 + (size_t)s * BG_STAGE + BG_WTILE);
+                    const uint32_t xs = smem_u32(stage0 + (size_t)s * STAGE + BG_WTILE);
                     const int kstep0 = (kc - it.c0) * (BG_KC / 16);  // the item's K steps so far
                     for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                         const int ab = (int)(ai % na);
@@ -312,14 +321,19 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                             // 16 columns = 32 bytes into the swizzle atoms: A's 128 rows, B's 64 rows (half h)
                             const uint64_t dh = bg_desc(ah + ks * 32);
                             const uint64_t dl = bg_desc(al + ks * 32);
-                            const uint64_t db = bg_desc(xs + h * 8192 + ks * 32);
                             // consecutive K steps go to independent accumulator sets (the MMAs of one set depend
-                            // on each other; of different sets, not); a set's first step overwrites it
+                            // on each other; of different sets, not); a set's first step overwrites it. Group gi
+                            // (its activation chunk gi x 16 KB into the stage) owns sets gi x NSET …
                             const int kstep = kstep0 + h * (BG_KS / 16) + ks;
-                            const uint32_t dset = tmem + (uint32_t)(kstep % BG_NACC) * BG_SET_COLS;
-                            const uint32_t acc = kstep >= BG_NACC ? 1u : 0u;
-                            mma_f16(dset, dh, db, id1, acc);
-                            mma_f16(dset + 64, dl, db, id2, acc);
+                            const uint32_t acc = kstep >= NSET ? 1u : 0u;
+#pragma unroll
+                            for (int gi = 0; gi < NG; gi++) {
+                                if (gi >= ngr) break;
+                                const uint64_t db = bg_desc(xs + gi * BG_CHUNK_BYTES + h * 8192 + ks * 32);
+                                const uint32_t dset = tmem + (uint32_t)(gi * NSET + kstep % NSET) * BG_SET_COLS;
+                                mma_f16(dset, dh, db, id1, acc);
+                                mma_f16(dset + 64, dl, db, id2, acc);
+                            }
                         }
                         mma_commit(&sh.aempty[ab]);
                         any = true;
@@ -377,7 +391,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             }
             for (int kc = it.c0; kc < it.c1; kc++) {
                 const int s = kc - it.c0, k0 = kc * BG_KC + pc * 8;
-                uint8_t* xs = stage0 + (size_t)s * BG_STAGE + BG_WTILE;
+                uint8_t* xs = stage0 + (size_t)s * STAGE + BG_WTILE;
                 uint32_t hi[4] = {0u, 0u, 0u, 0u}, lo[4] = {0u, 0u, 0u, 0u};
                 if (live) {
                     const float2* xr = reinterpret_cast<const float2*>(a.xn + (size_t)b * K + k0);
@@ -409,8 +423,8 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
             for (int kc = it.c0; kc < it.c1; kc++, g++) {
                 const int s = (int)(g % (uint32_t)ns);
                 ok = ok && bg_wait(&sh.wfull[s], (g / ns) & 1, abort_flag, a.err);
-                const uint8_t* wt = stage0 + (size_t)s * BG_STAGE + drow * 128;
-                const __half* sc = reinterpret_cast<const __half*>(stage0 + (size_t)s * BG_STAGE + 16384 + drow * 8);
+                const uint8_t* wt = stage0 + (size_t)s * STAGE + drow * 128;
+                const __half* sc = reinterpret_cast<const __half*>(stage0 + (size_t)s * STAGE + 16384 + drow * 8);
                 for (int h = 0; h < BG_KC / BG_KS; h++, ai++) {
                     const int ab = (int)(ai % na);
                     // (one call site: before the first piece that waits for the tensor cores, or the item's last)
@@ -460,6 +474,67 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     }
                 }
                 bar_sync(2, BG_DQ);
+            }
+            if constexpr (NG > 1) {
+                // each group's sets summed in order, then its store / residual add / SwiGLU (no split, no LM head)
+                ok = ok && bg_wait(&sh.tfin, li & 1, abort_flag, a.err);
+                if (ok) tc_fence_after();
+                for (int gi = 0; gi < ngr; gi++) {
+                    float y[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) y[j] = 0.0f;
+                    if (ok) {
+#pragma unroll
+                        for (int st = 0; st < NSET; st++) {
+                            uint32_t rh[8], rl[8], rw[8];
+                            const uint32_t ta =
+                                tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(gi * NSET + st) * BG_SET_COLS;
+                            tmem_ld8(ta + 8 * part, rh);
+                            tmem_ld8(ta + 32 + 8 * part, rl);
+                            tmem_ld8(ta + 64 + 8 * part, rw);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 8; j++)
+                                y[j] += (__uint_as_float(rh[j]) + __uint_as_float(rw[j])) + __uint_as_float(rl[j]);
+                        }
+                    }
+                    if (!ok) continue;
+                    const int sl0 = (grp + gi) * BG_SLOTS, nbg = min(BG_SLOTS, a.nb - sl0);
+                    bool ag[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int sl = 8 * part + j;
+                        ag[j] = sl < nbg && (!a.active || a.active[sl0 + sl] != 0);
+                    }
+                    if (MODE == MV_SWIGLU) {
+                        const int col = row >> 1;
+                        uint8_t* y16 = a.y16 ? a.y16 + (size_t)(grp + gi) * x16_group_bytes(N / 2) : nullptr;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const float up = __shfl_xor_sync(FULL, y[j], 1);
+                            const int sl = 8 * part + j;
+                            if ((lane & 1) || !ag[j] || row >= N) continue;
+                            const float gv = y[j];
+                            const float hv = gv / (1.0f + expf(-gv)) * up;
+                            if (a.y) a.y[(long)(sl0 + sl) * a.y_stride + col] = hv;
+                            if (y16) {
+                                const __half hh = __float2half_rn(hv);
+                                const __half hl = __float2half_rn(hv - __half2float(hh));
+                                *reinterpret_cast<__half*>(y16 + x16_offset(sl, col)) = hh;
+                                *reinterpret_cast<__half*>(y16 + x16_offset(BG_SLOTS + sl, col)) = hl;
+                            }
+                        }
+                    } else if (row < N) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            if (!ag[j]) continue;
+                            float* yp = a.y + (long)(sl0 + 8 * part + j) * a.y_stride + row;
+                            *yp = MODE == MV_ADD ? *yp + y[j] : y[j];
+                        }
+                    }
+                }
+                tc_fence_before();  // these reads, before the next item's MMAs overwrite the accumulators
+                continue;
             }
             ok = ok && bg_wait(&sh.tfin, li & 1, abort_flag, a.err);
             float y[8];
@@ -775,7 +850,12 @@ void launch_tile_q8_0(cudaStream_t st, const QMat& w, uint8_t* out) {
 
 // the instances launched: (mode, operand built in the kernel)
 using BgKernel = void (*)(BgArgs, const uint8_t*, int, int);
-static BgKernel bg_kernel(int mode, bool xn) {
+static BgKernel bg_kernel(int mode, bool xn, int ng) {
+    if (ng == 2) {
+        if (xn) return nullptr;
+        return mode == MV_ADD ? k_bgemm<MV_ADD, false, 2> : mode == MV_SWIGLU ? k_bgemm<MV_SWIGLU, false, 2>
+             : mode == MV_STORE ? k_bgemm<MV_STORE, false, 2> : nullptr;
+    }
     switch (mode) {
         case MV_ADD: return xn ? nullptr : k_bgemm<MV_ADD, false>;
         case MV_SWIGLU: return xn ? k_bgemm<MV_SWIGLU, true> : k_bgemm<MV_SWIGLU, false>;
@@ -783,8 +863,9 @@ static BgKernel bg_kernel(int mode, bool xn) {
         default: return xn ? k_bgemm<MV_STORE, true> : k_bgemm<MV_STORE, false>;
     }
 }
-static const BgKernel BG_ALL[] = {k_bgemm<MV_STORE, false>, k_bgemm<MV_STORE, true>, k_bgemm<MV_ADD, false>,
-                                  k_bgemm<MV_SWIGLU, false>, k_bgemm<MV_SWIGLU, true>, k_bgemm<MV_LMHEAD, false>};
+static const BgKernel BG_ALL[] = {k_bgemm<MV_STORE, false>,    k_bgemm<MV_STORE, true>,     k_bgemm<MV_ADD, false>,
+                                  k_bgemm<MV_SWIGLU, false>,   k_bgemm<MV_SWIGLU, true>,    k_bgemm<MV_LMHEAD, false>,
+                                  k_bgemm<MV_STORE, false, 2>, k_bgemm<MV_ADD, false, 2>, k_bgemm<MV_SWIGLU, false, 2>};
 
 // the largest static shared memory of the instances (the dynamic budget is sized against it)
 static int bg_static_smem() {
@@ -800,13 +881,14 @@ static int bg_static_smem() {
     return bytes;
 }
 
-// shared memory: ns copy stages and na operand buffers (+ the 1024-B alignment slack): as many operand buffers as fit
-// beside 3 stages, then as many stages as fit
-static void bg_ring(int& ns, int& na, int& fixed) {
+// shared memory: ns copy stages (weights + ng activation chunks each) and na operand buffers (+ the 1024-B alignment
+// slack): as many operand buffers as fit beside 3 stages (2 for two groups), then as many stages as fit
+static void bg_ring(int& ns, int& na, int& fixed, int ng = 1) {
+    const int stage = (int)BG_WTILE + ng * (int)BG_CHUNK_BYTES;
     const int room = BG_SMEM_OPTIN - bg_static_smem() - 1024;
-    na = std::max(2, std::min(BG_NA, (room - 3 * (int)BG_STAGE) / (int)BG_ABUF));
+    na = std::max(2, std::min(BG_NA, (room - (ng == 1 ? 3 : 2) * stage) / (int)BG_ABUF));
     fixed = na * (int)BG_ABUF + 1024;
-    ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / (int)BG_STAGE));
+    ns = std::max(1, std::min(BG_MAX_NS, (BG_SMEM_OPTIN - bg_static_smem() - fixed) / stage));
 }
 
 bool bgemm_norm_in_ok(int num_sms, int rows, int cols, int ksplit) {
@@ -822,19 +904,23 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
         for (BgKernel k : BG_ALL)
             cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BG_SMEM_OPTIN - bg_static_smem());
     });
+    // two groups of 32 rows per CTA for unsplit launches over more than one group (the long prefill): each weight
+    // piece dequantised once for both
+    const int groups = (a.nb + BG_SLOTS - 1) / BG_SLOTS;
+    const int ng = (a.ksplit == 1 && !a.xn && a.mode != MV_LMHEAD && groups >= 2) ? 2 : 1;
     int ns, na, fixed;
-    bg_ring(ns, na, fixed);
+    bg_ring(ns, na, fixed, ng);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((a.nb + BG_SLOTS - 1) / BG_SLOTS), 1);
+    cfg.gridDim = dim3((unsigned)bgemm_grid(num_sms, a.w.rows, a.ksplit), (unsigned)((groups + ng - 1) / ng), 1);
     cfg.blockDim = dim3(BG_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = (size_t)fixed + (size_t)ns * BG_STAGE;
+    cfg.dynamicSmemBytes = (size_t)fixed + (size_t)ns * ((size_t)BG_WTILE + (size_t)ng * BG_CHUNK_BYTES);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    const BgKernel k = bg_kernel(a.mode, a.xn != nullptr);
+    const BgKernel k = bg_kernel(a.mode, a.xn != nullptr, ng);
     if (!k) {  // (an in-kernel operand for a mode that has no such instance: a caller's error, nothing launched)
         fprintf(stderr, "launch_bgemm: mode %d has no instance with the operand built in the kernel\n", a.mode);
         return;
