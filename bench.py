@@ -246,11 +246,17 @@ def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0,
     hist = np.full((B, 64), IMAGE_PAD, np.int32)
     stream = torch.cuda.ExternalStream(ctx.stream())
 
+    last_block = np.stack(last_rows).astype(np.float32)
+
     def step():
-        # every slot back to its prefix (the last prefix row re-fed: every step starts from the same logits)
+        # every slot back to its prefix, the last prefix row re-fed (every step starts from the same logits): one
+        # batched step of all slots' rows (ocr_step_embd), or the slot's one-row prefill
         for b in range(B):
             sess.rewind(b, prefix_len - 1)
-            sess.prefill(b, embd=last_rows[b], logits=False)
+        if B > 1:
+            sess.step_embd(last_block)
+        else:
+            sess.prefill(0, embd=last_rows[0], logits=False)
         if B == 1:
             return sess.decode_gpu(0, preset, hist[0])
         return sess.decode_batch(preset, hist)
@@ -312,10 +318,10 @@ def run_ours(args):
     out = None
     if rank == 0:
         classes = kernel_classes(r["sess"], B, prefix_len, r["last_rows"])
-        # per step: the one-row prefill per slot (a decode step of that slot), choice 0, then new - 1 decode steps;
-        # a decode step's launches as the profiler counted them (kernels per layer + the LM head / choice)
+        # per step: the re-feed of the slots' last prefix rows (one batched step), choice 0, then new - 1 decode
+        # steps; a decode step's launches as the timeline counted them (kernels per layer + the LM head / choice)
         launches_per_token = sum(k["launches"] for k in classes) // 4
-        launches = args.steps * (launches_per_token * B + 1 + (new - 1) * launches_per_token)
+        launches = args.steps * (launches_per_token + 1 + (new - 1) * launches_per_token)
         roof = kernel_roofline(classes)
         out = {
             "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",

@@ -1802,6 +1802,40 @@ ocr_status ocr_step(ocr_session* s, const int32_t* tok, float* logits_out) {
     return OCR_OK;
 }
 
+ocr_status ocr_step_embd(ocr_session* s, const int32_t* active, const float* embd, float* logits_out) {
+    if (!s || !active || !embd) return fail(OCR_ERR_ARG, "null argument");
+    const auto& c = s->m->cfg;
+    ocr_ctx* ctx = s->ctx;
+    std::vector<int32_t> act(s->B), pos(s->B), tok(s->B, -1);
+    for (int b = 0; b < s->B; b++) {
+        act[b] = active[b] != 0;
+        pos[b] = s->n_past[b];
+        if (act[b] && s->n_past[b] + 1 > s->n_ctx) return fail(OCR_ERR_STATE, "slot " + std::to_string(b) + ": the session is full");
+    }
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t st = ctx->stream;
+    // the active slots' rows into the residual (an inactive slot's row is not read)
+    for (int b = 0; b < s->B; b++)
+        if (act[b])
+            OCR_CUDA(cudaMemcpyAsync(s->x + (size_t)b * c.dim, embd + (size_t)b * c.dim, (size_t)c.dim * 4,
+                                     cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->tok, tok.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->active, act.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
+    record_step(s, false, 1.0f, 1, 0, 0.0f, nullptr, true);
+    OCR_CUDA(cudaGetLastError());
+    if (logits_out)
+        OCR_CUDA(cudaMemcpyAsync(logits_out, s->logits, (size_t)s->B * c.n_vocab * 4, cudaMemcpyDeviceToHost, st));
+    OCR_CUDA(cudaStreamSynchronize(st));
+    OCR_TRY(check_device_error(ctx));
+    for (int b = 0; b < s->B; b++)
+        if (act[b]) {
+            s->n_past[b] += 1;
+            s->has_logits[b] = 1;
+        }
+    return OCR_OK;
+}
+
 ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time* out, int cap, int* n) {
     if (!s || !tok || !out || !n) return fail(OCR_ERR_ARG, "null argument");
     const auto& c = s->m->cfg;

@@ -89,6 +89,7 @@ _SIGS = {
                              C.POINTER(C.c_int)]),
     "ocr_decode_batch": (C.c_int, [_P, C.POINTER(SamplerCfg), _P, C.c_int, _P]),
     "ocr_read_pages": (C.c_int, [_P, C.POINTER(SamplerCfg), C.c_int, C.POINTER(PageIO)]),
+    "ocr_step_embd": (C.c_int, [_P, _P, _P, _P]),
     "ocr_profile_step": (C.c_int, [_P, _P, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_timeline_step": (C.c_int, [_P, _P, C.c_int, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
@@ -376,6 +377,16 @@ class Session:
         _check(lib().ocr_profile_step(self.h, _ptr(t), out, 1024, C.byref(n)))
         return [dict(name=out[i].name.decode(), layer=out[i].layer, us=out[i].us, bytes=out[i].bytes)
                 for i in range(n.value)]
+
+    def step_embd(self, rows: np.ndarray, active: Optional[Sequence[int]] = None,
+                  logits: bool = False) -> Optional[np.ndarray]:
+        """one Input::Embeddings row per active slot (rows [batch][dim]), every slot in one step; the logits
+        [batch][n_vocab] when asked"""
+        r = np.ascontiguousarray(rows, dtype=np.float32).reshape(self.batch, -1)
+        act = np.ascontiguousarray(np.ones(self.batch) if active is None else active, dtype=np.int32)
+        out = np.empty((self.batch, self.model.cfg.n_vocab), np.float32) if logits else None
+        _check(lib().ocr_step_embd(self.h, _ptr(act), _ptr(r), _ptr(out) if logits else None))
+        return out
 
     def timeline_step(self, tokens: Sequence[int], reps: int = 3) -> list[dict]:
         """the in-chain times of one decode step: the step chained as the decode's graph runs it, `reps` times in one

@@ -129,6 +129,11 @@ typedef struct {
     float us;
     double bytes;
 } ocr_kernel_time;
+/* One step of every slot with active[slot] != 0 taking one Input::Embeddings row (embd [B][dim], row b for slot b)
+   at its position: TextModel::prefill of a single embedding row (text.rs:437-521), for every slot at once — the same
+   KV rows and logits as ocr_prefill(s, b, NULL, row b, 1, …) slot by slot, in one batched step. logits_out
+   (nullable): [B][n_vocab]. */
+ocr_status ocr_step_embd(ocr_session* s, const int32_t* active, const float* embd, float* logits_out);
 ocr_status ocr_profile_step(ocr_session* s, const int32_t* tok, ocr_kernel_time* out, int cap, int* n);
 /* The in-chain timeline of one decode step (the same slots and tokens as ocr_profile_step): the step captured `reps`
    (2..16) times back to back into one graph whose launches are chained as the decode's graph chains them

@@ -158,6 +158,28 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
     assert all(r["us"] > 0 for r in rec)
 
 
+def test_step_embd_equals_per_slot_prefill(ocr, ctx):
+    """ocr_step_embd (one embedding row for every active slot in one step) leaves what a one-row prefill of each slot
+    leaves: the same logits bit for bit, the same positions; an inactive slot does not move"""
+    cfg = BATCH_CFG
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 51, 0.2, 1.0)
+    a, b = gm.session(32, batch=16), gm.session(32, batch=16)
+    for s in (a, b):
+        for k in range(16):
+            s.prefill(k, ids=[2 + k, 4, 6, 8, 10], logits=False)
+    rows = ocr.gauss(77, 16 * cfg["dim"], 1.0).reshape(16, cfg["dim"])
+    act = [1] * 16
+    act[5] = 0
+    la = a.step_embd(rows, act, logits=True)
+    for k in range(16):
+        if act[k]:
+            lb = b.prefill(k, embd=rows[k:k + 1])
+            assert np.array_equal(la[k], lb), k
+    assert a.n_past(5) == 5 and a.n_past(0) == b.n_past(0) == 6
+    nxt_a, nxt_b = a.step([9] * 16), b.step([9] * 16)
+    assert np.array_equal(nxt_a, nxt_b)
+
+
 def test_norms_inside_contractions_match_separate_prep(ocr, orc, ctx, monkeypatch):
     """the norms built inside the contractions (sums of squares per 128-row tile from the residual-adding
     contraction, added in tile order) against the separate prep kernel (OCR_NORM_IN=0; one CTA's sum per row): the
