@@ -1,0 +1,315 @@
+// k_attn_prefill_tc.cu — the prefill's causal attention on the 5th-generation tensor cores (tcgen05, sm_100a): the
+// reference's attention_causal.wgsl (TextModel::prefill, app/crates/ocr-wgpu/src/text.rs:437-521) over the f16 K/V
+// cache, one CTA per (tile of 128 queries, head).
+//
+// Numerics. K and V are f16 in the cache, so they are tensor-core operands as they are. Each query row (f32, scaled
+// by 1/sqrt(128) as the f32 kernel does) splits exactly into f16 hi + lo, so S = Q_hi K^T + Q_lo K^T (f32
+// accumulation) is the f32 product up to the dropped remainder (below 2^-22 of each term). Softmax in two passes: the
+// first takes each row's maximum over its causal keys, the second forms p = exp(s - max) (0 past the row's position),
+// sums them in key order, splits each p exactly into f16 hi + lo and accumulates O += P_hi V + P_lo V in TMEM — no
+// rescaling of O. The output row is O / sum.
+//
+// Roles (256 threads): warps 0-3 own the 128 query rows (TMEM lanes): read S, the maxima, P, the output; warp 4 (one
+// lane) allocates TMEM and issues the MMAs; warps 5-7 stage the K tiles (both passes) and the V tiles (pass 2),
+// transposed so that every operand is K-major with the 128-byte swizzle. S is double-buffered in TMEM, so the
+// product of the next key tile runs while the rows read the current one. Every wait is bounded; the staging is plain
+// loads and stores (no asynchronous copy to drain).
+#include "kernels.cuh"
+#include "tc.cuh"
+
+namespace ocr {
+
+constexpr int PA_QT = 128;       // queries per CTA: the MMA's M, one TMEM lane each
+constexpr int PA_KT = 64;        // keys per tile
+constexpr int PA_THREADS = 256;
+constexpr int PA_LOADERS = 3;    // warps 5-7
+constexpr uint32_t PA_Q_BYTES = PA_QT * 128 * 2;  // one f16 operand of the Q tile: two halves of 64 dims
+constexpr uint32_t PA_K_BYTES = PA_KT * 128 * 2;  // a K tile: two halves of 64 dims, 64 key rows each
+constexpr uint32_t PA_V_BYTES = 128 * PA_KT * 2;  // a V tile transposed: 128 dim rows of the tile's 64 keys
+constexpr uint32_t PA_P_BYTES = PA_QT * PA_KT * 2;  // one f16 operand of P: 128 query rows of 64 keys
+constexpr uint32_t PA_SMEM = 2 * PA_Q_BYTES + 2 * PA_K_BYTES + 2 * PA_V_BYTES + 2 * PA_P_BYTES + 1024;
+constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128-255
+
+struct PaShared {
+    uint64_t kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], sfree[2];
+    uint64_t pfull, pfree, ofull, mdone;
+    uint32_t tmem;
+    int abort_flag;
+};
+
+// byte offset of 16-byte piece p (8 columns) of row r in a K-major 128-byte-swizzle region (64 f16 columns per row)
+__device__ __forceinline__ uint32_t sw128(int r, int p) { return (uint32_t)r * 128u + (uint32_t)((p ^ (r & 7)) << 4); }
+
+// a bounded wait that also gives up when another role has given up
+__device__ __forceinline__ bool pa_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    for (uint32_t i = 0; i < MBAR_TRIES; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    dev_error(err, DEV_TIMEOUT);
+    return false;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __halves2half2(__float2half_rn(a), __float2half_rn(b));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(PA_THREADS, 1)
+    k_attn_prefill_tc(const float* __restrict__ qkv, int L, int n_head, int n_kv, const __half* __restrict__ kc,
+                      const __half* __restrict__ vc, int n_ctx, int pos0, float scale, float* __restrict__ out,
+                      int* err) {
+    extern __shared__ uint8_t sm_raw[];
+    __shared__ __align__(8) PaShared sh;
+    volatile int* abort_flag = &sh.abort_flag;
+    uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
+    uint8_t* Qh = smp;
+    uint8_t* Ql = Qh + PA_Q_BYTES;
+    uint8_t* Kr = Ql + PA_Q_BYTES;      // [2] K tiles
+    uint8_t* Vr = Kr + 2 * PA_K_BYTES;  // [2] V tiles, transposed
+    uint8_t* Ph = Vr + 2 * PA_V_BYTES;
+    uint8_t* Pl = Ph + PA_P_BYTES;
+    const int h = blockIdx.y, kh = h / (n_head / n_kv), q0 = blockIdx.x * PA_QT;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int width = (n_head + 2 * n_kv) * 128;
+    const int n_keys = pos0 + min(L, q0 + PA_QT);  // keys 0 … pos of the tile's last query
+    const int T = (n_keys + PA_KT - 1) / PA_KT;
+    const __half* kbase = kc + (size_t)kh * n_ctx * 128;
+    const __half* vbase = vc + (size_t)kh * n_ctx * 128;
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sh.kfull[i], PA_LOADERS);
+            mbar_init(&sh.kempty[i], 1);
+            mbar_init(&sh.vfull[i], PA_LOADERS);
+            mbar_init(&sh.vempty[i], 1);
+            mbar_init(&sh.sfull[i], 1);
+            mbar_init(&sh.sfree[i], 4);
+        }
+        mbar_init(&sh.pfull, 4);
+        mbar_init(&sh.pfree, 1);
+        mbar_init(&sh.ofull, 1);
+        mbar_init(&sh.mdone, 1);
+        sh.abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 4) {
+        tmem_alloc(&sh.tmem, PA_TMEM_COLS);
+        tmem_relinquish();
+    }
+    // the Q tile, scaled, split f16 hi / lo: row r, 8 dims per 16-byte piece, dims in two 64-column halves (rows past
+    // L zero)
+    for (int e = tid; e < PA_QT * 16; e += PA_THREADS) {
+        const int r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
+        uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = make_uint4(0u, 0u, 0u, 0u);
+        if (q0 + r < L) {
+            const float4* src = reinterpret_cast<const float4*>(qkv + (size_t)(q0 + r) * width + h * 128 + pc * 8);
+            const float4 a0 = src[0], a1 = src[1];
+            const float v[8] = {a0.x * scale, a0.y * scale, a0.z * scale, a0.w * scale,
+                                a1.x * scale, a1.y * scale, a1.z * scale, a1.w * scale};
+            float vh[8];
+#pragma unroll
+            for (int c = 0; c < 8; c++) vh[c] = __half2float(__float2half_rn(v[c]));
+            hi = make_uint4(pack_h2(vh[0], vh[1]), pack_h2(vh[2], vh[3]), pack_h2(vh[4], vh[5]), pack_h2(vh[6], vh[7]));
+            lo = make_uint4(pack_h2(v[0] - vh[0], v[1] - vh[1]), pack_h2(v[2] - vh[2], v[3] - vh[3]),
+                            pack_h2(v[4] - vh[4], v[5] - vh[5]), pack_h2(v[6] - vh[6], v[7] - vh[7]));
+        }
+        *reinterpret_cast<uint4*>(Qh + hf * (PA_QT * 128) + sw128(r, p)) = hi;
+        *reinterpret_cast<uint4*>(Ql + hf * (PA_QT * 128) + sw128(r, p)) = lo;
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp >= 5) {
+        // ---- staging: pass 1 the K tiles; pass 2 each tile's K, then its V transposed ----
+        const int lt = tid - 5 * 32;
+        bool ok = true;
+        for (int seq = 0; seq < 2 * T && ok; seq++) {
+            const int t = seq < T ? seq : seq - T, kb0 = t * PA_KT, ks = seq & 1;
+            if (seq >= 2 && !pa_wait(&sh.kempty[ks], ((seq >> 1) - 1) & 1, abort_flag, err)) {
+                ok = false;
+                break;
+            }
+            uint8_t* kt = Kr + ks * PA_K_BYTES;
+            for (int e = lt; e < PA_KT * 16; e += PA_LOADERS * 32) {
+                const int r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (kb0 + r < n_keys) v = *reinterpret_cast<const uint4*>(kbase + (size_t)(kb0 + r) * 128 + pc * 8);
+                *reinterpret_cast<uint4*>(kt + hf * (PA_KT * 128) + sw128(r, p)) = v;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.kfull[ks]);
+            if (seq < T) continue;
+            // V of tile t: 8 x 8 blocks (keys 8a …, dims 8b …) transposed in registers into rows of the dims
+            const int vs = t & 1;
+            if (t >= 2 && !pa_wait(&sh.vempty[vs], ((t >> 1) - 1) & 1, abort_flag, err)) {
+                ok = false;
+                break;
+            }
+            uint8_t* vt = Vr + vs * PA_V_BYTES;
+            for (int e = lt; e < (PA_KT / 8) * 16; e += PA_LOADERS * 32) {
+                const int a = e % (PA_KT / 8), b = e / (PA_KT / 8);
+                uint32_t w[8][4];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int key = kb0 + 8 * a + i;
+                    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                    if (key < n_keys) x = *reinterpret_cast<const uint4*>(vbase + (size_t)key * 128 + 8 * b);
+                    w[i][0] = x.x, w[i][1] = x.y, w[i][2] = x.z, w[i][3] = x.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;  // the high or the low half of each pair
+                    const int wi = j >> 1;
+                    const uint4 o = make_uint4(__byte_perm(w[0][wi], w[1][wi], sel), __byte_perm(w[2][wi], w[3][wi], sel),
+                                               __byte_perm(w[4][wi], w[5][wi], sel), __byte_perm(w[6][wi], w[7][wi], sel));
+                    *reinterpret_cast<uint4*>(vt + sw128(8 * b + j, a)) = o;
+                }
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.vfull[vs]);
+        }
+        if (!ok) *abort_flag = 1;
+    } else if (warp == 4) {
+        // ---- the tensor cores ----
+        if (lane == 0) {
+            const uint32_t idS = bg_idesc(PA_KT), idO = bg_idesc(128);
+            bool ok = true, any = false;
+            // S[sq % 2] = Q K^T for the K tile of staging sequence `seq`
+            auto qk = [&](int sq, int seq) -> bool {
+                const int sb = sq & 1, ks = seq & 1;
+                if (sq >= 2 && !pa_wait(&sh.sfree[sb], ((sq >> 1) - 1) & 1, abort_flag, err)) return false;
+                if (!pa_wait(&sh.kfull[ks], (seq >> 1) & 1, abort_flag, err)) return false;
+                tc_fence_after();
+                const uint32_t qh = smem_u32(Qh), ql = smem_u32(Ql), kt = smem_u32(Kr + ks * PA_K_BYTES);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {  // 16 dims per step, 4 steps per 64-dim half
+                    const uint32_t oq = (k >> 2) * (PA_QT * 128) + (k & 3) * 32;
+                    const uint32_t ok_ = (k >> 2) * (PA_KT * 128) + (k & 3) * 32;
+                    mma_f16(tS + sb * PA_KT, bg_desc(qh + oq), bg_desc(kt + ok_), idS, k > 0 ? 1u : 0u);
+                    mma_f16(tS + sb * PA_KT, bg_desc(ql + oq), bg_desc(kt + ok_), idS, 1u);
+                }
+                mma_commit(&sh.sfull[sb]);
+                mma_commit(&sh.kempty[ks]);
+                any = true;
+                return true;
+            };
+            for (int t = 0; t < T && ok; t++) ok = qk(t, t);
+            if (ok) ok = qk(T, T);
+            for (int t = 0; t < T && ok; t++) {
+                if (t + 1 < T && !(ok = qk(T + t + 1, T + t + 1))) break;  // the next tile's S while the rows read this
+                const int vs = t & 1;
+                if (!pa_wait(&sh.pfull, t & 1, abort_flag, err) ||
+                    !pa_wait(&sh.vfull[vs], (t >> 1) & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ph = smem_u32(Ph), pl = smem_u32(Pl), vt = smem_u32(Vr + vs * PA_V_BYTES);
+#pragma unroll
+                for (int k = 0; k < PA_KT / 16; k++) {
+                    mma_f16(tO, bg_desc(ph + k * 32), bg_desc(vt + k * 32), idO, (t > 0 || k > 0) ? 1u : 0u);
+                    mma_f16(tO, bg_desc(pl + k * 32), bg_desc(vt + k * 32), idO, 1u);
+                }
+                mma_commit(&sh.pfree);
+                mma_commit(&sh.vempty[vs]);
+            }
+            if (ok) mma_commit(&sh.ofull);
+            if (any) {  // every MMA complete before the TMEM is freed (bounded, abort or not)
+                mma_commit(&sh.mdone);
+                mbar_wait(&sh.mdone, 0, err);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- the rows: thread tid owns query q0 + tid (TMEM lane tid) ----
+        const int qpos = pos0 + q0 + tid;
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        float m = -INFINITY, l = 0.0f;
+        uint32_t sv[PA_KT];
+        bool ok = true;
+        auto read_s = [&](int sq) -> bool {
+            const int sb = sq & 1;
+            if (!pa_wait(&sh.sfull[sb], (sq >> 1) & 1, abort_flag, err)) return false;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < PA_KT / 16; c++) tmem_ld16(tS + lane_base + sb * PA_KT + c * 16, sv + c * 16);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.sfree[sb]);
+            return true;
+        };
+        for (int t = 0; t < T && ok; t++) {
+            if (!(ok = read_s(t))) break;
+#pragma unroll
+            for (int j = 0; j < PA_KT; j++)
+                if (t * PA_KT + j <= qpos) m = fmaxf(m, __uint_as_float(sv[j]));
+        }
+        for (int t = 0; t < T && ok; t++) {
+            if (!(ok = read_s(T + t))) break;
+            if (t >= 1 && !(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;  // P·V of t - 1 done
+#pragma unroll
+            for (int p = 0; p < PA_KT / 8; p++) {
+                float pv[8], ph[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const int j = p * 8 + c;
+                    pv[c] = t * PA_KT + j <= qpos ? expf(__uint_as_float(sv[j]) - m) : 0.0f;
+                    l += pv[c];
+                    ph[c] = __half2float(__float2half_rn(pv[c]));
+                }
+                const uint4 hi = make_uint4(pack_h2(ph[0], ph[1]), pack_h2(ph[2], ph[3]), pack_h2(ph[4], ph[5]),
+                                            pack_h2(ph[6], ph[7]));
+                const uint4 lo = make_uint4(pack_h2(pv[0] - ph[0], pv[1] - ph[1]), pack_h2(pv[2] - ph[2], pv[3] - ph[3]),
+                                            pack_h2(pv[4] - ph[4], pv[5] - ph[5]), pack_h2(pv[6] - ph[6], pv[7] - ph[7]));
+                *reinterpret_cast<uint4*>(Ph + sw128(tid, p)) = hi;
+                *reinterpret_cast<uint4*>(Pl + sw128(tid, p)) = lo;
+            }
+            fence_proxy_async();  // the generic stores, before the tensor cores read them
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.pfull);
+        }
+        // the output row: O / sum
+        if (ok && pa_wait(&sh.ofull, 0, abort_flag, err)) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                uint32_t o[16];
+                tmem_ld16(tO + lane_base + c * 16, o);
+                tmem_wait_ld();
+                if (q0 + tid < L) {
+                    float4* op = reinterpret_cast<float4*>(out + (size_t)(q0 + tid) * n_head * 128 + h * 128 + c * 16);
+#pragma unroll
+                    for (int d = 0; d < 4; d++)
+                        op[d] = make_float4(__uint_as_float(o[4 * d]) * inv, __uint_as_float(o[4 * d + 1]) * inv,
+                                            __uint_as_float(o[4 * d + 2]) * inv, __uint_as_float(o[4 * d + 3]) * inv);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tmem, PA_TMEM_COLS);
+    }
+}
+
+void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
+                                 const __half* vc, int n_ctx, int pos0, float scale, float* out, int* err) {
+    static PerDeviceOnce once;
+    once([] { cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PA_SMEM); });
+    k_attn_prefill_tc<<<dim3((L + PA_QT - 1) / PA_QT, n_head, 1), PA_THREADS, PA_SMEM, st>>>(
+        qkv, L, n_head, n_kv, kc, vc, n_ctx, pos0, scale, out, err);
+}
+
+}  // namespace ocr

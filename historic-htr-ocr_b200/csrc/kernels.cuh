@@ -346,5 +346,9 @@ void launch_qk_norm_rope_store(cudaStream_t st, float* qkv, int L, int n_head, i
 // causal attention of L queries (positions pos0…) over the f16 cache rows 0…pos0+r → out [L][n_head*128]
 void launch_attention_prefill(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
                               const __half* vc, int n_ctx, int pos0, float scale, float* out);
+// the same causal attention on the tensor cores (k_attn_prefill_tc.cu): 128-query tiles, f16 hi / lo splits of Q and
+// of the probabilities, two softmax passes; `err` takes a bounded wait's timeout
+void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
+                                 const __half* vc, int n_ctx, int pos0, float scale, float* out, int* err);
 
 }  // namespace ocr

@@ -1697,6 +1697,9 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
     // the tensor-core contractions (k_bgemm.cu) take the rows in groups of 32 like decode slots; the operands after
     // the ids, 256-B aligned
     const bool tc = s->m->tc;
+    // the causal attention on the tensor cores with the contractions (OCR_PF_ATTN=0: the f32 kernel)
+    const char* pfa_env = getenv("OCR_PF_ATTN");
+    const bool pf_attn_tc = tc && c.d_head == 128 && !(pfa_env && pfa_env[0] == '0');
     uint8_t* x16a = (uint8_t*)(((uintptr_t)(d_ids + n) + 255) & ~(uintptr_t)255);
     uint8_t* x16o = x16a + prefill_x16_bytes(s, n, c.dim);
     uint8_t* x16g = x16o + prefill_x16_bytes(s, n, s->qd);
@@ -1734,7 +1737,10 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
             gemm(L.qkv, L.bq_qkv, x16a, MV_STORE, qkv, s->qkv_w, nullptr);
             launch_qk_norm_rope_store(st, qkv, n, c.n_head, c.n_kv, L.q_norm, L.k_norm, s->rope, pos0, c.eps, kc, vc,
                                       s->n_ctx);
-            launch_attention_prefill(st, qkv, n, c.n_head, c.n_kv, kc, vc, s->n_ctx, pos0, scale, a);
+            if (pf_attn_tc)
+                launch_attention_prefill_tc(st, qkv, n, c.n_head, c.n_kv, kc, vc, s->n_ctx, pos0, scale, a, ctx->d_err);
+            else
+                launch_attention_prefill(st, qkv, n, c.n_head, c.n_kv, kc, vc, s->n_ctx, pos0, scale, a);
             prep(a, s->qd, nullptr, x16o);
             gemm(L.o, L.bq_o, x16o, MV_ADD, x, c.dim, nullptr);
             prep(x, c.dim, L.ffn_norm, x16a);

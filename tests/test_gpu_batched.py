@@ -158,6 +158,32 @@ def test_tensor_core_profile_step(ocr, orc, ctx):
     assert all(r["us"] > 0 for r in rec)
 
 
+def test_prefill_attention_tensor_cores_match_f32_kernel(ocr, ctx, monkeypatch):
+    """the prefill's causal attention on the tensor cores (Q and the probabilities split f16 hi / lo, two softmax
+    passes) against the f32 kernel (OCR_PF_ATTN=0): a 200-row prefill then 173 embedding rows continuing at position
+    200 (tiles of 128 queries and 64 keys, neither size a multiple), logits within 1e-5 of max |logit| after each,
+    then the same 16 greedy choices"""
+    cfg = BATCH_CFG
+    gm = ocr.TextModel.synthetic(ctx, text_config(ocr, cfg), 57, 0.2, 1.0)
+    ids = [int(t) for t in ocr.fill_ids(58, 200, cfg["n_vocab"])]
+    rows = ocr.gauss(59, 173 * cfg["dim"], 1.0).reshape(173, cfg["dim"])
+    out = []
+    for env in ("1", "0"):
+        monkeypatch.setenv("OCR_PF_ATTN", env)
+        s = gm.session(400)
+        l1 = s.prefill(0, ids=ids)
+        l2 = s.prefill(0, embd=rows)
+        pre = ocr.Preset("t", 0.0, 1.0, 1.1, 16, 0.0, 16)
+        out.append((l1, l2, s.decode_gpu(0, pre, ids[-16:])))
+        s.close()
+    monkeypatch.delenv("OCR_PF_ATTN")
+    (a1, a2, ai), (b1, b2, bi) = out
+    for a, b in ((a1, b1), (a2, b2)):
+        m = np.abs(b).max()
+        assert np.abs(a - b).max() <= 1e-5 * m, np.abs(a - b).max() / m
+    assert ai == bi
+
+
 def test_step_embd_equals_per_slot_prefill(ocr, ctx):
     """ocr_step_embd (one embedding row for every active slot in one step) leaves what a one-row prefill of each slot
     leaves: the same logits bit for bit, the same positions; an inactive slot does not move"""
