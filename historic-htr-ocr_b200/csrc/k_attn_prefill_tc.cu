@@ -9,11 +9,11 @@
 // sums them in key order, splits each p exactly into f16 hi + lo and accumulates O += P_hi V + P_lo V in TMEM — no
 // rescaling of O. The output row is O / sum.
 //
-// Roles (256 threads): warps 0-3 own the 128 query rows (TMEM lanes): read S, the maxima, P, the output; warp 4 (one
-// lane) allocates TMEM and issues the MMAs; warps 5-7 stage the K tiles (both passes) and the V tiles (pass 2),
-// transposed so that every operand is K-major with the 128-byte swizzle. S is double-buffered in TMEM, so the
-// product of the next key tile runs while the rows read the current one. Every wait is bounded; the staging is plain
-// loads and stores (no asynchronous copy to drain).
+// Roles (416 threads): warps 0-3 own the 128 query rows (TMEM lanes): read S, the maxima, P, the output; warp 4 (one
+// lane) allocates TMEM and issues the MMAs; warps 5-12 stage the K tiles (both passes) and the V tiles (pass 2),
+// transposed so that every operand is K-major with the 128-byte swizzle — each thread issuing all its loads of a
+// tile before its stores. S is double-buffered in TMEM, so the product of the next key tile runs while the rows read
+// the current one. Every wait is bounded; the staging is plain loads and stores (no asynchronous copy to drain).
 #include "kernels.cuh"
 #include "tc.cuh"
 
@@ -21,8 +21,9 @@ namespace ocr {
 
 constexpr int PA_QT = 128;       // queries per CTA: the MMA's M, one TMEM lane each
 constexpr int PA_KT = 64;        // keys per tile
-constexpr int PA_THREADS = 256;
-constexpr int PA_LOADERS = 3;    // warps 5-7
+constexpr int PA_LOADERS = 8;    // warps 5-12: the staging
+constexpr int PA_THREADS = (5 + PA_LOADERS) * 32;
+constexpr int PA_KPT = (PA_KT * 16 + PA_LOADERS * 32 - 1) / (PA_LOADERS * 32);  // K pieces per staging thread
 constexpr uint32_t PA_Q_BYTES = PA_QT * 128 * 2;  // one f16 operand of the Q tile: two halves of 64 dims
 constexpr uint32_t PA_K_BYTES = PA_KT * 128 * 2;  // a K tile: two halves of 64 dims, 64 key rows each
 constexpr uint32_t PA_V_BYTES = 128 * PA_KT * 2;  // a V tile transposed: 128 dim rows of the tile's 64 keys
@@ -136,11 +137,18 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                 break;
             }
             uint8_t* kt = Kr + ks * PA_K_BYTES;
-            for (int e = lt; e < PA_KT * 16; e += PA_LOADERS * 32) {
-                const int r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (kb0 + r < n_keys) v = *reinterpret_cast<const uint4*>(kbase + (size_t)(kb0 + r) * 128 + pc * 8);
-                *reinterpret_cast<uint4*>(kt + hf * (PA_KT * 128) + sw128(r, p)) = v;
+            uint4 kv[PA_KPT];
+#pragma unroll
+            for (int i = 0; i < PA_KPT; i++) {  // every load of the thread's pieces in flight, then the stores
+                const int e = lt + i * PA_LOADERS * 32, r = e >> 4, pc = e & 15;
+                kv[i] = make_uint4(0u, 0u, 0u, 0u);
+                if (e < PA_KT * 16 && kb0 + r < n_keys)
+                    kv[i] = *reinterpret_cast<const uint4*>(kbase + (size_t)(kb0 + r) * 128 + pc * 8);
+            }
+#pragma unroll
+            for (int i = 0; i < PA_KPT; i++) {
+                const int e = lt + i * PA_LOADERS * 32, r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
+                if (e < PA_KT * 16) *reinterpret_cast<uint4*>(kt + hf * (PA_KT * 128) + sw128(r, p)) = kv[i];
             }
             fence_proxy_async();
             __syncwarp();
