@@ -18,6 +18,10 @@ the line also carries config 2 (`config2`: one sequence, 2048-row prefix, 512 to
 --config 2: one sequence per GPU, 2048-row prefix, 512 tokens.
 --config 1: the LM head + windowed penalty + greedy argmax alone (ocr_op_lm_head_sample),
 x N(0,1) [1024], W [151936 x 1024] N(0, 0.02) q8_0, history 512 uniform ids, penalty 1.15 over the last 64.
+--config 4: one synthetic page end to end at batch 1 — a 1540 x 1100 RGB image (uniform bytes) baked
+(white-padded to 1540 x 1120) and encoded by the Pixtral-shaped q8_0 vision encoder + projector (24 layers, 8800
+patches → 2200 image tokens), prefilled between 7 + 7 prompt ids, then 1500 greedy tokens; time to first token
+(encode + prefill + choice 0) and the decode rate reported separately.
 --config 5: the page sweep — 512 seeded pages (prefix U[1500,3072] rows, U[800,1500] tokens) claimed
 from a shared queue by one page engine per GPU (prefill included; strong scaling).
 
@@ -214,7 +218,7 @@ def kernel_roofline(classes):
 # ---------------------------------------------------------------------------------------------------------------------
 # the decode workloads: slots per GPU, prefix rows per slot, tokens decoded per slot (BASELINE configs[1] and [2])
 WORKLOADS = {2: dict(B=1, prefix=PREFIX, new=NEW), 3: dict(B=32, prefix=3072, new=1024),
-             5: dict(B=32, prefix=2286, new=1150)}  # (config 5: its mean page, for the CPU samples' positions)
+             4: dict(B=1, prefix=2214, new=1500), 5: dict(B=32, prefix=2286, new=1150)}  # (config 5: its mean page, for the CPU samples' positions)
 
 
 def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0, prefix=0, profile_range=False):
@@ -311,6 +315,8 @@ def run_ours(args):
         return run_config1(args, ocr, ctx, torch, pg, rank, world)
     if args.config == 5:
         return run_config5(args, ocr, ctx, torch, pg if pg else None, rank, world, local)
+    if args.config == 4:
+        return run_config4(args, ocr, ctx, torch, pg, rank, world, local)
     r = decode_workload(ocr, ctx, torch, args.config, args.steps, args.warmup, pg, local, args.tokens, args.prefix,
                         args.profile_range)
     B, prefix_len, new, dev_s, wall = r["B"], r["prefix"], r["new"], r["dev_s"], r["wall"]
@@ -439,6 +445,109 @@ def run_config5(args, ocr, ctx, torch, pg, rank, world, local):
     P.PageQueue(store, rank, world, n_pages, ns="sweep/").leave()
     sess.close()
     model.close()
+    return out
+
+
+PAGE_W, PAGE_H, PROMPT_PRE, PROMPT_POST = 1540, 1100, 7, 7
+
+
+def run_config4(args, ocr, ctx, torch, pg, rank, world, local):
+    """BASELINE config 4: one page end to end at batch 1 (Engine::read_text, engine.rs:447-524). A step: the page's
+    bytes (pinned host memory) baked and encoded (ocr_vision_encode_page: the white pad inside the patch gather, 24
+    encoder layers on 8800 patches, the projector → 2200 rows left on the device), the prompt [7 ids, 2200 image
+    rows, 7 ids] prefilled from the device rows, choice 0, then 1500 greedy choices (ocr_decode: host history in,
+    host ids out). TTFT = encode + prefill (device events); the decode rate over the 1500 choices after it."""
+    seed = ocr.SEED_BASE + 4
+    vcfg = ocr.VisionConfig()
+    vision = ocr.Vision.synthetic(ctx, vcfg, seed, 0.02)
+    model = ocr.TextModel.synthetic(ctx, ocr.TextConfig(**CONFIG2), ocr.SEED_BASE + 2, 0.02, 0.02)
+    g = 28
+    sw, sh, left, top, right, bottom = ocr.bake_plan(vcfg.image_size, g, PAGE_W, PAGE_H)
+    n_img = ((sw + left + right) // g) * ((sh + top + bottom) // g)
+    rng = np.random.default_rng(seed)
+    page = torch.from_numpy(rng.integers(0, 256, (PAGE_H, PAGE_W, 3), dtype=np.uint8)).pin_memory()
+    ids_pre = [int(t) for t in rng.integers(0, CONFIG2["n_vocab"], PROMPT_PRE)]
+    ids_post = [int(t) for t in rng.integers(0, CONFIG2["n_vocab"], PROMPT_POST)]
+    ids = ids_pre + [-1] * n_img + ids_post
+    n_prompt, new = len(ids), WORKLOADS[4]["new"]
+    rows = torch.zeros((n_prompt, CONFIG2["dim"]), dtype=torch.float32, device="cuda")
+    img_rows = rows[PROMPT_PRE:PROMPT_PRE + n_img]
+    sess = model.session(n_prompt + new)
+    preset = ocr.Preset("page", 0.0, 1.0, 1.15, 64, 0.0, new)
+    history = [IMAGE_PAD] * n_img + ids_post
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    page_np = page.numpy()
+
+    def read(ev):
+        sess.rewind(0, 0)
+        ev[0].record(stream)
+        vision.encode_page(page_np, out=img_rows)
+        ev[1].record(stream)
+        sess.prefill(0, ids=ids, embd=rows, logits=False)
+        ev[2].record(stream)
+        out = sess.decode_gpu(0, preset, history)
+        ev[3].record(stream)
+        ev[3].synchronize()
+        return out
+
+    def events():
+        return [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    for _ in range(args.warmup):
+        read(events())
+    torch.cuda.synchronize()
+    enc, pf, dec, tot = [], [], [], []
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ev = events()
+            out = read(ev)
+            assert len(out) == new
+            enc.append(ev[0].elapsed_time(ev[1]))
+            pf.append(ev[1].elapsed_time(ev[2]))
+            dec.append(ev[2].elapsed_time(ev[3]))
+            tot.append(ev[0].elapsed_time(ev[3]))
+        wall = time.perf_counter() - t0
+    k = args.steps
+    dev_s = sum(tot) / 1e3
+    dev_s, wall = max_over_ranks([dev_s, wall], pg)
+    decode_rate = new * k / (sum(dec) / 1e3)
+    ttft = (sum(enc) + sum(pf)) / k
+    out = None
+    if rank == 0:
+        flops_vit = 24 * (2 * 8800 * (4 * 1024 * 1024 + 3 * 4096 * 1024) + 4 * 8800 * 8800 * 1024)
+        out = {
+            "metric": "decode tok/s per B200 & per box (q8_0 1B VLM); matvec HBM GB/s vs peak",
+            "value": round(world * decode_rate, 1), "unit": "tok/s", "n_gpus": world, "steps": k,
+            "warmup": args.warmup, "ms_per_step": round(dev_s / k * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights x f32 activations (f16 hi/lo tensor-core "
+                                                           "operands), f16 KV",
+            "data": "synthetic (seeded 1540x1100 RGB page, uniform bytes; seeded q8_0 vision and text weights)",
+            "config": {"workload": f"BASELINE config 4: one page end to end at batch 1 — bake to {sw + left + right}x"
+                                   f"{sh + top + bottom}, Pixtral-shaped q8_0 encoder (24 x 1024, 16 heads of 64, "
+                                   f"ffn 4096) + projector → {n_img} image rows, prompt {n_prompt} rows, {new} greedy "
+                                   "tokens (rp 1.15, window 64)",
+                       "model": "vision: Pixtral ViT + LightOnOCR projector; text: Qwen3-0.6B-shaped decoder",
+                       "global_batch": world, "seq_len": n_prompt + new, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (633 MB of text weights per token; 0.86 GB of vision weights and "
+                             "activations per page)"},
+            "ttft": {"ms": round(ttft, 2), "encode_ms": round(sum(enc) / k, 2), "prefill_ms": round(sum(pf) / k, 2),
+                     "image_rows": n_img, "prompt_rows": n_prompt,
+                     "encode_tflops": round(flops_vit / (sum(enc) / k * 1e-3) / 1e12, 1),
+                     "note": "device events on the library's stream: encode (the page's host-to-device copy, the bake's "
+                             "pad fused into the patch gather, 24 layers, the projector) + prefill (the prompt's last "
+                             "logits); choice 0 is the decode's first kernel"},
+            "decode": {"tok_per_s": round(decode_rate, 1), "ms": round(sum(dec) / k, 1), "tokens": new},
+            "e2e": {"value": round(world * new * k / wall, 1), "unit": "tok/s (whole page read, TTFT included)",
+                    "h2d_bytes_per_step": PAGE_W * PAGE_H * 3 + len(ids) * 4 + len(history) * 4,
+                    "d2h_bytes_per_step": new * 4},
+            "clocks": clk.summary()}
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline_sample(4, tokens_sample=16)
+        print(json.dumps(out), flush=True)
+    sess.close()
+    model.close()
+    vision.close()
     return out
 
 
@@ -606,7 +715,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=3)
     ap.add_argument("--pages", type=int, default=0, help="config 5: pages in the sweep (default 512)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="config 3: skip the config-2 measurement beside it")

@@ -1,11 +1,15 @@
-// k_attn_prefill_tc.cu — the prefill's causal attention on the 5th-generation tensor cores (tcgen05, sm_100a): the
-// reference's attention_causal.wgsl (TextModel::prefill, app/crates/ocr-wgpu/src/text.rs:437-521) over the f16 K/V
-// cache, one CTA per (tile of 128 queries, head).
+// k_attn_prefill_tc.cu — attention over f16 keys and values on the 5th-generation tensor cores (tcgen05, sm_100a),
+// one CTA per (tile of 128 queries, head), in two forms of one template:
+//   - causal, head dim 128: the text prefill, the reference's attention_causal.wgsl (TextModel::prefill,
+//     app/crates/ocr-wgpu/src/text.rs:437-521) over the f16 KV cache;
+//   - full (every query sees every key), head dim 64: the vision encoder's attention over all patches, the
+//     reference's attention_coop.wgsl / attention.wgsl (Vision::run, app/crates/ocr-wgpu/src/vision.rs:290-295),
+//     over K / V rounded to f16 like its f16 path (vision.rs:319-327), writing the o-projection's operand.
 //
-// Numerics. K and V are f16 in the cache, so they are tensor-core operands as they are. Each query row (f32, scaled
-// by 1/sqrt(128) as the f32 kernel does) splits exactly into f16 hi + lo, so S = Q_hi K^T + Q_lo K^T (f32
+// Numerics. K and V are f16, so they are tensor-core operands as they are. Each query row (f32, scaled by
+// 1/sqrt(d_head) as the f32 kernels do) splits exactly into f16 hi + lo, so S = Q_hi K^T + Q_lo K^T (f32
 // accumulation) is the f32 product up to the dropped remainder (below 2^-22 of each term). Softmax in two passes: the
-// first takes each row's maximum over its causal keys, the second forms p = exp(s - max) (0 past the row's position),
+// first takes each row's maximum over its keys, the second forms p = exp(s - max) (0 for keys the row does not see),
 // sums them in key order, splits each p exactly into f16 hi + lo and accumulates O += P_hi V + P_lo V in TMEM — no
 // rescaling of O. The output row is O / sum.
 //
@@ -23,13 +27,17 @@ constexpr int PA_QT = 128;       // queries per CTA: the MMA's M, one TMEM lane 
 constexpr int PA_KT = 64;        // keys per tile
 constexpr int PA_LOADERS = 8;    // warps 5-12: the staging
 constexpr int PA_THREADS = (5 + PA_LOADERS) * 32;
-constexpr int PA_KPT = (PA_KT * 16 + PA_LOADERS * 32 - 1) / (PA_LOADERS * 32);  // K pieces per staging thread
-constexpr uint32_t PA_Q_BYTES = PA_QT * 128 * 2;  // one f16 operand of the Q tile: two halves of 64 dims
-constexpr uint32_t PA_K_BYTES = PA_KT * 128 * 2;  // a K tile: two halves of 64 dims, 64 key rows each
-constexpr uint32_t PA_V_BYTES = 128 * PA_KT * 2;  // a V tile transposed: 128 dim rows of the tile's 64 keys
-constexpr uint32_t PA_P_BYTES = PA_QT * PA_KT * 2;  // one f16 operand of P: 128 query rows of 64 keys
-constexpr uint32_t PA_SMEM = 2 * PA_Q_BYTES + 2 * PA_K_BYTES + 2 * PA_V_BYTES + 2 * PA_P_BYTES + 1024;
-constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128-255
+constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128 … 128 + D
+// the shared-memory plan of head dim D: Q hi / lo, two K tiles, two V tiles (transposed), P hi / lo
+template <int D>
+struct PaPlan {
+    static constexpr int KPT = (PA_KT * D / 8 + PA_LOADERS * 32 - 1) / (PA_LOADERS * 32);  // K pieces per thread
+    static constexpr uint32_t Q_BYTES = PA_QT * D * 2;  // one f16 operand of the Q tile: D/64 halves of 64 dims
+    static constexpr uint32_t K_BYTES = PA_KT * D * 2;  // a K tile: D/64 halves of 64 dims, 64 key rows each
+    static constexpr uint32_t V_BYTES = D * PA_KT * 2;  // a V tile transposed: D dim rows of the tile's 64 keys
+    static constexpr uint32_t P_BYTES = PA_QT * PA_KT * 2;  // one f16 operand of P: 128 query rows of 64 keys
+    static constexpr uint32_t SMEM = 2 * Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 1024;
+};
 
 struct PaShared {
     uint64_t kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], sfree[2];
@@ -57,27 +65,29 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(PA_THREADS, 1)
-    k_attn_prefill_tc(const float* __restrict__ qkv, int L, int n_head, int n_kv, const __half* __restrict__ kc,
-                      const __half* __restrict__ vc, int n_ctx, int pos0, float scale, float* __restrict__ out,
-                      int* err) {
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
+    using P = PaPlan<D>;
+    const int L = a.L, n_head = a.n_head, pos0 = a.pos0;
+    const float scale = a.scale;
+    int* err = a.err;
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(8) PaShared sh;
     volatile int* abort_flag = &sh.abort_flag;
     uint8_t* smp = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
     uint8_t* Qh = smp;
-    uint8_t* Ql = Qh + PA_Q_BYTES;
-    uint8_t* Kr = Ql + PA_Q_BYTES;      // [2] K tiles
-    uint8_t* Vr = Kr + 2 * PA_K_BYTES;  // [2] V tiles, transposed
-    uint8_t* Ph = Vr + 2 * PA_V_BYTES;
-    uint8_t* Pl = Ph + PA_P_BYTES;
-    const int h = blockIdx.y, kh = h / (n_head / n_kv), q0 = blockIdx.x * PA_QT;
+    uint8_t* Ql = Qh + P::Q_BYTES;
+    uint8_t* Kr = Ql + P::Q_BYTES;      // [2] K tiles
+    uint8_t* Vr = Kr + 2 * P::K_BYTES;  // [2] V tiles, transposed
+    uint8_t* Ph = Vr + 2 * P::V_BYTES;
+    uint8_t* Pl = Ph + P::P_BYTES;
+    const int h = blockIdx.y, kh = h / a.group, q0 = blockIdx.x * PA_QT;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int width = (n_head + 2 * n_kv) * 128;
-    const int n_keys = pos0 + min(L, q0 + PA_QT);  // keys 0 … pos of the tile's last query
+    // causal: keys 0 … the position of the tile's last query; full: every key
+    const int n_keys = CAUSAL ? pos0 + min(L, q0 + PA_QT) : a.n_keys;
     const int T = (n_keys + PA_KT - 1) / PA_KT;
-    const __half* kbase = kc + (size_t)kh * n_ctx * 128;
-    const __half* vbase = vc + (size_t)kh * n_ctx * 128;
+    const __half* kbase = a.k + (size_t)kh * a.kv_head_stride;
+    const __half* vbase = a.v + (size_t)kh * a.kv_head_stride;
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
@@ -99,13 +109,13 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
         tmem_alloc(&sh.tmem, PA_TMEM_COLS);
         tmem_relinquish();
     }
-    // the Q tile, scaled, split f16 hi / lo: row r, 8 dims per 16-byte piece, dims in two 64-column halves (rows past
-    // L zero)
-    for (int e = tid; e < PA_QT * 16; e += PA_THREADS) {
-        const int r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
+    // the Q tile, scaled, split f16 hi / lo: row r, 8 dims per 16-byte piece, dims in D/64 halves of 64 columns (rows
+    // past L zero)
+    for (int e = tid; e < PA_QT * (D / 8); e += PA_THREADS) {
+        const int r = e / (D / 8), pc = e % (D / 8), hf = pc >> 3, p = pc & 7;
         uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = make_uint4(0u, 0u, 0u, 0u);
         if (q0 + r < L) {
-            const float4* src = reinterpret_cast<const float4*>(qkv + (size_t)(q0 + r) * width + h * 128 + pc * 8);
+            const float4* src = reinterpret_cast<const float4*>(a.q + (size_t)(q0 + r) * a.q_stride + h * D + pc * 8);
             const float4 a0 = src[0], a1 = src[1];
             const float v[8] = {a0.x * scale, a0.y * scale, a0.z * scale, a0.w * scale,
                                 a1.x * scale, a1.y * scale, a1.z * scale, a1.w * scale};
@@ -136,19 +146,19 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                 ok = false;
                 break;
             }
-            uint8_t* kt = Kr + ks * PA_K_BYTES;
-            uint4 kv[PA_KPT];
+            uint8_t* kt = Kr + ks * P::K_BYTES;
+            uint4 kv[P::KPT];
 #pragma unroll
-            for (int i = 0; i < PA_KPT; i++) {  // every load of the thread's pieces in flight, then the stores
-                const int e = lt + i * PA_LOADERS * 32, r = e >> 4, pc = e & 15;
+            for (int i = 0; i < P::KPT; i++) {  // every load of the thread's pieces in flight, then the stores
+                const int e = lt + i * PA_LOADERS * 32, r = e / (D / 8), pc = e % (D / 8);
                 kv[i] = make_uint4(0u, 0u, 0u, 0u);
-                if (e < PA_KT * 16 && kb0 + r < n_keys)
-                    kv[i] = *reinterpret_cast<const uint4*>(kbase + (size_t)(kb0 + r) * 128 + pc * 8);
+                if (e < PA_KT * (D / 8) && kb0 + r < n_keys)
+                    kv[i] = *reinterpret_cast<const uint4*>(kbase + (size_t)(kb0 + r) * D + pc * 8);
             }
 #pragma unroll
-            for (int i = 0; i < PA_KPT; i++) {
-                const int e = lt + i * PA_LOADERS * 32, r = e >> 4, pc = e & 15, hf = pc >> 3, p = pc & 7;
-                if (e < PA_KT * 16) *reinterpret_cast<uint4*>(kt + hf * (PA_KT * 128) + sw128(r, p)) = kv[i];
+            for (int i = 0; i < P::KPT; i++) {
+                const int e = lt + i * PA_LOADERS * 32, r = e / (D / 8), pc = e % (D / 8), hf = pc >> 3, p = pc & 7;
+                if (e < PA_KT * (D / 8)) *reinterpret_cast<uint4*>(kt + hf * (PA_KT * 128) + sw128(r, p)) = kv[i];
             }
             fence_proxy_async();
             __syncwarp();
@@ -160,15 +170,15 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                 ok = false;
                 break;
             }
-            uint8_t* vt = Vr + vs * PA_V_BYTES;
-            for (int e = lt; e < (PA_KT / 8) * 16; e += PA_LOADERS * 32) {
-                const int a = e % (PA_KT / 8), b = e / (PA_KT / 8);
+            uint8_t* vt = Vr + vs * P::V_BYTES;
+            for (int e = lt; e < (PA_KT / 8) * (D / 8); e += PA_LOADERS * 32) {
+                const int ka = e % (PA_KT / 8), b = e / (PA_KT / 8);
                 uint32_t w[8][4];
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const int key = kb0 + 8 * a + i;
+                    const int key = kb0 + 8 * ka + i;
                     uint4 x = make_uint4(0u, 0u, 0u, 0u);
-                    if (key < n_keys) x = *reinterpret_cast<const uint4*>(vbase + (size_t)key * 128 + 8 * b);
+                    if (key < n_keys) x = *reinterpret_cast<const uint4*>(vbase + (size_t)key * D + 8 * b);
                     w[i][0] = x.x, w[i][1] = x.y, w[i][2] = x.z, w[i][3] = x.w;
                 }
 #pragma unroll
@@ -177,7 +187,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                     const int wi = j >> 1;
                     const uint4 o = make_uint4(__byte_perm(w[0][wi], w[1][wi], sel), __byte_perm(w[2][wi], w[3][wi], sel),
                                                __byte_perm(w[4][wi], w[5][wi], sel), __byte_perm(w[6][wi], w[7][wi], sel));
-                    *reinterpret_cast<uint4*>(vt + sw128(8 * b + j, a)) = o;
+                    *reinterpret_cast<uint4*>(vt + sw128(8 * b + j, ka)) = o;
                 }
             }
             fence_proxy_async();
@@ -188,7 +198,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
     } else if (warp == 4) {
         // ---- the tensor cores ----
         if (lane == 0) {
-            const uint32_t idS = bg_idesc(PA_KT), idO = bg_idesc(128);
+            const uint32_t idS = bg_idesc(PA_KT), idO = bg_idesc(D);
             bool ok = true, any = false;
             // S[sq % 2] = Q K^T for the K tile of staging sequence `seq`
             auto qk = [&](int sq, int seq) -> bool {
@@ -196,9 +206,9 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                 if (sq >= 2 && !pa_wait(&sh.sfree[sb], ((sq >> 1) - 1) & 1, abort_flag, err)) return false;
                 if (!pa_wait(&sh.kfull[ks], (seq >> 1) & 1, abort_flag, err)) return false;
                 tc_fence_after();
-                const uint32_t qh = smem_u32(Qh), ql = smem_u32(Ql), kt = smem_u32(Kr + ks * PA_K_BYTES);
+                const uint32_t qh = smem_u32(Qh), ql = smem_u32(Ql), kt = smem_u32(Kr + ks * P::K_BYTES);
 #pragma unroll
-                for (int k = 0; k < 8; k++) {  // 16 dims per step, 4 steps per 64-dim half
+                for (int k = 0; k < D / 16; k++) {  // 16 dims per step, 4 steps per 64-dim half
                     const uint32_t oq = (k >> 2) * (PA_QT * 128) + (k & 3) * 32;
                     const uint32_t ok_ = (k >> 2) * (PA_KT * 128) + (k & 3) * 32;
                     mma_f16(tS + sb * PA_KT, bg_desc(qh + oq), bg_desc(kt + ok_), idS, k > 0 ? 1u : 0u);
@@ -220,7 +230,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ph = smem_u32(Ph), pl = smem_u32(Pl), vt = smem_u32(Vr + vs * PA_V_BYTES);
+                const uint32_t ph = smem_u32(Ph), pl = smem_u32(Pl), vt = smem_u32(Vr + vs * P::V_BYTES);
 #pragma unroll
                 for (int k = 0; k < PA_KT / 16; k++) {
                     mma_f16(tO, bg_desc(ph + k * 32), bg_desc(vt + k * 32), idO, (t > 0 || k > 0) ? 1u : 0u);
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
             if (!(ok = read_s(t))) break;
 #pragma unroll
             for (int j = 0; j < PA_KT; j++)
-                if (t * PA_KT + j <= qpos) m = fmaxf(m, __uint_as_float(sv[j]));
+                if (CAUSAL ? t * PA_KT + j <= qpos : t * PA_KT + j < n_keys) m = fmaxf(m, __uint_as_float(sv[j]));
         }
         for (int t = 0; t < T && ok; t++) {
             if (!(ok = read_s(T + t))) break;
@@ -270,7 +280,8 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
                     const int j = p * 8 + c;
-                    pv[c] = t * PA_KT + j <= qpos ? expf(__uint_as_float(sv[j]) - m) : 0.0f;
+                    const bool seen = CAUSAL ? t * PA_KT + j <= qpos : t * PA_KT + j < n_keys;
+                    pv[c] = seen ? expf(__uint_as_float(sv[j]) - m) : 0.0f;
                     l += pv[c];
                     ph[c] = __half2float(__float2half_rn(pv[c]));
                 }
@@ -285,21 +296,42 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.pfull);
         }
-        // the output row: O / sum
+        // the output row: O / sum, as f32 (out) and / or split f16 hi / lo into the next contraction's operand (out16)
         if (ok && pa_wait(&sh.ofull, 0, abort_flag, err)) {
             tc_fence_after();
             const float inv = 1.0f / l;
+            const int row = q0 + tid;
+            uint8_t* g16 = a.out16 ? a.out16 + (size_t)(row / BG_SLOTS) * x16_group_bytes(a.out16_K) : nullptr;
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
+            for (int c = 0; c < D / 16; c++) {
                 uint32_t o[16];
                 tmem_ld16(tO + lane_base + c * 16, o);
                 tmem_wait_ld();
-                if (q0 + tid < L) {
-                    float4* op = reinterpret_cast<float4*>(out + (size_t)(q0 + tid) * n_head * 128 + h * 128 + c * 16);
+                if (row < L) {
+                    float y[16];
 #pragma unroll
-                    for (int d = 0; d < 4; d++)
-                        op[d] = make_float4(__uint_as_float(o[4 * d]) * inv, __uint_as_float(o[4 * d + 1]) * inv,
-                                            __uint_as_float(o[4 * d + 2]) * inv, __uint_as_float(o[4 * d + 3]) * inv);
+                    for (int d = 0; d < 16; d++) y[d] = __uint_as_float(o[d]) * inv;
+                    if (a.out) {
+                        float4* op = reinterpret_cast<float4*>(a.out + (size_t)row * a.out_stride + h * D + c * 16);
+#pragma unroll
+                        for (int d = 0; d < 4; d++) op[d] = make_float4(y[4 * d], y[4 * d + 1], y[4 * d + 2], y[4 * d + 3]);
+                    }
+                    if (g16) {
+#pragma unroll
+                        for (int hp = 0; hp < 2; hp++) {  // two 8-column pieces
+                            float yh[8];
+#pragma unroll
+                            for (int d = 0; d < 8; d++) yh[d] = __half2float(__float2half_rn(y[8 * hp + d]));
+                            const float* yy = y + 8 * hp;
+                            const int col = h * D + c * 16 + 8 * hp, n = row % BG_SLOTS;
+                            *reinterpret_cast<uint4*>(g16 + x16_offset(n, col)) =
+                                make_uint4(pack_h2(yh[0], yh[1]), pack_h2(yh[2], yh[3]), pack_h2(yh[4], yh[5]),
+                                           pack_h2(yh[6], yh[7]));
+                            *reinterpret_cast<uint4*>(g16 + x16_offset(BG_SLOTS + n, col)) =
+                                make_uint4(pack_h2(yy[0] - yh[0], yy[1] - yh[1]), pack_h2(yy[2] - yh[2], yy[3] - yh[3]),
+                                           pack_h2(yy[4] - yh[4], yy[5] - yh[5]), pack_h2(yy[6] - yh[6], yy[7] - yh[7]));
+                        }
+                    }
                 }
             }
         }
@@ -312,12 +344,34 @@ __global__ void __launch_bounds__(PA_THREADS, 1)
     }
 }
 
+template <int D, bool CAUSAL>
+static void launch_tc(cudaStream_t st, const TcAttnArgs& a) {
+    static PerDeviceOnce once;
+    once([] {
+        cudaFuncSetAttribute(k_attn_tc<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PaPlan<D>::SMEM);
+    });
+    k_attn_tc<D, CAUSAL><<<dim3((a.L + PA_QT - 1) / PA_QT, a.n_head, 1), PA_THREADS, PaPlan<D>::SMEM, st>>>(a);
+}
+
 void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
                                  const __half* vc, int n_ctx, int pos0, float scale, float* out, int* err) {
-    static PerDeviceOnce once;
-    once([] { cudaFuncSetAttribute(k_attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PA_SMEM); });
-    k_attn_prefill_tc<<<dim3((L + PA_QT - 1) / PA_QT, n_head, 1), PA_THREADS, PA_SMEM, st>>>(
-        qkv, L, n_head, n_kv, kc, vc, n_ctx, pos0, scale, out, err);
+    TcAttnArgs a;
+    a.q = qkv;
+    a.q_stride = (n_head + 2 * n_kv) * 128;
+    a.L = L;
+    a.n_head = n_head;
+    a.group = n_head / n_kv;
+    a.k = kc;
+    a.v = vc;
+    a.kv_head_stride = (size_t)n_ctx * 128;
+    a.pos0 = pos0;
+    a.scale = scale;
+    a.out = out;
+    a.out_stride = n_head * 128;
+    a.err = err;
+    launch_tc<128, true>(st, a);
 }
+
+void launch_attention_full_tc(cudaStream_t st, const TcAttnArgs& a) { launch_tc<64, false>(st, a); }
 
 }  // namespace ocr

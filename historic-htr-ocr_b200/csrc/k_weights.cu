@@ -71,22 +71,25 @@ __device__ __forceinline__ int8_t sat_i8(float v) {
 }
 
 // one q8_0 block of generated values, quantized as ggml's quantize_row_q8_0_ref (text.rs:676-691)
-__global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, uint8_t* __restrict__ w, int row_mul,
-                             int row_add) {
+__global__ void k_synth_q8_0(uint64_t seed, float sigma, int rows, int cols, int valid, uint8_t* __restrict__ w,
+                             int row_mul, int row_add) {
     const int nbr = cols / 32, stride = q8_stride(cols);
     const long nblk = (long)rows * nbr;
     for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < nblk; b += (long)gridDim.x * blockDim.x) {
         float x[32];
         float amax = 0.0f;
+        const int r = (int)(b / nbr), c = (int)(b % nbr);
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-            x[j] = __fmul_rn(sigma, gauss(seed, (uint64_t)b * 32 + j));
+            // value (r, col) = sigma * gauss(r * valid + col) for col < valid, zero past it (valid == cols: the flat
+            // index b * 32 + j)
+            const int col = c * 32 + j;
+            x[j] = col < valid ? __fmul_rn(sigma, gauss(seed, (uint64_t)r * valid + col)) : 0.0f;
             const float a = fabsf(x[j]);
             if (a > amax) amax = a;
         }
         const float dv = __fdiv_rn(amax, 127.0f);
         const float id = dv != 0.0f ? __fdiv_rn(1.0f, dv) : 0.0f;
-        const int r = (int)(b / nbr), c = (int)(b % nbr);
         uint8_t* row = w + ((long)r * row_mul + row_add) * stride;
         uint32_t v[8];
 #pragma unroll
@@ -142,9 +145,10 @@ void launch_unpack_q8_0(cudaStream_t st, const uint8_t* w, int rows, int cols, i
 }
 
 void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, uint8_t* w, int row_mul,
-                       int row_add) {
+                       int row_add, int valid) {
     const long n = (long)rows * (cols / 32);
-    k_synth_q8_0<<<grid_for(n, 128), 128, 0, st>>>(seed, sigma, rows, cols, w, row_mul, row_add);
+    k_synth_q8_0<<<grid_for(n, 128), 128, 0, st>>>(seed, sigma, rows, cols, valid > 0 ? valid : cols, w, row_mul,
+                                                   row_add);
 }
 
 void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out) {

@@ -22,9 +22,10 @@ struct QMat {
 // GGUF blocks [rows][cols/32] x 34 B → the row layout at destination row r * row_mul + row_add
 void launch_repack_q8_0(cudaStream_t st, const uint8_t* blocks, int rows, int cols, uint8_t* w, int row_mul,
                         int row_add);
-// the synthetic generator (bit-identical to the oracle's orc_synth_q8_0 / orc_fill_norm)
+// the synthetic generator (bit-identical to the oracle's orc_synth_q8_0 / orc_fill_norm); valid > 0: only columns
+// below it hold values (sigma * gauss(r * valid + col)), the rest zeros (orc_synth_q8_0_padded)
 void launch_synth_q8_0(cudaStream_t st, uint64_t seed, float sigma, int rows, int cols, uint8_t* w, int row_mul,
-                       int row_add);
+                       int row_add, int valid = 0);
 void launch_synth_norm(cudaStream_t st, uint64_t seed, int n, float* out);
 // back to GGUF blocks (ocr_model_tensor_gguf): source rows r * row_mul + row_add
 void launch_unpack_q8_0(cudaStream_t st, const uint8_t* w, int rows, int cols, int row_mul, int row_add,
@@ -350,5 +351,47 @@ void launch_attention_prefill(cudaStream_t st, const float* qkv, int L, int n_he
 // of the probabilities, two softmax passes; `err` takes a bounded wait's timeout
 void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
                                  const __half* vc, int n_ctx, int pos0, float scale, float* out, int* err);
+// the general form of that kernel: query row r, head h at q[r * q_stride + h * D]; key / value row j of kv head
+// h / group at k[(h / group) * kv_head_stride + j * D] (f16); causal (query r at position pos0 + r sees keys ≤ its
+// position) or full (every query sees keys 0 … n_keys - 1); the output row r, head h as f32 at
+// out[r * out_stride + h * D] and / or split f16 hi / lo into out16 (x16 groups of 32 rows over out16_K columns)
+struct TcAttnArgs {
+    const float* q = nullptr;
+    int q_stride = 0;
+    int L = 0, n_head = 0, group = 1;
+    const __half* k = nullptr;
+    const __half* v = nullptr;
+    size_t kv_head_stride = 0;
+    int pos0 = 0, n_keys = 0;
+    float scale = 1.0f;
+    float* out = nullptr;
+    int out_stride = 0;
+    uint8_t* out16 = nullptr;
+    int out16_K = 0;
+    int* err = nullptr;
+};
+// the full attention of head dim 64 (the vision encoder)
+void launch_attention_full_tc(cudaStream_t st, const TcAttnArgs& a);
+
+// ---- the vision encoder's own kernels (k_vision.cu) --------------------------------------------------------------------
+// The placement of a (not yet baked) image inside the baked canvas: the image's pixel (x, y) sits at (x + left,
+// y + top) of a canvas width x height; every other canvas pixel is white (the bake's pad).
+struct Placement {
+    int img_w = 0, img_h = 0, left = 0, top = 0, width = 0, height = 0;
+};
+// rgb bytes [img_h][img_w][3] → the patch embedding's operand (x16 groups of 32 patches over K columns): patch
+// t = ty * px + tx, column c * p² + ky * p + kx = lut[c][pixel(tx * p + kx, ty * p + ky)[c]], columns past 3 p² zero
+void launch_patchify(cudaStream_t st, const uint8_t* rgb, const Placement& pl, int patch, const float* lut, int K,
+                     uint8_t* x16);
+// the q and k parts of qkv rows [n][3 * dim] rotated by the 2D RoPE (in place for q); k and v written f16
+// head-major: kh[h][n_pad][d_head], vh likewise (rows past n zero)
+void launch_rope2d_heads(cudaStream_t st, float* qkv, int n, int n_head, int d_head, int px, const float* cs,
+                         int max_pos, __half* kh, __half* vh, int n_pad);
+// the projector's input: x [n][dim] RMS-normalised by w, 2x2-unfolded (merged token o = oy * px/2 + ox gets column
+// c * 4 + ky * 2 + kx = xn[(2 oy + ky) * px + 2 ox + kx][c]) into the merger's operand (x16 over 4 dim columns)
+void launch_unfold_prep(cudaStream_t st, const float* x, const float* w, float eps, int px, int py, int dim,
+                        uint8_t* x16);
+// rows [n][K] → GELU (tanh form) → x16 operand (act = 1), or the plain split (act = 0)
+void launch_act_prep(cudaStream_t st, const float* y, int n, int K, int act, uint8_t* x16);
 
 }  // namespace ocr

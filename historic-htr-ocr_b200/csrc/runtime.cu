@@ -16,6 +16,7 @@
 #include <string>
 #include <vector>
 
+#include "ctx.h"
 #include "gguf.h"
 #include "kernels.cuh"
 
@@ -36,29 +37,9 @@ ocr_status cuda_fail(cudaError_t e, const char* what) {
 
 using namespace ocr;
 
-// ---------------------------------------------------------------------------------------------------------------------
-// context
-// ---------------------------------------------------------------------------------------------------------------------
-struct ocr_ctx {
-    int refs = 1;  // the caller's handle + one per live model: freed when the last is released
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    int num_sms = 148;
-    bool pdl = true;
-    int* d_err = nullptr;
-    uint64_t mem_weights = 0, mem_kv = 0, mem_work = 0;
-    // scratch of the low-level ops (grown on demand, freed with the context)
-    void* op_scratch = nullptr;
-    size_t op_scratch_bytes = 0;
-    // pinned staging for uploads
-    void* h_stage = nullptr;
-    void* d_stage = nullptr;
-    size_t stage_bytes = 0;
-};
-
-namespace {
-
 constexpr size_t STAGE_BYTES = 64u << 20;
+
+namespace ocr {
 
 // device memory, zeroed before it is returned. cudaMemset on device memory is asynchronous and runs on the legacy
 // stream, which does not order against the contexts' non-blocking streams: without the wait, the zeroing of a buffer
@@ -102,7 +83,7 @@ ocr_status check_device_error(ocr_ctx* ctx) {
     return OCR_OK;
 }
 
-}  // namespace
+}  // namespace ocr
 
 // ---------------------------------------------------------------------------------------------------------------------
 // model
@@ -1250,6 +1231,18 @@ ocr_status ensure_prefill(ocr_session* s, int n) {
 // =====================================================================================================================
 // the C ABI
 // =====================================================================================================================
+void ocr::ctx_release(ocr_ctx* c) {
+    if (--c->refs > 0) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->op_scratch) cudaFree(c->op_scratch);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->d_stage) cudaFree(c->d_stage);
+    if (c->d_err) cudaFree(c->d_err);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
 extern "C" {
 
 const char* ocr_last_error(void) { return g_err.c_str(); }
@@ -1281,17 +1274,6 @@ ocr_status ocr_ctx_create(int device, ocr_ctx** out) {
 
 // Handles may be released in any order (a garbage collector's, say): a context lives while a model made in it does,
 // a model while a session of it does; each destroy call releases the caller's reference.
-static void ctx_release(ocr_ctx* c) {
-    if (--c->refs > 0) return;
-    cudaSetDevice(c->device);
-    cudaStreamSynchronize(c->stream);
-    if (c->op_scratch) cudaFree(c->op_scratch);
-    if (c->h_stage) cudaFreeHost(c->h_stage);
-    if (c->d_stage) cudaFree(c->d_stage);
-    if (c->d_err) cudaFree(c->d_err);
-    cudaStreamDestroy(c->stream);
-    delete c;
-}
 
 ocr_status ocr_ctx_destroy(ocr_ctx* c) {
     if (c) ctx_release(c);
@@ -1647,7 +1629,7 @@ ocr_status prefill_short(ocr_session* s, int slot, const int32_t* ids, const flo
         tok[slot] = given ? -1 : ids[i];
         if (given)
             OCR_CUDA(cudaMemcpyAsync(s->x + (size_t)slot * c.dim, embd + (size_t)i * c.dim, (size_t)c.dim * 4,
-                                     cudaMemcpyHostToDevice, st));
+                                     cudaMemcpyDefault, st));
         OCR_CUDA(cudaMemcpyAsync(s->tok, tok.data(), s->B * 4, cudaMemcpyHostToDevice, st));
         OCR_CUDA(cudaMemcpyAsync(s->pos, pos.data(), s->B * 4, cudaMemcpyHostToDevice, st));
         record_step(s, false, 1.0f, 1, 0, 0.0f, nullptr, given);
@@ -1689,7 +1671,7 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
     int32_t* d_ids = (int32_t*)(g + (size_t)n * c.n_ff);
     std::vector<int32_t> hid(n);
     for (int i = 0; i < n; i++) hid[i] = ids ? ids[i] : -1;
-    if (any_embd) OCR_CUDA(cudaMemcpyAsync(x, embd, (size_t)n * c.dim * 4, cudaMemcpyHostToDevice, st));
+    if (any_embd) OCR_CUDA(cudaMemcpyAsync(x, embd, (size_t)n * c.dim * 4, cudaMemcpyDefault, st));
     OCR_CUDA(cudaMemcpyAsync(d_ids, hid.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
     launch_embed_rows(st, d_ids, n, s->m->tok, x);
     const int pos0 = s->n_past[slot];

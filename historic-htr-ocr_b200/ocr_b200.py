@@ -39,6 +39,16 @@ class TextCfg(C.Structure):
                                           "n_ctx_train")] + [("eps", C.c_float), ("rope_base", C.c_float)]
 
 
+class VisionCfg(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("n_layer", "dim", "n_head", "n_ff", "patch", "merge", "image_size",
+                                         "proj_dim")] + [("eps", C.c_float), ("rope_theta", C.c_float),
+                                                         ("mean", C.c_float * 3), ("std", C.c_float * 3)]
+
+
+class BakePlan(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("scaled_w", "scaled_h", "left", "top", "right", "bottom")]
+
+
 class SamplerCfg(C.Structure):
     _fields_ = [("rp", C.c_float), ("window", C.c_int32), ("fp", C.c_float), ("max_new", C.c_int32)]
 
@@ -93,6 +103,13 @@ _SIGS = {
     "ocr_profile_step": (C.c_int, [_P, _P, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_timeline_step": (C.c_int, [_P, _P, C.c_int, C.POINTER(KernelTime), C.c_int, C.POINTER(C.c_int)]),
     "ocr_sample_logits": (C.c_int, [_P, _P, C.c_int, C.POINTER(SamplerCfg), _P, C.c_int, _P, _P, C.c_int, _P]),
+    "ocr_bake_plan_for": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(BakePlan)]),
+    "ocr_vision_synthetic": (C.c_int, [_P, C.POINTER(VisionCfg), C.c_uint64, C.c_float, C.POINTER(_P)]),
+    "ocr_vision_destroy": (C.c_int, [_P]),
+    "ocr_vision_config": (C.c_int, [_P, C.POINTER(VisionCfg)]),
+    "ocr_vision_encode": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(C.c_int),
+                                    C.POINTER(C.c_int)]),
+    "ocr_vision_encode_page": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(C.c_int)]),
     "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
     "ocr_gguf_open_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
     "ocr_gguf_close": (C.c_int, [_P]),
@@ -309,6 +326,104 @@ class TextModel:
         return Session(self, h, n_ctx, batch)
 
 
+# ---------------------------------------------------------------------------------------------------------------------
+# the vision encoder + projector (Vision, app/crates/ocr-wgpu/src/vision.rs:37-450) and the bake's plan
+# ---------------------------------------------------------------------------------------------------------------------
+@dataclass
+class VisionConfig:
+    """VisionConfig (vision.rs:37-88); the defaults are the LightOnOCR mmproj's shape (Pixtral ViT, 1540 px)"""
+    n_layer: int = 24
+    dim: int = 1024
+    n_head: int = 16
+    n_ff: int = 4096
+    patch: int = 14
+    merge: int = 2
+    image_size: int = 1540
+    proj_dim: int = 1024
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+    mean: tuple = (0.48145466, 0.4578275, 0.40821073)
+    std: tuple = (0.26862954, 0.26130258, 0.27577711)
+
+    def c(self) -> VisionCfg:
+        return VisionCfg(self.n_layer, self.dim, self.n_head, self.n_ff, self.patch, self.merge, self.image_size,
+                         self.proj_dim, self.eps, self.rope_theta, (C.c_float * 3)(*self.mean),
+                         (C.c_float * 3)(*self.std))
+
+    def as_dict(self) -> dict:
+        return dict(n_layer=self.n_layer, dim=self.dim, n_head=self.n_head, n_ff=self.n_ff, patch=self.patch,
+                    merge=self.merge, image_size=self.image_size, proj_dim=self.proj_dim, eps=self.eps,
+                    rope_theta=self.rope_theta, mean=list(self.mean), std=list(self.std))
+
+
+def bake_plan(longest: int, grid: int, w0: int, h0: int) -> tuple:
+    """imageops.rs plan(Bake { longest, grid }, w0, h0): (scaled_w, scaled_h, left, top, right, bottom)"""
+    p = BakePlan()
+    _check(lib().ocr_bake_plan_for(longest, grid, w0, h0, C.byref(p)))
+    return (p.scaled_w, p.scaled_h, p.left, p.top, p.right, p.bottom)
+
+
+class Vision:
+    def __init__(self, ctx: Context, h: C.c_void_p):
+        self.ctx, self.h = ctx, h
+        c = VisionCfg()
+        _check(lib().ocr_vision_config(h, C.byref(c)))
+        self.cfg = VisionConfig(c.n_layer, c.dim, c.n_head, c.n_ff, c.patch, c.merge, c.image_size, c.proj_dim, c.eps,
+                                c.rope_theta, tuple(c.mean), tuple(c.std))
+
+    @classmethod
+    def synthetic(cls, ctx: Context, cfg: VisionConfig, seed: int, sigma_w: float = 0.02) -> "Vision":
+        h = C.c_void_p()
+        c = cfg.c()
+        _check(lib().ocr_vision_synthetic(ctx.h, C.byref(c), C.c_uint64(seed), sigma_w, C.byref(h)))
+        return cls(ctx, h)
+
+    def close(self) -> None:
+        if self.h:
+            lib().ocr_vision_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, rgb, layers: int = -1, out=None, w: int = 0, h: int = 0) -> np.ndarray:
+        """Vision::encode: a baked rgb image (uint8 [h][w][3] numpy, or a device pointer with w, h) → the embeddings
+        [n_tokens][proj_dim] (layers < 0) or the residual [n_patches][dim] after `layers` encoder layers. `out` (a
+        torch tensor on the device, or None for a new host array) receives the rows."""
+        if not isinstance(rgb, int):
+            rgb = np.ascontiguousarray(rgb, np.uint8)
+            h, w = rgb.shape[:2]
+        c = self.cfg
+        n = (w // c.patch) * (h // c.patch)
+        rows, width = (n, c.dim) if layers >= 0 else (n // (c.merge * c.merge), c.proj_dim)
+        host = out is None
+        if host:
+            out = np.empty((rows, width), np.float32)
+        cap = rows * width if host else out.numel()
+        nr, rw = C.c_int(), C.c_int()
+        _check(lib().ocr_vision_encode(self.h, _ptr(rgb), w, h, layers, _ptr(out), cap, C.byref(nr), C.byref(rw)))
+        return out
+
+    def encode_page(self, rgb: np.ndarray, out=None) -> np.ndarray:
+        """the bake (white pads, no resize) and the encode in one call: rgb uint8 [h0][w0][3]"""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        h0, w0 = rgb.shape[:2]
+        c = self.cfg
+        sw, sh, left, top, right, bottom = bake_plan(c.image_size, c.patch * c.merge, w0, h0)
+        g = c.patch * c.merge
+        rows = ((sw + left + right) // g) * ((sh + top + bottom) // g)
+        host = out is None
+        if host:
+            out = np.empty((rows, c.proj_dim), np.float32)
+        cap = rows * c.proj_dim if host else out.numel()
+        nr = C.c_int()
+        _check(lib().ocr_vision_encode_page(self.h, _ptr(rgb), w0, h0, _ptr(out), cap, C.byref(nr)))
+        return out
+
+
 class Session:
     def __init__(self, model: TextModel, h: C.c_void_p, n_ctx: int, batch: int):
         self.model, self.h, self.n_ctx, self.batch = model, h, n_ctx, batch
@@ -342,11 +457,17 @@ class Session:
 
     def prefill(self, slot: int = 0, ids: Optional[Sequence[int]] = None, embd: Optional[np.ndarray] = None,
                 logits: bool = True) -> Optional[np.ndarray]:
-        """rows: ids[i] >= 0 → token, else embedding row i of embd ([n][dim] f32)"""
+        """rows: ids[i] >= 0 → token, else embedding row i of embd ([n][dim] f32: a host array, or a device tensor
+        such as Vision.encode's output)"""
         dim, V = self.model.cfg.dim, self.model.cfg.n_vocab
         ida = None if ids is None else np.ascontiguousarray(ids, dtype=np.int32)
-        ea = None if embd is None else np.ascontiguousarray(embd, dtype=np.float32).reshape(-1, dim)
-        n = len(ida) if ida is not None else (0 if ea is None else ea.shape[0])
+        if embd is None or hasattr(embd, "data_ptr"):
+            ea = embd
+            n_e = 0 if embd is None else embd.numel() // dim
+        else:
+            ea = np.ascontiguousarray(embd, dtype=np.float32).reshape(-1, dim)
+            n_e = ea.shape[0]
+        n = len(ida) if ida is not None else n_e
         out = np.empty(V, np.float32) if logits else None
         _check(lib().ocr_prefill(self.h, slot, _ptr(ida), _ptr(ea), n, _ptr(out)))
         return out

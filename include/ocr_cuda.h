@@ -101,7 +101,8 @@ ocr_status ocr_session_kv(const ocr_session* s, int layer, int slot, int row0, i
                           uint16_t* v_out);
 
 /* TextModel::prefill (text.rs:437-521) for one slot: n_rows rows at positions n_past…; row i is token ids[i] when
- * ids != NULL and ids[i] >= 0, else embedding row i of embd ([n_rows][dim] f32, Input::Embeddings). Host buffers.
+ * ids != NULL and ids[i] >= 0, else embedding row i of embd ([n_rows][dim] f32, Input::Embeddings; host or device
+ * memory, e.g. the output of ocr_vision_encode). ids is a host buffer.
  * logits_out (nullable, [n_vocab]) = the last row's logits; they also stay on the device for the first choice. */
 ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float* embd, int n_rows, float* logits_out);
 
@@ -181,6 +182,49 @@ ocr_status ocr_read_pages(ocr_session* s, const ocr_sampler_cfg* cfg, int chunk,
 ocr_status ocr_sample_logits(ocr_ctx* ctx, const float* d_logits, int n_vocab, const ocr_sampler_cfg* cfg,
                              const int32_t* history, int n_hist, const int32_t* count_tok, const uint32_t* count_n,
                              int n_counts, int32_t* tok);
+
+/* ---- the vision encoder + projector (replaces Vision, app/crates/ocr-wgpu/src/vision.rs:37-450) ------------------ */
+typedef struct ocr_vision ocr_vision;
+
+/* VisionConfig (vision.rs:37-88): the Pixtral-shaped ViT and the LightOnOCR projector. dim / n_head must be 64
+ * (vision.rs:71-73), merge 2 and n_ff >= 4 dim (the 2x2 unfold, vision.rs:412-414). */
+typedef struct {
+    int32_t n_layer, dim, n_head, n_ff, patch, merge, image_size, proj_dim;
+    float eps, rope_theta;
+    float mean[3], std[3];
+} ocr_vision_cfg;
+
+/* the bake's plan (BakePlan, app/crates/ocr-core/src/imageops.rs:262-316): the image scaled to scaled_w x scaled_h
+ * (longest edge <= longest, never up), then white pads on each side up to 56 px on the short edge and the grid */
+typedef struct {
+    int32_t scaled_w, scaled_h, left, top, right, bottom;
+} ocr_bake_plan;
+/* imageops.rs:275-316 plan(Bake { longest, grid }, w0, h0). Host only. */
+ocr_status ocr_bake_plan_for(int longest, int grid, int w0, int h0, ocr_bake_plan* out);
+
+/* A seeded synthetic encoder with q8_0 weights (the reference loads bf16 / f32 mmproj weights, vision.rs:131-135;
+ * BASELINE config 4 asks q8_0): every matrix sigma_w * N(0,1)-like values quantised, the patch embedding's 3 p²
+ * columns padded with zero columns to a multiple of 256, norms 1 + 0.01 U(-1,1). Bit-identical to the CPU
+ * oracle's orc_vision_synthetic of the same seed (sub-streams 200000 + layer * 16 + kind, 300000 … 300005). */
+ocr_status ocr_vision_synthetic(ocr_ctx* ctx, const ocr_vision_cfg* cfg, uint64_t seed, float sigma_w,
+                                ocr_vision** out);
+ocr_status ocr_vision_destroy(ocr_vision* v);
+ocr_status ocr_vision_config(const ocr_vision* v, ocr_vision_cfg* out);
+
+/* Vision::encode / encode_gpu (vision.rs:256-317): rgb [h][w][3] bytes of a BAKED image — both sides multiples of
+ * patch * merge, the longest <= image_size, else OCR_ERR_ARG ("not baked"), like the reference — in host or device
+ * memory. layers < 0: the image's embeddings for the text model, [n_tokens][proj_dim] f32 with n_tokens = (w / 28) *
+ * (h / 28); layers = k in 0 … n_layer: the residual stream [n_patches][dim] after k encoder layers (the reference's
+ * bisect hook, vision.rs:253-255). out: host or device memory of cap floats; *n_rows and *row_width (nullable) get
+ * the shape. Synchronous. */
+ocr_status ocr_vision_encode(ocr_vision* v, const uint8_t* rgb, int w, int h, int layers, float* out, size_t cap,
+                             int* n_rows, int* row_width);
+/* The bake and the encode of a page in one call: rgb [h0][w0][3] of any size whose bake needs no resize (longest
+ * edge <= image_size), placed per ocr_bake_plan_for(image_size, patch * merge, …) in its white canvas — the pad is
+ * made inside the patch gather, no baked copy is formed — then encoded as ocr_vision_encode(layers = -1). A page
+ * whose bake would resize it is refused with OCR_ERR_ARG. */
+ocr_status ocr_vision_encode_page(ocr_vision* v, const uint8_t* rgb, int w0, int h0, float* out, size_t cap,
+                                  int* n_rows);
 
 /* ---- GGUF reader, host only (ocr_gguf::Gguf, app/crates/ocr-gguf/src/lib.rs:213-509) ------------------------------ */
 typedef struct ocr_gguf ocr_gguf;

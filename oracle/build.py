@@ -1,4 +1,4 @@
-"""Build the CPU oracle (test infrastructure): oracle/_build/liboracle.so from oracle.c with gcc.
+"""Build the CPU oracle (test infrastructure): oracle/_build/liboracle.so from oracle.c and vision.c with gcc.
 
     python oracle/build.py [--force]
 
@@ -20,7 +20,7 @@ FLAGS = ["-O3", "-march=x86-64-v3", "-fopenmp", "-ffp-contract=off", "-fno-math-
 
 
 def build(force: bool = False) -> Path:
-    src = [HERE / "oracle.c"]
+    src = [HERE / "oracle.c", HERE / "vision.c"]
     hdr = [HERE / "oracle.h"]
     if not force and OUT.exists() and OUT.stat().st_mtime >= max(p.stat().st_mtime for p in src + hdr):
         return OUT

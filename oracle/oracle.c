@@ -187,6 +187,14 @@ static inline double row_dot_q8_0(const uint8_t* row, int nb, const float* x) {
     return s;
 }
 
+void orc_matvec_q8_0_serial(const uint8_t* w, int rows, int k, const float* x, float* y, int accumulate) {
+    int nb = k / 32;
+    for (int r = 0; r < rows; r++) {
+        float v = (float)row_dot_q8_0(w + (size_t)r * nb * 34, nb, x);
+        y[r] = accumulate ? y[r] + v : v;
+    }
+}
+
 void orc_matvec_q8_0(const uint8_t* w, int rows, int k, const float* x, float* y, int accumulate) {
     int nb = k / 32;
 #pragma omp parallel for schedule(static)

@@ -117,6 +117,47 @@ const uint16_t* orc_session_v(const orc_session* s, int layer);
 int orc_session_set_kv(orc_session* s, int layer, int row0, int n, const uint16_t* k, const uint16_t* v);
 
 int orc_num_threads(void);
+/* orc_matvec_q8_0 on the calling thread alone (for callers already inside a parallel loop) */
+void orc_matvec_q8_0_serial(const uint8_t* w, int rows, int k, const float* x, float* y, int accumulate);
+
+/* ---------- the vision encoder + projector (vision.c; vision.rs:266-423) ---------- */
+typedef struct {
+    int n_layer, dim, n_head, n_ff, patch, merge, image_size, proj_dim;
+    float eps, rope_theta;
+    float mean[3], std[3];
+} orc_vcfg;
+
+typedef struct orc_vision orc_vision;
+
+/* tensor kinds of one encoder layer, numbered like their synthetic sub-streams */
+enum { ORC_V_LN1 = 0, ORC_V_Q, ORC_V_K, ORC_V_V, ORC_V_O, ORC_V_LN2, ORC_V_GATE, ORC_V_UP, ORC_V_DOWN, ORC_V_N_KINDS };
+#define ORC_V_LAYER_STREAM 200000u      /* layer l, kind k: sub-stream ORC_V_LAYER_STREAM + l * 16 + k */
+#define ORC_V_PATCH_STREAM 300000u
+#define ORC_V_PRE_LN_STREAM 300001u
+#define ORC_V_INPUT_NORM_STREAM 300002u
+#define ORC_V_MERGER_STREAM 300003u
+#define ORC_V_MM1_STREAM 300004u
+#define ORC_V_MM2_STREAM 300005u
+
+/* the patch embedding's padded width: 3 * patch² rounded up to a multiple of 256 (zero columns past 3 * patch²) */
+int orc_vision_patch_cols(const orc_vcfg* c);
+void orc_synth_q8_0_padded(uint8_t* blocks, int rows, int cols, int valid, uint64_t seed, float sigma);
+orc_vision* orc_vision_synthetic(const orc_vcfg* cfg, uint64_t seed, float sigma_w);
+void orc_vision_free(orc_vision* v);
+void orc_pixel_lut(const orc_vcfg* c, float* lut /* [3][256] */);
+void orc_rope2d_table(float theta, int d_head, int max_pos, float* out /* [2][max_pos][d_head/4][2] */);
+float orc_gelu_tanh(float x);
+/* a baked image rgb [h][w][3] → out [n_tokens][proj_dim]; layers >= 0 stops after that many encoder layers and gives
+ * the residual [n_patches][dim]. Returns the rows written, -1 for an image that is not baked. */
+int orc_vision_encode(const orc_vision* v, const uint8_t* rgb, int w, int h, int layers, float* out);
+/* the residual after the first encoder layer for the listed patch rows only ([n_rows][dim]); the keys and values of
+ * every patch are computed */
+int orc_vision_layer1_rows(const orc_vision* v, const uint8_t* rgb, int w, int h, const int* rows, int n_rows,
+                           float* out);
+/* the bake (imageops.rs:275-323): out = [scaled_w, scaled_h, left, top, right, bottom] */
+void orc_bake_plan(int longest, int grid, int w0, int h0, int* out);
+/* the bake of an image that needs no resize: white pads per the plan; -1 when the plan resizes */
+int orc_bake_pad(const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out);
 
 #ifdef __cplusplus
 }

@@ -19,6 +19,12 @@ ATTN_NORM, Q, K, V, O, Q_NORM, K_NORM, FFN_NORM, GATE, UP, DOWN = range(11)
 TOK_EMBD_STREAM, OUTPUT_NORM_STREAM = 100000, 100001
 
 
+class VCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layer", "dim", "n_head", "n_ff", "patch", "merge", "image_size",
+                                         "proj_dim")] + [("eps", C.c_float), ("rope_theta", C.c_float),
+                                                         ("mean", C.c_float * 3), ("std", C.c_float * 3)]
+
+
 class Cfg(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("n_layer", "dim", "n_head", "n_kv", "d_head", "n_ff", "n_vocab")] + [
         ("eps", C.c_float), ("rope_base", C.c_float)]
@@ -60,6 +66,17 @@ _SIGS = {
     "orc_session_v": (_P, [_P, C.c_int]),
     "orc_session_set_kv": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, _P, _P]),
     "orc_num_threads": (C.c_int, []),
+    "orc_vision_patch_cols": (C.c_int, [_P]),
+    "orc_synth_q8_0_padded": (None, [_P, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_float]),
+    "orc_vision_synthetic": (_P, [_P, C.c_uint64, C.c_float]),
+    "orc_vision_free": (None, [_P]),
+    "orc_pixel_lut": (None, [_P, _P]),
+    "orc_rope2d_table": (None, [C.c_float, C.c_int, C.c_int, _P]),
+    "orc_gelu_tanh": (C.c_float, [C.c_float]),
+    "orc_vision_encode": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P]),
+    "orc_vision_layer1_rows": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, C.c_int, _P]),
+    "orc_bake_plan": (None, [C.c_int, C.c_int, C.c_int, C.c_int, _P]),
+    "orc_bake_pad": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -292,3 +309,80 @@ class Session:
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+# ---- the vision encoder + projector (vision.c) --------------------------------------------------------------------------
+V_LN1, V_Q, V_K, V_V, V_O, V_LN2, V_GATE, V_UP, V_DOWN = range(9)
+V_LAYER_STREAM, V_PATCH_STREAM, V_PRE_LN_STREAM, V_INPUT_NORM_STREAM = 200000, 300000, 300001, 300002
+V_MERGER_STREAM, V_MM1_STREAM, V_MM2_STREAM = 300003, 300004, 300005
+
+
+def vcfg(d: dict) -> VCfg:
+    return VCfg(d["n_layer"], d["dim"], d["n_head"], d["n_ff"], d["patch"], d["merge"], d["image_size"],
+                d["proj_dim"], d["eps"], d["rope_theta"], (C.c_float * 3)(*d["mean"]), (C.c_float * 3)(*d["std"]))
+
+
+class Vision:
+    """the synthetic q8_0 encoder + projector of a config dict (the keys of VCfg)"""
+
+    def __init__(self, cfg: dict, seed: int, sigma_w: float = 0.02):
+        self.cfg = dict(cfg)
+        self._c = vcfg(cfg)
+        self.h = lib().orc_vision_synthetic(C.byref(self._c), seed, sigma_w)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_vision_free(self.h)
+            self.h = None
+
+    def grid(self, w: int, h: int) -> tuple[int, int]:
+        return w // self.cfg["patch"], h // self.cfg["patch"]
+
+    def encode(self, rgb: np.ndarray, layers: int = -1) -> np.ndarray:
+        """rgb uint8 [h][w][3] (baked) → [n_tokens][proj_dim], or the residual [n_patches][dim] after `layers`"""
+        h, w = rgb.shape[:2]
+        px, py = self.grid(w, h)
+        n = px * py
+        m = self.cfg["merge"] ** 2
+        out = np.empty((n, self.cfg["dim"]) if layers >= 0 else (n // m, self.cfg["proj_dim"]), np.float32)
+        rc = lib().orc_vision_encode(self.h, _p(np.ascontiguousarray(rgb, np.uint8)), w, h, layers, _p(out))
+        if rc < 0:
+            raise ValueError(f"image {w}x{h} is not baked")
+        return out
+
+    def layer1_rows(self, rgb: np.ndarray, rows: Sequence[int]) -> np.ndarray:
+        h, w = rgb.shape[:2]
+        r = np.ascontiguousarray(rows, np.int32)
+        out = np.empty((r.size, self.cfg["dim"]), np.float32)
+        if lib().orc_vision_layer1_rows(self.h, _p(np.ascontiguousarray(rgb, np.uint8)), w, h, _p(r), r.size,
+                                        _p(out)) < 0:
+            raise ValueError("bad image or rows")
+        return out
+
+
+def rope2d_table(theta: float, d_head: int, max_pos: int) -> np.ndarray:
+    out = np.empty((2, max_pos, d_head // 4, 2), np.float32)
+    lib().orc_rope2d_table(theta, d_head, max_pos, _p(out))
+    return out
+
+
+def pixel_lut(cfg: dict) -> np.ndarray:
+    out = np.empty((3, 256), np.float32)
+    c = vcfg(cfg)
+    lib().orc_pixel_lut(C.byref(c), _p(out))
+    return out
+
+
+def bake_plan(longest: int, grid: int, w0: int, h0: int) -> tuple[int, ...]:
+    out = np.empty(6, np.int32)
+    lib().orc_bake_plan(longest, grid, w0, h0, _p(out))
+    return tuple(int(v) for v in out)
+
+
+def bake_pad(rgb: np.ndarray, longest: int = 1540, grid: int = 28) -> np.ndarray:
+    h0, w0 = rgb.shape[:2]
+    sw, sh, left, top, right, bottom = bake_plan(longest, grid, w0, h0)
+    out = np.empty((sh + top + bottom, sw + left + right, 3), np.uint8)
+    if lib().orc_bake_pad(_p(np.ascontiguousarray(rgb, np.uint8)), w0, h0, longest, grid, _p(out)) != 0:
+        raise ValueError("the bake of this image resizes it")
+    return out

@@ -1,0 +1,137 @@
+"""The vision encoder's host pieces without a GPU: the bake's plan (libocrcuda's ocr_bake_plan_for and the oracle's
+orc_bake_plan) against a plain-Python restatement of the reference's plan (app/crates/ocr-core/src/imageops.rs:275-316)
+and its known cases, the bake's pad, the oracle's 2D RoPE table, pixel LUT and GELU against numpy restatements of
+vision.rs:152-175 and gelu.wgsl, the synthetic vision weights' padded patch embedding, and the oracle's layer-1 row
+subset (the full-size pin of the device encoder) against its whole-image encode.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+VCFG = dict(n_layer=2, dim=256, n_head=4, n_ff=1024, patch=14, merge=2, image_size=1540, proj_dim=256, eps=1e-5,
+            rope_theta=1e4, mean=[0.48145466, 0.4578275, 0.40821073], std=[0.26862954, 0.26130258, 0.27577711])
+
+
+def plan_py(longest, grid, w0, h0):
+    """imageops.rs:275-316, step by step"""
+    w, h = float(w0), float(h0)
+    if max(w, h) > longest:
+        s = longest / max(w, h)
+        w, h = max(1.0, float(round_half_away(w * s))), max(1.0, float(round_half_away(h * s)))
+    sw, sh = int(w), int(h)
+    pads = [0, 0, 0, 0]  # left, top, right, bottom
+
+    def pad(nw, nh):
+        nonlocal w, h
+        pw, ph = int(nw - w), int(nh - h)
+        pads[0] += pw // 2
+        pads[2] += pw - pw // 2
+        pads[1] += ph // 2
+        pads[3] += ph - ph // 2
+        w, h = nw, nh
+
+    if min(w, h) < 56.0:
+        pad(56.0, h) if w <= h else pad(w, 56.0)
+    gw, gh = math.ceil(w / grid) * grid, math.ceil(h / grid) * grid
+    if gw != w or gh != h:
+        pad(float(gw), float(gh))
+    return (sw, sh, pads[0], pads[1], pads[2], pads[3])
+
+
+def round_half_away(x):  # Rust f64::round
+    return math.floor(x + 0.5) if x >= 0 else -math.floor(-x + 0.5)
+
+
+SIZES = [(1540, 1100), (1540, 1120), (3000, 2000), (2000, 3000), (40, 30), (30, 40), (10, 2000), (1541, 700),
+         (1100, 1540), (28, 28), (56, 57), (1, 1), (777, 333), (4000, 4000), (1539, 1541)]
+
+
+@pytest.mark.parametrize("w0,h0", SIZES)
+def test_bake_plan_matches_the_reference_rules(ocr, orc, w0, h0):
+    want = plan_py(1540, 28, w0, h0)
+    assert orc.bake_plan(1540, 28, w0, h0) == want
+    assert ocr.bake_plan(1540, 28, w0, h0) == want
+    sw, sh, l, t, r, b = want
+    fw, fh = sw + l + r, sh + t + b
+    assert fw % 28 == 0 and fh % 28 == 0
+    assert (fw if sw <= sh else fh) >= 56  # the short edge (width on a tie) reaches 56
+    assert max(sw, sh) <= 1540
+
+
+def test_bake_plan_known_cases(ocr):
+    # config 4's page: 1540 x 1100 is on the size limit; the height pads 20 px, 10 top and 10 bottom → 110 x 80 patches
+    assert ocr.bake_plan(1540, 28, 1540, 1100) == (1540, 1100, 0, 10, 0, 10)
+    # the pad's odd pixel goes right / bottom (left / top take the smaller half)
+    assert ocr.bake_plan(1540, 28, 1540, 1099) == (1540, 1099, 0, 10, 0, 11)
+
+
+def test_bake_pad_places_the_image_in_white(orc):
+    rng = np.random.default_rng(5)
+    img = rng.integers(0, 255, (1099, 1540, 3), dtype=np.uint8)
+    out = orc.bake_pad(img)
+    assert out.shape == (1120, 1540, 3)
+    assert (out[:10] == 255).all() and (out[1109:] == 255).all()
+    assert np.array_equal(out[10:1109], img)
+    with pytest.raises(ValueError):
+        orc.bake_pad(np.zeros((2000, 3000, 3), np.uint8))
+
+
+def test_rope2d_table_and_lut_and_gelu(orc):
+    # vision.rs:159-175 in numpy f32, the angle multiplied up step by step
+    theta, dh, mp = np.float32(1e4), 64, 110
+    tab = orc.rope2d_table(1e4, dh, mp)
+    ts = np.power(theta, np.float32(-2.0 / 32), dtype=np.float32)
+    for half in range(2):
+        fs = np.float32(1.0) if half == 0 else np.power(theta, np.float32(-2.0 / 64), dtype=np.float32)
+        for pos in (0, 1, 37, 109):
+            t = np.float32(pos)
+            for k in range(16):
+                a = np.float32(fs * t)
+                # (numpy's f32 power and the C library's powf may differ by an ulp, which the step-by-step products
+                # carry into the angle: a bound of a few ulps of the angle)
+                tol = 2e-7 + 8 * abs(float(a)) * 2.0 ** -24 * (k + 1)
+                assert abs(tab[half, pos, k, 0] - math.cos(a)) <= tol and abs(tab[half, pos, k, 1] - math.sin(a)) <= tol
+                t = np.float32(t * ts)
+    assert (tab[:, 0, :, 0] == 1).all() and (tab[:, 0, :, 1] == 0).all()
+    assert tab[0, 1, 0, 0] == np.float32(math.cos(1.0)) and tab[0, 1, 0, 1] == np.float32(math.sin(1.0))
+    lut = orc.pixel_lut(VCFG)
+    v = np.arange(256, dtype=np.float32)
+    for c in range(3):
+        want = (v / np.float32(255) - np.float32(VCFG["mean"][c])) / np.float32(VCFG["std"][c])
+        assert np.array_equal(lut[c], want.astype(np.float32))
+    x = np.linspace(-30, 30, 2001).astype(np.float32)
+    g = np.array([orc.lib().orc_gelu_tanh(float(a)) for a in x], np.float32)
+    xd = x.astype(np.float64)
+    t = np.clip(0.7978845608028654 * xd * (1 + 0.044715 * xd * xd), -15, 15)
+    # (1 + tanh) cancels for negative x: the bound is in units of |x|, the f32 evaluation's error there
+    assert (np.abs(g - 0.5 * xd * (1 + np.tanh(t))) <= 1e-6 * np.maximum(1.0, np.abs(xd))).all()
+
+
+def test_padded_patch_embedding_is_zero_past_the_patch(orc):
+    rows, cols, valid = 8, 768, 588
+    b = np.empty(rows * cols // 32 * 34, np.uint8)
+    orc.lib().orc_synth_q8_0_padded(b.ctypes.data, rows, cols, valid, 1234, 0.02)
+    w = orc.dequantize_q8_0(b, rows * cols).reshape(rows, cols)
+    assert (w[:, valid:] == 0).all() and (w[:, :valid] != 0).mean() > 0.9
+    # columns below `valid` hold the generator's values for the flat index r * valid + c
+    x = orc.gauss(1234, rows * valid, 0.02).reshape(rows, valid)
+    assert np.abs(w[:, :576] - x[:, :576]).max() <= np.abs(x).max() / 127 * 0.51 + 1e-7
+    # valid == cols: the plain generator
+    b2 = np.empty(4 * 256 // 32 * 34, np.uint8)
+    orc.lib().orc_synth_q8_0_padded(b2.ctypes.data, 4, 256, 256, 77, 0.02)
+    assert np.array_equal(b2, orc.synth_q8_0(4 * 256, 77, 0.02))
+
+
+def test_oracle_layer1_rows_equal_its_encode(orc):
+    v = orc.Vision(VCFG, 11)
+    img = np.random.default_rng(0).integers(0, 256, (84, 112, 3), dtype=np.uint8)
+    full = v.encode(img, layers=1)
+    rows = [0, 5, 23, 47]
+    assert np.array_equal(v.layer1_rows(img, rows), full[rows])
+    out = v.encode(img)
+    assert out.shape == (12, 256) and np.isfinite(out).all()
+    with pytest.raises(ValueError):
+        v.encode(img[:, :100])  # 100 px: not on the 28 grid
