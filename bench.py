@@ -469,7 +469,7 @@ def run_config4(args, ocr, ctx, torch, pg, rank, world, local):
     ids_pre = [int(t) for t in rng.integers(0, CONFIG2["n_vocab"], PROMPT_PRE)]
     ids_post = [int(t) for t in rng.integers(0, CONFIG2["n_vocab"], PROMPT_POST)]
     ids = ids_pre + [-1] * n_img + ids_post
-    n_prompt, new = len(ids), WORKLOADS[4]["new"]
+    n_prompt, new = len(ids), args.tokens or WORKLOADS[4]["new"]
     rows = torch.zeros((n_prompt, CONFIG2["dim"]), dtype=torch.float32, device="cuda")
     img_rows = rows[PROMPT_PRE:PROMPT_PRE + n_img]
     sess = model.session(n_prompt + new)

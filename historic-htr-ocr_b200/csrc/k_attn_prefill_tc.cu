@@ -27,6 +27,10 @@ constexpr int PA_QT = 128;       // queries per CTA: the MMA's M, one TMEM lane 
 constexpr int PA_KT = 64;        // keys per tile
 constexpr int PA_LOADERS = 8;    // warps 5-12: the staging
 constexpr int PA_THREADS = (5 + PA_LOADERS) * 32;
+// the pre-tiled form (K and V^T already in the operand layout in global memory, each tile one bulk copy): warps 0-3
+// the rows, warp 4 the tensor cores, warp 5 the copies — two CTAs per SM
+constexpr int PA_THREADS_TILED = 6 * 32;
+__host__ __device__ constexpr int pa_threads(bool tiled) { return tiled ? PA_THREADS_TILED : PA_THREADS; }
 constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128 … 128 + D
 // the shared-memory plan of head dim D: Q hi / lo, two K tiles, two V tiles (transposed), P hi / lo
 template <int D>
@@ -65,8 +69,10 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int D, bool CAUSAL>
-__global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
+template <int D, bool CAUSAL, bool TILED>
+__global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(TcAttnArgs a) {
+    constexpr int THREADS = pa_threads(TILED);
+    static_assert(!TILED || D == 64, "the pre-tiled operands are written for head dim 64");
     using P = PaPlan<D>;
     const int L = a.L, n_head = a.n_head, pos0 = a.pos0;
     const float scale = a.scale;
@@ -91,9 +97,9 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
 
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
-            mbar_init(&sh.kfull[i], PA_LOADERS);
+            mbar_init(&sh.kfull[i], TILED ? 1 : PA_LOADERS);
             mbar_init(&sh.kempty[i], 1);
-            mbar_init(&sh.vfull[i], PA_LOADERS);
+            mbar_init(&sh.vfull[i], TILED ? 1 : PA_LOADERS);
             mbar_init(&sh.vempty[i], 1);
             mbar_init(&sh.sfull[i], 1);
             mbar_init(&sh.sfree[i], 4);
@@ -111,7 +117,7 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
     }
     // the Q tile, scaled, split f16 hi / lo: row r, 8 dims per 16-byte piece, dims in D/64 halves of 64 columns (rows
     // past L zero)
-    for (int e = tid; e < PA_QT * (D / 8); e += PA_THREADS) {
+    for (int e = tid; e < PA_QT * (D / 8); e += THREADS) {
         const int r = e / (D / 8), pc = e % (D / 8), hf = pc >> 3, p = pc & 7;
         uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = make_uint4(0u, 0u, 0u, 0u);
         if (q0 + r < L) {
@@ -136,7 +142,33 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
     const uint32_t tmem = sh.tmem;
     const uint32_t tS = tmem, tO = tmem + 128;
 
-    if (warp >= 5) {
+    if (TILED && warp == 5) {
+        // ---- the copies: pass 1 the K tiles; pass 2 each tile's K, then its V^T (one bulk copy each) ----
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t kn[2] = {0u, 0u}, vn[2] = {0u, 0u};  // copies issued per ring slot
+            for (int seq = 0; seq < 2 * T && ok; seq++) {
+                const int t = seq < T ? seq : seq - T, ks = seq & 1;
+                if (seq >= 2 && !(ok = pa_wait(&sh.kempty[ks], ((seq >> 1) - 1) & 1, abort_flag, err))) break;
+                mbar_expect_tx(&sh.kfull[ks], P::K_BYTES);
+                bulk_g2s(Kr + ks * P::K_BYTES, kbase + (size_t)t * PA_KT * D, P::K_BYTES, &sh.kfull[ks]);
+                kn[ks]++;
+                if (seq < T) continue;
+                const int vs = t & 1;
+                if (t >= 2 && !(ok = pa_wait(&sh.vempty[vs], ((t >> 1) - 1) & 1, abort_flag, err))) break;
+                mbar_expect_tx(&sh.vfull[vs], P::V_BYTES);
+                bulk_g2s(Vr + vs * P::V_BYTES, vbase + (size_t)t * PA_KT * D, P::V_BYTES, &sh.vfull[vs]);
+                vn[vs]++;
+            }
+            if (!ok) *abort_flag = 1;
+            // every copy landed before the shared memory is given back (bounded; the last phase of each slot)
+            for (int i = 0; i < 2; i++) {
+                if (kn[i]) mbar_wait(&sh.kfull[i], (kn[i] - 1) & 1, err);
+                if (vn[i]) mbar_wait(&sh.vfull[i], (vn[i] - 1) & 1, err);
+            }
+        }
+        __syncwarp();
+    } else if (!TILED && warp >= 5) {
         // ---- staging: pass 1 the K tiles; pass 2 each tile's K, then its V transposed ----
         const int lt = tid - 5 * 32;
         bool ok = true;
@@ -344,13 +376,15 @@ __global__ void __launch_bounds__(PA_THREADS, 1) k_attn_tc(TcAttnArgs a) {
     }
 }
 
-template <int D, bool CAUSAL>
+template <int D, bool CAUSAL, bool TILED>
 static void launch_tc(cudaStream_t st, const TcAttnArgs& a) {
     static PerDeviceOnce once;
     once([] {
-        cudaFuncSetAttribute(k_attn_tc<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PaPlan<D>::SMEM);
+        cudaFuncSetAttribute(k_attn_tc<D, CAUSAL, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)PaPlan<D>::SMEM);
     });
-    k_attn_tc<D, CAUSAL><<<dim3((a.L + PA_QT - 1) / PA_QT, a.n_head, 1), PA_THREADS, PaPlan<D>::SMEM, st>>>(a);
+    k_attn_tc<D, CAUSAL, TILED><<<dim3((a.L + PA_QT - 1) / PA_QT, a.n_head, 1), pa_threads(TILED), PaPlan<D>::SMEM,
+                                  st>>>(a);
 }
 
 void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
@@ -369,9 +403,9 @@ void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n
     a.out = out;
     a.out_stride = n_head * 128;
     a.err = err;
-    launch_tc<128, true>(st, a);
+    launch_tc<128, true, false>(st, a);
 }
 
-void launch_attention_full_tc(cudaStream_t st, const TcAttnArgs& a) { launch_tc<64, false>(st, a); }
+void launch_attention_full_tc(cudaStream_t st, const TcAttnArgs& a) { launch_tc<64, false, true>(st, a); }
 
 }  // namespace ocr

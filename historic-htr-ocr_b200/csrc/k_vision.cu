@@ -68,8 +68,21 @@ void launch_patchify(cudaStream_t st, const uint8_t* rgb, const Placement& pl, i
     k_patchify<<<blocks, 256, 0, st>>>(rgb, pl, patch, lut, K, n, px, x16);
 }
 
+// The attention's operands as they land in shared memory: per head, per tile of 64 keys, 8 KB of K (key row r, the
+// 16-byte piece p of its 64 dims at r * 128 + ((p ^ (r % 8)) << 4): K-major with the 128-byte swizzle) and 8 KB of V
+// transposed (dim row d, the piece q of keys 8q … 8q + 7 at d * 128 + ((q ^ (d % 8)) << 4)), so one bulk copy of a
+// tile is a tensor-core operand. Keys past n are zero.
+__device__ __forceinline__ size_t k_tiled(int h, int n_pad, int t, int d) {
+    const int r = t & 63;
+    return ((size_t)h * n_pad + (t & ~63)) * 64 + r * 64 + ((((d >> 3) ^ (r & 7))) << 3) + (d & 7);
+}
+__device__ __forceinline__ size_t vt_tiled(int h, int n_pad, int t, int d) {
+    const int j = t & 63;
+    return ((size_t)h * n_pad + (t & ~63)) * 64 + d * 64 + ((((j >> 3) ^ (d & 7))) << 3) + (j & 7);
+}
+
 // one thread per (row, head, rotation pair); the pair (2k, 2k + 1) of half `hf` (dims [0, d/2) by the patch row, [d/2,
-// d) by the patch column) rotated in q (in place) and k, k and v stored f16 head-major
+// d) by the patch column) rotated in q (in place) and k; k and v stored f16 in the attention's tiled layouts
 __global__ void __launch_bounds__(256) k_rope2d_heads(float* __restrict__ qkv, int n, int n_head, int d_head, int px,
                                                       const float* __restrict__ cs, int max_pos,
                                                       __half* __restrict__ kh, __half* __restrict__ vh, int n_pad) {
@@ -78,11 +91,12 @@ __global__ void __launch_bounds__(256) k_rope2d_heads(float* __restrict__ qkv, i
     for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
         const int j = (int)(e % pairs), h = (int)((e / pairs) % n_head), t = (int)(e / ((long)pairs * n_head));
         const int hf = j / nk, k = j % nk, o = hf * (d_head / 2) + 2 * k;
-        __half2* kd = reinterpret_cast<__half2*>(kh + ((size_t)h * n_pad + t) * d_head + o);
-        __half2* vd = reinterpret_cast<__half2*>(vh + ((size_t)h * n_pad + t) * d_head + o);
+        __half2* kd = reinterpret_cast<__half2*>(kh + k_tiled(h, n_pad, t, o));
+        __half* v0 = vh + vt_tiled(h, n_pad, t, o);
+        __half* v1 = vh + vt_tiled(h, n_pad, t, o + 1);
         if (t >= n) {
             *kd = __floats2half2_rn(0.0f, 0.0f);
-            *vd = __floats2half2_rn(0.0f, 0.0f);
+            *v0 = *v1 = __float2half_rn(0.0f);
             continue;
         }
         const int pos = hf == 0 ? t / px : t % px;
@@ -93,7 +107,8 @@ __global__ void __launch_bounds__(256) k_rope2d_heads(float* __restrict__ qkv, i
         row[1] = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
         const float k0 = row[dim], k1 = row[dim + 1];
         *kd = __floats2half2_rn(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s)), __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c)));
-        *vd = __floats2half2_rn(row[2 * dim], row[2 * dim + 1]);
+        *v0 = __float2half_rn(row[2 * dim]);
+        *v1 = __float2half_rn(row[2 * dim + 1]);
     }
 }
 

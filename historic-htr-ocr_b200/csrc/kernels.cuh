@@ -370,7 +370,8 @@ struct TcAttnArgs {
     int out16_K = 0;
     int* err = nullptr;
 };
-// the full attention of head dim 64 (the vision encoder)
+// the full attention of head dim 64 (the vision encoder) over k / v in the tiled layouts launch_rope2d_heads writes
+// (kv_head_stride = n_pad * 64): each 64-key tile of K and of V^T one bulk copy, two CTAs per SM
 void launch_attention_full_tc(cudaStream_t st, const TcAttnArgs& a);
 
 // ---- the vision encoder's own kernels (k_vision.cu) --------------------------------------------------------------------
@@ -383,8 +384,9 @@ struct Placement {
 // t = ty * px + tx, column c * p² + ky * p + kx = lut[c][pixel(tx * p + kx, ty * p + ky)[c]], columns past 3 p² zero
 void launch_patchify(cudaStream_t st, const uint8_t* rgb, const Placement& pl, int patch, const float* lut, int K,
                      uint8_t* x16);
-// the q and k parts of qkv rows [n][3 * dim] rotated by the 2D RoPE (in place for q); k and v written f16
-// head-major: kh[h][n_pad][d_head], vh likewise (rows past n zero)
+// the q and k parts of qkv rows [n][3 * dim] rotated by the 2D RoPE (in place for q); k and v written f16 per head
+// in tiles of 64 keys already in the attention's operand layouts (K: key rows, V: transposed, both K-major with the
+// 128-byte swizzle; d_head 64; keys past n zero): head h's tiles at kh + h * n_pad * 64, each 64 * 64 halves
 void launch_rope2d_heads(cudaStream_t st, float* qkv, int n, int n_head, int d_head, int px, const float* cs,
                          int max_pos, __half* kh, __half* vh, int n_pad);
 // the projector's input: x [n][dim] RMS-normalised by w, 2x2-unfolded (merged token o = oy * px/2 + ox gets column
