@@ -32,6 +32,7 @@ constexpr int PA_THREADS = (5 + PA_LOADERS) * 32;
 constexpr int PA_THREADS_TILED = 6 * 32;
 __host__ __device__ constexpr int pa_threads(bool tiled) { return tiled ? PA_THREADS_TILED : PA_THREADS; }
 constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128 … 128 + D
+constexpr float PA_RESCALE = 8.0f;      // the one-pass form's headroom over the running maximum (log2 units)
 // the shared-memory plan of head dim D: Q hi / lo, two K tiles, two V tiles (transposed), P hi / lo
 template <int D>
 struct PaPlan {
@@ -74,8 +75,9 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
     constexpr int THREADS = pa_threads(TILED);
     static_assert(!TILED || D == 64, "the pre-tiled operands are written for head dim 64");
     using P = PaPlan<D>;
-    const int L = a.L, n_head = a.n_head, pos0 = a.pos0;
-    const float scale = a.scale;
+    const int L = a.L, pos0 = a.pos0;
+    // the tiled form works in log2 units (scores times log2 e, probabilities by exp2)
+    const float qscale = TILED ? a.scale * 1.4426950408889634f : a.scale;
     int* err = a.err;
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(8) PaShared sh;
@@ -123,8 +125,8 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
         if (q0 + r < L) {
             const float4* src = reinterpret_cast<const float4*>(a.q + (size_t)(q0 + r) * a.q_stride + h * D + pc * 8);
             const float4 a0 = src[0], a1 = src[1];
-            const float v[8] = {a0.x * scale, a0.y * scale, a0.z * scale, a0.w * scale,
-                                a1.x * scale, a1.y * scale, a1.z * scale, a1.w * scale};
+            const float v[8] = {a0.x * qscale, a0.y * qscale, a0.z * qscale, a0.w * qscale,
+                                a1.x * qscale, a1.y * qscale, a1.z * qscale, a1.w * qscale};
             float vh[8];
 #pragma unroll
             for (int c = 0; c < 8; c++) vh[c] = __half2float(__float2half_rn(v[c]));
@@ -143,22 +145,20 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
     const uint32_t tS = tmem, tO = tmem + 128;
 
     if (TILED && warp == 5) {
-        // ---- the copies: pass 1 the K tiles; pass 2 each tile's K, then its V^T (one bulk copy each) ----
+        // ---- the copies: each tile's K, then its V^T (one bulk copy each) ----
         if (lane == 0) {
             bool ok = true;
             uint32_t kn[2] = {0u, 0u}, vn[2] = {0u, 0u};  // copies issued per ring slot
-            for (int seq = 0; seq < 2 * T && ok; seq++) {
-                const int t = seq < T ? seq : seq - T, ks = seq & 1;
-                if (seq >= 2 && !(ok = pa_wait(&sh.kempty[ks], ((seq >> 1) - 1) & 1, abort_flag, err))) break;
+            for (int t = 0; t < T && ok; t++) {  // each tile's K, then its V^T (one pass)
+                const int ks = t & 1;
+                if (t >= 2 && !(ok = pa_wait(&sh.kempty[ks], ((t >> 1) - 1) & 1, abort_flag, err))) break;
                 mbar_expect_tx(&sh.kfull[ks], P::K_BYTES);
                 bulk_g2s(Kr + ks * P::K_BYTES, kbase + (size_t)t * PA_KT * D, P::K_BYTES, &sh.kfull[ks]);
                 kn[ks]++;
-                if (seq < T) continue;
-                const int vs = t & 1;
-                if (t >= 2 && !(ok = pa_wait(&sh.vempty[vs], ((t >> 1) - 1) & 1, abort_flag, err))) break;
-                mbar_expect_tx(&sh.vfull[vs], P::V_BYTES);
-                bulk_g2s(Vr + vs * P::V_BYTES, vbase + (size_t)t * PA_KT * D, P::V_BYTES, &sh.vfull[vs]);
-                vn[vs]++;
+                if (t >= 2 && !(ok = pa_wait(&sh.vempty[ks], ((t >> 1) - 1) & 1, abort_flag, err))) break;
+                mbar_expect_tx(&sh.vfull[ks], P::V_BYTES);
+                bulk_g2s(Vr + ks * P::V_BYTES, vbase + (size_t)t * PA_KT * D, P::V_BYTES, &sh.vfull[ks]);
+                vn[ks]++;
             }
             if (!ok) *abort_flag = 1;
             // every copy landed before the shared memory is given back (bounded; the last phase of each slot)
@@ -251,10 +251,14 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                 any = true;
                 return true;
             };
-            for (int t = 0; t < T && ok; t++) ok = qk(t, t);
-            if (ok) ok = qk(T, T);
+            // two passes (the row maxima, then P V): S of sequence number T + t is tile t's second product; the tiled
+            // form makes one pass (sequence t = tile t)
+            const int s0 = TILED ? 0 : T;
+            if constexpr (!TILED)
+                for (int t = 0; t < T && ok; t++) ok = qk(t, t);
+            if (ok) ok = qk(s0, s0);
             for (int t = 0; t < T && ok; t++) {
-                if (t + 1 < T && !(ok = qk(T + t + 1, T + t + 1))) break;  // the next tile's S while the rows read this
+                if (t + 1 < T && !(ok = qk(s0 + t + 1, s0 + t + 1))) break;  // the next tile's S while the rows read this
                 const int vs = t & 1;
                 if (!pa_wait(&sh.pfull, t & 1, abort_flag, err) ||
                     !pa_wait(&sh.vfull[vs], (t >> 1) & 1, abort_flag, err)) {
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
 #pragma unroll
                 for (int k = 0; k < PA_KT / 16; k++) {
                     mma_f16(tO, bg_desc(ph + k * 32), bg_desc(vt + k * 32), idO, (t > 0 || k > 0) ? 1u : 0u);
-                    mma_f16(tO, bg_desc(pl + k * 32), bg_desc(vt + k * 32), idO, 1u);
+                    if constexpr (!TILED) mma_f16(tO, bg_desc(pl + k * 32), bg_desc(vt + k * 32), idO, 1u);
                 }
                 mma_commit(&sh.pfree);
                 mma_commit(&sh.vempty[vs]);
@@ -297,13 +301,68 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
             if (lane == 0) mbar_arrive(&sh.sfree[sb]);
             return true;
         };
-        for (int t = 0; t < T && ok; t++) {
+        if constexpr (TILED) {
+            // one pass, online: m is the running maximum (log2 units); a tile whose maximum exceeds it by more than
+            // PA_RESCALE rescales l and the row of O (after the previous P V completes) — otherwise p = 2^(s - m)
+            // <= 2^PA_RESCALE stays in f16's range. P is rounded to f16 (the reference's f16 path rounds P so).
+            for (int t = 0; t < T && ok; t++) {
+                if (!(ok = read_s(t))) break;
+                float mt = -INFINITY;
+                const bool edge = (t + 1) * PA_KT > n_keys;  // the last tile may hold keys past n_keys
+#pragma unroll
+                for (int j = 0; j < PA_KT; j++)
+                    if (!edge || t * PA_KT + j < n_keys) mt = fmaxf(mt, __uint_as_float(sv[j]));
+                bool waited = false;
+                if (t == 0) {
+                    m = mt;
+                } else if (mt > m + PA_RESCALE) {
+                    if (!(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;  // P V of t - 1 done
+                    waited = true;
+                    const float f = exp2f(m - mt);
+                    l *= f;
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < D / 16; c++) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + lane_base + c * 16, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int d = 0; d < 16; d++) o[d] = __float_as_uint(__uint_as_float(o[d]) * f);
+                        tmem_st16(tO + lane_base + c * 16, o);
+                    }
+                    tmem_wait_st();
+                    m = mt;
+                }
+                uint32_t pk[PA_KT / 2];
+#pragma unroll
+                for (int j = 0; j < PA_KT; j += 2) {
+                    float p0 = exp2f(__uint_as_float(sv[j]) - m), p1 = exp2f(__uint_as_float(sv[j + 1]) - m);
+                    if (edge) {
+                        if (t * PA_KT + j >= n_keys) p0 = 0.0f;
+                        if (t * PA_KT + j + 1 >= n_keys) p1 = 0.0f;
+                    }
+                    l += p0;
+                    l += p1;
+                    pk[j >> 1] = pack_h2(p0, p1);
+                }
+                if (t >= 1 && !waited && !(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;
+#pragma unroll
+                for (int p = 0; p < PA_KT / 8; p++)
+                    *reinterpret_cast<uint4*>(Ph + sw128(tid, p)) =
+                        make_uint4(pk[4 * p], pk[4 * p + 1], pk[4 * p + 2], pk[4 * p + 3]);
+                tc_fence_before();    // (the rescaled O, before the tensor cores accumulate into it)
+                fence_proxy_async();  // the generic stores, before the tensor cores read them
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.pfull);
+            }
+        }
+        for (int t = 0; t < T && ok && !TILED; t++) {
             if (!(ok = read_s(t))) break;
 #pragma unroll
             for (int j = 0; j < PA_KT; j++)
                 if (CAUSAL ? t * PA_KT + j <= qpos : t * PA_KT + j < n_keys) m = fmaxf(m, __uint_as_float(sv[j]));
         }
-        for (int t = 0; t < T && ok; t++) {
+        for (int t = 0; t < T && ok && !TILED; t++) {
             if (!(ok = read_s(T + t))) break;
             if (t >= 1 && !(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;  // P·V of t - 1 done
 #pragma unroll

@@ -480,4 +480,31 @@ ocr_status ocr_vision_encode_page(ocr_vision* v, const uint8_t* rgb, int w0, int
     return encode(v, rgb, pl, -1, out, cap, n_rows, nullptr);
 }
 
+ocr_status ocr_op_attention_full(ocr_ctx* ctx, const float* d_q, int q_stride, int L, int n_head,
+                                 const uint16_t* d_k_tiled, const uint16_t* d_vt_tiled, int n_pad, int n_keys,
+                                 float scale, float* d_out, int out_stride) {
+    if (!ctx || !d_q || !d_k_tiled || !d_vt_tiled || !d_out) return fail(OCR_ERR_ARG, "null argument");
+    if (L <= 0 || n_head <= 0 || n_keys <= 0 || n_pad % 64 || n_keys > n_pad || q_stride < n_head * 64 ||
+        out_stride < n_head * 64)
+        return fail(OCR_ERR_ARG, "attention shape out of range");
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    TcAttnArgs a;
+    a.q = d_q;
+    a.q_stride = q_stride;
+    a.L = L;
+    a.n_head = n_head;
+    a.group = 1;
+    a.k = reinterpret_cast<const __half*>(d_k_tiled);
+    a.v = reinterpret_cast<const __half*>(d_vt_tiled);
+    a.kv_head_stride = (size_t)n_pad * 64;
+    a.n_keys = n_keys;
+    a.scale = scale;
+    a.out = d_out;
+    a.out_stride = out_stride;
+    a.err = ctx->d_err;
+    launch_attention_full_tc(ctx->stream, a);
+    OCR_CUDA(cudaGetLastError());
+    return OCR_OK;
+}
+
 }  // extern "C"

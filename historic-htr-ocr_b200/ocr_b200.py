@@ -132,6 +132,8 @@ _SIGS = {
     "ocr_op_lm_head_sample_noalloc": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, _P, C.c_float, C.c_float, C.c_int, _P,
                                                 _P, _P, _P]),
     "ocr_op_wait_probe": (C.c_int, [_P, C.c_int, C.POINTER(C.c_int)]),
+    "ocr_op_attention_full": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P, _P, C.c_int, C.c_int, C.c_float, _P,
+                                        C.c_int]),
     "ocr_op_attention_decode": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                           _P]),
 }
@@ -707,6 +709,34 @@ def op_lm_head_sample_noalloc(ctx: Context, d_w: int, n_vocab: int, dim: int, d_
     """op_lm_head_sample with its scratch in a static device array: the call allocates no device memory"""
     _check(lib().ocr_op_lm_head_sample_noalloc(ctx.h, d_w, n_vocab, dim, d_x, d_norm_w, eps, rp, window, d_hist, d_len,
                                                d_tok, d_logits))
+
+
+def op_attention_full(ctx: Context, d_q: int, q_stride: int, L: int, n_head: int, d_k_tiled: int, d_vt_tiled: int,
+                      n_pad: int, n_keys: int, scale: float, d_out: int, out_stride: int) -> None:
+    _check(lib().ocr_op_attention_full(ctx.h, d_q, q_stride, L, n_head, d_k_tiled, d_vt_tiled, n_pad, n_keys, scale,
+                                       d_out, out_stride))
+
+
+def attention_tiles(k: np.ndarray, v: np.ndarray, n_pad: int) -> tuple[np.ndarray, np.ndarray]:
+    """K and V [n_head][n][64] (f16) → the vision attention's tiled layouts (ocr_op_attention_full), as uint16"""
+    H, n, D = k.shape
+    kt = np.zeros((H, n_pad // 64, 64, 64), np.float16)
+    vt = np.zeros((H, n_pad // 64, 64, 64), np.float16)
+    r = np.arange(64)
+    for t0 in range(0, n, 64):
+        m = min(64, n - t0)
+        kb = np.zeros((H, 64, 64), np.float16)
+        vb = np.zeros((H, 64, 64), np.float16)
+        kb[:, :m] = k[:, t0:t0 + m]
+        vb[:, :m] = v[:, t0:t0 + m]
+        for p in range(8):  # key row r, dims 8p … 8p + 7 → piece p ^ (r % 8)
+            dst = ((p ^ (r & 7)) * 8)[:, None] + np.arange(8)[None, :]
+            kt[:, t0 // 64, r[:, None], dst] = kb[:, :, 8 * p:8 * p + 8]
+        vtb = vb.transpose(0, 2, 1)  # [H][dim][key]
+        for q in range(8):  # dim row d, keys 8q … 8q + 7 → piece q ^ (d % 8)
+            dst = ((q ^ (r & 7)) * 8)[:, None] + np.arange(8)[None, :]
+            vt[:, t0 // 64, r[:, None], dst] = vtb[:, :, 8 * q:8 * q + 8]
+    return kt.view(np.uint16), vt.view(np.uint16)
 
 
 def op_wait_probe(ctx: Context, tries: int) -> bool:

@@ -293,6 +293,16 @@ ocr_status ocr_op_attention_decode(ocr_ctx* ctx, float* d_qkv, const float* d_q_
  * about 1 µs: *waited_out = 1 when it gave up. The context's error flag stays set — the next ocr_ctx_sync returns
  * OCR_ERR_DEVICE and clears it; the context stays usable. Synchronous. */
 ocr_status ocr_op_wait_probe(ocr_ctx* ctx, int tries, int* waited_out);
+/* The vision encoder's attention alone (test entry point; the reference's attention_coop.wgsl, vision.rs:290-295):
+ * softmax(q k^T * scale) v over keys 0 … n_keys - 1 for L query rows of n_head heads of 64 (q row r, head h at
+ * d_q[r * q_stride + h * 64], f32), the keys and values f16 per head in the tiled layout the encoder's RoPE kernel
+ * writes (n_pad a multiple of 64; head h's tiles at h * n_pad * 64 halves; per 64-key tile, K row r's 16-byte
+ * piece p at r * 128 + ((p ^ (r % 8)) << 4) bytes, V transposed: dim row d's piece q of keys 8q … 8q + 7 at
+ * d * 128 + ((q ^ (d % 8)) << 4); keys past n_keys zero) → d_out[r * out_stride + h * 64] f32. Queued on the
+ * context's stream. */
+ocr_status ocr_op_attention_full(ocr_ctx* ctx, const float* d_q, int q_stride, int L, int n_head,
+                                 const uint16_t* d_k_tiled, const uint16_t* d_vt_tiled, int n_pad, int n_keys,
+                                 float scale, float* d_out, int out_stride);
 
 #ifdef __cplusplus
 }

@@ -132,3 +132,35 @@ def test_page_read_end_to_end_small(ocr, orc, ctx, torch_cuda):
     s.close()
     m.close()
     v.close()
+
+
+@pytest.mark.parametrize("n_keys,L,step", [(300, 200, 0.0), (1000, 130, 0.0), (300, 200, 6.0), (640, 129, 2.5)])
+def test_full_attention_op_matches_f64(ocr, ctx, torch_cuda, n_keys, L, step):
+    """ocr_op_attention_full against softmax(q k^T / 8) v in f64 on the same f16 K / V. `step` > 0 raises every
+    key tile's scores by step nats over the tile before (dimension 0 of q is 10, of K tile t is step * 8 t / 10), so
+    the one-pass softmax's running maximum jumps past its headroom (8 in log2 units, 5.5 nats) and rescales O and
+    the row sums at every tile (step 6), or at some tiles (step 2.5)."""
+    torch = torch_cuda
+    H, D = 2, 64
+    rng = np.random.default_rng(n_keys + L)
+    q = rng.standard_normal((L, H, D)).astype(np.float32)
+    k = rng.standard_normal((H, n_keys, D)).astype(np.float16)
+    v = rng.standard_normal((H, n_keys, D)).astype(np.float16)
+    if step:
+        q[:, :, 0] = 10.0
+        k[:, :, 0] = (step * 8.0 / 10.0 * (np.arange(n_keys) // 64)).astype(np.float16)
+    n_pad = (n_keys + 63) // 64 * 64
+    kt, vt = ocr.attention_tiles(k, v, n_pad)
+    dq = torch.from_numpy(q.reshape(L, H * D)).cuda()
+    dk = torch.from_numpy(kt.reshape(-1).view(np.int16)).cuda()
+    dv = torch.from_numpy(vt.reshape(-1).view(np.int16)).cuda()
+    out = torch.zeros((L, H * D), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    ocr.op_attention_full(ctx, dq.data_ptr(), H * D, L, H, dk.data_ptr(), dv.data_ptr(), n_pad, n_keys, 0.125,
+                          out.data_ptr(), H * D)
+    ctx.sync()
+    got = out.cpu().numpy().reshape(L, H, D)
+    s = np.einsum("lhd,hnd->lhn", q.astype(np.float64), k.astype(np.float64)) * 0.125
+    p = np.exp(s - s.max(axis=2, keepdims=True))
+    want = np.einsum("lhn,hnd->lhd", p / p.sum(axis=2, keepdims=True), v.astype(np.float64))
+    close(got, want.astype(np.float32))
