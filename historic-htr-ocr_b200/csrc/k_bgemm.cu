@@ -122,12 +122,18 @@ __device__ __forceinline__ BgItem bg_item(int w, int ksplit, int nkc) {
 // NG: groups of 32 slots (rows of the activations) per CTA. Two for long prefills: each dequantised weight piece
 // then feeds the MMAs of both groups (2 accumulator sets each), halving the dequantisation per row; one item per CTA
 // pass, no split-K (the host picks it only for unsplit launches over more than one group).
+// Three ("merged", for thousands of rows: the vision encoder): the three groups' activation halves land side by side
+// in the stage (64 columns: g0 hi, g0 lo, g1 hi, … — 192 rows of 128 bytes), so one K step is two MMAs of N = 192,
+// A = w_hi then A = w_lo into the same accumulator (w x_hi and w x_lo per group: the w_lo x_lo term, below 2^-22 of
+// the product, is kept rather than dropped), over two accumulator sets of 192 columns.
 template <int MODE, bool XN, int NG = 1>
 __global__ void __launch_bounds__(BG_THREADS, 1)
     k_bgemm(const __grid_constant__ BgArgs a, const uint8_t* __restrict__ wtiles, int ns, int na) {
-    static_assert(NG == 1 || (NG == 2 && !XN && MODE != MV_LMHEAD), "two groups: plain operands, no LM head");
+    static_assert(NG == 1 || (NG <= 3 && !XN && MODE != MV_LMHEAD), "several groups: plain operands, no LM head");
+    constexpr bool MERGED = NG == 3;
     constexpr uint32_t STAGE = BG_WTILE + NG * BG_CHUNK_BYTES;  // weights + each group's activation chunk
-    constexpr int NSET = BG_NACC / NG;                             // accumulator sets per group
+    constexpr int NSET = MERGED ? 2 : BG_NACC / NG;                // accumulator sets (per group, unless merged)
+    constexpr uint32_t MSET = 64u * NG;                            // a merged set's columns
     extern __shared__ uint8_t sm_raw[];
     __shared__ __align__(16) BgShared sh;
     volatile int* abort_flag = &sh.abort_flag;
@@ -220,10 +226,17 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                 if (XN) continue;  // (the operand is built by warps 2-17)
                 if (lane == 0) mbar_expect_tx(&sh.xfull[s], (uint32_t)ngr * BG_CHUNK_BYTES);
                 __syncwarp();
-                for (int gi = 0; gi < ngr; gi++)
-                    bulk_g2s_lanes(st + BG_WTILE + gi * BG_CHUNK_BYTES,
-                                   xg + ((size_t)gi * nkc + kc) * BG_CHUNK_BYTES, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
-                                   lane, 32);
+                for (int gi = 0; gi < ngr; gi++) {
+                    const uint8_t* src = xg + ((size_t)gi * nkc + kc) * BG_CHUNK_BYTES;
+                    if (MERGED) {  // half h of group gi at h x (NG x 8 KB) + gi x 8 KB
+                        for (int h = 0; h < 2; h++)
+                            bulk_g2s_lanes(st + BG_WTILE + h * (NG * 8192) + gi * 8192, src + h * 8192, 8192,
+                                           &sh.xfull[s], 0ull, lane, 32);
+                    } else {
+                        bulk_g2s_lanes(st + BG_WTILE + gi * BG_CHUNK_BYTES, src, BG_CHUNK_BYTES, &sh.xfull[s], 0ull,
+                                       lane, 32);
+                    }
+                }
             }
         }
         // every copy issued lands before the CTA can exit (in a normal run these phases are long complete): the
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
     } else if (warp == 1) {
         // ---- the tensor cores ----
         if (lane == 0) {
-            const uint32_t id1 = bg_idesc(64), id2 = bg_idesc(32);
+            const uint32_t id1 = bg_idesc(64), id2 = bg_idesc(32), idm = bg_idesc((int)MSET);
             uint32_t g = 0, ai = 0;
             bool any = false, ok = true;
             for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
@@ -271,6 +284,13 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                             // (its activation chunk gi x 16 KB into the stage) owns sets gi x NSET …
                             const int kstep = kstep0 + h * (BG_KS / 16) + ks;
                             const uint32_t acc = kstep >= NSET ? 1u : 0u;
+                            if constexpr (MERGED) {
+                                const uint64_t db = bg_desc(xs + h * (NG * 8192) + ks * 32);
+                                const uint32_t dset = tmem + (uint32_t)(kstep % NSET) * MSET;
+                                mma_f16(dset, dh, db, idm, acc);
+                                mma_f16(dset, dl, db, idm, 1u);
+                                continue;
+                            }
 #pragma unroll
                             for (int gi = 0; gi < NG; gi++) {
                                 if (gi >= ngr) break;
@@ -431,6 +451,17 @@ __global__ void __launch_bounds__(BG_THREADS, 1)
                     if (ok) {
 #pragma unroll
                         for (int st = 0; st < NSET; st++) {
+                            if constexpr (MERGED) {  // group gi: w x_hi in columns gi x 64 …, w x_lo 32 further
+                                uint32_t rh[8], rl[8];
+                                const uint32_t ta =
+                                    tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)st * MSET + (uint32_t)gi * 64;
+                                tmem_ld8(ta + 8 * part, rh);
+                                tmem_ld8(ta + 32 + 8 * part, rl);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 8; j++) y[j] += __uint_as_float(rh[j]) + __uint_as_float(rl[j]);
+                                continue;
+                            }
                             uint32_t rh[8], rl[8], rw[8];
                             const uint32_t ta =
                                 tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(gi * NSET + st) * BG_SET_COLS;
@@ -796,6 +827,11 @@ void launch_tile_q8_0(cudaStream_t st, const QMat& w, uint8_t* out) {
 // the instances launched: (mode, operand built in the kernel)
 using BgKernel = void (*)(BgArgs, const uint8_t*, int, int);
 static BgKernel bg_kernel(int mode, bool xn, int ng) {
+    if (ng == 3) {
+        if (xn) return nullptr;
+        return mode == MV_ADD ? k_bgemm<MV_ADD, false, 3> : mode == MV_SWIGLU ? k_bgemm<MV_SWIGLU, false, 3>
+             : mode == MV_STORE ? k_bgemm<MV_STORE, false, 3> : nullptr;
+    }
     if (ng == 2) {
         if (xn) return nullptr;
         return mode == MV_ADD ? k_bgemm<MV_ADD, false, 2> : mode == MV_SWIGLU ? k_bgemm<MV_SWIGLU, false, 2>
@@ -810,7 +846,8 @@ static BgKernel bg_kernel(int mode, bool xn, int ng) {
 }
 static const BgKernel BG_ALL[] = {k_bgemm<MV_STORE, false>,    k_bgemm<MV_STORE, true>,     k_bgemm<MV_ADD, false>,
                                   k_bgemm<MV_SWIGLU, false>,   k_bgemm<MV_SWIGLU, true>,    k_bgemm<MV_LMHEAD, false>,
-                                  k_bgemm<MV_STORE, false, 2>, k_bgemm<MV_ADD, false, 2>, k_bgemm<MV_SWIGLU, false, 2>};
+                                  k_bgemm<MV_STORE, false, 2>, k_bgemm<MV_ADD, false, 2>, k_bgemm<MV_SWIGLU, false, 2>,
+                                  k_bgemm<MV_STORE, false, 3>, k_bgemm<MV_ADD, false, 3>, k_bgemm<MV_SWIGLU, false, 3>};
 
 // the largest static shared memory of the instances (the dynamic budget is sized against it)
 static int bg_static_smem() {
@@ -852,7 +889,8 @@ void launch_bgemm(cudaStream_t st, const BgArgs& a, const BgMaps& m, int num_sms
     // two groups of 32 rows per CTA for unsplit launches over more than one group (the long prefill): each weight
     // piece dequantised once for both
     const int groups = (a.nb + BG_SLOTS - 1) / BG_SLOTS;
-    const int ng = (a.ksplit == 1 && !a.xn && a.mode != MV_LMHEAD && groups >= 2) ? 2 : 1;
+    const bool multi = a.ksplit == 1 && !a.xn && a.mode != MV_LMHEAD;
+    const int ng = (multi && a.wide && groups >= 3) ? 3 : (multi && groups >= 2) ? 2 : 1;
     int ns, na, fixed;
     bg_ring(ns, na, fixed, ng);
     cudaLaunchConfig_t cfg = {};

@@ -172,6 +172,65 @@ void launch_unfold_prep(cudaStream_t st, const float* x, const float* w, float e
     k_unfold_prep<<<(n_out + BG_SLOTS - 1) / BG_SLOTS * BG_SLOTS, UP_THREADS, 0, st>>>(x, w, eps, px, n_out, dim, x16);
 }
 
+// ---- the bake's Lanczos-3 resize (imageops::resize of the `image` crate 0.25, Lanczos3): separable, a vertical pass
+// into f32, then a horizontal pass into bytes. The taps and their normalised weights per output row / column come from
+// the host (the same f32 arithmetic as the CPU restatement); every sum runs tap by tap in order, each product rounded
+// before the add (no fused multiply-add), as the reference's Rust evaluates it.
+__global__ void __launch_bounds__(256) k_resize_v(const uint8_t* __restrict__ rgb, int w0, int h, const int* __restrict__ left,
+                                                  const int* __restrict__ cnt, const float* __restrict__ wt, int maxn,
+                                                  float* __restrict__ tmp) {
+    const long total = (long)h * w0 * 3;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+        const int y = (int)(e / ((long)w0 * 3)), xc = (int)(e % ((long)w0 * 3));
+        const int l = left[y], n = cnt[y];
+        const float* w = wt + (size_t)y * maxn;
+        float t = 0.0f;
+        for (int i = 0; i < n; i++) t = __fadd_rn(t, __fmul_rn((float)rgb[(size_t)(l + i) * w0 * 3 + xc], w[i]));
+        tmp[e] = t;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_resize_h(const float* __restrict__ tmp, int w0, int h, int w,
+                                                  const int* __restrict__ left, const int* __restrict__ cnt,
+                                                  const float* __restrict__ wt, int maxn, uint8_t* __restrict__ out) {
+    const long total = (long)h * w * 3;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+        const int c = (int)(e % 3), x = (int)((e / 3) % w), y = (int)(e / (3L * w));
+        const int l = left[x], n = cnt[x];
+        const float* ww = wt + (size_t)x * maxn;
+        const float* row = tmp + (size_t)y * w0 * 3 + c;
+        float t = 0.0f;
+        for (int i = 0; i < n; i++) t = __fadd_rn(t, __fmul_rn(row[(size_t)(l + i) * 3], ww[i]));
+        t = fminf(fmaxf(t, 0.0f), 255.0f);
+        out[e] = (uint8_t)roundf(t);  // half away from zero, as Rust's f32::round
+    }
+}
+
+void launch_resize(cudaStream_t st, const uint8_t* rgb, int w0, int h0, int w, int h, const int* vleft,
+                   const int* vcnt, const float* vw, int vmax, const int* hleft, const int* hcnt, const float* hw,
+                   int hmax, float* tmp, uint8_t* out) {
+    (void)h0;
+    const long tv = (long)h * w0 * 3, th = (long)h * w * 3;
+    k_resize_v<<<(int)std::min<long>((tv + 255) / 256, 148L * 32), 256, 0, st>>>(rgb, w0, h, vleft, vcnt, vw, vmax, tmp);
+    k_resize_h<<<(int)std::min<long>((th + 255) / 256, 148L * 32), 256, 0, st>>>(tmp, w0, h, w, hleft, hcnt, hw, hmax, out);
+}
+
+// the baked canvas: the (scaled) image at (left, top) of a white fw x fh canvas
+__global__ void __launch_bounds__(256) k_bake_place(const uint8_t* __restrict__ src, int sw, int sh, int left, int top,
+                                                    int fw, int fh, uint8_t* __restrict__ out) {
+    const long total = (long)fw * fh * 3;
+    for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total; e += (long)gridDim.x * blockDim.x) {
+        const int c = (int)(e % 3), x = (int)((e / 3) % fw) - left, y = (int)(e / (3L * fw)) - top;
+        out[e] = (x >= 0 && x < sw && y >= 0 && y < sh) ? src[((size_t)y * sw + x) * 3 + c] : (uint8_t)255;
+    }
+}
+
+void launch_bake_place(cudaStream_t st, const uint8_t* src, int sw, int sh, int left, int top, int fw, int fh,
+                       uint8_t* out) {
+    const long total = (long)fw * fh * 3;
+    k_bake_place<<<(int)std::min<long>((total + 255) / 256, 148L * 32), 256, 0, st>>>(src, sw, sh, left, top, fw, fh, out);
+}
+
 // gelu.wgsl:22-26: 0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x²))), the tanh argument clamped to ±15
 __device__ __forceinline__ float gelu_tanh(float x) {
     float t = __fmul_rn(__fmul_rn(0.7978845608028654f, x), __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, x), x)));

@@ -263,6 +263,8 @@ struct BgArgs {
     float eps = 1e-6f;
     // MV_ADD: the new residual rows' sums of squares per 128-row tile, ssq_out [rows/128][B] (for the next norm)
     float* ssq_out = nullptr;
+    // thousands of rows (unsplit, plain operand): three groups of 32 per CTA, their operands merged into MMAs of N = 192
+    int wide = 0;
     int* err = nullptr;
     TlSlot* tl = nullptr;  // the in-chain timeline slot of this launch (null: not recorded)
 };
@@ -395,5 +397,13 @@ void launch_unfold_prep(cudaStream_t st, const float* x, const float* w, float e
                         uint8_t* x16);
 // rows [n][K] → GELU (tanh form) → x16 operand (act = 1), or the plain split (act = 0)
 void launch_act_prep(cudaStream_t st, const float* y, int n, int K, int act, uint8_t* x16);
+// the bake's Lanczos-3 resize, rgb [h0][w0][3] → out [h][w][3] through tmp [h][w0][3] f32: per output row y the taps
+// vleft[y] … + vcnt[y] - 1 with weights vw[y * vmax …], per output column x likewise (h…)
+void launch_resize(cudaStream_t st, const uint8_t* rgb, int w0, int h0, int w, int h, const int* vleft,
+                   const int* vcnt, const float* vw, int vmax, const int* hleft, const int* hcnt, const float* hw,
+                   int hmax, float* tmp, uint8_t* out);
+// src [sh][sw][3] placed at (left, top) of a white canvas [fh][fw][3]
+void launch_bake_place(cudaStream_t st, const uint8_t* src, int sw, int sh, int left, int top, int fw, int fh,
+                       uint8_t* out);
 
 }  // namespace ocr

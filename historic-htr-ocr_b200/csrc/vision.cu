@@ -212,6 +212,7 @@ ocr_status encode(ocr_vision* v, const uint8_t* rgb, const Placement& pl, int la
         g.y_stride = y_stride;
         g.y16 = y16;
         g.nb = nb;
+        g.wide = 1;
         g.err = ctx->d_err;
         launch_bgemm(st, g, bq, ctx->num_sms, false);
     };
@@ -274,6 +275,92 @@ ocr_status encode(ocr_vision* v, const uint8_t* rgb, const Placement& pl, int la
     OCR_TRY(check_device_error(ctx));
     if (n_rows) *n_rows = rows;
     if (row_width) *row_width = width;
+    return OCR_OK;
+}
+
+// the Lanczos-3 taps of a resize from n_in to n_out samples (imageops::resize, FilterType::Lanczos3, of the `image`
+// crate 0.25): for output o, ratio = in / out, sratio = max(ratio, 1), the centre (o + 0.5) ratio, taps [floor(centre
+// - 3 sratio), ceil(centre + 3 sratio)) clamped to the input, weights lanczos3((i - (centre - 0.5)) / sratio) divided
+// by their sum — all in f32 as the crate computes them. One row of max_n weights per output.
+struct Taps {
+    std::vector<int32_t> left, n;
+    std::vector<float> w;
+    int max_n = 0;
+};
+float sinc_f(float t) {
+    const float a = t * 3.14159265358979323846f;
+    return t == 0.0f ? 1.0f : sinf(a) / a;
+}
+float lanczos3(float x) { return fabsf(x) < 3.0f ? sinc_f(x) * sinc_f(x / 3.0f) : 0.0f; }
+Taps taps_for(int n_in, int n_out) {
+    Taps t;
+    const float ratio = (float)n_in / (float)n_out;
+    const float sratio = ratio < 1.0f ? 1.0f : ratio;
+    const float support = 3.0f * sratio;
+    std::vector<std::vector<float>> rows(n_out);
+    for (int o = 0; o < n_out; o++) {
+        float centre = ((float)o + 0.5f) * ratio;
+        long l = (long)floorf(centre - support), r = (long)ceilf(centre + support);
+        l = std::min(std::max(l, 0L), (long)n_in - 1);
+        r = std::min(std::max(r, l + 1), (long)n_in);
+        centre -= 0.5f;
+        std::vector<float>& w = rows[o];
+        float sum = 0.0f;
+        for (long i = l; i < r; i++) {
+            w.push_back(lanczos3(((float)i - centre) / sratio));
+            sum += w.back();
+        }
+        for (float& x : w) x /= sum;
+        t.left.push_back((int32_t)l);
+        t.n.push_back((int32_t)w.size());
+        t.max_n = std::max(t.max_n, (int)w.size());
+    }
+    t.w.assign((size_t)n_out * t.max_n, 0.0f);
+    for (int o = 0; o < n_out; o++) std::copy(rows[o].begin(), rows[o].end(), t.w.begin() + (size_t)o * t.max_n);
+    return t;
+}
+
+// The bake on the device (imageops.rs:318-323): rgb (host or device) [h0][w0][3] → the scaled image in `scaled`
+// (device, [p.scaled_h][p.scaled_w][3]; the input itself, copied, when the plan does not scale). Temporaries are
+// allocated for the call and freed before it returns (synchronous).
+ocr_status bake_scaled(ocr_ctx* ctx, const uint8_t* rgb, int w0, int h0, const ocr_bake_plan& p, uint8_t* scaled,
+                       bool rgb_dev) {
+    cudaStream_t st = ctx->stream;
+    const size_t in_bytes = (size_t)w0 * h0 * 3;
+    if (p.scaled_w == w0 && p.scaled_h == h0)
+        return cudaMemcpyAsync(scaled, rgb, in_bytes, cudaMemcpyDefault, st) == cudaSuccess
+                   ? OCR_OK
+                   : cuda_fail(cudaGetLastError(), "bake: copy");
+    const int w = p.scaled_w, h = p.scaled_h;
+    const Taps tv = taps_for(h0, h), th = taps_for(w0, w);
+    Plan pl;
+    const size_t o_in = pl.take(rgb_dev ? 16 : in_bytes), o_tmp = pl.take((size_t)h * w0 * 3 * 4);
+    const size_t o_vl = pl.take((size_t)h * 4), o_vn = pl.take((size_t)h * 4), o_vw = pl.take(tv.w.size() * 4);
+    const size_t o_hl = pl.take((size_t)w * 4), o_hn = pl.take((size_t)w * 4), o_hw = pl.take(th.w.size() * 4);
+    void* buf = nullptr;
+    OCR_CUDA(dalloc(&buf, pl.off, &ctx->mem_work));
+    uint8_t* b = (uint8_t*)buf;
+    cudaError_t e = cudaSuccess;
+    const uint8_t* d_rgb = rgb;
+    if (!rgb_dev) {
+        e = cudaMemcpyAsync(b + o_in, rgb, in_bytes, cudaMemcpyHostToDevice, st);
+        d_rgb = b + o_in;
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_vl, tv.left.data(), (size_t)h * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_vn, tv.n.data(), (size_t)h * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_vw, tv.w.data(), tv.w.size() * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_hl, th.left.data(), (size_t)w * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_hn, th.n.data(), (size_t)w * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b + o_hw, th.w.data(), th.w.size() * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) {
+        launch_resize(st, d_rgb, w0, h0, w, h, (const int*)(b + o_vl), (const int*)(b + o_vn),
+                      (const float*)(b + o_vw), tv.max_n, (const int*)(b + o_hl), (const int*)(b + o_hn),
+                      (const float*)(b + o_hw), th.max_n, (float*)(b + o_tmp), scaled);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    dfree(buf, pl.off, &ctx->mem_work);
+    if (e != cudaSuccess) return cuda_fail(e, "bake: resize");
     return OCR_OK;
 }
 
@@ -462,22 +549,60 @@ ocr_status ocr_vision_encode(ocr_vision* v, const uint8_t* rgb, int w, int h, in
 
 ocr_status ocr_vision_encode_page(ocr_vision* v, const uint8_t* rgb, int w0, int h0, float* out, size_t cap,
                                   int* n_rows) {
-    if (!v) return fail(OCR_ERR_ARG, "null encoder");
+    if (!v || !rgb) return fail(OCR_ERR_ARG, "null encoder or image");
     if (w0 <= 0 || h0 <= 0) return fail(OCR_ERR_ARG, "image sizes must be positive");
     ocr_bake_plan p;
     plan_for(v->cfg.image_size, v->cfg.patch * v->cfg.merge, w0, h0, &p);
-    if (p.scaled_w != w0 || p.scaled_h != h0)
-        return fail(OCR_ERR_ARG, "image " + std::to_string(w0) + "x" + std::to_string(h0) + ": its bake scales it to " +
-                                     std::to_string(p.scaled_w) + "x" + std::to_string(p.scaled_h) +
-                                     " (the resize is not built here; pass a baked image)");
     Placement pl;
-    pl.img_w = w0;
-    pl.img_h = h0;
+    pl.img_w = p.scaled_w;
+    pl.img_h = p.scaled_h;
     pl.left = p.left;
     pl.top = p.top;
-    pl.width = w0 + p.left + p.right;
-    pl.height = h0 + p.top + p.bottom;
-    return encode(v, rgb, pl, -1, out, cap, n_rows, nullptr);
+    pl.width = p.scaled_w + p.left + p.right;
+    pl.height = p.scaled_h + p.top + p.bottom;
+    if (p.scaled_w == w0 && p.scaled_h == h0) return encode(v, rgb, pl, -1, out, cap, n_rows, nullptr);
+    // the Lanczos-3 resize first (a device copy of the scaled page, for the call), then the pad inside the gather
+    ocr_ctx* ctx = v->ctx;
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    const size_t sbytes = (size_t)p.scaled_w * p.scaled_h * 3;
+    void* scaled = nullptr;
+    OCR_CUDA(dalloc(&scaled, sbytes, &ctx->mem_work));
+    ocr_status r = bake_scaled(ctx, rgb, w0, h0, p, (uint8_t*)scaled, is_device_ptr(rgb));
+    if (r == OCR_OK) r = encode(v, (const uint8_t*)scaled, pl, -1, out, cap, n_rows, nullptr);
+    dfree(scaled, sbytes, &ctx->mem_work);
+    return r;
+}
+
+ocr_status ocr_image_bake(ocr_ctx* ctx, const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out,
+                          size_t cap, int* out_w, int* out_h) {
+    if (!ctx || !rgb || !out) return fail(OCR_ERR_ARG, "null argument");
+    if (w0 <= 0 || h0 <= 0 || longest <= 0 || grid <= 0) return fail(OCR_ERR_ARG, "sizes must be positive");
+    ocr_bake_plan p;
+    plan_for(longest, grid, w0, h0, &p);
+    const int fw = p.scaled_w + p.left + p.right, fh = p.scaled_h + p.top + p.bottom;
+    if ((size_t)fw * fh * 3 > cap)
+        return fail(OCR_ERR_ARG, "output holds " + std::to_string(cap) + " bytes, the baked image " +
+                                     std::to_string((size_t)fw * fh * 3));
+    OCR_CUDA(cudaSetDevice(ctx->device));
+    const size_t sbytes = (size_t)p.scaled_w * p.scaled_h * 3, fbytes = (size_t)fw * fh * 3;
+    void* buf = nullptr;
+    OCR_CUDA(dalloc(&buf, sbytes + fbytes, &ctx->mem_work));
+    uint8_t* scaled = (uint8_t*)buf;
+    uint8_t* canvas = scaled + sbytes;
+    ocr_status r = bake_scaled(ctx, rgb, w0, h0, p, scaled, is_device_ptr(rgb));
+    if (r == OCR_OK) {
+        launch_bake_place(ctx->stream, scaled, p.scaled_w, p.scaled_h, p.left, p.top, fw, fh, canvas);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpyAsync(out, canvas, fbytes, cudaMemcpyDefault, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) r = cuda_fail(e, "ocr_image_bake");
+    }
+    dfree(buf, sbytes + fbytes, &ctx->mem_work);
+    if (r == OCR_OK) {
+        if (out_w) *out_w = fw;
+        if (out_h) *out_h = fh;
+    }
+    return r;
 }
 
 ocr_status ocr_op_attention_full(ocr_ctx* ctx, const float* d_q, int q_stride, int L, int n_head,

@@ -110,6 +110,8 @@ _SIGS = {
     "ocr_vision_encode": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(C.c_int),
                                     C.POINTER(C.c_int)]),
     "ocr_vision_encode_page": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(C.c_int)]),
+    "ocr_image_bake": (C.c_int, [_P, _P, C.c_int, C.c_int, C.c_int, C.c_int, _P, C.c_size_t, C.POINTER(C.c_int),
+                                 C.POINTER(C.c_int)]),
     "ocr_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_P)]),
     "ocr_gguf_open_memory": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
     "ocr_gguf_close": (C.c_int, [_P]),
@@ -363,6 +365,18 @@ def bake_plan(longest: int, grid: int, w0: int, h0: int) -> tuple:
     p = BakePlan()
     _check(lib().ocr_bake_plan_for(longest, grid, w0, h0, C.byref(p)))
     return (p.scaled_w, p.scaled_h, p.left, p.top, p.right, p.bottom)
+
+
+def image_bake(ctx: Context, rgb: np.ndarray, longest: int = 1540, grid: int = 28) -> np.ndarray:
+    """imageops::bake on the device: the Lanczos-3 resize when the plan scales, then the white pads"""
+    rgb = np.ascontiguousarray(rgb, np.uint8)
+    h0, w0 = rgb.shape[:2]
+    sw, sh, left, top, right, bottom = bake_plan(longest, grid, w0, h0)
+    out = np.empty((sh + top + bottom, sw + left + right, 3), np.uint8)
+    fw, fh = C.c_int(), C.c_int()
+    _check(lib().ocr_image_bake(ctx.h, _ptr(rgb), w0, h0, longest, grid, _ptr(out), out.nbytes, C.byref(fw),
+                                C.byref(fh)))
+    return out
 
 
 class Vision:

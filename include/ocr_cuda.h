@@ -219,12 +219,18 @@ ocr_status ocr_vision_config(const ocr_vision* v, ocr_vision_cfg* out);
  * the shape. Synchronous. */
 ocr_status ocr_vision_encode(ocr_vision* v, const uint8_t* rgb, int w, int h, int layers, float* out, size_t cap,
                              int* n_rows, int* row_width);
-/* The bake and the encode of a page in one call: rgb [h0][w0][3] of any size whose bake needs no resize (longest
- * edge <= image_size), placed per ocr_bake_plan_for(image_size, patch * merge, …) in its white canvas — the pad is
- * made inside the patch gather, no baked copy is formed — then encoded as ocr_vision_encode(layers = -1). A page
- * whose bake would resize it is refused with OCR_ERR_ARG. */
+/* The bake and the encode of a page in one call: rgb [h0][w0][3] of any size (host or device), scaled per
+ * ocr_bake_plan_for(image_size, patch * merge, …) on the device when its longest edge is above image_size (the
+ * bake's Lanczos-3 resize, as ocr_image_bake) and placed in its white canvas — the pad is made inside the patch
+ * gather, no baked copy is formed — then encoded as ocr_vision_encode(layers = -1). */
 ocr_status ocr_vision_encode_page(ocr_vision* v, const uint8_t* rgb, int w0, int h0, float* out, size_t cap,
                                   int* n_rows);
+/* imageops::bake (app/crates/ocr-core/src/imageops.rs:318-323) on the device: rgb [h0][w0][3] (host or device) →
+ * out [out_h][out_w][3] (host or device, cap bytes): the longest edge scaled down to `longest` with the Lanczos-3
+ * filter of imageops::resize (the `image` crate 0.25: separable, a vertical pass into f32 then a horizontal pass into
+ * bytes, rounded half away from zero), then white pads to the `grid` per the plan. Synchronous. */
+ocr_status ocr_image_bake(ocr_ctx* ctx, const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out,
+                          size_t cap, int* out_w, int* out_h);
 
 /* ---- GGUF reader, host only (ocr_gguf::Gguf, app/crates/ocr-gguf/src/lib.rs:213-509) ------------------------------ */
 typedef struct ocr_gguf ocr_gguf;

@@ -158,6 +158,12 @@ int orc_vision_layer1_rows(const orc_vision* v, const uint8_t* rgb, int w, int h
 void orc_bake_plan(int longest, int grid, int w0, int h0, int* out);
 /* the bake of an image that needs no resize: white pads per the plan; -1 when the plan resizes */
 int orc_bake_pad(const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out);
+/* the Lanczos-3 resampling taps of output index o (in → out samples): *left and the normalised weights; their count */
+int orc_resize_taps(int in, int out, int o, int* left, float* w, int cap);
+/* imageops::resize(.., Lanczos3) of the image crate 0.25: rgb [h0][w0][3] → out [h][w][3] */
+int orc_resize_lanczos3(const uint8_t* rgb, int w0, int h0, int w, int h, uint8_t* out);
+/* the whole bake (imageops.rs:318-323): the resize when the plan scales, then the white pads → [fh][fw][3] */
+int orc_bake(const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out);
 
 #ifdef __cplusplus
 }

@@ -77,6 +77,9 @@ _SIGS = {
     "orc_vision_layer1_rows": (C.c_int, [_P, _P, C.c_int, C.c_int, _P, C.c_int, _P]),
     "orc_bake_plan": (None, [C.c_int, C.c_int, C.c_int, C.c_int, _P]),
     "orc_bake_pad": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
+    "orc_resize_taps": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), _P, C.c_int]),
+    "orc_resize_lanczos3": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
+    "orc_bake": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P]),
 }
 
 _lib: Optional[C.CDLL] = None
@@ -385,4 +388,29 @@ def bake_pad(rgb: np.ndarray, longest: int = 1540, grid: int = 28) -> np.ndarray
     out = np.empty((sh + top + bottom, sw + left + right, 3), np.uint8)
     if lib().orc_bake_pad(_p(np.ascontiguousarray(rgb, np.uint8)), w0, h0, longest, grid, _p(out)) != 0:
         raise ValueError("the bake of this image resizes it")
+    return out
+
+
+def resize_lanczos3(rgb: np.ndarray, w: int, h: int) -> np.ndarray:
+    h0, w0 = rgb.shape[:2]
+    out = np.empty((h, w, 3), np.uint8)
+    if lib().orc_resize_lanczos3(_p(np.ascontiguousarray(rgb, np.uint8)), w0, h0, w, h, _p(out)) != 0:
+        raise ValueError("resize out of range")
+    return out
+
+
+def resize_taps(n_in: int, n_out: int, o: int) -> tuple[int, np.ndarray]:
+    w = np.empty(4096, np.float32)
+    left = C.c_int()
+    n = lib().orc_resize_taps(n_in, n_out, o, C.byref(left), _p(w), 4096)
+    return left.value, w[:n].copy()
+
+
+def bake(rgb: np.ndarray, longest: int = 1540, grid: int = 28) -> np.ndarray:
+    """the whole bake: the Lanczos-3 resize when the plan scales, then the white pads"""
+    h0, w0 = rgb.shape[:2]
+    sw, sh, left, top, right, bottom = bake_plan(longest, grid, w0, h0)
+    out = np.empty((sh + top + bottom, sw + left + right, 3), np.uint8)
+    if lib().orc_bake(_p(np.ascontiguousarray(rgb, np.uint8)), w0, h0, longest, grid, _p(out)) != 0:
+        raise ValueError("bake failed")
     return out

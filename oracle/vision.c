@@ -14,6 +14,12 @@
  *   - the projector: input_norm → 2×2 unfold → merger → mm.1 → GELU (tanh form, argument clamped ±15) → mm.2
  *                                                     vision.rs:405-423, shaders/unfold2x2.wgsl, shaders/gelu.wgsl
  *   - the bake's plan (longest edge, pads)            app/crates/ocr-core/src/imageops.rs:275-323 (plan)
+ *   - the bake's resize: imageops::resize(img, w, h, FilterType::Lanczos3) (imageops.rs:320) of the `image` crate,
+ *     pinned at 0.25.10 in app/Cargo.lock and not vendored: restated from that crate's published separable sampler —
+ *     a vertical pass to f32, then a horizontal pass to u8 (clamped to [0, 255], rounded half away from zero); per
+ *     output index o: ratio = in / out, sratio = max(ratio, 1), centre = (o + 0.5) ratio, taps [floor(centre - 3
+ *     sratio), ceil(centre + 3 sratio)) clamped to the image, weight lanczos3((i - (centre - 0.5)) / sratio)
+ *     normalised by their f32 sum, lanczos3(x) = sinc(x) sinc(x / 3) for |x| < 3, sinc(t) = sin(pi t) / (pi t)
  * Weights are q8_0 (config 4 asks q8_0; the reference loads bf16 / f32 vision weights): each matrix is a q8_0
  * matrix of the same shape, the patch embedding's 3·14·14 = 588 columns padded with zero columns to 768 (q8_0 needs
  * whole 32-blocks; the device contraction whole 256-column pieces). Accumulations are f64 (the order-free limit of
@@ -380,5 +386,83 @@ int orc_bake_pad(const uint8_t* rgb, int w0, int h0, int longest, int grid, uint
     const int fw = p[0] + p[2] + p[4], fh = p[1] + p[3] + p[5];
     memset(out, 255, (size_t)fw * fh * 3);
     for (int y = 0; y < h0; y++) memcpy(out + ((size_t)(y + p[3]) * fw + p[2]) * 3, rgb + (size_t)y * w0 * 3, (size_t)w0 * 3);
+    return 0;
+}
+
+/* ---- the bake's Lanczos-3 resize -------------------------------------------------------------------------------- */
+static float sinc_f(float t) {
+    const float a = t * 3.14159265358979323846f;
+    return t == 0.0f ? 1.0f : sinf(a) / a;
+}
+static float lanczos3(float x) { return fabsf(x) < 3.0f ? sinc_f(x) * sinc_f(x / 3.0f) : 0.0f; }
+
+int orc_resize_taps(int in, int out, int o, int* left, float* w, int cap) {
+    const float ratio = (float)in / (float)out;
+    const float sratio = ratio < 1.0f ? 1.0f : ratio;
+    const float support = 3.0f * sratio;
+    float centre = ((float)o + 0.5f) * ratio;
+    long l = (long)floorf(centre - support), r = (long)ceilf(centre + support);
+    if (l < 0) l = 0;
+    if (l > in - 1) l = in - 1;
+    if (r < l + 1) r = l + 1;
+    if (r > in) r = in;
+    centre -= 0.5f;
+    const int n = (int)(r - l);
+    if (n > cap) return -1;
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) {
+        w[i] = lanczos3(((float)(l + i) - centre) / sratio);
+        sum += w[i];
+    }
+    for (int i = 0; i < n; i++) w[i] /= sum;
+    *left = (int)l;
+    return n;
+}
+
+int orc_resize_lanczos3(const uint8_t* rgb, int w0, int h0, int w, int h, uint8_t* out) {
+    enum { CAP = 4096 };
+    float* tmp = (float*)malloc(sizeof(float) * (size_t)w0 * h * 3);
+    float* wt = (float*)malloc(sizeof(float) * CAP);
+    for (int y = 0; y < h; y++) { /* vertical: u8 → f32 [h][w0][3] */
+        int l, n = orc_resize_taps(h0, h, y, &l, wt, CAP);
+        if (n < 0) { free(tmp), free(wt); return -1; }
+        for (int x = 0; x < w0; x++)
+            for (int c = 0; c < 3; c++) {
+                float t = 0.0f;
+                for (int i = 0; i < n; i++) t += (float)rgb[((size_t)(l + i) * w0 + x) * 3 + c] * wt[i];
+                tmp[((size_t)y * w0 + x) * 3 + c] = t;
+            }
+    }
+    for (int x = 0; x < w; x++) { /* horizontal: f32 → u8 [h][w][3] */
+        int l, n = orc_resize_taps(w0, w, x, &l, wt, CAP);
+        if (n < 0) { free(tmp), free(wt); return -1; }
+        for (int y = 0; y < h; y++)
+            for (int c = 0; c < 3; c++) {
+                float t = 0.0f;
+                for (int i = 0; i < n; i++) t += tmp[((size_t)y * w0 + l + i) * 3 + c] * wt[i];
+                t = t < 0.0f ? 0.0f : (t > 255.0f ? 255.0f : t);
+                out[((size_t)y * w + x) * 3 + c] = (uint8_t)roundf(t);
+            }
+    }
+    free(tmp);
+    free(wt);
+    return 0;
+}
+
+int orc_bake(const uint8_t* rgb, int w0, int h0, int longest, int grid, uint8_t* out) {
+    int p[6];
+    orc_bake_plan(longest, grid, w0, h0, p);
+    const int fw = p[0] + p[2] + p[4], fh = p[1] + p[3] + p[5];
+    const uint8_t* src = rgb;
+    uint8_t* scaled = NULL;
+    if (p[0] != w0 || p[1] != h0) {
+        scaled = (uint8_t*)malloc((size_t)p[0] * p[1] * 3);
+        if (orc_resize_lanczos3(rgb, w0, h0, p[0], p[1], scaled)) { free(scaled); return -1; }
+        src = scaled;
+    }
+    memset(out, 255, (size_t)fw * fh * 3);
+    for (int y = 0; y < p[1]; y++)
+        memcpy(out + ((size_t)(y + p[3]) * fw + p[2]) * 3, src + (size_t)y * p[0] * 3, (size_t)p[0] * 3);
+    free(scaled);
     return 0;
 }

@@ -164,3 +164,25 @@ def test_full_attention_op_matches_f64(ocr, ctx, torch_cuda, n_keys, L, step):
     p = np.exp(s - s.max(axis=2, keepdims=True))
     want = np.einsum("lhn,hnd->lhd", p / p.sum(axis=2, keepdims=True), v.astype(np.float64))
     close(got, want.astype(np.float32))
+
+
+@pytest.mark.parametrize("w0,h0", [(3000, 2000), (1700, 500), (800, 1600), (1540, 1100), (40, 30)])
+def test_image_bake_matches_oracle(ocr, orc, ctx, w0, h0):
+    """ocr_image_bake (the Lanczos-3 resize of pages longer than 1540 px and the white pads, on the device) equals the
+    CPU restatement byte for byte: the same taps (computed on the host in f32) and each sum taken tap by tap"""
+    img = np.random.default_rng(w0 * h0).integers(0, 256, (h0, w0, 3), dtype=np.uint8)
+    got = ocr.image_bake(ctx, img)
+    want = orc.bake(img)
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+
+
+def test_encode_page_with_resize_matches_oracle(ocr, orc, ctx):
+    cfg = small_cfg(ocr, image_size=280)
+    v = ocr.Vision.synthetic(ctx, cfg, 17)
+    ov = orc.Vision(cfg.as_dict(), 17)
+    page = image(12, 300, 400)  # scaled to 280 x 210, padded to 280 x 224: 20 x 16 patches
+    got = v.encode_page(page)
+    want = ov.encode(orc.bake(page, longest=280))
+    close(got, want)
+    v.close()

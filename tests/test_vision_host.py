@@ -135,3 +135,67 @@ def test_oracle_layer1_rows_equal_its_encode(orc):
     assert out.shape == (12, 256) and np.isfinite(out).all()
     with pytest.raises(ValueError):
         v.encode(img[:, :100])  # 100 px: not on the 28 grid
+
+
+def resize_np(img: np.ndarray, w: int, h: int) -> np.ndarray:
+    """imageops::resize(.., Lanczos3) of the image crate 0.25 in numpy f32: a vertical pass into f32, a horizontal pass
+    into bytes; the taps summed one by one in order"""
+    f = np.float32
+
+    def lanczos3(x):
+        def sinc(t):
+            a = f(t * f(np.pi))
+            return f(1.0) if t == 0 else f(np.sin(a) / a)
+        return f(sinc(x) * sinc(f(x / f(3.0)))) if abs(x) < 3 else f(0.0)
+
+    def taps(n_in, n_out, o):
+        ratio = f(f(n_in) / f(n_out))
+        sr = max(ratio, f(1.0))
+        sup = f(f(3.0) * sr)
+        c = f(f(f(o) + f(0.5)) * ratio)
+        left = min(max(int(math.floor(f(c - sup))), 0), n_in - 1)
+        right = min(max(int(math.ceil(f(c + sup))), left + 1), n_in)
+        c = f(c - f(0.5))
+        ws = [lanczos3(f(f(f(i) - c) / sr)) for i in range(left, right)]
+        s = f(0.0)
+        for x in ws:
+            s = f(s + x)
+        return left, [f(x / s) for x in ws]
+
+    h0, w0 = img.shape[:2]
+    tmp = np.zeros((h, w0, 3), np.float32)
+    for y in range(h):
+        l, ws = taps(h0, h, y)
+        t = np.zeros((w0, 3), np.float32)
+        for i, wv in enumerate(ws):
+            t = (t + img[l + i].astype(np.float32) * wv).astype(np.float32)
+        tmp[y] = t
+    out = np.zeros((h, w, 3), np.uint8)
+    for x in range(w):
+        l, ws = taps(w0, w, x)
+        t = np.zeros((h, 3), np.float32)
+        for i, wv in enumerate(ws):
+            t = (t + tmp[:, l + i] * wv).astype(np.float32)
+        t = np.clip(t, 0, 255)
+        out[:, x] = np.where(t >= 0, np.floor(t + 0.5), -np.floor(-t + 0.5)).astype(np.uint8)
+    return out
+
+
+@pytest.mark.parametrize("src,dst", [((90, 60), (41, 27)), ((37, 80), (20, 43)), ((64, 48), (64, 24))])
+def test_oracle_resize_matches_a_numpy_restatement(orc, src, dst):
+    # (numpy's sin and the C library's sinf may differ by an ulp in a weight: a byte may move by one)
+    img = np.random.default_rng(sum(src)).integers(0, 256, (src[1], src[0], 3), dtype=np.uint8)
+    got = orc.resize_lanczos3(img, *dst).astype(int)
+    want = resize_np(img, *dst).astype(int)
+    assert np.abs(got - want).max() <= 1 and (got != want).mean() < 0.01
+    flat = np.full((src[1], src[0], 3), 131, np.uint8)
+    assert (orc.resize_lanczos3(flat, *dst) == 131).all()  # the weights sum to one
+
+
+def test_oracle_bake_scales_then_pads(orc):
+    img = np.random.default_rng(3).integers(0, 256, (2000, 3000, 3), dtype=np.uint8)
+    out = orc.bake(img)
+    sw, sh, l, t, r, b = orc.bake_plan(1540, 28, 3000, 2000)
+    assert out.shape == (sh + t + b, sw + l + r, 3) == (1036, 1540, 3)
+    assert (out[:t] == 255).all() and (out[t + sh:] == 255).all()
+    assert np.array_equal(out[t:t + sh, l:l + sw], orc.resize_lanczos3(img, sw, sh))
