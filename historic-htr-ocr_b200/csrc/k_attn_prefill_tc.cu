@@ -315,10 +315,13 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                 bool waited = false;
                 if (t == 0) {
                     m = mt;
-                } else if (mt > m + PA_RESCALE) {
+                } else if (__any_sync(FULL, mt > m + PA_RESCALE)) {
+                    // (warp-uniform: the TMEM loads and stores are collective over the warp's 32 lanes; a row whose
+                    // maximum did not move scales by 1)
                     if (!(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;  // P V of t - 1 done
                     waited = true;
-                    const float f = exp2f(m - mt);
+                    const bool up = mt > m + PA_RESCALE;
+                    const float f = up ? exp2f(m - mt) : 1.0f;
                     l *= f;
                     tc_fence_after();
 #pragma unroll
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                         tmem_st16(tO + lane_base + c * 16, o);
                     }
                     tmem_wait_st();
-                    m = mt;
+                    if (up) m = mt;
                 }
                 uint32_t pk[PA_KT / 2];
 #pragma unroll
