@@ -1707,6 +1707,7 @@ ocr_status ocr_prefill(ocr_session* s, int slot, const int32_t* ids, const float
         g.y_stride = y_stride;
         g.y16 = y16;
         g.nb = n;
+        g.wide = 1;  // (three groups of 32 rows per CTA when there are three or more)
         g.err = ctx->d_err;
         launch_bgemm(st, g, bq, ctx->num_sms, false);
     };
