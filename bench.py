@@ -291,8 +291,8 @@ def decode_workload(ocr, ctx, torch, config, steps, warmup, pg, local, tokens=0,
                 prefill={"rows": B * prefix_len, "rows_per_slot": prefix_len, "ms": round(pf_ms, 1),
                          "rows_per_s": round(B * prefix_len / (pf_ms * 1e-3), 1),
                          "note": "each slot's prefix prefilled through ocr_prefill (Input::Embeddings rows): the "
-                                 "projections on the tensor cores in groups of 32 rows, the causal attention on the "
-                                 "CUDA cores; device time, untimed for the decode metric"})
+                                 "projections on the tensor cores (three groups of 32 rows per CTA), the causal "
+                                 "attention on the tensor cores; device time, untimed for the decode metric"})
 
 
 def run_ours(args):
