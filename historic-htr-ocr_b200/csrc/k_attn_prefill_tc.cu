@@ -34,12 +34,14 @@ __host__ __device__ constexpr int pa_threads(bool tiled) { return tiled ? PA_THR
 constexpr uint32_t PA_TMEM_COLS = 256;  // S at columns 0 and 64 (double buffer), O at 128 … 128 + D
 constexpr float PA_RESCALE = 8.0f;      // the one-pass form's headroom over the running maximum (log2 units)
 // the shared-memory plan of head dim D: Q hi / lo, two K tiles, two V tiles (transposed), P hi / lo
-template <int D>
+// (the tiled form's V^T tiles carry 16 more rows: a row of ones, whose product with P is the row sum of P, then zeros)
+template <int D, bool TILED = false>
 struct PaPlan {
     static constexpr int KPT = (PA_KT * D / 8 + PA_LOADERS * 32 - 1) / (PA_LOADERS * 32);  // K pieces per thread
+    static constexpr int VROWS = TILED ? D + 16 : D;    // the P V product's N
     static constexpr uint32_t Q_BYTES = PA_QT * D * 2;  // one f16 operand of the Q tile: D/64 halves of 64 dims
     static constexpr uint32_t K_BYTES = PA_KT * D * 2;  // a K tile: D/64 halves of 64 dims, 64 key rows each
-    static constexpr uint32_t V_BYTES = D * PA_KT * 2;  // a V tile transposed: D dim rows of the tile's 64 keys
+    static constexpr uint32_t V_BYTES = VROWS * PA_KT * 2;  // a V tile transposed: the dim rows of the tile's 64 keys
     static constexpr uint32_t P_BYTES = PA_QT * PA_KT * 2;  // one f16 operand of P: 128 query rows of 64 keys
     static constexpr uint32_t SMEM = 2 * Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 1024;
 };
@@ -74,7 +76,7 @@ template <int D, bool CAUSAL, bool TILED>
 __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(TcAttnArgs a) {
     constexpr int THREADS = pa_threads(TILED);
     static_assert(!TILED || D == 64, "the pre-tiled operands are written for head dim 64");
-    using P = PaPlan<D>;
+    using P = PaPlan<D, TILED>;
     const int L = a.L, pos0 = a.pos0;
     // the tiled form works in log2 units (scores times log2 e, probabilities by exp2)
     const float qscale = TILED ? a.scale * 1.4426950408889634f : a.scale;
@@ -137,6 +139,13 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
         *reinterpret_cast<uint4*>(Qh + hf * (PA_QT * 128) + sw128(r, p)) = hi;
         *reinterpret_cast<uint4*>(Ql + hf * (PA_QT * 128) + sw128(r, p)) = lo;
     }
+    if constexpr (TILED) {  // rows D … D + 15 of both V^T buffers: ones, then zeros (the copies never write them)
+        for (int e = tid; e < 2 * 16 * 8; e += THREADS) {
+            const int b = e / 128, r = (e / 8) % 16, p = e % 8;
+            const uint32_t one = r == 0 ? 0x3C003C00u : 0u;
+            *reinterpret_cast<uint4*>(Vr + b * P::V_BYTES + sw128(D + r, p)) = make_uint4(one, one, one, one);
+        }
+    }
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
@@ -156,8 +165,8 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                 bulk_g2s(Kr + ks * P::K_BYTES, kbase + (size_t)t * PA_KT * D, P::K_BYTES, &sh.kfull[ks]);
                 kn[ks]++;
                 if (t >= 2 && !(ok = pa_wait(&sh.vempty[ks], ((t >> 1) - 1) & 1, abort_flag, err))) break;
-                mbar_expect_tx(&sh.vfull[ks], P::V_BYTES);
-                bulk_g2s(Vr + ks * P::V_BYTES, vbase + (size_t)t * PA_KT * D, P::V_BYTES, &sh.vfull[ks]);
+                mbar_expect_tx(&sh.vfull[ks], D * PA_KT * 2);  // (the dim rows; the ones row stays)
+                bulk_g2s(Vr + ks * P::V_BYTES, vbase + (size_t)t * PA_KT * D, D * PA_KT * 2, &sh.vfull[ks]);
                 vn[ks]++;
             }
             if (!ok) *abort_flag = 1;
@@ -230,7 +239,7 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
     } else if (warp == 4) {
         // ---- the tensor cores ----
         if (lane == 0) {
-            const uint32_t idS = bg_idesc(PA_KT), idO = bg_idesc(D);
+            const uint32_t idS = bg_idesc(PA_KT), idO = bg_idesc(P::VROWS);
             bool ok = true, any = false;
             // S[sq % 2] = Q K^T for the K tile of staging sequence `seq`
             auto qk = [&](int sq, int seq) -> bool {
@@ -307,11 +316,12 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
             // <= 2^PA_RESCALE stays in f16's range. P is rounded to f16 (the reference's f16 path rounds P so).
             for (int t = 0; t < T && ok; t++) {
                 if (!(ok = read_s(t))) break;
-                float mt = -INFINITY;
                 const bool edge = (t + 1) * PA_KT > n_keys;  // the last tile may hold keys past n_keys
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
                 for (int j = 0; j < PA_KT; j++)
-                    if (!edge || t * PA_KT + j < n_keys) mt = fmaxf(mt, __uint_as_float(sv[j]));
+                    if (!edge || t * PA_KT + j < n_keys) mq[j & 3] = fmaxf(mq[j & 3], __uint_as_float(sv[j]));
+                const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
                 bool waited = false;
                 if (t == 0) {
                     m = mt;
@@ -322,10 +332,9 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                     waited = true;
                     const bool up = mt > m + PA_RESCALE;
                     const float f = up ? exp2f(m - mt) : 1.0f;
-                    l *= f;
                     tc_fence_after();
 #pragma unroll
-                    for (int c = 0; c < D / 16; c++) {
+                    for (int c = 0; c < P::VROWS / 16; c++) {  // (the row sum's column with O)
                         uint32_t o[16];
                         tmem_ld16(tO + lane_base + c * 16, o);
                         tmem_wait_ld();
@@ -344,9 +353,7 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
                         if (t * PA_KT + j >= n_keys) p0 = 0.0f;
                         if (t * PA_KT + j + 1 >= n_keys) p1 = 0.0f;
                     }
-                    l += p0;
-                    l += p1;
-                    pk[j >> 1] = pack_h2(p0, p1);
+                    pk[j >> 1] = pack_h2(p0, p1);  // (the row sum comes from the ones row of V^T)
                 }
                 if (t >= 1 && !waited && !(ok = pa_wait(&sh.pfree, (t - 1) & 1, abort_flag, err))) break;
 #pragma unroll
@@ -393,6 +400,12 @@ __global__ void __launch_bounds__(pa_threads(TILED), TILED ? 2 : 1) k_attn_tc(Tc
         // the output row: O / sum, as f32 (out) and / or split f16 hi / lo into the next contraction's operand (out16)
         if (ok && pa_wait(&sh.ofull, 0, abort_flag, err)) {
             tc_fence_after();
+            if constexpr (TILED) {  // the row sum of the rounded P, column D of the product
+                uint32_t o[16];
+                tmem_ld16(tO + lane_base + D, o);
+                tmem_wait_ld();
+                l = __uint_as_float(o[0]);
+            }
             const float inv = 1.0f / l;
             const int row = q0 + tid;
             uint8_t* g16 = a.out16 ? a.out16 + (size_t)(row / BG_SLOTS) * x16_group_bytes(a.out16_K) : nullptr;
@@ -443,10 +456,10 @@ static void launch_tc(cudaStream_t st, const TcAttnArgs& a) {
     static PerDeviceOnce once;
     once([] {
         cudaFuncSetAttribute(k_attn_tc<D, CAUSAL, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)PaPlan<D>::SMEM);
+                             (int)PaPlan<D, TILED>::SMEM);
     });
-    k_attn_tc<D, CAUSAL, TILED><<<dim3((a.L + PA_QT - 1) / PA_QT, a.n_head, 1), pa_threads(TILED), PaPlan<D>::SMEM,
-                                  st>>>(a);
+    k_attn_tc<D, CAUSAL, TILED><<<dim3((a.L + PA_QT - 1) / PA_QT, a.n_head, 1), pa_threads(TILED),
+                                  PaPlan<D, TILED>::SMEM, st>>>(a);
 }
 
 void launch_attention_prefill_tc(cudaStream_t st, const float* qkv, int L, int n_head, int n_kv, const __half* kc,
