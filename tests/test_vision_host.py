@@ -199,3 +199,19 @@ def test_oracle_bake_scales_then_pads(orc):
     assert out.shape == (sh + t + b, sw + l + r, 3) == (1036, 1540, 3)
     assert (out[:t] == 255).all() and (out[t + sh:] == 255).all()
     assert np.array_equal(out[t:t + sh, l:l + sw], orc.resize_lanczos3(img, sw, sh))
+
+
+def test_vision_c_abi_refuses_bad_arguments_without_a_device(ocr):
+    import ctypes as C
+
+    L = ocr.lib()
+    p = ocr.BakePlan()
+    assert L.ocr_bake_plan_for(1540, 28, 0, 10, C.byref(p)) == 1  # OCR_ERR_ARG: sizes must be positive
+    assert L.ocr_bake_plan_for(1540, 28, 10, 10, None) == 1
+    assert L.ocr_vision_encode(None, None, 56, 56, -1, None, 0, None, None) == 1
+    assert "null" in L.ocr_last_error().decode()
+    assert L.ocr_vision_encode_page(None, None, 56, 56, None, 0, None) == 1
+    assert L.ocr_vision_config(None, None) == 1
+    assert L.ocr_vision_destroy(None) == 0
+    assert L.ocr_image_bake(None, None, 10, 10, 1540, 28, None, 0, None, None) == 1
+    assert L.ocr_op_attention_full(None, None, 0, 0, 0, None, None, 0, 0, 0.0, None, 0) == 1
