@@ -215,3 +215,76 @@ def test_vision_c_abi_refuses_bad_arguments_without_a_device(ocr):
     assert L.ocr_vision_destroy(None) == 0
     assert L.ocr_image_bake(None, None, 10, 10, 1540, 28, None, 0, None, None) == 1
     assert L.ocr_op_attention_full(None, None, 0, 0, 0, None, None, 0, 0, 0.0, None, 0) == 1
+
+
+def encode_np(orc, cfg: dict, seed: int, sigma: float, img: np.ndarray) -> np.ndarray:
+    """An independent numpy restatement of the vision encoder + projector (vision.rs:266-317, 405-423; patchify.wgsl,
+    rope2d.wgsl, attention.wgsl with K / V rounded to f16, swiglu.wgsl, unfold2x2.wgsl, gelu.wgsl), in f64 on the
+    synthetic weights' dequantised values — a second implementation the C restatement is checked against"""
+    d, H, f, p, pd = cfg["dim"], cfg["n_head"], cfg["n_ff"], cfg["patch"], cfg["proj_dim"]
+    dh, pp = d // H, 3 * p * p
+    pcols = (pp + 255) // 256 * 256
+
+    def mat(kind_stream, rows, cols):
+        return orc.dequantize_q8_0(orc.synth_q8_0(rows * cols, orc.substream(seed, kind_stream), sigma),
+                                   rows * cols).reshape(rows, cols).astype(np.float64)
+
+    def norm(x, w):
+        return x / np.sqrt((x * x).mean(axis=1, keepdims=True) + cfg["eps"]) * w
+
+    h0, w0 = img.shape[:2]
+    px, py = w0 // p, h0 // p
+    n = px * py
+    lut = orc.pixel_lut(cfg).astype(np.float64)
+    P = np.zeros((n, pcols))
+    for t in range(n):
+        ty, tx = divmod(t, px)
+        patch = img[ty * p:(ty + 1) * p, tx * p:(tx + 1) * p]  # [ky][kx][c]
+        P[t, :pp] = np.stack([lut[c][patch[:, :, c]] for c in range(3)]).reshape(-1)
+    wp = np.zeros((d, pcols))
+    b = np.empty(d * pcols // 32 * 34, np.uint8)
+    orc.lib().orc_synth_q8_0_padded(b.ctypes.data, d, pcols, pp, orc.substream(seed, orc.V_PATCH_STREAM), sigma)
+    wp[:] = orc.dequantize_q8_0(b, d * pcols).reshape(d, pcols)
+    x = norm(P @ wp.T, orc.fill_norm(orc.substream(seed, orc.V_PRE_LN_STREAM), d))
+    cs = orc.rope2d_table(cfg["rope_theta"], dh, max(px, py)).astype(np.float64)
+    pos = [np.arange(n) // px, np.arange(n) % px]
+
+    def rope(v):  # [n][H][dh]
+        v = v.copy()
+        for half in range(2):
+            c, s = cs[half, pos[half], :, 0][:, None, :], cs[half, pos[half], :, 1][:, None, :]
+            a = v[:, :, half * dh // 2:(half + 1) * dh // 2]
+            x0, x1 = a[:, :, 0::2].copy(), a[:, :, 1::2].copy()
+            a[:, :, 0::2], a[:, :, 1::2] = x0 * c - x1 * s, x0 * s + x1 * c
+        return v
+
+    for l in range(cfg["n_layer"]):
+        st = lambda k: orc.V_LAYER_STREAM + l * 16 + k
+        hn = norm(x, orc.fill_norm(orc.substream(seed, st(orc.V_LN1)), d))
+        q = rope((hn @ mat(st(orc.V_Q), d, d).T).reshape(n, H, dh))
+        k = rope((hn @ mat(st(orc.V_K), d, d).T).reshape(n, H, dh)).astype(np.float16).astype(np.float64)
+        v = (hn @ mat(st(orc.V_V), d, d).T).reshape(n, H, dh).astype(np.float16).astype(np.float64)
+        s = np.einsum("qhd,khd->hqk", q, k) / np.sqrt(dh)
+        pr = np.exp(s - s.max(axis=2, keepdims=True))
+        a = np.einsum("hqk,khd->qhd", pr / pr.sum(axis=2, keepdims=True), v).reshape(n, d)
+        x = x + a @ mat(st(orc.V_O), d, d).T
+        hn = norm(x, orc.fill_norm(orc.substream(seed, st(orc.V_LN2)), d))
+        g, u = hn @ mat(st(orc.V_GATE), f, d).T, hn @ mat(st(orc.V_UP), f, d).T
+        x = x + (g / (1 + np.exp(-g)) * u) @ mat(st(orc.V_DOWN), d, f).T
+    xn = norm(x, orc.fill_norm(orc.substream(seed, orc.V_INPUT_NORM_STREAM), d))
+    grid = xn.reshape(py, px, d)
+    z = np.stack([grid[ky::2, kx::2] for ky in range(2) for kx in range(2)], axis=-1)  # [oy][ox][c][ky*2+kx]
+    z = z.reshape(-1, 4 * d)
+    m1 = (z @ mat(orc.V_MERGER_STREAM, d, 4 * d).T) @ mat(orc.V_MM1_STREAM, pd, d).T
+    t = np.clip(0.7978845608028654 * m1 * (1 + 0.044715 * m1 * m1), -15, 15)
+    return (0.5 * m1 * (1 + np.tanh(t))) @ mat(orc.V_MM2_STREAM, pd, pd).T
+
+
+def test_oracle_encoder_matches_a_numpy_restatement(orc):
+    cfg = dict(VCFG, n_layer=2)
+    img = np.random.default_rng(4).integers(0, 256, (56, 84, 3), dtype=np.uint8)
+    got = orc.Vision(cfg, 29).encode(img)
+    want = encode_np(orc, cfg, 29, 0.02, img)
+    assert got.shape == want.shape == (6, 256)
+    err = np.abs(got - want).max() / np.abs(want).max()
+    assert err <= 1e-5, f"{err:.2e}"  # (3e-7 here: f32 vs f64 roundings)
