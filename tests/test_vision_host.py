@@ -288,3 +288,13 @@ def test_oracle_encoder_matches_a_numpy_restatement(orc):
     assert got.shape == want.shape == (6, 256)
     err = np.abs(got - want).max() / np.abs(want).max()
     assert err <= 1e-5, f"{err:.2e}"  # (3e-7 here: f32 vs f64 roundings)
+
+
+def test_bake_plan_reference_known_answers(ocr, orc):
+    """the reference's own tests of the plan (app/crates/ocr-core/src/imageops.rs:517-530:
+    plan_scales_down_and_pads_to_grid, plan_never_upscales)"""
+    for bake_plan in (ocr.bake_plan, orc.bake_plan):
+        sw, sh, l, t, r, b = bake_plan(1540, 28, 3000, 2000)
+        assert (sw, sh) == (1540, 1027) and (sw + l + r, sh + t + b) == (1540, 1036) and (t, b) == (4, 5)
+        sw, sh, l, t, r, b = bake_plan(1540, 28, 500, 30)
+        assert (sw, sh) == (500, 30) and (sw + l + r, sh + t + b) == (504, 56)
