@@ -13,7 +13,12 @@ Checked:
   (every patch's keys and values computed), and the bake fused into the patch gather equals the encode of the
   oracle's baked copy bit for bit;
 - the page read end to end at small size: the embeddings left on the device, prefilled between prompt ids (the
-  reference's prompt layout, engine.rs:460-474), then greedy ids equal to the oracle text model's on the same rows.
+  reference's prompt layout, engine.rs:460-474), then greedy ids equal to the oracle text model's on the same rows;
+- the attention alone (ocr_op_attention_full) against f64, including scores that force the one-pass softmax to
+  rescale (the reference's own check of its f16 vision attention against f64 is f16_paths_match_cpu,
+  app/crates/ocr-wgpu/src/text.rs:1186-1240);
+- the bake on the device (the Lanczos-3 resize and the pads) byte for byte against the CPU restatement, and a page
+  that needs the resize encoded end to end.
 """
 from __future__ import annotations
 
