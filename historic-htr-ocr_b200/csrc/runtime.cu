@@ -2486,6 +2486,53 @@ ocr_status ocr_gguf_text_config(const ocr_gguf* h, ocr_text_cfg* out) {
     return OCR_OK;
 }
 
+ocr_status ocr_gguf_vision_config(const ocr_gguf* h, ocr_vision_cfg* out) {
+    if (!h || !out) return fail(OCR_ERR_ARG, "null argument");
+    const Gguf& g = h->g;
+    std::string msg, proj;
+    if (!g.get_str("clip.projector_type", proj, msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (proj != "lightonocr") return fail(OCR_ERR_FORMAT, "projector \"" + proj + "\": this engine runs lightonocr only");
+    auto it = g.meta.find("clip.use_silu");
+    if (it == g.meta.end()) return fail(OCR_ERR_FORMAT, "GGUF has no metadata key clip.use_silu");
+    if (it->second.type != 7) return fail(OCR_ERR_FORMAT, "clip.use_silu is not a bool");
+    if (!it->second.u) return fail(OCR_ERR_FORMAT, "clip.use_silu is false: the encoder's FFN would not be SwiGLU");
+    ocr_vision_cfg c{};
+    const char* keys[] = {"clip.vision.embedding_length", "clip.vision.attention.head_count", "clip.vision.block_count",
+                          "clip.vision.feed_forward_length", "clip.vision.patch_size",
+                          "clip.vision.spatial_merge_size", "clip.vision.image_size", "clip.vision.projection_dim"};
+    uint32_t v[8];
+    for (int i = 0; i < 8; i++)
+        if (!g.get_u32(keys[i], v[i], msg)) return fail(OCR_ERR_FORMAT, msg);
+    if (v[1] == 0 || v[0] % v[1] != 0 || v[0] / v[1] != 64)
+        return fail(OCR_ERR_FORMAT, "head dim " + std::to_string(v[0]) + "/" + std::to_string(v[1]) +
+                                        ": the attention kernel is written for 64");
+    c.dim = (int32_t)v[0];
+    c.n_head = (int32_t)v[1];
+    c.n_layer = (int32_t)v[2];
+    c.n_ff = (int32_t)v[3];
+    c.patch = (int32_t)v[4];
+    c.merge = (int32_t)v[5];
+    c.image_size = (int32_t)v[6];
+    c.proj_dim = (int32_t)v[7];
+    if (!g.get_f32("clip.vision.attention.layer_norm_epsilon", c.eps, msg)) return fail(OCR_ERR_FORMAT, msg);
+    c.rope_theta = 10000.0f;  // clip.cpp sets it in code for this projector; the GGUF carries no key (vision.rs:30-31)
+    for (int k = 0; k < 2; k++) {
+        const char* key = k == 0 ? "clip.vision.image_mean" : "clip.vision.image_std";
+        float* dst = k == 0 ? c.mean : c.std;
+        auto a = g.meta.find(key);
+        if (a == g.meta.end()) return fail(OCR_ERR_FORMAT, std::string("GGUF has no metadata key ") + key);
+        if (a->second.type != 9) return fail(OCR_ERR_FORMAT, std::string(key) + " is not an array");
+        if (a->second.arr.size() != 3)
+            return fail(OCR_ERR_FORMAT, std::string(key) + " has " + std::to_string(a->second.arr.size()) + " values");
+        for (int i = 0; i < 3; i++) {
+            if (a->second.arr[i].type != 6) return fail(OCR_ERR_FORMAT, std::string(key) + " holds a non-f32 value");
+            dst[i] = (float)a->second.arr[i].f;
+        }
+    }
+    *out = c;
+    return OCR_OK;
+}
+
 ocr_status ocr_op_wait_probe(ocr_ctx* ctx, int tries, int* waited_out) {
     if (!ctx || !waited_out) return fail(OCR_ERR_ARG, "null argument");
     if (tries < 1 || tries > 100000) return fail(OCR_ERR_ARG, "tries must be in [1, 100000]");

@@ -125,6 +125,7 @@ _SIGS = {
                                   C.POINTER(C.c_int), C.POINTER(C.c_uint64)]),
     "ocr_gguf_to_f32": (C.c_int, [_P, C.c_char_p, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
     "ocr_gguf_text_config": (C.c_int, [_P, C.POINTER(TextCfg)]),
+    "ocr_gguf_vision_config": (C.c_int, [_P, C.POINTER(VisionCfg)]),
     "ocr_op_penalize": (C.c_int, [_P, _P, C.c_int, C.c_float, C.c_int, _P, C.c_int]),
     "ocr_q8_row_bytes": (C.c_int, [C.c_int]),
     "ocr_op_repack_q8_0": (C.c_int, [_P, _P, C.c_int, C.c_int, _P]),
@@ -681,6 +682,13 @@ class Gguf:
         c = TextCfg()
         _check(lib().ocr_gguf_text_config(self.h, C.byref(c)))
         return TextConfig.from_c(c)
+
+    def vision_config(self) -> "VisionConfig":
+        """VisionConfig::from_gguf of an mmproj GGUF"""
+        c = VisionCfg()
+        _check(lib().ocr_gguf_vision_config(self.h, C.byref(c)))
+        return VisionConfig(c.n_layer, c.dim, c.n_head, c.n_ff, c.patch, c.merge, c.image_size, c.proj_dim, c.eps,
+                            c.rope_theta, tuple(c.mean), tuple(c.std))
 
 
 def op_penalize(ctx: Context, d_logits: int, n_vocab: int, rp: float, window: int, d_hist: int, n_hist: int) -> None:

@@ -252,6 +252,10 @@ ocr_status ocr_gguf_tensor(const ocr_gguf* g, const char* name, int* ggml_type, 
 ocr_status ocr_gguf_to_f32(const ocr_gguf* g, const char* name, float* out, size_t cap, size_t* n);
 /* TextConfig::from_gguf + TextModel::load's tensor checks (text.rs:51-82, 111-128, 332-375), no device */
 ocr_status ocr_gguf_text_config(const ocr_gguf* g, ocr_text_cfg* out);
+/* VisionConfig::from_gguf (app/crates/ocr-wgpu/src/vision.rs:55-88) of an mmproj GGUF: clip.projector_type must be
+ * "lightonocr", clip.use_silu true, the head dim 64; the clip.vision.* sizes, layer_norm_epsilon, image_mean /
+ * image_std (3 values each); rope_theta 10000 (clip.cpp's constant). Host only. */
+ocr_status ocr_gguf_vision_config(const ocr_gguf* g, ocr_vision_cfg* out);
 
 /* ---- low-level ops on device buffers (the kernels behind the calls above; tests and the LM-head benchmark) ------ */
 /* choose_pen.wgsl: the windowed repetition penalty in place on d_logits [n_vocab] over the distinct tokens of

@@ -298,3 +298,38 @@ def test_bake_plan_reference_known_answers(ocr, orc):
         assert (sw, sh) == (1540, 1027) and (sw + l + r, sh + t + b) == (1540, 1036) and (t, b) == (4, 5)
         sw, sh, l, t, r, b = bake_plan(1540, 28, 500, 30)
         assert (sw, sh) == (500, 30) and (sw + l + r, sh + t + b) == (504, 56)
+
+
+def mmproj_kvs(**over):
+    """the clip.* metadata of a LightOnOCR mmproj GGUF (VisionConfig::from_gguf's keys, vision.rs:55-88)"""
+    import gguf_writer as W
+
+    kv = {"clip.projector_type": (W.STR, "lightonocr"), "clip.use_silu": (W.BOOL, 1),
+          "clip.vision.embedding_length": (W.U32, 1024), "clip.vision.attention.head_count": (W.U32, 16),
+          "clip.vision.block_count": (W.U32, 24), "clip.vision.feed_forward_length": (W.U32, 4096),
+          "clip.vision.patch_size": (W.U32, 14), "clip.vision.spatial_merge_size": (W.U32, 2),
+          "clip.vision.image_size": (W.U32, 1540), "clip.vision.projection_dim": (W.U32, 1024),
+          "clip.vision.attention.layer_norm_epsilon": (W.F32, 1e-5),
+          "clip.vision.image_mean": (W.ARR, (W.F32, [0.48145466, 0.4578275, 0.40821073])),
+          "clip.vision.image_std": (W.ARR, (W.F32, [0.26862954, 0.26130258, 0.27577711]))}
+    kv.update(over)
+    return [(k, t, v) for k, (t, v) in kv.items() if t is not None]
+
+
+def test_vision_config_from_gguf(ocr):
+    import gguf_writer as W
+
+    c = ocr.Gguf(data=W.write(mmproj_kvs(), [])).vision_config()
+    want = ocr.VisionConfig()
+    assert (c.n_layer, c.dim, c.n_head, c.n_ff, c.patch, c.merge, c.image_size, c.proj_dim) == \
+        (want.n_layer, want.dim, want.n_head, want.n_ff, want.patch, want.merge, want.image_size, want.proj_dim)
+    assert c.eps == np.float32(1e-5) and c.rope_theta == 10000.0
+    assert np.allclose(c.mean, want.mean) and np.allclose(c.std, want.std)
+    # the reference's refusals (vision.rs:57-73), message for message
+    for over, match in [({"clip.projector_type": (W.STR, "pixtral")}, "runs lightonocr only"),
+                        ({"clip.use_silu": (W.BOOL, 0)}, "would not be SwiGLU"),
+                        ({"clip.vision.attention.head_count": (W.U32, 8)}, "written for 64"),
+                        ({"clip.vision.image_std": (W.ARR, (W.F32, [0.5, 0.5]))}, "has 2 values"),
+                        ({"clip.vision.block_count": (None, None)}, "clip.vision.block_count")]:
+        with pytest.raises(ocr.OcrError, match=match):
+            ocr.Gguf(data=W.write(mmproj_kvs(**over), [])).vision_config()
