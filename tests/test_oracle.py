@@ -9,6 +9,7 @@
 - the q8_0 quantizer (text.rs:676-691, ggml quantize_row_q8_0_ref) against an independent numpy restatement
 - f16 round to nearest even (half 2.7.1) against numpy's float16
 - the seeded generators: the numpy spec (ocr_b200.gauss / fill_ids) and the C oracle give identical bits
+- the C decoder against an independent numpy restatement of the Qwen3 prefill (7e-7 of the largest logit)
 """
 from __future__ import annotations
 
@@ -166,3 +167,62 @@ def test_oracle_decoder_is_deterministic_and_causal(orc):
     for t in ids[8:]:
         lb = b.step(int(t))
     assert np.allclose(la, lb, rtol=1e-4, atol=1e-4 * np.abs(la).max())
+
+
+def decoder_np(orc, m, cfg: dict, ids) -> np.ndarray:
+    """An independent numpy restatement of the Qwen3 prefill (text.rs:4-10, 437-521: RMSNorm → q / k / v → per-head
+    q / k RMSNorm → NEOX RoPE → K / V rounded to f16 → causal softmax attention / sqrt(128) → o + residual → RMSNorm →
+    SwiGLU → down + residual; output_norm and the tied head), in f64 on the dequantised tensors: the last row's
+    logits"""
+    d, H, G, dh, f, V = cfg["dim"], cfg["n_head"], cfg["n_kv"], cfg["d_head"], cfg["n_ff"], cfg["n_vocab"]
+    eps = cfg.get("eps", 1e-6)
+
+    def q8(layer, kind, rows, cols):
+        return orc.dequantize_q8_0(m.tensor(layer, kind), rows * cols).reshape(rows, cols).astype(np.float64)
+
+    def vec(layer, kind):
+        return m.tensor(layer, kind).view(np.float32).astype(np.float64)
+
+    def norm(x, w):
+        return x / np.sqrt((x * x).mean(axis=-1, keepdims=True) + eps) * w
+
+    n = len(ids)
+    emb = q8(-1, 0, V, d)
+    x = emb[np.asarray(ids)]
+    cs = orc.rope_table(cfg.get("rope_base", 1e6), dh, n).astype(np.float64)  # [pos][dh/2][2]
+    c, s = cs[:, None, :, 0], cs[:, None, :, 1]
+
+    def rope(v):  # [n][heads][dh], NEOX pairs (i, i + dh/2)
+        a, b = v[..., :dh // 2], v[..., dh // 2:]
+        return np.concatenate([a * c - b * s, a * s + b * c], axis=-1)
+
+    for l in range(cfg["n_layer"]):
+        h = norm(x, vec(l, orc.ATTN_NORM))
+        q = (h @ q8(l, orc.Q, H * dh, d).T).reshape(n, H, dh)
+        k = (h @ q8(l, orc.K, G * dh, d).T).reshape(n, G, dh)
+        v = (h @ q8(l, orc.V, G * dh, d).T).reshape(n, G, dh)
+        q = rope(norm(q, vec(l, orc.Q_NORM)))
+        k = rope(norm(k, vec(l, orc.K_NORM))).astype(np.float16).astype(np.float64)
+        v = v.astype(np.float16).astype(np.float64)
+        kk, vv = np.repeat(k, H // G, axis=1), np.repeat(v, H // G, axis=1)
+        sc = np.einsum("qhd,khd->hqk", q, kk) / np.sqrt(dh)
+        sc = np.where(np.tril(np.ones((n, n), bool))[None], sc, -np.inf)
+        p = np.exp(sc - sc.max(axis=2, keepdims=True))
+        a = np.einsum("hqk,khd->qhd", p / p.sum(axis=2, keepdims=True), vv).reshape(n, H * dh)
+        x = x + a @ q8(l, orc.O, d, H * dh).T
+        h = norm(x, vec(l, orc.FFN_NORM))
+        g, u = h @ q8(l, orc.GATE, f, d).T, h @ q8(l, orc.UP, f, d).T
+        x = x + (g / (1 + np.exp(-g)) * u) @ q8(l, orc.DOWN, d, f).T
+    out_norm = m.tensor(-1, 1).view(np.float32).astype(np.float64)
+    return norm(x[-1], out_norm) @ emb.T
+
+
+def test_oracle_decoder_matches_a_numpy_restatement(orc):
+    cfg = dict(n_layer=2, dim=256, n_head=2, n_kv=1, d_head=128, n_ff=512, n_vocab=1000, eps=1e-6, rope_base=1e6)
+    m = orc.Model(cfg, seed=13, sigma_w=0.2, sigma_e=1.0)
+    ids = [int(t) for t in orc.fill_ids(3, 17, 1000)]
+    got = m.session(32).prefill(ids, None, len(ids))
+    want = decoder_np(orc, m, cfg, ids)
+    err = np.abs(got - want).max() / np.abs(want).max()
+    assert err <= 1e-5, f"{err:.2e}"  # (7e-7 here: the C oracle's f32 roundings)
+    assert int(np.argmax(got)) == int(np.argmax(want))
