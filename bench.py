@@ -544,6 +544,10 @@ def run_config4(args, ocr, ctx, torch, pg, rank, world, local):
             "clocks": clk.summary()}
         if not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline_sample(4, tokens_sample=16)
+            enc = cpu_encode_sample()
+            n_patches = ((sw + left + right) // vcfg.patch) * ((sh + top + bottom) // vcfg.patch)
+            enc["gpu_patches_per_s"] = round(n_patches / (out["ttft"]["encode_ms"] * 1e-3), 1)
+            out["cpu_encode"] = enc
         print(json.dumps(out), flush=True)
     sess.close()
     model.close()
@@ -645,6 +649,26 @@ class CpuLmHead:
 
     def cores(self) -> int:
         return self.O.num_threads()
+
+
+def cpu_encode_sample(side: int = 280):
+    """the vision encoder on the host cores: the oracle's encode (OpenMP) of a side x side page with the full
+    24-layer LightOnOCR-shaped encoder — a bounded sample of config 4's encode (8800 patches), reported per patch"""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    import ocr_b200 as ocr
+
+    cfg = ocr.VisionConfig().as_dict()
+    v = O.Vision(cfg, ocr.SEED_BASE + 4, 0.02)
+    img = np.random.default_rng(4).integers(0, 256, (side, side, 3), dtype=np.uint8)
+    t0 = time.perf_counter()
+    v.encode(img)
+    dt = time.perf_counter() - t0
+    n = (side // 14) ** 2
+    return {"value": round(n / dt, 1), "unit": "patches/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"the oracle's encode of a {side} x {side} page ({n} patches, 24 layers, the projector), "
+                      f"{dt:.1f} s, oracle/vision.c (OpenMP); config 4's page has 8800 patches"}
 
 
 def cpu_baseline_sample(config: int, tokens_sample: int = 16):
